@@ -1,0 +1,328 @@
+// Torch bindings of the zstep_b200 kernel library (module zstep_b200._C).
+//
+// Each binding validates devices/dtypes/contiguity, converts tensors to raw pointers
+// and calls the C ABI in zs_kernels.h on the current CUDA stream.  Any non-zero return
+// code raises, so a missing or rejected kernel is never silently replaced.
+#include <ATen/cuda/CUDAContext.h>
+#include <torch/extension.h>
+
+#include <optional>
+
+#include "zs_kernels.h"
+
+namespace {
+
+using Tensor = at::Tensor;
+using OptT = std::optional<Tensor>;
+
+template <typename T = void>
+T* ptr(const Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+template <typename T = void>
+T* optptr(const OptT& t) {
+  return t.has_value() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+void check_cuda(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+void check_opt(const OptT& t, const char* name) {
+  if (t.has_value()) check_cuda(*t, name);
+}
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void rc(int code, const char* what) { TORCH_CHECK(code == 0, what, " failed with code ", code); }
+
+void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor& sfb, int64_t k,
+               int64_t n_pad, int64_t n_valid, int64_t groups, int64_t m_rows,
+               const OptT& group_count, const OptT& group_offset, const OptT& chunk_prefix,
+               int64_t epi_mode, const Tensor& out, int64_t ldo, const OptT& out_sf,
+               const OptT& row_dst, const OptT& row_scale, const OptT& err, int64_t max_items) {
+  check_cuda(a, "a");
+  check_cuda(sfa, "sfa");
+  check_cuda(b, "b");
+  check_cuda(sfb, "sfb");
+  check_cuda(out, "out");
+  check_opt(group_count, "group_count");
+  check_opt(group_offset, "group_offset");
+  check_opt(chunk_prefix, "chunk_prefix");
+  TORCH_CHECK(a.element_size() == 1 && b.element_size() == 1, "a/b must be 8-bit");
+  TORCH_CHECK(a.numel() >= groups * n_pad * k, "a too small");
+  TORCH_CHECK(b.numel() % k == 0, "b must be [rows, k]");
+  GemmMxf8Args p{};
+  p.a = ptr<const uint8_t>(a);
+  p.sfa = ptr<const uint8_t>(sfa);
+  p.b = ptr<const uint8_t>(b);
+  p.sfb = ptr<const uint8_t>(sfb);
+  p.k = (int)k;
+  p.n_pad = (int)n_pad;
+  p.n_valid = (int)n_valid;
+  p.groups = (int)groups;
+  p.b_rows = (int)(b.numel() / k);
+  p.m_rows = (int)m_rows;
+  p.group_count = optptr<const int>(group_count);
+  p.group_offset = optptr<const int>(group_offset);
+  p.chunk_prefix = optptr<const int>(chunk_prefix);
+  p.max_items = (int)max_items;
+  p.epi_mode = (int)epi_mode;
+  p.out = ptr(out);
+  p.ldo = (int)ldo;
+  p.out_sf = optptr<uint8_t>(out_sf);
+  p.row_dst = optptr<const int>(row_dst);
+  p.row_scale = optptr<const float>(row_scale);
+  p.err = optptr<int>(err);
+  TORCH_CHECK(p.chunk_prefix == nullptr || (p.group_count && p.group_offset), "grouped mode args");
+  if (p.chunk_prefix == nullptr) TORCH_CHECK(m_rows <= p.b_rows, "m_rows > rows of b");
+  rc(zs_gemm_mxf8(&p, stream()), "zs_gemm_mxf8");
+}
+
+void quant_mxf8(const Tensor& x, const Tensor& q, const Tensor& sf) {
+  check_cuda(x, "x");
+  check_cuda(q, "q");
+  check_cuda(sf, "sf");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2, "x must be bf16 [rows, k]");
+  const int rows = (int)x.size(0), k = (int)x.size(1);
+  TORCH_CHECK(q.numel() >= (int64_t)rows * k, "q too small");
+  TORCH_CHECK(sf.numel() >= (int64_t)((rows + 127) / 128) * (k / 128) * 512, "sf too small");
+  rc(zs_quant_mxf8(ptr(x), rows, k, k, ptr<uint8_t>(q), ptr<uint8_t>(sf), stream()), "zs_quant_mxf8");
+}
+
+void add_rmsnorm_quant(const Tensor& residual, const OptT& delta, int64_t n_terms,
+                       int64_t d_row_stride, int64_t d_term_stride, const Tensor& weight,
+                       double w_offset, double eps, int64_t rows, const OptT& normed,
+                       const OptT& q, const OptT& sf) {
+  check_cuda(residual, "residual");
+  check_opt(delta, "delta");
+  check_opt(normed, "normed");
+  check_opt(q, "q");
+  check_opt(sf, "sf");
+  const int hidden = (int)residual.size(-1);
+  TORCH_CHECK(residual.numel() >= rows * hidden, "residual too small");
+  rc(zs_add_rmsnorm_quant(ptr(residual), optptr(delta), (int)n_terms, d_row_stride, d_term_stride,
+                          ptr(weight), (float)w_offset, (float)eps, (int)rows, hidden,
+                          optptr(normed), optptr<uint8_t>(q), optptr<uint8_t>(sf), stream()),
+     "zs_add_rmsnorm_quant");
+}
+
+void embed_rmsnorm_quant(const Tensor& ids, const Tensor& embed, const Tensor& hidden,
+                         const Tensor& weight, double w_offset, double eps, int64_t rows,
+                         const OptT& normed, const OptT& q, const OptT& sf) {
+  check_cuda(ids, "ids");
+  check_cuda(embed, "embed");
+  check_cuda(hidden, "hidden");
+  TORCH_CHECK(ids.scalar_type() == at::kInt, "ids must be int32");
+  rc(zs_embed_rmsnorm_quant(ptr<const int>(ids), ptr(embed), ptr(hidden), ptr(weight),
+                            (float)w_offset, (float)eps, (int)rows, (int)embed.size(1),
+                            optptr(normed), optptr<uint8_t>(q), optptr<uint8_t>(sf), stream()),
+     "zs_embed_rmsnorm_quant");
+}
+
+void argmax_reduce(const Tensor& keys, int64_t rows, int64_t tiles, const OptT& ids,
+                   const OptT& vals, const OptT& out_keys) {
+  check_cuda(keys, "keys");
+  rc(zs_argmax_reduce(ptr<const unsigned long long>(keys), (int)rows, (int)tiles,
+                      optptr<int>(ids), optptr<float>(vals), optptr<unsigned long long>(out_keys),
+                      stream()),
+     "zs_argmax_reduce");
+}
+
+void gdn(bool prefill, const Tensor& proj, int64_t num_k_heads, int64_t num_v_heads,
+         const Tensor& conv_w, const Tensor& conv_state, const Tensor& ssm_state,
+         const Tensor& a_log, const Tensor& dt_bias, const Tensor& norm_w, double eps,
+         const Tensor& slots, const Tensor& positions, int64_t rows, const OptT& out_bf16,
+         const OptT& out_q, const OptT& out_sf, const OptT& seq_start, int64_t num_seqs,
+         const OptT& ckpt_rows, const OptT& ckpt_slots, int64_t max_ckpt, const OptT& err) {
+  check_cuda(proj, "proj");
+  check_cuda(ssm_state, "ssm_state");
+  check_cuda(conv_state, "conv_state");
+  TORCH_CHECK(ssm_state.scalar_type() == at::kFloat, "ssm_state must be f32");
+  TORCH_CHECK(a_log.scalar_type() == at::kFloat && dt_bias.scalar_type() == at::kFloat,
+              "a_log/dt_bias must be f32");
+  GdnArgs g{};
+  g.proj = ptr(proj);
+  g.ld_proj = (int)proj.size(-1);
+  g.num_k_heads = (int)num_k_heads;
+  g.num_v_heads = (int)num_v_heads;
+  g.head_k = 128;
+  g.head_v = 128;
+  g.conv_w = ptr(conv_w);
+  g.conv_state = ptr(conv_state);
+  g.ssm_state = ptr<float>(ssm_state);
+  g.a_log = ptr<const float>(a_log);
+  g.dt_bias = ptr<const float>(dt_bias);
+  g.norm_w = ptr(norm_w);
+  g.eps = (float)eps;
+  g.slots = ptr<const int>(slots);
+  g.positions = ptr<const int>(positions);
+  g.rows = (int)rows;
+  g.out_bf16 = optptr(out_bf16);
+  g.out_q = optptr<uint8_t>(out_q);
+  g.out_sf = optptr<uint8_t>(out_sf);
+  g.seq_start = optptr<const int>(seq_start);
+  g.num_seqs = (int)num_seqs;
+  g.ckpt_rows = optptr<const int>(ckpt_rows);
+  g.ckpt_slots = optptr<const int>(ckpt_slots);
+  g.max_ckpt = (int)max_ckpt;
+  g.err = optptr<int>(err);
+  rc(prefill ? zs_gdn_prefill(&g, stream()) : zs_gdn_decode(&g, stream()), "zs_gdn");
+}
+
+AttnArgs make_attn(const Tensor& qkv, int64_t num_q_heads, int64_t num_kv_heads,
+                   int64_t rotary_dim, double rope_theta, const Tensor& q_norm_w,
+                   const Tensor& k_norm_w, double eps, const Tensor& k_cache,
+                   const Tensor& v_cache, int64_t page_size, const Tensor& page_table,
+                   const Tensor& slots, const Tensor& positions, int64_t rows,
+                   const Tensor& q_out, const Tensor& gate_out) {
+  check_cuda(qkv, "qkv");
+  check_cuda(k_cache, "k_cache");
+  check_cuda(v_cache, "v_cache");
+  check_cuda(page_table, "page_table");
+  TORCH_CHECK(page_table.scalar_type() == at::kInt, "page_table must be int32");
+  AttnArgs a{};
+  a.qkv = ptr(qkv);
+  a.ld_qkv = (int)qkv.size(-1);
+  a.num_q_heads = (int)num_q_heads;
+  a.num_kv_heads = (int)num_kv_heads;
+  a.head_dim = 256;
+  a.rotary_dim = (int)rotary_dim;
+  a.rope_theta = (float)rope_theta;
+  a.q_norm_w = ptr(q_norm_w);
+  a.k_norm_w = ptr(k_norm_w);
+  a.eps = (float)eps;
+  a.k_cache = ptr(k_cache);
+  a.v_cache = ptr(v_cache);
+  a.page_size = (int)page_size;
+  a.page_table = ptr<const int>(page_table);
+  a.max_pages = (int)page_table.size(1);
+  a.slots = ptr<const int>(slots);
+  a.positions = ptr<const int>(positions);
+  a.rows = (int)rows;
+  a.q_out = ptr(q_out);
+  a.gate_out = ptr(gate_out);
+  return a;
+}
+
+void attn_prologue(const Tensor& qkv, int64_t num_q_heads, int64_t num_kv_heads,
+                   int64_t rotary_dim, double rope_theta, const Tensor& q_norm_w,
+                   const Tensor& k_norm_w, double eps, const Tensor& k_cache,
+                   const Tensor& v_cache, int64_t page_size, const Tensor& page_table,
+                   const Tensor& slots, const Tensor& positions, int64_t rows,
+                   const Tensor& q_out, const Tensor& gate_out) {
+  AttnArgs a = make_attn(qkv, num_q_heads, num_kv_heads, rotary_dim, rope_theta, q_norm_w,
+                         k_norm_w, eps, k_cache, v_cache, page_size, page_table, slots,
+                         positions, rows, q_out, gate_out);
+  rc(zs_attn_prologue(&a, stream()), "zs_attn_prologue");
+}
+
+void attn_decode(const Tensor& q_out, const Tensor& gate_out, int64_t num_q_heads,
+                 int64_t num_kv_heads, const Tensor& k_cache, const Tensor& v_cache,
+                 int64_t page_size, const Tensor& page_table, const Tensor& slots,
+                 const Tensor& seq_lens, int64_t rows, const Tensor& partial, int64_t num_splits,
+                 double sm_scale, const OptT& out_bf16, const OptT& out_q, const OptT& out_sf) {
+  check_cuda(q_out, "q_out");
+  check_cuda(partial, "partial");
+  TORCH_CHECK(partial.numel() >= rows * num_q_heads * num_splits * 260, "partial too small");
+  AttnArgs a{};
+  a.num_q_heads = (int)num_q_heads;
+  a.num_kv_heads = (int)num_kv_heads;
+  a.head_dim = 256;
+  a.k_cache = ptr(k_cache);
+  a.v_cache = ptr(v_cache);
+  a.page_size = (int)page_size;
+  a.page_table = ptr<const int>(page_table);
+  a.max_pages = (int)page_table.size(1);
+  a.slots = ptr<const int>(slots);
+  a.seq_lens = ptr<const int>(seq_lens);
+  a.rows = (int)rows;
+  a.q_out = ptr(q_out);
+  a.gate_out = ptr(gate_out);
+  a.partial = ptr<float>(partial);
+  a.num_splits = (int)num_splits;
+  a.sm_scale = (float)sm_scale;
+  a.out_bf16 = optptr(out_bf16);
+  a.out_q = optptr<uint8_t>(out_q);
+  a.out_sf = optptr<uint8_t>(out_sf);
+  rc(zs_attn_decode(&a, stream()), "zs_attn_decode");
+}
+
+void moe_route(const Tensor& logits, int64_t rows, int64_t num_experts, int64_t top_k,
+               bool norm_topk, int64_t scoring, const OptT& bias, int64_t n_group,
+               int64_t topk_group, double routed_scale, int64_t shared_gate_col,
+               int64_t expert_begin, int64_t expert_end, bool has_shared, const Tensor& topk_ids,
+               const Tensor& topk_w, const Tensor& group_count, const Tensor& group_offset,
+               const Tensor& chunk_prefix, const Tensor& pair_slot, const Tensor& row_dst,
+               const Tensor& row_scale, const Tensor& x_q, const Tensor& x_sf,
+               const Tensor& xg_q, const Tensor& xg_sf, const OptT& err) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat, "logits must be f32");
+  MoeRouteArgs a{};
+  a.logits = ptr<const float>(logits);
+  a.ld_logits = (int)logits.size(-1);
+  a.rows = (int)rows;
+  a.num_experts = (int)num_experts;
+  a.top_k = (int)top_k;
+  a.norm_topk = norm_topk ? 1 : 0;
+  a.scoring = (int)scoring;
+  a.bias = optptr<const float>(bias);
+  a.n_group = (int)n_group;
+  a.topk_group = (int)topk_group;
+  a.routed_scale = (float)routed_scale;
+  a.shared_gate_col = (int)shared_gate_col;
+  a.expert_begin = (int)expert_begin;
+  a.expert_end = (int)expert_end;
+  a.has_shared = has_shared ? 1 : 0;
+  a.topk_ids = ptr<int>(topk_ids);
+  a.topk_w = ptr<float>(topk_w);
+  a.group_count = ptr<int>(group_count);
+  a.group_offset = ptr<int>(group_offset);
+  a.chunk_prefix = ptr<int>(chunk_prefix);
+  a.pair_slot = ptr<int>(pair_slot);
+  a.row_dst = ptr<int>(row_dst);
+  a.row_scale = ptr<float>(row_scale);
+  a.max_grouped_rows = (int)(xg_q.numel() / x_q.size(-1));
+  a.x_q = ptr<const uint8_t>(x_q);
+  a.x_sf = ptr<const uint8_t>(x_sf);
+  a.hidden = (int)x_q.size(-1);
+  a.xg_q = ptr<uint8_t>(xg_q);
+  a.xg_sf = ptr<uint8_t>(xg_sf);
+  a.err = optptr<int>(err);
+  rc(zs_moe_route(&a, stream()), "zs_moe_route");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "zstep_b200 sm_100a kernels";
+  m.def("gemm_mxf8", &gemm_mxf8);
+  m.def("quant_mxf8", &quant_mxf8);
+  m.def("add_rmsnorm_quant", &add_rmsnorm_quant);
+  m.def("embed_rmsnorm_quant", &embed_rmsnorm_quant);
+  m.def("argmax_reduce", &argmax_reduce);
+  m.def("gdn_decode", [](const Tensor& proj, int64_t hk, int64_t hv, const Tensor& conv_w,
+                         const Tensor& conv_state, const Tensor& ssm_state, const Tensor& a_log,
+                         const Tensor& dt_bias, const Tensor& norm_w, double eps,
+                         const Tensor& slots, const Tensor& positions, int64_t rows,
+                         const OptT& out_bf16, const OptT& out_q, const OptT& out_sf,
+                         const OptT& err) {
+    gdn(false, proj, hk, hv, conv_w, conv_state, ssm_state, a_log, dt_bias, norm_w, eps, slots,
+        positions, rows, out_bf16, out_q, out_sf, std::nullopt, 0, std::nullopt, std::nullopt, 0,
+        err);
+  });
+  m.def("gdn_prefill", [](const Tensor& proj, int64_t hk, int64_t hv, const Tensor& conv_w,
+                          const Tensor& conv_state, const Tensor& ssm_state, const Tensor& a_log,
+                          const Tensor& dt_bias, const Tensor& norm_w, double eps,
+                          const Tensor& slots, const Tensor& positions, int64_t rows,
+                          const OptT& out_bf16, const OptT& out_q, const OptT& out_sf,
+                          const Tensor& seq_start, int64_t num_seqs, const OptT& ckpt_rows,
+                          const OptT& ckpt_slots, int64_t max_ckpt, const OptT& err) {
+    gdn(true, proj, hk, hv, conv_w, conv_state, ssm_state, a_log, dt_bias, norm_w, eps, slots,
+        positions, rows, out_bf16, out_q, out_sf, seq_start, num_seqs, ckpt_rows, ckpt_slots,
+        max_ckpt, err);
+  });
+  m.def("attn_prologue", &attn_prologue);
+  m.def("attn_decode", &attn_decode);
+  m.def("moe_route", &moe_route);
+}

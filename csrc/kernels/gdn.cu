@@ -1,0 +1,320 @@
+// GatedDeltaNet (Qwen3.5 linear attention) for sm_100a.
+//
+// One CTA owns one (sequence, value head) pair and fuses the whole layer body:
+//   causal depthwise conv (k=4) + SiLU on the q/k/v channels of that head,
+//   L2-normalisation of q and k (q additionally scaled by 1/sqrt(dk)),
+//   beta = sigmoid(b), g = exp(-exp(A_log) * softplus(a + dt_bias)),
+//   delta-rule update of the fp32 state S[dv, dk]:
+//       S = g*S ;  kv = S k ;  S += (beta*(v - kv)) k^T ;  o = S q
+//   gated RMSNorm o -> bf16(o * rstd) * w * silu(z), optionally quantized to MXFP8
+//   for the out_proj GEMM.
+// The state row (128 fp32) of each value channel is split across 4 threads (32
+// coefficients each), so a CTA of 512 threads streams the whole 64 KiB state with
+// 128-byte contiguous accesses per thread; the state loads are issued first so the
+// conv/normalisation prologue overlaps their latency.  Decode is one token per CTA;
+// prefill walks the sequence's tokens with the state held in registers and
+// snapshots it into checkpoint slots at the requested rows (automatic prefix caching
+// of recurrent state).
+//
+// Reference parity: worker/zstep_worker/kernels_sm120/qwen35_ops.py:659-935 (conv,
+// delta rule, gated norm; state stored [V, K]) and the fused CUDA decode/prefill
+// kernels in kernels_sm120/csrc/qwen35_ops_kernels.cu:354-1067 (checkpoint save and
+// restore per row).
+#include "sm100_common.cuh"
+#include "zs_kernels.h"
+
+namespace zs {
+namespace gdn {
+
+constexpr int DK = 128;
+constexpr int DV = 128;
+constexpr int THREADS = 512;  // 128 value rows x 4 k-quarters
+
+struct Smem {
+  float q[DK];
+  float k[DK];
+  float v[DV];
+  float o[DV];
+  float conv[3 * DK + DV][3];  // running conv window (prefill)
+  float red[16];
+  float scal[4];
+};
+
+__device__ __forceinline__ float bf(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+__device__ __forceinline__ float block_sum_512(float v, float* red) {
+  v = warp_sum(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < THREADS / 32; ++i) t += red[i];
+  return t;
+}
+
+// Conv + SiLU for the head's 384 channels of one token, writing q/k/v into smem.
+// `win` holds the previous 3 inputs per channel; it is shifted in place.
+__device__ __forceinline__ void conv_token(const GdnArgs& a, int row, int kh, int vh, Smem& s,
+                                           bool fresh_window) {
+  const int t = threadIdx.x;
+  if (t < 2 * DK + DV) {
+    int ch;  // channel index in the conv space
+    if (t < DK) ch = kh * DK + t;                                  // q
+    else if (t < 2 * DK) ch = a.num_k_heads * DK + kh * DK + (t - DK);  // k
+    else ch = 2 * a.num_k_heads * DK + vh * DV + (t - 2 * DK);       // v
+    const __nv_bfloat16* proj = static_cast<const __nv_bfloat16*>(a.proj);
+    const __nv_bfloat16* w = static_cast<const __nv_bfloat16*>(a.conv_w) + (size_t)ch * 4;
+    const float x = bf(proj + (size_t)row * a.ld_proj + ch);
+    float* win = s.conv[t];
+    if (fresh_window) win[0] = win[1] = win[2] = 0.f;
+    float acc = bf(w + 0) * win[0] + bf(w + 1) * win[1] + bf(w + 2) * win[2] + bf(w + 3) * x;
+    win[0] = win[1];
+    win[1] = win[2];
+    // The conv window stores the bf16 input (matching the stored conv state).
+    win[2] = x;
+    const float y = siluf_(acc);
+    // Activation is rounded to bf16 like the reference's conv output buffer.
+    const float yb = __bfloat162float(__float2bfloat16_rn(y));
+    if (t < DK) s.q[t] = yb;
+    else if (t < 2 * DK) s.k[t - DK] = yb;
+    else s.v[t - 2 * DK] = yb;
+  }
+}
+
+// The conv window is double-buffered by position parity: the window that precedes the
+// token at position p (inputs p-3..p-1) lives in buffer p & 1.  A decode step reads
+// buffer p & 1 and writes buffer (p+1) & 1, so the CTAs of the value heads that share
+// a q/k head can all read the old q/k window while one of them writes the new one.
+__device__ __forceinline__ void load_window(const GdnArgs& a, int slot, int pos, int kh, int vh, Smem& s) {
+  const int t = threadIdx.x;
+  if (t < 2 * DK + DV) {
+    int ch;
+    if (t < DK) ch = kh * DK + t;
+    else if (t < 2 * DK) ch = a.num_k_heads * DK + kh * DK + (t - DK);
+    else ch = 2 * a.num_k_heads * DK + vh * DV + (t - 2 * DK);
+    const int conv_dim = 2 * a.num_k_heads * DK + a.num_v_heads * DV;
+    const __nv_bfloat16* cs = static_cast<const __nv_bfloat16*>(a.conv_state) +
+                              (((size_t)slot * 2 + (pos & 1)) * conv_dim + ch) * 3;
+    s.conv[t][0] = bf(cs + 0);
+    s.conv[t][1] = bf(cs + 1);
+    s.conv[t][2] = bf(cs + 2);
+  }
+}
+
+__device__ __forceinline__ void store_window(const GdnArgs& a, int slot, int pos, int kh, int vh,
+                                             Smem& s, bool owns_qk) {
+  const int t = threadIdx.x;
+  if (t < 2 * DK + DV) {
+    if (t < 2 * DK && !owns_qk) return;
+    int ch;
+    if (t < DK) ch = kh * DK + t;
+    else if (t < 2 * DK) ch = a.num_k_heads * DK + kh * DK + (t - DK);
+    else ch = 2 * a.num_k_heads * DK + vh * DV + (t - 2 * DK);
+    const int conv_dim = 2 * a.num_k_heads * DK + a.num_v_heads * DV;
+    __nv_bfloat16* cs = static_cast<__nv_bfloat16*>(a.conv_state) +
+                        (((size_t)slot * 2 + (pos & 1)) * conv_dim + ch) * 3;
+    cs[0] = __float2bfloat16_rn(s.conv[t][0]);
+    cs[1] = __float2bfloat16_rn(s.conv[t][1]);
+    cs[2] = __float2bfloat16_rn(s.conv[t][2]);
+  }
+}
+
+// L2-normalise q,k in smem, compute beta / decay for this token.
+__device__ __forceinline__ void qk_norm_and_gates(const GdnArgs& a, int row, int vh, Smem& s) {
+  const int t = threadIdx.x;
+  float qq = 0.f, kk = 0.f;
+  if (t < DK) qq = s.q[t] * s.q[t];
+  if (t < DK) kk = s.k[t] * s.k[t];
+  const float sq = block_sum_512(qq, s.red);
+  const float sk = block_sum_512(kk, s.red);
+  if (t < DK) {
+    s.q[t] = s.q[t] * rsqrtf(sq + 1e-6f) * rsqrtf((float)DK);
+    s.k[t] = s.k[t] * rsqrtf(sk + 1e-6f);
+  }
+  if (t == 0) {
+    const __nv_bfloat16* proj = static_cast<const __nv_bfloat16*>(a.proj) + (size_t)row * a.ld_proj;
+    const int zoff = 2 * a.num_k_heads * DK + a.num_v_heads * DV;
+    const int boff = zoff + a.num_v_heads * DV;
+    const int aoff = boff + a.num_v_heads;
+    const float b_raw = bf(proj + boff + vh);
+    const float a_raw = bf(proj + aoff + vh);
+    const float sp_in = a_raw + a.dt_bias[vh];
+    const float softplus = sp_in > 20.f ? sp_in : log1pf(__expf(sp_in));
+    s.scal[0] = sigmoidf_(b_raw);
+    s.scal[1] = __expf(-__expf(a.a_log[vh]) * softplus);
+  }
+  __syncthreads();
+}
+
+// Gated RMSNorm of s.o and output (bf16 and/or MXFP8).  Threads 0..127.
+__device__ __forceinline__ void gated_norm_out(const GdnArgs& a, int row, int vh, Smem& s) {
+  const int t = threadIdx.x;
+  float ov = t < DV ? s.o[t] : 0.f;
+  const float ss = block_sum_512(ov * ov, s.red);
+  if (t < DV) {
+    const float rstd = rsqrtf(ss / DV + a.eps);
+    const __nv_bfloat16* proj = static_cast<const __nv_bfloat16*>(a.proj) + (size_t)row * a.ld_proj;
+    const int zoff = 2 * a.num_k_heads * DK + a.num_v_heads * DV;
+    const float z = bf(proj + zoff + vh * DV + t);
+    const float w = bf(static_cast<const __nv_bfloat16*>(a.norm_w) + t);
+    const float nrm = __bfloat162float(__float2bfloat16_rn(ov * rstd)) * w;
+    const float y = nrm * siluf_(z);
+    const int width = a.num_v_heads * DV;
+    const int col = vh * DV + t;
+    if (a.out_bf16 != nullptr)
+      static_cast<__nv_bfloat16*>(a.out_bf16)[(size_t)row * width + col] = __float2bfloat16_rn(y);
+    if (a.out_q != nullptr) {
+      const float yb = __bfloat162float(__float2bfloat16_rn(y));
+      const float amax = warp_max(fabsf(yb));
+      const uint8_t code = mx_scale_e8m0(amax);
+      a.out_q[(size_t)row * width + col] = f32_to_e4m3(yb * mx_inv_scale(code));
+      if ((t & 31) == 0) {
+        const int kb = col >> 5;
+        a.out_sf[((size_t)(row >> 7) * (width >> 7) + (kb >> 2)) * 512 + sf_atom_offset(row & 127, kb & 3)] =
+            code;
+      }
+    }
+  }
+}
+
+// Delta-rule step for the 32 coefficients st[] of value row `vr`, k-quarter `kq`.
+__device__ __forceinline__ float delta_step(float (&st)[32], int vr, int kq, const Smem& s) {
+  const float beta = s.scal[0];
+  const float g = s.scal[1];
+  float kv = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    st[i] *= g;
+    kv += st[i] * s.k[kq * 32 + i];
+  }
+  kv += __shfl_xor_sync(0xffffffff, kv, 1);
+  kv += __shfl_xor_sync(0xffffffff, kv, 2);
+  const float delta = (s.v[vr] - kv) * beta;
+  float o = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    st[i] += s.k[kq * 32 + i] * delta;
+    o += st[i] * s.q[kq * 32 + i];
+  }
+  o += __shfl_xor_sync(0xffffffff, o, 1);
+  o += __shfl_xor_sync(0xffffffff, o, 2);
+  return o;
+}
+
+__global__ void __launch_bounds__(THREADS, 1) gdn_decode_kernel(const GdnArgs a) {
+  __shared__ Smem s;
+  const int row = blockIdx.x;
+  const int vh = blockIdx.y;
+  const int ratio = a.num_v_heads / a.num_k_heads;
+  const int kh = vh / ratio;
+  const int t = threadIdx.x;
+  const int vr = t >> 2, kq = t & 3;
+  const int slot = a.slots[row];
+  const int pos = a.positions[row];
+  const bool fresh = pos == 0;
+  float* sp = a.ssm_state + (((size_t)slot * a.num_v_heads + vh) * DV + vr) * DK + kq * 32;
+  float st[32];
+  if (!fresh) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float4 f = reinterpret_cast<const float4*>(sp)[i];
+      st[4 * i] = f.x; st[4 * i + 1] = f.y; st[4 * i + 2] = f.z; st[4 * i + 3] = f.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) st[i] = 0.f;
+  }
+  if (!fresh) load_window(a, slot, pos, kh, vh, s);
+  __syncthreads();
+  conv_token(a, row, kh, vh, s, fresh);
+  __syncthreads();
+  store_window(a, slot, pos + 1, kh, vh, s, (vh % ratio) == 0);
+  qk_norm_and_gates(a, row, vh, s);
+  const float o = delta_step(st, vr, kq, s);
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    reinterpret_cast<float4*>(sp)[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
+  if (kq == 0) s.o[vr] = o;
+  __syncthreads();
+  gated_norm_out(a, row, vh, s);
+}
+
+__global__ void __launch_bounds__(THREADS, 1) gdn_prefill_kernel(const GdnArgs a) {
+  __shared__ Smem s;
+  const int seq = blockIdx.x;
+  const int vh = blockIdx.y;
+  const int r0 = a.seq_start[seq], r1 = a.seq_start[seq + 1];
+  if (r0 >= r1) return;
+  const int ratio = a.num_v_heads / a.num_k_heads;
+  const int kh = vh / ratio;
+  const int t = threadIdx.x;
+  const int vr = t >> 2, kq = t & 3;
+  const int slot = a.slots[r0];
+  const int pos0 = a.positions[r0];
+  const bool fresh = pos0 == 0;
+  float* sp = a.ssm_state + (((size_t)slot * a.num_v_heads + vh) * DV + vr) * DK + kq * 32;
+  float st[32];
+  if (!fresh) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float4 f = reinterpret_cast<const float4*>(sp)[i];
+      st[4 * i] = f.x; st[4 * i + 1] = f.y; st[4 * i + 2] = f.z; st[4 * i + 3] = f.w;
+    }
+    load_window(a, slot, pos0, kh, vh, s);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) st[i] = 0.f;
+  }
+  __syncthreads();
+  int ck = 0;  // next checkpoint index for this sequence
+  for (int row = r0; row < r1; ++row) {
+    conv_token(a, row, kh, vh, s, fresh && row == r0);
+    __syncthreads();
+    qk_norm_and_gates(a, row, vh, s);
+    const float o = delta_step(st, vr, kq, s);
+    if (kq == 0) s.o[vr] = o;
+    __syncthreads();
+    gated_norm_out(a, row, vh, s);
+    // Snapshot state (+ conv window) into checkpoint slots requested at this row.
+    while (a.ckpt_rows != nullptr && ck < a.max_ckpt && a.ckpt_rows[seq * a.max_ckpt + ck] == row) {
+      const int cslot = a.ckpt_slots[seq * a.max_ckpt + ck];
+      float* cp = a.ssm_state + (((size_t)cslot * a.num_v_heads + vh) * DV + vr) * DK + kq * 32;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        reinterpret_cast<float4*>(cp)[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
+      store_window(a, cslot, pos0 + (row - r0) + 1, kh, vh, s, (vh % ratio) == 0);
+      ++ck;
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    reinterpret_cast<float4*>(sp)[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
+  store_window(a, slot, pos0 + (r1 - r0), kh, vh, s, (vh % ratio) == 0);
+}
+
+}  // namespace gdn
+}  // namespace zs
+
+extern "C" int zs_gdn_decode(const GdnArgs* args, cudaStream_t stream) {
+  const GdnArgs& a = *args;
+  if (a.head_k != zs::gdn::DK || a.head_v != zs::gdn::DV || a.num_k_heads <= 0 ||
+      a.num_v_heads % a.num_k_heads != 0)
+    return -1;
+  if (a.rows == 0) return 0;
+  dim3 grid(a.rows, a.num_v_heads);
+  zs::gdn::gdn_decode_kernel<<<grid, zs::gdn::THREADS, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+extern "C" int zs_gdn_prefill(const GdnArgs* args, cudaStream_t stream) {
+  const GdnArgs& a = *args;
+  if (a.head_k != zs::gdn::DK || a.head_v != zs::gdn::DV || a.num_k_heads <= 0 ||
+      a.num_v_heads % a.num_k_heads != 0 || a.seq_start == nullptr)
+    return -1;
+  if (a.num_seqs == 0) return 0;
+  dim3 grid(a.num_seqs, a.num_v_heads);
+  zs::gdn::gdn_prefill_kernel<<<grid, zs::gdn::THREADS, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}

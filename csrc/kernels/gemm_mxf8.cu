@@ -1,0 +1,424 @@
+// Block-scaled MXFP8 GEMM for sm_100a: tcgen05.mma.kind::mxf8f6f4.block_scale with
+// TMA-fed shared-memory operands and TMEM accumulators.
+//
+// Orientation ("swap-AB"): the weight matrix is the MMA's M side (128 output features
+// per tile) and the tokens are the N side (16..128 per pass), so decode batches of a
+// handful of tokens per expert still issue full-height MMAs and the kernel streams the
+// weights at HBM rate.  One persistent CTA per SM walks a static list of work items
+// (group, 128-feature tile, 128-token chunk).  Roles inside a CTA:
+//   warps 0-3 : epilogue (TMEM -> registers -> fused op -> global)
+//   warp 4    : TMA / bulk-copy producer
+//   warp 5    : MMA issuer (one elected thread) + scale-factor TMEM staging
+// Accumulators are double-buffered in TMEM so the epilogue of tile i overlaps the
+// main loop of tile i+1.
+//
+// Operand formats (all produced by this library's quantizers):
+//   A  weights      e4m3 [G * Npad, K], K contiguous; Npad % 128 == 0, K % 128 == 0
+//   SFA weight sf   e8m0 [G, Npad/128, K/128, 512]   (128-row x 4-block atoms)
+//   B  activations  e4m3 [rows, K] in per-group segments starting at multiples of 128
+//   SFB act sf      e8m0 [rows/128, K/128, 512]
+// Atom byte layout: row r = r0 + 32*r1 (r0 < 32) and 32-wide K block j (j < 4) live
+// at byte r0*16 + r1*4 + j, which is what tcgen05.cp.32x128b.warpx4 expects.
+//
+// Reference parity: replaces the reference's Triton grouped MoE GEMMs and skinny
+// linears (worker/zstep_worker/kernels_sm120/qwen35_ops.py:1226-1438) and the
+// b12x MXFP8 linears (kernels_sm120/b12x_dsv41.py:370) with one tcgen05 kernel.
+#include "sm100_common.cuh"
+#include "zs_kernels.h"
+
+namespace zs {
+namespace gemm {
+
+constexpr int BM = 128;          // weight rows per tile (MMA M)
+constexpr int BK = 128;          // K elements (bytes) per stage = one 128B swizzle span
+constexpr int BN = 128;          // max tokens per work item (MMA N <= BN)
+constexpr int STAGES = 6;
+constexpr int A_BYTES = BM * BK;             // 16 KiB
+constexpr int B_BYTES = BN * BK;             // 16 KiB
+constexpr int SF_BYTES = 512;
+constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int ACC_COL0 = 0;                  // acc buffer b at column b*BN
+constexpr int SFA_COL = 2 * BN;              // 4 columns
+constexpr int SFB_COL = 2 * BN + 4;          // 4 columns
+
+struct SmemLayout {
+  uint8_t a[STAGES][A_BYTES];
+  uint8_t b[STAGES][B_BYTES];
+  uint8_t sfa[STAGES][SF_BYTES];
+  uint8_t sfb[STAGES][SF_BYTES];
+  float xch[16][64];  // epilogue exchange (gate/up pairing)
+  unsigned long long red[4][16];  // epilogue exchange (argmax)
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+struct Item {
+  int g, m, c, count, seg_off;
+};
+
+__device__ __forceinline__ bool get_item(const GemmMxf8Args& p, int idx, Item& it) {
+  const int m_tiles = p.n_pad / BM;
+  if (p.chunk_prefix == nullptr) {
+    const int chunks = (p.m_rows + BN - 1) / BN;
+    if (idx >= chunks * m_tiles) return false;
+    it.g = 0;
+    it.m = idx % m_tiles;
+    it.c = idx / m_tiles;
+    it.seg_off = 0;
+    it.count = min(BN, p.m_rows - it.c * BN);
+    return true;
+  }
+  const int total_chunks = __ldg(p.chunk_prefix + p.groups);
+  if (idx >= total_chunks * m_tiles) return false;
+  const int chunk = idx / m_tiles;
+  it.m = idx % m_tiles;
+  int lo = 0, hi = p.groups;  // largest g with prefix[g] <= chunk
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(p.chunk_prefix + mid) <= chunk) lo = mid; else hi = mid;
+  }
+  it.g = lo;
+  it.c = chunk - __ldg(p.chunk_prefix + lo);
+  it.seg_off = __ldg(p.group_offset + lo);
+  it.count = min(BN, __ldg(p.group_count + lo) - it.c * BN);
+  return true;
+}
+
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t phase, int* err,
+                                              volatile int* abort_flag) {
+  for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {
+    if (mbar_try_wait(bar, phase)) return true;
+    if (*abort_flag) return false;
+    if (i > 64) __nanosleep(64);
+  }
+  report_error(err, kErrMbarTimeout);
+  *abort_flag = 1;
+  return false;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_pack(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                 const __grid_constant__ CUtensorMap tmap_b, const GemmMxf8Args p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  SmemLayout& s = *reinterpret_cast<SmemLayout*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = warp_id();
+  const int lane = lane_id();
+  volatile int* abort_flag = &s.abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_empty[i], 4);
+    }
+    mbar_init(&s.drain, 1);
+    s.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&s.tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  const int k_tiles = p.k / BK;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t issued = 0;  // total stage fills issued
+      Item it;
+      for (int idx = blockIdx.x; get_item(p, idx, it) && !*abort_flag; idx += gridDim.x) {
+        const int n16 = (it.count + 15) >> 4;
+        const int a_row = it.g * p.n_pad + it.m * BM;
+        const int b_row = it.seg_off + it.c * BN;
+        const uint8_t* sfa_src =
+            p.sfa + ((size_t)(it.g * (p.n_pad / BM) + it.m) * k_tiles) * SF_BYTES;
+        const uint8_t* sfb_src = p.sfb + ((size_t)(b_row / BM) * k_tiles) * SF_BYTES;
+        const uint32_t bytes = A_BYTES + n16 * 16 * BK + 2 * SF_BYTES;
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          const int st = issued % STAGES;
+          const uint32_t ph = ((issued / STAGES) & 1) ^ 1;
+          if (!wait_or_abort(&s.empty[st], ph, p.err, abort_flag)) break;
+          mbar_expect_tx(&s.full[st], bytes);
+          tma_load_2d(s.a[st], &tmap_a, &s.full[st], kt * BK, a_row);
+          for (int j = 0; j < n16; ++j)
+            tma_load_2d(s.b[st] + j * 16 * BK, &tmap_b, &s.full[st], kt * BK, b_row + j * 16);
+          bulk_load(s.sfa[st], sfa_src + (size_t)kt * SF_BYTES, SF_BYTES, &s.full[st]);
+          bulk_load(s.sfb[st], sfb_src + (size_t)kt * SF_BYTES, SF_BYTES, &s.full[st]);
+          ++issued;
+        }
+      }
+      // Drain: wait (bounded) until every fill this thread issued has landed, so no
+      // copy is still writing shared memory when the CTA exits.
+      const uint32_t first = issued > STAGES ? issued - STAGES : 0;
+      for (uint32_t q = first; q < issued; ++q) {
+        if (!mbar_wait(&s.full[q % STAGES], (q / STAGES) & 1, nullptr)) {
+          report_error(p.err, kErrDrainTimeout);
+          break;
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t consumed = 0;
+      uint32_t acc_uses[2] = {0, 0};
+      int local = 0;
+      Item it;
+      for (int idx = blockIdx.x; get_item(p, idx, it) && !*abort_flag; idx += gridDim.x, ++local) {
+        const int buf = local & 1;
+        if (!wait_or_abort(&s.acc_empty[buf], (acc_uses[buf] & 1) ^ 1, p.err, abort_flag)) break;
+        ++acc_uses[buf];
+        tc_fence_after();
+        const uint32_t n_mma = ((it.count + 15) >> 4) << 4;
+        const uint32_t d_tmem = tmem + ACC_COL0 + buf * BN;
+        bool ok = true;
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          const int st = consumed % STAGES;
+          if (!wait_or_abort(&s.full[st], (consumed / STAGES) & 1, p.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t sfa_desc = make_smem_desc(smem_u32(s.sfa[st]), 0, 128, 0);
+          const uint64_t sfb_desc = make_smem_desc(smem_u32(s.sfb[st]), 0, 128, 0);
+          tmem_cp_32x128b_warpx4(tmem + SFA_COL, sfa_desc);
+          tmem_cp_32x128b_warpx4(tmem + SFB_COL, sfb_desc);
+          const uint32_t a_base = smem_u32(s.a[st]);
+          const uint32_t b_base = smem_u32(s.b[st]);
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb) {
+            const uint64_t adesc = make_smem_desc(a_base + kb * 32, 16, 1024, 2);
+            const uint64_t bdesc = make_smem_desc(b_base + kb * 32, 16, 1024, 2);
+            const uint32_t idesc = make_idesc_mxf8(BM, n_mma, kb, kb);
+            mma_mxf8(d_tmem, adesc, bdesc, idesc, (tmem + SFA_COL) | (uint32_t(kb) << 30),
+                     (tmem + SFB_COL) | (uint32_t(kb) << 30), (kt > 0 || kb > 0) ? 1u : 0u);
+          }
+          tc_commit(&s.empty[st]);
+          ++consumed;
+        }
+        if (!ok) break;
+        tc_commit(&s.acc_full[buf]);
+      }
+      // Make sure no MMA is still running before TMEM is released.
+      tc_commit(&s.drain);
+      if (!mbar_wait(&s.drain, 0, nullptr)) report_error(p.err, kErrDrainTimeout);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int q = warp;  // TMEM subpartition (lanes 32q .. 32q+31)
+    const int row_in_tile = q * 32 + lane;
+    uint32_t acc_uses[2] = {0, 0};
+    int local = 0;
+    Item it;
+    for (int idx = blockIdx.x; get_item(p, idx, it); idx += gridDim.x, ++local) {
+      const int buf = local & 1;
+      if (!wait_or_abort(&s.acc_full[buf], acc_uses[buf] & 1, p.err, abort_flag)) break;
+      ++acc_uses[buf];
+      tc_fence_after();
+      const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16) + ACC_COL0 + buf * BN;
+      const int n16 = (it.count + 15) >> 4;
+      const int seg_row0 = it.seg_off + it.c * BN;
+      const int n_glob = it.m * BM + row_in_tile;
+
+      if (p.epi_mode == kEpiSiluQuant) {
+        // Tile rows 0..63 are gate features, 64..127 the matching up features of
+        // intermediate columns [64m, 64m+64).  Pair them through shared memory,
+        // form silu(g)*u and quantize to MXFP8 (32-feature blocks = one warp).
+        for (int ch = 0; ch < n16; ++ch) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(t_base + ch * 16, r);
+          tmem_ld_wait();
+          if (q >= 2) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) s.xch[j][(q - 2) * 32 + lane] = __uint_as_float(r[j]);
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (q < 2) {
+            const int feat = it.m * 64 + q * 32 + lane;  // intermediate column
+            uint8_t* act = reinterpret_cast<uint8_t*>(p.out);
+#pragma unroll 4
+            for (int j = 0; j < 16; ++j) {
+              const int col = ch * 16 + j;
+              const float g = __uint_as_float(r[j]);
+              const float u = s.xch[j][q * 32 + lane];
+              const float h = siluf_(g) * u;
+              const float amax = warp_max(fabsf(h));
+              const uint8_t code = mx_scale_e8m0(amax);
+              if (col < it.count) {
+                const int row = seg_row0 + col;
+                act[(size_t)row * p.ldo + feat] = f32_to_e4m3(h * mx_inv_scale(code));
+                if (lane == 0) {
+                  const int kb = feat >> 5;
+                  uint8_t* sf = p.out_sf + ((size_t)(row >> 7) * (p.ldo >> 7) + (kb >> 2)) * 512;
+                  sf[sf_atom_offset(row & 127, kb & 3)] = code;
+                }
+              }
+            }
+          }
+          asm volatile("bar.sync 2, 128;" ::: "memory");
+        }
+      } else if (p.epi_mode == kEpiArgmaxPartial) {
+        // Vocab-tile argmax: reduce each token column over this tile's 128 rows into
+        // one packed (orderable logit, ~id) word; the max over words gives the largest
+        // logit with the smallest id on ties.
+        const bool valid_n = n_glob < p.n_valid;
+        unsigned long long* part = reinterpret_cast<unsigned long long*>(p.out);
+        for (int ch = 0; ch < n16; ++ch) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(t_base + ch * 16, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            unsigned long long key = valid_n ? pack_argmax(__uint_as_float(r[j]), n_glob) : 0ull;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+              const unsigned long long other = __shfl_xor_sync(0xffffffff, key, o);
+              key = other > key ? other : key;
+            }
+            if (lane == 0) s.red[q][j] = key;
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (q == 0 && lane < 16) {
+            const int col = ch * 16 + lane;
+            unsigned long long key = s.red[0][lane];
+#pragma unroll
+            for (int w = 1; w < 4; ++w) key = s.red[w][lane] > key ? s.red[w][lane] : key;
+            if (col < it.count) part[(size_t)(seg_row0 + col) * p.ldo + it.m] = key;
+          }
+          asm volatile("bar.sync 2, 128;" ::: "memory");
+        }
+      } else {
+        const bool valid_n = n_glob < p.n_valid;
+        for (int ch = 0; ch < n16; ++ch) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(t_base + ch * 16, r);
+          tmem_ld_wait();
+          if (!valid_n) continue;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int col = ch * 16 + j;
+            if (col >= it.count) break;
+            const int row = seg_row0 + col;
+            float v = __uint_as_float(r[j]);
+            if (p.epi_mode == kEpiStoreF32) {
+              reinterpret_cast<float*>(p.out)[(size_t)row * p.ldo + n_glob] = v;
+            } else if (p.epi_mode == kEpiScatterScaled) {
+              const int dst = __ldg(p.row_dst + row);
+              v *= __ldg(p.row_scale + row);
+              reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)dst * p.ldo + n_glob] =
+                  __float2bfloat16_rn(v);
+            } else {
+              reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)row * p.ldo + n_glob] =
+                  __float2bfloat16_rn(v);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+}  // namespace gemm
+}  // namespace zs
+
+// ------------------------------------------------------------------------------------
+// Host side
+// ------------------------------------------------------------------------------------
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 2-D e4m3 matrix [rows, k] (k contiguous) with a {128 x box_rows} 128B-swizzled box.
+int make_tmap_u8(CUtensorMap* m, const void* base, int64_t rows, int64_t k, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return -1;
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)k};
+  cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+int g_num_sms = 0;
+
+}  // namespace
+
+extern "C" int zs_gemm_mxf8(const GemmMxf8Args* args, cudaStream_t stream) {
+  using namespace zs::gemm;
+  const GemmMxf8Args& p = *args;
+  if (p.k % BK != 0 || p.n_pad % BM != 0 || p.k <= 0 || p.n_pad <= 0) return -10;
+  if ((reinterpret_cast<uintptr_t>(p.a) & 15) || (reinterpret_cast<uintptr_t>(p.b) & 15) ||
+      (reinterpret_cast<uintptr_t>(p.sfa) & 15) || (reinterpret_cast<uintptr_t>(p.sfb) & 15))
+    return -11;
+  if (p.b_rows % BM != 0) return -12;
+  CUtensorMap ta, tb;
+  if (make_tmap_u8(&ta, p.a, (int64_t)p.groups * p.n_pad, p.k, BM) != 0) return -13;
+  if (make_tmap_u8(&tb, p.b, p.b_rows, p.k, 16) != 0) return -14;
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  int grid = g_num_sms;
+  if (p.chunk_prefix == nullptr) {
+    const int items = ((p.m_rows + BN - 1) / BN) * (p.n_pad / BM);
+    if (items == 0) return 0;
+    grid = items < grid ? items : grid;
+  } else if (p.max_items > 0 && p.max_items < grid) {
+    grid = p.max_items;
+  }
+  const size_t smem = sizeof(SmemLayout) + 1024;
+  cudaFuncSetAttribute(gemm_mxf8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  gemm_mxf8_kernel<<<grid, NUM_THREADS, smem, stream>>>(ta, tb, p);
+  return cudaGetLastError() == cudaSuccess ? 0 : -15;
+}

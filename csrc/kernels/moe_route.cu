@@ -1,0 +1,242 @@
+// MoE routing for the grouped MXFP8 expert GEMMs.
+//
+//   route_topk : one warp per token.  Softmax (Qwen) or sigmoid + correction bias with
+//                grouped top-k (DeepSeek-V3 style) scoring, top-k with the
+//                smallest-index tie break, optional renormalisation, then a slot in
+//                the expert's segment via an atomic per-expert counter.  Experts
+//                outside [expert_begin, expert_end) belong to other expert-parallel
+//                ranks and are skipped; the shared expert (if any) is an extra local
+//                group that every token visits with weight sigmoid(shared gate).
+//   offsets    : one CTA; 128-row aligned segment offsets and the per-group prefix
+//                of 128-token chunks that the GEMM's work list is built from.
+//   scatter    : copies each routed token's MXFP8 row and its scale bytes into the
+//                expert's segment and records (destination pair row, weight) for the
+//                down-projection epilogue.
+//
+// Reference parity: router softmax-256/top-8/renorm + shared gate
+// (worker/zstep_worker/kernels_sm120/qwen35_ops.py:1165-1222), moe_align_block_size
+// (csrc/qwen35_ops_kernels.cu:26), sigmoid/sqrt-softplus routers
+// (kernels_sm120/moe_router.py:31-110).
+#include "sm100_common.cuh"
+#include "zs_kernels.h"
+
+namespace zs {
+namespace moe {
+
+constexpr int kMaxExperts = 512;
+constexpr int kMaxTopK = 16;
+
+__device__ __forceinline__ void warp_argmax(float& v, int& i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v2 = __shfl_xor_sync(0xffffffff, v, o);
+    const int i2 = __shfl_xor_sync(0xffffffff, i, o);
+    if (v2 > v || (v2 == v && i2 < i)) {
+      v = v2;
+      i = i2;
+    }
+  }
+}
+
+__global__ void route_topk_kernel(const MoeRouteArgs a) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= a.rows) return;
+  const int E = a.num_experts;
+  const int per = (E + 31) / 32;  // experts per lane: e = lane + 32*j
+  const float* lg = a.logits + (size_t)row * a.ld_logits;
+  float score[kMaxExperts / 32];   // routing weight source
+  float choice[kMaxExperts / 32];  // selection key
+  if (a.scoring == 0) {
+    float mx = -INFINITY;
+    for (int j = 0; j < per; ++j) {
+      const int e = lane + 32 * j;
+      score[j] = e < E ? lg[e] : -INFINITY;
+      mx = fmaxf(mx, score[j]);
+    }
+    mx = warp_max(mx);
+    float sum = 0.f;
+    for (int j = 0; j < per; ++j) {
+      score[j] = (lane + 32 * j) < E ? __expf(score[j] - mx) : 0.f;
+      sum += score[j];
+    }
+    sum = warp_sum(sum);
+    for (int j = 0; j < per; ++j) {
+      score[j] /= sum;
+      choice[j] = (lane + 32 * j) < E ? score[j] : -INFINITY;
+    }
+  } else {
+    for (int j = 0; j < per; ++j) {
+      const int e = lane + 32 * j;
+      score[j] = e < E ? sigmoidf_(lg[e]) : 0.f;
+      choice[j] = e < E ? score[j] + (a.bias ? a.bias[e] : 0.f) : -INFINITY;
+    }
+    if (a.n_group > 1) {
+      // Group score = sum of the two best choice scores in the group; keep the best
+      // topk_group groups, mask the rest.
+      const int gsize = E / a.n_group;
+      __shared__ float gscore_s[8][64];
+      float* gs = gscore_s[threadIdx.x >> 5];
+      for (int g = 0; g < a.n_group; ++g) {
+        float b1 = -INFINITY, b2 = -INFINITY;
+        for (int j = 0; j < per; ++j) {
+          const int e = lane + 32 * j;
+          if (e >= g * gsize && e < (g + 1) * gsize) {
+            const float c = choice[j];
+            if (c > b1) { b2 = b1; b1 = c; } else if (c > b2) { b2 = c; }
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float o1 = __shfl_xor_sync(0xffffffff, b1, o);
+          const float o2 = __shfl_xor_sync(0xffffffff, b2, o);
+          const float n1 = fmaxf(b1, o1);
+          const float n2 = fmaxf(fminf(b1, o1), fmaxf(b2, o2));
+          b1 = n1;
+          b2 = n2;
+        }
+        if (lane == 0) gs[g] = b1 + b2;
+      }
+      __syncwarp();
+      // Select topk_group groups (ties -> lower group index).
+      uint64_t keep = 0;
+      for (int r = 0; r < a.topk_group; ++r) {
+        int best = -1;
+        float bv = -INFINITY;
+        for (int g = 0; g < a.n_group; ++g)
+          if (!((keep >> g) & 1) && (best < 0 || gs[g] > bv)) { best = g; bv = gs[g]; }
+        keep |= 1ull << best;
+      }
+      for (int j = 0; j < per; ++j) {
+        const int e = lane + 32 * j;
+        if (e < E && !((keep >> (e / gsize)) & 1)) choice[j] = -INFINITY;
+      }
+      __syncwarp();
+    }
+  }
+  // Top-k by choice key.
+  int ids[kMaxTopK];
+  float wts[kMaxTopK];
+  float wsum = 0.f;
+  for (int k = 0; k < a.top_k; ++k) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int j = 0; j < per; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && (choice[j] > bv || (choice[j] == bv && e < bi))) { bv = choice[j]; bi = e; }
+    }
+    warp_argmax(bv, bi);
+    // Owner lane removes the winner and publishes its weight.
+    float w = 0.f;
+    for (int j = 0; j < per; ++j)
+      if (lane + 32 * j == bi) { w = score[j]; choice[j] = -INFINITY; }
+    w = __shfl_sync(0xffffffff, w, bi & 31);
+    ids[k] = bi;
+    wts[k] = w;
+    wsum += w;
+  }
+  if (lane == 0) {
+    const int K1 = a.top_k + 1;
+    const int G_local = a.expert_end - a.expert_begin;
+    for (int k = 0; k < a.top_k; ++k) {
+      float w = wts[k];
+      if (a.norm_topk) w = w / (wsum > 0.f ? wsum : 1.f);
+      w *= a.routed_scale;
+      a.topk_ids[row * a.top_k + k] = ids[k];
+      a.topk_w[row * a.top_k + k] = w;
+      int slot = -1;
+      if (ids[k] >= a.expert_begin && ids[k] < a.expert_end)
+        slot = atomicAdd(a.group_count + (ids[k] - a.expert_begin), 1);
+      a.pair_slot[row * K1 + k] = slot;
+    }
+    int sslot = -1;
+    if (a.has_shared) sslot = atomicAdd(a.group_count + G_local, 1);
+    a.pair_slot[row * K1 + a.top_k] = sslot;
+  }
+}
+
+__global__ void offsets_kernel(const MoeRouteArgs a, int groups) {
+  // Single CTA of 1024 threads; groups <= kMaxExperts + 1.
+  __shared__ int seg[kMaxExperts + 2];
+  __shared__ int chk[kMaxExperts + 2];
+  const int t = threadIdx.x;
+  for (int g = t; g < groups; g += blockDim.x) {
+    const int c = a.group_count[g];
+    seg[g] = (c + 127) & ~127;
+    chk[g] = (c + 127) >> 7;
+  }
+  __syncthreads();
+  if (t == 0) {
+    int so = 0, co = 0;
+    for (int g = 0; g < groups; ++g) {
+      const int s = seg[g], c = chk[g];
+      a.group_offset[g] = so;
+      a.chunk_prefix[g] = co;
+      so += s;
+      co += c;
+    }
+    a.chunk_prefix[groups] = co;
+    if (so > a.max_grouped_rows) {
+      report_error(a.err, kErrBadShape);
+      // Make the GEMMs do nothing rather than run past the buffer.
+      for (int g = 0; g <= groups; ++g) a.chunk_prefix[g] = 0;
+    }
+  }
+}
+
+// One warp per (row, pair): copy hidden bytes + hidden/32 scale bytes.
+__global__ void scatter_kernel(const MoeRouteArgs a) {
+  const int K1 = a.top_k + 1;
+  const int pair = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (pair >= a.rows * K1) return;
+  const int row = pair / K1, j = pair % K1;
+  const int slot = a.pair_slot[pair];
+  if (slot < 0) return;
+  int g;
+  float w;
+  if (j < a.top_k) {
+    g = a.topk_ids[row * a.top_k + j] - a.expert_begin;
+    w = a.topk_w[row * a.top_k + j];
+  } else {
+    g = a.expert_end - a.expert_begin;
+    w = a.shared_gate_col >= 0 ? sigmoidf_(a.logits[(size_t)row * a.ld_logits + a.shared_gate_col]) : 1.f;
+  }
+  const int dst = a.group_offset[g] + slot;
+  if (dst >= a.max_grouped_rows) return;  // overflow (reported by offsets_kernel)
+  const uint4* src = reinterpret_cast<const uint4*>(a.x_q + (size_t)row * a.hidden);
+  uint4* dq = reinterpret_cast<uint4*>(a.xg_q + (size_t)dst * a.hidden);
+  for (int c = lane; c < a.hidden / 16; c += 32) dq[c] = src[c];
+  const int nkb = a.hidden / 32;
+  for (int kb = lane; kb < nkb; kb += 32) {
+    const size_t so = ((size_t)(row >> 7) * (a.hidden >> 7) + (kb >> 2)) * 512 + sf_atom_offset(row & 127, kb & 3);
+    const size_t dso = ((size_t)(dst >> 7) * (a.hidden >> 7) + (kb >> 2)) * 512 + sf_atom_offset(dst & 127, kb & 3);
+    a.xg_sf[dso] = a.x_sf[so];
+  }
+  if (lane == 0) {
+    a.row_dst[dst] = row * K1 + j;
+    a.row_scale[dst] = w;
+  }
+}
+
+}  // namespace moe
+}  // namespace zs
+
+extern "C" int zs_moe_route(const MoeRouteArgs* args, cudaStream_t stream) {
+  const MoeRouteArgs& a = *args;
+  if (a.num_experts > zs::moe::kMaxExperts || a.top_k > zs::moe::kMaxTopK || a.top_k <= 0) return -1;
+  if (a.n_group > 64 || (a.n_group > 1 && a.num_experts % a.n_group != 0)) return -1;
+  if (a.hidden % 128 != 0) return -1;
+  const int groups = (a.expert_end - a.expert_begin) + (a.has_shared ? 1 : 0);
+  if (cudaMemsetAsync(a.group_count, 0, sizeof(int) * groups, stream) != cudaSuccess) return -2;
+  if (a.rows == 0) {
+    zs::moe::offsets_kernel<<<1, 1024, 0, stream>>>(a, groups);
+    return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  }
+  const int wpb = 8;
+  zs::moe::route_topk_kernel<<<(a.rows + wpb - 1) / wpb, wpb * 32, 0, stream>>>(a);
+  zs::moe::offsets_kernel<<<1, 1024, 0, stream>>>(a, groups);
+  const int pairs = a.rows * (a.top_k + 1);
+  zs::moe::scatter_kernel<<<(pairs + wpb - 1) / wpb, wpb * 32, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}

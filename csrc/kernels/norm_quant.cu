@@ -1,0 +1,250 @@
+// MXFP8 quantization, fused residual-add + RMSNorm + quantize, embedding gather,
+// and the argmax row reduction.
+//
+// Reference parity: zero-centered RMSNorm and its fused-residual form
+// (worker/zstep_worker/kernels_sm120/qwen35_ops.py:88-178), the RMSNorm + MXFP8
+// group-32 quantizer (kernels_sm120/norm_quant.py:31-77; same ceil(log2(amax/448))
+// e8m0 scale rule) and the deterministic (logit DESC, id ASC) top-1 of
+// csrc/qwen35_ops_kernels.cu:145-198.
+#include "sm100_common.cuh"
+#include "zs_kernels.h"
+
+namespace zs {
+
+// One thread per 32-element block: 64 B in, 32 B + 1 scale byte out.
+__global__ void quant_mxf8_kernel(const __nv_bfloat16* __restrict__ x, int rows, int k, int ld_x,
+                                  uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  const int blocks_per_row = k / 32;
+  const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= (long long)rows * blocks_per_row) return;
+  const int row = static_cast<int>(gid / blocks_per_row);
+  const int kb = static_cast<int>(gid % blocks_per_row);
+  const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)row * ld_x + kb * 32);
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 u = src[i];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __bfloat1622float2(h[j]);
+      v[i * 8 + j * 2] = f.x;
+      v[i * 8 + j * 2 + 1] = f.y;
+    }
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const uint8_t code = mx_scale_e8m0(amax);
+  const float inv = mx_inv_scale(code);
+  uint32_t packed[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w |= static_cast<uint32_t>(f32_to_e4m3(v[i * 4 + j] * inv)) << (8 * j);
+    packed[i] = w;
+  }
+  uint4* dst = reinterpret_cast<uint4*>(q + (size_t)row * k + kb * 32);
+  dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+  sf[((size_t)(row >> 7) * (k >> 7) + (kb >> 2)) * 512 + sf_atom_offset(row & 127, kb & 3)] = code;
+}
+
+// Fused: residual += sum(delta terms); y = rmsnorm(residual) * (w + w_offset);
+// emit y as bf16 and/or MXFP8.  One CTA (256 threads) per row; each thread owns
+// 8 consecutive columns per 2048-column pass (hidden <= 8192).
+constexpr int kNormThreads = 256;
+constexpr int kNormMaxIter = 4;
+
+template <bool kEmbed>
+__global__ void __launch_bounds__(kNormThreads)
+add_rmsnorm_quant_kernel(__nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ delta,
+                         int n_terms, long long d_row_stride, long long d_term_stride,
+                         const int* __restrict__ ids, const __nv_bfloat16* __restrict__ embed,
+                         const __nv_bfloat16* __restrict__ weight, float w_offset, float eps,
+                         int hidden, __nv_bfloat16* __restrict__ normed, uint8_t* __restrict__ q,
+                         uint8_t* __restrict__ sf) {
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int iters = hidden / (kNormThreads * 8);
+  float x[kNormMaxIter][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int it = 0; it < kNormMaxIter; ++it) {
+    if (it >= iters) break;
+    const int col = (it * kNormThreads + tid) * 8;
+    uint4 u;
+    if (kEmbed) {
+      const int tok = ids[row];
+      u = *reinterpret_cast<const uint4*>(embed + (size_t)tok * hidden + col);
+    } else {
+      u = *reinterpret_cast<const uint4*>(residual + (size_t)row * hidden + col);
+    }
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __bfloat1622float2(h[j]);
+      x[it][2 * j] = f.x;
+      x[it][2 * j + 1] = f.y;
+    }
+    if (!kEmbed && delta != nullptr) {
+      for (int t = 0; t < n_terms; ++t) {
+        uint4 d = *reinterpret_cast<const uint4*>(delta + row * d_row_stride + t * d_term_stride + col);
+        const __nv_bfloat162* dh = reinterpret_cast<const __nv_bfloat162*>(&d);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = __bfloat1622float2(dh[j]);
+          x[it][2 * j] += f.x;
+          x[it][2 * j + 1] += f.y;
+        }
+      }
+    }
+    // Round the updated residual to bf16 (the stored value) and norm from it.
+    uint32_t packed[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __nv_bfloat162 b = __floats2bfloat162_rn(x[it][2 * j], x[it][2 * j + 1]);
+      packed[j] = *reinterpret_cast<uint32_t*>(&b);
+      float2 f = __bfloat1622float2(b);
+      x[it][2 * j] = f.x;
+      x[it][2 * j + 1] = f.y;
+      ss += f.x * f.x + f.y * f.y;
+    }
+    if (kEmbed || delta != nullptr)
+      *reinterpret_cast<uint4*>(residual + (size_t)row * hidden + col) =
+          make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  }
+  __shared__ float red[kNormThreads / 32];
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  if (tid < 32) {
+    float v = tid < kNormThreads / 32 ? red[tid] : 0.f;
+    v = warp_sum(v);
+    if (tid == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float rstd = rsqrtf(red[0] / hidden + eps);
+#pragma unroll
+  for (int it = 0; it < kNormMaxIter; ++it) {
+    if (it >= iters) break;
+    const int col = (it * kNormThreads + tid) * 8;
+    uint4 wu = *reinterpret_cast<const uint4*>(weight + col);
+    const __nv_bfloat162* wh = reinterpret_cast<const __nv_bfloat162*>(&wu);
+    float y[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 w = __bfloat1622float2(wh[j]);
+      y[2 * j] = x[it][2 * j] * rstd * (w.x + w_offset);
+      y[2 * j + 1] = x[it][2 * j + 1] * rstd * (w.y + w_offset);
+    }
+    if (normed != nullptr) {
+      uint32_t packed[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 b = __floats2bfloat162_rn(y[2 * j], y[2 * j + 1]);
+        packed[j] = *reinterpret_cast<uint32_t*>(&b);
+      }
+      *reinterpret_cast<uint4*>(normed + (size_t)row * hidden + col) =
+          make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    }
+    if (q != nullptr) {
+      // A 32-column MX block spans 4 consecutive threads.
+      float amax = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(y[j]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffff, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffff, amax, 2));
+      const uint8_t code = mx_scale_e8m0(amax);
+      const float inv = mx_inv_scale(code);
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        lo |= static_cast<uint32_t>(f32_to_e4m3(y[j] * inv)) << (8 * j);
+        hi |= static_cast<uint32_t>(f32_to_e4m3(y[4 + j] * inv)) << (8 * j);
+      }
+      *reinterpret_cast<uint2*>(q + (size_t)row * hidden + col) = make_uint2(lo, hi);
+      if ((tid & 3) == 0) {
+        const int kb = col >> 5;
+        sf[((size_t)(row >> 7) * (hidden >> 7) + (kb >> 2)) * 512 + sf_atom_offset(row & 127, kb & 3)] =
+            code;
+      }
+    }
+  }
+}
+
+__global__ void argmax_reduce_kernel(const unsigned long long* __restrict__ keys, int rows, int tiles,
+                                     int* out_ids, float* out_vals, unsigned long long* out_keys) {
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  unsigned long long best = 0;
+  for (int t = lane; t < tiles; t += 32) {
+    const unsigned long long k = keys[(size_t)row * tiles + t];
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffff, best, o);
+    best = other > best ? other : best;
+  }
+  if (lane == 0) {
+    if (out_ids) out_ids[row] = unpack_argmax_id(best);
+    if (out_vals) out_vals[row] = unpack_argmax_value(best);
+    if (out_keys) out_keys[row] = best;
+  }
+}
+
+}  // namespace zs
+
+extern "C" int zs_quant_mxf8(const void* x, int rows, int k, int ld_x, uint8_t* q, uint8_t* sf,
+                             cudaStream_t stream) {
+  if (k % 128 != 0 || rows < 0) return -1;
+  if (rows == 0) return 0;
+  const long long total = (long long)rows * (k / 32);
+  const int threads = 256;
+  const long long grid = (total + threads - 1) / threads;
+  zs::quant_mxf8_kernel<<<(unsigned)grid, threads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), rows, k, ld_x, q, sf);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+extern "C" int zs_add_rmsnorm_quant(void* residual, const void* delta, int n_terms,
+                                    long long d_row_stride, long long d_term_stride,
+                                    const void* weight, float w_offset, float eps, int rows,
+                                    int hidden, void* normed, uint8_t* q, uint8_t* sf,
+                                    cudaStream_t stream) {
+  if (hidden % (zs::kNormThreads * 8) != 0 || hidden > zs::kNormThreads * 8 * zs::kNormMaxIter)
+    return -1;
+  if (rows == 0) return 0;
+  zs::add_rmsnorm_quant_kernel<false><<<rows, zs::kNormThreads, 0, stream>>>(
+      static_cast<__nv_bfloat16*>(residual), static_cast<const __nv_bfloat16*>(delta), n_terms,
+      d_row_stride, d_term_stride, nullptr, nullptr, static_cast<const __nv_bfloat16*>(weight),
+      w_offset, eps, hidden, static_cast<__nv_bfloat16*>(normed), q, sf);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+extern "C" int zs_embed_rmsnorm_quant(const int* ids, const void* embed, void* hidden,
+                                      const void* weight, float w_offset, float eps, int rows,
+                                      int hidden_size, void* normed, uint8_t* q, uint8_t* sf,
+                                      cudaStream_t stream) {
+  if (hidden_size % (zs::kNormThreads * 8) != 0 ||
+      hidden_size > zs::kNormThreads * 8 * zs::kNormMaxIter)
+    return -1;
+  if (rows == 0) return 0;
+  zs::add_rmsnorm_quant_kernel<true><<<rows, zs::kNormThreads, 0, stream>>>(
+      static_cast<__nv_bfloat16*>(hidden), nullptr, 0, 0, 0, ids,
+      static_cast<const __nv_bfloat16*>(embed), static_cast<const __nv_bfloat16*>(weight),
+      w_offset, eps, hidden_size, static_cast<__nv_bfloat16*>(normed), q, sf);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+extern "C" int zs_argmax_reduce(const unsigned long long* keys, int rows, int tiles, int* out_ids,
+                                float* out_vals, unsigned long long* out_keys, cudaStream_t stream) {
+  if (rows == 0) return 0;
+  const int warps = 8;
+  zs::argmax_reduce_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, stream>>>(
+      keys, rows, tiles, out_ids, out_vals, out_keys);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}

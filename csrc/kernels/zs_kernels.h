@@ -1,0 +1,196 @@
+// C ABI of the zstep_b200 sm_100a kernel library.
+//
+// Every entry point takes raw device pointers plus a cudaStream_t and returns 0 on
+// success or a negative code for a rejected argument / launch failure.  The torch
+// binding layer (bindings.cpp) and any non-torch host (the C++ master's own tests,
+// ctypes) call these directly.  Kernels report device-side failures (bounded waits
+// that ran out, bad shapes seen on device) through the `err` word.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// ----------------------------------------------------------------------------------
+// MXFP8 GEMM (tcgen05 block-scaled): out[tokens, features] = act[tokens, K] . W[features, K]^T
+// ----------------------------------------------------------------------------------
+enum GemmEpilogue {
+  kEpiStoreBf16 = 0,      // out bf16 [rows, ldo], column = feature
+  kEpiStoreF32 = 1,       // out f32  [rows, ldo]
+  kEpiSiluQuant = 2,      // gate/up tile pairs -> silu(g)*u -> MXFP8 out (e4m3 [rows, ldo]) + out_sf atoms
+  kEpiScatterScaled = 3,  // out bf16 [row_dst[row], ldo] = acc * row_scale[row]
+  kEpiArgmaxPartial = 4,  // out u64 [rows, ldo = Npad/128]: per-tile packed argmax key
+};
+
+typedef struct GemmMxf8Args {
+  const uint8_t* a;        // weights e4m3 [groups * n_pad, k]
+  const uint8_t* sfa;      // weight scale atoms [groups, n_pad/128, k/128, 512]
+  const uint8_t* b;        // activations e4m3 [b_rows, k]
+  const uint8_t* sfb;      // activation scale atoms [b_rows/128, k/128, 512]
+  int k;
+  int n_pad;               // padded features per group (multiple of 128)
+  int n_valid;             // real features per group (stores skip the padding)
+  int groups;
+  int b_rows;              // rows of the activation buffer (multiple of 128)
+  int m_rows;              // dense mode: number of token rows
+  const int* group_count;  // grouped mode: [groups] tokens per group (device)
+  const int* group_offset; // grouped mode: [groups] first row of each group's segment
+  const int* chunk_prefix; // grouped mode: [groups+1] prefix of ceil(count/128); NULL = dense
+  int max_items;           // grouped mode: optional cap on CTAs (0 = one per SM)
+  int epi_mode;
+  void* out;
+  int ldo;                 // leading dimension of out in elements
+  uint8_t* out_sf;         // kEpiSiluQuant: scale atoms of the quantized output
+  const int* row_dst;      // kEpiScatterScaled
+  const float* row_scale;  // kEpiScatterScaled
+  int* err;                // device error word (may be NULL)
+} GemmMxf8Args;
+
+int zs_gemm_mxf8(const GemmMxf8Args* args, cudaStream_t stream);
+
+// ----------------------------------------------------------------------------------
+// MXFP8 quantization and fused norms
+// ----------------------------------------------------------------------------------
+// Quantize bf16 rows [rows, k] into e4m3 [rows, k] + scale atoms [ceil(rows/128), k/128, 512].
+int zs_quant_mxf8(const void* x_bf16, int rows, int k, int ld_x, uint8_t* q, uint8_t* sf,
+                  cudaStream_t stream);
+
+// residual[r] = bf16(residual[r] + sum_t delta[r, t]) (if delta != NULL), then
+// y = rmsnorm(residual[r]) * (w + w_offset); y written as bf16 (normed, optional) and/or
+// MXFP8 (q + sf, optional).  Reduction in fp32, hidden % 256 == 0.
+int zs_add_rmsnorm_quant(void* residual, const void* delta, int n_terms, long long delta_row_stride,
+                         long long delta_term_stride, const void* weight, float w_offset,
+                         float eps, int rows, int hidden, void* normed, uint8_t* q, uint8_t* sf,
+                         cudaStream_t stream);
+
+// hidden[r] = embed[ids[r]]; then as zs_add_rmsnorm_quant without delta.
+int zs_embed_rmsnorm_quant(const int* ids, const void* embed, void* hidden, const void* weight,
+                           float w_offset, float eps, int rows, int hidden_size, void* normed,
+                           uint8_t* q, uint8_t* sf, cudaStream_t stream);
+
+// Reduce per-tile argmax keys [rows, tiles] to a token id and its logit per row.
+int zs_argmax_reduce(const unsigned long long* keys, int rows, int tiles, int* out_ids,
+                     float* out_vals, unsigned long long* out_keys, cudaStream_t stream);
+
+// ----------------------------------------------------------------------------------
+// GatedDeltaNet (Qwen3.5 linear attention)
+// ----------------------------------------------------------------------------------
+typedef struct GdnArgs {
+  const void* proj;        // bf16 [rows, ld_proj]: [q | k | v | z | b | a] per the layout below
+  int ld_proj;
+  int num_k_heads;         // local q/k heads
+  int num_v_heads;         // local v heads (multiple of num_k_heads)
+  int head_k;              // 128
+  int head_v;              // 128
+  const void* conv_w;      // bf16 [conv_dim, 4]; conv_dim = 2*Hk*dk + Hv*dv
+  void* conv_state;        // bf16 [slots, 2, conv_dim, 3] (double-buffered by position parity)
+  float* ssm_state;        // f32  [slots, Hv, dv, dk]  (row v holds the dk coefficients)
+  const float* a_log;      // [Hv]
+  const float* dt_bias;    // [Hv]
+  const void* norm_w;      // bf16 [dv] gated RMSNorm weight
+  float eps;
+  const int* slots;        // [rows] state slot of each row
+  const int* positions;    // [rows] position of the row's token (0 => fresh state)
+  int rows;
+  void* out_bf16;          // optional bf16 [rows, Hv*dv]
+  uint8_t* out_q;          // optional MXFP8 [rows_pad, Hv*dv]
+  uint8_t* out_sf;         //   + scale atoms
+  // Prefill (varlen) extension: rows grouped into sequences.
+  const int* seq_start;    // [num_seqs+1] row ranges (prefill only)
+  int num_seqs;
+  const int* ckpt_rows;    // prefill: [num_seqs * max_ckpt] row index after which to snapshot (-1 none)
+  const int* ckpt_slots;   // prefill: matching checkpoint slot ids
+  int max_ckpt;
+  int* err;
+} GdnArgs;
+
+int zs_gdn_decode(const GdnArgs* args, cudaStream_t stream);
+int zs_gdn_prefill(const GdnArgs* args, cudaStream_t stream);
+
+// ----------------------------------------------------------------------------------
+// Gated GQA attention (Qwen3.5 full-attention layers), paged KV, 16-token pages
+// ----------------------------------------------------------------------------------
+typedef struct AttnArgs {
+  const void* qkv;         // bf16 [rows, ld_qkv]: per q head [q(256) | gate(256)], then K heads, V heads
+  int ld_qkv;
+  int num_q_heads;         // local
+  int num_kv_heads;        // local
+  int head_dim;            // 256
+  int rotary_dim;          // 64 (partial rope on the first rotary_dim dims)
+  float rope_theta;
+  const void* q_norm_w;    // bf16 [head_dim] (zero-centered: scale = 1 + w)
+  const void* k_norm_w;
+  float eps;
+  void* k_cache;           // bf16 [pages, page_size, kv_heads, head_dim]
+  void* v_cache;
+  int page_size;
+  const int* page_table;   // [slots, max_pages]
+  int max_pages;
+  const int* slots;        // [rows]
+  const int* positions;    // [rows]
+  int rows;
+  void* q_out;             // bf16 [rows, Hq, head_dim] (normed + roped)
+  void* gate_out;          // bf16 [rows, Hq, head_dim]
+  // decode
+  const int* seq_lens;     // [rows] context length including the current token
+  float* partial;          // split-K scratch
+  int num_splits;
+  float sm_scale;
+  void* out_bf16;          // [rows, Hq*head_dim] gated attention output
+  uint8_t* out_q;          // optional MXFP8 output
+  uint8_t* out_sf;
+  // prefill varlen
+  const int* seq_start;    // [num_seqs+1]
+  int num_seqs;
+  int* err;
+} AttnArgs;
+
+int zs_attn_prologue(const AttnArgs* args, cudaStream_t stream);
+int zs_attn_decode(const AttnArgs* args, cudaStream_t stream);
+int zs_attn_prefill(const AttnArgs* args, cudaStream_t stream);
+
+// ----------------------------------------------------------------------------------
+// MoE routing
+// ----------------------------------------------------------------------------------
+typedef struct MoeRouteArgs {
+  const float* logits;     // f32 [rows, ld_logits]: router logits (num_experts) then shared-gate logit
+  int ld_logits;
+  int rows;
+  int num_experts;         // routed experts (global)
+  int top_k;
+  int norm_topk;           // renormalise the top-k weights to sum 1
+  int scoring;             // 0 = softmax, 1 = sigmoid (+ bias, grouped)
+  const float* bias;       // sigmoid scoring: per-expert correction bias (may be NULL)
+  int n_group, topk_group; // grouped routing (sigmoid scoring)
+  float routed_scale;
+  int shared_gate_col;     // column of the shared-expert gate logit (-1: shared weight 1)
+  int expert_begin;        // experts [expert_begin, expert_end) are local (EP); others dropped
+  int expert_end;
+  int has_shared;          // local group `expert_end - expert_begin` is the shared expert
+  // outputs
+  int* topk_ids;           // [rows, top_k] global expert ids
+  float* topk_w;           // [rows, top_k]
+  int* group_count;        // [G] G = local experts (+1 if shared)
+  int* group_offset;       // [G]
+  int* chunk_prefix;       // [G+1]
+  int* pair_slot;          // [rows, top_k + 1] row in the grouped buffer (-1 if not local)
+  int* row_dst;            // [grouped rows] destination pair row (token * (top_k+1) + j)
+  float* row_scale;        // [grouped rows] routing weight
+  int max_grouped_rows;
+  // activation scatter
+  const uint8_t* x_q;      // [rows, hidden] e4m3
+  const uint8_t* x_sf;     // scale atoms of x
+  int hidden;
+  uint8_t* xg_q;           // [max_grouped_rows, hidden]
+  uint8_t* xg_sf;          // atoms
+  int* err;
+} MoeRouteArgs;
+
+int zs_moe_route(const MoeRouteArgs* args, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif

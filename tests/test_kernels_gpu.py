@@ -1,0 +1,418 @@
+"""Numerics of every sm_100a kernel against a PyTorch fp32 reference of the same op."""
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from zstep_b200.ops import mx
+from zstep_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+
+EPI_BF16, EPI_F32, EPI_SILU, EPI_SCATTER, EPI_ARGMAX = 0, 1, 2, 3, 4
+
+
+@pytest.fixture(scope="module")
+def C():
+    from zstep_b200.ops import _ext
+
+    return _ext.load()
+
+
+def _pad_rows(n: int) -> int:
+    return (n + 127) // 128 * 128
+
+
+def _quant_weights(w: torch.Tensor):
+    """w [G, N, K] fp32 -> (q [G*Npad, K] u8, atoms, dequant [G, Npad, K])."""
+    g, n, k = w.shape
+    npad = _pad_rows(n)
+    wp = torch.zeros(g, npad, k)
+    wp[:, :n] = w
+    q, code = mx.quantize(wp.reshape(g * npad, k))
+    deq = mx.dequantize(q, code).reshape(g, npad, k)
+    return q.cuda(), mx.atoms_from_codes(code).cuda(), deq, npad
+
+
+def _quant_act(x: torch.Tensor, rows_pad: int):
+    rows, k = x.shape
+    xp = torch.zeros(rows_pad, k)
+    xp[:rows] = x
+    q, code = mx.quantize(xp)
+    return q.cuda(), mx.atoms_from_codes(code).cuda(), mx.dequantize(q, code)[:rows]
+
+
+@pytest.mark.parametrize("m,n,k", [(200, 300, 512), (1, 128, 128), (256, 1024, 2048), (37, 129, 384)])
+def test_gemm_dense_f32(C, m, n, k):
+    torch.manual_seed(m + n + k)
+    w = torch.randn(1, n, k) * 0.05
+    x = torch.randn(m, k)
+    wq, wsf, wd, npad = _quant_weights(w)
+    xq, xsf, xd = _quant_act(x, _pad_rows(m))
+    out = torch.zeros(m, n, device="cuda", dtype=torch.float32)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    C.gemm_mxf8(wq, wsf, xq, xsf, k, npad, n, 1, m, None, None, None, EPI_F32, out, n,
+                None, None, None, err, 0)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    expect = xd @ wd[0, :n].T
+    torch.testing.assert_close(out.cpu(), expect, rtol=1e-4, atol=1e-3)
+
+
+def test_gemm_dense_bf16(C):
+    torch.manual_seed(1)
+    m, n, k = 130, 640, 1024
+    w = torch.randn(1, n, k) * 0.05
+    x = torch.randn(m, k)
+    wq, wsf, wd, npad = _quant_weights(w)
+    xq, xsf, xd = _quant_act(x, _pad_rows(m))
+    out = torch.zeros(m, n, device="cuda", dtype=torch.bfloat16)
+    C.gemm_mxf8(wq, wsf, xq, xsf, k, npad, n, 1, m, None, None, None, EPI_BF16, out, n,
+                None, None, None, None, 0)
+    torch.cuda.synchronize()
+    expect = (xd @ wd[0, :n].T).to(torch.bfloat16)
+    torch.testing.assert_close(out.cpu(), expect, rtol=1e-2, atol=1e-2)
+
+
+def _grouped_setup(counts, k, n, seed=0):
+    torch.manual_seed(seed)
+    g = len(counts)
+    w = torch.randn(g, n, k) * 0.05
+    wq, wsf, wd, npad = _quant_weights(w)
+    offsets, chunk_prefix, o, c = [], [0], 0, 0
+    for cnt in counts:
+        offsets.append(o)
+        o += _pad_rows(cnt) if cnt else 0
+        c += (cnt + 127) // 128
+        chunk_prefix.append(c)
+    rows = max(o, 128)
+    x = torch.randn(rows, k)
+    xq, xsf, xd = _quant_act(x, rows)
+    dev = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")  # noqa: E731
+    return dict(w=w, wq=wq, wsf=wsf, wd=wd, npad=npad, x=x, xq=xq, xsf=xsf, xd=xd, rows=rows,
+                offsets=offsets, cnt=dev(counts), off=dev(offsets), pre=dev(chunk_prefix))
+
+
+def test_gemm_grouped_f32(C):
+    counts = [0, 7, 130, 16, 1, 300]
+    k, n = 256, 256
+    s = _grouped_setup(counts, k, n)
+    out = torch.full((s["rows"], n), float("nan"), device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    C.gemm_mxf8(s["wq"], s["wsf"], s["xq"], s["xsf"], k, s["npad"], n, len(counts), 0,
+                s["cnt"], s["off"], s["pre"], EPI_F32, out, n, None, None, None, err, 0)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    out = out.cpu()
+    for gi, cnt in enumerate(counts):
+        if cnt == 0:
+            continue
+        o = s["offsets"][gi]
+        expect = s["xd"][o:o + cnt] @ s["wd"][gi, :n].T
+        torch.testing.assert_close(out[o:o + cnt], expect, rtol=1e-4, atol=1e-3)
+
+
+def test_gemm_silu_quant(C):
+    counts = [5, 0, 140]
+    k, inter = 256, 256  # 4 tiles of (64 gate + 64 up)
+    torch.manual_seed(3)
+    g = len(counts)
+    wg = torch.randn(g, inter, k) * 0.05
+    wu = torch.randn(g, inter, k) * 0.05
+    # Interleave per 128-row tile: [gate 64m..64m+63 ; up 64m..64m+63]
+    packed = torch.stack([wg.reshape(g, inter // 64, 64, k), wu.reshape(g, inter // 64, 64, k)], dim=2)
+    packed = packed.reshape(g, 2 * inter, k)
+    s = _grouped_setup(counts, k, 2 * inter)
+    wq, wsf, wd, npad = _quant_weights(packed)
+    act = torch.zeros(s["rows"], inter, dtype=torch.uint8, device="cuda")
+    act_sf = torch.zeros(mx.atoms_bytes(s["rows"], inter), dtype=torch.uint8, device="cuda")
+    C.gemm_mxf8(wq, wsf, s["xq"], s["xsf"], k, npad, 2 * inter, g, 0, s["cnt"], s["off"], s["pre"],
+                EPI_SILU, act, inter, act_sf, None, None, None, 0)
+    torch.cuda.synchronize()
+    codes = mx.codes_from_atoms(act_sf.cpu(), s["rows"], inter)
+    got = mx.dequantize(act.cpu(), codes)
+    for gi, cnt in enumerate(counts):
+        if cnt == 0:
+            continue
+        o = s["offsets"][gi]
+        full = s["xd"][o:o + cnt] @ wd[gi].T  # [cnt, 2*inter] in packed order
+        full = full.reshape(cnt, inter // 64, 2, 64)
+        h = (F.silu(full[:, :, 0]) * full[:, :, 1]).reshape(cnt, inter)
+        expect = mx.fake_quant(h)
+        tol = h.abs().amax(-1, keepdim=True) / 8
+        assert ((got[o:o + cnt] - expect).abs() <= tol + 1e-6).all()
+        torch.testing.assert_close(got[o:o + cnt], h, rtol=0.07, atol=0.02 * h.abs().max().item())
+
+
+def test_gemm_scatter_scaled(C):
+    counts = [3, 9]
+    k, n = 128, 256
+    s = _grouped_setup(counts, k, n, seed=5)
+    rows = s["rows"]
+    row_dst = torch.full((rows,), -1, dtype=torch.int32)
+    row_scale = torch.zeros(rows)
+    perm = torch.randperm(12)
+    i = 0
+    for gi, cnt in enumerate(counts):
+        for r in range(cnt):
+            row_dst[s["offsets"][gi] + r] = perm[i]
+            row_scale[s["offsets"][gi] + r] = 0.5 + i
+            i += 1
+    out = torch.zeros(12, n, dtype=torch.bfloat16, device="cuda")
+    C.gemm_mxf8(s["wq"], s["wsf"], s["xq"], s["xsf"], k, s["npad"], n, 2, 0, s["cnt"], s["off"],
+                s["pre"], EPI_SCATTER, out, n, None, row_dst.cuda(), row_scale.cuda(), None, 0)
+    torch.cuda.synchronize()
+    out = out.cpu().float()
+    for gi, cnt in enumerate(counts):
+        for r in range(cnt):
+            src = s["offsets"][gi] + r
+            expect = (s["xd"][src] @ s["wd"][gi, :n].T) * row_scale[src]
+            torch.testing.assert_close(out[row_dst[src]], expect, rtol=1e-2, atol=1e-2)
+
+
+def test_gemm_argmax_ties(C):
+    torch.manual_seed(7)
+    m, vocab, k = 37, 1000, 256
+    w = torch.randn(1, vocab, k) * 0.05
+    w[0, 900] = w[0, 5]  # exact duplicate row -> tie must resolve to id 5
+    x = torch.randn(m, k)
+    x[3] = w[0, 5] * 40  # make row 3 pick the tied pair
+    wq, wsf, wd, npad = _quant_weights(w)
+    xq, xsf, xd = _quant_act(x, _pad_rows(m))
+    tiles = npad // 128
+    keys = torch.zeros(m, tiles, dtype=torch.int64, device="cuda")
+    C.gemm_mxf8(wq, wsf, xq, xsf, k, npad, vocab, 1, m, None, None, None, EPI_ARGMAX, keys, tiles,
+                None, None, None, None, 0)
+    ids = torch.zeros(m, dtype=torch.int32, device="cuda")
+    vals = torch.zeros(m, dtype=torch.float32, device="cuda")
+    C.argmax_reduce(keys, m, tiles, ids, vals, None)
+    torch.cuda.synchronize()
+    logits = xd @ wd[0, :vocab].T
+    assert ids[3].item() == 5
+    assert torch.equal(ids.cpu().long(), logits.argmax(-1))
+    torch.testing.assert_close(vals.cpu(), logits.max(-1).values, rtol=1e-4, atol=1e-3)
+
+
+def test_quant_bitexact(C):
+    torch.manual_seed(0)
+    x = (torch.randn(300, 512) * torch.rand(300, 1) * 5).to(torch.bfloat16)
+    x[7] = 0
+    q = torch.zeros(300, 512, dtype=torch.uint8, device="cuda")
+    sf = torch.zeros(mx.atoms_bytes(300, 512), dtype=torch.uint8, device="cuda")
+    C.quant_mxf8(x.cuda(), q, sf)
+    torch.cuda.synchronize()
+    qr, cr = mx.quantize(x.float())
+    assert torch.equal(q.cpu(), qr)
+    assert torch.equal(mx.codes_from_atoms(sf.cpu(), 300, 512), cr)
+
+
+def test_add_rmsnorm_quant(C):
+    torch.manual_seed(0)
+    rows, h, terms = 70, 2048, 3
+    res = torch.randn(rows, h).to(torch.bfloat16)
+    delta = torch.randn(rows, terms, h).to(torch.bfloat16)
+    w = (torch.randn(h) * 0.1).to(torch.bfloat16)
+    res_g = res.cuda()
+    normed = torch.zeros(rows, h, dtype=torch.bfloat16, device="cuda")
+    q = torch.zeros(rows, h, dtype=torch.uint8, device="cuda")
+    sf = torch.zeros(mx.atoms_bytes(rows, h), dtype=torch.uint8, device="cuda")
+    C.add_rmsnorm_quant(res_g, delta.cuda(), terms, terms * h, h, w.cuda(), 1.0, 1e-6, rows, normed, q, sf)
+    torch.cuda.synchronize()
+    r_ref, n_ref = ref.add_rmsnorm(res, delta.float().sum(1), w, 1e-6)
+    torch.testing.assert_close(res_g.cpu().float(), r_ref, rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(normed.cpu().float(), n_ref, rtol=2e-2, atol=2e-2)
+    got = mx.dequantize(q.cpu(), mx.codes_from_atoms(sf.cpu(), rows, h))
+    torch.testing.assert_close(got, n_ref, rtol=0.07, atol=0.05)
+
+
+def _gdn_setup(hk, hv, rows, slots_total, seed=0):
+    torch.manual_seed(seed)
+    dk = dv = 128
+    conv_dim = 2 * hk * dk + hv * dv
+    width = conv_dim + hv * dv + 2 * hv
+    proj = (torch.randn(rows, width) * 0.5).to(torch.bfloat16)
+    conv_w = (torch.randn(conv_dim, 4) * 0.3).to(torch.bfloat16)
+    a_log = torch.rand(hv) * 2 - 1
+    dt_bias = torch.rand(hv) * 0.5
+    norm_w = (1 + 0.1 * torch.randn(dv)).to(torch.bfloat16)
+    conv_state = (torch.randn(slots_total, 2, conv_dim, 3) * 0.5).to(torch.bfloat16)
+    ssm = torch.randn(slots_total, hv, dv, dk) * 0.1
+    return dict(proj=proj, conv_w=conv_w, a_log=a_log, dt_bias=dt_bias, norm_w=norm_w,
+                conv_state=conv_state, ssm=ssm, conv_dim=conv_dim)
+
+
+def test_gdn_decode(C):
+    hk, hv, rows = 2, 4, 5
+    s = _gdn_setup(hk, hv, rows, 8)
+    slots = torch.tensor([3, 0, 7, 5, 1], dtype=torch.int32)
+    pos = torch.tensor([10, 0, 3, 1, 6], dtype=torch.int32)
+    cs, ssm = s["conv_state"].cuda(), s["ssm"].cuda()
+    out = torch.zeros(rows, hv * 128, dtype=torch.bfloat16, device="cuda")
+    C.gdn_decode(s["proj"].cuda(), hk, hv, s["conv_w"].cuda(), cs, ssm, s["a_log"].cuda(),
+                 s["dt_bias"].cuda(), s["norm_w"].cuda(), 1e-6, slots.cuda(), pos.cuda(), rows,
+                 out, None, None, None)
+    torch.cuda.synchronize()
+    for r in range(rows):
+        sl, p = slots[r].item(), pos[r].item()
+        win = s["conv_state"][sl, p & 1].float() if p > 0 else torch.zeros(s["conv_dim"], 3)
+        st = s["ssm"][sl] if p > 0 else torch.zeros(hv, 128, 128)
+        y, win2, st2 = ref.gdn_token(s["proj"][r].float(), win, st, hk=hk, hv=hv, conv_w=s["conv_w"],
+                                     a_log=s["a_log"], dt_bias=s["dt_bias"], norm_w=s["norm_w"], eps=1e-6)
+        torch.testing.assert_close(out[r].cpu().float(), y, rtol=2e-2, atol=2e-2)
+        torch.testing.assert_close(ssm[sl].cpu(), st2, rtol=1e-3, atol=1e-4)
+        torch.testing.assert_close(cs[sl, (p + 1) & 1].cpu().float(), win2, rtol=1e-2, atol=1e-2)
+
+
+def test_gdn_prefill_matches_decode_and_checkpoints(C):
+    hk, hv = 2, 4
+    lens = [5, 1, 9]
+    rows = sum(lens)
+    s = _gdn_setup(hk, hv, rows, 8, seed=1)
+    seq_slots = [2, 4, 6]
+    starts = [0, 3, 0]  # second sequence continues from position 3
+    slots, pos, seq_start = [], [], [0]
+    for sl, st, ln in zip(seq_slots, starts, lens):
+        slots += [sl] * ln
+        pos += list(range(st, st + ln))
+        seq_start.append(seq_start[-1] + ln)
+    max_ckpt = 2
+    ck_rows = torch.full((3, max_ckpt), -1, dtype=torch.int32)
+    ck_slots = torch.zeros(3, max_ckpt, dtype=torch.int32)
+    ck_rows[0, 0], ck_slots[0, 0] = 2, 7   # after row 2 of seq 0
+    ck_rows[2, 0], ck_slots[2, 0] = 6 + 3, 1  # seq 2 starts at row 6; after its 4th token
+    cs, ssm = s["conv_state"].cuda(), s["ssm"].cuda()
+    out = torch.zeros(rows, hv * 128, dtype=torch.bfloat16, device="cuda")
+    C.gdn_prefill(s["proj"].cuda(), hk, hv, s["conv_w"].cuda(), cs, ssm, s["a_log"].cuda(),
+                  s["dt_bias"].cuda(), s["norm_w"].cuda(), 1e-6, torch.tensor(slots, dtype=torch.int32).cuda(),
+                  torch.tensor(pos, dtype=torch.int32).cuda(), rows, out, None, None,
+                  torch.tensor(seq_start, dtype=torch.int32).cuda(), 3, ck_rows.cuda(), ck_slots.cuda(),
+                  max_ckpt, None)
+    torch.cuda.synchronize()
+    for si, (sl, st0, ln) in enumerate(zip(seq_slots, starts, lens)):
+        win = s["conv_state"][sl, st0 & 1].float() if st0 > 0 else torch.zeros(s["conv_dim"], 3)
+        st = s["ssm"][sl] if st0 > 0 else torch.zeros(hv, 128, 128)
+        for j in range(ln):
+            r = seq_start[si] + j
+            y, win, st = ref.gdn_token(s["proj"][r].float(), win, st, hk=hk, hv=hv, conv_w=s["conv_w"],
+                                       a_log=s["a_log"], dt_bias=s["dt_bias"], norm_w=s["norm_w"], eps=1e-6)
+            torch.testing.assert_close(out[r].cpu().float(), y, rtol=3e-2, atol=3e-2)
+            for c in range(max_ckpt):
+                if ck_rows[si, c].item() == r:
+                    cslot = ck_slots[si, c].item()
+                    torch.testing.assert_close(ssm[cslot].cpu(), st, rtol=1e-3, atol=1e-4)
+                    torch.testing.assert_close(cs[cslot, (st0 + j + 1) & 1].cpu().float(), win, rtol=1e-2, atol=1e-2)
+        torch.testing.assert_close(ssm[sl].cpu(), st, rtol=1e-3, atol=1e-4)
+
+
+def test_attention_prologue_and_decode(C):
+    torch.manual_seed(0)
+    hq, hkv, d, page = 8, 2, 256, 16
+    rows = 3
+    ctx = [40, 1, 17]
+    max_pages = 4
+    pages_total = 16
+    qkv_w = hq * 2 * d + 2 * hkv * d
+    page_table = torch.tensor([[3, 9, 5, 0], [1, 0, 0, 0], [12, 2, 0, 0]], dtype=torch.int32)
+    slots = torch.arange(rows, dtype=torch.int32)
+    kc = (torch.randn(pages_total, page, hkv, d) * 0.5).to(torch.bfloat16)
+    vc = (torch.randn(pages_total, page, hkv, d) * 0.5).to(torch.bfloat16)
+    qkv = (torch.randn(rows, qkv_w)).to(torch.bfloat16)
+    qn = (0.1 * torch.randn(d)).to(torch.bfloat16)
+    kn = (0.1 * torch.randn(d)).to(torch.bfloat16)
+    pos = torch.tensor([c - 1 for c in ctx], dtype=torch.int32)
+    kc_g, vc_g = kc.cuda(), vc.cuda()
+    q_out = torch.zeros(rows, hq, d, dtype=torch.bfloat16, device="cuda")
+    g_out = torch.zeros(rows, hq, d, dtype=torch.bfloat16, device="cuda")
+    C.attn_prologue(qkv.cuda(), hq, hkv, 64, 1e7, qn.cuda(), kn.cuda(), 1e-6, kc_g, vc_g, page,
+                    page_table.cuda(), slots.cuda(), pos.cuda(), rows, q_out, g_out)
+    splits = 3
+    partial = torch.zeros(rows * hq * splits * 260, device="cuda")
+    out = torch.zeros(rows, hq * d, dtype=torch.bfloat16, device="cuda")
+    sm = 1 / math.sqrt(d)
+    C.attn_decode(q_out, g_out, hq, hkv, kc_g, vc_g, page, page_table.cuda(), slots.cuda(),
+                  torch.tensor(ctx, dtype=torch.int32).cuda(), rows, partial, splits, sm, out, None, None)
+    torch.cuda.synchronize()
+    for r in range(rows):
+        q, gate, k_new, v_new = ref.attn_prologue_row(qkv[r].float(), pos[r].item(), hq=hq, hkv=hkv,
+                                                      q_norm_w=qn, k_norm_w=kn, eps=1e-6, rotary_dim=64,
+                                                      theta=1e7)
+        torch.testing.assert_close(q_out[r].cpu().float(), q, rtol=2e-2, atol=2e-2)
+        p_last = pos[r].item()
+        pg = page_table[r, p_last // page].item()
+        torch.testing.assert_close(kc_g[pg, p_last % page].cpu().float(), k_new, rtol=2e-2, atol=2e-2)
+        keys = torch.stack([kc_g[page_table[r, t // page], t % page].cpu().float() for t in range(ctx[r])])
+        vals = torch.stack([vc_g[page_table[r, t // page], t % page].cpu().float() for t in range(ctx[r])])
+        expect = ref.gated_attention(q_out[r].cpu().float(), g_out[r].cpu().float(), keys, vals, sm)
+        torch.testing.assert_close(out[r].cpu().float(), expect, rtol=2e-2, atol=2e-2)
+
+
+def test_moe_route_softmax_shared(C):
+    torch.manual_seed(0)
+    rows, E, k, hidden = 50, 64, 4, 256
+    logits = torch.randn(rows, E + 1)
+    x = torch.randn(rows, hidden)
+    xq, xsf, _ = _quant_act(x, _pad_rows(rows))
+    G = E + 1
+    max_rows = rows * (k + 1) + 128 * G
+    dev = dict(device="cuda")
+    topk_ids = torch.zeros(rows, k, dtype=torch.int32, **dev)
+    topk_w = torch.zeros(rows, k, **dev)
+    cnt = torch.zeros(G, dtype=torch.int32, **dev)
+    off = torch.zeros(G, dtype=torch.int32, **dev)
+    pre = torch.zeros(G + 1, dtype=torch.int32, **dev)
+    pair_slot = torch.zeros(rows, k + 1, dtype=torch.int32, **dev)
+    row_dst = torch.full((max_rows,), -1, dtype=torch.int32, **dev)
+    row_scale = torch.zeros(max_rows, **dev)
+    xg = torch.zeros(max_rows, hidden, dtype=torch.uint8, **dev)
+    xg_sf = torch.zeros(mx.atoms_bytes(max_rows, hidden), dtype=torch.uint8, **dev)
+    err = torch.zeros(1, dtype=torch.int32, **dev)
+    C.moe_route(logits.cuda(), rows, E, k, True, 0, None, 1, 1, 1.0, E, 0, E, True, topk_ids, topk_w,
+                cnt, off, pre, pair_slot, row_dst, row_scale, xq, xsf, xg, xg_sf, err)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    ids_ref, w_ref = ref.route(logits[:, :E], top_k=k)
+    assert torch.equal(topk_ids.cpu().long(), ids_ref)
+    torch.testing.assert_close(topk_w.cpu(), w_ref, rtol=1e-5, atol=1e-6)
+    counts = torch.bincount(ids_ref.reshape(-1), minlength=E).tolist() + [rows]
+    assert cnt.cpu().tolist() == counts
+    xg_c, rd, rs = xg.cpu(), row_dst.cpu(), row_scale.cpu()
+    codes = mx.codes_from_atoms(xg_sf.cpu(), max_rows, hidden)
+    codes_x = mx.codes_from_atoms(xsf.cpu(), rows, hidden)
+    offs = off.cpu().tolist()
+    for g in range(G):
+        for j in range(counts[g]):
+            gr = offs[g] + j
+            tok, slot = divmod(rd[gr].item(), k + 1)
+            assert torch.equal(xg_c[gr], xq.cpu()[tok])
+            assert torch.equal(codes[gr], codes_x[tok])
+            if slot < k:
+                assert ids_ref[tok, slot].item() == g
+                assert abs(rs[gr].item() - w_ref[tok, slot].item()) < 1e-6
+            else:
+                assert g == E
+                assert abs(rs[gr].item() - torch.sigmoid(logits[tok, E]).item()) < 1e-6
+
+
+def test_moe_route_sigmoid_grouped(C):
+    torch.manual_seed(1)
+    rows, E, k, hidden, ng, tg = 20, 64, 6, 128, 8, 3
+    logits = torch.randn(rows, E)
+    bias = torch.randn(E) * 0.1
+    x = torch.randn(rows, hidden)
+    xq, xsf, _ = _quant_act(x, _pad_rows(rows))
+    max_rows = rows * (k + 1) + 128 * E
+    dev = dict(device="cuda")
+    out = [torch.zeros(rows, k, dtype=torch.int32, **dev), torch.zeros(rows, k, **dev)]
+    C.moe_route(logits.cuda(), rows, E, k, True, 1, bias.cuda(), ng, tg, 2.5, -1, 0, E, False, out[0], out[1],
+                torch.zeros(E, dtype=torch.int32, **dev), torch.zeros(E, dtype=torch.int32, **dev),
+                torch.zeros(E + 1, dtype=torch.int32, **dev), torch.zeros(rows, k + 1, dtype=torch.int32, **dev),
+                torch.zeros(max_rows, dtype=torch.int32, **dev), torch.zeros(max_rows, **dev), xq, xsf,
+                torch.zeros(max_rows, hidden, dtype=torch.uint8, **dev),
+                torch.zeros(mx.atoms_bytes(max_rows, hidden), dtype=torch.uint8, **dev), None)
+    torch.cuda.synchronize()
+    ids_ref, w_ref = ref.route(logits, top_k=k, scoring="sigmoid", bias=bias, n_group=ng, topk_group=tg,
+                               routed_scale=2.5)
+    assert torch.equal(out[0].cpu().long(), ids_ref)
+    torch.testing.assert_close(out[1].cpu(), w_ref, rtol=1e-5, atol=1e-5)

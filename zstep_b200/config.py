@@ -1,0 +1,156 @@
+"""Model configurations.
+
+``Qwen35Config`` describes the Qwen3.5-MoE hybrid (GatedDeltaNet + gated GQA + MoE)
+backbone; ``from_hf`` reads a HuggingFace ``config.json`` (``text_config`` nesting and
+``rope_parameters`` handled as in the reference's config loader,
+worker/zstep_worker/models/qwen35_moe.py:82-150), without the reference's fixed
+TP=8 shape check -- any head counts divisible by the tensor-parallel degree work.
+"""
+
+from __future__ import annotations
+
+import json
+from dataclasses import asdict, dataclass, field
+from pathlib import Path
+
+
+@dataclass(frozen=True)
+class Qwen35Config:
+    vocab_size: int = 248320
+    hidden_size: int = 2048
+    num_hidden_layers: int = 40
+    layer_types: tuple[str, ...] = field(default_factory=tuple)
+    rms_norm_eps: float = 1e-6
+    num_attention_heads: int = 16
+    num_key_value_heads: int = 2
+    head_dim: int = 256
+    rope_theta: float = 1.0e7
+    partial_rotary_factor: float = 0.25
+    linear_num_key_heads: int = 16
+    linear_key_head_dim: int = 128
+    linear_num_value_heads: int = 32
+    linear_value_head_dim: int = 128
+    linear_conv_kernel_dim: int = 4
+    num_experts: int = 256
+    num_experts_per_tok: int = 8
+    moe_intermediate_size: int = 512
+    shared_expert_intermediate_size: int = 512
+    norm_topk_prob: bool = True
+    initializer_range: float = 0.02
+    # MTP draft head (one full-attention MoE layer) -- 0 disables.
+    mtp_num_hidden_layers: int = 1
+    name: str = "qwen3.5-35b-a3b"
+
+    def __post_init__(self):
+        if not self.layer_types:
+            object.__setattr__(self, "layer_types", tuple(
+                "full_attention" if (i + 1) % 4 == 0 else "linear_attention"
+                for i in range(self.num_hidden_layers)))
+        assert len(self.layer_types) == self.num_hidden_layers
+
+    # ---------------------------------------------------------------- derived sizes
+    @property
+    def rotary_dim(self) -> int:
+        return int(self.head_dim * self.partial_rotary_factor)
+
+    @property
+    def gdn_layers(self) -> list[int]:
+        return [i for i, t in enumerate(self.layer_types) if t == "linear_attention"]
+
+    @property
+    def attn_layers(self) -> list[int]:
+        return [i for i, t in enumerate(self.layer_types) if t == "full_attention"]
+
+    @property
+    def conv_dim(self) -> int:
+        return (2 * self.linear_num_key_heads * self.linear_key_head_dim
+                + self.linear_num_value_heads * self.linear_value_head_dim)
+
+    @property
+    def gdn_proj_dim(self) -> int:
+        """Width of the fused GDN input projection [q | k | v | z | b | a]."""
+        return self.conv_dim + self.linear_num_value_heads * (self.linear_value_head_dim + 2)
+
+    @property
+    def attn_qkv_dim(self) -> int:
+        """Width of the fused attention projection [per-head (q | gate) | k | v]."""
+        return (2 * self.num_attention_heads + 2 * self.num_key_value_heads) * self.head_dim
+
+    def params(self) -> int:
+        h, e, i = self.hidden_size, self.num_experts, self.moe_intermediate_size
+        per_moe = e * 3 * h * i + 3 * h * self.shared_expert_intermediate_size + h * (e + 1)
+        gdn = h * self.gdn_proj_dim + self.linear_num_value_heads * self.linear_value_head_dim * h
+        attn = h * self.attn_qkv_dim + self.num_attention_heads * self.head_dim * h
+        n = len(self.gdn_layers) * (gdn + per_moe) + len(self.attn_layers) * (attn + per_moe)
+        return n + 2 * self.vocab_size * h
+
+    def to_dict(self) -> dict:
+        d = asdict(self)
+        d["layer_types"] = list(self.layer_types)
+        return d
+
+    # ---------------------------------------------------------------- constructors
+    @classmethod
+    def from_hf(cls, path: str | Path) -> "Qwen35Config":
+        p = Path(path)
+        raw = json.loads((p / "config.json" if p.is_dir() else p).read_text(encoding="utf-8"))
+        tc = raw.get("text_config", raw)
+        rope = tc.get("rope_parameters") or {}
+        theta = rope.get("rope_theta", tc.get("rope_theta", 1.0e7))
+        prf = rope.get("partial_rotary_factor", tc.get("partial_rotary_factor", 0.25))
+        return cls(
+            vocab_size=int(tc["vocab_size"]),
+            hidden_size=int(tc["hidden_size"]),
+            num_hidden_layers=int(tc["num_hidden_layers"]),
+            layer_types=tuple(tc.get("layer_types") or ()),
+            rms_norm_eps=float(tc.get("rms_norm_eps", 1e-6)),
+            num_attention_heads=int(tc["num_attention_heads"]),
+            num_key_value_heads=int(tc["num_key_value_heads"]),
+            head_dim=int(tc.get("head_dim", 256)),
+            rope_theta=float(theta),
+            partial_rotary_factor=float(prf),
+            linear_num_key_heads=int(tc["linear_num_key_heads"]),
+            linear_key_head_dim=int(tc["linear_key_head_dim"]),
+            linear_num_value_heads=int(tc["linear_num_value_heads"]),
+            linear_value_head_dim=int(tc["linear_value_head_dim"]),
+            linear_conv_kernel_dim=int(tc.get("linear_conv_kernel_dim", 4)),
+            num_experts=int(tc["num_experts"]),
+            num_experts_per_tok=int(tc["num_experts_per_tok"]),
+            moe_intermediate_size=int(tc["moe_intermediate_size"]),
+            shared_expert_intermediate_size=int(tc["shared_expert_intermediate_size"]),
+            norm_topk_prob=bool(tc.get("norm_topk_prob", True)),
+            mtp_num_hidden_layers=int(tc.get("mtp_num_hidden_layers", 0)),
+            name=str(raw.get("_name_or_path", tc.get("model_type", "qwen3_5_moe"))),
+        )
+
+
+def qwen35_35b_a3b() -> Qwen35Config:
+    """The Qwen3.5-35B-A3B shape (random-init benchmark config)."""
+    return Qwen35Config()
+
+
+def qwen35_tiny() -> Qwen35Config:
+    """CPU plumbing model: 4 layers (3 GDN + 1 GQA), hidden 256, 8 experts top-2 + shared."""
+    return Qwen35Config(
+        vocab_size=4096, hidden_size=256, num_hidden_layers=4,
+        layer_types=("linear_attention", "linear_attention", "linear_attention", "full_attention"),
+        num_attention_heads=4, num_key_value_heads=2, head_dim=64,
+        linear_num_key_heads=4, linear_key_head_dim=32, linear_num_value_heads=8,
+        linear_value_head_dim=32, num_experts=8, num_experts_per_tok=2,
+        moe_intermediate_size=128, shared_expert_intermediate_size=128,
+        mtp_num_hidden_layers=1, name="qwen3.5-tiny")
+
+
+def qwen35_small_gpu(num_layers: int = 4, vocab: int = 8192, experts: int = 32) -> Qwen35Config:
+    """A reduced-depth config with the full per-layer shapes the sm_100a kernels serve
+    (hidden 2048, GDN 128-dim heads, GQA 256-dim heads) for fast GPU tests."""
+    types = tuple("full_attention" if (i + 1) % 4 == 0 else "linear_attention" for i in range(num_layers))
+    return Qwen35Config(vocab_size=vocab, num_hidden_layers=num_layers, layer_types=types,
+                        num_experts=experts, name=f"qwen3.5-small-{num_layers}l")
+
+
+PRESETS = {
+    "qwen3.5-35b-a3b": qwen35_35b_a3b,
+    "qwen3.5-tiny": qwen35_tiny,
+    "qwen3.5-small": qwen35_small_gpu,
+}

@@ -1,0 +1,487 @@
+"""Qwen3.5 hybrid (GatedDeltaNet + gated GQA + MoE) runner on B200 kernels.
+
+Flat model code: weights are packed once into the MXFP8 GEMM layout (e4m3 rows padded
+to 128 + e8m0 scale atoms), every intermediate lives in a preallocated buffer, and a
+decode step is a fixed sequence of sm_100a kernel launches that is captured into one
+CUDA graph per batch bucket.  Per layer (decode or varlen prefill):
+
+  GDN layer : in_proj GEMM -> fused conv/delta-rule/gated-norm kernel (MXFP8 out)
+              -> out_proj GEMM -> residual add + RMSNorm + MXFP8 quant
+  GQA layer : qkv GEMM -> q/k norm + partial RoPE + paged KV write -> split-KV gated
+              attention (MXFP8 out) -> o_proj GEMM -> residual add + RMSNorm + quant
+  MoE       : router GEMM (f32 logits) -> top-k + grouped scatter -> grouped gate/up
+              GEMM with SiLU*up + MXFP8 epilogue -> grouped down GEMM scattering
+              weight-scaled rows -> combine of the 9 pair rows + residual + RMSNorm
+  head      : lm_head GEMM with a fused per-tile argmax -> row argmax
+
+The shared expert is expert group E of the grouped GEMMs (every token visits it with
+weight sigmoid(shared gate)), so routed and shared experts stream in one launch.
+
+Tensor parallel (tp > 1): attention/GDN heads and the dense projections are sharded
+(column-parallel in, row-parallel out), experts are sharded by expert id over the
+replicated activations, and the row-parallel partial sums are reduced by the
+collective layer's fused all-reduce + residual + RMSNorm (parallel/collectives.py).
+
+Reference parity: worker/zstep_worker/models/qwen35_moe.py (runner, 1021-1168 decode
+forward, 1236 varlen prefill, 1404 graph capture, 484-524 state allocation).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from ..config import Qwen35Config
+from ..ops import _ext
+from ..ops import mx
+from .weights import RandomWeights
+
+EPI_BF16, EPI_F32, EPI_SILU, EPI_SCATTER, EPI_ARGMAX = 0, 1, 2, 3, 4
+
+DECODE_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256, 320, 384, 448, 512)
+
+
+def _pad128(n: int) -> int:
+    return (n + 127) // 128 * 128
+
+
+@dataclass
+class PackedLinear:
+    """MXFP8 weight in the GEMM layout: q [groups*n_pad, k] e4m3, sf scale atoms."""
+
+    q: torch.Tensor
+    sf: torch.Tensor
+    n: int
+    n_pad: int
+    k: int
+    groups: int = 1
+
+
+def pack_linear(w: torch.Tensor, C) -> PackedLinear:
+    """w [N, K] or [G, N, K] (bf16, on the GPU) -> PackedLinear (quantized by the GPU kernel)."""
+    if w.dim() == 2:
+        w = w.unsqueeze(0)
+    g, n, k = w.shape
+    npad = _pad128(n)
+    if npad != n:
+        wp = torch.zeros(g, npad, k, dtype=torch.bfloat16, device=w.device)
+        wp[:, :n] = w
+    else:
+        wp = w.to(torch.bfloat16).contiguous()
+    flat = wp.reshape(g * npad, k)
+    q = torch.empty(g * npad, k, dtype=torch.uint8, device=w.device)
+    sf = torch.empty(mx.atoms_bytes(g * npad, k), dtype=torch.uint8, device=w.device)
+    C.quant_mxf8(flat, q, sf)
+    return PackedLinear(q=q, sf=sf, n=n, n_pad=npad, k=k, groups=g)
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """[G, I, K] gate and up -> [G, 2I, K] with 128-row tiles [gate 64 rows ; up 64 rows]."""
+    g, i, k = gate.shape
+    assert i % 64 == 0
+    return torch.stack([gate.reshape(g, i // 64, 64, k), up.reshape(g, i // 64, 64, k)], dim=2).reshape(g, 2 * i, k)
+
+
+class Qwen35Runner:
+    """Single-process model runner for one GPU (tp_rank of tp_size)."""
+
+    def __init__(self, cfg: Qwen35Config, *, device="cuda", weights=None, max_seqs: int = 256,
+                 max_prefill_tokens: int = 4096, num_pages: int = 4096, page_size: int = 16,
+                 max_model_len: int = 4096, num_ckpt_slots: int = 0, tp_rank: int = 0, tp_size: int = 1,
+                 collectives=None, seed: int = 0):
+        self.cfg = cfg
+        self.dev = torch.device(device)
+        self.C = _ext.load()
+        self.tp_rank, self.tp = tp_rank, tp_size
+        self.coll = collectives
+        self.page_size = page_size
+        self.max_seqs = max_seqs
+        self.max_pages = (max_model_len + page_size - 1) // page_size
+        self.num_pages = num_pages
+        self.max_prefill_tokens = max_prefill_tokens
+        self.eps = cfg.rms_norm_eps
+        assert cfg.linear_key_head_dim == 128 and cfg.linear_value_head_dim == 128, "GDN kernels need 128-dim heads"
+        assert cfg.head_dim == 256, "attention kernels need head_dim 256"
+        assert cfg.hidden_size % 2048 == 0
+        # Local (per-rank) head counts.
+        self.hk = cfg.linear_num_key_heads // tp_size
+        self.hv = cfg.linear_num_value_heads // tp_size
+        self.hq = cfg.num_attention_heads // tp_size
+        self.hkv = max(1, cfg.num_key_value_heads // tp_size)
+        self.kv_rep = tp_size // cfg.num_key_value_heads if tp_size > cfg.num_key_value_heads else 1
+        E = cfg.num_experts
+        assert E % tp_size == 0
+        self.e_local = E // tp_size
+        self.e_begin = tp_rank * self.e_local
+        # Shared expert: replicated gate/up, down output-sharded by rank (only rank r writes
+        # its 1/tp slice of the hidden dim; the all-reduce then sums the slices).
+        assert cfg.shared_expert_intermediate_size == cfg.moe_intermediate_size
+        self.groups = self.e_local + 1
+        self.top_k = cfg.num_experts_per_tok
+        self.k1 = self.top_k + 1
+        self.num_slots = max_seqs + num_ckpt_slots + 1  # last slot = padding dummy
+        self.dummy_slot = self.num_slots - 1
+        self._load_weights(weights or RandomWeights(cfg, seed=seed))
+        self._alloc_state()
+        self._alloc_buffers()
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+
+    # ------------------------------------------------------------------ weights
+    def _shard_rows(self, t: torch.Tensor, parts: list[int]) -> torch.Tensor:
+        """Column-parallel shard of a fused projection made of consecutive row blocks."""
+        out, o = [], 0
+        for p in parts:
+            blk = t[o:o + p]
+            n = p // self.tp
+            out.append(blk[self.tp_rank * n:(self.tp_rank + 1) * n])
+            o += p
+        return torch.cat(out, 0)
+
+    def _load_weights(self, src) -> None:
+        cfg, C, dev, tp, r = self.cfg, self.C, self.dev, self.tp, self.tp_rank
+        get = lambda n: src.get(n, dev)  # noqa: E731
+        H = cfg.hidden_size
+        self.embed = get("embed").to(torch.bfloat16).contiguous()
+        self.final_norm = get("final_norm").to(torch.bfloat16).contiguous()
+        lm = get("lm_head")
+        vs = cfg.vocab_size // tp
+        self.vocab_local = vs
+        self.lm_head = pack_linear(lm[r * vs:(r + 1) * vs], C)
+        del lm
+        self.layers = []
+        Hk, Hv, dk, dv = cfg.linear_num_key_heads, cfg.linear_num_value_heads, 128, 128
+        Hq, Hkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        for i in range(cfg.num_hidden_layers):
+            p = f"layers.{i}."
+            L = {"type": cfg.layer_types[i]}
+            L["input_norm"] = get(p + "input_norm").to(torch.bfloat16)
+            L["post_norm"] = get(p + "post_norm").to(torch.bfloat16)
+            if L["type"] == "linear_attention":
+                w = get(p + "gdn.in_proj")
+                w = self._shard_rows(w, [Hk * dk, Hk * dk, Hv * dv, Hv * dv, Hv, Hv])
+                L["in_proj"] = pack_linear(w, C)
+                cw = get(p + "gdn.conv_w")
+                L["conv_w"] = self._shard_rows(cw, [Hk * dk, Hk * dk, Hv * dv]).to(torch.bfloat16).contiguous()
+                L["a_log"] = get(p + "gdn.a_log").float()[r * self.hv:(r + 1) * self.hv].contiguous()
+                L["dt_bias"] = get(p + "gdn.dt_bias").float()[r * self.hv:(r + 1) * self.hv].contiguous()
+                L["gnorm"] = get(p + "gdn.norm").to(torch.bfloat16).contiguous()
+                wo = get(p + "gdn.out_proj")
+                L["out_proj"] = pack_linear(wo[:, r * self.hv * dv:(r + 1) * self.hv * dv].contiguous(), C)
+            else:
+                L.update(self._load_attn(get, p))
+            L.update(self._load_moe(get, p))
+            self.layers.append(L)
+            torch.cuda.synchronize(dev)
+        self.gdn_index = {i: j for j, i in enumerate(cfg.gdn_layers)}
+        self.attn_index = {i: j for j, i in enumerate(cfg.attn_layers)}
+
+    def _load_attn(self, get, p: str) -> dict:
+        cfg, C, r = self.cfg, self.C, self.tp_rank
+        Hq, Hkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        w = get(p + "attn.qkv")
+        q = w[:Hq * 2 * D][r * self.hq * 2 * D:(r + 1) * self.hq * 2 * D]
+        kvh = (r * Hkv) // self.tp if self.tp > Hkv else r * self.hkv
+        k = w[Hq * 2 * D:Hq * 2 * D + Hkv * D][kvh * D:(kvh + self.hkv) * D]
+        v = w[Hq * 2 * D + Hkv * D:][kvh * D:(kvh + self.hkv) * D]
+        out = {"qkv": pack_linear(torch.cat([q, k, v], 0), C),
+               "q_norm": get(p + "attn.q_norm").to(torch.bfloat16).contiguous(),
+               "k_norm": get(p + "attn.k_norm").to(torch.bfloat16).contiguous()}
+        wo = get(p + "attn.o_proj")
+        out["o_proj"] = pack_linear(wo[:, r * self.hq * D:(r + 1) * self.hq * D].contiguous(), C)
+        return out
+
+    def _load_moe(self, get, p: str) -> dict:
+        cfg, C = self.cfg, self.C
+        H, E = cfg.hidden_size, cfg.num_experts
+        router = get(p + "moe.router")
+        sg = get(p + "moe.shared_gate")
+        out = {"router": pack_linear(torch.cat([router, sg], 0), C)}
+        eb, ee = self.e_begin, self.e_begin + self.e_local
+        gate = torch.cat([get(p + "moe.gate")[eb:ee], get(p + "moe.shared.gate")[None]], 0)
+        up = torch.cat([get(p + "moe.up")[eb:ee], get(p + "moe.shared.up")[None]], 0)
+        out["gate_up"] = pack_linear(interleave_gate_up(gate, up), C)
+        del gate, up
+        down = get(p + "moe.down")[eb:ee]
+        sd = get(p + "moe.shared.down")
+        if self.tp > 1:
+            # Output-sharded shared down-projection: zero the rows other ranks own.
+            n = H // self.tp
+            mask = torch.zeros(H, 1, dtype=sd.dtype, device=sd.device)
+            mask[self.tp_rank * n:(self.tp_rank + 1) * n] = 1
+            sd = sd * mask
+        out["down"] = pack_linear(torch.cat([down, sd[None]], 0), C)
+        return out
+
+    # ------------------------------------------------------------------ state
+    def _alloc_state(self) -> None:
+        cfg, dev = self.cfg, self.dev
+        nG, nA = len(cfg.gdn_layers), len(cfg.attn_layers)
+        conv_dim = 2 * self.hk * 128 + self.hv * 128
+        self.conv_dim = conv_dim
+        self.conv_state = torch.zeros(nG, self.num_slots, 2, conv_dim, 3, dtype=torch.bfloat16, device=dev)
+        self.ssm_state = torch.zeros(nG, self.num_slots, self.hv, 128, 128, dtype=torch.float32, device=dev)
+        kv_shape = (nA, self.num_pages, self.page_size, self.hkv, cfg.head_dim)
+        self.k_cache = torch.zeros(kv_shape, dtype=torch.bfloat16, device=dev)
+        self.v_cache = torch.zeros(kv_shape, dtype=torch.bfloat16, device=dev)
+        # Page table: one row per request slot (+ dummy row).  Page 0 is the dummy page.
+        self.page_table = torch.zeros(self.num_slots, self.max_pages, dtype=torch.int32, device=dev)
+
+    def _alloc_buffers(self) -> None:
+        cfg, dev = self.cfg, self.dev
+        H = cfg.hidden_size
+        R = max(self.max_seqs, self.max_prefill_tokens)
+        Rp = _pad128(R)
+        self.R = R
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.gdn_w = 2 * self.hk * 128 + 2 * self.hv * 128 + 2 * self.hv
+        self.qkv_w = (2 * self.hq + 2 * self.hkv) * cfg.head_dim
+        self.mid_w = max(self.hv * 128, self.hq * cfg.head_dim)
+        b = {}
+        b["hidden"] = torch.zeros(R, H, dtype=torch.bfloat16, device=dev)
+        b["xq"] = torch.zeros(Rp, H, dtype=torch.uint8, device=dev)
+        b["xsf"] = torch.zeros(mx.atoms_bytes(Rp, H), dtype=torch.uint8, device=dev)
+        b["proj"] = torch.zeros(R * max(self.gdn_w, self.qkv_w), dtype=torch.bfloat16, device=dev)
+        b["midq"] = torch.zeros(Rp * self.mid_w, dtype=torch.uint8, device=dev)
+        b["midsf"] = torch.zeros(mx.atoms_bytes(Rp, self.mid_w), dtype=torch.uint8, device=dev)
+        b["delta"] = torch.zeros(R, H, dtype=torch.bfloat16, device=dev)
+        b["q_out"] = torch.zeros(R, self.hq, cfg.head_dim, dtype=torch.bfloat16, device=dev)
+        b["gate_out"] = torch.zeros(R, self.hq, cfg.head_dim, dtype=torch.bfloat16, device=dev)
+        self.max_splits = 16
+        b["partial"] = torch.zeros(max(R * self.hq, self.max_seqs * self.hq * self.max_splits) * 260,
+                                   dtype=torch.float32, device=dev)
+        nr = self.layers[0]["router"].n_pad
+        b["logits"] = torch.zeros(R, nr, dtype=torch.float32, device=dev)
+        G = self.groups
+        b["topk_ids"] = torch.zeros(R, self.top_k, **i32)
+        b["topk_w"] = torch.zeros(R, self.top_k, dtype=torch.float32, device=dev)
+        b["gcount"] = torch.zeros(G, **i32)
+        b["goff"] = torch.zeros(G, **i32)
+        b["gpre"] = torch.zeros(G + 1, **i32)
+        b["pair_slot"] = torch.zeros(R, self.k1, **i32)
+        mg = _pad128(R * self.k1) + 128 * G
+        self.max_grouped = mg
+        b["row_dst"] = torch.zeros(mg, **i32)
+        b["row_scale"] = torch.zeros(mg, dtype=torch.float32, device=dev)
+        b["xg"] = torch.zeros(mg, H, dtype=torch.uint8, device=dev)
+        b["xg_sf"] = torch.zeros(mx.atoms_bytes(mg, H), dtype=torch.uint8, device=dev)
+        I = cfg.moe_intermediate_size
+        b["act"] = torch.zeros(mg, I, dtype=torch.uint8, device=dev)
+        b["act_sf"] = torch.zeros(mx.atoms_bytes(mg, I), dtype=torch.uint8, device=dev)
+        b["pair_out"] = torch.zeros(R * self.k1, H, dtype=torch.bfloat16, device=dev)
+        vt = self.lm_head.n_pad // 128
+        self.vocab_tiles = vt
+        b["lm_keys"] = torch.zeros(self.max_seqs, vt, dtype=torch.int64, device=dev)
+        b["out_ids"] = torch.zeros(self.max_seqs, **i32)
+        b["out_vals"] = torch.zeros(self.max_seqs, dtype=torch.float32, device=dev)
+        b["out_keys"] = torch.zeros(self.max_seqs, dtype=torch.int64, device=dev)
+        b["err"] = torch.zeros(1, **i32)
+        b["xq_last"] = torch.zeros(_pad128(self.max_seqs), H, dtype=torch.uint8, device=dev)
+        # Step inputs (static so graphs can read them): ids, positions, slots, seq_lens,
+        # packed as one [4, R] block so a step's inputs arrive in a single H2D copy.
+        b["inputs"] = torch.zeros(4, R, **i32)
+        b["in_ids"], b["in_pos"], b["in_slot"], b["in_len"] = b["inputs"].unbind(0)
+        self.host_inputs = torch.zeros(4, R, dtype=torch.int32, pin_memory=True)
+        b["seq_start"] = torch.zeros(self.max_seqs + 1, **i32)
+        b["last_rows"] = torch.zeros(self.max_seqs, dtype=torch.int64, device=dev)
+        self.buf = b
+
+    # ------------------------------------------------------------------ kernels
+    def _gemm(self, w: PackedLinear, xq, xsf, rows: int, out, ldo: int, epi=EPI_BF16, grouped=False,
+              out_sf=None, row_dst=None, row_scale=None):
+        b = self.buf
+        if grouped:
+            self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, w.groups, 0, b["gcount"], b["goff"], b["gpre"],
+                             epi, out, ldo, out_sf, row_dst, row_scale, b["err"], 0)
+        else:
+            self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, 1, rows, None, None, None, epi, out, ldo,
+                             out_sf, row_dst, row_scale, b["err"], 0)
+
+    def _mid(self, width: int) -> torch.Tensor:
+        rp = _pad128(self.R)
+        return self.buf["midq"][: rp * width].view(rp, width)
+
+    def _attn_splits(self, rows: int, decode: bool) -> int:
+        if not decode:
+            return 1
+        ctas = rows * self.hkv
+        return int(max(1, min(self.max_splits, math.ceil(2 * 148 / max(ctas, 1)))))
+
+    def _row_parallel_reduce(self, delta_rows: torch.Tensor, rows: int, n_terms: int, norm_w, term_stride: int,
+                             row_stride: int):
+        """hidden += sum of delta terms (all-reduced across tp ranks), then RMSNorm -> xq."""
+        b, H = self.buf, self.cfg.hidden_size
+        if self.tp > 1:
+            self.coll.allreduce_add_rmsnorm(delta_rows, n_terms, row_stride, term_stride, b["hidden"], norm_w,
+                                            self.eps, rows, b["xq"], b["xsf"])
+            return
+        self.C.add_rmsnorm_quant(b["hidden"], delta_rows, n_terms, row_stride, term_stride, norm_w, 1.0, self.eps,
+                                 rows, None, b["xq"], b["xsf"])
+
+    def _layers(self, rows: int, decode: bool, num_seqs: int = 0, ckpt=None) -> None:
+        cfg, C, b = self.cfg, self.C, self.buf
+        H = cfg.hidden_size
+        pos, slot, lens = b["in_pos"][:rows], b["in_slot"][:rows], b["in_len"][:rows]
+        C.embed_rmsnorm_quant(b["in_ids"][:rows], self.embed, b["hidden"], self.layers[0]["input_norm"], 1.0,
+                              self.eps, rows, None, b["xq"], b["xsf"])
+        for li, L in enumerate(self.layers):
+            if L["type"] == "linear_attention":
+                gi = self.gdn_index[li]
+                proj = b["proj"][:rows * self.gdn_w].view(rows, self.gdn_w)
+                self._gemm(L["in_proj"], b["xq"], b["xsf"], rows, proj, self.gdn_w)
+                midq = self._mid(self.hv * 128)
+                args = (proj, self.hk, self.hv, L["conv_w"], self.conv_state[gi], self.ssm_state[gi], L["a_log"],
+                        L["dt_bias"], L["gnorm"], self.eps, slot, pos, rows, None, midq, b["midsf"])
+                if decode:
+                    C.gdn_decode(*args, b["err"])
+                else:
+                    ck_rows, ck_slots, max_ck = ckpt if ckpt is not None else (None, None, 0)
+                    C.gdn_prefill(*args, b["seq_start"][:num_seqs + 1], num_seqs, ck_rows, ck_slots, max_ck,
+                                  b["err"])
+                self._gemm(L["out_proj"], midq, b["midsf"], rows, b["delta"], H)
+            else:
+                ai = self.attn_index[li]
+                qkv = b["proj"][:rows * self.qkv_w].view(rows, self.qkv_w)
+                self._gemm(L["qkv"], b["xq"], b["xsf"], rows, qkv, self.qkv_w)
+                C.attn_prologue(qkv, self.hq, self.hkv, cfg.rotary_dim, cfg.rope_theta, L["q_norm"], L["k_norm"],
+                                self.eps, self.k_cache[ai], self.v_cache[ai], self.page_size, self.page_table, slot,
+                                pos, rows, b["q_out"], b["gate_out"])
+                midq = self._mid(self.hq * cfg.head_dim)
+                splits = self._attn_splits(rows, decode)
+                C.attn_decode(b["q_out"], b["gate_out"], self.hq, self.hkv, self.k_cache[ai], self.v_cache[ai],
+                              self.page_size, self.page_table, slot, lens, rows, b["partial"], splits,
+                              1.0 / math.sqrt(cfg.head_dim), None, midq, b["midsf"])
+                self._gemm(L["o_proj"], midq, b["midsf"], rows, b["delta"], H)
+            self._row_parallel_reduce(b["delta"], rows, 1, L["post_norm"], H, H)
+            self._moe(L, rows)
+            next_w = self.layers[li + 1]["input_norm"] if li + 1 < len(self.layers) else self.final_norm
+            self._row_parallel_reduce(b["pair_out"], rows, self.k1, next_w, H, self.k1 * H)
+
+    def _moe(self, L, rows: int) -> None:
+        cfg, C, b = self.cfg, self.C, self.buf
+        E = cfg.num_experts
+        self._gemm(L["router"], b["xq"], b["xsf"], rows, b["logits"], b["logits"].shape[1], EPI_F32)
+        C.moe_route(b["logits"], rows, E, self.top_k, cfg.norm_topk_prob, 0, None, 1, 1, 1.0, E,
+                    self.e_begin, self.e_begin + self.e_local, True, b["topk_ids"], b["topk_w"], b["gcount"],
+                    b["goff"], b["gpre"], b["pair_slot"], b["row_dst"], b["row_scale"], b["xq"], b["xsf"], b["xg"],
+                    b["xg_sf"], b["err"])
+        if self.tp > 1:
+            # Pair rows of experts owned by other ranks must not leak stale values.
+            b["pair_out"][: rows * self.k1].zero_()
+        I = cfg.moe_intermediate_size
+        self._gemm(L["gate_up"], b["xg"], b["xg_sf"], rows, b["act"], I, EPI_SILU, grouped=True, out_sf=b["act_sf"])
+        self._gemm(L["down"], b["act"], b["act_sf"], rows, b["pair_out"], cfg.hidden_size, EPI_SCATTER, grouped=True,
+                   row_dst=b["row_dst"], row_scale=b["row_scale"])
+
+    def _lm_head_argmax(self, rows: int, xq=None, xsf=None) -> None:
+        b = self.buf
+        xq = b["xq"] if xq is None else xq
+        xsf = b["xsf"] if xsf is None else xsf
+        self._gemm(self.lm_head, xq, xsf, rows, b["lm_keys"], self.vocab_tiles, EPI_ARGMAX)
+        if self.tp > 1:
+            self.coll.argmax_allreduce(b["lm_keys"], rows, self.vocab_tiles, self.tp_rank * self.vocab_local,
+                                       b["out_ids"], b["out_vals"])
+        else:
+            self.C.argmax_reduce(b["lm_keys"], rows, self.vocab_tiles, b["out_ids"], b["out_vals"], b["out_keys"])
+
+    # ------------------------------------------------------------------ public step API
+    def decode_forward(self, rows: int) -> torch.Tensor:
+        """Run one decode step over the first `rows` staged inputs; returns out_ids[:rows]."""
+        self._layers(rows, decode=True)
+        self._lm_head_argmax(rows)
+        return self.buf["out_ids"][:rows]
+
+    def prefill_forward(self, rows: int, num_seqs: int, ckpt=None) -> torch.Tensor:
+        """Varlen prefill over `rows` staged tokens in `num_seqs` sequences (seq_start staged).
+        Returns the greedy next token of each sequence (from its last row)."""
+        b = self.buf
+        self._layers(rows, decode=False, num_seqs=num_seqs, ckpt=ckpt)
+        # lm_head only on each sequence's last row: gather those normed rows.
+        last = b["seq_start"][1:num_seqs + 1].long() - 1
+        H = self.cfg.hidden_size
+        xq_last = b["xq_last"]
+        codes = self._gather_sf(b["xsf"], last, H)
+        xq_last[:num_seqs] = b["xq"][last]
+        sf_last = mx.atoms_from_codes(codes)
+        self._lm_head_argmax(num_seqs, xq_last, sf_last)
+        return b["out_ids"][:num_seqs]
+
+    def _gather_sf(self, atoms: torch.Tensor, rows_idx: torch.Tensor, k: int):
+        """Gather scale codes of selected rows from an atom buffer (device ops)."""
+        nkb = k // 32
+        rb = rows_idx // 128
+        rr = rows_idx % 128
+        kb = torch.arange(nkb, device=atoms.device)
+        off = (rb[:, None] * (k // 128) + kb[None, :] // 4) * 512 + (rr[:, None] % 32) * 16 + (rr[:, None] // 32) * 4 \
+            + kb[None, :] % 4
+        return atoms[off]
+
+    def stage(self, ids, positions, slots, seq_lens=None, seq_start=None) -> int:
+        """Write step inputs into the pinned staging block and copy it to the device in one
+        H2D transfer (4 x R int32).  Returns the number of rows."""
+        b, h = self.buf, self.host_inputs
+        n = len(ids)
+        h[0, :n] = torch.as_tensor(ids, dtype=torch.int32)
+        h[1, :n] = torch.as_tensor(positions, dtype=torch.int32)
+        h[2, :n] = torch.as_tensor(slots, dtype=torch.int32)
+        if seq_lens is None:
+            h[3, :n] = h[1, :n] + 1
+        else:
+            h[3, :n] = torch.as_tensor(seq_lens, dtype=torch.int32)
+        for i in range(4):
+            b["inputs"][i, :n].copy_(h[i, :n], non_blocking=True)
+        if seq_start is not None:
+            b["seq_start"][:len(seq_start)].copy_(torch.as_tensor(seq_start, dtype=torch.int32))
+        self._staged_rows = n
+        return n
+
+    def staged_bytes(self) -> int:
+        """Host->device bytes moved by the last stage() call."""
+        return 4 * 4 * getattr(self, "_staged_rows", 0)
+
+    def set_pages(self, slot: int, pages: list[int]) -> None:
+        self.page_table[slot, :len(pages)] = torch.as_tensor(pages, dtype=torch.int32, device=self.dev)
+
+    def bucket_for(self, n: int) -> int:
+        for bk in DECODE_BUCKETS:
+            if bk >= n and bk <= self.max_seqs:
+                return bk
+        return self.max_seqs
+
+    def pad_decode_inputs(self, n: int, bucket: int) -> None:
+        """Point padding rows [n, bucket) at the dummy slot/page (their outputs are ignored)."""
+        if bucket > n:
+            b = self.buf
+            b["in_ids"][n:bucket] = 0
+            b["in_pos"][n:bucket] = 1
+            b["in_slot"][n:bucket] = self.dummy_slot
+            b["in_len"][n:bucket] = 1
+
+    def capture_decode_graph(self, bucket: int) -> None:
+        """Capture one decode step over `bucket` rows into a CUDA graph."""
+        b = self.buf
+        self.pad_decode_inputs(0, bucket)
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.decode_forward(bucket)
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            self.decode_forward(bucket)
+        self.graphs[bucket] = g
+
+    def decode_step(self, n: int) -> torch.Tensor:
+        """Replay the graph of the bucket that fits n staged rows (captured on demand)."""
+        bucket = self.bucket_for(n)
+        self.pad_decode_inputs(n, bucket)
+        if bucket not in self.graphs:
+            self.capture_decode_graph(bucket)
+            self.pad_decode_inputs(n, bucket)
+        self.graphs[bucket].replay()
+        return self.buf["out_ids"][:n]
+
+    def check_error(self) -> int:
+        return int(self.buf["err"].item())
