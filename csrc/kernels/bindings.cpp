@@ -40,7 +40,8 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
                int64_t n_pad, int64_t n_valid, int64_t groups, int64_t m_rows,
                const OptT& group_count, const OptT& group_offset, const OptT& chunk_prefix,
                int64_t epi_mode, const Tensor& out, int64_t ldo, const OptT& out_sf,
-               const OptT& row_dst, const OptT& row_scale, const OptT& err, int64_t max_items) {
+               const OptT& row_dst, const OptT& row_scale, const OptT& err, int64_t max_items,
+               int64_t block_n, int64_t k_splits, int64_t split_stride) {
   check_cuda(a, "a");
   check_cuda(sfa, "sfa");
   check_cuda(b, "b");
@@ -74,6 +75,12 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
   p.row_dst = optptr<const int>(row_dst);
   p.row_scale = optptr<const float>(row_scale);
   p.err = optptr<int>(err);
+  p.block_n = (int)block_n;
+  p.chunk_rows = (int)block_n;
+  p.k_splits = (int)k_splits;
+  p.split_stride = split_stride;
+  if (k_splits > 1)
+    TORCH_CHECK(out.numel() >= (k_splits - 1) * split_stride + m_rows * ldo, "split-K out too small");
   TORCH_CHECK(p.chunk_prefix == nullptr || (p.group_count && p.group_offset), "grouped mode args");
   if (p.chunk_prefix == nullptr) TORCH_CHECK(m_rows <= p.b_rows, "m_rows > rows of b");
   rc(zs_gemm_mxf8(&p, stream()), "zs_gemm_mxf8");
@@ -101,7 +108,10 @@ void add_rmsnorm_quant(const Tensor& residual, const OptT& delta, int64_t n_term
   check_opt(sf, "sf");
   const int hidden = (int)residual.size(-1);
   TORCH_CHECK(residual.numel() >= rows * hidden, "residual too small");
-  rc(zs_add_rmsnorm_quant(ptr(residual), optptr(delta), (int)n_terms, d_row_stride, d_term_stride,
+  const int f32 = delta.has_value() && delta->scalar_type() == at::kFloat ? 1 : 0;
+  if (delta.has_value())
+    TORCH_CHECK(f32 || delta->scalar_type() == at::kBFloat16, "delta must be bf16 or f32");
+  rc(zs_add_rmsnorm_quant(ptr(residual), optptr(delta), (int)n_terms, d_row_stride, d_term_stride, f32,
                           ptr(weight), (float)w_offset, (float)eps, (int)rows, hidden,
                           optptr(normed), optptr<uint8_t>(q), optptr<uint8_t>(sf), stream()),
      "zs_add_rmsnorm_quant");
@@ -255,12 +265,18 @@ void moe_route(const Tensor& logits, int64_t rows, int64_t num_experts, int64_t 
                const Tensor& topk_w, const Tensor& group_count, const Tensor& group_offset,
                const Tensor& chunk_prefix, const Tensor& pair_slot, const Tensor& row_dst,
                const Tensor& row_scale, const Tensor& x_q, const Tensor& x_sf,
-               const Tensor& xg_q, const Tensor& xg_sf, const OptT& err) {
+               const Tensor& xg_q, const Tensor& xg_sf, const OptT& err, int64_t ld_logits,
+               int64_t logit_splits, int64_t logit_split_stride, int64_t chunk_rows) {
   check_cuda(logits, "logits");
   TORCH_CHECK(logits.scalar_type() == at::kFloat, "logits must be f32");
   MoeRouteArgs a{};
   a.logits = ptr<const float>(logits);
-  a.ld_logits = (int)logits.size(-1);
+  a.ld_logits = (int)ld_logits;
+  a.logit_splits = (int)logit_splits;
+  a.logit_split_stride = logit_split_stride;
+  a.chunk_rows = (int)chunk_rows;
+  TORCH_CHECK(logits.numel() >= (logit_splits > 1 ? (logit_splits - 1) * logit_split_stride : 0) +
+                                    rows * ld_logits, "logits too small");
   a.rows = (int)rows;
   a.num_experts = (int)num_experts;
   a.top_k = (int)top_k;

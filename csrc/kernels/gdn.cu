@@ -1,4 +1,5 @@
-// GatedDeltaNet (Qwen3.5 linear attention) for sm_100a.
+// GatedDeltaNet (Qwen3.5 linear attention) varlen prefill for sm_100a (the decode step
+// lives in gdn_decode.cu).
 //
 // One CTA owns one (sequence, value head) pair and fuses the whole layer body:
 //   causal depthwise conv (k=4) + SiLU on the q/k/v channels of that head,
@@ -202,44 +203,6 @@ __device__ __forceinline__ float delta_step(float (&st)[32], int vr, int kq, con
   return o;
 }
 
-__global__ void __launch_bounds__(THREADS, 1) gdn_decode_kernel(const GdnArgs a) {
-  __shared__ Smem s;
-  const int row = blockIdx.x;
-  const int vh = blockIdx.y;
-  const int ratio = a.num_v_heads / a.num_k_heads;
-  const int kh = vh / ratio;
-  const int t = threadIdx.x;
-  const int vr = t >> 2, kq = t & 3;
-  const int slot = a.slots[row];
-  const int pos = a.positions[row];
-  const bool fresh = pos == 0;
-  float* sp = a.ssm_state + (((size_t)slot * a.num_v_heads + vh) * DV + vr) * DK + kq * 32;
-  float st[32];
-  if (!fresh) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float4 f = reinterpret_cast<const float4*>(sp)[i];
-      st[4 * i] = f.x; st[4 * i + 1] = f.y; st[4 * i + 2] = f.z; st[4 * i + 3] = f.w;
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) st[i] = 0.f;
-  }
-  if (!fresh) load_window(a, slot, pos, kh, vh, s);
-  __syncthreads();
-  conv_token(a, row, kh, vh, s, fresh);
-  __syncthreads();
-  store_window(a, slot, pos + 1, kh, vh, s, (vh % ratio) == 0);
-  qk_norm_and_gates(a, row, vh, s);
-  const float o = delta_step(st, vr, kq, s);
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-    reinterpret_cast<float4*>(sp)[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
-  if (kq == 0) s.o[vr] = o;
-  __syncthreads();
-  gated_norm_out(a, row, vh, s);
-}
-
 __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_kernel(const GdnArgs a) {
   __shared__ Smem s;
   const int seq = blockIdx.x;
@@ -296,17 +259,6 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_kernel(const GdnArgs a
 
 }  // namespace gdn
 }  // namespace zs
-
-extern "C" int zs_gdn_decode(const GdnArgs* args, cudaStream_t stream) {
-  const GdnArgs& a = *args;
-  if (a.head_k != zs::gdn::DK || a.head_v != zs::gdn::DV || a.num_k_heads <= 0 ||
-      a.num_v_heads % a.num_k_heads != 0)
-    return -1;
-  if (a.rows == 0) return 0;
-  dim3 grid(a.rows, a.num_v_heads);
-  zs::gdn::gdn_decode_kernel<<<grid, zs::gdn::THREADS, 0, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -2;
-}
 
 extern "C" int zs_gdn_prefill(const GdnArgs* args, cudaStream_t stream) {
   const GdnArgs& a = *args;

@@ -1,0 +1,315 @@
+// GatedDeltaNet decode step for sm_100a: persistent, TMA-pipelined state streaming.
+//
+// A decode step reads and rewrites the fp32 recurrent state of every (token, value
+// head): 64 KiB in + 64 KiB out, with almost no math per byte, so the kernel is built
+// as a pure streaming pipeline:
+//   * one CTA per SM walks a static list of (row, value head) items;
+//   * a producer warp stages each item's state (one 64 KiB cp.async.bulk), its conv
+//     windows, conv weights and projected q/k/v/z slices into a 3-deep shared-memory
+//     ring (mbarrier transaction counts), running up to 3 items ahead;
+//   * 16 compute warps (4 threads per value row, 32 state coefficients each) run the
+//     causal conv + SiLU, q/k L2 norms, the delta rule and the gated RMSNorm from
+//     shared memory, write the new state / windows back in place and emit the output
+//     (bf16 and/or one MXFP8 block per 32 values);
+//   * the producer writes each finished stage back with bulk stores
+//     (cp.async.bulk.global.shared::cta) before reusing it, so loads, compute and
+//     stores of different items overlap.
+// Conv windows are double-buffered by position parity (the window preceding position p
+// lives in buffer p & 1): an item reads buffer p & 1 and writes buffer (p+1) & 1, so
+// the value heads sharing a q/k head read the old q/k window while the owner (the
+// first value head of the group) writes the new one.
+//
+// Reference parity: worker/zstep_worker/kernels_sm120/qwen35_ops.py:659-935 (conv,
+// delta rule, gated norm; state stored [V, K]) and the fused decode kernels of
+// kernels_sm120/csrc/qwen35_ops_kernels.cu:354-757.
+#include "sm100_common.cuh"
+#include "zs_kernels.h"
+
+namespace zs {
+namespace gdn_dec {
+
+constexpr int DK = 128, DV = 128;
+constexpr int STAGES = 3;
+constexpr int COMPUTE_WARPS = 16;
+constexpr int THREADS = COMPUTE_WARPS * 32 + 32;  // + producer warp
+constexpr uint32_t STATE_BYTES = DK * DV * 4;
+
+struct Stage {
+  float state[DV * DK];          // [v][k]
+  __nv_bfloat16 x[3 * 128];      // projected q | k | v channels of the item (conv inputs)
+  __nv_bfloat16 z[128];          // gate input z
+  __nv_bfloat16 win[3 * 128 * 3];  // conv windows (q | k | v), 3 taps per channel
+  __nv_bfloat16 w[3 * 128 * 4];    // conv weights (q | k | v), 4 taps per channel
+};
+
+struct Smem {
+  Stage st[STAGES];
+  float conv_out[3 * 128];  // q | k | v after conv + SiLU (fp32)
+  float o[DV];
+  float red[COMPUTE_WARPS * 2];
+  float scal[4];
+  uint64_t full[STAGES];
+  uint64_t computed[STAGES];
+  int abort_flag;
+};
+
+__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst),
+               "r"(smem_u32(ssrc)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ bool wait_flag(uint64_t* bar, uint32_t phase, int* err, volatile int* abort_flag) {
+  for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {
+    if (mbar_try_wait(bar, phase)) return true;
+    if (*abort_flag) return false;
+    if (i > 32) __nanosleep(32);
+  }
+  report_error(err, kErrMbarTimeout);
+  *abort_flag = 1;
+  return false;
+}
+
+struct ItemInfo {
+  int row, vh, kh, slot, pos;
+};
+
+__device__ __forceinline__ ItemInfo item_info(const GdnArgs& a, int idx) {
+  ItemInfo it;
+  it.row = idx / a.num_v_heads;
+  it.vh = idx % a.num_v_heads;
+  it.kh = it.vh / (a.num_v_heads / a.num_k_heads);
+  it.slot = a.slots[it.row];
+  it.pos = a.positions[it.row];
+  return it;
+}
+
+// Write back a finished stage: state, the new conv windows (q/k only by the first value
+// head of the q/k head's group), all as bulk stores from shared memory.
+__device__ __forceinline__ void store_stage(const GdnArgs& a, Stage& st, const ItemInfo& it, int conv_dim) {
+  const int ratio = a.num_v_heads / a.num_k_heads;
+  float* gstate = a.ssm_state + ((size_t)it.slot * a.num_v_heads + it.vh) * DV * DK;
+  bulk_store(gstate, st.state, STATE_BYTES);
+  __nv_bfloat16* cs = static_cast<__nv_bfloat16*>(a.conv_state) +
+                      ((size_t)it.slot * 2 + ((it.pos + 1) & 1)) * conv_dim * 3;
+  if (it.vh % ratio == 0) {
+    bulk_store(cs + (size_t)it.kh * 128 * 3, st.win, 128 * 3 * 2);
+    bulk_store(cs + (size_t)(a.num_k_heads + it.kh) * 128 * 3, st.win + 128 * 3, 128 * 3 * 2);
+  }
+  bulk_store(cs + (size_t)(2 * a.num_k_heads * 128 + it.vh * 128) * 3, st.win + 2 * 128 * 3, 128 * 3 * 2);
+  bulk_commit();
+}
+
+__global__ void __launch_bounds__(THREADS, 1) gdn_decode_tma_kernel(const GdnArgs a, int total_items) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int Hk = a.num_k_heads, Hv = a.num_v_heads;
+  const int conv_dim = 2 * Hk * DK + Hv * DV;
+  volatile int* abort_flag = &s.abort_flag;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.computed[i], 1);
+    }
+    s.abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == COMPUTE_WARPS) {
+    // ------------------------------------------------------------------ producer
+    if (lane == 0) {
+      ItemInfo pend[STAGES];
+      int n_local = 0;
+      const __nv_bfloat16* proj = static_cast<const __nv_bfloat16*>(a.proj);
+      const __nv_bfloat16* cw = static_cast<const __nv_bfloat16*>(a.conv_w);
+      const __nv_bfloat16* csg = static_cast<const __nv_bfloat16*>(a.conv_state);
+      for (int idx = blockIdx.x; idx < total_items && !*abort_flag; idx += gridDim.x, ++n_local) {
+        const int sidx = n_local % STAGES;
+        Stage& st = s.st[sidx];
+        if (n_local >= STAGES) {
+          // Stage reuse: write back the item computed STAGES items ago first.
+          if (!wait_flag(&s.computed[sidx], ((n_local - STAGES) / STAGES) & 1, a.err, abort_flag)) break;
+          store_stage(a, st, pend[sidx], conv_dim);
+          bulk_wait_read0();
+        }
+        const ItemInfo it = item_info(a, idx);
+        pend[sidx] = it;
+        const bool fresh = it.pos == 0;
+        const uint32_t bytes = (fresh ? 0u : STATE_BYTES + 3 * 128 * 3 * 2) + 4 * 128 * 2 + 3 * 128 * 4 * 2;
+        mbar_expect_tx(&s.full[sidx], bytes);
+        const __nv_bfloat16* prow = proj + (size_t)it.row * a.ld_proj;
+        bulk_load(st.x, prow + it.kh * 128, 256, &s.full[sidx]);
+        bulk_load(st.x + 128, prow + (Hk + it.kh) * 128, 256, &s.full[sidx]);
+        bulk_load(st.x + 256, prow + 2 * Hk * 128 + it.vh * 128, 256, &s.full[sidx]);
+        bulk_load(st.z, prow + conv_dim + it.vh * 128, 256, &s.full[sidx]);
+        bulk_load(st.w, cw + (size_t)it.kh * 128 * 4, 1024, &s.full[sidx]);
+        bulk_load(st.w + 512, cw + (size_t)(Hk + it.kh) * 128 * 4, 1024, &s.full[sidx]);
+        bulk_load(st.w + 1024, cw + (size_t)(2 * Hk * 128 + it.vh * 128) * 4, 1024, &s.full[sidx]);
+        if (!fresh) {
+          const __nv_bfloat16* cs = csg + ((size_t)it.slot * 2 + (it.pos & 1)) * conv_dim * 3;
+          bulk_load(st.win, cs + (size_t)it.kh * 128 * 3, 768, &s.full[sidx]);
+          bulk_load(st.win + 384, cs + (size_t)(Hk + it.kh) * 128 * 3, 768, &s.full[sidx]);
+          bulk_load(st.win + 768, cs + (size_t)(2 * Hk * 128 + it.vh * 128) * 3, 768, &s.full[sidx]);
+          bulk_load(st.state, a.ssm_state + ((size_t)it.slot * Hv + it.vh) * DV * DK, STATE_BYTES, &s.full[sidx]);
+        }
+      }
+      // Drain: write back the last (up to STAGES) items, then wait for all stores.
+      const int first = n_local > STAGES ? n_local - STAGES : 0;
+      for (int j = first; j < n_local && !*abort_flag; ++j) {
+        const int sidx = j % STAGES;
+        if (!wait_flag(&s.computed[sidx], (j / STAGES) & 1, a.err, abort_flag)) break;
+        store_stage(a, s.st[sidx], pend[sidx], conv_dim);
+      }
+      bulk_wait_all0();
+      // Loads that were issued but never consumed (abort): wait for them to land.
+      for (int j = first; j < n_local; ++j)
+        if (!mbar_wait(&s.full[j % STAGES], (j / STAGES) & 1, nullptr)) report_error(a.err, kErrDrainTimeout);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------------- compute warps
+  const int t = threadIdx.x;  // 0..511
+  const int vr = t >> 2, kq = t & 3;
+  int n_local = 0;
+  for (int idx = blockIdx.x; idx < total_items; idx += gridDim.x, ++n_local) {
+    const int sidx = n_local % STAGES;
+    Stage& st = s.st[sidx];
+    if (!wait_flag(&s.full[sidx], (n_local / STAGES) & 1, a.err, abort_flag)) break;
+    const ItemInfo it = item_info(a, idx);
+    const bool fresh = it.pos == 0;
+    // 1. conv + SiLU (threads 0..383, one channel each); new window written in place.
+    if (t < 384) {
+      const float x = __bfloat162float(st.x[t]);
+      __nv_bfloat16* win = st.win + t * 3;
+      const float w0 = fresh ? 0.f : __bfloat162float(win[0]);
+      const float w1 = fresh ? 0.f : __bfloat162float(win[1]);
+      const float w2 = fresh ? 0.f : __bfloat162float(win[2]);
+      const __nv_bfloat16* w = st.w + t * 4;
+      const float acc = __bfloat162float(w[0]) * w0 + __bfloat162float(w[1]) * w1 +
+                        __bfloat162float(w[2]) * w2 + __bfloat162float(w[3]) * x;
+      win[0] = __float2bfloat16_rn(w1);
+      win[1] = __float2bfloat16_rn(w2);
+      win[2] = st.x[t];
+      const float y = __bfloat162float(__float2bfloat16_rn(siluf_(acc)));
+      s.conv_out[t] = y;
+      // Partial sums of squares: warps 0-3 hold q, 4-7 hold k.
+      const float sq = warp_sum(y * y);
+      if (lane == 0) s.red[warp] = sq;
+    }
+    if (t == 0) {
+      const __nv_bfloat16* prow = static_cast<const __nv_bfloat16*>(a.proj) + (size_t)it.row * a.ld_proj;
+      const int boff = conv_dim + Hv * DV;
+      const float b_raw = __bfloat162float(prow[boff + it.vh]);
+      const float a_raw = __bfloat162float(prow[boff + Hv + it.vh]);
+      const float sp_in = a_raw + a.dt_bias[it.vh];
+      const float softplus = sp_in > 20.f ? sp_in : log1pf(__expf(sp_in));
+      s.scal[0] = sigmoidf_(b_raw);
+      s.scal[1] = __expf(-__expf(a.a_log[it.vh]) * softplus);
+    }
+    asm volatile("bar.sync 3, 512;" ::: "memory");  // compute warps only
+    const float rq = rsqrtf(s.red[0] + s.red[1] + s.red[2] + s.red[3] + 1e-6f) * rsqrtf((float)DK);
+    const float rk = rsqrtf(s.red[4] + s.red[5] + s.red[6] + s.red[7] + 1e-6f);
+    const float beta = s.scal[0], g = s.scal[1];
+    // 2. delta rule on 32 coefficients (state row vr, k-quarter kq) from shared memory.
+    float4* srow = reinterpret_cast<float4*>(st.state + vr * DK + kq * 32);
+    float c[32];
+    if (!fresh) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 f = srow[i];
+        c[4 * i] = f.x; c[4 * i + 1] = f.y; c[4 * i + 2] = f.z; c[4 * i + 3] = f.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) c[i] = 0.f;
+    }
+    const float* qv = s.conv_out + kq * 32;
+    const float* kv = s.conv_out + 128 + kq * 32;
+    float kvm = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      c[i] *= g;
+      kvm += c[i] * kv[i];
+    }
+    kvm *= rk;
+    kvm += __shfl_xor_sync(0xffffffff, kvm, 1);
+    kvm += __shfl_xor_sync(0xffffffff, kvm, 2);
+    const float delta = (s.conv_out[256 + vr] - kvm) * beta * rk;  // folds the k norm into delta
+    float o = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      c[i] += kv[i] * delta;
+      o += c[i] * qv[i];
+    }
+    o *= rq;
+    o += __shfl_xor_sync(0xffffffff, o, 1);
+    o += __shfl_xor_sync(0xffffffff, o, 2);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) srow[i] = make_float4(c[4 * i], c[4 * i + 1], c[4 * i + 2], c[4 * i + 3]);
+    if (kq == 0) s.o[vr] = o;
+    // Make the generic-proxy smem writes (state, windows) visible to the bulk stores.
+    fence_proxy_async_shared();
+    asm volatile("bar.sync 3, 512;" ::: "memory");
+    // 3. gated RMSNorm + output (warps 0-3, one value each).
+    if (t < DV) {
+      const float ov = s.o[t];
+      const float ss = warp_sum(ov * ov);
+      if (lane == 0) s.red[8 + warp] = ss;
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // warps 0-3 only
+      const float tot = s.red[8] + s.red[9] + s.red[10] + s.red[11];
+      const float rstd = rsqrtf(tot / DV + a.eps);
+      const float z = __bfloat162float(st.z[t]);
+      const float w = __bfloat162float(static_cast<const __nv_bfloat16*>(a.norm_w)[t]);
+      const float y = __bfloat162float(__float2bfloat16_rn(ov * rstd)) * w * siluf_(z);
+      const int width = Hv * DV;
+      const int col = it.vh * DV + t;
+      if (a.out_bf16 != nullptr)
+        static_cast<__nv_bfloat16*>(a.out_bf16)[(size_t)it.row * width + col] = __float2bfloat16_rn(y);
+      if (a.out_q != nullptr) {
+        const float yb = __bfloat162float(__float2bfloat16_rn(y));
+        const uint8_t code = mx_scale_e8m0(warp_max(fabsf(yb)));
+        a.out_q[(size_t)it.row * width + col] = f32_to_e4m3(yb * mx_inv_scale(code));
+        if (lane == 0) {
+          const int kb = col >> 5;
+          a.out_sf[((size_t)(it.row >> 7) * (width >> 7) + (kb >> 2)) * 512 +
+                   sf_atom_offset(it.row & 127, kb & 3)] = code;
+        }
+      }
+    }
+    // 4. hand the stage to the producer for write-back (all compute warps are past
+    //    their last read of it once they reach this barrier).
+    asm volatile("bar.sync 2, 512;" ::: "memory");
+    if (t == 0) mbar_arrive(&s.computed[sidx]);
+  }
+}
+
+}  // namespace gdn_dec
+}  // namespace zs
+
+extern "C" int zs_gdn_decode(const GdnArgs* args, cudaStream_t stream) {
+  using namespace zs::gdn_dec;
+  const GdnArgs& a = *args;
+  if (a.head_k != DK || a.head_v != DV || a.num_k_heads <= 0 || a.num_v_heads % a.num_k_heads != 0) return -1;
+  if (a.ld_proj % 8 != 0) return -1;  // 16-byte aligned projection rows for the bulk copies
+  if (a.rows == 0) return 0;
+  const int items = a.rows * a.num_v_heads;
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const int grid = items < sms ? items : sms;
+  const size_t smem = sizeof(Smem) + 128;
+  cudaFuncSetAttribute(gdn_decode_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  gdn_decode_tma_kernel<<<grid, THREADS, smem, stream>>>(a, items);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}

@@ -2,15 +2,17 @@
 // TMA-fed shared-memory operands and TMEM accumulators.
 //
 // Orientation ("swap-AB"): the weight matrix is the MMA's M side (128 output features
-// per tile) and the tokens are the N side (16..128 per pass), so decode batches of a
+// per tile) and the tokens are the N side (16..BN per pass), so decode batches of a
 // handful of tokens per expert still issue full-height MMAs and the kernel streams the
 // weights at HBM rate.  One persistent CTA per SM walks a static list of work items
-// (group, 128-feature tile, 128-token chunk).  Roles inside a CTA:
+// (group, 128-feature tile, BN-token chunk, K split).  Roles inside a CTA:
 //   warps 0-3 : epilogue (TMEM -> registers -> fused op -> global)
 //   warp 4    : TMA / bulk-copy producer
-//   warp 5    : MMA issuer (one elected thread) + scale-factor TMEM staging
+//   warp 5    : MMA issuer (one thread) + scale-factor TMEM staging (tcgen05.cp)
 // Accumulators are double-buffered in TMEM so the epilogue of tile i overlaps the
-// main loop of tile i+1.
+// main loop of tile i+1.  Two instantiations: BN=128 (6 stages) for prefill-sized
+// token counts, BN=32 (9 stages) for decode, where each expert sees a few tokens and
+// the kernel is a weight stream that wants as many bytes in flight as possible.
 //
 // Operand formats (all produced by this library's quantizers):
 //   A  weights      e4m3 [G * Npad, K], K contiguous; Npad % 128 == 0, K % 128 == 0
@@ -18,7 +20,13 @@
 //   B  activations  e4m3 [rows, K] in per-group segments starting at multiples of 128
 //   SFB act sf      e8m0 [rows/128, K/128, 512]
 // Atom byte layout: row r = r0 + 32*r1 (r0 < 32) and 32-wide K block j (j < 4) live
-// at byte r0*16 + r1*4 + j, which is what tcgen05.cp.32x128b.warpx4 expects.
+// at byte r0*16 + r1*4 + j, which is what tcgen05.cp.32x128b.warpx4 expects: TMEM
+// column r1 holds rows 32*r1..32*r1+31, so a 32-token chunk that starts 32*j rows
+// into an atom points the MMA's B-scale address at column j of the staged atom.
+//
+// Split-K (dense mode): item (m, chunk, ks) covers K tiles [ks*kps, (ks+1)*kps) and
+// stores fp32 partials at out + ks*split_stride; consumers sum the splits in a fixed
+// order, so results are deterministic.
 //
 // Reference parity: replaces the reference's Triton grouped MoE GEMMs and skinny
 // linears (worker/zstep_worker/kernels_sm120/qwen35_ops.py:1226-1438) and the
@@ -29,64 +37,83 @@
 namespace zs {
 namespace gemm {
 
-constexpr int BM = 128;          // weight rows per tile (MMA M)
-constexpr int BK = 128;          // K elements (bytes) per stage = one 128B swizzle span
-constexpr int BN = 128;          // max tokens per work item (MMA N <= BN)
-constexpr int STAGES = 6;
-constexpr int A_BYTES = BM * BK;             // 16 KiB
-constexpr int B_BYTES = BN * BK;             // 16 KiB
+constexpr int BM = 128;   // weight rows per tile (MMA M)
+constexpr int BK = 128;   // K elements (bytes) per stage = one 128B swizzle span
+constexpr int A_BYTES = BM * BK;
 constexpr int SF_BYTES = 512;
 constexpr int NUM_THREADS = 192;
-constexpr int TMEM_COLS = 512;
-constexpr int ACC_COL0 = 0;                  // acc buffer b at column b*BN
-constexpr int SFA_COL = 2 * BN;              // 4 columns
-constexpr int SFB_COL = 2 * BN + 4;          // 4 columns
+constexpr int kMaxGroups = 520;  // grouped mode: per-group tables are staged in smem
 
-struct SmemLayout {
-  uint8_t a[STAGES][A_BYTES];
-  uint8_t b[STAGES][B_BYTES];
-  uint8_t sfa[STAGES][SF_BYTES];
-  uint8_t sfb[STAGES][SF_BYTES];
-  float xch[16][64];  // epilogue exchange (gate/up pairing)
-  unsigned long long red[4][16];  // epilogue exchange (argmax)
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
-  uint64_t acc_full[2];
-  uint64_t acc_empty[2];
-  uint64_t drain;
-  uint32_t tmem_base;
-  int abort_flag;
+template <int BN, int STAGES>
+struct Cfg {
+  static constexpr int B_BYTES = BN * BK;
+  static constexpr int ACC_COLS = BN;              // fp32 accumulator columns per buffer
+  static constexpr int SFA_COL = 2 * BN;           // 4 columns
+  static constexpr int SFB_COL = 2 * BN + 4;       // 4 columns
+  static constexpr int TMEM_COLS = (2 * BN + 8) <= 128 ? 128 : ((2 * BN + 8) <= 256 ? 256 : 512);
+  struct Smem {
+    uint8_t a[STAGES][A_BYTES];
+    uint8_t b[STAGES][B_BYTES];
+    uint8_t sfa[STAGES][SF_BYTES];
+    uint8_t sfb[STAGES][SF_BYTES];
+    float xch[16][64];              // epilogue exchange (gate/up pairing)
+    unsigned long long red[4][16];  // epilogue exchange (argmax)
+    int g_prefix[kMaxGroups + 1];   // grouped mode: chunk prefix, offsets, counts
+    int g_offset[kMaxGroups];
+    int g_count[kMaxGroups];
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t acc_full[2];
+    uint64_t acc_empty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort_flag;
+  };
 };
 
 struct Item {
-  int g, m, c, count, seg_off;
+  int g, m, c, count, seg_off, kt0, kt1, ks;
 };
 
-__device__ __forceinline__ bool get_item(const GemmMxf8Args& p, int idx, Item& it) {
+// Work item `idx`.  Grouped mode reads the per-group tables staged in shared memory
+// (pre/off/cnt), so the per-item lookup is a short binary search without global loads.
+template <int BN>
+__device__ __forceinline__ bool get_item(const GemmMxf8Args& p, int idx, Item& it, const int* pre,
+                                         const int* off, const int* cnt) {
   const int m_tiles = p.n_pad / BM;
+  const int k_tiles = p.k / BK;
   if (p.chunk_prefix == nullptr) {
     const int chunks = (p.m_rows + BN - 1) / BN;
-    if (idx >= chunks * m_tiles) return false;
+    const int splits = p.k_splits > 1 ? p.k_splits : 1;
+    if (idx >= chunks * m_tiles * splits) return false;
+    it.ks = idx % splits;
+    const int rest = idx / splits;
     it.g = 0;
-    it.m = idx % m_tiles;
-    it.c = idx / m_tiles;
+    it.m = rest % m_tiles;
+    it.c = rest / m_tiles;
     it.seg_off = 0;
     it.count = min(BN, p.m_rows - it.c * BN);
+    const int kps = (k_tiles + splits - 1) / splits;
+    it.kt0 = it.ks * kps;
+    it.kt1 = min(k_tiles, it.kt0 + kps);
     return true;
   }
-  const int total_chunks = __ldg(p.chunk_prefix + p.groups);
+  const int total_chunks = pre[p.groups];
   if (idx >= total_chunks * m_tiles) return false;
   const int chunk = idx / m_tiles;
   it.m = idx % m_tiles;
   int lo = 0, hi = p.groups;  // largest g with prefix[g] <= chunk
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (__ldg(p.chunk_prefix + mid) <= chunk) lo = mid; else hi = mid;
+    if (pre[mid] <= chunk) lo = mid; else hi = mid;
   }
   it.g = lo;
-  it.c = chunk - __ldg(p.chunk_prefix + lo);
-  it.seg_off = __ldg(p.group_offset + lo);
-  it.count = min(BN, __ldg(p.group_count + lo) - it.c * BN);
+  it.c = chunk - pre[lo];
+  it.seg_off = off[lo];
+  it.count = min(BN, cnt[lo] - it.c * BN);
+  it.kt0 = 0;
+  it.kt1 = k_tiles;
+  it.ks = 0;
   return true;
 }
 
@@ -102,17 +129,14 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t phase, int
   return false;
 }
 
-__device__ __forceinline__ uint32_t bf16x2_pack(float a, float b) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
+template <int BN, int STAGES>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
                  const __grid_constant__ CUtensorMap tmap_b, const GemmMxf8Args p) {
+  using C = Cfg<BN, STAGES>;
+  using Smem = typename C::Smem;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  SmemLayout& s = *reinterpret_cast<SmemLayout*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = warp_id();
   const int lane = lane_id();
   volatile int* abort_flag = &s.abort_flag;
@@ -130,8 +154,15 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
     s.abort_flag = 0;
     fence_barrier_init();
   }
+  if (p.chunk_prefix != nullptr) {
+    for (int g = threadIdx.x; g <= p.groups; g += NUM_THREADS) s.g_prefix[g] = __ldg(p.chunk_prefix + g);
+    for (int g = threadIdx.x; g < p.groups; g += NUM_THREADS) {
+      s.g_offset[g] = __ldg(p.group_offset + g);
+      s.g_count[g] = __ldg(p.group_count + g);
+    }
+  }
   if (warp == 0) {
-    tmem_alloc(&s.tmem_base, TMEM_COLS);
+    tmem_alloc(&s.tmem_base, C::TMEM_COLS);
     tmem_relinquish();
   }
   if (warp == 4 && lane == 0) {
@@ -147,17 +178,16 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
   if (warp == 4) {
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
-      uint32_t issued = 0;  // total stage fills issued
+      uint32_t issued = 0;
       Item it;
-      for (int idx = blockIdx.x; get_item(p, idx, it) && !*abort_flag; idx += gridDim.x) {
+      for (int idx = blockIdx.x; get_item<BN>(p, idx, it, s.g_prefix, s.g_offset, s.g_count) && !*abort_flag; idx += gridDim.x) {
         const int n16 = (it.count + 15) >> 4;
         const int a_row = it.g * p.n_pad + it.m * BM;
         const int b_row = it.seg_off + it.c * BN;
-        const uint8_t* sfa_src =
-            p.sfa + ((size_t)(it.g * (p.n_pad / BM) + it.m) * k_tiles) * SF_BYTES;
+        const uint8_t* sfa_src = p.sfa + ((size_t)(it.g * (p.n_pad / BM) + it.m) * k_tiles) * SF_BYTES;
         const uint8_t* sfb_src = p.sfb + ((size_t)(b_row / BM) * k_tiles) * SF_BYTES;
         const uint32_t bytes = A_BYTES + n16 * 16 * BK + 2 * SF_BYTES;
-        for (int kt = 0; kt < k_tiles; ++kt) {
+        for (int kt = it.kt0; kt < it.kt1; ++kt) {
           const int st = issued % STAGES;
           const uint32_t ph = ((issued / STAGES) & 1) ^ 1;
           if (!wait_or_abort(&s.empty[st], ph, p.err, abort_flag)) break;
@@ -182,30 +212,42 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      uint32_t consumed = 0;
-      uint32_t acc_uses[2] = {0, 0};
-      int local = 0;
-      Item it;
-      for (int idx = blockIdx.x; get_item(p, idx, it) && !*abort_flag; idx += gridDim.x, ++local) {
-        const int buf = local & 1;
-        if (!wait_or_abort(&s.acc_empty[buf], (acc_uses[buf] & 1) ^ 1, p.err, abort_flag)) break;
-        ++acc_uses[buf];
+    // The whole warp walks the loop (lane 0 issues the tcgen05 ops); for 32-token
+    // chunks that start 32*j0 rows into a scale atom, the warp first moves each
+    // line's 4 scale bytes of rows 32*j0.. to the line's first word, so the staged
+    // scales always start at an aligned TMEM column.
+    uint32_t consumed = 0;
+    uint32_t acc_uses[2] = {0, 0};
+    int local = 0;
+    Item it;
+    for (int idx = blockIdx.x; get_item<BN>(p, idx, it, s.g_prefix, s.g_offset, s.g_count) && !*abort_flag; idx += gridDim.x, ++local) {
+      const int buf = local & 1;
+      // Every lane waits itself, so each observes the barrier (acquire) before touching
+      // the staged data.
+      bool ok = wait_or_abort(&s.acc_empty[buf], (acc_uses[buf] & 1) ^ 1, p.err, abort_flag);
+      if (!__all_sync(0xffffffff, ok)) break;
+      ++acc_uses[buf];
+      tc_fence_after();
+      const uint32_t n_mma = ((it.count + 15) >> 4) << 4;
+      const uint32_t d_tmem = tmem + buf * C::ACC_COLS;
+      const int j0 = ((it.seg_off + it.c * BN) & 127) >> 5;  // nonzero only when BN < 128
+      for (int kt = it.kt0; kt < it.kt1; ++kt) {
+        const int st = consumed % STAGES;
+        ok = wait_or_abort(&s.full[st], (consumed / STAGES) & 1, p.err, abort_flag);
+        if (!__all_sync(0xffffffff, ok)) {
+          ok = false;
+          break;
+        }
+        if (BN < 128 && j0 != 0) {
+          uint32_t* line = reinterpret_cast<uint32_t*>(s.sfb[st] + lane * 16);
+          line[0] = line[j0];
+          fence_proxy_async_shared();
+          __syncwarp();
+        }
         tc_fence_after();
-        const uint32_t n_mma = ((it.count + 15) >> 4) << 4;
-        const uint32_t d_tmem = tmem + ACC_COL0 + buf * BN;
-        bool ok = true;
-        for (int kt = 0; kt < k_tiles; ++kt) {
-          const int st = consumed % STAGES;
-          if (!wait_or_abort(&s.full[st], (consumed / STAGES) & 1, p.err, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t sfa_desc = make_smem_desc(smem_u32(s.sfa[st]), 0, 128, 0);
-          const uint64_t sfb_desc = make_smem_desc(smem_u32(s.sfb[st]), 0, 128, 0);
-          tmem_cp_32x128b_warpx4(tmem + SFA_COL, sfa_desc);
-          tmem_cp_32x128b_warpx4(tmem + SFB_COL, sfb_desc);
+        if (lane == 0) {
+          tmem_cp_32x128b_warpx4(tmem + C::SFA_COL, make_smem_desc(smem_u32(s.sfa[st]), 0, 128, 0));
+          tmem_cp_32x128b_warpx4(tmem + C::SFB_COL, make_smem_desc(smem_u32(s.sfb[st]), 0, 128, 0));
           const uint32_t a_base = smem_u32(s.a[st]);
           const uint32_t b_base = smem_u32(s.b[st]);
 #pragma unroll
@@ -213,19 +255,24 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const uint64_t adesc = make_smem_desc(a_base + kb * 32, 16, 1024, 2);
             const uint64_t bdesc = make_smem_desc(b_base + kb * 32, 16, 1024, 2);
             const uint32_t idesc = make_idesc_mxf8(BM, n_mma, kb, kb);
-            mma_mxf8(d_tmem, adesc, bdesc, idesc, (tmem + SFA_COL) | (uint32_t(kb) << 30),
-                     (tmem + SFB_COL) | (uint32_t(kb) << 30), (kt > 0 || kb > 0) ? 1u : 0u);
+            mma_mxf8(d_tmem, adesc, bdesc, idesc, (tmem + C::SFA_COL) | (uint32_t(kb) << 30),
+                     (tmem + C::SFB_COL) | (uint32_t(kb) << 30), (kt > it.kt0 || kb > 0) ? 1u : 0u);
           }
           tc_commit(&s.empty[st]);
-          ++consumed;
         }
-        if (!ok) break;
-        tc_commit(&s.acc_full[buf]);
+        __syncwarp();
+        ++consumed;
       }
-      // Make sure no MMA is still running before TMEM is released.
+      if (!ok) break;
+      if (lane == 0) tc_commit(&s.acc_full[buf]);
+      __syncwarp();
+    }
+    // Make sure no MMA is still running before TMEM is released.
+    if (lane == 0) {
       tc_commit(&s.drain);
       if (!mbar_wait(&s.drain, 0, nullptr)) report_error(p.err, kErrDrainTimeout);
     }
+    __syncwarp();
   } else {
     // ------------------------------------------------------------------ epilogue
     const int q = warp;  // TMEM subpartition (lanes 32q .. 32q+31)
@@ -233,12 +280,12 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
     uint32_t acc_uses[2] = {0, 0};
     int local = 0;
     Item it;
-    for (int idx = blockIdx.x; get_item(p, idx, it); idx += gridDim.x, ++local) {
+    for (int idx = blockIdx.x; get_item<BN>(p, idx, it, s.g_prefix, s.g_offset, s.g_count); idx += gridDim.x, ++local) {
       const int buf = local & 1;
       if (!wait_or_abort(&s.acc_full[buf], acc_uses[buf] & 1, p.err, abort_flag)) break;
       ++acc_uses[buf];
       tc_fence_after();
-      const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16) + ACC_COL0 + buf * BN;
+      const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16) + buf * C::ACC_COLS;
       const int n16 = (it.count + 15) >> 4;
       const int seg_row0 = it.seg_off + it.c * BN;
       const int n_glob = it.m * BM + row_in_tile;
@@ -312,27 +359,33 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
         }
       } else {
         const bool valid_n = n_glob < p.n_valid;
+        float* outf = reinterpret_cast<float*>(p.out) + (size_t)it.ks * p.split_stride;
         for (int ch = 0; ch < n16; ++ch) {
           uint32_t r[16];
           tmem_ld_32x32b_x16(t_base + ch * 16, r);
+          // Scatter mode: lanes 0..15 fetch the chunk's destination rows and weights in
+          // parallel (instead of one dependent load per column).
+          int dst_l = 0;
+          float scl_l = 0.f;
+          if (p.epi_mode == kEpiScatterScaled && lane < 16 && ch * 16 + lane < it.count) {
+            dst_l = __ldg(p.row_dst + seg_row0 + ch * 16 + lane);
+            scl_l = __ldg(p.row_scale + seg_row0 + ch * 16 + lane);
+          }
           tmem_ld_wait();
-          if (!valid_n) continue;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int col = ch * 16 + j;
-            if (col >= it.count) break;
+            const int dst = __shfl_sync(0xffffffff, dst_l, j);
+            const float scl = __shfl_sync(0xffffffff, scl_l, j);
+            if (col >= it.count || !valid_n) continue;
             const int row = seg_row0 + col;
             float v = __uint_as_float(r[j]);
             if (p.epi_mode == kEpiStoreF32) {
-              reinterpret_cast<float*>(p.out)[(size_t)row * p.ldo + n_glob] = v;
+              outf[(size_t)row * p.ldo + n_glob] = v;
             } else if (p.epi_mode == kEpiScatterScaled) {
-              const int dst = __ldg(p.row_dst + row);
-              v *= __ldg(p.row_scale + row);
-              reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)dst * p.ldo + n_glob] =
-                  __float2bfloat16_rn(v);
+              reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)dst * p.ldo + n_glob] = __float2bfloat16_rn(v * scl);
             } else {
-              reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)row * p.ldo + n_glob] =
-                  __float2bfloat16_rn(v);
+              reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)row * p.ldo + n_glob] = __float2bfloat16_rn(v);
             }
           }
         }
@@ -346,7 +399,7 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
+  if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
 }  // namespace gemm
@@ -367,8 +420,7 @@ EncodeTiledFn get_encode_fn() {
   if (fn == nullptr) {
     void* ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
       fn = reinterpret_cast<EncodeTiledFn>(ptr);
   }
@@ -383,13 +435,40 @@ int make_tmap_u8(CUtensorMap* m, const void* base, int64_t rows, int64_t k, int 
   cuuint64_t strides[1] = {(cuuint64_t)k};
   cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
-                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
-int g_num_sms = 0;
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, int STAGES>
+int launch(const GemmMxf8Args& p, const CUtensorMap& ta, const CUtensorMap& tb, cudaStream_t stream) {
+  using namespace zs::gemm;
+  int grid = num_sms();
+  if (p.chunk_prefix == nullptr) {
+    const int splits = p.k_splits > 1 ? p.k_splits : 1;
+    const int items = ((p.m_rows + BN - 1) / BN) * (p.n_pad / BM) * splits;
+    if (items == 0) return 0;
+    grid = items < grid ? items : grid;
+  } else if (p.max_items > 0 && p.max_items < grid) {
+    grid = p.max_items;
+  }
+  const size_t smem = sizeof(typename Cfg<BN, STAGES>::Smem) + 1024;
+  auto kern = gemm_mxf8_kernel<BN, STAGES>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  kern<<<grid, NUM_THREADS, smem, stream>>>(ta, tb, p);
+  return cudaGetLastError() == cudaSuccess ? 0 : -15;
+}
 
 }  // namespace
 
@@ -401,24 +480,12 @@ extern "C" int zs_gemm_mxf8(const GemmMxf8Args* args, cudaStream_t stream) {
       (reinterpret_cast<uintptr_t>(p.sfa) & 15) || (reinterpret_cast<uintptr_t>(p.sfb) & 15))
     return -11;
   if (p.b_rows % BM != 0) return -12;
+  if (p.k_splits > 1 && (p.chunk_prefix != nullptr || p.epi_mode != kEpiStoreF32)) return -16;
+  const int bn = p.block_n == 32 ? 32 : 128;
+  if (p.chunk_prefix != nullptr && p.chunk_rows != bn) return -17;
+  if (p.chunk_prefix != nullptr && p.groups > kMaxGroups) return -18;
   CUtensorMap ta, tb;
   if (make_tmap_u8(&ta, p.a, (int64_t)p.groups * p.n_pad, p.k, BM) != 0) return -13;
   if (make_tmap_u8(&tb, p.b, p.b_rows, p.k, 16) != 0) return -14;
-  if (g_num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-  }
-  int grid = g_num_sms;
-  if (p.chunk_prefix == nullptr) {
-    const int items = ((p.m_rows + BN - 1) / BN) * (p.n_pad / BM);
-    if (items == 0) return 0;
-    grid = items < grid ? items : grid;
-  } else if (p.max_items > 0 && p.max_items < grid) {
-    grid = p.max_items;
-  }
-  const size_t smem = sizeof(SmemLayout) + 1024;
-  cudaFuncSetAttribute(gemm_mxf8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  gemm_mxf8_kernel<<<grid, NUM_THREADS, smem, stream>>>(ta, tb, p);
-  return cudaGetLastError() == cudaSuccess ? 0 : -15;
+  return bn == 32 ? launch<32, 9>(p, ta, tb, stream) : launch<128, 6>(p, ta, tb, stream);
 }

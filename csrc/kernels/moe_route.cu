@@ -38,20 +38,27 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
   }
 }
 
+// Router logit (row, col), summing the router GEMM's split-K partials in order.
+__device__ __forceinline__ float logit(const MoeRouteArgs& a, int row, int col) {
+  const float* lg = a.logits + (size_t)row * a.ld_logits + col;
+  float v = lg[0];
+  for (int s = 1; s < a.logit_splits; ++s) v += lg[s * a.logit_split_stride];
+  return v;
+}
+
 __global__ void route_topk_kernel(const MoeRouteArgs a) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= a.rows) return;
   const int E = a.num_experts;
   const int per = (E + 31) / 32;  // experts per lane: e = lane + 32*j
-  const float* lg = a.logits + (size_t)row * a.ld_logits;
   float score[kMaxExperts / 32];   // routing weight source
   float choice[kMaxExperts / 32];  // selection key
   if (a.scoring == 0) {
     float mx = -INFINITY;
     for (int j = 0; j < per; ++j) {
       const int e = lane + 32 * j;
-      score[j] = e < E ? lg[e] : -INFINITY;
+      score[j] = e < E ? logit(a, row, e) : -INFINITY;
       mx = fmaxf(mx, score[j]);
     }
     mx = warp_max(mx);
@@ -68,7 +75,7 @@ __global__ void route_topk_kernel(const MoeRouteArgs a) {
   } else {
     for (int j = 0; j < per; ++j) {
       const int e = lane + 32 * j;
-      score[j] = e < E ? sigmoidf_(lg[e]) : 0.f;
+      score[j] = e < E ? sigmoidf_(logit(a, row, e)) : 0.f;
       choice[j] = e < E ? score[j] + (a.bias ? a.bias[e] : 0.f) : -INFINITY;
     }
     if (a.n_group > 1) {
@@ -156,31 +163,50 @@ __global__ void route_topk_kernel(const MoeRouteArgs a) {
 }
 
 __global__ void offsets_kernel(const MoeRouteArgs a, int groups) {
-  // Single CTA of 1024 threads; groups <= kMaxExperts + 1.
-  __shared__ int seg[kMaxExperts + 2];
-  __shared__ int chk[kMaxExperts + 2];
-  const int t = threadIdx.x;
-  for (int g = t; g < groups; g += blockDim.x) {
-    const int c = a.group_count[g];
-    seg[g] = (c + 127) & ~127;
-    chk[g] = (c + 127) >> 7;
+  // Single CTA of 1024 threads (one group each, groups <= 1024): exclusive scans of the
+  // 128-aligned segment sizes and of the per-group chunk counts, warp scans + one
+  // warp over the 32 warp totals.
+  __shared__ int wsum_s[32], wsum_c[32];
+  __shared__ int overflow;
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int cr = a.chunk_rows;
+  const int cnt = t < groups ? a.group_count[t] : 0;
+  int s = (cnt + 127) & ~127;
+  int c = (cnt + cr - 1) / cr;
+  int is = s, ic = c;  // inclusive warp scans
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int ns = __shfl_up_sync(0xffffffff, is, o);
+    const int nc = __shfl_up_sync(0xffffffff, ic, o);
+    if (lane >= o) { is += ns; ic += nc; }
+  }
+  if (lane == 31) { wsum_s[w] = is; wsum_c[w] = ic; }
+  __syncthreads();
+  if (w == 0) {
+    int vs = wsum_s[lane], vc = wsum_c[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int ns = __shfl_up_sync(0xffffffff, vs, o);
+      const int nc = __shfl_up_sync(0xffffffff, vc, o);
+      if (lane >= o) { vs += ns; vc += nc; }
+    }
+    wsum_s[lane] = vs;  // inclusive totals per warp
+    wsum_c[lane] = vc;
   }
   __syncthreads();
+  const int base_s = w > 0 ? wsum_s[w - 1] : 0, base_c = w > 0 ? wsum_c[w - 1] : 0;
+  const int ex_s = base_s + is - s, ex_c = base_c + ic - c;
+  const int total_s = wsum_s[31], total_c = wsum_c[31];
+  if (t == 0) overflow = total_s > a.max_grouped_rows;
+  __syncthreads();
+  if (t < groups) {
+    a.group_offset[t] = ex_s;
+    // On overflow the GEMMs see no work rather than run past the buffer.
+    a.chunk_prefix[t] = overflow ? 0 : ex_c;
+  }
   if (t == 0) {
-    int so = 0, co = 0;
-    for (int g = 0; g < groups; ++g) {
-      const int s = seg[g], c = chk[g];
-      a.group_offset[g] = so;
-      a.chunk_prefix[g] = co;
-      so += s;
-      co += c;
-    }
-    a.chunk_prefix[groups] = co;
-    if (so > a.max_grouped_rows) {
-      report_error(a.err, kErrBadShape);
-      // Make the GEMMs do nothing rather than run past the buffer.
-      for (int g = 0; g <= groups; ++g) a.chunk_prefix[g] = 0;
-    }
+    a.chunk_prefix[groups] = overflow ? 0 : total_c;
+    if (overflow) report_error(a.err, kErrBadShape);
   }
 }
 
@@ -200,7 +226,7 @@ __global__ void scatter_kernel(const MoeRouteArgs a) {
     w = a.topk_w[row * a.top_k + j];
   } else {
     g = a.expert_end - a.expert_begin;
-    w = a.shared_gate_col >= 0 ? sigmoidf_(a.logits[(size_t)row * a.ld_logits + a.shared_gate_col]) : 1.f;
+    w = a.shared_gate_col >= 0 ? sigmoidf_(logit(a, row, a.shared_gate_col)) : 1.f;
   }
   const int dst = a.group_offset[g] + slot;
   if (dst >= a.max_grouped_rows) return;  // overflow (reported by offsets_kernel)
@@ -227,7 +253,9 @@ extern "C" int zs_moe_route(const MoeRouteArgs* args, cudaStream_t stream) {
   if (a.num_experts > zs::moe::kMaxExperts || a.top_k > zs::moe::kMaxTopK || a.top_k <= 0) return -1;
   if (a.n_group > 64 || (a.n_group > 1 && a.num_experts % a.n_group != 0)) return -1;
   if (a.hidden % 128 != 0) return -1;
+  if (a.chunk_rows != 32 && a.chunk_rows != 128) return -1;
   const int groups = (a.expert_end - a.expert_begin) + (a.has_shared ? 1 : 0);
+  if (groups > 1024) return -1;
   if (cudaMemsetAsync(a.group_count, 0, sizeof(int) * groups, stream) != cudaSuccess) return -2;
   if (a.rows == 0) {
     zs::moe::offsets_kernel<<<1, 1024, 0, stream>>>(a, groups);

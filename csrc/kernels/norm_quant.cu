@@ -59,8 +59,8 @@ constexpr int kNormMaxIter = 4;
 
 template <bool kEmbed>
 __global__ void __launch_bounds__(kNormThreads)
-add_rmsnorm_quant_kernel(__nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ delta,
-                         int n_terms, long long d_row_stride, long long d_term_stride,
+add_rmsnorm_quant_kernel(__nv_bfloat16* __restrict__ residual, const void* __restrict__ delta,
+                         int n_terms, long long d_row_stride, long long d_term_stride, int delta_f32,
                          const int* __restrict__ ids, const __nv_bfloat16* __restrict__ embed,
                          const __nv_bfloat16* __restrict__ weight, float w_offset, float eps,
                          int hidden, __nv_bfloat16* __restrict__ normed, uint8_t* __restrict__ q,
@@ -89,14 +89,25 @@ add_rmsnorm_quant_kernel(__nv_bfloat16* __restrict__ residual, const __nv_bfloat
       x[it][2 * j + 1] = f.y;
     }
     if (!kEmbed && delta != nullptr) {
-      for (int t = 0; t < n_terms; ++t) {
-        uint4 d = *reinterpret_cast<const uint4*>(delta + row * d_row_stride + t * d_term_stride + col);
-        const __nv_bfloat162* dh = reinterpret_cast<const __nv_bfloat162*>(&d);
+      if (delta_f32) {
+        const float* df = static_cast<const float*>(delta);
+        for (int t = 0; t < n_terms; ++t) {
+          const float4* p4 = reinterpret_cast<const float4*>(df + row * d_row_stride + t * d_term_stride + col);
+          const float4 a0 = p4[0], a1 = p4[1];
+          x[it][0] += a0.x; x[it][1] += a0.y; x[it][2] += a0.z; x[it][3] += a0.w;
+          x[it][4] += a1.x; x[it][5] += a1.y; x[it][6] += a1.z; x[it][7] += a1.w;
+        }
+      } else {
+        const __nv_bfloat16* db = static_cast<const __nv_bfloat16*>(delta);
+        for (int t = 0; t < n_terms; ++t) {
+          uint4 d = *reinterpret_cast<const uint4*>(db + row * d_row_stride + t * d_term_stride + col);
+          const __nv_bfloat162* dh = reinterpret_cast<const __nv_bfloat162*>(&d);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float2 f = __bfloat1622float2(dh[j]);
-          x[it][2 * j] += f.x;
-          x[it][2 * j + 1] += f.y;
+          for (int j = 0; j < 4; ++j) {
+            float2 f = __bfloat1622float2(dh[j]);
+            x[it][2 * j] += f.x;
+            x[it][2 * j + 1] += f.y;
+          }
         }
       }
     }
@@ -211,7 +222,7 @@ extern "C" int zs_quant_mxf8(const void* x, int rows, int k, int ld_x, uint8_t* 
 }
 
 extern "C" int zs_add_rmsnorm_quant(void* residual, const void* delta, int n_terms,
-                                    long long d_row_stride, long long d_term_stride,
+                                    long long d_row_stride, long long d_term_stride, int delta_f32,
                                     const void* weight, float w_offset, float eps, int rows,
                                     int hidden, void* normed, uint8_t* q, uint8_t* sf,
                                     cudaStream_t stream) {
@@ -219,8 +230,8 @@ extern "C" int zs_add_rmsnorm_quant(void* residual, const void* delta, int n_ter
     return -1;
   if (rows == 0) return 0;
   zs::add_rmsnorm_quant_kernel<false><<<rows, zs::kNormThreads, 0, stream>>>(
-      static_cast<__nv_bfloat16*>(residual), static_cast<const __nv_bfloat16*>(delta), n_terms,
-      d_row_stride, d_term_stride, nullptr, nullptr, static_cast<const __nv_bfloat16*>(weight),
+      static_cast<__nv_bfloat16*>(residual), delta, n_terms, d_row_stride, d_term_stride, delta_f32,
+      nullptr, nullptr, static_cast<const __nv_bfloat16*>(weight),
       w_offset, eps, hidden, static_cast<__nv_bfloat16*>(normed), q, sf);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
@@ -234,7 +245,7 @@ extern "C" int zs_embed_rmsnorm_quant(const int* ids, const void* embed, void* h
     return -1;
   if (rows == 0) return 0;
   zs::add_rmsnorm_quant_kernel<true><<<rows, zs::kNormThreads, 0, stream>>>(
-      static_cast<__nv_bfloat16*>(hidden), nullptr, 0, 0, 0, ids,
+      static_cast<__nv_bfloat16*>(hidden), nullptr, 0, 0, 0, 0, ids,
       static_cast<const __nv_bfloat16*>(embed), static_cast<const __nv_bfloat16*>(weight),
       w_offset, eps, hidden_size, static_cast<__nv_bfloat16*>(normed), q, sf);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;

@@ -38,8 +38,12 @@ typedef struct GemmMxf8Args {
   int m_rows;              // dense mode: number of token rows
   const int* group_count;  // grouped mode: [groups] tokens per group (device)
   const int* group_offset; // grouped mode: [groups] first row of each group's segment
-  const int* chunk_prefix; // grouped mode: [groups+1] prefix of ceil(count/128); NULL = dense
+  const int* chunk_prefix; // grouped mode: [groups+1] prefix of ceil(count/chunk_rows); NULL = dense
+  int chunk_rows;          // grouped mode: rows per chunk the prefix was built for (== block_n)
   int max_items;           // grouped mode: optional cap on CTAs (0 = one per SM)
+  int block_n;             // tokens per work item: 32 (decode) or 128
+  int k_splits;            // dense mode, kEpiStoreF32 only: split K into this many partials
+  long long split_stride;  // elements between split partials in out
   int epi_mode;
   void* out;
   int ldo;                 // leading dimension of out in elements
@@ -60,9 +64,10 @@ int zs_quant_mxf8(const void* x_bf16, int rows, int k, int ld_x, uint8_t* q, uin
 
 // residual[r] = bf16(residual[r] + sum_t delta[r, t]) (if delta != NULL), then
 // y = rmsnorm(residual[r]) * (w + w_offset); y written as bf16 (normed, optional) and/or
-// MXFP8 (q + sf, optional).  Reduction in fp32, hidden % 256 == 0.
+// MXFP8 (q + sf, optional).  Reduction in fp32, hidden % 2048 == 0.  Delta terms are
+// bf16, or f32 when delta_f32 != 0 (split-K partials); terms are summed in index order.
 int zs_add_rmsnorm_quant(void* residual, const void* delta, int n_terms, long long delta_row_stride,
-                         long long delta_term_stride, const void* weight, float w_offset,
+                         long long delta_term_stride, int delta_f32, const void* weight, float w_offset,
                          float eps, int rows, int hidden, void* normed, uint8_t* q, uint8_t* sf,
                          cudaStream_t stream);
 
@@ -158,6 +163,9 @@ int zs_attn_prefill(const AttnArgs* args, cudaStream_t stream);
 typedef struct MoeRouteArgs {
   const float* logits;     // f32 [rows, ld_logits]: router logits (num_experts) then shared-gate logit
   int ld_logits;
+  int logit_splits;        // split-K partials of the router GEMM (summed in order); <= 1: one
+  long long logit_split_stride;
+  int chunk_rows;          // chunk size of the consuming grouped GEMM (32 or 128)
   int rows;
   int num_experts;         // routed experts (global)
   int top_k;

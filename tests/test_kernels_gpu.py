@@ -21,6 +21,14 @@ def C():
     return _ext.load()
 
 
+def gemm(C, *args, block_n=128, k_splits=1, split_stride=0):
+    C.gemm_mxf8(*args, block_n, k_splits, split_stride)
+
+
+def route(C, logits, *args, splits=1, split_stride=0, chunk_rows=128):
+    C.moe_route(logits, *args, logits.shape[-1], splits, split_stride, chunk_rows)
+
+
 def _pad_rows(n: int) -> int:
     return (n + 127) // 128 * 128
 
@@ -53,7 +61,7 @@ def test_gemm_dense_f32(C, m, n, k):
     xq, xsf, xd = _quant_act(x, _pad_rows(m))
     out = torch.zeros(m, n, device="cuda", dtype=torch.float32)
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    C.gemm_mxf8(wq, wsf, xq, xsf, k, npad, n, 1, m, None, None, None, EPI_F32, out, n,
+    gemm(C,wq, wsf, xq, xsf, k, npad, n, 1, m, None, None, None, EPI_F32, out, n,
                 None, None, None, err, 0)
     torch.cuda.synchronize()
     assert err.item() == 0
@@ -69,7 +77,7 @@ def test_gemm_dense_bf16(C):
     wq, wsf, wd, npad = _quant_weights(w)
     xq, xsf, xd = _quant_act(x, _pad_rows(m))
     out = torch.zeros(m, n, device="cuda", dtype=torch.bfloat16)
-    C.gemm_mxf8(wq, wsf, xq, xsf, k, npad, n, 1, m, None, None, None, EPI_BF16, out, n,
+    gemm(C,wq, wsf, xq, xsf, k, npad, n, 1, m, None, None, None, EPI_BF16, out, n,
                 None, None, None, None, 0)
     torch.cuda.synchronize()
     expect = (xd @ wd[0, :n].T).to(torch.bfloat16)
@@ -101,7 +109,7 @@ def test_gemm_grouped_f32(C):
     s = _grouped_setup(counts, k, n)
     out = torch.full((s["rows"], n), float("nan"), device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    C.gemm_mxf8(s["wq"], s["wsf"], s["xq"], s["xsf"], k, s["npad"], n, len(counts), 0,
+    gemm(C,s["wq"], s["wsf"], s["xq"], s["xsf"], k, s["npad"], n, len(counts), 0,
                 s["cnt"], s["off"], s["pre"], EPI_F32, out, n, None, None, None, err, 0)
     torch.cuda.synchronize()
     assert err.item() == 0
@@ -112,6 +120,47 @@ def test_gemm_grouped_f32(C):
         o = s["offsets"][gi]
         expect = s["xd"][o:o + cnt] @ s["wd"][gi, :n].T
         torch.testing.assert_close(out[o:o + cnt], expect, rtol=1e-4, atol=1e-3)
+
+
+def test_gemm_grouped_bn32(C):
+    """32-token chunks: chunks start 0/32/64/96 rows into a scale atom."""
+    counts = [0, 3, 33, 64, 100, 17, 130]
+    k, n = 384, 256
+    s = _grouped_setup(counts, k, n, seed=4)
+    pre, c = [0], 0
+    for cnt in counts:
+        c += (cnt + 31) // 32
+        pre.append(c)
+    out = torch.full((s["rows"], n), float("nan"), device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    gemm(C, s["wq"], s["wsf"], s["xq"], s["xsf"], k, s["npad"], n, len(counts), 0, s["cnt"], s["off"],
+         torch.tensor(pre, dtype=torch.int32, device="cuda"), EPI_F32, out, n, None, None, None, err, 0,
+         block_n=32)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    out = out.cpu()
+    for gi, cnt in enumerate(counts):
+        if cnt == 0:
+            continue
+        o = s["offsets"][gi]
+        expect = s["xd"][o:o + cnt] @ s["wd"][gi, :n].T
+        torch.testing.assert_close(out[o:o + cnt], expect, rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("m,splits,bn", [(256, 4, 128), (20, 8, 32), (130, 3, 32)])
+def test_gemm_split_k(C, m, splits, bn):
+    torch.manual_seed(9)
+    n, k = 384, 2048
+    w = torch.randn(1, n, k) * 0.05
+    x = torch.randn(m, k)
+    wq, wsf, wd, npad = _quant_weights(w)
+    xq, xsf, xd = _quant_act(x, _pad_rows(m))
+    out = torch.zeros(splits, m, n, device="cuda")
+    gemm(C, wq, wsf, xq, xsf, k, npad, n, 1, m, None, None, None, EPI_F32, out, n, None, None, None, None, 0,
+         block_n=bn, k_splits=splits, split_stride=m * n)
+    torch.cuda.synchronize()
+    expect = xd @ wd[0, :n].T
+    torch.testing.assert_close(out.sum(0).cpu(), expect, rtol=1e-4, atol=1e-3)
 
 
 def test_gemm_silu_quant(C):
@@ -128,7 +177,7 @@ def test_gemm_silu_quant(C):
     wq, wsf, wd, npad = _quant_weights(packed)
     act = torch.zeros(s["rows"], inter, dtype=torch.uint8, device="cuda")
     act_sf = torch.zeros(mx.atoms_bytes(s["rows"], inter), dtype=torch.uint8, device="cuda")
-    C.gemm_mxf8(wq, wsf, s["xq"], s["xsf"], k, npad, 2 * inter, g, 0, s["cnt"], s["off"], s["pre"],
+    gemm(C,wq, wsf, s["xq"], s["xsf"], k, npad, 2 * inter, g, 0, s["cnt"], s["off"], s["pre"],
                 EPI_SILU, act, inter, act_sf, None, None, None, 0)
     torch.cuda.synchronize()
     codes = mx.codes_from_atoms(act_sf.cpu(), s["rows"], inter)
@@ -161,7 +210,7 @@ def test_gemm_scatter_scaled(C):
             row_scale[s["offsets"][gi] + r] = 0.5 + i
             i += 1
     out = torch.zeros(12, n, dtype=torch.bfloat16, device="cuda")
-    C.gemm_mxf8(s["wq"], s["wsf"], s["xq"], s["xsf"], k, s["npad"], n, 2, 0, s["cnt"], s["off"],
+    gemm(C,s["wq"], s["wsf"], s["xq"], s["xsf"], k, s["npad"], n, 2, 0, s["cnt"], s["off"],
                 s["pre"], EPI_SCATTER, out, n, None, row_dst.cuda(), row_scale.cuda(), None, 0)
     torch.cuda.synchronize()
     out = out.cpu().float()
@@ -183,7 +232,7 @@ def test_gemm_argmax_ties(C):
     xq, xsf, xd = _quant_act(x, _pad_rows(m))
     tiles = npad // 128
     keys = torch.zeros(m, tiles, dtype=torch.int64, device="cuda")
-    C.gemm_mxf8(wq, wsf, xq, xsf, k, npad, vocab, 1, m, None, None, None, EPI_ARGMAX, keys, tiles,
+    gemm(C,wq, wsf, xq, xsf, k, npad, vocab, 1, m, None, None, None, EPI_ARGMAX, keys, tiles,
                 None, None, None, None, 0)
     ids = torch.zeros(m, dtype=torch.int32, device="cuda")
     vals = torch.zeros(m, dtype=torch.float32, device="cuda")
@@ -368,7 +417,7 @@ def test_moe_route_softmax_shared(C):
     xg = torch.zeros(max_rows, hidden, dtype=torch.uint8, **dev)
     xg_sf = torch.zeros(mx.atoms_bytes(max_rows, hidden), dtype=torch.uint8, **dev)
     err = torch.zeros(1, dtype=torch.int32, **dev)
-    C.moe_route(logits.cuda(), rows, E, k, True, 0, None, 1, 1, 1.0, E, 0, E, True, topk_ids, topk_w,
+    route(C,logits.cuda(), rows, E, k, True, 0, None, 1, 1, 1.0, E, 0, E, True, topk_ids, topk_w,
                 cnt, off, pre, pair_slot, row_dst, row_scale, xq, xsf, xg, xg_sf, err)
     torch.cuda.synchronize()
     assert err.item() == 0
@@ -405,7 +454,7 @@ def test_moe_route_sigmoid_grouped(C):
     max_rows = rows * (k + 1) + 128 * E
     dev = dict(device="cuda")
     out = [torch.zeros(rows, k, dtype=torch.int32, **dev), torch.zeros(rows, k, **dev)]
-    C.moe_route(logits.cuda(), rows, E, k, True, 1, bias.cuda(), ng, tg, 2.5, -1, 0, E, False, out[0], out[1],
+    route(C,logits.cuda(), rows, E, k, True, 1, bias.cuda(), ng, tg, 2.5, -1, 0, E, False, out[0], out[1],
                 torch.zeros(E, dtype=torch.int32, **dev), torch.zeros(E, dtype=torch.int32, **dev),
                 torch.zeros(E + 1, dtype=torch.int32, **dev), torch.zeros(rows, k + 1, dtype=torch.int32, **dev),
                 torch.zeros(max_rows, dtype=torch.int32, **dev), torch.zeros(max_rows, **dev), xq, xsf,

@@ -1,0 +1,257 @@
+"""Kernel and step micro-benchmarks with roofline fractions.
+
+    python -m zstep_b200.microbench breakdown [--layers 40] [--batch 256] [--ctx 1280]
+    python -m zstep_b200.microbench step --eager 1        (one eager decode step; for ncu)
+    python -m zstep_b200.microbench gemm --m 256 --n 12352 --k 2048 [--groups 1]
+    python -m zstep_b200.microbench moe --m 256
+    python -m zstep_b200.microbench gdn --m 256
+    python -m zstep_b200.microbench attn --m 256 --ctx 1280
+
+Times are CUDA-event times on the launching stream after warm-up, with inputs larger
+than L2 (or an L2 flush between iterations for small operands).  Peaks come from
+MEASURED_PEAKS.json at the repository root when present (else 6.65 TB/s and 1.59
+PFLOP/s bf16 dense, doubled for fp8).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+from collections import defaultdict
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+def _flush(n_bytes=256 << 20):
+    buf = _flush.__dict__.setdefault("buf", torch.empty(n_bytes, dtype=torch.uint8, device="cuda"))
+    buf.zero_()
+
+
+def time_fn(fn, iters=20, warmup=3, flush=False) -> float:
+    """Median milliseconds per call."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        if flush:
+            _flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b))
+    return statistics.median(ts)
+
+
+def build_runner(layers: int, batch: int, ctx: int, experts: int = 256, vocab: int = 248320):
+    from .config import Qwen35Config
+    from .models.qwen35 import Qwen35Runner
+
+    types = tuple("full_attention" if (i + 1) % 4 == 0 else "linear_attention" for i in range(layers))
+    cfg = Qwen35Config(num_hidden_layers=layers, layer_types=types, num_experts=experts, vocab_size=vocab)
+    page = 16
+    pages_per_seq = (ctx + 64 + page - 1) // page
+    r = Qwen35Runner(cfg, max_seqs=batch, max_prefill_tokens=batch, num_pages=batch * pages_per_seq + 1,
+                     page_size=page, max_model_len=ctx + 64)
+    for s in range(batch):
+        r.set_pages(s, list(range(1 + s * pages_per_seq, 1 + (s + 1) * pages_per_seq)))
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, cfg.vocab_size, (batch,), generator=g)
+    r.stage(ids, [ctx] * batch, list(range(batch)))
+    return r
+
+
+def cmd_breakdown(a):
+    """Per-op device time of one eager decode step (events around every kernel call)."""
+    r = build_runner(a.layers, a.batch, a.ctx)
+    real = r.C
+    events = []
+
+    class Proxy:
+        def __getattr__(self, name):
+            fn = getattr(real, name)
+
+            def wrapped(*args, **kw):
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                out = fn(*args, **kw)
+                e.record()
+                tag = name
+                if name == "gemm_mxf8":
+                    tag = f"gemm[n={args[5]},k={args[4]},g={args[7]},epi={args[12]}]"
+                events.append((tag, s, e))
+                return out
+            return wrapped
+
+    for _ in range(2):
+        r.decode_forward(a.batch)
+    torch.cuda.synchronize()
+    r.C = Proxy()
+    events.clear()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    r.decode_forward(a.batch)
+    en.record()
+    torch.cuda.synchronize()
+    r.C = real
+    tot = defaultdict(float)
+    cnt = defaultdict(int)
+    for tag, s, e in events:
+        tot[tag] += s.elapsed_time(e)
+        cnt[tag] += 1
+    step = st.elapsed_time(en)
+    rows = sorted(tot.items(), key=lambda kv: -kv[1])
+    print(f"eager decode step: {step:.3f} ms  (batch {a.batch}, ctx {a.ctx}, layers {a.layers})")
+    for tag, ms in rows:
+        print(f"  {ms:8.3f} ms  {100 * ms / step:5.1f}%  x{cnt[tag]:<4d} {tag}")
+
+
+def cmd_step(a):
+    r = build_runner(a.layers, a.batch, a.ctx)
+    if a.eager:
+        for _ in range(a.warmup):
+            r.decode_forward(a.batch)
+        torch.cuda.synchronize()
+        r.decode_forward(a.batch)
+        torch.cuda.synchronize()
+        return
+    r.capture_decode_graph(r.bucket_for(a.batch))
+    g = r.graphs[r.bucket_for(a.batch)]
+    ms = time_fn(g.replay, iters=a.iters)
+    print(json.dumps({"decode_step_ms": ms, "tok_s": a.batch / ms * 1000}))
+
+
+def _gemm_case(m, n, k, groups=1):
+    from .ops import mx
+    from .models.qwen35 import pack_linear, _pad128
+
+    C = __import__("zstep_b200.ops._ext", fromlist=["load"]).load()
+    w = (torch.randn(groups, n, k, device="cuda") * 0.02).to(torch.bfloat16)
+    pw = pack_linear(w, C)
+    rows = _pad128(m) if groups == 1 else _pad128(m) * groups
+    x = torch.randn(rows, k, device="cuda").to(torch.bfloat16)
+    xq = torch.empty(rows, k, dtype=torch.uint8, device="cuda")
+    xsf = torch.empty(mx.atoms_bytes(rows, k), dtype=torch.uint8, device="cuda")
+    C.quant_mxf8(x, xq, xsf)
+    return C, pw, xq, xsf
+
+
+def cmd_gemm(a):
+    C, pw, xq, xsf = _gemm_case(a.m, a.n, a.k, a.groups)
+    out = torch.empty(_pad128_(a.m) * a.groups, a.n, dtype=torch.bfloat16, device="cuda")
+    if a.groups == 1:
+        bn = 32 if a.m <= 32 else 128
+        fn = lambda: C.gemm_mxf8(pw.q, pw.sf, xq, xsf, a.k, pw.n_pad, a.n, 1, a.m, None, None, None, 0, out, a.n,  # noqa
+                                 None, None, None, None, 0, bn, 1, 0)
+    else:
+        cnt = torch.full((a.groups,), a.m, dtype=torch.int32, device="cuda")
+        off = torch.arange(a.groups, dtype=torch.int32, device="cuda") * _pad128_(a.m)
+        bn = 32 if a.m <= 32 else 128
+        pre = torch.arange(a.groups + 1, dtype=torch.int32, device="cuda") * ((a.m + bn - 1) // bn)
+        fn = lambda: C.gemm_mxf8(pw.q, pw.sf, xq, xsf, a.k, pw.n_pad, a.n, a.groups, 0, cnt, off, pre, 0, out,  # noqa
+                                 a.n, None, None, None, None, 0, bn, 1, 0)
+    ms = time_fn(fn, flush=True)
+    pk = peaks()
+    flops = 2.0 * a.m * a.n * a.k * a.groups
+    bytes_ = a.n * a.k * a.groups * (1 + 1 / 32) + a.m * a.k * a.groups + a.m * a.n * 2 * a.groups
+    res = {"op": "gemm_mxf8", "m": a.m, "n": a.n, "k": a.k, "groups": a.groups, "ms": round(ms, 4),
+           "tflops": round(flops / ms / 1e9, 1), "gbs": round(bytes_ / ms / 1e6, 1),
+           "frac_fp8_peak": round(flops / ms / 1e9 / (2 * pk["bf16_tflops"]), 3),
+           "frac_hbm": round(bytes_ / ms / 1e6 / pk["hbm_gbs"], 3), "peaks": pk["src"]}
+    print(json.dumps(res))
+
+
+def _pad128_(n):
+    return (n + 127) // 128 * 128
+
+
+def cmd_gdn(a):
+    r = build_runner(4, a.m, 64, experts=32, vocab=8192)
+    b = r.buf
+    L = r.layers[0]
+    proj = b["proj"][: a.m * r.gdn_w].view(a.m, r.gdn_w)
+    proj.normal_()
+    midq = r._mid(r.hv * 128)
+    fn = lambda: r.C.gdn_decode(proj, r.hk, r.hv, L["conv_w"], r.conv_state[0], r.ssm_state[0], L["a_log"],  # noqa
+                                L["dt_bias"], L["gnorm"], r.eps, b["in_slot"][:a.m], b["in_pos"][:a.m], a.m, None,
+                                midq, b["midsf"], b["err"])
+    ms = time_fn(fn, flush=True)
+    state_bytes = a.m * r.hv * 128 * 128 * 4 * 2
+    pk = peaks()
+    print(json.dumps({"op": "gdn_decode", "rows": a.m, "ms": round(ms, 4), "gbs": round(state_bytes / ms / 1e6, 1),
+                      "frac_hbm": round(state_bytes / ms / 1e6 / pk["hbm_gbs"], 3), "peaks": pk["src"]}))
+
+
+def cmd_attn(a):
+    r = build_runner(4, a.m, a.ctx, experts=32, vocab=8192)
+    b = r.buf
+    b["q_out"].normal_()
+    b["gate_out"].normal_()
+    r.k_cache.normal_()
+    r.v_cache.normal_()
+    ai = 0
+    splits = r._attn_splits(a.m, True)
+    midq = r._mid(r.hq * 256)
+    fn = lambda: r.C.attn_decode(b["q_out"], b["gate_out"], r.hq, r.hkv, r.k_cache[ai], r.v_cache[ai], r.page_size,  # noqa
+                                 r.page_table, b["in_slot"][:a.m], b["in_len"][:a.m], a.m, b["partial"], splits,
+                                 1 / 16.0, None, midq, b["midsf"])
+    ms = time_fn(fn, flush=True)
+    kv_bytes = a.m * (a.ctx + 1) * r.hkv * 256 * 2 * 2
+    pk = peaks()
+    print(json.dumps({"op": "attn_decode", "rows": a.m, "ctx": a.ctx, "splits": splits, "ms": round(ms, 4),
+                      "gbs": round(kv_bytes / ms / 1e6, 1), "frac_hbm": round(kv_bytes / ms / 1e6 / pk["hbm_gbs"], 3),
+                      "peaks": pk["src"]}))
+
+
+def cmd_moe(a):
+    r = build_runner(4, a.m, 64, experts=256, vocab=8192)
+    L = r.layers[0]
+    # Realistic routing: quantize random activations into the MoE input buffer.
+    x = torch.randn(a.m, r.cfg.hidden_size, device="cuda").to(torch.bfloat16)
+    r.C.quant_mxf8(x, r.buf["xq"], r.buf["xsf"])
+    fn = lambda: r._moe(L, a.m)  # noqa: E731
+    ms = time_fn(fn, flush=True)
+    w_bytes = (L["gate_up"].q.numel() + L["down"].q.numel()) * (1 + 1 / 32)
+    pk = peaks()
+    print(json.dumps({"op": "moe_decode(router+route+gate_up+down)", "rows": a.m, "ms": round(ms, 4),
+                      "weight_gbs": round(w_bytes / ms / 1e6, 1),
+                      "frac_hbm": round(w_bytes / ms / 1e6 / pk["hbm_gbs"], 3), "peaks": pk["src"]}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("cmd", choices=["breakdown", "step", "gemm", "gdn", "attn", "moe"])
+    ap.add_argument("--layers", type=int, default=40)
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--ctx", type=int, default=1280)
+    ap.add_argument("--eager", type=int, default=0)
+    ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--m", type=int, default=256)
+    ap.add_argument("--n", type=int, default=2048)
+    ap.add_argument("--k", type=int, default=2048)
+    ap.add_argument("--groups", type=int, default=1)
+    a = ap.parse_args()
+    torch.manual_seed(0)
+    {"breakdown": cmd_breakdown, "step": cmd_step, "gemm": cmd_gemm, "gdn": cmd_gdn, "attn": cmd_attn,
+     "moe": cmd_moe}[a.cmd](a)
+
+
+if __name__ == "__main__":
+    main()

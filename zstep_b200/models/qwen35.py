@@ -245,14 +245,17 @@ class Qwen35Runner:
         b["proj"] = torch.zeros(R * max(self.gdn_w, self.qkv_w), dtype=torch.bfloat16, device=dev)
         b["midq"] = torch.zeros(Rp * self.mid_w, dtype=torch.uint8, device=dev)
         b["midsf"] = torch.zeros(mx.atoms_bytes(Rp, self.mid_w), dtype=torch.uint8, device=dev)
-        b["delta"] = torch.zeros(R, H, dtype=torch.bfloat16, device=dev)
+        # Row-parallel projection output: f32 split-K partials [splits, rows, H].
+        self.max_ksplit = 16
+        b["delta_f32"] = torch.zeros(max(R * H, self.max_ksplit * self.max_seqs * H), dtype=torch.float32,
+                                     device=dev)
         b["q_out"] = torch.zeros(R, self.hq, cfg.head_dim, dtype=torch.bfloat16, device=dev)
         b["gate_out"] = torch.zeros(R, self.hq, cfg.head_dim, dtype=torch.bfloat16, device=dev)
         self.max_splits = 16
         b["partial"] = torch.zeros(max(R * self.hq, self.max_seqs * self.hq * self.max_splits) * 260,
                                    dtype=torch.float32, device=dev)
         nr = self.layers[0]["router"].n_pad
-        b["logits"] = torch.zeros(R, nr, dtype=torch.float32, device=dev)
+        b["logits"] = torch.zeros(max(R * nr, self.max_ksplit * self.max_seqs * nr), dtype=torch.float32, device=dev)
         G = self.groups
         b["topk_ids"] = torch.zeros(R, self.top_k, **i32)
         b["topk_w"] = torch.zeros(R, self.top_k, dtype=torch.float32, device=dev)
@@ -289,14 +292,32 @@ class Qwen35Runner:
 
     # ------------------------------------------------------------------ kernels
     def _gemm(self, w: PackedLinear, xq, xsf, rows: int, out, ldo: int, epi=EPI_BF16, grouped=False,
-              out_sf=None, row_dst=None, row_scale=None):
+              out_sf=None, row_dst=None, row_scale=None, k_splits: int = 1):
         b = self.buf
         if grouped:
             self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, w.groups, 0, b["gcount"], b["goff"], b["gpre"],
-                             epi, out, ldo, out_sf, row_dst, row_scale, b["err"], 0)
+                             epi, out, ldo, out_sf, row_dst, row_scale, b["err"], 0, self._moe_bn(rows), 1, 0)
         else:
+            bn = 32 if rows <= 32 else 128
             self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, 1, rows, None, None, None, epi, out, ldo,
-                             out_sf, row_dst, row_scale, b["err"], 0)
+                             out_sf, row_dst, row_scale, b["err"], 0, bn, k_splits, rows * ldo)
+
+    def _moe_bn(self, rows: int) -> int:
+        """Token chunk of the grouped expert GEMMs: 32 while the average expert sees a few
+        tokens (decode), 128 for prefill-sized batches."""
+        return 32 if rows * self.top_k <= 32 * self.cfg.num_experts else 128
+
+    def _k_splits(self, w: PackedLinear, rows: int) -> int:
+        """Split K until the dense GEMM has about one wave of work items (decode only)."""
+        if rows > self.max_seqs:
+            return 1
+        bn = 32 if rows <= 32 else 128
+        items = ((rows + bn - 1) // bn) * (w.n_pad // 128)
+        k_tiles = w.k // 128
+        s = 1
+        while items * s * 2 <= 160 and s * 2 <= min(self.max_ksplit, k_tiles):
+            s *= 2
+        return s
 
     def _mid(self, width: int) -> torch.Tensor:
         rp = _pad128(self.R)
@@ -307,6 +328,14 @@ class Qwen35Runner:
             return 1
         ctas = rows * self.hkv
         return int(max(1, min(self.max_splits, math.ceil(2 * 148 / max(ctas, 1)))))
+
+    def _proj_out(self, w: PackedLinear, xq, xsf, rows: int, norm_w) -> None:
+        """Row-parallel output projection (GDN out_proj / attention o_proj) into f32
+        split-K partials, then residual add + RMSNorm (+ all-reduce across ranks)."""
+        H = self.cfg.hidden_size
+        s = self._k_splits(w, rows)
+        self._gemm(w, xq, xsf, rows, self.buf["delta_f32"], H, EPI_F32, k_splits=s)
+        self._row_parallel_reduce(self.buf["delta_f32"], rows, s, norm_w, rows * H, H)
 
     def _row_parallel_reduce(self, delta_rows: torch.Tensor, rows: int, n_terms: int, norm_w, term_stride: int,
                              row_stride: int):
@@ -339,7 +368,7 @@ class Qwen35Runner:
                     ck_rows, ck_slots, max_ck = ckpt if ckpt is not None else (None, None, 0)
                     C.gdn_prefill(*args, b["seq_start"][:num_seqs + 1], num_seqs, ck_rows, ck_slots, max_ck,
                                   b["err"])
-                self._gemm(L["out_proj"], midq, b["midsf"], rows, b["delta"], H)
+                self._proj_out(L["out_proj"], midq, b["midsf"], rows, L["post_norm"])
             else:
                 ai = self.attn_index[li]
                 qkv = b["proj"][:rows * self.qkv_w].view(rows, self.qkv_w)
@@ -352,8 +381,7 @@ class Qwen35Runner:
                 C.attn_decode(b["q_out"], b["gate_out"], self.hq, self.hkv, self.k_cache[ai], self.v_cache[ai],
                               self.page_size, self.page_table, slot, lens, rows, b["partial"], splits,
                               1.0 / math.sqrt(cfg.head_dim), None, midq, b["midsf"])
-                self._gemm(L["o_proj"], midq, b["midsf"], rows, b["delta"], H)
-            self._row_parallel_reduce(b["delta"], rows, 1, L["post_norm"], H, H)
+                self._proj_out(L["o_proj"], midq, b["midsf"], rows, L["post_norm"])
             self._moe(L, rows)
             next_w = self.layers[li + 1]["input_norm"] if li + 1 < len(self.layers) else self.final_norm
             self._row_parallel_reduce(b["pair_out"], rows, self.k1, next_w, H, self.k1 * H)
@@ -361,11 +389,13 @@ class Qwen35Runner:
     def _moe(self, L, rows: int) -> None:
         cfg, C, b = self.cfg, self.C, self.buf
         E = cfg.num_experts
-        self._gemm(L["router"], b["xq"], b["xsf"], rows, b["logits"], b["logits"].shape[1], EPI_F32)
+        nr = L["router"].n_pad
+        s = self._k_splits(L["router"], rows)
+        self._gemm(L["router"], b["xq"], b["xsf"], rows, b["logits"], nr, EPI_F32, k_splits=s)
         C.moe_route(b["logits"], rows, E, self.top_k, cfg.norm_topk_prob, 0, None, 1, 1, 1.0, E,
                     self.e_begin, self.e_begin + self.e_local, True, b["topk_ids"], b["topk_w"], b["gcount"],
                     b["goff"], b["gpre"], b["pair_slot"], b["row_dst"], b["row_scale"], b["xq"], b["xsf"], b["xg"],
-                    b["xg_sf"], b["err"])
+                    b["xg_sf"], b["err"], nr, s, rows * nr, self._moe_bn(rows))
         if self.tp > 1:
             # Pair rows of experts owned by other ranks must not leak stale values.
             b["pair_out"][: rows * self.k1].zero_()
@@ -461,6 +491,7 @@ class Qwen35Runner:
     def capture_decode_graph(self, bucket: int) -> None:
         """Capture one decode step over `bucket` rows into a CUDA graph."""
         b = self.buf
+        saved = b["inputs"].clone()
         self.pad_decode_inputs(0, bucket)
         s = torch.cuda.Stream(self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
@@ -472,6 +503,7 @@ class Qwen35Runner:
         with torch.cuda.graph(g, stream=s):
             self.decode_forward(bucket)
         self.graphs[bucket] = g
+        b["inputs"].copy_(saved)  # capture ran on dummy rows; restore the staged step
 
     def decode_step(self, n: int) -> torch.Tensor:
         """Replay the graph of the bucket that fits n staged rows (captured on demand)."""

@@ -10,6 +10,10 @@ Two implementations share one interface:
   reduces them in a fixed rank order (bit-identical on every rank), and applies the
   residual add, RMSNorm and MXFP8 quantization in the same pass.
 
+``allreduce_add_rmsnorm`` takes the local contribution as ``n_terms`` partial terms
+(split-K partials or MoE pair rows) addressed as ``delta[row*row_stride + t*term_stride
++ col]``; terms are summed in index order before the cross-rank reduction.
+
 Reference parity: the reference's host-SHM all-reduce + add + RMSNorm
 (worker/zstep_worker/kernels_sm120/shm_allreduce.py:437,514) and the TP=8 top-2
 argmax exchange (csrc/qwen35_ops_kernels.cu:202).
@@ -23,6 +27,16 @@ import torch.distributed as dist
 _SIGN = -(1 << 63)  # xor mask mapping unsigned key order onto signed int64 order
 
 
+def local_term_sum(delta: torch.Tensor, rows: int, hidden: int, n_terms: int, row_stride: int,
+                   term_stride: int) -> torch.Tensor:
+    """Sum of the local partial terms as fp32 [rows, hidden] (fixed term order)."""
+    view = torch.as_strided(delta, (n_terms, rows, hidden), (term_stride, row_stride, 1))
+    acc = view[0].float()
+    for t in range(1, n_terms):
+        acc = acc + view[t].float()
+    return acc
+
+
 class NcclCollectives:
     def __init__(self, group=None, device=None):
         from ..ops import _ext
@@ -32,22 +46,11 @@ class NcclCollectives:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.device = device
-        self._sum = None
-
-    def _scratch(self, rows: int, hidden: int, dtype) -> torch.Tensor:
-        if self._sum is None or self._sum.numel() < rows * hidden or self._sum.dtype != dtype:
-            self._sum = torch.empty(rows * hidden, dtype=dtype, device=self.device)
-        return self._sum[: rows * hidden].view(rows, hidden)
 
     def allreduce_add_rmsnorm(self, delta, n_terms: int, row_stride: int, term_stride: int, hidden_buf,
                               norm_w, eps: float, rows: int, xq, xsf) -> None:
         H = hidden_buf.shape[-1]
-        d = delta.view(-1)[: rows * row_stride].view(rows, row_stride)
-        acc = self._scratch(rows, H, torch.bfloat16)
-        if n_terms == 1:
-            acc.copy_(d[:, :H])
-        else:
-            acc.copy_(d.view(rows, n_terms, term_stride)[:, :, :H].float().sum(1))
+        acc = local_term_sum(delta, rows, H, n_terms, row_stride, term_stride).to(torch.bfloat16)
         dist.all_reduce(acc, group=self.group)
         self.C.add_rmsnorm_quant(hidden_buf, acc, 1, H, H, norm_w, 1.0, eps, rows, None, xq, xsf)
 
