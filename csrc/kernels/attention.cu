@@ -1,17 +1,22 @@
 // Gated GQA attention over a paged KV cache (Qwen3.5 full-attention layers).
 //
+// KV cache layout: [pages][kv_heads][page_size][head_dim] bf16, so the 16 tokens of one
+// (page, kv head) are one contiguous 8 KiB block that a single cp.async.bulk stages.
+//
 //  * prologue: per row, zero-centered RMSNorm of every q and k head ((1 + w) scale),
 //    partial rotary embedding (rotate-half over the first `rotary_dim` dims, cos/sin
 //    rounded to bf16 as a bf16 rotary cache would be), sigmoid-gate passthrough, and
 //    the K/V write into the row's page slot.
-//  * split-KV decode: one CTA per (row, kv head, split); one warp per query head of
-//    the GQA group; each warp splits into 4 lane groups that stream disjoint tokens
-//    (8 lanes x 32 dims per token), with an online softmax per lane group.  Partial
-//    (o, m, l) go to scratch and a combine kernel merges the splits, applies the
-//    sigmoid gate and emits bf16 and/or MXFP8 for the o_proj GEMM.
-//  * varlen prefill reuses the same kernels with each query row's causal context
-//    length (position + 1): K/V of the whole chunk are written first, then every
-//    query attends over its own prefix.
+//  * split-KV decode: one CTA per (row, kv head, split), one warp per query head of the
+//    GQA group.  Thread 0 streams the split's pages (K and V blocks) through a 4-deep
+//    shared-memory ring with cp.async.bulk + mbarriers; each warp splits into 4 lane
+//    groups that take one token each (8 lanes x 32 dims, bank-conflict-free 16-byte
+//    pieces), with an online softmax per lane group.  Partials (o, m, l) go to scratch
+//    and a combine kernel merges the splits, applies the sigmoid gate and emits bf16
+//    and/or MXFP8 for the o_proj GEMM.
+//  * varlen prefill reuses the same kernels with each query row's causal context length
+//    (position + 1): K/V of the whole chunk are written first, then every query row
+//    attends over its own prefix.
 //
 // Reference parity: worker/zstep_worker/kernels_sm120/qwen35_ops.py:187-560 (attention
 // prologue, split-K(16) paged GQA decode + gated reduce, varlen gated prefill).
@@ -21,11 +26,18 @@
 namespace zs {
 namespace attn {
 
-constexpr int D = 256;  // head_dim supported by these kernels
+constexpr int D = 256;       // head_dim supported by these kernels
+constexpr int PAGE = 16;     // tokens per page
+constexpr int RING = 4;      // staged pages per CTA
+constexpr int BLOCK_BYTES = PAGE * D * 2;  // one (page, kv head) block: 8 KiB
 
 __device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-// One CTA per row; one warp per head (q heads then k heads); lane owns 8 dims.
+__device__ __forceinline__ size_t kv_offset(const AttnArgs& a, int page, int kvh, int off) {
+  return (((size_t)page * a.num_kv_heads + kvh) * a.page_size + off) * D;
+}
+
+// One CTA per row; one warp per head (q heads then k heads then v heads); lane owns 8 dims.
 __global__ void prologue_kernel(const AttnArgs a) {
   const int row = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -33,15 +45,15 @@ __global__ void prologue_kernel(const AttnArgs a) {
   const int pos = a.positions[row];
   const int half = a.rotary_dim / 2;
   const __nv_bfloat16* qkv = static_cast<const __nv_bfloat16*>(a.qkv) + (size_t)row * a.ld_qkv;
+  const int slot = a.slots[row];
+  const int page = a.page_table[(size_t)slot * a.max_pages + pos / a.page_size];
   for (int h = warp; h < nh + a.num_kv_heads; h += blockDim.x >> 5) {
     if (h >= nh) {
       // V head: straight copy into the cache.
       const int kvh = h - nh;
-      const int slot = a.slots[row];
-      const int page = a.page_table[(size_t)slot * a.max_pages + pos / a.page_size];
-      const size_t dst = (((size_t)page * a.page_size + pos % a.page_size) * a.num_kv_heads + kvh) * D;
       const uint4* src = reinterpret_cast<const uint4*>(qkv + a.num_q_heads * 2 * D + a.num_kv_heads * D + kvh * D);
-      reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.v_cache) + dst)[lane] = src[lane];
+      reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.v_cache) + kv_offset(a, page, kvh, pos % a.page_size))[lane] =
+          src[lane];
       continue;
     }
     const bool is_q = h < a.num_q_heads;
@@ -104,94 +116,147 @@ __global__ void prologue_kernel(const AttnArgs a) {
       reinterpret_cast<uint4*>(go)[lane] = reinterpret_cast<const uint4*>(src + D)[lane];
     } else {
       const int kvh = h - a.num_q_heads;
-      const int slot = a.slots[row];
-      const int page = a.page_table[(size_t)slot * a.max_pages + pos / a.page_size];
-      const size_t dst = (((size_t)page * a.page_size + pos % a.page_size) * a.num_kv_heads + kvh) * D;
-      reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.k_cache) + dst)[lane] = pv;
+      reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.k_cache) + kv_offset(a, page, kvh, pos % a.page_size))[lane] =
+          pv;
     }
-  }
-}
-
-__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* f) {
-  uint4 u = *reinterpret_cast<const uint4*>(p);
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float2 v = __bfloat1622float2(h[j]);
-    f[2 * j] = v.x;
-    f[2 * j + 1] = v.y;
   }
 }
 
 // Partial record per (row, q head, split): o[256] (unnormalised), m, l, 2 pad floats.
 constexpr int PREC = D + 4;  // padded to keep each record 16-byte aligned
 
-__global__ void decode_partial_kernel(const AttnArgs a) {
+struct DecSmem {
+  __nv_bfloat16 k[RING][PAGE * D];
+  __nv_bfloat16 v[RING][PAGE * D];
+  uint64_t full[RING];
+  uint64_t empty[RING];
+  int abort_flag;
+};
+
+// Lane li of a lane group owns dims {c*64 + li*8 + 0..7 : c = 0..3}: a quarter-warp's
+// 16-byte accesses then cover 128 contiguous bytes (no bank conflicts).
+__device__ __forceinline__ void load_row_piece(const __nv_bfloat16* row, int li, float (&f)[32]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + c * 64 + li * 8);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 v = __bfloat1622float2(h[j]);
+      f[c * 8 + 2 * j] = v.x;
+      f[c * 8 + 2 * j + 1] = v.y;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) decode_partial_kernel(const AttnArgs a) {
+  __shared__ __align__(128) DecSmem s;
   const int row = blockIdx.x;
   const int kvh = blockIdx.y;
   const int split = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
   const int group = a.num_q_heads / a.num_kv_heads;
   const int qh = kvh * group + warp;
   const int grp = lane >> 3, li = lane & 7;
   const int ctx = a.seq_lens[row];
   const int slot = a.slots[row];
-  // Token range of this split, in whole pages.
-  const int pages = (ctx + a.page_size - 1) / a.page_size;
+  // Pages of this split.
+  const int pages = (ctx + PAGE - 1) / PAGE;
   const int pps = (pages + a.num_splits - 1) / a.num_splits;
-  const int t_begin = split * pps * a.page_size;
-  const int t_end = min(ctx, (split + 1) * pps * a.page_size);
+  const int p0 = split * pps;
+  const int p1 = min(pages, p0 + pps);
+  const int npg = max(0, p1 - p0);
+  const int* pt = a.page_table + (size_t)slot * a.max_pages;
+  const __nv_bfloat16* kc = static_cast<const __nv_bfloat16*>(a.k_cache);
+  const __nv_bfloat16* vc = static_cast<const __nv_bfloat16*>(a.v_cache);
+  volatile int* abort_flag = &s.abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < RING; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], nwarps);
+    }
+    s.abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  auto issue = [&](int pi) {
+    const int st = pi % RING;
+    const int page = __ldg(pt + p0 + pi);
+    mbar_expect_tx(&s.full[st], 2 * BLOCK_BYTES);
+    bulk_load(s.k[st], kc + kv_offset(a, page, kvh, 0), BLOCK_BYTES, &s.full[st]);
+    bulk_load(s.v[st], vc + kv_offset(a, page, kvh, 0), BLOCK_BYTES, &s.full[st]);
+  };
+  if (threadIdx.x == 0)
+    for (int pi = 0; pi < min(RING, npg); ++pi) issue(pi);
 
   const float qscale = a.sm_scale * 1.4426950408889634f;  // exp2 domain
   float q[32];
-  {
-    const __nv_bfloat16* qp = static_cast<const __nv_bfloat16*>(a.q_out) + ((size_t)row * a.num_q_heads + qh) * D + li * 32;
+  load_row_piece(static_cast<const __nv_bfloat16*>(a.q_out) + ((size_t)row * a.num_q_heads + qh) * D, li, q);
 #pragma unroll
-    for (int c = 0; c < 4; ++c) load8(qp + c * 8, q + c * 8);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) q[j] *= qscale;
-  }
+  for (int j = 0; j < 32; ++j) q[j] *= qscale;
   float o[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) o[j] = 0.f;
   float m = -INFINITY, l = 0.f;
-  const __nv_bfloat16* kc = static_cast<const __nv_bfloat16*>(a.k_cache);
-  const __nv_bfloat16* vc = static_cast<const __nv_bfloat16*>(a.v_cache);
-  const int* pt = a.page_table + (size_t)slot * a.max_pages;
-  // Every lane runs the same trip count (shuffles need the full warp); a lane group
-  // whose token is past the end contributes nothing.
-  for (int t0 = t_begin; t0 < t_end; t0 += 4) {
-    const int t = t0 + grp;
-    const bool valid = t < t_end;
-    const int tt = valid ? t : t_begin;
-    const int page = __ldg(pt + tt / a.page_size);
-    const size_t base = (((size_t)page * a.page_size + tt % a.page_size) * a.num_kv_heads + kvh) * D + li * 32;
-    float kf[32];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) load8(kc + base + c * 8, kf + c * 8);
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) s += q[j] * kf[j];
-    s += __shfl_xor_sync(0xffffffff, s, 1);
-    s += __shfl_xor_sync(0xffffffff, s, 2);
-    s += __shfl_xor_sync(0xffffffff, s, 4);
-    if (!valid) continue;
-    float vf[32];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) load8(vc + base + c * 8, vf + c * 8);
-    if (s > m) {
-      const float sc = exp2f(m - s);
-      l *= sc;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) o[j] *= sc;
-      m = s;
+
+  int pi = 0;
+  for (; pi < npg; ++pi) {
+    const int st = pi % RING;
+    bool ok = true;
+    for (uint32_t it = 0; !mbar_try_wait(&s.full[st], (pi / RING) & 1); ++it) {
+      if (*abort_flag || it > kMbarSpinLimit) { ok = false; break; }
     }
-    const float p = exp2f(s - m);
-    l += p;
+    if (!__all_sync(0xffffffff, ok)) {
+      report_error(a.err, kErrMbarTimeout);
+      *abort_flag = 1;
+      break;
+    }
+    const int tok0 = (p0 + pi) * PAGE;
+#pragma unroll 1
+    for (int t = grp; t < PAGE; t += 4) {
+      const bool valid = tok0 + t < ctx;
+      float kf[32];
+      load_row_piece(s.k[st] + t * D, li, kf);
+      float sc = 0.f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) o[j] += p * vf[j];
+      for (int j = 0; j < 32; ++j) sc += q[j] * kf[j];
+      sc += __shfl_xor_sync(0xffffffff, sc, 1);
+      sc += __shfl_xor_sync(0xffffffff, sc, 2);
+      sc += __shfl_xor_sync(0xffffffff, sc, 4);
+      if (!valid) continue;
+      float vf[32];
+      load_row_piece(s.v[st] + t * D, li, vf);
+      if (sc > m) {
+        const float r = exp2f(m - sc);
+        l *= r;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[j] *= r;
+        m = sc;
+      }
+      const float p = exp2f(sc - m);
+      l += p;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) o[j] += p * vf[j];
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&s.empty[st]);
+    // Refill this stage with page pi + RING once every warp is done with it.
+    if (threadIdx.x == 0 && pi + RING < npg) {
+      if (!mbar_wait(&s.empty[st], (pi / RING) & 1, a.err)) {
+        *abort_flag = 1;
+      } else {
+        issue(pi + RING);
+      }
+    }
   }
-  // Merge the 4 lane groups (xor 8, xor 16 swap groups with equal li).
+  // Drain (abort path): wait for copies that were issued but not consumed.
+  if (threadIdx.x == 0) {
+    const int issued = min(npg, pi + RING);
+    for (int j = pi; j < issued; ++j) mbar_wait(&s.full[j % RING], (j / RING) & 1, nullptr);
+  }
+  // Merge the 4 lane groups (xor 8, xor 16 pair groups with equal li).
 #pragma unroll
   for (int off = 8; off <= 16; off <<= 1) {
     const float m2 = __shfl_xor_sync(0xffffffff, m, off);
@@ -210,8 +275,11 @@ __global__ void decode_partial_kernel(const AttnArgs a) {
   if (grp == 0) {
     float* rec = a.partial + (((size_t)row * a.num_q_heads + qh) * a.num_splits + split) * PREC;
 #pragma unroll
-    for (int c = 0; c < 8; ++c)
-      reinterpret_cast<float4*>(rec + li * 32)[c] = make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+    for (int c = 0; c < 4; ++c) {
+      float4* dst = reinterpret_cast<float4*>(rec + c * 64 + li * 8);
+      dst[0] = make_float4(o[c * 8], o[c * 8 + 1], o[c * 8 + 2], o[c * 8 + 3]);
+      dst[1] = make_float4(o[c * 8 + 4], o[c * 8 + 5], o[c * 8 + 6], o[c * 8 + 7]);
+    }
     if (li == 0) {
       rec[D] = m;
       rec[D + 1] = l;
@@ -266,7 +334,7 @@ extern "C" int zs_attn_decode(const AttnArgs* args, cudaStream_t stream) {
   const AttnArgs& a = *args;
   if (a.head_dim != zs::attn::D || a.num_kv_heads <= 0 || a.num_q_heads % a.num_kv_heads != 0) return -1;
   const int group = a.num_q_heads / a.num_kv_heads;
-  if (group > 32 || a.num_splits < 1 || a.partial == nullptr) return -1;
+  if (group > 8 || a.num_splits < 1 || a.partial == nullptr || a.page_size != zs::attn::PAGE) return -1;
   if (a.rows == 0) return 0;
   dim3 g1(a.rows, a.num_kv_heads, a.num_splits);
   zs::attn::decode_partial_kernel<<<g1, group * 32, 0, stream>>>(a);

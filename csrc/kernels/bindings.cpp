@@ -41,7 +41,7 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
                const OptT& group_count, const OptT& group_offset, const OptT& chunk_prefix,
                int64_t epi_mode, const Tensor& out, int64_t ldo, const OptT& out_sf,
                const OptT& row_dst, const OptT& row_scale, const OptT& err, int64_t max_items,
-               int64_t block_n, int64_t k_splits, int64_t split_stride) {
+               int64_t block_n, int64_t k_splits, int64_t split_stride, int64_t a_tiled) {
   check_cuda(a, "a");
   check_cuda(sfa, "sfa");
   check_cuda(b, "b");
@@ -79,6 +79,7 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
   p.chunk_rows = (int)block_n;
   p.k_splits = (int)k_splits;
   p.split_stride = split_stride;
+  p.a_tiled = (int)a_tiled;
   if (k_splits > 1)
     TORCH_CHECK(out.numel() >= (k_splits - 1) * split_stride + m_rows * ldo, "split-K out too small");
   TORCH_CHECK(p.chunk_prefix == nullptr || (p.group_count && p.group_offset), "grouped mode args");

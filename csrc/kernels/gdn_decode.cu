@@ -218,26 +218,27 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_decode_tma_kernel(const GdnArg
     const float rq = rsqrtf(s.red[0] + s.red[1] + s.red[2] + s.red[3] + 1e-6f) * rsqrtf((float)DK);
     const float rk = rsqrtf(s.red[4] + s.red[5] + s.red[6] + s.red[7] + 1e-6f);
     const float beta = s.scal[0], g = s.scal[1];
-    // 2. delta rule on 32 coefficients (state row vr, k-quarter kq) from shared memory.
-    float4* srow = reinterpret_cast<float4*>(st.state + vr * DK + kq * 32);
-    float c[32];
-    if (!fresh) {
+    // 2. delta rule on 32 coefficients of state row vr.  The 4 threads of a row own
+    //    interleaved 16-byte pieces: piece i of thread kq covers k = seg(i)*16 + kq*4
+    //    + 0..3 with seg(i) = (i + vr) & 7, so each quarter-warp's 128-bit shared
+    //    accesses (2 rows x 4 threads) fall in distinct banks.
+    float* srow = st.state + vr * DK;
+    float c[32], qk[32], kk[32];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 f = srow[i];
-        c[4 * i] = f.x; c[4 * i + 1] = f.y; c[4 * i + 2] = f.z; c[4 * i + 3] = f.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) c[i] = 0.f;
+    for (int i = 0; i < 8; ++i) {
+      const int k0 = ((i + vr) & 7) * 16 + kq * 4;
+      const float4 f = fresh ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(srow + k0);
+      c[4 * i] = f.x; c[4 * i + 1] = f.y; c[4 * i + 2] = f.z; c[4 * i + 3] = f.w;
+      const float4 q4 = *reinterpret_cast<const float4*>(s.conv_out + k0);
+      const float4 k4 = *reinterpret_cast<const float4*>(s.conv_out + 128 + k0);
+      qk[4 * i] = q4.x; qk[4 * i + 1] = q4.y; qk[4 * i + 2] = q4.z; qk[4 * i + 3] = q4.w;
+      kk[4 * i] = k4.x; kk[4 * i + 1] = k4.y; kk[4 * i + 2] = k4.z; kk[4 * i + 3] = k4.w;
     }
-    const float* qv = s.conv_out + kq * 32;
-    const float* kv = s.conv_out + 128 + kq * 32;
     float kvm = 0.f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       c[i] *= g;
-      kvm += c[i] * kv[i];
+      kvm += c[i] * kk[i];
     }
     kvm *= rk;
     kvm += __shfl_xor_sync(0xffffffff, kvm, 1);
@@ -246,14 +247,17 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_decode_tma_kernel(const GdnArg
     float o = 0.f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      c[i] += kv[i] * delta;
-      o += c[i] * qv[i];
+      c[i] += kk[i] * delta;
+      o += c[i] * qk[i];
     }
     o *= rq;
     o += __shfl_xor_sync(0xffffffff, o, 1);
     o += __shfl_xor_sync(0xffffffff, o, 2);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) srow[i] = make_float4(c[4 * i], c[4 * i + 1], c[4 * i + 2], c[4 * i + 3]);
+    for (int i = 0; i < 8; ++i) {
+      const int k0 = ((i + vr) & 7) * 16 + kq * 4;
+      *reinterpret_cast<float4*>(srow + k0) = make_float4(c[4 * i], c[4 * i + 1], c[4 * i + 2], c[4 * i + 3]);
+    }
     if (kq == 0) s.o[vr] = o;
     // Make the generic-proxy smem writes (state, windows) visible to the bulk stores.
     fence_proxy_async_shared();

@@ -132,7 +132,8 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t phase, int
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                 const __grid_constant__ CUtensorMap tmap_b, const GemmMxf8Args p) {
+                 const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_b_full,
+                 const GemmMxf8Args p) {
   using C = Cfg<BN, STAGES>;
   using Smem = typename C::Smem;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -168,6 +169,7 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
   if (warp == 4 && lane == 0) {
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    tma_prefetch_desc(&tmap_b_full);
   }
   tc_fence_before();
   __syncthreads();
@@ -192,9 +194,16 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
           const uint32_t ph = ((issued / STAGES) & 1) ^ 1;
           if (!wait_or_abort(&s.empty[st], ph, p.err, abort_flag)) break;
           mbar_expect_tx(&s.full[st], bytes);
-          tma_load_2d(s.a[st], &tmap_a, &s.full[st], kt * BK, a_row);
-          for (int j = 0; j < n16; ++j)
-            tma_load_2d(s.b[st] + j * 16 * BK, &tmap_b, &s.full[st], kt * BK, b_row + j * 16);
+          if (p.a_tiled)
+            tma_load_3d(s.a[st], &tmap_a, &s.full[st], 0, 0, (a_row / BM) * k_tiles + kt);
+          else
+            tma_load_2d(s.a[st], &tmap_a, &s.full[st], kt * BK, a_row);
+          if (n16 * 16 == BN) {
+            tma_load_2d(s.b[st], &tmap_b_full, &s.full[st], kt * BK, b_row);  // one BN-row box
+          } else {
+            for (int j = 0; j < n16; ++j)
+              tma_load_2d(s.b[st] + j * 16 * BK, &tmap_b, &s.full[st], kt * BK, b_row + j * 16);
+          }
           bulk_load(s.sfa[st], sfa_src + (size_t)kt * SF_BYTES, SF_BYTES, &s.full[st]);
           bulk_load(s.sfb[st], sfb_src + (size_t)kt * SF_BYTES, SF_BYTES, &s.full[st]);
           ++issued;
@@ -441,6 +450,21 @@ int make_tmap_u8(CUtensorMap* m, const void* base, int64_t rows, int64_t k, int 
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
+// Pre-tiled weights: [tiles][128 rows][128 B] viewed as a 3-D tensor whose box is one
+// whole contiguous tile.
+int make_tmap_tiled(CUtensorMap* m, const void* base, int64_t tiles) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return -1;
+  cuuint64_t dims[3] = {128, 128, (cuuint64_t)tiles};
+  cuuint64_t strides[2] = {128, 128 * 128};
+  cuuint32_t box[3] = {128, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
 int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -452,7 +476,8 @@ int num_sms() {
 }
 
 template <int BN, int STAGES>
-int launch(const GemmMxf8Args& p, const CUtensorMap& ta, const CUtensorMap& tb, cudaStream_t stream) {
+int launch(const GemmMxf8Args& p, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbf,
+           cudaStream_t stream) {
   using namespace zs::gemm;
   int grid = num_sms();
   if (p.chunk_prefix == nullptr) {
@@ -466,7 +491,7 @@ int launch(const GemmMxf8Args& p, const CUtensorMap& ta, const CUtensorMap& tb, 
   const size_t smem = sizeof(typename Cfg<BN, STAGES>::Smem) + 1024;
   auto kern = gemm_mxf8_kernel<BN, STAGES>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  kern<<<grid, NUM_THREADS, smem, stream>>>(ta, tb, p);
+  kern<<<grid, NUM_THREADS, smem, stream>>>(ta, tb, tbf, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -15;
 }
 
@@ -485,7 +510,13 @@ extern "C" int zs_gemm_mxf8(const GemmMxf8Args* args, cudaStream_t stream) {
   if (p.chunk_prefix != nullptr && p.chunk_rows != bn) return -17;
   if (p.chunk_prefix != nullptr && p.groups > kMaxGroups) return -18;
   CUtensorMap ta, tb;
-  if (make_tmap_u8(&ta, p.a, (int64_t)p.groups * p.n_pad, p.k, BM) != 0) return -13;
+  if (p.a_tiled) {
+    if (make_tmap_tiled(&ta, p.a, (int64_t)p.groups * (p.n_pad / BM) * (p.k / BK)) != 0) return -13;
+  } else if (make_tmap_u8(&ta, p.a, (int64_t)p.groups * p.n_pad, p.k, BM) != 0) {
+    return -13;
+  }
   if (make_tmap_u8(&tb, p.b, p.b_rows, p.k, 16) != 0) return -14;
-  return bn == 32 ? launch<32, 9>(p, ta, tb, stream) : launch<128, 6>(p, ta, tb, stream);
+  CUtensorMap tbf;
+  if (make_tmap_u8(&tbf, p.b, p.b_rows, p.k, bn) != 0) return -14;
+  return bn == 32 ? launch<32, 9>(p, ta, tb, tbf, stream) : launch<128, 6>(p, ta, tb, tbf, stream);
 }

@@ -44,6 +44,8 @@ typedef struct GemmMxf8Args {
   int block_n;             // tokens per work item: 32 (decode) or 128
   int k_splits;            // dense mode, kEpiStoreF32 only: split K into this many partials
   long long split_stride;  // elements between split partials in out
+  int a_tiled;             // 1: weights pre-tiled as [groups*n_pad/128][k/128][128 rows][128 B]
+                           //    (each TMA box one contiguous 16 KiB block); 0: row-major
   int epi_mode;
   void* out;
   int ldo;                 // leading dimension of out in elements

@@ -21,8 +21,8 @@ def C():
     return _ext.load()
 
 
-def gemm(C, *args, block_n=128, k_splits=1, split_stride=0):
-    C.gemm_mxf8(*args, block_n, k_splits, split_stride)
+def gemm(C, *args, block_n=128, k_splits=1, split_stride=0, a_tiled=0):
+    C.gemm_mxf8(*args, block_n, k_splits, split_stride, a_tiled)
 
 
 def route(C, logits, *args, splits=1, split_stride=0, chunk_rows=128):
@@ -161,6 +161,30 @@ def test_gemm_split_k(C, m, splits, bn):
     torch.cuda.synchronize()
     expect = xd @ wd[0, :n].T
     torch.testing.assert_close(out.sum(0).cpu(), expect, rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("grouped", [False, True])
+def test_gemm_tiled_weights(C, grouped):
+    """Pre-tiled weight layout (contiguous 16 KiB blocks) gives identical results."""
+    counts = [5, 40, 0, 129]
+    k, n = 512, 384
+    s = _grouped_setup(counts if grouped else [200], k, n, seed=12)
+    g = len(counts) if grouped else 1
+    wq_t = mx.tile_weight(s["wq"].cpu()).cuda()
+    out = torch.full((s["rows"], n), float("nan"), device="cuda")
+    if grouped:
+        gemm(C, wq_t, s["wsf"], s["xq"], s["xsf"], k, s["npad"], n, g, 0, s["cnt"], s["off"], s["pre"], EPI_F32,
+             out, n, None, None, None, None, 0, a_tiled=1)
+    else:
+        gemm(C, wq_t, s["wsf"], s["xq"], s["xsf"], k, s["npad"], n, 1, 200, None, None, None, EPI_F32, out, n,
+             None, None, None, None, 0, a_tiled=1)
+    torch.cuda.synchronize()
+    out = out.cpu()
+    for gi, cnt in enumerate(counts if grouped else [200]):
+        if cnt == 0:
+            continue
+        o = s["offsets"][gi]
+        torch.testing.assert_close(out[o:o + cnt], s["xd"][o:o + cnt] @ s["wd"][gi, :n].T, rtol=1e-4, atol=1e-3)
 
 
 def test_gemm_silu_quant(C):
@@ -365,8 +389,8 @@ def test_attention_prologue_and_decode(C):
     qkv_w = hq * 2 * d + 2 * hkv * d
     page_table = torch.tensor([[3, 9, 5, 0], [1, 0, 0, 0], [12, 2, 0, 0]], dtype=torch.int32)
     slots = torch.arange(rows, dtype=torch.int32)
-    kc = (torch.randn(pages_total, page, hkv, d) * 0.5).to(torch.bfloat16)
-    vc = (torch.randn(pages_total, page, hkv, d) * 0.5).to(torch.bfloat16)
+    kc = (torch.randn(pages_total, hkv, page, d) * 0.5).to(torch.bfloat16)
+    vc = (torch.randn(pages_total, hkv, page, d) * 0.5).to(torch.bfloat16)
     qkv = (torch.randn(rows, qkv_w)).to(torch.bfloat16)
     qn = (0.1 * torch.randn(d)).to(torch.bfloat16)
     kn = (0.1 * torch.randn(d)).to(torch.bfloat16)
@@ -390,9 +414,9 @@ def test_attention_prologue_and_decode(C):
         torch.testing.assert_close(q_out[r].cpu().float(), q, rtol=2e-2, atol=2e-2)
         p_last = pos[r].item()
         pg = page_table[r, p_last // page].item()
-        torch.testing.assert_close(kc_g[pg, p_last % page].cpu().float(), k_new, rtol=2e-2, atol=2e-2)
-        keys = torch.stack([kc_g[page_table[r, t // page], t % page].cpu().float() for t in range(ctx[r])])
-        vals = torch.stack([vc_g[page_table[r, t // page], t % page].cpu().float() for t in range(ctx[r])])
+        torch.testing.assert_close(kc_g[pg, :, p_last % page].cpu().float(), k_new, rtol=2e-2, atol=2e-2)
+        keys = torch.stack([kc_g[page_table[r, t // page], :, t % page].cpu().float() for t in range(ctx[r])])
+        vals = torch.stack([vc_g[page_table[r, t // page], :, t % page].cpu().float() for t in range(ctx[r])])
         expect = ref.gated_attention(q_out[r].cpu().float(), g_out[r].cpu().float(), keys, vals, sm)
         torch.testing.assert_close(out[r].cpu().float(), expect, rtol=2e-2, atol=2e-2)
 

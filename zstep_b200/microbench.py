@@ -37,8 +37,10 @@ def peaks() -> dict:
 
 
 def _flush(n_bytes=256 << 20):
-    buf = _flush.__dict__.setdefault("buf", torch.empty(n_bytes, dtype=torch.uint8, device="cuda"))
-    buf.zero_()
+    """Evict L2 by *reading* a buffer twice its size (a write flush would leave dirty
+    lines that the timed kernel then has to write back)."""
+    buf = _flush.__dict__.setdefault("buf", torch.ones(n_bytes, dtype=torch.uint8, device="cuda"))
+    buf.max()
 
 
 def time_fn(fn, iters=20, warmup=3, flush=False) -> float:
@@ -158,14 +160,14 @@ def cmd_gemm(a):
     if a.groups == 1:
         bn = 32 if a.m <= 32 else 128
         fn = lambda: C.gemm_mxf8(pw.q, pw.sf, xq, xsf, a.k, pw.n_pad, a.n, 1, a.m, None, None, None, 0, out, a.n,  # noqa
-                                 None, None, None, None, 0, bn, 1, 0)
+                                 None, None, None, None, 0, bn, 1, 0, 1)
     else:
         cnt = torch.full((a.groups,), a.m, dtype=torch.int32, device="cuda")
         off = torch.arange(a.groups, dtype=torch.int32, device="cuda") * _pad128_(a.m)
         bn = 32 if a.m <= 32 else 128
         pre = torch.arange(a.groups + 1, dtype=torch.int32, device="cuda") * ((a.m + bn - 1) // bn)
         fn = lambda: C.gemm_mxf8(pw.q, pw.sf, xq, xsf, a.k, pw.n_pad, a.n, a.groups, 0, cnt, off, pre, 0, out,  # noqa
-                                 a.n, None, None, None, None, 0, bn, 1, 0)
+                                 a.n, None, None, None, None, 0, bn, 1, 0, 1)
     ms = time_fn(fn, flush=True)
     pk = peaks()
     flops = 2.0 * a.m * a.n * a.k * a.groups

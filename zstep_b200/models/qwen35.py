@@ -49,7 +49,8 @@ def _pad128(n: int) -> int:
 
 @dataclass
 class PackedLinear:
-    """MXFP8 weight in the GEMM layout: q [groups*n_pad, k] e4m3, sf scale atoms."""
+    """MXFP8 weight in the GEMM layout: q e4m3 pre-tiled into contiguous 128x128-byte
+    blocks ([groups*n_pad/128][k/128][128][128]), sf scale atoms."""
 
     q: torch.Tensor
     sf: torch.Tensor
@@ -74,7 +75,7 @@ def pack_linear(w: torch.Tensor, C) -> PackedLinear:
     q = torch.empty(g * npad, k, dtype=torch.uint8, device=w.device)
     sf = torch.empty(mx.atoms_bytes(g * npad, k), dtype=torch.uint8, device=w.device)
     C.quant_mxf8(flat, q, sf)
-    return PackedLinear(q=q, sf=sf, n=n, n_pad=npad, k=k, groups=g)
+    return PackedLinear(q=mx.tile_weight(q), sf=sf, n=n, n_pad=npad, k=k, groups=g)
 
 
 def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
@@ -222,7 +223,7 @@ class Qwen35Runner:
         self.conv_dim = conv_dim
         self.conv_state = torch.zeros(nG, self.num_slots, 2, conv_dim, 3, dtype=torch.bfloat16, device=dev)
         self.ssm_state = torch.zeros(nG, self.num_slots, self.hv, 128, 128, dtype=torch.float32, device=dev)
-        kv_shape = (nA, self.num_pages, self.page_size, self.hkv, cfg.head_dim)
+        kv_shape = (nA, self.num_pages, self.hkv, self.page_size, cfg.head_dim)  # head-major pages
         self.k_cache = torch.zeros(kv_shape, dtype=torch.bfloat16, device=dev)
         self.v_cache = torch.zeros(kv_shape, dtype=torch.bfloat16, device=dev)
         # Page table: one row per request slot (+ dummy row).  Page 0 is the dummy page.
@@ -296,11 +297,11 @@ class Qwen35Runner:
         b = self.buf
         if grouped:
             self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, w.groups, 0, b["gcount"], b["goff"], b["gpre"],
-                             epi, out, ldo, out_sf, row_dst, row_scale, b["err"], 0, self._moe_bn(rows), 1, 0)
+                             epi, out, ldo, out_sf, row_dst, row_scale, b["err"], 0, self._moe_bn(rows), 1, 0, 1)
         else:
             bn = 32 if rows <= 32 else 128
             self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, 1, rows, None, None, None, epi, out, ldo,
-                             out_sf, row_dst, row_scale, b["err"], 0, bn, k_splits, rows * ldo)
+                             out_sf, row_dst, row_scale, b["err"], 0, bn, k_splits, rows * ldo, 1)
 
     def _moe_bn(self, rows: int) -> int:
         """Token chunk of the grouped expert GEMMs: 32 while the average expert sees a few
@@ -327,7 +328,7 @@ class Qwen35Runner:
         if not decode:
             return 1
         ctas = rows * self.hkv
-        return int(max(1, min(self.max_splits, math.ceil(2 * 148 / max(ctas, 1)))))
+        return int(max(1, min(self.max_splits, math.ceil(1200 / max(ctas, 1)))))
 
     def _proj_out(self, w: PackedLinear, xq, xsf, rows: int, norm_w) -> None:
         """Row-parallel output projection (GDN out_proj / attention o_proj) into f32

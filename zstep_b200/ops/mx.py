@@ -87,6 +87,14 @@ def quantize_to_atoms(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return q, atoms_from_codes(code)
 
 
+def tile_weight(q: torch.Tensor) -> torch.Tensor:
+    """Row-major e4m3 weight [rows, k] (rows % 128 == 0, k % 128 == 0) -> the GEMM's
+    pre-tiled layout [rows/128][k/128][128][128]: every 128x128-byte block of one
+    (feature tile, K tile) becomes one contiguous 16 KiB chunk (one TMA box)."""
+    rows, k = q.shape
+    return q.view(rows // 128, 128, k // 128, 128).permute(0, 2, 1, 3).contiguous().view(rows, k)
+
+
 def fake_quant(x: torch.Tensor) -> torch.Tensor:
     """Quantize-dequantize round trip (the value an MXFP8 GEMM actually multiplies)."""
     q, code = quantize(x)
