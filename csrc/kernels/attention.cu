@@ -150,7 +150,8 @@ __device__ __forceinline__ void load_row_piece(const __nv_bfloat16* row, int li,
 }
 
 __global__ void __launch_bounds__(256) decode_partial_kernel(const AttnArgs a) {
-  __shared__ __align__(128) DecSmem s;
+  extern __shared__ __align__(128) uint8_t dec_smem_raw[];
+  DecSmem& s = *reinterpret_cast<DecSmem*>((reinterpret_cast<uintptr_t>(dec_smem_raw) + 127) & ~uintptr_t(127));
   const int row = blockIdx.x;
   const int kvh = blockIdx.y;
   const int split = blockIdx.z;
@@ -337,7 +338,9 @@ extern "C" int zs_attn_decode(const AttnArgs* args, cudaStream_t stream) {
   if (group > 8 || a.num_splits < 1 || a.partial == nullptr || a.page_size != zs::attn::PAGE) return -1;
   if (a.rows == 0) return 0;
   dim3 g1(a.rows, a.num_kv_heads, a.num_splits);
-  zs::attn::decode_partial_kernel<<<g1, group * 32, 0, stream>>>(a);
+  const size_t smem = sizeof(zs::attn::DecSmem) + 128;
+  cudaFuncSetAttribute(zs::attn::decode_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  zs::attn::decode_partial_kernel<<<g1, group * 32, smem, stream>>>(a);
   dim3 g2(a.rows, a.num_q_heads);
   zs::attn::decode_combine_kernel<<<g2, zs::attn::D, 0, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;

@@ -48,9 +48,11 @@ template <int BN, int STAGES>
 struct Cfg {
   static constexpr int B_BYTES = BN * BK;
   static constexpr int ACC_COLS = BN;              // fp32 accumulator columns per buffer
-  static constexpr int SFA_COL = 2 * BN;           // 4 columns
-  static constexpr int SFB_COL = 2 * BN + 4;       // 4 columns
-  static constexpr int TMEM_COLS = (2 * BN + 8) <= 128 ? 128 : ((2 * BN + 8) <= 256 ? 256 : 512);
+  // Scale factors are double-buffered by K-tile parity (8 columns per buffer: SFA 4 +
+  // SFB 4) so staging the next tile's scales does not wait for this tile's MMAs.
+  static constexpr int SFA_COL = 2 * BN;           // + 8 * (kt & 1), 4 columns
+  static constexpr int SFB_COL = 2 * BN + 4;       // + 8 * (kt & 1), 4 columns
+  static constexpr int TMEM_COLS = (2 * BN + 16) <= 128 ? 128 : ((2 * BN + 16) <= 256 ? 256 : 512);
   struct Smem {
     uint8_t a[STAGES][A_BYTES];
     uint8_t b[STAGES][B_BYTES];
@@ -194,8 +196,8 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
           const uint32_t ph = ((issued / STAGES) & 1) ^ 1;
           if (!wait_or_abort(&s.empty[st], ph, p.err, abort_flag)) break;
           mbar_expect_tx(&s.full[st], bytes);
-          if (p.a_tiled)
-            tma_load_3d(s.a[st], &tmap_a, &s.full[st], 0, 0, (a_row / BM) * k_tiles + kt);
+          if (p.a_tiled)  // pre-swizzled contiguous tile: plain bulk copy
+            bulk_load(s.a[st], p.a + ((size_t)(a_row / BM) * k_tiles + kt) * A_BYTES, A_BYTES, &s.full[st]);
           else
             tma_load_2d(s.a[st], &tmap_a, &s.full[st], kt * BK, a_row);
           if (n16 * 16 == BN) {
@@ -255,8 +257,9 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
         }
         tc_fence_after();
         if (lane == 0) {
-          tmem_cp_32x128b_warpx4(tmem + C::SFA_COL, make_smem_desc(smem_u32(s.sfa[st]), 0, 128, 0));
-          tmem_cp_32x128b_warpx4(tmem + C::SFB_COL, make_smem_desc(smem_u32(s.sfb[st]), 0, 128, 0));
+          const uint32_t sf_off = (consumed & 1) * 8;
+          tmem_cp_32x128b_warpx4(tmem + C::SFA_COL + sf_off, make_smem_desc(smem_u32(s.sfa[st]), 0, 128, 0));
+          tmem_cp_32x128b_warpx4(tmem + C::SFB_COL + sf_off, make_smem_desc(smem_u32(s.sfb[st]), 0, 128, 0));
           const uint32_t a_base = smem_u32(s.a[st]);
           const uint32_t b_base = smem_u32(s.b[st]);
 #pragma unroll
@@ -264,8 +267,8 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const uint64_t adesc = make_smem_desc(a_base + kb * 32, 16, 1024, 2);
             const uint64_t bdesc = make_smem_desc(b_base + kb * 32, 16, 1024, 2);
             const uint32_t idesc = make_idesc_mxf8(BM, n_mma, kb, kb);
-            mma_mxf8(d_tmem, adesc, bdesc, idesc, (tmem + C::SFA_COL) | (uint32_t(kb) << 30),
-                     (tmem + C::SFB_COL) | (uint32_t(kb) << 30), (kt > it.kt0 || kb > 0) ? 1u : 0u);
+            mma_mxf8(d_tmem, adesc, bdesc, idesc, (tmem + C::SFA_COL + sf_off) | (uint32_t(kb) << 30),
+                     (tmem + C::SFB_COL + sf_off) | (uint32_t(kb) << 30), (kt > it.kt0 || kb > 0) ? 1u : 0u);
           }
           tc_commit(&s.empty[st]);
         }

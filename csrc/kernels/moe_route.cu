@@ -261,8 +261,8 @@ extern "C" int zs_moe_route(const MoeRouteArgs* args, cudaStream_t stream) {
     zs::moe::offsets_kernel<<<1, 1024, 0, stream>>>(a, groups);
     return cudaGetLastError() == cudaSuccess ? 0 : -2;
   }
-  const int wpb = 8;
-  zs::moe::route_topk_kernel<<<(a.rows + wpb - 1) / wpb, wpb * 32, 0, stream>>>(a);
+  int wpb = 8;
+  zs::moe::route_topk_kernel<<<(a.rows + 1) / 2, 64, 0, stream>>>(a);  // 2 rows per block: more SMs busy
   zs::moe::offsets_kernel<<<1, 1024, 0, stream>>>(a, groups);
   const int pairs = a.rows * (a.top_k + 1);
   zs::moe::scatter_kernel<<<(pairs + wpb - 1) / wpb, wpb * 32, 0, stream>>>(a);

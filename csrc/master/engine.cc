@@ -1,0 +1,437 @@
+#include "engine.h"
+
+#include <algorithm>
+#include <cmath>
+#include <stdexcept>
+
+namespace zs {
+namespace engine {
+
+struct Engine::Seq {
+  Request req;
+  int32_t slot = -1;
+  std::vector<int32_t> tokens;  // prompt + generated
+  uint32_t prompt_len = 0;
+  uint32_t computed = 0;        // tokens whose KV / recurrent state is in cache
+  uint32_t generated = 0;
+  uint32_t cached_tokens = 0;   // prompt tokens served from the prefix cache
+  kv::PrefixLease prefix;       // pinned cached / promoted nodes
+  kv::BlockLease own;           // own pages not promoted yet (front = next node)
+  kv::BlockLease held;          // own pages that lost a promotion race (still in use)
+  std::vector<int32_t> page_table;
+  bool table_dirty = true;
+  int32_t restore_slot = -1;    // checkpoint restored before the first prefill chunk
+  uint64_t last_node = 0;       // deepest node of this sequence's prefix in the tree
+  uint32_t promoted_nodes = 0;
+  std::vector<int32_t> drafts;
+  // Staged in the current step:
+  uint32_t rows = 0;            // rows of this sequence in the step
+  bool sampled = false;
+  std::vector<std::pair<uint32_t, kv::BlockLease>> promote;  // (node index, checkpoint lease)
+  bool first_emitted = false;
+};
+
+uint64_t splitmix64(uint64_t& state) {
+  uint64_t z = (state += 0x9E3779B97F4A7C15ull);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+std::vector<std::vector<int32_t>> random_prompts(uint64_t seed, size_t count, size_t len, int32_t low, int32_t high) {
+  std::vector<std::vector<int32_t>> out(count, std::vector<int32_t>(len));
+  uint64_t st = seed;
+  const uint64_t span = uint64_t(std::max(1, high - low));
+  for (auto& p : out)
+    for (auto& t : p) t = low + int32_t(splitmix64(st) % span);
+  return out;
+}
+
+Engine::Engine(Config cfg, std::shared_ptr<Backend> backend)
+    : cfg_(std::move(cfg)),
+      backend_(std::move(backend)),
+      pages_(int32_t(cfg_.num_pages) - 1, 1),  // page 0 = dummy page for padding rows
+      ckpt_slots_(int32_t(cfg_.num_ckpt_slots), int32_t(cfg_.max_seqs)) {
+  if (cfg_.prefix_caching)
+    tree_ = std::make_unique<kv::PrefixTree>(cfg_.page_size, cfg_.pages_per_node, cfg_.kv_hash_seed);
+  for (int32_t s = int32_t(cfg_.max_seqs) - 1; s >= 0; --s) free_slots_.push_back(s);
+}
+
+Engine::~Engine() = default;
+
+void Engine::set_event_sink(kv::KvEventSink sink) {
+  if (tree_) tree_->set_event_sink(std::move(sink));
+}
+
+bool Engine::submit(Request r) {
+  if (waiting_.size() >= cfg_.max_waiting) return false;
+  waiting_since_[r.id] = stats_.steps;
+  waiting_.push_back(std::move(r));
+  return true;
+}
+
+bool Engine::cancel(uint64_t id) {
+  for (auto it = waiting_.begin(); it != waiting_.end(); ++it) {
+    if (it->id == id) {
+      waiting_since_.erase(id);
+      waiting_.erase(it);
+      return true;
+    }
+  }
+  for (auto& kvp : running_) {
+    if (kvp.second->req.id == id) {
+      retire(kvp.second.get());
+      running_.erase(kvp.first);
+      return true;
+    }
+  }
+  return false;
+}
+
+bool Engine::has_work() const { return !waiting_.empty() || !running_.empty(); }
+
+EngineStats Engine::stats() const {
+  EngineStats s = stats_;
+  s.waiting = uint32_t(waiting_.size());
+  s.running = uint32_t(running_.size());
+  const size_t total = cfg_.num_pages - 1;
+  s.kv_usage = total ? 1.0 - double(pages_.available()) / double(total) : 0.0;
+  if (tree_) {
+    const auto t = tree_->stats();
+    s.prefix_queries = t.queries;
+    s.prefix_query_tokens = t.query_tokens;
+    s.prefix_hit_tokens = t.hit_tokens;
+    s.prefix_evictions = t.evictions;
+  }
+  return s;
+}
+
+// ---------------------------------------------------------------------------- admission
+bool Engine::admit_one() {
+  if (waiting_.empty() || free_slots_.empty()) return false;
+  // Pick the candidate: FIFO, or shortest prompt first (SRPT) unless some request
+  // has waited longer than the starvation cap.
+  size_t pick = 0;
+  if (cfg_.prefill_policy == "srpt") {
+    size_t oldest = 0;
+    for (size_t i = 1; i < waiting_.size(); ++i)
+      if (waiting_since_[waiting_[i].id] < waiting_since_[waiting_[oldest].id]) oldest = i;
+    if (stats_.steps - waiting_since_[waiting_[oldest].id] >= cfg_.starvation_steps) {
+      pick = oldest;
+    } else {
+      for (size_t i = 1; i < waiting_.size(); ++i)
+        if (waiting_[i].prompt.size() < waiting_[pick].prompt.size()) pick = i;
+    }
+  }
+  Request& r = waiting_[pick];
+  const uint32_t ps = cfg_.page_size;
+  const uint64_t want = std::min<uint64_t>(uint64_t(r.prompt.size()) + r.max_tokens, cfg_.max_model_len);
+  const uint32_t total_pages = uint32_t((want + ps - 1) / ps);
+  if (r.prompt.empty() || r.prompt.size() >= cfg_.max_model_len || total_pages > cfg_.num_pages - 1) {
+    // Can never fit: fail this request (the caller reports it).
+    auto s = make_seq(std::move(r));
+    waiting_since_.erase(s->req.id);
+    waiting_.erase(waiting_.begin() + pick);
+    s->slot = -1;
+    error_ = "request " + std::to_string(s->req.id) + " exceeds the model length or KV capacity";
+    return false;
+  }
+  // Prefix match over prompt[:-1] (the last token must be computed to sample).
+  kv::PrefixLease lease;
+  if (tree_) {
+    std::vector<int32_t> key(r.prompt.begin(), r.prompt.end() - 1);
+    lease = tree_->match(key);
+    if (cfg_.recurrent_state && lease.matched_nodes() > 0 && lease.leaf_aux() < 0) lease.release();
+  }
+  const uint32_t matched_pages = uint32_t(lease.pages().size());
+  const uint32_t own_needed = total_pages > matched_pages ? total_pages - matched_pages : 0;
+  if (pages_.available() < own_needed && tree_) tree_->evict_lru(own_needed - pages_.available());
+  if (pages_.available() < own_needed) return false;  // wait for running requests to finish
+  auto own = pages_.allocate(own_needed);
+  auto seq = make_seq(std::move(r));
+  waiting_since_.erase(seq->req.id);
+  waiting_.erase(waiting_.begin() + pick);
+  seq->slot = free_slots_.back();
+  free_slots_.pop_back();
+  seq->page_table = lease.pages();
+  seq->page_table.insert(seq->page_table.end(), own->ids().begin(), own->ids().end());
+  seq->own = std::move(*own);
+  seq->computed = lease.matched_tokens();
+  seq->cached_tokens = lease.matched_tokens();
+  seq->restore_slot = cfg_.recurrent_state ? lease.leaf_aux() : -1;
+  seq->last_node = lease.leaf_node();
+  seq->promoted_nodes = uint32_t(lease.matched_nodes());
+  seq->prefix = std::move(lease);
+  running_[seq->slot] = std::move(seq);
+  return true;
+}
+
+std::unique_ptr<Engine::Seq> Engine::make_seq(Request&& r) {
+  auto s = std::make_unique<Seq>();
+  s->tokens = r.prompt;
+  s->prompt_len = uint32_t(r.prompt.size());
+  s->req = std::move(r);
+  return s;
+}
+
+// ---------------------------------------------------------------------------- drafting
+std::vector<int32_t> Engine::ngram_drafts(const Seq& s) const {
+  // Most recent earlier occurrence of the last n tokens; propose what followed it.
+  const size_t n = cfg_.ngram_n, k = cfg_.num_spec_tokens;
+  const auto& t = s.tokens;
+  if (t.size() <= n || k == 0) return {};
+  for (size_t start = t.size() - n; start-- > 0;) {
+    if (std::equal(t.begin() + start, t.begin() + start + n, t.end() - n)) {
+      std::vector<int32_t> d;
+      for (size_t j = start + n; j < t.size() - n + n && d.size() < k && j < t.size(); ++j) d.push_back(t[j]);
+      return d;
+    }
+  }
+  return {};
+}
+
+// ---------------------------------------------------------------------------- staging
+void Engine::stage(StepPlan& p, std::vector<Seq*>& order) {
+  p = StepPlan();
+  p.query_start.push_back(0);
+  uint32_t budget = cfg_.max_step_tokens;
+  bool any_prefill = false, any_spec = false, any_sampling = false, any_penalty = false, any_logprobs = false;
+  const uint32_t nt = tree_ ? tree_->node_tokens() : 0;
+
+  auto add_seq = [&](Seq* s, uint32_t rows, const int32_t* toks, uint32_t pos0, bool sample, uint32_t spec_w) {
+    const int32_t row0 = int32_t(p.token_ids.size());
+    for (uint32_t i = 0; i < rows; ++i) {
+      p.token_ids.push_back(toks[i]);
+      p.positions.push_back(int32_t(pos0 + i));
+      p.row_slot.push_back(s->slot);
+    }
+    p.query_start.push_back(int32_t(p.token_ids.size()));
+    p.seq_slot.push_back(s->slot);
+    p.seq_len.push_back(int32_t(pos0 + rows));
+    p.sample_row.push_back(sample ? int32_t(p.token_ids.size()) - 1 : -1);
+    p.spec_width.push_back(int32_t(spec_w));
+    wire::SamplingParams sp{};
+    sp.temperature = s->req.sampling.temperature;
+    sp.top_p = s->req.sampling.top_p;
+    sp.top_k = s->req.sampling.top_k;
+    sp.presence_penalty = s->req.sampling.presence_penalty;
+    sp.frequency_penalty = s->req.sampling.frequency_penalty;
+    sp.repetition_penalty = s->req.sampling.repetition_penalty;
+    sp.seed = s->req.sampling.seed + s->generated;
+    sp.logprobs = s->req.sampling.logprobs;
+    p.sampling.push_back(sp);
+    any_sampling |= sp.temperature > 0.f;
+    any_penalty |= sp.presence_penalty != 0.f || sp.frequency_penalty != 0.f || sp.repetition_penalty != 1.f;
+    any_logprobs |= sp.logprobs >= 0;
+    p.restore_slot.push_back(s->restore_slot);
+    s->restore_slot = -1;
+    s->rows = rows;
+    s->sampled = sample;
+    order.push_back(s);
+    (void)row0;
+  };
+
+  // 1. Decode rows (all sequences past their prompt), optionally with draft tokens.
+  for (auto& kvp : running_) {
+    Seq* s = kvp.second.get();
+    if (s->computed < s->prompt_len) continue;
+    const uint32_t pos = s->computed;  // feed tokens[computed]
+    std::vector<int32_t> rows{s->tokens[pos]};
+    uint32_t spec_w = 0;
+    if (cfg_.spec_method == "ngram" && cfg_.num_spec_tokens > 0) {
+      s->drafts = ngram_drafts(*s);
+      const uint32_t room = uint32_t(cfg_.max_model_len) - pos - 1;
+      while (s->drafts.size() > room) s->drafts.pop_back();
+      const uint32_t left = s->req.max_tokens - s->generated;
+      while (!s->drafts.empty() && s->drafts.size() + 1 > left) s->drafts.pop_back();
+    } else if (cfg_.spec_method == "mtp") {
+      // drafts were proposed by the worker in the previous step's result
+    } else {
+      s->drafts.clear();
+    }
+    if (!s->drafts.empty()) {
+      rows.insert(rows.end(), s->drafts.begin(), s->drafts.end());
+      spec_w = uint32_t(rows.size());
+      any_spec = true;
+      stats_.spec_drafts += s->drafts.size();
+    }
+    if (rows.size() > budget) continue;
+    budget -= uint32_t(rows.size());
+    add_seq(s, uint32_t(rows.size()), rows.data(), pos, true, spec_w);
+  }
+  // 2. Prefill chunks, in admission (slot) order.
+  for (auto& kvp : running_) {
+    Seq* s = kvp.second.get();
+    if (s->computed >= s->prompt_len || budget == 0) continue;
+    const uint32_t chunk = std::min({s->prompt_len - s->computed, cfg_.max_prefill_chunk, budget});
+    const uint32_t c0 = s->computed, c1 = c0 + chunk;
+    const int32_t row_base = int32_t(p.token_ids.size());
+    add_seq(s, chunk, s->tokens.data() + c0, c0, c1 == s->prompt_len, 0);
+    budget -= chunk;
+    any_prefill = true;
+    // APC: checkpoint + promote the nodes this chunk completes.
+    if (tree_) {
+      for (uint32_t node = s->promoted_nodes + uint32_t(s->promote.size()); (node + 1) * nt <= c1; ++node) {
+        if ((node + 1) * nt <= c0) continue;
+        kv::BlockLease aux;
+        if (cfg_.recurrent_state) {
+          auto a = ckpt_slots_.allocate(1);
+          if (!a) {
+            tree_->evict_lru(1);
+            a = ckpt_slots_.allocate(1);
+          }
+          if (!a) break;  // no checkpoint slot: stop promoting this sequence
+          p.ckpt_row.push_back(row_base + int32_t((node + 1) * nt - 1 - c0));
+          p.ckpt_slot.push_back(a->ids()[0]);
+          aux = std::move(*a);
+        }
+        s->promote.emplace_back(node, std::move(aux));
+      }
+    }
+  }
+  // 3. Page-table rows of newly admitted sequences.
+  for (Seq* s : order) {
+    if (s->table_dirty) {
+      p.dirty_rows.push_back(s->slot);
+      p.dirty_pages.push_back(s->page_table);
+      s->table_dirty = false;
+    }
+  }
+  if (!any_prefill && !any_spec && !order.empty()) {
+    p.flags |= wire::kFlagDecodeOnly;
+    p.bucket = wire::select_bucket(uint32_t(order.size()));
+  }
+  if (any_spec) p.flags |= wire::kFlagSpecVerify;
+  if (any_sampling) p.flags |= wire::kFlagSampling;
+  if (any_penalty) p.flags |= wire::kFlagPenalty | wire::kFlagSampling;
+  if (any_logprobs) p.flags |= wire::kFlagLogprobs;
+}
+
+// ---------------------------------------------------------------------------- step
+std::vector<TokenEvent> Engine::step() {
+  std::vector<TokenEvent> events;
+  if (poisoned_) return events;
+  while (admit_one()) {
+  }
+  if (!error_.empty() && running_.empty() && waiting_.empty()) {
+    // An unfittable request was dropped by admit_one.
+  }
+  if (running_.empty()) return events;
+  std::vector<Seq*> order;
+  stage(plan_, order);
+  if (order.empty()) return events;
+  ++stats_.steps;
+  if (plan_.flags & wire::kFlagDecodeOnly) ++stats_.decode_steps;
+  StepResult res;
+  if (!backend_->execute(plan_, &res) || res.status != 0 || res.outputs.size() < order.size()) {
+    poisoned_ = true;
+    error_ = backend_->error().empty() ? "worker step failed" : backend_->error();
+    for (auto& kvp : running_) {
+      TokenEvent ev;
+      ev.request_id = kvp.second->req.id;
+      ev.finish = Finish::kError;
+      events.push_back(ev);
+      retire(kvp.second.get());
+    }
+    running_.clear();
+    return events;
+  }
+  stats_.last_gpu_us = res.gpu_exec_us;
+  std::vector<int32_t> done;
+  for (size_t i = 0; i < order.size(); ++i) {
+    Seq* s = order[i];
+    const wire::SeqStepOutput& out = res.outputs[i];
+    // Promote the prefix nodes completed by this step.
+    for (auto& pr : s->promote) {
+      const uint32_t node = pr.first;
+      kv::BlockLease pages = s->own.take_front(cfg_.pages_per_node);
+      bool created = false;
+      const uint64_t id = tree_->insert(s->last_node, s->tokens.data() + size_t(node) * tree_->node_tokens(), pages,
+                                        pr.second, &created);
+      if (!created) s->held.absorb(std::move(pages));  // lost a race: keep using our copy
+      if (id == 0) break;
+      s->last_node = id;
+      s->prefix = tree_->pin_chain(id);
+      ++s->promoted_nodes;
+    }
+    s->promote.clear();
+    if (!s->sampled) {
+      s->computed += s->rows;
+      stats_.prefill_tokens += s->rows;
+      continue;
+    }
+    const bool was_prefill = s->computed < s->prompt_len;
+    if (was_prefill) stats_.prefill_tokens += s->rows; else stats_.decode_tokens += 1;
+    // Accepted tokens: for a verify step, drafts that matched plus the bonus token.
+    const int32_t n_tok = std::max(1, std::min<int32_t>(out.num_tokens, wire::kMaxSpecTokens));
+    if (s->rows > 1 && !was_prefill) {
+      stats_.spec_verify_rows += s->rows;
+      stats_.spec_accepted += uint32_t(n_tok - 1);
+      s->computed += uint32_t(n_tok);  // fed row 0 + accepted drafts
+    } else {
+      s->computed += s->rows;
+    }
+    TokenEvent ev;
+    ev.request_id = s->req.id;
+    ev.prompt_tokens = s->prompt_len;
+    ev.cached_tokens = s->cached_tokens;
+    ev.first = !s->first_emitted;
+    s->first_emitted = true;
+    Finish fin = Finish::kNone;
+    for (int32_t j = 0; j < n_tok; ++j) {
+      const int32_t tok = out.tokens[j];
+      s->tokens.push_back(tok);
+      ++s->generated;
+      ev.tokens.push_back(tok);
+      ev.logprobs.push_back(out.logprobs[j]);
+      if (s->req.sampling.logprobs > 0 && j == 0) {
+        std::vector<std::pair<int32_t, float>> top;
+        for (int32_t q = 0; q < std::min<int32_t>(s->req.sampling.logprobs, wire::kMaxTopLogprobs); ++q)
+          top.emplace_back(out.top_ids[q], out.top_logprobs[q]);
+        ev.top_logprobs.push_back(std::move(top));
+      }
+      const bool eos = !s->req.ignore_eos &&
+                       std::find(s->req.eos_ids.begin(), s->req.eos_ids.end(), tok) != s->req.eos_ids.end();
+      if (eos) {
+        fin = Finish::kStop;
+        break;
+      }
+      if (s->generated >= s->req.max_tokens || s->tokens.size() >= cfg_.max_model_len) {
+        fin = Finish::kLength;
+        break;
+      }
+    }
+    if (cfg_.spec_method == "mtp") {
+      s->drafts.assign(out.next_drafts, out.next_drafts + std::max(0, std::min<int32_t>(out.num_drafts, wire::kMaxSpecTokens)));
+    }
+    ev.completion_tokens = s->generated;
+    ev.finish = fin;
+    events.push_back(std::move(ev));
+    if (fin != Finish::kNone) done.push_back(s->slot);
+  }
+  for (int32_t slot : done) {
+    retire(running_.at(slot).get());
+    running_.erase(slot);
+  }
+  return events;
+}
+
+void Engine::retire(Seq* s) {
+  s->promote.clear();  // returns unused checkpoint slots
+  s->prefix.release();
+  s->own.release();
+  s->held.release();
+  if (s->slot >= 0) free_slots_.push_back(s->slot);
+  s->slot = -1;
+}
+
+void Engine::finish(Seq* s, Finish why, std::vector<TokenEvent>* out) {
+  TokenEvent ev;
+  ev.request_id = s->req.id;
+  ev.finish = why;
+  ev.completion_tokens = s->generated;
+  out->push_back(ev);
+}
+
+}  // namespace engine
+}  // namespace zs

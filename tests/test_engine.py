@@ -1,0 +1,227 @@
+"""Scheduler invariants of the C++ serving engine, driven through a fake backend.
+
+The fake model's next token is a hash of the sequence's full token history, which the
+backend reconstructs from the plans alone (positions, restores from checkpoint slots,
+checkpoint snapshots, speculative rollback).  Any mistake in chunking, prefix reuse or
+checkpoint bookkeeping therefore changes the generated tokens."""
+
+import pytest
+
+from zstep_b200 import _master as m
+
+V = 1000
+
+
+def f(history):
+    h = 0
+    for i, t in enumerate(history):
+        h = (h * 1000003 + (i + 1) * (t + 7)) % 2147483647
+    return h % V
+
+
+def expected(prompt, max_tokens, eos=(), fn=None):
+    fn = fn or f
+    hist, out = list(prompt), []
+    while len(out) < max_tokens:
+        t = fn(hist)
+        out.append(t)
+        hist.append(t)
+        if t in eos:
+            break
+    return out
+
+
+class FakeBackend:
+    def __init__(self, fn=None):
+        self.hist = {}
+        self.ckpt = {}
+        self.plans = []
+        self.f = fn or f
+
+    def __call__(self, p):
+        self.plans.append(p)
+        outs = []
+        qs = p["query_start"]
+        ck = dict(zip(p["ckpt_row"], p["ckpt_slot"]))
+        for i, slot in enumerate(p["seq_slot"]):
+            r0, r1 = qs[i], qs[i + 1]
+            if p["restore_slot"][i] >= 0:
+                self.hist[slot] = list(self.ckpt[p["restore_slot"][i]])
+            if p["positions"][r0] == 0:
+                self.hist[slot] = []
+            h = self.hist[slot]
+            assert len(h) == p["positions"][r0], "plan position does not continue the slot's history"
+            snaps = []
+            for r in range(r0, r1):
+                h.append(p["token_ids"][r])
+                if r in ck:
+                    self.ckpt[ck[r]] = list(h)
+                snaps.append(list(h))
+            if p["sample_row"][i] < 0:
+                outs.append({"tokens": []})
+                continue
+            if p["spec_width"][i] > 0:
+                drafts = p["token_ids"][r0 + 1:r1]
+                targets = [self.f(s) for s in snaps]
+                acc = []
+                for j, d in enumerate(drafts):
+                    if targets[j] != d:
+                        acc.append(targets[j])
+                        break
+                    acc.append(d)
+                else:
+                    acc.append(targets[len(drafts)])
+                self.hist[slot] = snaps[len(acc) - 1]
+                outs.append({"tokens": acc})
+            else:
+                outs.append({"tokens": [self.f(h)]})
+        return outs
+
+
+def make(**kw):
+    cfg = m.EngineConfig()
+    cfg.max_seqs = kw.get("max_seqs", 8)
+    cfg.max_step_tokens = kw.get("max_step_tokens", 64)
+    cfg.max_prefill_chunk = kw.get("chunk", 32)
+    cfg.page_size = 4
+    cfg.num_pages = kw.get("num_pages", 256)
+    cfg.max_model_len = 512
+    cfg.prefix_caching = kw.get("apc", False)
+    cfg.pages_per_node = kw.get("ppn", 2)
+    cfg.recurrent_state = kw.get("recurrent", False)
+    cfg.num_ckpt_slots = kw.get("ckpt", 0)
+    cfg.prefill_policy = kw.get("policy", "fifo")
+    cfg.spec_method = kw.get("spec", "none")
+    cfg.num_spec_tokens = kw.get("k", 0)
+    cfg.ngram_n = 2
+    be = FakeBackend(kw.get("fn"))
+    return m.Engine(cfg, be), be
+
+
+def run(eng, limit=10000):
+    out = {}
+    done = set()
+    for _ in range(limit):
+        if not eng.has_work():
+            break
+        for ev in eng.step():
+            out.setdefault(ev["request_id"], []).extend(ev["tokens"])
+            if ev["finish"]:
+                done.add(ev["request_id"])
+    return out, done
+
+
+def test_basic_generation_and_conservation():
+    eng, be = make()
+    reqs = {i: ([(i * 37 + j) % V for j in range(5 + 9 * i)], 3 + i) for i in range(6)}
+    for rid, (p, mt) in reqs.items():
+        assert eng.submit(rid, p, mt)
+    out, done = run(eng)
+    assert done == set(reqs)
+    for rid, (p, mt) in reqs.items():
+        assert out[rid] == expected(p, mt)
+    assert eng.free_pages() == 255 and eng.free_slots() == 8
+
+
+def test_chunked_prefill_and_decode_buckets():
+    eng, be = make(chunk=8, max_step_tokens=20)
+    p = list(range(50))
+    eng.submit(1, p, 4)
+    out, _ = run(eng)
+    assert out[1] == expected(p, 4)
+    prefill = [pl for pl in be.plans if not (pl["flags"] & 1)]
+    assert all(len(pl["token_ids"]) <= 20 for pl in be.plans)
+    assert len(prefill) >= 7  # 50 tokens in chunks of <= 8
+    decode = [pl for pl in be.plans if pl["flags"] & 1]
+    assert decode and all(pl["bucket"] >= len(pl["seq_slot"]) for pl in decode)
+
+
+def test_eos_and_ignore_eos():
+    p = [1, 2, 3]
+    ref = expected(p, 20)
+    eos = ref[2]
+    eng, _ = make()
+    eng.submit(1, p, 20, False, [eos])
+    eng.submit(2, p, 20, True, [eos])
+    out, _ = run(eng)
+    assert out[1] == ref[:ref.index(eos) + 1]
+    assert out[2] == ref
+
+
+def test_cancel_releases_everything():
+    eng, _ = make()
+    for i in range(4):
+        eng.submit(i, list(range(10 + i)), 50)
+    eng.step()
+    eng.step()
+    assert eng.cancel(1) and eng.cancel(3)
+    assert not eng.cancel(99)
+    run(eng)
+    assert eng.free_pages() == 255 and eng.free_slots() == 8
+
+
+def test_prefix_cache_reuse_with_recurrent_checkpoints():
+    eng, be = make(apc=True, ppn=2, recurrent=True, ckpt=16, chunk=16)
+    shared = [(7 * j + 3) % V for j in range(40)]
+    a = shared + [5, 6, 7]
+    b = shared + [9, 9]
+    eng.submit(1, a, 5)
+    out, _ = run(eng)
+    assert eng.cached_prefix_nodes() == 5  # 40 tokens / (2 pages x 4 tokens)
+    eng.submit(2, b, 5)
+    out2, _ = run(eng)
+    assert out[1] == expected(a, 5)
+    assert out2[2] == expected(b, 5)
+    st = eng.stats()
+    assert st.prefix_hit_tokens >= 40
+    # The second request restored a checkpoint instead of recomputing the prefix.
+    restores = [pl for pl in be.plans if any(r >= 0 for r in pl["restore_slot"])]
+    assert restores
+
+
+def test_prefix_cache_evicts_under_pressure():
+    eng, _ = make(apc=True, ppn=1, num_pages=40, recurrent=True, ckpt=64, chunk=64)
+    for i in range(12):
+        p = [(i * 101 + j) % V for j in range(24)]
+        eng.submit(i, p, 2)
+        out, _ = run(eng)
+        assert out[i] == expected(p, 2)
+    assert eng.stats().prefix_evictions > 0
+
+
+def test_ngram_speculative_matches_plain_decoding():
+    def periodic(h):  # mostly repeats with period 3, deviating every 7th position
+        return h[-3] if len(h) % 7 else (h[-1] + 1) % V
+
+    p = [3, 4, 5, 3, 4, 5, 3, 4, 5, 3, 4]
+    eng, be = make(spec="ngram", k=3, fn=periodic)
+    eng.submit(1, p, 30, True)
+    out, _ = run(eng)
+    assert out[1] == expected(p, 30, fn=periodic)
+    assert any(pl["flags"] & 32 for pl in be.plans)  # verify steps happened
+    st = eng.stats()
+    assert 0 < st.spec_accepted < st.spec_drafts  # some drafts accepted, some rejected
+    assert st.decode_tokens < 30  # fewer steps than tokens
+
+
+def test_srpt_admits_short_prompts_first():
+    eng, be = make(max_seqs=1, policy="srpt")
+    eng.submit(1, list(range(60)), 1)
+    eng.submit(2, list(range(5)), 1)
+    eng.submit(3, list(range(20)), 1)
+    order = []
+    for _ in range(100):
+        if not eng.has_work():
+            break
+        for ev in eng.step():
+            if ev["finish"]:
+                order.append(ev["request_id"])
+    assert order == [2, 3, 1]
+
+
+def test_overload_rejects_submit():
+    cfg = m.EngineConfig()
+    cfg.max_waiting = 2
+    eng = m.Engine(cfg, FakeBackend())
+    assert eng.submit(1, [1], 1) and eng.submit(2, [1], 1)
+    assert not eng.submit(3, [1], 1)

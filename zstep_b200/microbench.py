@@ -43,22 +43,50 @@ def _flush(n_bytes=256 << 20):
     buf.max()
 
 
-def time_fn(fn, iters=20, warmup=3, flush=False) -> float:
-    """Median milliseconds per call."""
+def time_fn(fn, iters=20, warmup=3, flush=False, reps=8) -> float:
+    """Median device milliseconds per call.  `fn` is captured `reps` times into one CUDA
+    graph so host launch overhead never sits between the timing events; with `flush`
+    an L2-evicting read is captured before every call and its own time subtracted."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    ts = []
-    for _ in range(iters):
-        if flush:
-            _flush()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        fn()
-        b.record()
-        b.synchronize()
-        ts.append(a.elapsed_time(b))
-    return statistics.median(ts)
+
+    def capture(body):
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            body()  # allocate any lazily created buffers outside the capture
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=s):
+                body()
+        torch.cuda.current_stream().wait_stream(s)
+        return g
+
+    def run_body(with_fn):
+        def body():
+            for _ in range(reps):
+                if flush:
+                    _flush()
+                if with_fn:
+                    fn()
+        return body
+
+    def med(g):
+        ts = []
+        for _ in range(iters):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
+    g = capture(run_body(True))
+    total = med(g)
+    base = med(capture(run_body(False))) if flush else 0.0
+    return (total - base) / reps
 
 
 def build_runner(layers: int, batch: int, ctx: int, experts: int = 256, vocab: int = 248320):
@@ -135,8 +163,25 @@ def cmd_step(a):
         return
     r.capture_decode_graph(r.bucket_for(a.batch))
     g = r.graphs[r.bucket_for(a.batch)]
-    ms = time_fn(g.replay, iters=a.iters)
-    print(json.dumps({"decode_step_ms": ms, "tok_s": a.batch / ms * 1000}))
+    for _ in range(a.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(a.iters):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        g.replay()
+        e.record()
+        e.synchronize()
+        ts.append(s.elapsed_time(e))
+    ms = statistics.median(ts)
+    if a.profile_replay:
+        # One replay bracketed for `ncu --profile-from-start off`.
+        torch.cuda.cudart().cudaProfilerStart()
+        g.replay()
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+    print(json.dumps({"decode_step_ms": round(ms, 4), "tok_s": round(a.batch / ms * 1000, 1)}))
 
 
 def _gemm_case(m, n, k, groups=1):
@@ -243,6 +288,7 @@ def main():
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--ctx", type=int, default=1280)
     ap.add_argument("--eager", type=int, default=0)
+    ap.add_argument("--profile-replay", type=int, default=0)
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--m", type=int, default=256)

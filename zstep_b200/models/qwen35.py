@@ -308,7 +308,7 @@ class Qwen35Runner:
         tokens (decode), 128 for prefill-sized batches."""
         return 32 if rows * self.top_k <= 32 * self.cfg.num_experts else 128
 
-    def _k_splits(self, w: PackedLinear, rows: int) -> int:
+    def _k_splits(self, w: PackedLinear, rows: int, cap: int | None = None) -> int:
         """Split K until the dense GEMM has about one wave of work items (decode only)."""
         if rows > self.max_seqs:
             return 1
@@ -316,7 +316,8 @@ class Qwen35Runner:
         items = ((rows + bn - 1) // bn) * (w.n_pad // 128)
         k_tiles = w.k // 128
         s = 1
-        while items * s * 2 <= 160 and s * 2 <= min(self.max_ksplit, k_tiles):
+        limit = min(self.max_ksplit, k_tiles, cap or self.max_ksplit)
+        while items * s * 2 <= 160 and s * 2 <= limit:
             s *= 2
         return s
 
@@ -391,7 +392,7 @@ class Qwen35Runner:
         cfg, C, b = self.cfg, self.C, self.buf
         E = cfg.num_experts
         nr = L["router"].n_pad
-        s = self._k_splits(L["router"], rows)
+        s = self._k_splits(L["router"], rows, cap=4)  # the router kernel re-reads every split
         self._gemm(L["router"], b["xq"], b["xsf"], rows, b["logits"], nr, EPI_F32, k_splits=s)
         C.moe_route(b["logits"], rows, E, self.top_k, cfg.norm_topk_prob, 0, None, 1, 1, 1.0, E,
                     self.e_begin, self.e_begin + self.e_local, True, b["topk_ids"], b["topk_w"], b["gcount"],
@@ -470,6 +471,33 @@ class Qwen35Runner:
     def staged_bytes(self) -> int:
         """Host->device bytes moved by the last stage() call."""
         return 4 * 4 * getattr(self, "_staged_rows", 0)
+
+    def copy_recurrent_state(self, src_slot: int, dst_slot: int) -> None:
+        """Restore a checkpoint: GDN state and both conv-window buffers of every layer."""
+        self.ssm_state[:, dst_slot].copy_(self.ssm_state[:, src_slot])
+        self.conv_state[:, dst_slot].copy_(self.conv_state[:, src_slot])
+
+    def checkpoint_args(self, ckpt_rows, ckpt_slots, query_start):
+        """Per-sequence checkpoint tables for the GDN prefill kernel: for sequence s,
+        entries [s*max_ck, (s+1)*max_ck) list (global row, checkpoint slot) pairs in row
+        order, -1 padded."""
+        rows = [int(x) for x in ckpt_rows]
+        slots = [int(x) for x in ckpt_slots]
+        qs = [int(x) for x in query_start]
+        n = len(qs) - 1
+        per = [[] for _ in range(n)]
+        for r, s in sorted(zip(rows, slots)):
+            for i in range(n):
+                if qs[i] <= r < qs[i + 1]:
+                    per[i].append((r, s))
+                    break
+        max_ck = max(1, max(len(p) for p in per))
+        rt = torch.full((n, max_ck), -1, dtype=torch.int32)
+        st = torch.zeros((n, max_ck), dtype=torch.int32)
+        for i, p in enumerate(per):
+            for j, (r, s) in enumerate(p):
+                rt[i, j], st[i, j] = r, s
+        return rt.to(self.dev), st.to(self.dev), max_ck
 
     def set_pages(self, slot: int, pages: list[int]) -> None:
         self.page_table[slot, :len(pages)] = torch.as_tensor(pages, dtype=torch.int32, device=self.dev)

@@ -89,10 +89,19 @@ def quantize_to_atoms(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 
 def tile_weight(q: torch.Tensor) -> torch.Tensor:
     """Row-major e4m3 weight [rows, k] (rows % 128 == 0, k % 128 == 0) -> the GEMM's
-    pre-tiled layout [rows/128][k/128][128][128]: every 128x128-byte block of one
-    (feature tile, K tile) becomes one contiguous 16 KiB chunk (one TMA box)."""
+    pre-tiled, pre-swizzled layout: every 128x128-byte block of one (feature tile,
+    K tile) becomes one contiguous 16 KiB chunk ([rows/128][k/128][128][128]) whose
+    16-byte pieces are already in the 128-byte-swizzle order (piece c of row r stored
+    at piece c ^ (r % 8)).  A plain bulk copy of the chunk to a 1024-byte aligned
+    shared-memory buffer then yields exactly the image a swizzled TMA load would."""
     rows, k = q.shape
-    return q.view(rows // 128, 128, k // 128, 128).permute(0, 2, 1, 3).contiguous().view(rows, k)
+    t = q.view(rows // 128, 128, k // 128, 128).permute(0, 2, 1, 3)  # [mt, kt, 128 r, 128 B]
+    t = t.reshape(rows // 128, k // 128, 16, 8, 8, 16)              # [.., row grp, r%8, piece, 16 B]
+    j = torch.arange(8, device=q.device)
+    src_piece = (j[None, :] ^ j[:, None])                           # [r%8, dst piece] -> src piece
+    idx = src_piece.view(1, 1, 1, 8, 8, 1).expand(t.shape)
+    t = torch.gather(t, 4, idx)
+    return t.contiguous().view(rows, k)
 
 
 def fake_quant(x: torch.Tensor) -> torch.Tensor:

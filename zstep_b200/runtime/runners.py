@@ -1,0 +1,190 @@
+"""Step runners driven by the worker loop.
+
+A runner turns one decoded step plan (numpy arrays, see runtime/wire.py) into one
+SeqStepOutput record per planned sequence.  Two implementations:
+
+* ``CpuReferenceRunner`` -- the fp32 PyTorch reference model, tensor-parallel over
+  gloo.  It is the CPU plumbing model: the whole control plane (C++ master, shared
+  memory, eventfds, scheduling, prefix caching with recurrent checkpoints, speculative
+  verify) runs end to end without a GPU.
+* ``GpuRunner`` -- the B200 runner (models/qwen35.py): decode-only plans replay the
+  bucket's CUDA graph, other plans run the varlen prefill path; recurrent-state
+  checkpoints are snapshotted by the GDN prefill kernel and restored with device copies.
+
+Both implement greedy sampling (global argmax, smallest id on ties) and temperature /
+top-k / top-p sampling with a per-sequence seed, identical on every rank.
+
+Reference parity: worker/zstep_worker/models/qwen35_moe.py (launch :1622, finish
+:1908, rollback :1861), sampler.py (sample_tp8_logits :127), spec_decode.py
+(verify_greedy :41, verify_batch :55).
+"""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import wire
+from ..sampling import sample_logits, verify_greedy
+
+
+def _resolve_config(name: str):
+    from ..config import PRESETS, Qwen35Config
+
+    if name in PRESETS:
+        return PRESETS[name]()
+    return Qwen35Config.from_hf(name)
+
+
+def _weights(cfg, name: str, seed: int):
+    from ..models.weights import RandomWeights, SafetensorsWeights
+
+    if os.path.isdir(name):
+        return SafetensorsWeights(cfg, name)
+    return RandomWeights(cfg, seed=seed)
+
+
+def make_runner(args, rank: int, world: int, geo):
+    if world > 1 and not dist.is_initialized():
+        backend = "nccl" if args.device == "cuda" else "gloo"
+        if args.device == "cuda":
+            torch.cuda.set_device(rank % max(1, torch.cuda.device_count()))
+        dist.init_process_group(backend, rank=rank, world_size=world)
+    if args.device == "cpu":
+        return CpuReferenceRunner(args, rank, world, geo)
+    return GpuRunner(args, rank, world, geo)
+
+
+def _outputs(n: int) -> np.ndarray:
+    out = np.zeros(n, dtype=wire.SEQ_OUTPUT_DTYPE)
+    return out
+
+
+class CpuReferenceRunner:
+    """fp32 reference model, one ``SeqState`` per request slot (+ checkpoint slots)."""
+
+    def __init__(self, args, rank: int, world: int, geo):
+        from ..models.qwen35_ref import Qwen35Reference
+
+        torch.set_num_threads(max(1, (os.cpu_count() or 2) // max(1, world)))
+        self.cfg = _resolve_config(args.model)
+        self.rank, self.world = rank, world
+        ar = (lambda x: self._allreduce(x)) if world > 1 else None
+        self.model = Qwen35Reference(self.cfg, _weights(self.cfg, args.model, args.seed), device="cpu",
+                                     quant=False, tp_rank=rank, tp_size=world, allreduce=ar)
+        self.states: dict[int, object] = {}
+        self.ckpt: dict[int, object] = {}
+
+    def _allreduce(self, x: torch.Tensor) -> torch.Tensor:
+        x = x.contiguous()
+        dist.all_reduce(x)
+        return x
+
+    def _full_logits(self, shard: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return shard
+        parts = [torch.empty_like(shard) for _ in range(self.world)]
+        dist.all_gather(parts, shard.contiguous())
+        return torch.cat(parts)
+
+    def execute(self, plan: dict) -> np.ndarray:
+        n = plan["num_seqs"]
+        out = _outputs(n)
+        qs, toks, pos = plan["query_start"], plan["token_ids"], plan["positions"]
+        ckpt_at = {int(r): int(s) for r, s in zip(plan["ckpt_row"], plan["ckpt_slot"])}
+        for i in range(n):
+            slot = int(plan["seq_slot"][i])
+            r0, r1 = int(qs[i]), int(qs[i + 1])
+            if int(plan["restore_slot"][i]) >= 0:
+                self.states[slot] = self.model.clone_state(self.ckpt[int(plan["restore_slot"][i])])
+            if r1 > r0 and int(pos[r0]) == 0:
+                self.states[slot] = self.model.new_state()
+            st = self.states[slot]
+            width = int(plan["spec_width"][i])
+            row_logits, row_states = [], []
+            for r in range(r0, r1):
+                assert st.pos == int(pos[r]), f"slot {slot}: state at {st.pos}, plan position {int(pos[r])}"
+                lg = self.model.step(st, int(toks[r]))
+                if r in ckpt_at:
+                    self.ckpt[ckpt_at[r]] = self.model.clone_state(st)
+                if width > 0:
+                    row_logits.append(self._full_logits(lg))
+                    row_states.append(self.model.clone_state(st))
+                elif r == r1 - 1 and int(plan["sample_row"][i]) >= 0:
+                    row_logits.append(self._full_logits(lg))
+            out[i]["req_slot"] = slot
+            if int(plan["sample_row"][i]) < 0:
+                continue
+            sp = plan["sampling"][i]
+            if width > 0:
+                drafts = [int(t) for t in toks[r0 + 1:r1]]
+                targets = [sample_logits(l, sp) for l in row_logits]
+                acc = verify_greedy(drafts, targets)  # accepted drafts + bonus token
+                # Roll the state back to the last accepted row.
+                self.states[slot] = row_states[len(acc) - 1]
+                tokens = acc
+            else:
+                tokens = [sample_logits(row_logits[-1], sp)]
+            out[i]["num_tokens"] = len(tokens)
+            out[i]["tokens"][:len(tokens)] = tokens
+        return out
+
+    def close(self) -> None:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+class GpuRunner:
+    """B200 runner: the kernels of models/qwen35.py driven by step plans."""
+
+    def __init__(self, args, rank: int, world: int, geo):
+        from ..models.qwen35 import Qwen35Runner
+        from ..parallel import make_collectives
+
+        self.cfg = _resolve_config(args.model)
+        self.dev = torch.device("cuda", torch.cuda.current_device())
+        coll = make_collectives(self.dev) if world > 1 else None
+        self.r = Qwen35Runner(self.cfg, device=self.dev, weights=_weights(self.cfg, args.model, args.seed),
+                              max_seqs=geo.max_seqs, max_prefill_tokens=geo.max_step_tokens,
+                              num_pages=args.num_pages, page_size=geo.page_size, max_model_len=args.max_model_len,
+                              num_ckpt_slots=args.num_ckpt_slots, tp_rank=rank, tp_size=world, collectives=coll,
+                              seed=args.seed)
+        self.rank = rank
+
+    def execute(self, plan: dict) -> np.ndarray:
+        r = self.r
+        n = plan["num_seqs"]
+        out = _outputs(n)
+        for k, slot in enumerate(plan["dirty_rows"]):
+            r.page_table[int(slot)].copy_(torch.from_numpy(plan["dirty_pages"][k][: r.max_pages]).to(r.dev))
+        for i in range(n):
+            src = int(plan["restore_slot"][i])
+            if src >= 0:
+                r.copy_recurrent_state(src, int(plan["seq_slot"][i]))
+        rows = plan["num_rows"]
+        greedy = not (plan["flags"] & wire.FLAG_SAMPLING)
+        decode_only = bool(plan["flags"] & wire.FLAG_DECODE_ONLY)
+        if decode_only and greedy:
+            r.stage(plan["token_ids"], plan["positions"], plan["row_slot"])
+            ids = r.decode_step(rows).cpu().numpy()
+        else:
+            seq_start = plan["query_start"].tolist()
+            r.stage(plan["token_ids"], plan["positions"], plan["row_slot"], seq_start=seq_start)
+            ck = None
+            if len(plan["ckpt_row"]):
+                ck = r.checkpoint_args(plan["ckpt_row"], plan["ckpt_slot"], plan["query_start"])
+            ids = r.prefill_forward(rows, n, ckpt=ck).cpu().numpy()
+        for i in range(n):
+            out[i]["req_slot"] = int(plan["seq_slot"][i])
+            if int(plan["sample_row"][i]) >= 0:
+                out[i]["num_tokens"] = 1
+                out[i]["tokens"][0] = int(ids[i])
+        return out
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        if dist.is_initialized():
+            dist.destroy_process_group()
