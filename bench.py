@@ -111,9 +111,10 @@ def main():
     if args.impl == "reference":
         if rank == 0:
             reference_unavailable(
-                "reference zstep cannot run on B200: its CUDA extensions are built only for compute_120 "
-                "(shm_allreduce.py:98, qwen35_ops.py:75), its master needs a Rust toolchain (absent), and "
-                "`pip install /root/reference` has no build backend at the repository root")
+                "reference zstep cannot run on B200: its worker (installed into baseline/_ref with --no-deps) "
+                "refuses any device but sm_120 (zstep_worker/runtime_loop.py:138) and builds its CUDA "
+                "extensions for compute_120 only (kernels_sm120/qwen35_ops.py:75); its master and bench CLI "
+                "are Rust and no Rust toolchain is installed")
         return
 
     import torch

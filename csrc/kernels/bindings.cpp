@@ -309,9 +309,102 @@ void moe_route(const Tensor& logits, int64_t rows, int64_t num_experts, int64_t 
   rc(zs_moe_route(&a, stream()), "zs_moe_route");
 }
 
+void fused_allreduce_norm(int64_t rank, int64_t world, const Tensor& delta, int64_t n_terms, int64_t row_stride,
+                          int64_t term_stride, const std::vector<int64_t>& part, const std::vector<int64_t>& out,
+                          const std::vector<int64_t>& flags, const Tensor& epoch, const Tensor& grid_counter,
+                          const Tensor& residual, const Tensor& weight, double w_offset, double eps, int64_t rows,
+                          const OptT& normed, const OptT& q, const OptT& sf, const OptT& err) {
+  TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)part.size() == world && (int64_t)out.size() == world &&
+                  (int64_t)flags.size() == world,
+              "bad world / pointer lists");
+  check_cuda(delta, "delta");
+  check_cuda(residual, "residual");
+  FusedArArgs a{};
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.delta = ptr(delta);
+  a.n_terms = (int)n_terms;
+  a.row_stride = row_stride;
+  a.term_stride = term_stride;
+  a.delta_f32 = delta.scalar_type() == at::kFloat ? 1 : 0;
+  for (int r = 0; r < world; ++r) {
+    a.part[r] = reinterpret_cast<void*>(part[r]);
+    a.out[r] = reinterpret_cast<void*>(out[r]);
+    a.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
+  }
+  a.epoch = ptr<uint32_t>(epoch);
+  a.grid_counter = ptr<uint32_t>(grid_counter);
+  a.residual = ptr(residual);
+  a.weight = ptr(weight);
+  a.w_offset = (float)w_offset;
+  a.eps = (float)eps;
+  a.rows = (int)rows;
+  a.hidden = (int)residual.size(-1);
+  a.normed = optptr(normed);
+  a.q = optptr<uint8_t>(q);
+  a.sf = optptr<uint8_t>(sf);
+  a.err = optptr<int>(err);
+  rc(zs_fused_allreduce_norm(&a, stream()), "zs_fused_allreduce_norm");
+}
+
+void allreduce_argmax(int64_t rank, int64_t world, int64_t rows, const std::vector<int64_t>& keys,
+                      const std::vector<int64_t>& flags, const Tensor& epoch, const Tensor& local_keys,
+                      int64_t id_offset, const OptT& out_ids, const OptT& out_vals, const OptT& err) {
+  TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)keys.size() == world && (int64_t)flags.size() == world,
+              "bad world / pointer lists");
+  ArgmaxArArgs a{};
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.rows = (int)rows;
+  for (int r = 0; r < world; ++r) {
+    a.keys[r] = reinterpret_cast<const void*>(keys[r]);
+    a.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
+  }
+  a.epoch = ptr<uint32_t>(epoch);
+  a.out_ids = optptr<int>(out_ids);
+  a.out_vals = optptr<float>(out_vals);
+  a.err = optptr<int>(err);
+  rc(zs_allreduce_argmax(&a, ptr<const unsigned long long>(local_keys), (int)id_offset, stream()),
+     "zs_allreduce_argmax");
+}
+
+int64_t symm_alloc(int64_t bytes) {
+  void* p = nullptr;
+  rc(zs_symm_alloc((size_t)bytes, &p), "zs_symm_alloc");
+  return reinterpret_cast<int64_t>(p);
+}
+
+py::bytes ipc_handle(int64_t p) {
+  char h[64];
+  rc(zs_ipc_handle(reinterpret_cast<void*>(p), h), "zs_ipc_handle");
+  return py::bytes(h, 64);
+}
+
+int64_t ipc_open(py::bytes handle) {
+  std::string s = handle;
+  TORCH_CHECK(s.size() == 64, "IPC handle must be 64 bytes");
+  void* p = nullptr;
+  rc(zs_ipc_open(s.data(), &p), "zs_ipc_open");
+  return reinterpret_cast<int64_t>(p);
+}
+
+// Non-owning tensor view of device memory at `p` (lifetime managed by the caller).
+Tensor tensor_from_ptr(int64_t p, std::vector<int64_t> sizes, at::ScalarType dtype, int64_t device) {
+  auto opts = at::TensorOptions().dtype(dtype).device(at::kCUDA, device);
+  return at::from_blob(reinterpret_cast<void*>(p), sizes, opts);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("fused_allreduce_norm", &fused_allreduce_norm);
+  m.def("allreduce_argmax", &allreduce_argmax);
+  m.def("symm_alloc", &symm_alloc);
+  m.def("symm_free", [](int64_t p) { rc(zs_symm_free(reinterpret_cast<void*>(p)), "zs_symm_free"); });
+  m.def("ipc_handle", &ipc_handle);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", [](int64_t p) { rc(zs_ipc_close(reinterpret_cast<void*>(p)), "zs_ipc_close"); });
+  m.def("tensor_from_ptr", &tensor_from_ptr);
   m.doc() = "zstep_b200 sm_100a kernels";
   m.def("gemm_mxf8", &gemm_mxf8);
   m.def("quant_mxf8", &quant_mxf8);

@@ -201,6 +201,56 @@ typedef struct MoeRouteArgs {
 
 int zs_moe_route(const MoeRouteArgs* args, cudaStream_t stream);
 
+// ----------------------------------------------------------------------------------
+// Fused tensor-parallel collectives over NVLink peer memory (symmetric buffers)
+// ----------------------------------------------------------------------------------
+#define FAR_CTAS 128  // persistent grid of the fused all-reduce (must be co-resident)
+
+typedef struct FusedArArgs {
+  int rank, world;
+  const void* delta;         // local partial terms: delta[row*row_stride + t*term_stride + col]
+  int n_terms;
+  long long row_stride, term_stride;
+  int delta_f32;             // terms are f32 (split-K partials) or bf16 (MoE pair rows)
+  void* part[8];             // symmetric bf16 [rows, hidden] per rank (local sum)
+  void* out[8];              // symmetric bf16 [rows, hidden] per rank (reduced owned rows)
+  uint32_t* flags[8];        // symmetric u32 [32] per rank (barrier slots)
+  uint32_t* epoch;           // local device counter (same sequence on every rank)
+  uint32_t* grid_counter;    // local device counter for the in-kernel grid barrier
+  const int* abort_word;     // optional device-visible abort flag (nonzero: give up waits)
+  void* residual;            // bf16 [rows, hidden], replicated residual stream (in/out)
+  const void* weight;        // RMSNorm weight
+  float w_offset, eps;
+  int rows, hidden;
+  void* normed;              // optional bf16 output
+  uint8_t* q;                // optional MXFP8 output + scale atoms
+  uint8_t* sf;
+  int* err;
+} FusedArArgs;
+
+int zs_fused_allreduce_norm(const FusedArArgs* args, cudaStream_t stream);
+
+typedef struct ArgmaxArArgs {
+  int rank, world, rows;
+  const void* keys[8];       // symmetric u64 [rows] per rank (global ids)
+  uint32_t* flags[8];
+  uint32_t* epoch;           // its own counter (not shared with the all-reduce)
+  int* out_ids;
+  float* out_vals;
+  int* err;
+} ArgmaxArArgs;
+
+// local_keys: this rank's per-row best key over its vocab shard (local ids); ids are
+// rebased by id_offset and max-reduced across ranks.
+int zs_allreduce_argmax(const ArgmaxArArgs* args, const unsigned long long* local_keys, int id_offset,
+                        cudaStream_t stream);
+
+int zs_symm_alloc(size_t bytes, void** ptr);
+int zs_symm_free(void* ptr);
+int zs_ipc_handle(void* ptr, void* handle_out);
+int zs_ipc_open(const void* handle, void** ptr);
+int zs_ipc_close(void* ptr);
+
 #ifdef __cplusplus
 }
 #endif

@@ -235,6 +235,8 @@ class Qwen35Runner:
         R = max(self.max_seqs, self.max_prefill_tokens)
         Rp = _pad128(R)
         self.R = R
+        if self.tp > 1 and hasattr(self.coll, "reserve"):
+            self.coll.reserve(R, H)  # collective: symmetric buffers for the fused all-reduce
         i32 = dict(dtype=torch.int32, device=dev)
         self.gdn_w = 2 * self.hk * 128 + 2 * self.hv * 128 + 2 * self.hv
         self.qkv_w = (2 * self.hq + 2 * self.hkv) * cfg.head_dim
@@ -545,4 +547,7 @@ class Qwen35Runner:
         return self.buf["out_ids"][:n]
 
     def check_error(self) -> int:
-        return int(self.buf["err"].item())
+        err = int(self.buf["err"].item())
+        if not err and self.coll is not None and hasattr(self.coll, "check_error"):
+            err = self.coll.check_error()
+        return err
