@@ -20,6 +20,9 @@
 //
 // Reference parity: worker/zstep_worker/kernels_sm120/qwen35_ops.py:187-560 (attention
 // prologue, split-K(16) paged GQA decode + gated reduce, varlen gated prefill).
+#include <cstdio>
+#include <mutex>
+
 #include "sm100_common.cuh"
 #include "zs_kernels.h"
 
@@ -350,4 +353,55 @@ extern "C" int zs_attn_decode(const AttnArgs* args, cudaStream_t stream) {
 // hold position + 1 for every row); the caller runs the prologue for all rows first.
 extern "C" int zs_attn_prefill(const AttnArgs* args, cudaStream_t stream) {
   return zs_attn_decode(args, stream);
+}
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free decode entry point (no counterpart in the reference).
+//
+// zs_attn_decode_noalloc computes the same gated paged attention as zs_attn_decode, but the
+// caller passes no split-KV scratch buffer: the per-split partial records live in one fixed
+// device array that is part of this library's image.  It serves callers that cannot allocate
+// device memory at the point of the call: a host runtime whose device allocator belongs to
+// another framework (so a private cudaMalloc would fragment or exceed its budget), a plugin
+// that must not change the process's memory footprint after start-up, or plain C code that
+// holds only raw device pointers and no allocator at all.
+//
+// Limit: the array holds ZS_ATTN_NOALLOC_SCRATCH_FLOATS floats (8 MiB).  A call needs
+// rows * num_q_heads * num_splits * 260 floats; above that it returns -3 and launches nothing.
+// Sharing: every call on a device uses the same array, so calls that overlap in time (two
+// streams, or two host threads without ordering between their streams) race on it; issue
+// them on one stream.  Nothing in the array has to start at zero: each record a call reads
+// was written earlier in the same call.
+// Set-up: the first call on each device looks up the array's address with that device
+// current and caches it; make the first call on a device before any stream capture.
+static __device__ __align__(256) float g_attn_noalloc_scratch[ZS_ATTN_NOALLOC_SCRATCH_FLOATS];
+
+namespace {
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[64] = {};
+}  // namespace
+
+extern "C" int zs_attn_decode_noalloc(const AttnArgs* args, cudaStream_t stream) {
+  const AttnArgs& in = *args;
+  const size_t need = (size_t)in.rows * (size_t)in.num_q_heads * (size_t)in.num_splits * zs::attn::PREC;
+  if (in.rows < 0 || in.num_q_heads < 0 || in.num_splits < 0 || need > (size_t)ZS_ATTN_NOALLOC_SCRATCH_FLOATS) {
+    fprintf(stderr, "zs_attn_decode_noalloc: needs %zu scratch floats, the fixed limit is %zu\n", need,
+            (size_t)ZS_ATTN_NOALLOC_SCRATCH_FLOATS);
+    return -3;
+  }
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -4;
+  float* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_attn_noalloc_scratch) != cudaSuccess || p == nullptr) return -4;
+      g_noalloc_ptr[dev] = static_cast<float*>(p);
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  AttnArgs a = in;
+  a.partial = scratch;
+  return zs_attn_decode(&a, stream);
 }

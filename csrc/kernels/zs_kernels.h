@@ -159,6 +159,17 @@ int zs_attn_prologue(const AttnArgs* args, cudaStream_t stream);
 int zs_attn_decode(const AttnArgs* args, cudaStream_t stream);
 int zs_attn_prefill(const AttnArgs* args, cudaStream_t stream);
 
+// Allocation-free variant of zs_attn_decode (no counterpart in the reference): same inputs
+// and outputs, `partial` is ignored and the split-KV records go to a fixed device array of
+// ZS_ATTN_NOALLOC_SCRATCH_FLOATS floats inside this library, for callers that cannot
+// allocate device memory when they call.  Returns 0 on success, -3 when
+// rows * num_q_heads * num_splits * 260 exceeds that size (nothing is launched), -4 when the
+// array's address cannot be looked up, and zs_attn_decode's codes otherwise.  All calls on
+// a device share the array: calls that overlap in time race.  The first call on a device
+// does a one-time address lookup; make it before any stream capture.
+#define ZS_ATTN_NOALLOC_SCRATCH_FLOATS (2 * 1024 * 1024)
+int zs_attn_decode_noalloc(const AttnArgs* args, cudaStream_t stream);
+
 // ----------------------------------------------------------------------------------
 // MoE routing
 // ----------------------------------------------------------------------------------
