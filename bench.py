@@ -127,7 +127,7 @@ def main():
     dev = torch.device("cuda", local_rank)
     coll = None
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
         from zstep_b200.parallel import make_collectives
 
         coll = make_collectives(dev)
@@ -200,12 +200,14 @@ def main():
         graph.replay()
         advance()
     sampler = ClockSampler(range(world) if rank == 0 else [])
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     if rank == 0:
         sampler.start()
         time.sleep(0.3)
+    # The barrier comes after the sampler's start-up so no rank enters the timed region
+    # while another is still on the host (the fused collectives would time that wait).
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     step_ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     start.record()
@@ -275,6 +277,8 @@ def main():
             "init_s": round(init_s, 1),
         }
         print(json.dumps(res), flush=True)
+    del graph
+    runner.graphs.clear()  # release graphs before the process group goes away
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -284,7 +288,7 @@ def count_launches(runner, rows: int) -> int:
     """Number of zstep_b200 kernels one decode step launches (counted on an eager step)."""
     per_call = {"gemm_mxf8": 1, "quant_mxf8": 1, "add_rmsnorm_quant": 1, "embed_rmsnorm_quant": 1,
                 "argmax_reduce": 1, "gdn_decode": 1, "gdn_prefill": 1, "attn_prologue": 1, "attn_decode": 2,
-                "moe_route": 3, "allreduce_add_rmsnorm": 1, "argmax_allreduce": 1}
+                "moe_route": 3, "fused_allreduce_norm": 1, "allreduce_argmax": 2}
     counts = {"n": 0}
     real = runner.C
 
@@ -297,12 +301,18 @@ def count_launches(runner, rows: int) -> int:
                 return fn(*a, **k)
             return wrapped
 
+    coll = runner.coll
+    coll_real = getattr(coll, "C", None)
     runner.C = Proxy()
+    if coll_real is not None:
+        coll.C = Proxy()
     try:
         runner.pad_decode_inputs(0, runner.bucket_for(rows))
         runner.decode_forward(runner.bucket_for(rows))
     finally:
         runner.C = real
+        if coll_real is not None:
+            coll.C = coll_real
     return counts["n"]
 
 

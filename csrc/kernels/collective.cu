@@ -36,7 +36,16 @@ namespace zs {
 namespace coll {
 
 constexpr int THREADS = 256;
-constexpr uint32_t kSpinLimit = 1u << 24;  // ~1 s of polling with backoff
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ uint64_t limit_ns(unsigned int timeout_ms) {
+  return (uint64_t)(timeout_ms ? timeout_ms : 5000u) * 1000000ull;
+}
+
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -59,20 +68,38 @@ __device__ __forceinline__ uint4 ld_cv_v4(const void* p) {
   return v;
 }
 
+// Spin until `*p - value >= 0` (wrap-safe) or `budget_ns` passes; acquire at system scope.
+__device__ __forceinline__ bool wait_flag_sys(const uint32_t* p, uint32_t value, uint64_t budget_ns,
+                                              const int* abort_word) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    if ((int)(ld_acquire_sys(p) - value) >= 0) return true;
+    if (abort_word && *reinterpret_cast<const volatile int*>(abort_word)) return false;
+    if (i > 32) {
+      __nanosleep(64);
+      if ((i & 255) == 0 && globaltimer_ns() - t0 > budget_ns) return false;
+    }
+  }
+}
+
 // Grid-wide barrier for a persistent grid; `target` grows monotonically across calls.
-__device__ __forceinline__ bool grid_sync(uint32_t* counter, uint32_t target, int* err) {
+__device__ __forceinline__ bool grid_sync(uint32_t* counter, uint32_t target, uint64_t budget_ns, int* err) {
   __syncthreads();
   __shared__ int ok;
   if (threadIdx.x == 0) {
     __threadfence_system();
     atomicAdd(counter, 1u);
     ok = 0;
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 0;; ++i) {
       if ((int)(ld_acquire_gpu(counter) - target) >= 0) {
         ok = 1;
         break;
       }
-      if (i > 32) __nanosleep(64);
+      if (i > 32) {
+        __nanosleep(32);
+        if ((i & 255) == 0 && globaltimer_ns() - t0 > budget_ns) break;
+      }
     }
     if (!ok) report_error(err, kErrPeerTimeout);
   }
@@ -90,16 +117,7 @@ __device__ __forceinline__ bool rank_barrier(const FusedArArgs& a, int phase, ui
     ok = 1;
     const uint32_t* mine = a.flags[a.rank] + phase * 8;
     for (int r = 0; r < a.world && ok; ++r) {
-      uint32_t i = 0;
-      for (; i < kSpinLimit; ++i) {
-        if ((int)(ld_acquire_sys(mine + r) - value) >= 0) break;
-        if (a.abort_word && *reinterpret_cast<const volatile int*>(a.abort_word)) {
-          i = kSpinLimit;
-          break;
-        }
-        if (i > 32) __nanosleep(64);
-      }
-      if (i == kSpinLimit) {
+      if (!wait_flag_sys(mine + r, value, limit_ns(a.timeout_ms), a.abort_word)) {
         ok = 0;
         report_error(a.err, kErrPeerTimeout);
       }
@@ -157,7 +175,7 @@ __global__ void __launch_bounds__(THREADS) fused_allreduce_norm_kernel(const Fus
     *reinterpret_cast<uint4*>(my_part + (size_t)row * H + c) = pack8(acc);
   }
   // Two grid barriers per call: the counter reaches 2*G*(E+1) when call E completes.
-  if (!grid_sync(a.grid_counter, (E * 2 + 1) * G, a.err)) return;
+  if (!grid_sync(a.grid_counter, (E * 2 + 1) * G, limit_ns(a.timeout_ms), a.err)) return;
   if (blockIdx.x == 0 && tid == 0) *reinterpret_cast<volatile uint32_t*>(a.epoch) = E + 1;  // everyone has read E
   if (!rank_barrier(a, 0, E + 1)) return;
 
@@ -179,7 +197,7 @@ __global__ void __launch_bounds__(THREADS) fused_allreduce_norm_kernel(const Fus
     }
     *reinterpret_cast<uint4*>(my_out + off) = pack8(acc);
   }
-  if (!grid_sync(a.grid_counter, (E * 2 + 2) * G, a.err)) return;
+  if (!grid_sync(a.grid_counter, (E * 2 + 2) * G, limit_ns(a.timeout_ms), a.err)) return;
   if (!rank_barrier(a, 1, E + 1)) return;
 
   // 5. all-gather rows into the residual stream, then RMSNorm + MXFP8 quantization.
@@ -251,12 +269,7 @@ __global__ void allreduce_argmax_kernel(const ArgmaxArArgs a) {
   if (tid == 0) {
     ok = 1;
     for (int r = 0; r < a.world && ok; ++r) {
-      uint32_t i = 0;
-      for (; i < kSpinLimit; ++i) {
-        if ((int)(ld_acquire_sys(a.flags[a.rank] + 16 + r) - (E + 1)) >= 0) break;
-        if (i > 32) __nanosleep(64);
-      }
-      if (i == kSpinLimit) {
+      if (!wait_flag_sys(a.flags[a.rank] + 16 + r, E + 1, limit_ns(a.timeout_ms), nullptr)) {
         ok = 0;
         report_error(a.err, kErrPeerTimeout);
       }
@@ -279,14 +292,9 @@ __global__ void allreduce_argmax_kernel(const ArgmaxArArgs a) {
   // Second barrier: no rank may overwrite its keys before every peer has read them.
   if (tid < a.world) st_release_sys(a.flags[tid] + 24 + a.rank, E + 1);
   if (tid == 0) {
-    for (int r = 0; r < a.world; ++r) {
-      uint32_t i = 0;
-      for (; i < kSpinLimit; ++i) {
-        if ((int)(ld_acquire_sys(a.flags[a.rank] + 24 + r) - (E + 1)) >= 0) break;
-        if (i > 32) __nanosleep(64);
-      }
-      if (i == kSpinLimit) report_error(a.err, kErrPeerTimeout);
-    }
+    for (int r = 0; r < a.world; ++r)
+      if (!wait_flag_sys(a.flags[a.rank] + 24 + r, E + 1, limit_ns(a.timeout_ms), nullptr))
+        report_error(a.err, kErrPeerTimeout);
     *reinterpret_cast<volatile uint32_t*>(a.epoch) = E + 1;
   }
 }

@@ -237,6 +237,7 @@ typedef struct FusedArArgs {
   uint8_t* q;                // optional MXFP8 output + scale atoms
   uint8_t* sf;
   int* err;
+  unsigned int timeout_ms;   // bound on every cross-rank wait (0: 5000 ms)
 } FusedArArgs;
 
 int zs_fused_allreduce_norm(const FusedArArgs* args, cudaStream_t stream);
@@ -249,6 +250,7 @@ typedef struct ArgmaxArArgs {
   int* out_ids;
   float* out_vals;
   int* err;
+  unsigned int timeout_ms;   // bound on every cross-rank wait (0: 5000 ms)
 } ArgmaxArArgs;
 
 // local_keys: this rank's per-row best key over its vocab shard (local ids); ids are
