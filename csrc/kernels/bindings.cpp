@@ -6,6 +6,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <torch/extension.h>
 
+#include <algorithm>
 #include <optional>
 
 #include "zs_kernels.h"
@@ -41,7 +42,8 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
                const OptT& group_count, const OptT& group_offset, const OptT& chunk_prefix,
                int64_t epi_mode, const Tensor& out, int64_t ldo, const OptT& out_sf,
                const OptT& row_dst, const OptT& row_scale, const OptT& err, int64_t max_items,
-               int64_t block_n, int64_t k_splits, int64_t split_stride, int64_t a_tiled) {
+               int64_t block_n, int64_t k_splits, int64_t split_stride, int64_t a_tiled,
+               int64_t fix_splits, const OptT& ws, const OptT& tile_sem) {
   check_cuda(a, "a");
   check_cuda(sfa, "sfa");
   check_cuda(b, "b");
@@ -80,6 +82,15 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
   p.k_splits = (int)k_splits;
   p.split_stride = split_stride;
   p.a_tiled = (int)a_tiled;
+  p.fix_splits = (int)fix_splits;
+  if (fix_splits > 1) {
+    TORCH_CHECK(ws.has_value() && tile_sem.has_value(), "split-K needs ws and tile_sem");
+    TORCH_CHECK(ws->scalar_type() == at::kFloat && tile_sem->scalar_type() == at::kInt, "ws f32, tile_sem i32");
+    p.ws = ptr<float>(*ws);
+    p.tile_sem = ptr<int>(*tile_sem);
+    const int64_t tile_floats = fix_splits * 128 * (block_n == 32 ? 32 : 128);
+    p.max_tiles = (int)std::min<int64_t>(tile_sem->numel(), ws->numel() / tile_floats);
+  }
   if (k_splits > 1)
     TORCH_CHECK(out.numel() >= (k_splits - 1) * split_stride + m_rows * ldo, "split-K out too small");
   TORCH_CHECK(p.chunk_prefix == nullptr || (p.group_count && p.group_offset), "grouped mode args");
@@ -101,7 +112,7 @@ void quant_mxf8(const Tensor& x, const Tensor& q, const Tensor& sf) {
 void add_rmsnorm_quant(const Tensor& residual, const OptT& delta, int64_t n_terms,
                        int64_t d_row_stride, int64_t d_term_stride, const Tensor& weight,
                        double w_offset, double eps, int64_t rows, const OptT& normed,
-                       const OptT& q, const OptT& sf) {
+                       const OptT& q, const OptT& sf, const OptT& term_index, const OptT& term_scale) {
   check_cuda(residual, "residual");
   check_opt(delta, "delta");
   check_opt(normed, "normed");
@@ -113,7 +124,7 @@ void add_rmsnorm_quant(const Tensor& residual, const OptT& delta, int64_t n_term
   if (delta.has_value())
     TORCH_CHECK(f32 || delta->scalar_type() == at::kBFloat16, "delta must be bf16 or f32");
   rc(zs_add_rmsnorm_quant(ptr(residual), optptr(delta), (int)n_terms, d_row_stride, d_term_stride, f32,
-                          ptr(weight), (float)w_offset, (float)eps, (int)rows, hidden,
+                          optptr<const int>(term_index), optptr<const float>(term_scale), ptr(weight), (float)w_offset, (float)eps, (int)rows, hidden,
                           optptr(normed), optptr<uint8_t>(q), optptr<uint8_t>(sf), stream()),
      "zs_add_rmsnorm_quant");
 }
@@ -267,7 +278,8 @@ void moe_route(const Tensor& logits, int64_t rows, int64_t num_experts, int64_t 
                const Tensor& chunk_prefix, const Tensor& pair_slot, const Tensor& row_dst,
                const Tensor& row_scale, const Tensor& x_q, const Tensor& x_sf,
                const Tensor& xg_q, const Tensor& xg_sf, const OptT& err, int64_t ld_logits,
-               int64_t logit_splits, int64_t logit_split_stride, int64_t chunk_rows) {
+               int64_t logit_splits, int64_t logit_split_stride, int64_t chunk_rows, const OptT& pair_src,
+               const OptT& pair_w) {
   check_cuda(logits, "logits");
   TORCH_CHECK(logits.scalar_type() == at::kFloat, "logits must be f32");
   MoeRouteArgs a{};
@@ -299,6 +311,9 @@ void moe_route(const Tensor& logits, int64_t rows, int64_t num_experts, int64_t 
   a.pair_slot = ptr<int>(pair_slot);
   a.row_dst = ptr<int>(row_dst);
   a.row_scale = ptr<float>(row_scale);
+  a.pair_src = optptr<int>(pair_src);
+  a.pair_w = optptr<float>(pair_w);
+  TORCH_CHECK(a.pair_src == nullptr || a.pair_w != nullptr, "pair_src needs pair_w");
   a.max_grouped_rows = (int)(xg_q.numel() / x_q.size(-1));
   a.x_q = ptr<const uint8_t>(x_q);
   a.x_sf = ptr<const uint8_t>(x_sf);
@@ -313,7 +328,8 @@ void fused_allreduce_norm(int64_t rank, int64_t world, const Tensor& delta, int6
                           int64_t term_stride, const std::vector<int64_t>& part, const std::vector<int64_t>& out,
                           const std::vector<int64_t>& flags, const Tensor& epoch, const Tensor& grid_counter,
                           const Tensor& residual, const Tensor& weight, double w_offset, double eps, int64_t rows,
-                          const OptT& normed, const OptT& q, const OptT& sf, const OptT& err) {
+                          const OptT& normed, const OptT& q, const OptT& sf, const OptT& err,
+                          const OptT& term_index, const OptT& term_scale) {
   TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)part.size() == world && (int64_t)out.size() == world &&
                   (int64_t)flags.size() == world,
               "bad world / pointer lists");
@@ -344,6 +360,8 @@ void fused_allreduce_norm(int64_t rank, int64_t world, const Tensor& delta, int6
   a.q = optptr<uint8_t>(q);
   a.sf = optptr<uint8_t>(sf);
   a.err = optptr<int>(err);
+  a.term_index = optptr<const int>(term_index);
+  a.term_scale = optptr<const float>(term_scale);
   rc(zs_fused_allreduce_norm(&a, stream()), "zs_fused_allreduce_norm");
 }
 
@@ -397,7 +415,11 @@ Tensor tensor_from_ptr(int64_t p, std::vector<int64_t> sizes, at::ScalarType dty
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
-  m.def("fused_allreduce_norm", &fused_allreduce_norm);
+  m.def("fused_allreduce_norm", &fused_allreduce_norm, py::arg("rank"), py::arg("world"), py::arg("delta"),
+        py::arg("n_terms"), py::arg("row_stride"), py::arg("term_stride"), py::arg("part"), py::arg("out"),
+        py::arg("flags"), py::arg("epoch"), py::arg("grid_counter"), py::arg("residual"), py::arg("weight"),
+        py::arg("w_offset"), py::arg("eps"), py::arg("rows"), py::arg("normed"), py::arg("q"), py::arg("sf"),
+        py::arg("err"), py::arg("term_index") = py::none(), py::arg("term_scale") = py::none());
   m.def("allreduce_argmax", &allreduce_argmax);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_free", [](int64_t p) { rc(zs_symm_free(reinterpret_cast<void*>(p)), "zs_symm_free"); });
@@ -406,9 +428,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", [](int64_t p) { rc(zs_ipc_close(reinterpret_cast<void*>(p)), "zs_ipc_close"); });
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.doc() = "zstep_b200 sm_100a kernels";
-  m.def("gemm_mxf8", &gemm_mxf8);
+  m.def("gemm_mxf8", &gemm_mxf8, py::arg("a"), py::arg("sfa"), py::arg("b"), py::arg("sfb"), py::arg("k"),
+        py::arg("n_pad"), py::arg("n_valid"), py::arg("groups"), py::arg("m_rows"), py::arg("group_count"),
+        py::arg("group_offset"), py::arg("chunk_prefix"), py::arg("epi_mode"), py::arg("out"), py::arg("ldo"),
+        py::arg("out_sf"), py::arg("row_dst"), py::arg("row_scale"), py::arg("err"), py::arg("max_items"),
+        py::arg("block_n"), py::arg("k_splits"), py::arg("split_stride"), py::arg("a_tiled"),
+        py::arg("fix_splits") = 1, py::arg("ws") = py::none(), py::arg("tile_sem") = py::none());
   m.def("quant_mxf8", &quant_mxf8);
-  m.def("add_rmsnorm_quant", &add_rmsnorm_quant);
+  m.def("add_rmsnorm_quant", &add_rmsnorm_quant, py::arg("residual"), py::arg("delta"), py::arg("n_terms"),
+        py::arg("d_row_stride"), py::arg("d_term_stride"), py::arg("weight"), py::arg("w_offset"), py::arg("eps"),
+        py::arg("rows"), py::arg("normed"), py::arg("q"), py::arg("sf"), py::arg("term_index") = py::none(),
+        py::arg("term_scale") = py::none());
   m.def("embed_rmsnorm_quant", &embed_rmsnorm_quant);
   m.def("argmax_reduce", &argmax_reduce);
   m.def("gdn_decode", [](const Tensor& proj, int64_t hk, int64_t hv, const Tensor& conv_w,
@@ -434,5 +464,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   });
   m.def("attn_prologue", &attn_prologue);
   m.def("attn_decode", &attn_decode);
-  m.def("moe_route", &moe_route);
+  m.def("moe_route", &moe_route, py::arg("logits"), py::arg("rows"), py::arg("num_experts"), py::arg("top_k"),
+        py::arg("norm_topk"), py::arg("scoring"), py::arg("bias"), py::arg("n_group"), py::arg("topk_group"),
+        py::arg("routed_scale"), py::arg("shared_gate_col"), py::arg("expert_begin"), py::arg("expert_end"),
+        py::arg("has_shared"), py::arg("topk_ids"), py::arg("topk_w"), py::arg("group_count"),
+        py::arg("group_offset"), py::arg("chunk_prefix"), py::arg("pair_slot"), py::arg("row_dst"),
+        py::arg("row_scale"), py::arg("x_q"), py::arg("x_sf"), py::arg("xg_q"), py::arg("xg_sf"), py::arg("err"),
+        py::arg("ld_logits"), py::arg("logit_splits"), py::arg("logit_split_stride"), py::arg("chunk_rows"),
+        py::arg("pair_src") = py::none(), py::arg("pair_w") = py::none());
 }

@@ -159,17 +159,24 @@ __global__ void __launch_bounds__(THREADS) fused_allreduce_norm_kernel(const Fus
     const int row = int(idx / chunks), c = int(idx % chunks) * 8;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int t = 0; t < a.n_terms; ++t) {
-      const long long off = row * a.row_stride + t * a.term_stride + c;
+      long long off = row * a.row_stride + t * a.term_stride + c;
+      float sc = 1.f;
+      if (a.term_index != nullptr) {  // gathered term; negative = not produced on this rank
+        const int src = a.term_index[row * a.n_terms + t];
+        if (src < 0) continue;
+        off = (long long)src * a.row_stride + c;
+      }
+      if (a.term_scale != nullptr) sc = a.term_scale[row * a.n_terms + t];
       if (a.delta_f32) {
         const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(a.delta) + off);
         const float4 x0 = p[0], x1 = p[1];
-        acc[0] += x0.x; acc[1] += x0.y; acc[2] += x0.z; acc[3] += x0.w;
-        acc[4] += x1.x; acc[5] += x1.y; acc[6] += x1.z; acc[7] += x1.w;
+        acc[0] += sc * x0.x; acc[1] += sc * x0.y; acc[2] += sc * x0.z; acc[3] += sc * x0.w;
+        acc[4] += sc * x1.x; acc[5] += sc * x1.y; acc[6] += sc * x1.z; acc[7] += sc * x1.w;
       } else {
         float f[8];
         unpack8(*reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.delta) + off), f);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] += f[j];
+        for (int j = 0; j < 8; ++j) acc[j] += sc * f[j];
       }
     }
     *reinterpret_cast<uint4*>(my_part + (size_t)row * H + c) = pack8(acc);

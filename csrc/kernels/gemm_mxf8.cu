@@ -24,9 +24,13 @@
 // column r1 holds rows 32*r1..32*r1+31, so a 32-token chunk that starts 32*j rows
 // into an atom points the MMA's B-scale address at column j of the staged atom.
 //
-// Split-K (dense mode): item (m, chunk, ks) covers K tiles [ks*kps, (ks+1)*kps) and
-// stores fp32 partials at out + ks*split_stride; consumers sum the splits in a fixed
-// order, so results are deterministic.
+// Split-K, two forms.  (1) k_splits (dense, fp32 output): item (m, chunk, ks) covers K
+// tiles [ks*kps, (ks+1)*kps) and stores its partial at out + ks*split_stride; the
+// consumer sums the splits in a fixed order.  (2) fix_splits (any mode): the splits of
+// one output tile run on different CTAs, publish fp32 partials to a workspace and bump
+// a per-tile counter; the CTA that completes the tile sums the partials in split order
+// (deterministic) and runs the epilogue.  A single CTA streams only ~90 GB/s from HBM,
+// so small GEMMs need the extra CTAs to reach full bandwidth.
 //
 // Reference parity: replaces the reference's Triton grouped MoE GEMMs and skinny
 // linears (worker/zstep_worker/kernels_sm120/qwen35_ops.py:1226-1438) and the
@@ -43,9 +47,14 @@ constexpr int A_BYTES = BM * BK;
 constexpr int SF_BYTES = 512;
 constexpr int NUM_THREADS = 192;
 constexpr int kMaxGroups = 520;  // grouped mode: per-group tables are staged in smem
+constexpr int kMaxFixSplits = 8; // in-kernel split-K factor limit
 
 template <int BN, int STAGES>
 struct Cfg {
+  // Each pipeline stage holds KT consecutive K tiles, so one bulk copy moves 32 KiB of
+  // weights and one 3-D TMA box both tiles of activations: the producer issues half as
+  // many copy instructions (each costs ~50-90 ns of issue time on one SM).
+  static constexpr int KT = 2;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int ACC_COLS = BN;              // fp32 accumulator columns per buffer
   // Scale factors are double-buffered by K-tile parity (8 columns per buffer: SFA 4 +
@@ -54,12 +63,12 @@ struct Cfg {
   static constexpr int SFB_COL = 2 * BN + 4;       // + 8 * (kt & 1), 4 columns
   static constexpr int TMEM_COLS = (2 * BN + 16) <= 128 ? 128 : ((2 * BN + 16) <= 256 ? 256 : 512);
   struct Smem {
-    uint8_t a[STAGES][A_BYTES];
-    uint8_t b[STAGES][B_BYTES];
-    uint8_t sfa[STAGES][SF_BYTES];
-    uint8_t sfb[STAGES][SF_BYTES];
-    float xch[16][64];              // epilogue exchange (gate/up pairing)
-    unsigned long long red[4][16];  // epilogue exchange (argmax)
+    uint8_t a[STAGES][KT][A_BYTES];
+    uint8_t b[STAGES][KT][B_BYTES];
+    uint8_t sfa[STAGES][KT][SF_BYTES];
+    uint8_t sfb[STAGES][KT][SF_BYTES];
+    float xch[32][64];              // epilogue exchange (gate/up pairing)
+    unsigned long long red[4][32];  // epilogue exchange (argmax)
     int g_prefix[kMaxGroups + 1];   // grouped mode: chunk prefix, offsets, counts
     int g_offset[kMaxGroups];
     int g_count[kMaxGroups];
@@ -70,11 +79,13 @@ struct Cfg {
     uint64_t drain;
     uint32_t tmem_base;
     int abort_flag;
+    int fix_last;                   // split-K: this CTA completed the current tile
   };
 };
 
 struct Item {
   int g, m, c, count, seg_off, kt0, kt1, ks;
+  int tile;  // output tile id (split-K bookkeeping)
 };
 
 // Work item `idx`.  Grouped mode reads the per-group tables staged in shared memory
@@ -86,10 +97,11 @@ __device__ __forceinline__ bool get_item(const GemmMxf8Args& p, int idx, Item& i
   const int k_tiles = p.k / BK;
   if (p.chunk_prefix == nullptr) {
     const int chunks = (p.m_rows + BN - 1) / BN;
-    const int splits = p.k_splits > 1 ? p.k_splits : 1;
+    const int splits = p.k_splits > 1 ? p.k_splits : (p.fix_splits > 1 ? p.fix_splits : 1);
     if (idx >= chunks * m_tiles * splits) return false;
     it.ks = idx % splits;
     const int rest = idx / splits;
+    it.tile = rest;
     it.g = 0;
     it.m = rest % m_tiles;
     it.c = rest / m_tiles;
@@ -100,10 +112,15 @@ __device__ __forceinline__ bool get_item(const GemmMxf8Args& p, int idx, Item& i
     it.kt1 = min(k_tiles, it.kt0 + kps);
     return true;
   }
+  const int S = p.fix_splits > 1 ? p.fix_splits : 1;
   const int total_chunks = pre[p.groups];
-  if (idx >= total_chunks * m_tiles) return false;
-  const int chunk = idx / m_tiles;
-  it.m = idx % m_tiles;
+  if (idx >= total_chunks * m_tiles * S) return false;
+  const int t = idx / S;
+  if (S > 1 && t >= p.max_tiles) return false;  // workspace too small: the producer reports it
+  it.ks = idx % S;
+  it.tile = t;
+  const int chunk = t / m_tiles;
+  it.m = t % m_tiles;
   int lo = 0, hi = p.groups;  // largest g with prefix[g] <= chunk
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
@@ -113,10 +130,41 @@ __device__ __forceinline__ bool get_item(const GemmMxf8Args& p, int idx, Item& i
   it.c = chunk - pre[lo];
   it.seg_off = off[lo];
   it.count = min(BN, cnt[lo] - it.c * BN);
-  it.kt0 = 0;
-  it.kt1 = k_tiles;
-  it.ks = 0;
+  const int kps = k_tiles / S;
+  it.kt0 = it.ks * kps;
+  it.kt1 = it.kt0 + kps;
   return true;
+}
+
+// Accumulator columns [col0, col0 + ncols) (ncols <= 32) of this thread's row.  Without
+// split-K they come straight from TMEM (col0 is a multiple of 32 then); with split-K they
+// are the sum of every split's fp32 partial, in split order, from the workspace.
+template <int BN>
+__device__ __forceinline__ void load_cols(uint32_t t_base, const GemmMxf8Args& p, const Item& it, int S, int col0,
+                                          int ncols, int row_in_tile, float (&v)[32]) {
+  if (S == 1) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_base + col0, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = 0.f;
+  const float* base = p.ws + (size_t)it.tile * S * (BN * BM) + (size_t)col0 * BM + row_in_tile;
+  for (int q = 0; q < S; ++q) {
+    const float* w = base + (size_t)q * (BN * BM);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < ncols) v[j] += __ldcg(w + j * BM);
+  }
+}
+
+__device__ __forceinline__ int sem_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t phase, int* err,
@@ -190,27 +238,36 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
         const int b_row = it.seg_off + it.c * BN;
         const uint8_t* sfa_src = p.sfa + ((size_t)(it.g * (p.n_pad / BM) + it.m) * k_tiles) * SF_BYTES;
         const uint8_t* sfb_src = p.sfb + ((size_t)(b_row / BM) * k_tiles) * SF_BYTES;
-        const uint32_t bytes = A_BYTES + n16 * 16 * BK + 2 * SF_BYTES;
-        for (int kt = it.kt0; kt < it.kt1; ++kt) {
+        for (int kt = it.kt0; kt < it.kt1; kt += C::KT) {
+          const int n_sub = min(C::KT, it.kt1 - kt);
           const int st = issued % STAGES;
           const uint32_t ph = ((issued / STAGES) & 1) ^ 1;
-          if (!wait_or_abort(&s.empty[st], ph, p.err, abort_flag)) break;
-          mbar_expect_tx(&s.full[st], bytes);
-          if (p.a_tiled)  // pre-swizzled contiguous tile: plain bulk copy
-            bulk_load(s.a[st], p.a + ((size_t)(a_row / BM) * k_tiles + kt) * A_BYTES, A_BYTES, &s.full[st]);
-          else
-            tma_load_2d(s.a[st], &tmap_a, &s.full[st], kt * BK, a_row);
-          if (n16 * 16 == BN) {
-            tma_load_2d(s.b[st], &tmap_b_full, &s.full[st], kt * BK, b_row);  // one BN-row box
+          if (issued >= STAGES && !wait_or_abort(&s.empty[st], ph, p.err, abort_flag)) break;
+          // A full-height B box spans KT tiles (a tile past the end of K is zero-filled);
+          // short chunks load n16 16-row boxes per tile.
+          const bool full_b = n16 * 16 == BN;
+          mbar_expect_tx(&s.full[st], n_sub * (A_BYTES + 2 * SF_BYTES) + (full_b ? C::KT : n_sub) * n16 * 16 * BK);
+          if (p.a_tiled) {  // pre-swizzled contiguous tiles: one plain bulk copy
+            bulk_load(s.a[st][0], p.a + ((size_t)(a_row / BM) * k_tiles + kt) * A_BYTES, n_sub * A_BYTES,
+                      &s.full[st]);
           } else {
-            for (int j = 0; j < n16; ++j)
-              tma_load_2d(s.b[st] + j * 16 * BK, &tmap_b, &s.full[st], kt * BK, b_row + j * 16);
+            for (int j = 0; j < n_sub; ++j) tma_load_2d(s.a[st][j], &tmap_a, &s.full[st], (kt + j) * BK, a_row);
           }
-          bulk_load(s.sfa[st], sfa_src + (size_t)kt * SF_BYTES, SF_BYTES, &s.full[st]);
-          bulk_load(s.sfb[st], sfb_src + (size_t)kt * SF_BYTES, SF_BYTES, &s.full[st]);
+          if (full_b) {
+            tma_load_3d(s.b[st][0], &tmap_b_full, &s.full[st], 0, b_row, kt);  // one BN-row x KT box
+          } else {
+            for (int t = 0; t < n_sub; ++t)
+              for (int j = 0; j < n16; ++j)
+                tma_load_2d(s.b[st][t] + j * 16 * BK, &tmap_b, &s.full[st], (kt + t) * BK, b_row + j * 16);
+          }
+          bulk_load(s.sfa[st][0], sfa_src + (size_t)kt * SF_BYTES, n_sub * SF_BYTES, &s.full[st]);
+          bulk_load(s.sfb[st][0], sfb_src + (size_t)kt * SF_BYTES, n_sub * SF_BYTES, &s.full[st]);
           ++issued;
         }
       }
+      if (blockIdx.x == 0 && p.fix_splits > 1 && p.chunk_prefix != nullptr &&
+          s.g_prefix[p.groups] * (p.n_pad / BM) > p.max_tiles)
+        report_error(p.err, kErrBadShape);  // split-K workspace smaller than the tile count
       // Drain: wait (bounded) until every fill this thread issued has landed, so no
       // copy is still writing shared memory when the CTA exits.
       const uint32_t first = issued > STAGES ? issued - STAGES : 0;
@@ -227,7 +284,7 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
     // chunks that start 32*j0 rows into a scale atom, the warp first moves each
     // line's 4 scale bytes of rows 32*j0.. to the line's first word, so the staged
     // scales always start at an aligned TMEM column.
-    uint32_t consumed = 0;
+    uint32_t consumed = 0, sub_count = 0;
     uint32_t acc_uses[2] = {0, 0};
     int local = 0;
     Item it;
@@ -242,36 +299,41 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
       const uint32_t n_mma = ((it.count + 15) >> 4) << 4;
       const uint32_t d_tmem = tmem + buf * C::ACC_COLS;
       const int j0 = ((it.seg_off + it.c * BN) & 127) >> 5;  // nonzero only when BN < 128
-      for (int kt = it.kt0; kt < it.kt1; ++kt) {
+      for (int kt = it.kt0; kt < it.kt1; kt += C::KT) {
+        const int n_sub = min(C::KT, it.kt1 - kt);
         const int st = consumed % STAGES;
         ok = wait_or_abort(&s.full[st], (consumed / STAGES) & 1, p.err, abort_flag);
         if (!__all_sync(0xffffffff, ok)) {
           ok = false;
           break;
         }
-        if (BN < 128 && j0 != 0) {
-          uint32_t* line = reinterpret_cast<uint32_t*>(s.sfb[st] + lane * 16);
-          line[0] = line[j0];
-          fence_proxy_async_shared();
-          __syncwarp();
-        }
-        tc_fence_after();
-        if (lane == 0) {
-          const uint32_t sf_off = (consumed & 1) * 8;
-          tmem_cp_32x128b_warpx4(tmem + C::SFA_COL + sf_off, make_smem_desc(smem_u32(s.sfa[st]), 0, 128, 0));
-          tmem_cp_32x128b_warpx4(tmem + C::SFB_COL + sf_off, make_smem_desc(smem_u32(s.sfb[st]), 0, 128, 0));
-          const uint32_t a_base = smem_u32(s.a[st]);
-          const uint32_t b_base = smem_u32(s.b[st]);
-#pragma unroll
-          for (int kb = 0; kb < 4; ++kb) {
-            const uint64_t adesc = make_smem_desc(a_base + kb * 32, 16, 1024, 2);
-            const uint64_t bdesc = make_smem_desc(b_base + kb * 32, 16, 1024, 2);
-            const uint32_t idesc = make_idesc_mxf8(BM, n_mma, kb, kb);
-            mma_mxf8(d_tmem, adesc, bdesc, idesc, (tmem + C::SFA_COL + sf_off) | (uint32_t(kb) << 30),
-                     (tmem + C::SFB_COL + sf_off) | (uint32_t(kb) << 30), (kt > it.kt0 || kb > 0) ? 1u : 0u);
+        for (int j = 0; j < n_sub; ++j) {
+          if (BN < 128 && j0 != 0) {
+            uint32_t* line = reinterpret_cast<uint32_t*>(s.sfb[st][j] + lane * 16);
+            line[0] = line[j0];
+            fence_proxy_async_shared();
+            __syncwarp();
           }
-          tc_commit(&s.empty[st]);
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t sf_off = (sub_count & 1) * 8;
+            tmem_cp_32x128b_warpx4(tmem + C::SFA_COL + sf_off, make_smem_desc(smem_u32(s.sfa[st][j]), 0, 128, 0));
+            tmem_cp_32x128b_warpx4(tmem + C::SFB_COL + sf_off, make_smem_desc(smem_u32(s.sfb[st][j]), 0, 128, 0));
+            const uint32_t a_base = smem_u32(s.a[st][j]);
+            const uint32_t b_base = smem_u32(s.b[st][j]);
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb) {
+              const uint64_t adesc = make_smem_desc(a_base + kb * 32, 16, 1024, 2);
+              const uint64_t bdesc = make_smem_desc(b_base + kb * 32, 16, 1024, 2);
+              const uint32_t idesc = make_idesc_mxf8(BM, n_mma, kb, kb);
+              mma_mxf8(d_tmem, adesc, bdesc, idesc, (tmem + C::SFA_COL + sf_off) | (uint32_t(kb) << 30),
+                       (tmem + C::SFB_COL + sf_off) | (uint32_t(kb) << 30), (kt + j > it.kt0 || kb > 0) ? 1u : 0u);
+            }
+          }
+          __syncwarp();
+          ++sub_count;
         }
+        if (lane == 0) tc_commit(&s.empty[st]);
         __syncwarp();
         ++consumed;
       }
@@ -287,8 +349,14 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ epilogue
+    // Each thread owns one accumulator row (a weight feature) and walks the token
+    // columns 32 at a time.  With in-kernel split-K the CTA first publishes its fp32
+    // partial; only the CTA that completes the tile sums all partials (fixed split
+    // order, so the result does not depend on arrival order) and runs the epilogue.
     const int q = warp;  // TMEM subpartition (lanes 32q .. 32q+31)
     const int row_in_tile = q * 32 + lane;
+    const int S = p.fix_splits > 1 ? p.fix_splits : 1;
+    const long long split_off = p.k_splits > 1 ? 1 : 0;
     uint32_t acc_uses[2] = {0, 0};
     int local = 0;
     Item it;
@@ -298,109 +366,150 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
       ++acc_uses[buf];
       tc_fence_after();
       const uint32_t t_base = tmem + ((uint32_t)(q * 32) << 16) + buf * C::ACC_COLS;
-      const int n16 = (it.count + 15) >> 4;
+      const int nch = (it.count + 31) >> 5;
       const int seg_row0 = it.seg_off + it.c * BN;
       const int n_glob = it.m * BM + row_in_tile;
-
-      if (p.epi_mode == kEpiSiluQuant) {
-        // Tile rows 0..63 are gate features, 64..127 the matching up features of
-        // intermediate columns [64m, 64m+64).  Pair them through shared memory,
-        // form silu(g)*u and quantize to MXFP8 (32-feature blocks = one warp).
-        for (int ch = 0; ch < n16; ++ch) {
-          uint32_t r[16];
-          tmem_ld_32x32b_x16(t_base + ch * 16, r);
+      // Columns this CTA finishes: all of them, or with split-K one slice of the tile
+      // (dense: every split reduces BN/S columns once all partials exist) or the whole
+      // tile in the CTA that completes it (grouped: items may exceed one wave).
+      int c_begin = 0, c_end = it.count;
+      bool finish = true;
+      if (S > 1) {
+        float* mine = p.ws + ((size_t)it.tile * S + it.ks) * (size_t)(BN * BM) + row_in_tile;
+        for (int ch = 0; ch < nch; ++ch) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_base + ch * 32, r);
           tmem_ld_wait();
-          if (q >= 2) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) s.xch[j][(q - 2) * 32 + lane] = __uint_as_float(r[j]);
+          for (int j = 0; j < 32; ++j) __stcg(mine + (ch * 32 + j) * BM, __uint_as_float(r[j]));
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const bool parallel = p.chunk_prefix == nullptr;  // host guarantees one wave
+        if (q == 0 && lane == 0) {
+          __threadfence();
+          const int old = atomicAdd(p.tile_sem + it.tile, 1);
+          int ok = 1;
+          if (parallel) {
+            ok = 0;
+            for (uint32_t i = 0; i < kMbarSpinLimit; ++i) {
+              if (sem_acquire(p.tile_sem + it.tile) >= S) { ok = 1; break; }
+              if (*abort_flag) break;
+              if (i > 16) __nanosleep(32);
+            }
+            if (!ok) {
+              report_error(p.err, kErrMbarTimeout);
+              *abort_flag = 1;
+            }
+          } else {
+            ok = old == S - 1;
+            if (ok) p.tile_sem[it.tile] = 0;  // every split has arrived: re-arm for the next call
+            __threadfence();
           }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (q < 2) {
-            const int feat = it.m * 64 + q * 32 + lane;  // intermediate column
-            uint8_t* act = reinterpret_cast<uint8_t*>(p.out);
-#pragma unroll 4
-            for (int j = 0; j < 16; ++j) {
-              const int col = ch * 16 + j;
-              const float g = __uint_as_float(r[j]);
-              const float u = s.xch[j][q * 32 + lane];
-              const float h = siluf_(g) * u;
-              const float amax = warp_max(fabsf(h));
-              const uint8_t code = mx_scale_e8m0(amax);
-              if (col < it.count) {
-                const int row = seg_row0 + col;
-                act[(size_t)row * p.ldo + feat] = f32_to_e4m3(h * mx_inv_scale(code));
-                if (lane == 0) {
-                  const int kb = feat >> 5;
-                  uint8_t* sf = p.out_sf + ((size_t)(row >> 7) * (p.ldo >> 7) + (kb >> 2)) * 512;
-                  sf[sf_atom_offset(row & 127, kb & 3)] = code;
+          s.fix_last = ok;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        finish = s.fix_last != 0;
+        if (parallel) {
+          const int width = (BN + S - 1) / S;
+          c_begin = it.ks * width;
+          c_end = min(it.count, c_begin + width);
+        }
+      }
+      if (finish) {
+        const bool valid_n = n_glob < p.n_valid;
+        const int nchunks = c_end > c_begin ? (c_end - c_begin + 31) >> 5 : 0;
+        for (int ch = 0; ch < nchunks; ++ch) {
+          const int col0 = c_begin + ch * 32;
+          const int ncols = min(32, c_end - col0);
+          float v[32];
+          load_cols<BN>(t_base, p, it, S, col0, ncols, row_in_tile, v);
+          if (p.epi_mode == kEpiSiluQuant) {
+            // Tile rows 0..63 are gate features, 64..127 the matching up features of
+            // intermediate columns [64m, 64m+64).  Pair them through shared memory,
+            // form silu(g)*u and quantize to MXFP8 (32-feature blocks = one warp).
+            if (q >= 2) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) s.xch[j][(q - 2) * 32 + lane] = v[j];
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (q < 2) {
+              const int feat = it.m * 64 + q * 32 + lane;  // intermediate column
+              uint8_t* act = reinterpret_cast<uint8_t*>(p.out);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const int col = col0 + j;
+                const float h = siluf_(v[j]) * s.xch[j][q * 32 + lane];
+                const float amax = warp_max(fabsf(h));
+                const uint8_t code = mx_scale_e8m0(amax);
+                if (j < ncols) {
+                  const int row = seg_row0 + col;
+                  act[(size_t)row * p.ldo + feat] = f32_to_e4m3(h * mx_inv_scale(code));
+                  if (lane == 0) {
+                    const int kb = feat >> 5;
+                    uint8_t* sf = p.out_sf + ((size_t)(row >> 7) * (p.ldo >> 7) + (kb >> 2)) * 512;
+                    sf[sf_atom_offset(row & 127, kb & 3)] = code;
+                  }
                 }
               }
             }
-          }
-          asm volatile("bar.sync 2, 128;" ::: "memory");
-        }
-      } else if (p.epi_mode == kEpiArgmaxPartial) {
-        // Vocab-tile argmax: reduce each token column over this tile's 128 rows into
-        // one packed (orderable logit, ~id) word; the max over words gives the largest
-        // logit with the smallest id on ties.
-        const bool valid_n = n_glob < p.n_valid;
-        unsigned long long* part = reinterpret_cast<unsigned long long*>(p.out);
-        for (int ch = 0; ch < n16; ++ch) {
-          uint32_t r[16];
-          tmem_ld_32x32b_x16(t_base + ch * 16, r);
-          tmem_ld_wait();
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+          } else if (p.epi_mode == kEpiArgmaxPartial) {
+            // Vocab-tile argmax: reduce each token column over this tile's 128 rows into
+            // one packed (orderable logit, ~id) word; the max over words gives the largest
+            // logit with the smallest id on ties.
+            unsigned long long* part = reinterpret_cast<unsigned long long*>(p.out);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            unsigned long long key = valid_n ? pack_argmax(__uint_as_float(r[j]), n_glob) : 0ull;
+            for (int j = 0; j < 32; ++j) {
+              unsigned long long key = valid_n ? pack_argmax(v[j], n_glob) : 0ull;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-              const unsigned long long other = __shfl_xor_sync(0xffffffff, key, o);
-              key = other > key ? other : key;
+              for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xffffffff, key, o);
+                key = other > key ? other : key;
+              }
+              if (lane == 0) s.red[q][j] = key;
             }
-            if (lane == 0) s.red[q][j] = key;
-          }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (q == 0 && lane < 16) {
-            const int col = ch * 16 + lane;
-            unsigned long long key = s.red[0][lane];
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (q == 0) {
+              const int col = col0 + lane;
+              unsigned long long key = s.red[0][lane];
 #pragma unroll
-            for (int w = 1; w < 4; ++w) key = s.red[w][lane] > key ? s.red[w][lane] : key;
-            if (col < it.count) part[(size_t)(seg_row0 + col) * p.ldo + it.m] = key;
-          }
-          asm volatile("bar.sync 2, 128;" ::: "memory");
-        }
-      } else {
-        const bool valid_n = n_glob < p.n_valid;
-        float* outf = reinterpret_cast<float*>(p.out) + (size_t)it.ks * p.split_stride;
-        for (int ch = 0; ch < n16; ++ch) {
-          uint32_t r[16];
-          tmem_ld_32x32b_x16(t_base + ch * 16, r);
-          // Scatter mode: lanes 0..15 fetch the chunk's destination rows and weights in
-          // parallel (instead of one dependent load per column).
-          int dst_l = 0;
-          float scl_l = 0.f;
-          if (p.epi_mode == kEpiScatterScaled && lane < 16 && ch * 16 + lane < it.count) {
-            dst_l = __ldg(p.row_dst + seg_row0 + ch * 16 + lane);
-            scl_l = __ldg(p.row_scale + seg_row0 + ch * 16 + lane);
-          }
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int col = ch * 16 + j;
-            const int dst = __shfl_sync(0xffffffff, dst_l, j);
-            const float scl = __shfl_sync(0xffffffff, scl_l, j);
-            if (col >= it.count || !valid_n) continue;
-            const int row = seg_row0 + col;
-            float v = __uint_as_float(r[j]);
-            if (p.epi_mode == kEpiStoreF32) {
-              outf[(size_t)row * p.ldo + n_glob] = v;
-            } else if (p.epi_mode == kEpiScatterScaled) {
-              reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)dst * p.ldo + n_glob] = __float2bfloat16_rn(v * scl);
-            } else {
-              reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)row * p.ldo + n_glob] = __float2bfloat16_rn(v);
+              for (int w = 1; w < 4; ++w) key = s.red[w][lane] > key ? s.red[w][lane] : key;
+              if (lane < ncols) part[(size_t)(seg_row0 + col) * p.ldo + it.m] = key;
             }
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+          } else if (p.epi_mode == kEpiScatterScaled) {
+            // Destination rows and routing weights: the same address for all lanes, so
+            // each is one broadcast load; all 32 are issued before the stores.
+            int dst[32];
+            float scl[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const bool ok = j < ncols;
+              dst[j] = ok ? __ldg(p.row_dst + seg_row0 + col0 + j) : 0;
+              scl[j] = ok ? __ldg(p.row_scale + seg_row0 + col0 + j) : 0.f;
+            }
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + n_glob;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (valid_n && j < ncols) o[(size_t)dst[j] * p.ldo] = __float2bfloat16_rn(v[j] * scl[j]);
+          } else if (p.epi_mode == kEpiStoreF32) {
+            float* o = reinterpret_cast<float*>(p.out) + it.ks * p.split_stride * split_off +
+                       (size_t)(seg_row0 + col0) * p.ldo + n_glob;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (valid_n && j < ncols) o[(size_t)j * p.ldo] = v[j];
+          } else {
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)(seg_row0 + col0) * p.ldo + n_glob;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (valid_n && j < ncols) o[(size_t)j * p.ldo] = __float2bfloat16_rn(v[j]);
           }
         }
+      }
+      if (S > 1 && p.chunk_prefix == nullptr) {
+        // Second arrival: once all S splits have read every partial, the last re-arms the counter.
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (q == 0 && lane == 0 && atomicAdd(p.tile_sem + it.tile, 1) == 2 * S - 1) atomicExch(p.tile_sem + it.tile, 0);
       }
       tc_fence_before();
       __syncwarp();
@@ -453,6 +562,21 @@ int make_tmap_u8(CUtensorMap* m, const void* base, int64_t rows, int64_t k, int 
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
+// Activations [rows, k] viewed as {128 B, rows, k/128 tiles}: one box = box_rows rows of
+// kt_box consecutive 128-byte K tiles, laid out in shared memory tile after tile.
+int make_tmap_b3(CUtensorMap* m, const void* base, int64_t rows, int64_t k, int box_rows, int kt_box) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (enc == nullptr) return -1;
+  cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)(k / 128)};
+  cuuint64_t strides[2] = {(cuuint64_t)k, 128};
+  cuuint32_t box[3] = {128, (cuuint32_t)box_rows, (cuuint32_t)kt_box};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
 // Pre-tiled weights: [tiles][128 rows][128 B] viewed as a 3-D tensor whose box is one
 // whole contiguous tile.
 int make_tmap_tiled(CUtensorMap* m, const void* base, int64_t tiles) {
@@ -484,7 +608,7 @@ int launch(const GemmMxf8Args& p, const CUtensorMap& ta, const CUtensorMap& tb, 
   using namespace zs::gemm;
   int grid = num_sms();
   if (p.chunk_prefix == nullptr) {
-    const int splits = p.k_splits > 1 ? p.k_splits : 1;
+    const int splits = p.k_splits > 1 ? p.k_splits : (p.fix_splits > 1 ? p.fix_splits : 1);
     const int items = ((p.m_rows + BN - 1) / BN) * (p.n_pad / BM) * splits;
     if (items == 0) return 0;
     grid = items < grid ? items : grid;
@@ -509,6 +633,16 @@ extern "C" int zs_gemm_mxf8(const GemmMxf8Args* args, cudaStream_t stream) {
     return -11;
   if (p.b_rows % BM != 0) return -12;
   if (p.k_splits > 1 && (p.chunk_prefix != nullptr || p.epi_mode != kEpiStoreF32)) return -16;
+  if (p.fix_splits > 1) {
+    if (p.k_splits > 1 || p.fix_splits > kMaxFixSplits || (p.k / BK) % p.fix_splits != 0 || p.ws == nullptr ||
+        p.tile_sem == nullptr)
+      return -19;
+    const int bn_ = p.block_n == 32 ? 32 : 128;
+    const int tiles = ((p.m_rows + bn_ - 1) / bn_) * (p.n_pad / BM);
+    if (p.chunk_prefix == nullptr && tiles > p.max_tiles) return -20;
+    // Dense split-K waits for the tile's other splits, so every item must be resident at once.
+    if (p.chunk_prefix == nullptr && tiles * p.fix_splits > num_sms()) return -21;
+  }
   const int bn = p.block_n == 32 ? 32 : 128;
   if (p.chunk_prefix != nullptr && p.chunk_rows != bn) return -17;
   if (p.chunk_prefix != nullptr && p.groups > kMaxGroups) return -18;
@@ -520,6 +654,6 @@ extern "C" int zs_gemm_mxf8(const GemmMxf8Args* args, cudaStream_t stream) {
   }
   if (make_tmap_u8(&tb, p.b, p.b_rows, p.k, 16) != 0) return -14;
   CUtensorMap tbf;
-  if (make_tmap_u8(&tbf, p.b, p.b_rows, p.k, bn) != 0) return -14;
-  return bn == 32 ? launch<32, 9>(p, ta, tb, tbf, stream) : launch<128, 6>(p, ta, tb, tbf, stream);
+  if (make_tmap_b3(&tbf, p.b, p.b_rows, p.k, bn, Cfg<32, 4>::KT) != 0) return -14;
+  return bn == 32 ? launch<32, 4>(p, ta, tb, tbf, stream) : launch<128, 3>(p, ta, tb, tbf, stream);
 }

@@ -46,36 +46,55 @@ __device__ __forceinline__ float logit(const MoeRouteArgs& a, int row, int col) 
   return v;
 }
 
+// One warp per row.  PER = experts per lane (lane owns experts lane + 32*j), a
+// compile-time constant so scores, selection keys and the chosen top-k stay in registers.
+template <int PER>
 __global__ void route_topk_kernel(const MoeRouteArgs a) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= a.rows) return;
   const int E = a.num_experts;
-  const int per = (E + 31) / 32;  // experts per lane: e = lane + 32*j
-  float score[kMaxExperts / 32];   // routing weight source
-  float choice[kMaxExperts / 32];  // selection key
+  float score[PER];   // routing weight source
+  float choice[PER];  // selection key
+  {
+    // Router logits (sum of the router GEMM's K partials, in order), loads issued together.
+    const float* lg = a.logits + (size_t)row * a.ld_logits;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int e = lane + 32 * j;
+      score[j] = e < E ? lg[e] : -INFINITY;
+    }
+    for (int sp = 1; sp < a.logit_splits; ++sp) {
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        const int e = lane + 32 * j;
+        if (e < E) score[j] += lg[(size_t)sp * a.logit_split_stride + e];
+      }
+    }
+  }
   if (a.scoring == 0) {
     float mx = -INFINITY;
-    for (int j = 0; j < per; ++j) {
-      const int e = lane + 32 * j;
-      score[j] = e < E ? logit(a, row, e) : -INFINITY;
-      mx = fmaxf(mx, score[j]);
-    }
+#pragma unroll
+    for (int j = 0; j < PER; ++j) mx = fmaxf(mx, score[j]);
     mx = warp_max(mx);
     float sum = 0.f;
-    for (int j = 0; j < per; ++j) {
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
       score[j] = (lane + 32 * j) < E ? __expf(score[j] - mx) : 0.f;
       sum += score[j];
     }
     sum = warp_sum(sum);
-    for (int j = 0; j < per; ++j) {
-      score[j] /= sum;
+    const float inv = 1.f / sum;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      score[j] *= inv;
       choice[j] = (lane + 32 * j) < E ? score[j] : -INFINITY;
     }
   } else {
-    for (int j = 0; j < per; ++j) {
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
       const int e = lane + 32 * j;
-      score[j] = e < E ? sigmoidf_(logit(a, row, e)) : 0.f;
+      score[j] = e < E ? sigmoidf_(score[j]) : 0.f;
       choice[j] = e < E ? score[j] + (a.bias ? a.bias[e] : 0.f) : -INFINITY;
     }
     if (a.n_group > 1) {
@@ -86,7 +105,8 @@ __global__ void route_topk_kernel(const MoeRouteArgs a) {
       float* gs = gscore_s[threadIdx.x >> 5];
       for (int g = 0; g < a.n_group; ++g) {
         float b1 = -INFINITY, b2 = -INFINITY;
-        for (int j = 0; j < per; ++j) {
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
           const int e = lane + 32 * j;
           if (e >= g * gsize && e < (g + 1) * gsize) {
             const float c = choice[j];
@@ -114,51 +134,53 @@ __global__ void route_topk_kernel(const MoeRouteArgs a) {
           if (!((keep >> g) & 1) && (best < 0 || gs[g] > bv)) { best = g; bv = gs[g]; }
         keep |= 1ull << best;
       }
-      for (int j = 0; j < per; ++j) {
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
         const int e = lane + 32 * j;
         if (e < E && !((keep >> (e / gsize)) & 1)) choice[j] = -INFINITY;
       }
       __syncwarp();
     }
   }
-  // Top-k by choice key.
-  int ids[kMaxTopK];
-  float wts[kMaxTopK];
-  float wsum = 0.f;
-  for (int k = 0; k < a.top_k; ++k) {
+  // Top-k by choice key (ties -> smaller expert id); lane k keeps pick k.
+  int my_id = 0;
+  float my_w = 0.f, wsum = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k) {
+    if (k >= a.top_k) break;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int j = 0; j < per; ++j) {
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
       const int e = lane + 32 * j;
       if (e < E && (choice[j] > bv || (choice[j] == bv && e < bi))) { bv = choice[j]; bi = e; }
     }
     warp_argmax(bv, bi);
     // Owner lane removes the winner and publishes its weight.
     float w = 0.f;
-    for (int j = 0; j < per; ++j)
+#pragma unroll
+    for (int j = 0; j < PER; ++j)
       if (lane + 32 * j == bi) { w = score[j]; choice[j] = -INFINITY; }
     w = __shfl_sync(0xffffffff, w, bi & 31);
-    ids[k] = bi;
-    wts[k] = w;
+    if (lane == k) { my_id = bi; my_w = w; }
     wsum += w;
   }
-  if (lane == 0) {
-    const int K1 = a.top_k + 1;
+  // Lanes 0..top_k-1 write their pick; the arrival order of the slot counters only
+  // decides a pair's row inside its expert's segment.
+  const int K1 = a.top_k + 1;
+  if (lane < a.top_k) {
+    float w = my_w;
+    if (a.norm_topk) w = w / (wsum > 0.f ? wsum : 1.f);
+    w *= a.routed_scale;
+    a.topk_ids[row * a.top_k + lane] = my_id;
+    a.topk_w[row * a.top_k + lane] = w;
+    int slot = -1;
+    if (my_id >= a.expert_begin && my_id < a.expert_end)
+      slot = atomicAdd(a.group_count + (my_id - a.expert_begin), 1);
+    a.pair_slot[row * K1 + lane] = slot;
+  } else if (lane == a.top_k) {
     const int G_local = a.expert_end - a.expert_begin;
-    for (int k = 0; k < a.top_k; ++k) {
-      float w = wts[k];
-      if (a.norm_topk) w = w / (wsum > 0.f ? wsum : 1.f);
-      w *= a.routed_scale;
-      a.topk_ids[row * a.top_k + k] = ids[k];
-      a.topk_w[row * a.top_k + k] = w;
-      int slot = -1;
-      if (ids[k] >= a.expert_begin && ids[k] < a.expert_end)
-        slot = atomicAdd(a.group_count + (ids[k] - a.expert_begin), 1);
-      a.pair_slot[row * K1 + k] = slot;
-    }
-    int sslot = -1;
-    if (a.has_shared) sslot = atomicAdd(a.group_count + G_local, 1);
-    a.pair_slot[row * K1 + a.top_k] = sslot;
+    a.pair_slot[row * K1 + a.top_k] = a.has_shared ? atomicAdd(a.group_count + G_local, 1) : -1;
   }
 }
 
@@ -218,7 +240,10 @@ __global__ void scatter_kernel(const MoeRouteArgs a) {
   if (pair >= a.rows * K1) return;
   const int row = pair / K1, j = pair % K1;
   const int slot = a.pair_slot[pair];
-  if (slot < 0) return;
+  if (slot < 0) {
+    if (a.pair_src != nullptr && lane == 0) a.pair_src[pair] = -1;
+    return;
+  }
   int g;
   float w;
   if (j < a.top_k) {
@@ -229,7 +254,10 @@ __global__ void scatter_kernel(const MoeRouteArgs a) {
     w = a.shared_gate_col >= 0 ? sigmoidf_(logit(a, row, a.shared_gate_col)) : 1.f;
   }
   const int dst = a.group_offset[g] + slot;
-  if (dst >= a.max_grouped_rows) return;  // overflow (reported by offsets_kernel)
+  if (dst >= a.max_grouped_rows) {  // overflow (reported by offsets_kernel)
+    if (a.pair_src != nullptr && lane == 0) a.pair_src[pair] = -1;
+    return;
+  }
   const uint4* src = reinterpret_cast<const uint4*>(a.x_q + (size_t)row * a.hidden);
   uint4* dq = reinterpret_cast<uint4*>(a.xg_q + (size_t)dst * a.hidden);
   for (int c = lane; c < a.hidden / 16; c += 32) dq[c] = src[c];
@@ -240,8 +268,12 @@ __global__ void scatter_kernel(const MoeRouteArgs a) {
     a.xg_sf[dso] = a.x_sf[so];
   }
   if (lane == 0) {
-    a.row_dst[dst] = row * K1 + j;
-    a.row_scale[dst] = w;
+    if (a.row_dst != nullptr) a.row_dst[dst] = row * K1 + j;
+    if (a.row_scale != nullptr) a.row_scale[dst] = w;
+    if (a.pair_src != nullptr) {
+      a.pair_src[pair] = dst;
+      a.pair_w[pair] = w;
+    }
   }
 }
 
@@ -262,7 +294,13 @@ extern "C" int zs_moe_route(const MoeRouteArgs* args, cudaStream_t stream) {
     return cudaGetLastError() == cudaSuccess ? 0 : -2;
   }
   int wpb = 8;
-  zs::moe::route_topk_kernel<<<(a.rows + 1) / 2, 64, 0, stream>>>(a);  // 2 rows per block: more SMs busy
+  {
+    const dim3 grid((a.rows + 1) / 2), block(64);  // 2 rows per block: more SMs busy
+    if (a.num_experts <= 64) zs::moe::route_topk_kernel<2><<<grid, block, 0, stream>>>(a);
+    else if (a.num_experts <= 128) zs::moe::route_topk_kernel<4><<<grid, block, 0, stream>>>(a);
+    else if (a.num_experts <= 256) zs::moe::route_topk_kernel<8><<<grid, block, 0, stream>>>(a);
+    else zs::moe::route_topk_kernel<16><<<grid, block, 0, stream>>>(a);
+  }
   zs::moe::offsets_kernel<<<1, 1024, 0, stream>>>(a, groups);
   const int pairs = a.rows * (a.top_k + 1);
   zs::moe::scatter_kernel<<<(pairs + wpb - 1) / wpb, wpb * 32, 0, stream>>>(a);

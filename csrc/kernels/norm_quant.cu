@@ -61,6 +61,7 @@ template <bool kEmbed>
 __global__ void __launch_bounds__(kNormThreads)
 add_rmsnorm_quant_kernel(__nv_bfloat16* __restrict__ residual, const void* __restrict__ delta,
                          int n_terms, long long d_row_stride, long long d_term_stride, int delta_f32,
+                         const int* __restrict__ term_index, const float* __restrict__ term_scale,
                          const int* __restrict__ ids, const __nv_bfloat16* __restrict__ embed,
                          const __nv_bfloat16* __restrict__ weight, float w_offset, float eps,
                          int hidden, __nv_bfloat16* __restrict__ normed, uint8_t* __restrict__ q,
@@ -92,21 +93,37 @@ add_rmsnorm_quant_kernel(__nv_bfloat16* __restrict__ residual, const void* __res
       if (delta_f32) {
         const float* df = static_cast<const float*>(delta);
         for (int t = 0; t < n_terms; ++t) {
-          const float4* p4 = reinterpret_cast<const float4*>(df + row * d_row_stride + t * d_term_stride + col);
+          long long off = row * d_row_stride + t * d_term_stride;
+          float sc = 1.f;
+          if (term_index != nullptr) {
+            const int src = term_index[row * n_terms + t];
+            if (src < 0) continue;
+            off = src * d_row_stride;
+          }
+          if (term_scale != nullptr) sc = term_scale[row * n_terms + t];
+          const float4* p4 = reinterpret_cast<const float4*>(df + off + col);
           const float4 a0 = p4[0], a1 = p4[1];
-          x[it][0] += a0.x; x[it][1] += a0.y; x[it][2] += a0.z; x[it][3] += a0.w;
-          x[it][4] += a1.x; x[it][5] += a1.y; x[it][6] += a1.z; x[it][7] += a1.w;
+          x[it][0] += sc * a0.x; x[it][1] += sc * a0.y; x[it][2] += sc * a0.z; x[it][3] += sc * a0.w;
+          x[it][4] += sc * a1.x; x[it][5] += sc * a1.y; x[it][6] += sc * a1.z; x[it][7] += sc * a1.w;
         }
       } else {
         const __nv_bfloat16* db = static_cast<const __nv_bfloat16*>(delta);
         for (int t = 0; t < n_terms; ++t) {
-          uint4 d = *reinterpret_cast<const uint4*>(db + row * d_row_stride + t * d_term_stride + col);
+          long long off = row * d_row_stride + t * d_term_stride;
+          float sc = 1.f;
+          if (term_index != nullptr) {
+            const int src = term_index[row * n_terms + t];
+            if (src < 0) continue;
+            off = src * d_row_stride;
+          }
+          if (term_scale != nullptr) sc = term_scale[row * n_terms + t];
+          uint4 d = *reinterpret_cast<const uint4*>(db + off + col);
           const __nv_bfloat162* dh = reinterpret_cast<const __nv_bfloat162*>(&d);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             float2 f = __bfloat1622float2(dh[j]);
-            x[it][2 * j] += f.x;
-            x[it][2 * j + 1] += f.y;
+            x[it][2 * j] += sc * f.x;
+            x[it][2 * j + 1] += sc * f.y;
           }
         }
       }
@@ -223,7 +240,8 @@ extern "C" int zs_quant_mxf8(const void* x, int rows, int k, int ld_x, uint8_t* 
 
 extern "C" int zs_add_rmsnorm_quant(void* residual, const void* delta, int n_terms,
                                     long long d_row_stride, long long d_term_stride, int delta_f32,
-                                    const void* weight, float w_offset, float eps, int rows,
+                                    const int* term_index, const float* term_scale, const void* weight,
+                                    float w_offset, float eps, int rows,
                                     int hidden, void* normed, uint8_t* q, uint8_t* sf,
                                     cudaStream_t stream) {
   if (hidden % (zs::kNormThreads * 8) != 0 || hidden > zs::kNormThreads * 8 * zs::kNormMaxIter)
@@ -231,7 +249,7 @@ extern "C" int zs_add_rmsnorm_quant(void* residual, const void* delta, int n_ter
   if (rows == 0) return 0;
   zs::add_rmsnorm_quant_kernel<false><<<rows, zs::kNormThreads, 0, stream>>>(
       static_cast<__nv_bfloat16*>(residual), delta, n_terms, d_row_stride, d_term_stride, delta_f32,
-      nullptr, nullptr, static_cast<const __nv_bfloat16*>(weight),
+      term_index, term_scale, nullptr, nullptr, static_cast<const __nv_bfloat16*>(weight),
       w_offset, eps, hidden, static_cast<__nv_bfloat16*>(normed), q, sf);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
@@ -245,7 +263,7 @@ extern "C" int zs_embed_rmsnorm_quant(const int* ids, const void* embed, void* h
     return -1;
   if (rows == 0) return 0;
   zs::add_rmsnorm_quant_kernel<true><<<rows, zs::kNormThreads, 0, stream>>>(
-      static_cast<__nv_bfloat16*>(hidden), nullptr, 0, 0, 0, 0, ids,
+      static_cast<__nv_bfloat16*>(hidden), nullptr, 0, 0, 0, 0, nullptr, nullptr, ids,
       static_cast<const __nv_bfloat16*>(embed), static_cast<const __nv_bfloat16*>(weight),
       w_offset, eps, hidden_size, static_cast<__nv_bfloat16*>(normed), q, sf);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;

@@ -53,6 +53,13 @@ typedef struct GemmMxf8Args {
   const int* row_dst;      // kEpiScatterScaled
   const float* row_scale;  // kEpiScatterScaled
   int* err;                // device error word (may be NULL)
+  // In-kernel split-K (any epilogue, dense or grouped): each output tile's K range is
+  // split over fix_splits CTAs; each writes an fp32 partial to ws, and the last to
+  // arrive (tile_sem counter) sums all partials in split order and runs the epilogue.
+  int fix_splits;          // 1 = off; must divide k/128
+  float* ws;               // >= tiles * fix_splits * 128 * block_n floats
+  int* tile_sem;           // >= tiles ints, zero before the first call (kept zero after)
+  int max_tiles;           // capacity of ws / tile_sem in tiles (the kernel checks)
 } GemmMxf8Args;
 
 int zs_gemm_mxf8(const GemmMxf8Args* args, cudaStream_t stream);
@@ -68,8 +75,12 @@ int zs_quant_mxf8(const void* x_bf16, int rows, int k, int ld_x, uint8_t* q, uin
 // y = rmsnorm(residual[r]) * (w + w_offset); y written as bf16 (normed, optional) and/or
 // MXFP8 (q + sf, optional).  Reduction in fp32, hidden % 2048 == 0.  Delta terms are
 // bf16, or f32 when delta_f32 != 0 (split-K partials); terms are summed in index order.
+// Gathered terms (optional, [rows, n_terms]): with term_index, term t of row r is row
+// term_index[r*n_terms+t] of delta (negative: skipped; term_stride unused), times
+// term_scale[r*n_terms+t] when term_scale is given.
 int zs_add_rmsnorm_quant(void* residual, const void* delta, int n_terms, long long delta_row_stride,
-                         long long delta_term_stride, int delta_f32, const void* weight, float w_offset,
+                         long long delta_term_stride, int delta_f32, const int* term_index,
+                         const float* term_scale, const void* weight, float w_offset,
                          float eps, int rows, int hidden, void* normed, uint8_t* q, uint8_t* sf,
                          cudaStream_t stream);
 
@@ -208,6 +219,8 @@ typedef struct MoeRouteArgs {
   uint8_t* xg_q;           // [max_grouped_rows, hidden]
   uint8_t* xg_sf;          // atoms
   int* err;
+  int* pair_src;           // optional [rows, top_k+1]: grouped row of each (token, pair), -1 = none
+  float* pair_w;           // optional [rows, top_k+1]: routing weight of each pair
 } MoeRouteArgs;
 
 int zs_moe_route(const MoeRouteArgs* args, cudaStream_t stream);
@@ -221,6 +234,8 @@ typedef struct FusedArArgs {
   int rank, world;
   const void* delta;         // local partial terms: delta[row*row_stride + t*term_stride + col]
   int n_terms;
+  const int* term_index;     // optional gathered terms (as in zs_add_rmsnorm_quant)
+  const float* term_scale;
   long long row_stride, term_stride;
   int delta_f32;             // terms are f32 (split-K partials) or bf16 (MoE pair rows)
   void* part[8];             // symmetric bf16 [rows, hidden] per rank (local sum)

@@ -219,6 +219,77 @@ def test_gemm_silu_quant(C):
         torch.testing.assert_close(got[o:o + cnt], h, rtol=0.07, atol=0.02 * h.abs().max().item())
 
 
+def _split_ws():
+    return torch.zeros(8 << 20, device="cuda"), torch.zeros(16384, dtype=torch.int32, device="cuda")
+
+
+@pytest.mark.parametrize("epi,S,bn", [(EPI_BF16, 4, 128), (EPI_F32, 8, 128), (EPI_BF16, 2, 32), (EPI_ARGMAX, 4, 128)])
+def test_gemm_fix_splits_dense(C, epi, S, bn):
+    # tiles * S must fit one wave: 640 features = 5 tiles x (2 or 1) token chunks.
+    """In-kernel split-K (last CTA reduces) matches the unsplit kernel and the fp32
+    reference, is deterministic across calls, and leaves the tile counters at zero."""
+    torch.manual_seed(21)
+    m = 200 if bn == 128 else 30
+    n, k = 640, 1024
+    w = torch.randn(1, n, k) * 0.05
+    x = torch.randn(m, k)
+    wq, wsf, wd, npad = _quant_weights(w)
+    xq, xsf, xd = _quant_act(x, _pad_rows(m))
+    ws, sem = _split_ws()
+    if epi == EPI_ARGMAX:
+        ldo = npad // 128
+        mk = lambda: torch.zeros(m, ldo, dtype=torch.int64, device="cuda")  # noqa: E731
+    else:
+        ldo = n
+        dt = torch.bfloat16 if epi == EPI_BF16 else torch.float32
+        mk = lambda: torch.zeros(m, n, device="cuda", dtype=dt)  # noqa: E731
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    args = (wq, wsf, xq, xsf, k, npad, n, 1, m, None, None, None, epi)
+    ref_out = mk()
+    C.gemm_mxf8(*args, ref_out, ldo, None, None, None, err, 0, bn, 1, 0, 0)
+    outs = []
+    for _ in range(2):
+        o = mk()
+        C.gemm_mxf8(*args, o, ldo, None, None, None, err, 0, bn, 1, 0, 0, S, ws, sem)
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    assert int(sem.abs().sum()) == 0
+    assert torch.equal(outs[0], outs[1])
+    if epi == EPI_ARGMAX:
+        assert torch.equal(outs[0] & 0xFFFFFFFF, ref_out & 0xFFFFFFFF)
+    else:
+        torch.testing.assert_close(outs[0].float(), ref_out.float(), rtol=2e-3, atol=2e-3)
+        expect = xd @ wd[0, :n].T
+        torch.testing.assert_close(outs[0].cpu().float(), expect, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("S,bn", [(2, 128), (4, 32)])
+def test_gemm_fix_splits_grouped(C, S, bn):
+    counts = [0, 7, 130, 16, 1, 45]
+    k, n = 512, 256
+    s = _grouped_setup(counts, k, n, seed=8)
+    pre, c = [0], 0
+    for cnt in counts:
+        c += (cnt + bn - 1) // bn
+        pre.append(c)
+    pre = torch.tensor(pre, dtype=torch.int32, device="cuda")
+    ws, sem = _split_ws()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = torch.full((s["rows"], n), float("nan"), device="cuda")
+    C.gemm_mxf8(s["wq"], s["wsf"], s["xq"], s["xsf"], k, s["npad"], n, len(counts), 0, s["cnt"], s["off"], pre,
+                EPI_F32, out, n, None, None, None, err, 0, bn, 1, 0, 0, S, ws, sem)
+    torch.cuda.synchronize()
+    assert err.item() == 0 and int(sem.abs().sum()) == 0
+    out = out.cpu()
+    for gi, cnt in enumerate(counts):
+        if cnt == 0:
+            continue
+        o = s["offsets"][gi]
+        expect = s["xd"][o:o + cnt] @ s["wd"][gi, :n].T
+        torch.testing.assert_close(out[o:o + cnt], expect, rtol=1e-4, atol=1e-3)
+
+
 def test_gemm_scatter_scaled(C):
     counts = [3, 9]
     k, n = 128, 256
@@ -298,6 +369,30 @@ def test_add_rmsnorm_quant(C):
     torch.testing.assert_close(normed.cpu().float(), n_ref, rtol=2e-2, atol=2e-2)
     got = mx.dequantize(q.cpu(), mx.codes_from_atoms(sf.cpu(), rows, h))
     torch.testing.assert_close(got, n_ref, rtol=0.07, atol=0.05)
+
+
+def test_add_rmsnorm_gathered_terms(C):
+    """MoE combine: each row adds weighted, gathered rows of the expert output (negative
+    index = pair handled elsewhere)."""
+    torch.manual_seed(2)
+    rows, h, k1, n_src = 40, 2048, 3, 100
+    res = torch.randn(rows, h).to(torch.bfloat16)
+    y = torch.randn(n_src, h).to(torch.bfloat16)
+    idx = torch.randint(-1, n_src, (rows, k1), dtype=torch.int32)
+    wts = torch.rand(rows, k1)
+    w = (torch.randn(h) * 0.1).to(torch.bfloat16)
+    res_g = res.cuda()
+    q = torch.zeros(128, h, dtype=torch.uint8, device="cuda")
+    sf = torch.zeros(mx.atoms_bytes(128, h), dtype=torch.uint8, device="cuda")
+    C.add_rmsnorm_quant(res_g, y.cuda(), k1, h, 0, w.cuda(), 1.0, 1e-6, rows, None, q, sf, idx.cuda(), wts.cuda())
+    torch.cuda.synchronize()
+    delta = torch.zeros(rows, h)
+    for r in range(rows):
+        for t in range(k1):
+            if idx[r, t] >= 0:
+                delta[r] += wts[r, t] * y[idx[r, t]].float()
+    r_ref, _ = ref.add_rmsnorm(res, delta, w, 1e-6)
+    torch.testing.assert_close(res_g.cpu().float(), r_ref, rtol=1e-2, atol=1e-2)
 
 
 def _gdn_setup(hk, hv, rows, slots_total, seed=0):

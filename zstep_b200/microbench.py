@@ -89,16 +89,20 @@ def time_fn(fn, iters=20, warmup=3, flush=False, reps=8) -> float:
     return (total - base) / reps
 
 
-def build_runner(layers: int, batch: int, ctx: int, experts: int = 256, vocab: int = 248320):
+def build_runner(layers: int, batch: int, ctx: int, experts: int = 256, vocab: int = 248320, tp: int = 1):
+    """Runner on one GPU; with tp > 1 it holds rank 0's shard of a tp-way layout and its
+    reductions stay local (LocalCollectives), so timings are one rank's compute only."""
     from .config import Qwen35Config
     from .models.qwen35 import Qwen35Runner
+    from .parallel.collectives import LocalCollectives
 
     types = tuple("full_attention" if (i + 1) % 4 == 0 else "linear_attention" for i in range(layers))
     cfg = Qwen35Config(num_hidden_layers=layers, layer_types=types, num_experts=experts, vocab_size=vocab)
     page = 16
     pages_per_seq = (ctx + 64 + page - 1) // page
     r = Qwen35Runner(cfg, max_seqs=batch, max_prefill_tokens=batch, num_pages=batch * pages_per_seq + 1,
-                     page_size=page, max_model_len=ctx + 64)
+                     page_size=page, max_model_len=ctx + 64, tp_rank=0, tp_size=tp,
+                     collectives=LocalCollectives() if tp > 1 else None)
     for s in range(batch):
         r.set_pages(s, list(range(1 + s * pages_per_seq, 1 + (s + 1) * pages_per_seq)))
     g = torch.Generator().manual_seed(0)
@@ -109,7 +113,7 @@ def build_runner(layers: int, batch: int, ctx: int, experts: int = 256, vocab: i
 
 def cmd_breakdown(a):
     """Per-op device time of one eager decode step (events around every kernel call)."""
-    r = build_runner(a.layers, a.batch, a.ctx)
+    r = build_runner(a.layers, a.batch, a.ctx, tp=a.tp)
     real = r.C
     events = []
 
@@ -153,7 +157,7 @@ def cmd_breakdown(a):
 
 
 def cmd_step(a):
-    r = build_runner(a.layers, a.batch, a.ctx)
+    r = build_runner(a.layers, a.batch, a.ctx, tp=a.tp)
     if a.eager:
         for _ in range(a.warmup):
             r.decode_forward(a.batch)
@@ -213,7 +217,7 @@ def cmd_gemm(a):
         pre = torch.arange(a.groups + 1, dtype=torch.int32, device="cuda") * ((a.m + bn - 1) // bn)
         fn = lambda: C.gemm_mxf8(pw.q, pw.sf, xq, xsf, a.k, pw.n_pad, a.n, a.groups, 0, cnt, off, pre, 0, out,  # noqa
                                  a.n, None, None, None, None, 0, bn, 1, 0, 1)
-    ms = time_fn(fn, flush=True)
+    ms = time_fn(fn, flush=bool(a.flush))
     pk = peaks()
     flops = 2.0 * a.m * a.n * a.k * a.groups
     bytes_ = a.n * a.k * a.groups * (1 + 1 / 32) + a.m * a.k * a.groups + a.m * a.n * 2 * a.groups
@@ -295,6 +299,8 @@ def main():
     ap.add_argument("--n", type=int, default=2048)
     ap.add_argument("--k", type=int, default=2048)
     ap.add_argument("--groups", type=int, default=1)
+    ap.add_argument("--flush", type=int, default=1, help="evict L2 before every timed call")
+    ap.add_argument("--tp", type=int, default=1, help="time rank 0 of a tp-way layout (no communication)")
     a = ap.parse_args()
     torch.manual_seed(0)
     {"breakdown": cmd_breakdown, "step": cmd_step, "gemm": cmd_gemm, "gdn": cmd_gdn, "attn": cmd_attn,

@@ -29,6 +29,7 @@ forward, 1236 varlen prefill, 1404 graph capture, 484-524 state allocation).
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -243,6 +244,13 @@ class Qwen35Runner:
         self.mid_w = max(self.hv * 128, self.hq * cfg.head_dim)
         b = {}
         b["hidden"] = torch.zeros(R, H, dtype=torch.bfloat16, device=dev)
+        # In-kernel split-K: fp32 partial tiles + per-tile arrival counters (kept zero).
+        b["gemm_ws"] = torch.zeros(8 << 20, dtype=torch.float32, device=dev)
+        b["gemm_sem"] = torch.zeros(16384, dtype=torch.int32, device=dev)
+        self.num_sms = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
+        # In-kernel split-K for dense GEMMs with few output tiles.  Off by default: on the
+        # decode shapes measured so far it did not beat the unsplit kernel.
+        self.use_fix_splits = os.environ.get("ZSTEP_GEMM_FIX_SPLITS", "0") == "1"
         b["xq"] = torch.zeros(Rp, H, dtype=torch.uint8, device=dev)
         b["xsf"] = torch.zeros(mx.atoms_bytes(Rp, H), dtype=torch.uint8, device=dev)
         b["proj"] = torch.zeros(R * max(self.gdn_w, self.qkv_w), dtype=torch.bfloat16, device=dev)
@@ -275,7 +283,11 @@ class Qwen35Runner:
         I = cfg.moe_intermediate_size
         b["act"] = torch.zeros(mg, I, dtype=torch.uint8, device=dev)
         b["act_sf"] = torch.zeros(mx.atoms_bytes(mg, I), dtype=torch.uint8, device=dev)
-        b["pair_out"] = torch.zeros(R * self.k1, H, dtype=torch.bfloat16, device=dev)
+        # Expert outputs in grouped-row order; each token gathers its pairs' rows (pair_src)
+        # weighted by its routing weights (pair_w) inside the residual/all-reduce kernel.
+        b["moe_y"] = torch.zeros(mg, H, dtype=torch.bfloat16, device=dev)
+        b["pair_src"] = torch.zeros(R, self.k1, **i32)
+        b["pair_w"] = torch.zeros(R, self.k1, dtype=torch.float32, device=dev)
         vt = self.lm_head.n_pad // 128
         self.vocab_tiles = vt
         b["lm_keys"] = torch.zeros(self.max_seqs, vt, dtype=torch.int64, device=dev)
@@ -298,12 +310,28 @@ class Qwen35Runner:
               out_sf=None, row_dst=None, row_scale=None, k_splits: int = 1):
         b = self.buf
         if grouped:
+            bn = self._moe_bn(rows)
             self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, w.groups, 0, b["gcount"], b["goff"], b["gpre"],
-                             epi, out, ldo, out_sf, row_dst, row_scale, b["err"], 0, self._moe_bn(rows), 1, 0, 1)
+                             epi, out, ldo, out_sf, row_dst, row_scale, b["err"], 0, bn, 1, 0, 1)
         else:
             bn = 32 if rows <= 32 else 128
+            tiles = -(-rows // bn) * (w.n_pad // 128)
+            fs = self._fix_splits(tiles, tiles, w.k // 128, bn) if (k_splits == 1 and self.use_fix_splits) else 1
             self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, 1, rows, None, None, None, epi, out, ldo,
-                             out_sf, row_dst, row_scale, b["err"], 0, bn, k_splits, rows * ldo, 1)
+                             out_sf, row_dst, row_scale, b["err"], 0, bn, k_splits, rows * ldo, 1,
+                             fs, b["gemm_ws"], b["gemm_sem"])
+
+    def _fix_splits(self, max_tiles: int, items: int, k_tiles: int, bn: int) -> int:
+        """In-kernel split-K factor for a dense GEMM: double while all split items still fit
+        in one wave (the splits of a tile wait for each other), each split keeps >= 2 K
+        tiles, and the workspace holds every tile.  A single CTA streams only ~100 GB/s,
+        so a GEMM with few output tiles needs the extra CTAs to approach HBM bandwidth."""
+        s = 1
+        cap = self.buf["gemm_ws"].numel()
+        while (items * s * 2 <= self.num_sms and s * 2 <= 8 and k_tiles % (s * 2) == 0 and k_tiles // (s * 2) >= 2
+               and max_tiles * s * 2 * 128 * bn <= cap and max_tiles <= self.buf["gemm_sem"].numel()):
+            s *= 2
+        return s
 
     def _moe_bn(self, rows: int) -> int:
         """Token chunk of the grouped expert GEMMs: 32 while the average expert sees a few
@@ -342,15 +370,18 @@ class Qwen35Runner:
         self._row_parallel_reduce(self.buf["delta_f32"], rows, s, norm_w, rows * H, H)
 
     def _row_parallel_reduce(self, delta_rows: torch.Tensor, rows: int, n_terms: int, norm_w, term_stride: int,
-                             row_stride: int):
-        """hidden += sum of delta terms (all-reduced across tp ranks), then RMSNorm -> xq."""
+                             row_stride: int, term_index=None, term_scale=None):
+        """hidden += sum of delta terms (all-reduced across tp ranks), then RMSNorm -> xq.
+        With ``term_index`` [rows, n_terms] the terms are gathered rows of delta (negative:
+        not produced on this rank), scaled by ``term_scale``."""
         b, H = self.buf, self.cfg.hidden_size
         if self.tp > 1:
             self.coll.allreduce_add_rmsnorm(delta_rows, n_terms, row_stride, term_stride, b["hidden"], norm_w,
-                                            self.eps, rows, b["xq"], b["xsf"])
+                                            self.eps, rows, b["xq"], b["xsf"], term_index=term_index,
+                                            term_scale=term_scale)
             return
         self.C.add_rmsnorm_quant(b["hidden"], delta_rows, n_terms, row_stride, term_stride, norm_w, 1.0, self.eps,
-                                 rows, None, b["xq"], b["xsf"])
+                                 rows, None, b["xq"], b["xsf"], term_index, term_scale)
 
     def _layers(self, rows: int, decode: bool, num_seqs: int = 0, ckpt=None) -> None:
         cfg, C, b = self.cfg, self.C, self.buf
@@ -388,25 +419,24 @@ class Qwen35Runner:
                 self._proj_out(L["o_proj"], midq, b["midsf"], rows, L["post_norm"])
             self._moe(L, rows)
             next_w = self.layers[li + 1]["input_norm"] if li + 1 < len(self.layers) else self.final_norm
-            self._row_parallel_reduce(b["pair_out"], rows, self.k1, next_w, H, self.k1 * H)
+            self._row_parallel_reduce(b["moe_y"], rows, self.k1, next_w, 0, H, term_index=b["pair_src"],
+                                      term_scale=b["pair_w"])
 
     def _moe(self, L, rows: int) -> None:
         cfg, C, b = self.cfg, self.C, self.buf
         E = cfg.num_experts
         nr = L["router"].n_pad
-        s = self._k_splits(L["router"], rows, cap=4)  # the router kernel re-reads every split
+        # Router logits: split-K partials summed by the routing kernel (or one term when the
+        # GEMM reduces its splits in-kernel).
+        s = 1 if self.use_fix_splits else self._k_splits(L["router"], rows, cap=4)
         self._gemm(L["router"], b["xq"], b["xsf"], rows, b["logits"], nr, EPI_F32, k_splits=s)
         C.moe_route(b["logits"], rows, E, self.top_k, cfg.norm_topk_prob, 0, None, 1, 1, 1.0, E,
                     self.e_begin, self.e_begin + self.e_local, True, b["topk_ids"], b["topk_w"], b["gcount"],
                     b["goff"], b["gpre"], b["pair_slot"], b["row_dst"], b["row_scale"], b["xq"], b["xsf"], b["xg"],
-                    b["xg_sf"], b["err"], nr, s, rows * nr, self._moe_bn(rows))
-        if self.tp > 1:
-            # Pair rows of experts owned by other ranks must not leak stale values.
-            b["pair_out"][: rows * self.k1].zero_()
+                    b["xg_sf"], b["err"], nr, s, rows * nr, self._moe_bn(rows), b["pair_src"], b["pair_w"])
         I = cfg.moe_intermediate_size
         self._gemm(L["gate_up"], b["xg"], b["xg_sf"], rows, b["act"], I, EPI_SILU, grouped=True, out_sf=b["act_sf"])
-        self._gemm(L["down"], b["act"], b["act_sf"], rows, b["pair_out"], cfg.hidden_size, EPI_SCATTER, grouped=True,
-                   row_dst=b["row_dst"], row_scale=b["row_scale"])
+        self._gemm(L["down"], b["act"], b["act_sf"], rows, b["moe_y"], cfg.hidden_size, EPI_BF16, grouped=True)
 
     def _lm_head_argmax(self, rows: int, xq=None, xsf=None) -> None:
         b = self.buf

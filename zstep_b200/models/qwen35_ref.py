@@ -212,6 +212,7 @@ class Qwen35Reference:
         terms.append((L["sgate"], L["sup"], L["sdown"], torch.sigmoid(logits[self.E]).item()))
         for wg, wu, wd, wt in terms:
             h = F.silu(wg @ xq) * (wu @ xq)
-            o = (wd @ self._q(h)) * wt
-            out = out + self._bf(o)
+            # Expert output rounded to bf16, then weighted (the GPU combine gathers the
+            # bf16 expert rows and applies the routing weight in fp32).
+            out = out + self._bf(wd @ self._q(h)) * wt
         return out

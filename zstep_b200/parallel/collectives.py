@@ -12,7 +12,9 @@ Two implementations share one interface:
 
 ``allreduce_add_rmsnorm`` takes the local contribution as ``n_terms`` partial terms
 (split-K partials or MoE pair rows) addressed as ``delta[row*row_stride + t*term_stride
-+ col]``; terms are summed in index order before the cross-rank reduction.
++ col]``, or gathered (``term_index``/``term_scale``: the MoE expert outputs of each
+token, weighted by its routing weights); terms are summed in index order before the
+cross-rank reduction.
 
 Reference parity: the reference's host-SHM all-reduce + add + RMSNorm
 (worker/zstep_worker/kernels_sm120/shm_allreduce.py:437,514) and the TP=8 top-2
@@ -28,12 +30,26 @@ _SIGN = -(1 << 63)  # xor mask mapping unsigned key order onto signed int64 orde
 
 
 def local_term_sum(delta: torch.Tensor, rows: int, hidden: int, n_terms: int, row_stride: int,
-                   term_stride: int) -> torch.Tensor:
-    """Sum of the local partial terms as fp32 [rows, hidden] (fixed term order)."""
-    view = torch.as_strided(delta, (n_terms, rows, hidden), (term_stride, row_stride, 1))
-    acc = view[0].float()
-    for t in range(1, n_terms):
-        acc = acc + view[t].float()
+                   term_stride: int, term_index: torch.Tensor | None = None,
+                   term_scale: torch.Tensor | None = None) -> torch.Tensor:
+    """Sum of the local partial terms as fp32 [rows, hidden] in term order.  With
+    ``term_index`` term t of row r is row ``term_index[r, t]`` of delta (negative:
+    skipped), scaled by ``term_scale[r, t]`` when given."""
+    acc = None
+    if term_index is None:
+        view = torch.as_strided(delta, (n_terms, rows, hidden), (term_stride, row_stride, 1))
+    else:
+        n_src = (delta.numel() - hidden) // row_stride + 1
+        src = torch.as_strided(delta, (n_src, hidden), (row_stride, 1))
+    for t in range(n_terms):
+        if term_index is None:
+            v = view[t].float()
+        else:
+            idx = term_index[:rows, t].long()
+            v = src[idx.clamp(min=0)].float() * (idx >= 0).unsqueeze(1)
+        if term_scale is not None:
+            v = v * term_scale[:rows, t:t + 1]
+        acc = v if acc is None else acc + v
     return acc
 
 
@@ -48,9 +64,10 @@ class NcclCollectives:
         self.device = device
 
     def allreduce_add_rmsnorm(self, delta, n_terms: int, row_stride: int, term_stride: int, hidden_buf,
-                              norm_w, eps: float, rows: int, xq, xsf) -> None:
+                              norm_w, eps: float, rows: int, xq, xsf, term_index=None, term_scale=None) -> None:
         H = hidden_buf.shape[-1]
-        acc = local_term_sum(delta, rows, H, n_terms, row_stride, term_stride).to(torch.bfloat16)
+        acc = local_term_sum(delta, rows, H, n_terms, row_stride, term_stride, term_index,
+                             term_scale).to(torch.bfloat16)
         dist.all_reduce(acc, group=self.group)
         self.C.add_rmsnorm_quant(hidden_buf, acc, 1, H, H, norm_w, 1.0, eps, rows, None, xq, xsf)
 
@@ -68,3 +85,23 @@ class NcclCollectives:
         hi = (k >> 32) & 0xFFFFFFFF
         bits = torch.where(hi >= 0x80000000, hi & 0x7FFFFFFF, (~hi) & 0xFFFFFFFF).to(torch.int32)
         out_vals[:rows] = bits.view(torch.float32)
+
+
+class LocalCollectives:
+    """Single-process stand-in with the collective interface: every reduction sees only this
+    rank's own contribution.  Used to time one rank's compute of a tensor-parallel layout on
+    one GPU (the numbers then exclude communication); never for real outputs."""
+
+    def __init__(self, device=None):
+        from ..ops import _ext
+
+        self.C = _ext.load()
+        self.device = device
+
+    def allreduce_add_rmsnorm(self, delta, n_terms: int, row_stride: int, term_stride: int, hidden_buf,
+                              norm_w, eps: float, rows: int, xq, xsf, term_index=None, term_scale=None) -> None:
+        self.C.add_rmsnorm_quant(hidden_buf, delta, n_terms, row_stride, term_stride, norm_w, 1.0, eps, rows, None,
+                                 xq, xsf, term_index, term_scale)
+
+    def argmax_allreduce(self, keys, rows: int, tiles: int, id_offset: int, out_ids, out_vals) -> None:
+        self.C.argmax_reduce(keys, rows, tiles, out_ids, out_vals, None)

@@ -97,7 +97,7 @@ class FusedCollectives:
 
     # ---------------------------------------------------------------- ops
     def allreduce_add_rmsnorm(self, delta, n_terms: int, row_stride: int, term_stride: int, hidden_buf,
-                              norm_w, eps: float, rows: int, xq, xsf) -> None:
+                              norm_w, eps: float, rows: int, xq, xsf, term_index=None, term_scale=None) -> None:
         """hidden_buf[:rows] += sum over ranks of the local term sums; then RMSNorm(norm_w)
         -> MXFP8 (xq, xsf).  Every rank ends with the same bf16 residual stream."""
         H = hidden_buf.shape[-1]
@@ -105,7 +105,7 @@ class FusedCollectives:
             raise ValueError(f"fused all-reduce reserved for {self.max_rows}x{self.hidden}, got {rows}x{H}")
         self.C.fused_allreduce_norm(self.rank, self.world, delta, n_terms, row_stride, term_stride, self.part_ptrs,
                                     self.out_ptrs, self.flag_ptrs, self.epoch[0:1], self.grid, hidden_buf, norm_w,
-                                    1.0, eps, rows, None, xq, xsf, self.err)
+                                    1.0, eps, rows, None, xq, xsf, self.err, term_index, term_scale)
 
     def argmax_allreduce(self, keys, rows: int, tiles: int, id_offset: int, out_ids, out_vals) -> None:
         """Global greedy token per row from per-tile packed keys of this rank's vocab shard."""
