@@ -1,0 +1,653 @@
+// `zstep` command line: `zstep serve` (OpenAI-compatible HTTP/SSE server) and
+// `zstep run` (offline generation, greedy parity check, benchmark tiers).
+//
+// The master is this process; GPU (or CPU) workers are `python -m
+// zstep_b200.runtime.worker` processes spawned by the shared-memory coordinator, one per
+// tensor-parallel rank.  `--mock` replaces the workers by a deterministic scripted
+// backend (no GPU, no Python) for API and control-plane testing.
+//
+// Reference parity: crates/zs-server/src/serve/cli.rs (SERVE_USAGE :6-49,
+// validate_known_flags :143, parse_with_env :273, engine_config :622),
+// crates/zs-server/src/lib.rs (USAGE :176, run_greedy_verification :417,
+// run_engine :696), crates/zs-scheduler/src/serving/report.rs (tiers, provenance).
+#include <limits.h>
+#include <signal.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+#include <unistd.h>
+
+#include <chrono>
+#include <cmath>
+#include <fstream>
+#include <map>
+#include <set>
+#include <sstream>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "coordinator.h"
+#include "engine.h"
+#include "http_server.h"
+#include "json.h"
+#include "serve_loop.h"
+#include "shm.h"
+#include "tokenizer.h"
+
+using namespace zs;
+
+extern char** environ;
+
+namespace {
+
+const char* kServeUsage =
+    "zstep serve - persistent OpenAI-compatible HTTP/SSE engine\n"
+    "Usage: zstep serve --model-dir <PATH> [OPTIONS]\n"
+    "  --model-dir PATH             Model directory (config.json, tokenizer.json, weights)\n"
+    "  --model NAME                 Worker model: preset name or directory (default: --model-dir)\n"
+    "  --served-model-name ID       Model id on /v1/models (default: directory basename)\n"
+    "  --host IP                    Bind address (default 127.0.0.1)\n"
+    "  --port PORT                  Bind port (default 43537; 0 = any free port)\n"
+    "  --api-key TOKEN              Bearer token for /v1/*, /admin/*, /metrics (or ZSTEP_API_KEY)\n"
+    "  --admin-port PORT            Loopback-only port for probes, /metrics and /admin\n"
+    "  --allow-remote-metrics | --no-allow-remote-metrics\n"
+    "  --world-size N               Tensor-parallel workers 1..8 (default 1)\n"
+    "  --device cuda|cpu            Worker device (default cuda)\n"
+    "  --max-model-len N            Max prompt + output tokens (default 32768)\n"
+    "  --max-seqs N                 Max concurrent sequences (default 128)\n"
+    "  --max-step-tokens N          Max tokens per step (default 4096)\n"
+    "  --max-prefill-chunk N        Max prefill chunk (default 2048)\n"
+    "  --page-block-tokens N        KV page size (default 16)\n"
+    "  --num-kv-pages N             KV pages per GPU (default 32768)\n"
+    "  --tokenizer-mode auto|chatml|deepseek\n"
+    "  --enable-prefix-caching | --no-enable-prefix-caching   (default on)\n"
+    "  --apc-node-pages N           Pages per prefix-cache node (default 8)\n"
+    "  --num-ckpt-slots N           Recurrent-state checkpoint slots (default 64 with APC)\n"
+    "  --max-waiting-requests N     Bounded waiting queue (default 1024)\n"
+    "  --prefill-policy srpt|fifo   (default srpt)\n"
+    "  --drain-timeout-secs N       SIGTERM drain grace period (default 30)\n"
+    "  --python PATH                Python for workers (default: python3)\n"
+    "  --worker-root PATH           Directory containing the zstep_b200 package\n"
+    "  --ready-timeout-secs N       Worker start-up timeout (default 1800)\n"
+    "  --step-timeout-secs N        Per-step timeout (default 300)\n"
+    "  --speculative-method none|ngram|mtp\n"
+    "  --num-speculative-tokens K   Draft tokens per verify step 1..7\n"
+    "  --mock                       Scripted backend instead of workers (no GPU)\n";
+
+const char* kRunUsage =
+    "zstep run - offline generation / parity / benchmark\n"
+    "Usage: zstep run --model-dir <PATH> [OPTIONS]\n"
+    "  (all engine/worker options of `zstep serve`, plus)\n"
+    "  --prompt-ids 1,2,3           Generate from these token ids\n"
+    "  --prompt TEXT                Generate from this text (chat template applied)\n"
+    "  --max-tokens N               Tokens to generate (default 32)\n"
+    "  --verify-greedy-json PATH    {\"prompts\": [[ids]], \"expected\": [[ids]]}: exit 1 on mismatch\n"
+    "  --bench-tiers SPEC[,SPEC]    label:concurrency:prompts:input_len:output_len\n"
+    "  --bench-repeats N            Interleaved repeats per tier (default 1)\n"
+    "  --seed N                     Prompt seed (default 0)\n";
+
+struct Args {
+  std::map<std::string, std::string> kv;
+  std::set<std::string> flags;
+  bool has(const std::string& k) const { return kv.count(k) || flags.count(k); }
+  std::string get(const std::string& k, const std::string& d = "") const {
+    auto it = kv.find(k);
+    return it == kv.end() ? d : it->second;
+  }
+  long num(const std::string& k, long d) const {
+    auto it = kv.find(k);
+    if (it == kv.end()) return d;
+    char* end = nullptr;
+    const long v = strtol(it->second.c_str(), &end, 10);
+    if (end == it->second.c_str() || *end) {
+      fprintf(stderr, "zstep: --%s expects an integer, got `%s`\n", k.c_str(), it->second.c_str());
+      exit(2);
+    }
+    return v;
+  }
+};
+
+const std::set<std::string> kValueFlags = {
+    "model-dir", "model", "served-model-name", "host", "port", "api-key", "admin-port", "world-size", "device",
+    "max-model-len", "max-seqs", "max-step-tokens", "max-prefill-chunk", "page-block-tokens", "num-kv-pages",
+    "tokenizer-mode", "apc-node-pages", "num-ckpt-slots", "max-waiting-requests", "prefill-policy",
+    "drain-timeout-secs", "python", "worker-root", "ready-timeout-secs", "step-timeout-secs", "speculative-method",
+    "num-speculative-tokens", "prompt-ids", "prompt", "max-tokens", "verify-greedy-json", "bench-tiers",
+    "bench-repeats", "seed"};
+const std::set<std::string> kBoolFlags = {"allow-remote-metrics", "no-allow-remote-metrics", "enable-prefix-caching",
+                                          "no-enable-prefix-caching", "mock", "help"};
+
+bool parse_args(int argc, char** argv, int start, Args* a, std::string* err) {
+  for (int i = start; i < argc; ++i) {
+    std::string s = argv[i];
+    if (s.rfind("--", 0) != 0) {
+      *err = "unexpected argument `" + s + "`";
+      return false;
+    }
+    s = s.substr(2);
+    std::string val;
+    const size_t eq = s.find('=');
+    const bool inline_val = eq != std::string::npos;
+    if (inline_val) {
+      val = s.substr(eq + 1);
+      s = s.substr(0, eq);
+    }
+    if (kBoolFlags.count(s)) {
+      if (inline_val) {
+        *err = "--" + s + " takes no value";
+        return false;
+      }
+      a->flags.insert(s);
+    } else if (kValueFlags.count(s)) {
+      if (!inline_val) {
+        if (i + 1 >= argc) {
+          *err = "--" + s + " needs a value";
+          return false;
+        }
+        val = argv[++i];
+      }
+      a->kv[s] = val;
+    } else {
+      *err = "unknown flag --" + s;
+      return false;
+    }
+  }
+  return true;
+}
+
+std::string basename_of(const std::string& p) {
+  std::string s = p;
+  while (!s.empty() && s.back() == '/') s.pop_back();
+  const size_t k = s.rfind('/');
+  return k == std::string::npos ? s : s.substr(k + 1);
+}
+
+std::string self_root() {
+  char buf[PATH_MAX];
+  const ssize_t n = readlink("/proc/self/exe", buf, sizeof(buf) - 1);
+  if (n <= 0) return ".";
+  buf[n] = 0;
+  std::string p = buf;  // <root>/zstep_b200/bin/zstep
+  for (int k = 0; k < 3; ++k) {
+    const size_t s = p.rfind('/');
+    if (s == std::string::npos) return ".";
+    p = p.substr(0, s);
+  }
+  return p.empty() ? "/" : p;
+}
+
+struct Built {
+  std::shared_ptr<engine::Engine> engine;
+  std::shared_ptr<Coordinator> coord;
+  tok::Tokenizer tokenizer;
+  bool has_tokenizer = false;
+  engine::Config cfg;
+};
+
+// Engine + backend from the common flags.
+bool build_engine(const Args& a, Built* b, std::string* err) {
+  const std::string dir = a.get("model-dir");
+  if (dir.empty()) {
+    *err = "--model-dir is required";
+    return false;
+  }
+  if (b->tokenizer.load_dir(dir, err)) {
+    b->has_tokenizer = true;
+  } else if (!a.has("prompt-ids") && !a.has("bench-tiers") && !a.has("verify-greedy-json")) {
+    return false;  // text serving needs the tokenizer
+  }
+  err->clear();
+  engine::Config& c = b->cfg;
+  c.max_seqs = (uint32_t)a.num("max-seqs", 128);
+  c.max_step_tokens = (uint32_t)a.num("max-step-tokens", 4096);
+  c.max_prefill_chunk = (uint32_t)a.num("max-prefill-chunk", 2048);
+  c.page_size = (uint32_t)a.num("page-block-tokens", 16);
+  c.num_pages = (uint32_t)a.num("num-kv-pages", 32768);
+  c.max_model_len = (uint32_t)a.num("max-model-len", 32768);
+  c.prefix_caching = !a.has("no-enable-prefix-caching");
+  c.pages_per_node = (uint32_t)a.num("apc-node-pages", 8);
+  c.recurrent_state = true;
+  c.num_ckpt_slots = (uint32_t)a.num("num-ckpt-slots", c.prefix_caching ? 64 : 0);
+  c.prefill_policy = a.get("prefill-policy", "srpt");
+  c.max_waiting = (uint32_t)a.num("max-waiting-requests", 1024);
+  c.spec_method = a.get("speculative-method", "none");
+  c.num_spec_tokens = (uint32_t)a.num("num-speculative-tokens", c.spec_method == "none" ? 0 : 3);
+  if (c.max_step_tokens < c.max_seqs) {
+    *err = "--max-step-tokens must be >= --max-seqs";
+    return false;
+  }
+  if (c.prefill_policy != "srpt" && c.prefill_policy != "fifo") {
+    *err = "--prefill-policy must be srpt or fifo";
+    return false;
+  }
+  if (c.spec_method != "none" && c.spec_method != "ngram" && c.spec_method != "mtp") {
+    *err = "--speculative-method must be none, ngram or mtp";
+    return false;
+  }
+  if (c.spec_method != "none" && (c.num_spec_tokens < 1 || c.num_spec_tokens > 7)) {
+    *err = "--num-speculative-tokens must be within 1..7";
+    return false;
+  }
+  const long world = a.num("world-size", 1);
+  if (world < 1 || world > 8) {
+    *err = "--world-size must be within 1..8";
+    return false;
+  }
+  std::shared_ptr<engine::Backend> backend;
+  if (a.has("mock")) {
+    const int32_t vocab = b->has_tokenizer ? (int32_t)b->tokenizer.vocab_size() : 1000;
+    const int32_t eos = b->has_tokenizer && !b->tokenizer.eos_ids().empty() ? b->tokenizer.eos_ids()[0] : -1;
+    backend = serve::make_mock_backend(0, std::max<int32_t>(2, std::min<int32_t>(vocab, 256)), eos, 0);
+  } else {
+    CoordinatorConfig cc;
+    cc.geo.world_size = (uint32_t)world;
+    cc.geo.max_seqs = c.max_seqs;
+    cc.geo.max_step_tokens = c.max_step_tokens;
+    cc.geo.page_size = c.page_size;
+    cc.geo.max_pages_per_seq = (c.max_model_len + c.page_size - 1) / c.page_size;
+    cc.geo.vocab_size = 0;
+    const std::string py = a.get("python", "python3");
+    cc.worker_argv = {py,
+                      "-m",
+                      "zstep_b200.runtime.worker",
+                      "--model",
+                      a.get("model", dir),
+                      "--device",
+                      a.get("device", "cuda"),
+                      "--num-pages",
+                      std::to_string(c.num_pages),
+                      "--max-model-len",
+                      std::to_string(c.max_model_len),
+                      "--num-ckpt-slots",
+                      std::to_string(c.num_ckpt_slots),
+                      "--spec-method",
+                      c.spec_method,
+                      "--num-spec-tokens",
+                      std::to_string(c.num_spec_tokens)};
+    const std::string root = a.get("worker-root", self_root());
+    const char* pp = getenv("PYTHONPATH");
+    cc.env["PYTHONPATH"] = root + (pp ? std::string(":") + pp : std::string());
+    cc.env["MASTER_ADDR"] = "127.0.0.1";
+    cc.env["MASTER_PORT"] = std::to_string(29500 + (getpid() % 20000));
+    cc.ready_timeout_ms = (int)a.num("ready-timeout-secs", 1800) * 1000;
+    cc.step_timeout_ms = (int)a.num("step-timeout-secs", 300) * 1000;
+    b->coord = std::make_shared<Coordinator>(cc);
+    b->coord->launch();
+    if (!b->coord->error().empty()) {
+      *err = "worker start-up failed: " + b->coord->error();
+      return false;
+    }
+    backend = b->coord;
+  }
+  b->engine = std::make_shared<engine::Engine>(c, backend);
+  return true;
+}
+
+volatile sig_atomic_t g_signal = 0;
+void on_signal(int sig) { g_signal = sig; }
+
+// ------------------------------------------------------------------ serve
+int cmd_serve(const Args& a) {
+  if (a.has("help")) {
+    fputs(kServeUsage, stdout);
+    return 0;
+  }
+  Built b;
+  std::string err;
+  if (!build_engine(a, &b, &err)) {
+    fprintf(stderr, "zstep serve: %s\n\n%s", err.c_str(), kServeUsage);
+    return 2;
+  }
+  if (!b.has_tokenizer) {
+    fprintf(stderr, "zstep serve: tokenizer.json not found in --model-dir\n");
+    return 2;
+  }
+  serve::ServeLoop loop(b.engine, b.coord, b.cfg.max_waiting);
+  http::ServerConfig sc;
+  sc.host = a.get("host", "127.0.0.1");
+  sc.port = (int)a.num("port", 43537);
+  sc.admin_port = a.has("admin-port") ? (int)a.num("admin-port", 0) : -1;
+  sc.api_key = a.get("api-key", getenv("ZSTEP_API_KEY") ? getenv("ZSTEP_API_KEY") : "");
+  sc.served_model_name = a.get("served-model-name", basename_of(a.get("model-dir")));
+  sc.max_model_len = b.cfg.max_model_len;
+  const char* arm = getenv("ZSTEP_ALLOW_REMOTE_METRICS");
+  sc.allow_remote_metrics = !(a.has("no-allow-remote-metrics") || (arm && std::string(arm) == "0"));
+  const std::string mode = a.get("tokenizer-mode", "auto");
+  sc.template_format = mode == "deepseek" ? tok::TemplateFormat::kDeepSeek : tok::TemplateFormat::kChatML;
+  if (mode == "auto" && b.tokenizer.token_id("<｜User｜>") >= 0) sc.template_format = tok::TemplateFormat::kDeepSeek;
+  http::HttpServer server(sc, &loop, &b.tokenizer);
+  if (!server.start(&err)) {
+    fprintf(stderr, "zstep serve: %s\n", err.c_str());
+    return 1;
+  }
+  loop.start();
+  signal(SIGTERM, on_signal);
+  signal(SIGINT, on_signal);
+  signal(SIGPIPE, SIG_IGN);
+  fprintf(stderr, "zstep serve: listening on %s:%d (model %s)\n", sc.host.c_str(), server.port(),
+          sc.served_model_name.c_str());
+  printf("{\"event\": \"ready\", \"port\": %d, \"admin_port\": %d}\n", server.port(), server.admin_port());
+  fflush(stdout);
+  while (!g_signal && loop.state() != serve::EngineState::kFaulted) usleep(50000);
+  // Drain: stop admitting, let in-flight requests finish within the grace period.
+  server.request_drain();
+  const long grace_ms = a.num("drain-timeout-secs", 30) * 1000;
+  for (long t = 0; t < grace_ms && !loop.idle(); t += 50) usleep(50000);
+  server.stop();
+  loop.shutdown();
+  if (b.coord) b.coord->shutdown();
+  return loop.state() == serve::EngineState::kFaulted ? 1 : 0;
+}
+
+// ------------------------------------------------------------------ run
+std::vector<int32_t> parse_ids(const std::string& s) {
+  std::vector<int32_t> out;
+  std::stringstream ss(s);
+  std::string tok;
+  while (std::getline(ss, tok, ',')) {
+    if (!tok.empty()) out.push_back((int32_t)strtol(tok.c_str(), nullptr, 10));
+  }
+  return out;
+}
+
+// Runs requests to completion; returns tokens per request id.
+std::map<uint64_t, std::vector<int32_t>> drive(engine::Engine& e, std::string* err) {
+  std::map<uint64_t, std::vector<int32_t>> out;
+  while (e.has_work()) {
+    for (auto& ev : e.step()) out[ev.request_id].insert(out[ev.request_id].end(), ev.tokens.begin(), ev.tokens.end());
+    if (e.poisoned()) {
+      *err = e.error();
+      break;
+    }
+  }
+  return out;
+}
+
+std::string git_sha(const std::string& root) {
+  if (const char* e = getenv("ZSTEP_GIT_SHA")) return e;
+  std::ifstream h(root + "/.git/HEAD");
+  std::string line;
+  if (!std::getline(h, line)) return "unknown";
+  if (line.rfind("ref: ", 0) == 0) {
+    std::ifstream r(root + "/.git/" + line.substr(5));
+    std::string sha;
+    if (std::getline(r, sha)) return sha;
+    return "unknown";
+  }
+  return line;
+}
+
+json::Value provenance(const std::string& root) {
+  json::Value p = json::Value::object();
+  p.set("git_sha", git_sha(root));
+  p.set("unix_time", (int64_t)time(nullptr));
+  char host[256] = {0};
+  gethostname(host, sizeof(host) - 1);
+  p.set("hostname", std::string(host));
+  json::Value env = json::Value::object();
+  for (char** e = environ; *e; ++e) {
+    std::string kv = *e;
+    if (kv.rfind("ZSTEP_", 0) != 0 && kv.rfind("NCCL_", 0) != 0 && kv.rfind("CUDA_", 0) != 0) continue;
+    const size_t eq = kv.find('=');
+    std::string k = kv.substr(0, eq), v = eq == std::string::npos ? "" : kv.substr(eq + 1);
+    std::string up = k;
+    for (auto& ch : up) ch = (char)toupper(ch);
+    if (up.find("KEY") != std::string::npos || up.find("TOKEN") != std::string::npos ||
+        up.find("SECRET") != std::string::npos || up.find("PASSWORD") != std::string::npos)
+      v = "<redacted>";
+    env.set(k, v);
+  }
+  p.set("env", env);
+  return p;
+}
+
+double mean_of(const std::vector<double>& v) {
+  double s = 0;
+  for (double x : v) s += x;
+  return v.empty() ? 0 : s / v.size();
+}
+double std_of(const std::vector<double>& v) {
+  if (v.size() < 2) return 0;
+  const double m = mean_of(v);
+  double s = 0;
+  for (double x : v) s += (x - m) * (x - m);
+  return std::sqrt(s / (v.size() - 1));
+}
+double pct(std::vector<double> v, double q) {
+  if (v.empty()) return 0;
+  std::sort(v.begin(), v.end());
+  return v[std::min(v.size() - 1, (size_t)(q * (v.size() - 1) + 0.5))];
+}
+
+struct Tier {
+  std::string label;
+  int conc = 1, prompts = 1, in = 128, out = 128;
+};
+
+json::Value run_tier(engine::Engine& e, const Tier& t, uint64_t seed, int32_t vocab, std::string* err) {
+  auto prompts = engine::random_prompts(seed, (size_t)t.prompts, (size_t)t.in, 10, std::max<int32_t>(11, vocab - 10));
+  std::map<uint64_t, double> t_submit, t_first, t_last;
+  std::map<uint64_t, uint32_t> produced;
+  size_t next = 0, done = 0;
+  uint64_t id_base = seed << 20;
+  const double t0 = (double)monotonic_ns() * 1e-9;
+  uint64_t gen_tokens = 0;
+  while (done < prompts.size()) {
+    while (next < prompts.size() && (int)(next - done) < t.conc) {
+      engine::Request r;
+      r.id = id_base + next;
+      r.prompt = prompts[next];
+      r.max_tokens = (uint32_t)t.out;
+      r.ignore_eos = true;
+      if (!e.submit(r)) break;
+      t_submit[r.id] = (double)monotonic_ns() * 1e-9;
+      ++next;
+    }
+    auto evs = e.step();
+    if (e.poisoned()) {
+      *err = e.error();
+      break;
+    }
+    const double now = (double)monotonic_ns() * 1e-9;
+    for (auto& ev : evs) {
+      if (!ev.tokens.empty()) {
+        if (!t_first.count(ev.request_id)) t_first[ev.request_id] = now;
+        t_last[ev.request_id] = now;
+        produced[ev.request_id] += (uint32_t)ev.tokens.size();
+        gen_tokens += ev.tokens.size();
+      }
+      if (ev.finish != engine::Finish::kNone) ++done;
+    }
+  }
+  const double wall = (double)monotonic_ns() * 1e-9 - t0;
+  std::vector<double> ttft, tpot;
+  for (auto& kv : t_first) {
+    ttft.push_back((kv.second - t_submit[kv.first]) * 1e3);
+    const uint32_t n = produced[kv.first];
+    if (n > 1) tpot.push_back((t_last[kv.first] - kv.second) * 1e3 / (n - 1));
+  }
+  json::Value r = json::Value::object();
+  r.set("label", t.label);
+  r.set("concurrency", t.conc);
+  r.set("num_prompts", t.prompts);
+  r.set("input_len", t.in);
+  r.set("output_len", t.out);
+  r.set("wall_s", wall);
+  r.set("output_tok_s", gen_tokens / std::max(wall, 1e-9));
+  r.set("total_tok_s", (gen_tokens + (double)t.prompts * t.in) / std::max(wall, 1e-9));
+  r.set("mean_ttft_ms", mean_of(ttft));
+  r.set("p50_ttft_ms", pct(ttft, 0.5));
+  r.set("p99_ttft_ms", pct(ttft, 0.99));
+  r.set("mean_tpot_ms", mean_of(tpot));
+  r.set("p50_tpot_ms", pct(tpot, 0.5));
+  return r;
+}
+
+int cmd_run(const Args& a) {
+  if (a.has("help")) {
+    fputs(kRunUsage, stdout);
+    return 0;
+  }
+  Built b;
+  std::string err;
+  if (!build_engine(a, &b, &err)) {
+    fprintf(stderr, "zstep run: %s\n\n%s", err.c_str(), kRunUsage);
+    return 2;
+  }
+  signal(SIGPIPE, SIG_IGN);
+  int rc = 0;
+  engine::Engine& e = *b.engine;
+  const std::string root = a.get("worker-root", self_root());
+  if (a.has("verify-greedy-json")) {
+    std::ifstream f(a.get("verify-greedy-json"));
+    std::stringstream ss;
+    ss << f.rdbuf();
+    json::Value v;
+    if (!json::parse(ss.str(), &v, &err)) {
+      fprintf(stderr, "zstep run: bad --verify-greedy-json: %s\n", err.c_str());
+      return 2;
+    }
+    const auto& prompts = v.get("prompts");
+    const auto& expected = v.get("expected");
+    for (size_t i = 0; i < prompts.size(); ++i) {
+      engine::Request r;
+      r.id = i + 1;
+      for (const auto& t : prompts[i].items()) r.prompt.push_back((int32_t)t.as_int());
+      r.max_tokens = (uint32_t)(i < expected.size() ? expected[i].size() : a.num("max-tokens", 32));
+      r.ignore_eos = true;
+      e.submit(r);
+    }
+    auto out = drive(e, &err);
+    int mismatches = 0;
+    json::Value rep = json::Value::array();
+    for (size_t i = 0; i < prompts.size(); ++i) {
+      std::vector<int32_t> exp;
+      if (i < expected.size())
+        for (const auto& t : expected[i].items()) exp.push_back((int32_t)t.as_int());
+      const auto& got = out[i + 1];
+      const bool ok = got == exp;
+      mismatches += ok ? 0 : 1;
+      json::Value r = json::Value::object();
+      r.set("index", (int64_t)i);
+      r.set("match", ok);
+      json::Value g = json::Value::array();
+      for (int32_t t : got) g.push(t);
+      r.set("tokens", g);
+      rep.push(r);
+    }
+    json::Value root_v = json::Value::object();
+    root_v.set("verify_greedy", rep);
+    root_v.set("mismatches", mismatches);
+    printf("%s\n", root_v.dump().c_str());
+    rc = (mismatches || !err.empty()) ? 1 : 0;
+  } else if (a.has("bench-tiers")) {
+    std::vector<Tier> tiers;
+    std::stringstream ss(a.get("bench-tiers"));
+    std::string spec;
+    while (std::getline(ss, spec, ',')) {
+      std::vector<std::string> f;
+      std::stringstream s2(spec);
+      std::string part;
+      while (std::getline(s2, part, ':')) f.push_back(part);
+      if (f.size() != 5) {
+        fprintf(stderr, "zstep run: tier `%s` is not label:conc:prompts:in:out\n", spec.c_str());
+        return 2;
+      }
+      Tier t{f[0], atoi(f[1].c_str()), atoi(f[2].c_str()), atoi(f[3].c_str()), atoi(f[4].c_str())};
+      if (t.conc < 1 || t.prompts < 1 || t.in < 1 || t.out < 1) {
+        fprintf(stderr, "zstep run: tier `%s` has non-positive fields\n", spec.c_str());
+        return 2;
+      }
+      tiers.push_back(t);
+    }
+    const int repeats = (int)a.num("bench-repeats", 1);
+    const int32_t vocab = b.has_tokenizer ? (int32_t)b.tokenizer.vocab_size() : 1000;
+    std::map<std::string, std::vector<json::Value>> runs;
+    for (int rep = 0; rep < repeats && err.empty(); ++rep)  // interleaved: tier order repeats
+      for (const auto& t : tiers) runs[t.label].push_back(run_tier(e, t, a.num("seed", 0) + rep, vocab, &err));
+    json::Value report = json::Value::object();
+    json::Value tv = json::Value::array();
+    for (const auto& t : tiers) {
+      std::vector<double> tps, ttft, tpot;
+      json::Value reps = json::Value::array();
+      for (const auto& r : runs[t.label]) {
+        tps.push_back(r.get("output_tok_s").as_double());
+        ttft.push_back(r.get("p50_ttft_ms").as_double());
+        tpot.push_back(r.get("p50_tpot_ms").as_double());
+        reps.push(r);
+      }
+      json::Value agg = json::Value::object();
+      agg.set("label", t.label);
+      agg.set("output_tok_s_mean", mean_of(tps));
+      agg.set("output_tok_s_std", std_of(tps));
+      agg.set("p50_ttft_ms_mean", mean_of(ttft));
+      agg.set("p50_tpot_ms_mean", mean_of(tpot));
+      agg.set("runs", reps);
+      tv.push(agg);
+    }
+    report.set("tiers", tv);
+    report.set("provenance", provenance(root));
+    if (!err.empty()) report.set("error", err);
+    printf("%s\n", report.dump().c_str());
+    rc = err.empty() ? 0 : 1;
+  } else {
+    engine::Request r;
+    r.id = 1;
+    if (a.has("prompt-ids")) {
+      r.prompt = parse_ids(a.get("prompt-ids"));
+    } else if (a.has("prompt") && b.has_tokenizer) {
+      std::string prompt;
+      tok::TemplateOptions to;
+      if (!tok::render_chat({{"user", a.get("prompt"), ""}}, to, &prompt, &err)) {
+        fprintf(stderr, "zstep run: %s\n", err.c_str());
+        return 2;
+      }
+      r.prompt = b.tokenizer.encode(prompt);
+      r.eos_ids = b.tokenizer.eos_ids();
+    } else {
+      fprintf(stderr, "zstep run: give --prompt-ids, --prompt, --verify-greedy-json or --bench-tiers\n");
+      return 2;
+    }
+    r.max_tokens = (uint32_t)a.num("max-tokens", 32);
+    e.submit(r);
+    auto out = drive(e, &err);
+    json::Value res = json::Value::object();
+    json::Value toks = json::Value::array();
+    for (int32_t t : out[1]) toks.push(t);
+    res.set("tokens", toks);
+    if (b.has_tokenizer) res.set("text", tok::sanitize_utf8(b.tokenizer.decode(out[1])));
+    if (!err.empty()) res.set("error", err);
+    printf("%s\n", res.dump().c_str());
+    rc = err.empty() ? 0 : 1;
+  }
+  if (b.coord) b.coord->shutdown();
+  return rc;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  if (argc < 2 || !strcmp(argv[1], "--help") || !strcmp(argv[1], "-h")) {
+    printf("zstep <serve|run> [OPTIONS]\n\n%s\n%s", kServeUsage, kRunUsage);
+    return argc < 2 ? 2 : 0;
+  }
+  const std::string sub = argv[1];
+  Args a;
+  std::string err;
+  if (sub != "serve" && sub != "run") {
+    fprintf(stderr, "zstep: unknown subcommand `%s` (serve | run)\n", sub.c_str());
+    return 2;
+  }
+  if (!parse_args(argc, argv, 2, &a, &err)) {
+    fprintf(stderr, "zstep %s: %s\n\n%s", sub.c_str(), err.c_str(), sub == "serve" ? kServeUsage : kRunUsage);
+    return 2;
+  }
+  try {
+    return sub == "serve" ? cmd_serve(a) : cmd_run(a);
+  } catch (const std::exception& ex) {
+    fprintf(stderr, "zstep %s: %s\n", sub.c_str(), ex.what());
+    return 1;
+  }
+}

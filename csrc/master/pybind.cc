@@ -1,11 +1,16 @@
 // Python bindings of the C++ control plane (module zstep_b200._master).  Tests and the
 // offline engine API drive the real C++ engine / coordinator / KV code through this.
+#include <unistd.h>
+
 #include <pybind11/functional.h>
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
 #include "coordinator.h"
 #include "engine.h"
+#include "http_server.h"
+#include "serve_loop.h"
+#include "tokenizer.h"
 #include "kv.h"
 #include "sha256.h"
 #include "wire.h"
@@ -311,6 +316,128 @@ PYBIND11_MODULE(_master, m) {
       .def("free_pages", &engine::Engine::free_pages)
       .def("free_slots", &engine::Engine::free_slots)
       .def("cached_prefix_nodes", [](engine::Engine& e) { return e.prefix_tree() ? e.prefix_tree()->cached_nodes() : 0; });
+
+
+  // ---------------------------------------------------------------- tokenizer
+  py::class_<tok::Tokenizer, std::shared_ptr<tok::Tokenizer>>(m, "Tokenizer")
+      .def(py::init<>())
+      .def("load_dir",
+           [](tok::Tokenizer& t, const std::string& d) {
+             std::string err;
+             if (!t.load_dir(d, &err)) throw std::runtime_error(err);
+           })
+      .def("load_json",
+           [](tok::Tokenizer& t, const std::string& j) {
+             std::string err;
+             if (!t.load_json(j, &err)) throw std::runtime_error(err);
+           })
+      .def("encode", &tok::Tokenizer::encode)
+      .def("decode",
+           [](const tok::Tokenizer& t, const std::vector<int32_t>& ids, bool skip) {
+             return py::bytes(t.decode(ids, skip));
+           },
+           py::arg("ids"), py::arg("skip_special") = true)
+      .def("token_bytes", [](const tok::Tokenizer& t, int32_t id) { return py::bytes(t.token_bytes(id)); })
+      .def("token_id", &tok::Tokenizer::token_id)
+      .def("is_special", &tok::Tokenizer::is_special)
+      .def("vocab_size", &tok::Tokenizer::vocab_size)
+      .def("eos_ids", &tok::Tokenizer::eos_ids)
+      .def("set_eos_ids", &tok::Tokenizer::set_eos_ids)
+      .def_static("pre_split", [](const std::string& text) {
+        py::list out;
+        for (auto& p : tok::Tokenizer::pre_split(text)) out.append(py::bytes(p));
+        return out;
+      });
+  m.def("render_chat",
+        [](std::vector<std::tuple<std::string, std::string, std::string>> msgs, const std::string& format, bool thinking,
+           bool add_bos, const std::string& effort) {
+          std::vector<tok::ChatMessage> ms;
+          for (auto& t : msgs) ms.push_back({std::get<0>(t), std::get<1>(t), std::get<2>(t)});
+          tok::TemplateOptions o;
+          o.format = format == "deepseek" ? tok::TemplateFormat::kDeepSeek : tok::TemplateFormat::kChatML;
+          o.thinking = thinking;
+          o.add_bos = add_bos;
+          o.reasoning_effort = effort;
+          std::string prompt, err;
+          if (!tok::render_chat(ms, o, &prompt, &err)) throw std::invalid_argument(err);
+          return prompt;
+        },
+        py::arg("messages"), py::arg("format") = "chatml", py::arg("thinking") = false, py::arg("add_bos") = true,
+        py::arg("reasoning_effort") = "");
+  py::class_<tok::StreamDecoder>(m, "StreamDecoder")
+      .def(py::init([](std::shared_ptr<tok::Tokenizer> t, std::vector<std::string> stop) {
+             return new tok::StreamDecoder(t.get(), std::move(stop));
+           }),
+           py::keep_alive<1, 2>())
+      .def("push", [](tok::StreamDecoder& d, int32_t id) { return py::bytes(d.push(id)); })
+      .def("finish", [](tok::StreamDecoder& d) { return py::bytes(d.finish()); })
+      .def("stopped", &tok::StreamDecoder::stopped);
+
+  // ---------------------------------------------------------------- online server (mock backend)
+  struct MockServer {
+    std::shared_ptr<tok::Tokenizer> tok;
+    std::shared_ptr<engine::Engine> engine;
+    std::unique_ptr<serve::ServeLoop> loop;
+    std::unique_ptr<http::HttpServer> server;
+  };
+  py::class_<MockServer, std::shared_ptr<MockServer>>(m, "MockServer")
+      .def("port", [](MockServer& s) { return s.server->port(); })
+      .def("admin_port", [](MockServer& s) { return s.server->admin_port(); })
+      .def("state", [](MockServer& s) { return std::string(serve::state_name(s.loop->state())); })
+      .def("set_state", [](MockServer& s, int st) { s.loop->set_state((serve::EngineState)st); })
+      .def("drain", [](MockServer& s) { s.server->request_drain(); })
+      .def("idle", [](MockServer& s) { return s.loop->idle(); })
+      .def("free_pages", [](MockServer& s) { return s.engine->free_pages(); })
+      .def("free_slots", [](MockServer& s) { return s.engine->free_slots(); })
+      .def("metrics_text", [](MockServer& s) { return http::HttpServer::render_metrics(s.loop.get(), http::ServerConfig()); })
+      .def("stop", [](MockServer& s) {
+        py::gil_scoped_release nogil;
+        s.server->stop();
+        s.loop->shutdown();
+      });
+  m.def("serve_mock",
+        [](std::shared_ptr<tok::Tokenizer> t, engine::Config cfg, int port, std::string api_key, int admin_port,
+           std::string model_name, size_t max_waiting, int32_t mock_high, int32_t eos_every, bool allow_remote_metrics,
+           std::string template_format, int step_delay_us, int32_t mock_low) {
+          auto ms = std::make_shared<MockServer>();
+          ms->tok = t;
+          const int32_t eos = t->eos_ids().empty() ? -1 : t->eos_ids()[0];
+          auto backend = serve::make_mock_backend(mock_low, mock_high, eos, eos_every);
+          if (step_delay_us > 0) {
+            struct Slow : engine::Backend {
+              std::shared_ptr<engine::Backend> inner;
+              int us;
+              bool execute(const engine::StepPlan& p, engine::StepResult* r) override {
+                usleep(us);
+                return inner->execute(p, r);
+              }
+            };
+            auto slow = std::make_shared<Slow>();
+            slow->inner = backend;
+            slow->us = step_delay_us;
+            backend = slow;
+          }
+          ms->engine = std::make_shared<engine::Engine>(cfg, backend);
+          ms->loop.reset(new serve::ServeLoop(ms->engine, nullptr, max_waiting));
+          http::ServerConfig sc;
+          sc.port = port;
+          sc.api_key = api_key;
+          sc.admin_port = admin_port;
+          sc.served_model_name = model_name;
+          sc.max_model_len = cfg.max_model_len;
+          sc.allow_remote_metrics = allow_remote_metrics;
+          sc.template_format = template_format == "deepseek" ? tok::TemplateFormat::kDeepSeek : tok::TemplateFormat::kChatML;
+          ms->server.reset(new http::HttpServer(sc, ms->loop.get(), t.get()));
+          std::string err;
+          if (!ms->server->start(&err)) throw std::runtime_error(err);
+          ms->loop->start();
+          return ms;
+        },
+        py::arg("tokenizer"), py::arg("config"), py::arg("port") = 0, py::arg("api_key") = "",
+        py::arg("admin_port") = -1, py::arg("model_name") = "zstep-mock", py::arg("max_waiting") = 64,
+        py::arg("mock_high") = 256, py::arg("eos_every") = 0, py::arg("allow_remote_metrics") = true,
+        py::arg("template_format") = "chatml", py::arg("step_delay_us") = 0, py::arg("mock_low") = 0);
+  m.def("mock_next_token", &serve::mock_next_token);
 
   // ---------------------------------------------------------------- coordinator engine
   m.def("make_shm_engine",
