@@ -329,7 +329,7 @@ void fused_allreduce_norm(int64_t rank, int64_t world, const Tensor& delta, int6
                           const std::vector<int64_t>& flags, const Tensor& epoch, const Tensor& grid_counter,
                           const Tensor& residual, const Tensor& weight, double w_offset, double eps, int64_t rows,
                           const OptT& normed, const OptT& q, const OptT& sf, const OptT& err,
-                          const OptT& term_index, const OptT& term_scale) {
+                          const OptT& term_index, const OptT& term_scale, int64_t timeout_ms) {
   TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)part.size() == world && (int64_t)out.size() == world &&
                   (int64_t)flags.size() == world,
               "bad world / pointer lists");
@@ -362,12 +362,14 @@ void fused_allreduce_norm(int64_t rank, int64_t world, const Tensor& delta, int6
   a.err = optptr<int>(err);
   a.term_index = optptr<const int>(term_index);
   a.term_scale = optptr<const float>(term_scale);
+  a.timeout_ms = (unsigned int)timeout_ms;
   rc(zs_fused_allreduce_norm(&a, stream()), "zs_fused_allreduce_norm");
 }
 
 void allreduce_argmax(int64_t rank, int64_t world, int64_t rows, const std::vector<int64_t>& keys,
                       const std::vector<int64_t>& flags, const Tensor& epoch, const Tensor& local_keys,
-                      int64_t id_offset, const OptT& out_ids, const OptT& out_vals, const OptT& err) {
+                      int64_t id_offset, const OptT& out_ids, const OptT& out_vals, const OptT& err,
+                      int64_t timeout_ms) {
   TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)keys.size() == world && (int64_t)flags.size() == world,
               "bad world / pointer lists");
   ArgmaxArArgs a{};
@@ -382,6 +384,7 @@ void allreduce_argmax(int64_t rank, int64_t world, int64_t rows, const std::vect
   a.out_ids = optptr<int>(out_ids);
   a.out_vals = optptr<float>(out_vals);
   a.err = optptr<int>(err);
+  a.timeout_ms = (unsigned int)timeout_ms;
   rc(zs_allreduce_argmax(&a, ptr<const unsigned long long>(local_keys), (int)id_offset, stream()),
      "zs_allreduce_argmax");
 }
@@ -419,8 +422,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("n_terms"), py::arg("row_stride"), py::arg("term_stride"), py::arg("part"), py::arg("out"),
         py::arg("flags"), py::arg("epoch"), py::arg("grid_counter"), py::arg("residual"), py::arg("weight"),
         py::arg("w_offset"), py::arg("eps"), py::arg("rows"), py::arg("normed"), py::arg("q"), py::arg("sf"),
-        py::arg("err"), py::arg("term_index") = py::none(), py::arg("term_scale") = py::none());
-  m.def("allreduce_argmax", &allreduce_argmax);
+        py::arg("err"), py::arg("term_index") = py::none(), py::arg("term_scale") = py::none(),
+        py::arg("timeout_ms") = 0);
+  m.def("allreduce_argmax", &allreduce_argmax, py::arg("rank"), py::arg("world"), py::arg("rows"), py::arg("keys"),
+        py::arg("flags"), py::arg("epoch"), py::arg("local_keys"), py::arg("id_offset"), py::arg("out_ids"),
+        py::arg("out_vals"), py::arg("err"), py::arg("timeout_ms") = 0);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_free", [](int64_t p) { rc(zs_symm_free(reinterpret_cast<void*>(p)), "zs_symm_free"); });
   m.def("ipc_handle", &ipc_handle);

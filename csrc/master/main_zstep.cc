@@ -32,6 +32,7 @@
 #include "engine.h"
 #include "http_server.h"
 #include "json.h"
+#include "kv_events.h"
 #include "serve_loop.h"
 #include "shm.h"
 #include "tokenizer.h"
@@ -74,6 +75,8 @@ const char* kServeUsage =
     "  --step-timeout-secs N        Per-step timeout (default 300)\n"
     "  --speculative-method none|ngram|mtp\n"
     "  --num-speculative-tokens K   Draft tokens per verify step 1..7\n"
+    "  --kv-events-endpoint ADDR    Publish prefix-cache events: tcp://host:port (ZMTP PUB) or file://path\n"
+    "  --kv-events-topic TOPIC      Topic of published events (default <served-model-name>/0)\n"
     "  --mock                       Scripted backend instead of workers (no GPU)\n";
 
 const char* kRunUsage =
@@ -115,7 +118,7 @@ const std::set<std::string> kValueFlags = {
     "tokenizer-mode", "apc-node-pages", "num-ckpt-slots", "max-waiting-requests", "prefill-policy",
     "drain-timeout-secs", "python", "worker-root", "ready-timeout-secs", "step-timeout-secs", "speculative-method",
     "num-speculative-tokens", "prompt-ids", "prompt", "max-tokens", "verify-greedy-json", "bench-tiers",
-    "bench-repeats", "seed"};
+    "bench-repeats", "seed", "kv-events-endpoint", "kv-events-topic"};
 const std::set<std::string> kBoolFlags = {"allow-remote-metrics", "no-allow-remote-metrics", "enable-prefix-caching",
                                           "no-enable-prefix-caching", "mock", "help"};
 
@@ -304,6 +307,16 @@ int cmd_serve(const Args& a) {
     fprintf(stderr, "zstep serve: tokenizer.json not found in --model-dir\n");
     return 2;
   }
+  std::unique_ptr<kvev::Publisher> kv_pub;
+  if (a.has("kv-events-endpoint")) {
+    const std::string topic = a.get("kv-events-topic", a.get("served-model-name", basename_of(a.get("model-dir"))) + "/0");
+    kv_pub.reset(new kvev::Publisher(a.get("kv-events-endpoint"), topic));
+    if (!kv_pub->start(&err)) {
+      fprintf(stderr, "zstep serve: %s\n", err.c_str());
+      return 1;
+    }
+    b.engine->set_event_sink(kv_pub->sink());
+  }
   serve::ServeLoop loop(b.engine, b.coord, b.cfg.max_waiting);
   http::ServerConfig sc;
   sc.host = a.get("host", "127.0.0.1");
@@ -337,6 +350,7 @@ int cmd_serve(const Args& a) {
   for (long t = 0; t < grace_ms && !loop.idle(); t += 50) usleep(50000);
   server.stop();
   loop.shutdown();
+  if (kv_pub) kv_pub->stop();
   if (b.coord) b.coord->shutdown();
   return loop.state() == serve::EngineState::kFaulted ? 1 : 0;
 }

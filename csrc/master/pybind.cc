@@ -9,6 +9,7 @@
 #include "coordinator.h"
 #include "engine.h"
 #include "http_server.h"
+#include "kv_events.h"
 #include "serve_loop.h"
 #include "tokenizer.h"
 #include "kv.h"
@@ -438,6 +439,41 @@ PYBIND11_MODULE(_master, m) {
         py::arg("mock_high") = 256, py::arg("eos_every") = 0, py::arg("allow_remote_metrics") = true,
         py::arg("template_format") = "chatml", py::arg("step_delay_us") = 0, py::arg("mock_low") = 0);
   m.def("mock_next_token", &serve::mock_next_token);
+
+
+  // ---------------------------------------------------------------- KV events
+  auto mk_event = [](int kind, std::vector<uint64_t> keys) {
+    kv::KvEvent e;
+    e.kind = kind == 0 ? kv::KvEvent::kStored : kind == 1 ? kv::KvEvent::kRemoved : kv::KvEvent::kAllCleared;
+    e.block_keys = std::move(keys);
+    return e;
+  };
+  m.def("encode_kv_batch",
+        [mk_event](int kind, std::vector<uint64_t> keys, double ts) {
+          return py::bytes(kvev::encode_batch(mk_event(kind, std::move(keys)), ts));
+        });
+  py::class_<kvev::Publisher, std::shared_ptr<kvev::Publisher>>(m, "KvEventPublisher")
+      .def(py::init<std::string, std::string, size_t>(), py::arg("endpoint"), py::arg("topic"),
+           py::arg("queue_cap") = 4096)
+      .def("start",
+           [](kvev::Publisher& p) {
+             std::string err;
+             bool ok;
+             {
+               py::gil_scoped_release nogil;
+               ok = p.start(&err);
+             }
+             if (!ok) throw std::runtime_error(err);
+           })
+      .def("publish",
+           [mk_event](kvev::Publisher& p, int kind, std::vector<uint64_t> keys) { p.publish(mk_event(kind, keys)); })
+      .def("stop",
+           [](kvev::Publisher& p) {
+             py::gil_scoped_release nogil;
+             p.stop();
+           })
+      .def("sent", &kvev::Publisher::sent)
+      .def("dropped", &kvev::Publisher::dropped);
 
   // ---------------------------------------------------------------- coordinator engine
   m.def("make_shm_engine",

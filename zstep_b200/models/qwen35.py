@@ -29,13 +29,13 @@ forward, 1236 varlen prefill, 1404 graph capture, 484-524 state allocation).
 from __future__ import annotations
 
 import math
-import os
 from dataclasses import dataclass
 
 import torch
 
 from ..config import Qwen35Config
 from ..ops import _ext
+from ..utils.env import runtime_config
 from ..ops import mx
 from .weights import RandomWeights
 
@@ -250,7 +250,7 @@ class Qwen35Runner:
         self.num_sms = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
         # In-kernel split-K for dense GEMMs with few output tiles.  Off by default: on the
         # decode shapes measured so far it did not beat the unsplit kernel.
-        self.use_fix_splits = os.environ.get("ZSTEP_GEMM_FIX_SPLITS", "0") == "1"
+        self.use_fix_splits = runtime_config().gemm_fix_splits
         b["xq"] = torch.zeros(Rp, H, dtype=torch.uint8, device=dev)
         b["xsf"] = torch.zeros(mx.atoms_bytes(Rp, H), dtype=torch.uint8, device=dev)
         b["proj"] = torch.zeros(R * max(self.gdn_w, self.qkv_w), dtype=torch.bfloat16, device=dev)

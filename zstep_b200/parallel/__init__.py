@@ -3,13 +3,13 @@ kernels), symmetric memory, and topology checks."""
 
 from __future__ import annotations
 
-import os
-
 
 def make_collectives(device, group=None, kind: str | None = None):
     """Pick the collective implementation for the runner (``ZSTEP_COLLECTIVES`` =
     ``fused`` (default when available) or ``nccl``)."""
-    kind = kind or os.environ.get("ZSTEP_COLLECTIVES", "fused")
+    from ..utils.env import runtime_config
+
+    kind = kind or runtime_config().collectives
     if kind == "fused":
         try:
             from .fused import FusedCollectives

@@ -16,7 +16,6 @@ from __future__ import annotations
 
 import datetime
 import json
-import os
 import statistics
 
 import torch
@@ -24,6 +23,7 @@ import torch.distributed as dist
 
 from ..ops import _ext, mx
 from .collectives import NcclCollectives
+from ..utils.env import dist_env
 from .fused import FusedCollectives
 
 LINK_GBS = 770.0  # measured peer copy bandwidth per direction per GPU on this pool
@@ -60,8 +60,8 @@ def _time_graph(body, calls: int, reps: int) -> float:
 
 
 def main():
-    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
-    local = int(os.environ.get("LOCAL_RANK", rank))
+    de = dist_env()
+    rank, world, local = de.rank, de.world_size, de.local_rank
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))

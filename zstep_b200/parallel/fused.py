@@ -26,6 +26,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops import _ext
+from ..utils.env import runtime_config
 
 _ALIGN = 256
 
@@ -51,6 +52,7 @@ class FusedCollectives:
         self.grid = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.local_keys = None
+        self.timeout_ms = runtime_config().coll_timeout_ms  # bound on every cross-rank wait
         if max_rows and hidden:
             self.reserve(max_rows, hidden)
 
@@ -105,7 +107,8 @@ class FusedCollectives:
             raise ValueError(f"fused all-reduce reserved for {self.max_rows}x{self.hidden}, got {rows}x{H}")
         self.C.fused_allreduce_norm(self.rank, self.world, delta, n_terms, row_stride, term_stride, self.part_ptrs,
                                     self.out_ptrs, self.flag_ptrs, self.epoch[0:1], self.grid, hidden_buf, norm_w,
-                                    1.0, eps, rows, None, xq, xsf, self.err, term_index, term_scale)
+                                    1.0, eps, rows, None, xq, xsf, self.err, term_index, term_scale,
+                                    self.timeout_ms)
 
     def argmax_allreduce(self, keys, rows: int, tiles: int, id_offset: int, out_ids, out_vals) -> None:
         """Global greedy token per row from per-tile packed keys of this rank's vocab shard."""
@@ -113,4 +116,4 @@ class FusedCollectives:
             raise ValueError(f"fused argmax reserved for {self.max_rows} rows, got {rows}")
         self.C.argmax_reduce(keys, rows, tiles, None, None, self.local_keys)
         self.C.allreduce_argmax(self.rank, self.world, rows, self.key_ptrs, self.flag_ptrs, self.epoch[1:2],
-                                self.local_keys, id_offset, out_ids, out_vals, self.err)
+                                self.local_keys, id_offset, out_ids, out_vals, self.err, self.timeout_ms)

@@ -13,6 +13,7 @@ import socket
 import sys
 
 from .. import _master
+from ..utils.env import python_path
 
 
 def free_port() -> int:
@@ -51,7 +52,7 @@ def launch(*, model: str = "qwen3.5-tiny", world_size: int = 1, device: str = "c
             str(num_ckpt_slots)]
     root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     env = {"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(free_port()),
-           "PYTHONPATH": root + os.pathsep + os.environ.get("PYTHONPATH", "")}
+           "PYTHONPATH": root + os.pathsep + python_path()}
     env.update(extra_env or {})
     return _master.make_shm_engine(ecfg, geo, argv, env, ready_timeout_ms, step_timeout_ms, heartbeat_timeout_ms)
 

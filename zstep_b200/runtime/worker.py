@@ -164,6 +164,17 @@ def parse_args(argv=None):
 def main(argv=None) -> int:
     _set_pdeathsig()
     args = parse_args(argv)
+    from ..utils.env import runtime_config
+
+    cfg = runtime_config()  # validates every ZSTEP_* variable before any work
+    print(f"[rank {args.rank}] {cfg.format_log_line()}", file=sys.stderr, flush=True)
+    if args.device == "cuda" and cfg.numa_pin:
+        # Before the shared-memory segment and CUDA are touched, so their pages and the
+        # pinned staging buffers are allocated on the GPU's node.
+        from ..utils.numa import pin_process_to_device
+
+        info = pin_process_to_device(args.rank)
+        print(f"[rank {args.rank}] numa: {info}", file=sys.stderr, flush=True)
     WorkerLoop(args).run()
     return 0
 
