@@ -43,7 +43,8 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
                int64_t epi_mode, const Tensor& out, int64_t ldo, const OptT& out_sf,
                const OptT& row_dst, const OptT& row_scale, const OptT& err, int64_t max_items,
                int64_t block_n, int64_t k_splits, int64_t split_stride, int64_t a_tiled,
-               int64_t fix_splits, const OptT& ws, const OptT& tile_sem) {
+               int64_t fix_splits, const OptT& ws, const OptT& tile_sem, const OptT& row_temp,
+               const OptT& row_seed, const OptT& row_pos, int64_t id_offset, const OptT& sample_any) {
   check_cuda(a, "a");
   check_cuda(sfa, "sfa");
   check_cuda(b, "b");
@@ -83,6 +84,17 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
   p.split_stride = split_stride;
   p.a_tiled = (int)a_tiled;
   p.fix_splits = (int)fix_splits;
+  if (row_temp.has_value()) {
+    TORCH_CHECK(row_seed.has_value() && row_pos.has_value(), "sampling needs row_temp, row_seed and row_pos");
+    TORCH_CHECK(row_temp->scalar_type() == at::kFloat && row_seed->scalar_type() == at::kLong &&
+                    row_pos->scalar_type() == at::kInt,
+                "row_temp f32, row_seed i64, row_pos i32");
+    p.row_temp = ptr<const float>(*row_temp);
+    p.row_seed = ptr<const long long>(*row_seed);
+    p.row_pos = ptr<const int>(*row_pos);
+  }
+  p.id_offset = (int)id_offset;
+  p.sample_any = optptr<const float>(sample_any);
   if (fix_splits > 1) {
     TORCH_CHECK(ws.has_value() && tile_sem.has_value(), "split-K needs ws and tile_sem");
     TORCH_CHECK(ws->scalar_type() == at::kFloat && tile_sem->scalar_type() == at::kInt, "ws f32, tile_sem i32");
@@ -439,7 +451,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("group_offset"), py::arg("chunk_prefix"), py::arg("epi_mode"), py::arg("out"), py::arg("ldo"),
         py::arg("out_sf"), py::arg("row_dst"), py::arg("row_scale"), py::arg("err"), py::arg("max_items"),
         py::arg("block_n"), py::arg("k_splits"), py::arg("split_stride"), py::arg("a_tiled"),
-        py::arg("fix_splits") = 1, py::arg("ws") = py::none(), py::arg("tile_sem") = py::none());
+        py::arg("fix_splits") = 1, py::arg("ws") = py::none(), py::arg("tile_sem") = py::none(),
+        py::arg("row_temp") = py::none(), py::arg("row_seed") = py::none(), py::arg("row_pos") = py::none(),
+        py::arg("id_offset") = 0, py::arg("sample_any") = py::none());
   m.def("quant_mxf8", &quant_mxf8);
   m.def("add_rmsnorm_quant", &add_rmsnorm_quant, py::arg("residual"), py::arg("delta"), py::arg("n_terms"),
         py::arg("d_row_stride"), py::arg("d_term_stride"), py::arg("weight"), py::arg("w_offset"), py::arg("eps"),

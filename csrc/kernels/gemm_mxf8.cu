@@ -458,6 +458,17 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
             // one packed (orderable logit, ~id) word; the max over words gives the largest
             // logit with the smallest id on ties.
             unsigned long long* part = reinterpret_cast<unsigned long long*>(p.out);
+            if (p.row_temp != nullptr && (p.sample_any == nullptr || __ldg(p.sample_any) > 0.f)) {
+              // Sampling rows: Gumbel-perturbed scaled logits (same noise on every rank).
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const int row = seg_row0 + col0 + j;
+                const float t = j < ncols ? __ldg(p.row_temp + row) : 0.f;
+                if (t > 0.f)
+                  v[j] = v[j] / t + gumbel_noise((unsigned long long)__ldg(p.row_seed + row), __ldg(p.row_pos + row),
+                                                 p.id_offset + n_glob);
+              }
+            }
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               unsigned long long key = valid_n ? pack_argmax(v[j], n_glob) : 0ull;

@@ -325,6 +325,20 @@ ZS_DEVICE uint8_t f32_to_e4m3(float v) {
 
 // Argmax key: high word = logit bits mapped to an unsigned order, low word = ~id,
 // so an unsigned max picks the largest logit and, among equal logits, the smallest id.
+// Gumbel(0, 1) noise for sampling by perturbed argmax: the same (seed, position, token
+// id) gives the same noise on every rank, so a vocab-sharded lm_head samples one token
+// consistently.  Uniform from one SplitMix64 step (24-bit mantissa, open interval).
+ZS_DEVICE float gumbel_noise(unsigned long long seed, int pos, int id) {
+  unsigned long long z = seed ^ ((unsigned long long)(unsigned)pos * 0x9E3779B97F4A7C15ull) ^
+                         ((unsigned long long)(unsigned)id * 0xD1B54A32D192ED03ull);
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  const float u = ((float)(z >> 40) + 0.5f) * (1.0f / 16777216.0f);
+  return -logf(-logf(u));
+}
+
 ZS_DEVICE unsigned long long pack_argmax(float v, int id) {
   uint32_t b = __float_as_uint(v);
   b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);

@@ -60,6 +60,14 @@ typedef struct GemmMxf8Args {
   float* ws;               // >= tiles * fix_splits * 128 * block_n floats
   int* tile_sem;           // >= tiles ints, zero before the first call (kept zero after)
   int max_tiles;           // capacity of ws / tile_sem in tiles (the kernel checks)
+  // kEpiArgmaxPartial sampling (optional): rows with row_temp > 0 take the argmax of
+  // logit / temp + Gumbel(seed, pos, id_offset + feature), i.e. a sample from
+  // softmax(logit / temp); rows with temp <= 0 stay greedy.
+  const float* row_temp;
+  const long long* row_seed;
+  const int* row_pos;
+  int id_offset;           // global id of feature 0 (vocab shard offset)
+  const float* sample_any; // optional scalar: <= 0 means no row samples (skips the per-row loads)
 } GemmMxf8Args;
 
 int zs_gemm_mxf8(const GemmMxf8Args* args, cudaStream_t stream);

@@ -219,6 +219,59 @@ def test_gemm_silu_quant(C):
         torch.testing.assert_close(got[o:o + cnt], h, rtol=0.07, atol=0.02 * h.abs().max().item())
 
 
+def test_gemm_argmax_gumbel_sampling(C):
+    """Sampling rows take argmax(logit / T + Gumbel(seed, pos, id)): matches the host
+    reference on the kernel's own logits, and the sample frequencies follow softmax(l / T)."""
+    from zstep_b200.sampling import gumbel_noise
+
+    torch.manual_seed(5)
+    m, vocab, k = 64, 1000, 256
+    w = torch.randn(1, vocab, k) * 0.05
+    x = torch.randn(m, k)
+    wq, wsf, wd, npad = _quant_weights(w)
+    xq, xsf, xd = _quant_act(x, _pad_rows(m))
+    tiles = npad // 128
+    logits = torch.zeros(m, vocab, device="cuda")
+    gemm(C, wq, wsf, xq, xsf, k, npad, vocab, 1, m, None, None, None, EPI_F32, logits, vocab, None, None, None, None, 0)
+    temp = torch.tensor([0.0 if r % 4 == 0 else 0.7 for r in range(m)], device="cuda")
+    seed = torch.arange(m, dtype=torch.int64, device="cuda") * 7919 + 11
+    pos = torch.arange(m, dtype=torch.int32, device="cuda") + 100
+    keys = torch.zeros(m, tiles, dtype=torch.int64, device="cuda")
+    C.gemm_mxf8(wq, wsf, xq, xsf, k, npad, vocab, 1, m, None, None, None, EPI_ARGMAX, keys, tiles, None, None, None,
+                None, 0, 128, 1, 0, 0, 1, None, None, temp, seed, pos, 5000)
+    ids = torch.zeros(m, dtype=torch.int32, device="cuda")
+    C.argmax_reduce(keys, m, tiles, ids, None, None)
+    torch.cuda.synchronize()
+    lg = logits.cpu()
+    agree = 0
+    for r in range(m):
+        t = float(temp[r])
+        if t == 0:
+            exp = int(lg[r].argmax())
+        else:
+            exp = int(torch.argmax(lg[r] / t + gumbel_noise(int(seed[r]), int(pos[r]), torch.arange(vocab) + 5000)))
+        agree += int(exp == int(ids[r]))
+    assert agree >= m - 1, agree
+    # Distribution: one 4-way row repeated at many positions.
+    m2, v2 = 2048, 128
+    w2 = torch.zeros(1, v2, k)
+    w2[0, :4, 0] = torch.tensor([1.0, 0.5, 0.0, -0.5])
+    x2 = torch.zeros(m2, k)
+    x2[:, 0] = 1.0
+    wq2, wsf2, wd2, npad2 = _quant_weights(w2)
+    xq2, xsf2, xd2 = _quant_act(x2, _pad_rows(m2))
+    l2 = (xd2[0] @ wd2[0, :v2].T)[:4]
+    keys2 = torch.zeros(m2, 1, dtype=torch.int64, device="cuda")
+    C.gemm_mxf8(wq2, wsf2, xq2, xsf2, k, npad2, 4, 1, m2, None, None, None, EPI_ARGMAX, keys2, 1, None, None, None,
+                None, 0, 128, 1, 0, 0, 1, None, None, torch.full((m2,), 0.5, device="cuda"),
+                torch.full((m2,), 1234, dtype=torch.int64, device="cuda"),
+                torch.arange(m2, dtype=torch.int32, device="cuda"), 0)
+    ids2 = torch.zeros(m2, dtype=torch.int32, device="cuda")
+    C.argmax_reduce(keys2, m2, 1, ids2, None, None)
+    freq = torch.bincount(ids2.cpu().long(), minlength=4)[:4].float() / m2
+    torch.testing.assert_close(freq, torch.softmax(l2 / 0.5, 0), atol=0.04, rtol=0)
+
+
 def _split_ws():
     return torch.zeros(8 << 20, device="cuda"), torch.zeros(16384, dtype=torch.int32, device="cuda")
 

@@ -244,6 +244,11 @@ class Qwen35Runner:
         self.mid_w = max(self.hv * 128, self.hq * cfg.head_dim)
         b = {}
         b["hidden"] = torch.zeros(R, H, dtype=torch.bfloat16, device=dev)
+        # Sampling parameters of the lm_head rows (temperature 0 = greedy).
+        b["samp_temp"] = torch.zeros(R, dtype=torch.float32, device=dev)
+        b["samp_seed"] = torch.zeros(R, dtype=torch.int64, device=dev)
+        b["samp_pos"] = torch.zeros(R, dtype=torch.int32, device=dev)
+        b["samp_any"] = torch.zeros(1, dtype=torch.float32, device=dev)  # max temperature of the batch
         # In-kernel split-K: fp32 partial tiles + per-tile arrival counters (kept zero).
         b["gemm_ws"] = torch.zeros(8 << 20, dtype=torch.float32, device=dev)
         b["gemm_sem"] = torch.zeros(16384, dtype=torch.int32, device=dev)
@@ -307,7 +312,7 @@ class Qwen35Runner:
 
     # ------------------------------------------------------------------ kernels
     def _gemm(self, w: PackedLinear, xq, xsf, rows: int, out, ldo: int, epi=EPI_BF16, grouped=False,
-              out_sf=None, row_dst=None, row_scale=None, k_splits: int = 1):
+              out_sf=None, row_dst=None, row_scale=None, k_splits: int = 1, **sampling):
         b = self.buf
         if grouped:
             bn = self._moe_bn(rows)
@@ -319,7 +324,7 @@ class Qwen35Runner:
             fs = self._fix_splits(tiles, tiles, w.k // 128, bn) if (k_splits == 1 and self.use_fix_splits) else 1
             self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, 1, rows, None, None, None, epi, out, ldo,
                              out_sf, row_dst, row_scale, b["err"], 0, bn, k_splits, rows * ldo, 1,
-                             fs, b["gemm_ws"], b["gemm_sem"])
+                             fs, b["gemm_ws"], b["gemm_sem"], **sampling)
 
     def _fix_splits(self, max_tiles: int, items: int, k_tiles: int, bn: int) -> int:
         """In-kernel split-K factor for a dense GEMM: double while all split items still fit
@@ -438,11 +443,16 @@ class Qwen35Runner:
         self._gemm(L["gate_up"], b["xg"], b["xg_sf"], rows, b["act"], I, EPI_SILU, grouped=True, out_sf=b["act_sf"])
         self._gemm(L["down"], b["act"], b["act_sf"], rows, b["moe_y"], cfg.hidden_size, EPI_BF16, grouped=True)
 
-    def _lm_head_argmax(self, rows: int, xq=None, xsf=None) -> None:
+    def _lm_head_argmax(self, rows: int, xq=None, xsf=None, pos=None) -> None:
+        """Greedy (temperature 0) or sampled next token of each row: the lm_head GEMM's
+        epilogue reduces each vocab tile to one packed key of the (Gumbel-perturbed, for
+        sampling rows) logits; the keys are then max-reduced locally or across ranks."""
         b = self.buf
         xq = b["xq"] if xq is None else xq
         xsf = b["xsf"] if xsf is None else xsf
-        self._gemm(self.lm_head, xq, xsf, rows, b["lm_keys"], self.vocab_tiles, EPI_ARGMAX)
+        self._gemm(self.lm_head, xq, xsf, rows, b["lm_keys"], self.vocab_tiles, EPI_ARGMAX,
+                   row_temp=b["samp_temp"], row_seed=b["samp_seed"], row_pos=b["in_pos"] if pos is None else pos,
+                   id_offset=self.tp_rank * self.vocab_local, sample_any=b["samp_any"])
         if self.tp > 1:
             self.coll.argmax_allreduce(b["lm_keys"], rows, self.vocab_tiles, self.tp_rank * self.vocab_local,
                                        b["out_ids"], b["out_vals"])
@@ -468,8 +478,22 @@ class Qwen35Runner:
         codes = self._gather_sf(b["xsf"], last, H)
         xq_last[:num_seqs] = b["xq"][last]
         sf_last = mx.atoms_from_codes(codes)
-        self._lm_head_argmax(num_seqs, xq_last, sf_last)
+        b["samp_pos"][:num_seqs] = b["in_pos"][last]
+        self._lm_head_argmax(num_seqs, xq_last, sf_last, pos=b["samp_pos"])
         return b["out_ids"][:num_seqs]
+
+    def set_sampling(self, temperatures, seeds) -> None:
+        """Per-sequence temperature (0 = greedy) and seed for the next steps' lm_head.
+        Sequence i of a decode step is row i; of a prefill step, its last row."""
+        n = len(temperatures)
+        self.buf["samp_temp"][:n].copy_(torch.tensor(temperatures, dtype=torch.float32))
+        self.buf["samp_seed"][:n].copy_(torch.tensor([s & 0x7FFFFFFFFFFFFFFF for s in seeds], dtype=torch.int64))
+        self.buf["samp_temp"][n:].zero_()
+        self.buf["samp_any"].fill_(max([0.0] + [float(t) for t in temperatures]))
+
+    def clear_sampling(self) -> None:
+        self.buf["samp_temp"].zero_()
+        self.buf["samp_any"].zero_()
 
     def _gather_sf(self, atoms: torch.Tensor, rows_idx: torch.Tensor, k: int):
         """Gather scale codes of selected rows from an atom buffer (device ops)."""

@@ -165,9 +165,18 @@ class GpuRunner:
             if src >= 0:
                 r.copy_recurrent_state(src, int(plan["seq_slot"][i]))
         rows = plan["num_rows"]
-        greedy = not (plan["flags"] & wire.FLAG_SAMPLING)
+        sampling = bool(plan["flags"] & wire.FLAG_SAMPLING)
         decode_only = bool(plan["flags"] & wire.FLAG_DECODE_ONLY)
-        if decode_only and greedy:
+        if sampling:
+            # Temperature sampling runs inside the lm_head GEMM (Gumbel-perturbed argmax);
+            # the per-sequence seed plus the row position make it reproducible.
+            sp = plan["sampling"]
+            r.set_sampling([float(sp[i]["temperature"]) for i in range(n)], [int(sp[i]["seed"]) for i in range(n)])
+            self._sampling_set = True
+        elif getattr(self, "_sampling_set", False):
+            r.clear_sampling()
+            self._sampling_set = False
+        if decode_only:
             r.stage(plan["token_ids"], plan["positions"], plan["row_slot"])
             ids = r.decode_step(rows).cpu().numpy()
         else:

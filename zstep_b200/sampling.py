@@ -87,3 +87,28 @@ def verify_greedy(drafts: list[int], targets: list[int]) -> list[int]:
         out.append(d)
     out.append(targets[len(drafts)])
     return out
+
+
+def gumbel_noise(seed: int, pos: int, ids: torch.Tensor) -> torch.Tensor:
+    """Gumbel(0, 1) noise of the GPU sampler for token ids `ids` at (seed, position):
+    one SplitMix64 step of seed ^ pos*C1 ^ id*C2, 24-bit uniform in (0, 1)."""
+    m = _MASK64
+    z = [(((seed ^ ((pos & 0xFFFFFFFF) * 0x9E3779B97F4A7C15) ^ ((int(i) & 0xFFFFFFFF) * 0xD1B54A32D192ED03)) & m)
+          + 0x9E3779B97F4A7C15) & m for i in ids.tolist()]
+    out = []
+    for v in z:
+        v = ((v ^ (v >> 30)) * 0xBF58476D1CE4E5B9) & m
+        v = ((v ^ (v >> 27)) * 0x94D049BB133111EB) & m
+        v ^= v >> 31
+        out.append(((v >> 40) + 0.5) / float(1 << 24))
+    u = torch.tensor(out, dtype=torch.float32)
+    return -torch.log(-torch.log(u))
+
+
+def gumbel_sample(logits: torch.Tensor, temperature: float, seed: int, pos: int) -> int:
+    """Reference of the fused lm_head sampler: argmax of logits / T + Gumbel noise
+    (distributed as softmax(logits / T)); greedy when T <= 0."""
+    if temperature <= 0:
+        return int(torch.argmax(logits))
+    ids = torch.arange(logits.numel())
+    return int(torch.argmax(logits.float().cpu() / temperature + gumbel_noise(seed, pos, ids)))
