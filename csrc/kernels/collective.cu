@@ -5,23 +5,11 @@
 // from and store to rank q's buffer directly over NVLink / NVSwitch.  No host memory
 // and no library collective sits on the data path.
 //
-// fused_allreduce_norm (one persistent kernel, grid of FAR_CTAS co-resident CTAs):
-//   1. local term sum   : part[r][row] = sum of this rank's partial terms (f32 split-K
-//                         partials or bf16 MoE pair rows), written to symmetric memory
-//   2. cross-rank barrier "ready" (release stores into every peer's flag word, acquire
-//                         spins on the local flags; all waits bounded)
-//   3. reduce-scatter   : rank r owns rows [r*M/W, (r+1)*M/W); for them it adds
-//                         residual + part[0] + ... + part[W-1] in rank order (so the
-//                         result is bit-identical whichever rank computes it), rounds to
-//                         bf16 and writes out[r][row]
-//   4. cross-rank barrier "reduced"
-//   5. all-gather + norm: every rank copies each row from its owner's out buffer into
-//                         its residual stream, then RMSNorm + MXFP8 quantize locally
-// A grid-wide barrier (atomic counter, bounded spin) separates the phases inside a rank.
-// Phase-3 reads of part[] finish before barrier 4 and phase-5 reads of out[] finish
-// before the next call's barrier 2, so no buffer is overwritten while a peer reads it.
-// An epoch counter in device memory (same sequence on every rank, advanced by the
-// kernel itself) makes flag values monotonic and keeps the kernel CUDA-graph safe.
+// fused_allreduce_norm (one cooperative launch): push-based two-shot all-reduce of the
+// row-parallel partial sums with flag-in-data words, fused with the residual add, RMSNorm
+// and MXFP8 quantization (details at the kernel).  Every word carries the call's epoch
+// (a counter in device memory advanced by the kernel itself), so there is no separate
+// barrier round trip and the kernel stays CUDA-graph safe.
 //
 // allreduce_argmax: per-row packed (logit, ~id) keys of each rank's vocab shard are
 // exchanged the same way and max-reduced, giving the global greedy token on every rank.
@@ -82,51 +70,6 @@ __device__ __forceinline__ bool wait_flag_sys(const uint32_t* p, uint32_t value,
   }
 }
 
-// Grid-wide barrier for a persistent grid; `target` grows monotonically across calls.
-__device__ __forceinline__ bool grid_sync(uint32_t* counter, uint32_t target, uint64_t budget_ns, int* err) {
-  __syncthreads();
-  __shared__ int ok;
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    atomicAdd(counter, 1u);
-    ok = 0;
-    const uint64_t t0 = globaltimer_ns();
-    for (uint32_t i = 0;; ++i) {
-      if ((int)(ld_acquire_gpu(counter) - target) >= 0) {
-        ok = 1;
-        break;
-      }
-      if (i > 32) {
-        __nanosleep(32);
-        if ((i & 255) == 0 && globaltimer_ns() - t0 > budget_ns) break;
-      }
-    }
-    if (!ok) report_error(err, kErrPeerTimeout);
-  }
-  __syncthreads();
-  return ok != 0;
-}
-
-// Cross-rank barrier: CTA 0 releases `value` into slot `rank` of every peer's flag
-// array; every CTA then waits until all `world` slots of its local array reach it.
-__device__ __forceinline__ bool rank_barrier(const FusedArArgs& a, int phase, uint32_t value) {
-  __shared__ int ok;
-  if (blockIdx.x == 0 && threadIdx.x < a.world)
-    st_release_sys(a.flags[threadIdx.x] + phase * 8 + a.rank, value);
-  if (threadIdx.x == 0) {
-    ok = 1;
-    const uint32_t* mine = a.flags[a.rank] + phase * 8;
-    for (int r = 0; r < a.world && ok; ++r) {
-      if (!wait_flag_sys(mine + r, value, limit_ns(a.timeout_ms), a.abort_word)) {
-        ok = 0;
-        report_error(a.err, kErrPeerTimeout);
-      }
-    }
-  }
-  __syncthreads();
-  return ok != 0;
-}
-
 __device__ __forceinline__ void unpack8(const uint4& u, float* f) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
@@ -146,84 +89,143 @@ __device__ __forceinline__ uint4 pack8(const float* f) {
   return make_uint4(p[0], p[1], p[2], p[3]);
 }
 
+// Flag-in-data word: 32 bits of payload (two bf16) + the call's epoch, stored with one
+// 8-byte store so a reader never sees the payload of one call with the flag of another.
+__device__ __forceinline__ void st_ll(uint2* p, uint32_t data, uint32_t epoch) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(data), "r"(epoch) : "memory");
+}
+__device__ __forceinline__ uint2 ld_ll(const uint2* p) {
+  uint2 v;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits for the word at p to carry `epoch`; returns its payload (0 and an error on timeout).
+__device__ __forceinline__ uint32_t wait_ll(const uint2* p, uint32_t epoch, uint64_t budget_ns, int* err,
+                                            volatile int* give_up) {
+  uint2 v = ld_ll(p);
+  if (v.y == epoch) return v.x;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    v = ld_ll(p);
+    if (v.y == epoch) return v.x;
+    if (*give_up) return 0u;
+    if ((i & 63) == 63) {
+      if (globaltimer_ns() - t0 > budget_ns) {
+        report_error(err, kErrPeerTimeout);
+        *give_up = 1;
+        return 0u;
+      }
+      __nanosleep(32);
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
+  return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u));
+}
+
+// Local contribution to word w (elements 2w, 2w+1) of `row`: the rank's terms summed in
+// term order, rounded to bf16 (what the other ranks receive).
+__device__ __forceinline__ uint32_t local_word(const FusedArArgs& a, int row, int w) {
+  float s0 = 0.f, s1 = 0.f;
+  const int c = 2 * w;
+  for (int t = 0; t < a.n_terms; ++t) {
+    long long off = row * a.row_stride + t * a.term_stride + c;
+    float sc = 1.f;
+    if (a.term_index != nullptr) {  // gathered term; negative = not produced on this rank
+      const int src = a.term_index[row * a.n_terms + t];
+      if (src < 0) continue;
+      off = (long long)src * a.row_stride + c;
+    }
+    if (a.term_scale != nullptr) sc = a.term_scale[row * a.n_terms + t];
+    if (a.delta_f32) {
+      const float2 v = *reinterpret_cast<const float2*>(static_cast<const float*>(a.delta) + off);
+      s0 += sc * v.x;
+      s1 += sc * v.y;
+    } else {
+      const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(static_cast<const __nv_bfloat16*>(a.delta) + off));
+      s0 += sc * v.x;
+      s1 += sc * v.y;
+    }
+  }
+  return pack_bf16x2(s0, s1);
+}
+
+// Push-based two-shot all-reduce with flag-in-data words (no grid barrier, no remote loads):
+//  1. send   : every rank pushes its bf16 local sum of each row to the row's owner
+//              (rs buffer slot [sender][row - owner_first_row])
+//  2. reduce : the owner waits for the W contributions of its rows, adds residual + the
+//              contributions in rank order (identical on every rank) and pushes the bf16
+//              result to every rank's ag buffer
+//  3. gather : every rank waits for each row's result, writes it to its residual stream
+//              and applies RMSNorm + MXFP8 quantization
+// CTA c handles rows c, c+G, ... in all three phases on every rank, so a CTA only waits for
+// words that other CTAs (same index, other ranks) produce before they wait themselves.
+// Buffers are reused across calls without extra barriers: a rank writes call E+1's words
+// only after it finished call E, which needed every peer's call-E words it is about to
+// overwrite to have been consumed (an owner sends its results only after reading all
+// contributions; a sender starts the next call only after reading all results).
 __global__ void __launch_bounds__(THREADS) fused_allreduce_norm_kernel(const FusedArArgs a) {
   const int H = a.hidden, M = a.rows, W = a.world;
+  const int words = H / 2;
   const int tid = threadIdx.x;
-  const uint32_t E = *reinterpret_cast<volatile uint32_t*>(a.epoch);
-  const uint32_t G = gridDim.x;
-  const int chunks = H / 8;  // 16-byte chunks per row
-
-  // 1. local term sum -> part[rank] (bf16)
-  __nv_bfloat16* my_part = static_cast<__nv_bfloat16*>(a.part[a.rank]);
-  for (long long idx = (long long)blockIdx.x * THREADS + tid; idx < (long long)M * chunks; idx += (long long)G * THREADS) {
-    const int row = int(idx / chunks), c = int(idx % chunks) * 8;
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int t = 0; t < a.n_terms; ++t) {
-      long long off = row * a.row_stride + t * a.term_stride + c;
-      float sc = 1.f;
-      if (a.term_index != nullptr) {  // gathered term; negative = not produced on this rank
-        const int src = a.term_index[row * a.n_terms + t];
-        if (src < 0) continue;
-        off = (long long)src * a.row_stride + c;
-      }
-      if (a.term_scale != nullptr) sc = a.term_scale[row * a.n_terms + t];
-      if (a.delta_f32) {
-        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(a.delta) + off);
-        const float4 x0 = p[0], x1 = p[1];
-        acc[0] += sc * x0.x; acc[1] += sc * x0.y; acc[2] += sc * x0.z; acc[3] += sc * x0.w;
-        acc[4] += sc * x1.x; acc[5] += sc * x1.y; acc[6] += sc * x1.z; acc[7] += sc * x1.w;
-      } else {
-        float f[8];
-        unpack8(*reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.delta) + off), f);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] += sc * f[j];
-      }
-    }
-    *reinterpret_cast<uint4*>(my_part + (size_t)row * H + c) = pack8(acc);
-  }
-  // Two grid barriers per call: the counter reaches 2*G*(E+1) when call E completes.
-  if (!grid_sync(a.grid_counter, (E * 2 + 1) * G, limit_ns(a.timeout_ms), a.err)) return;
-  if (blockIdx.x == 0 && tid == 0) *reinterpret_cast<volatile uint32_t*>(a.epoch) = E + 1;  // everyone has read E
-  if (!rank_barrier(a, 0, E + 1)) return;
-
-  // 3. reduce-scatter of owned rows: out[rank][row] = bf16(residual + sum_r part[r])
+  const uint32_t E = *reinterpret_cast<volatile uint32_t*>(a.epoch) + 1;  // this call's flag value (never 0)
+  const int G = gridDim.x;
   const int per = (M + W - 1) / W;
-  const int r0 = a.rank * per, r1 = min(M, r0 + per);
-  __nv_bfloat16* my_out = static_cast<__nv_bfloat16*>(a.out[a.rank]);
-  const __nv_bfloat16* resid = static_cast<const __nv_bfloat16*>(a.residual);
-  for (long long idx = (long long)blockIdx.x * THREADS + tid; idx < (long long)(r1 - r0) * chunks;
-       idx += (long long)G * THREADS) {
-    const int row = r0 + int(idx / chunks), c = int(idx % chunks) * 8;
-    const size_t off = (size_t)row * H + c;
-    float acc[8], f[8];
-    unpack8(*reinterpret_cast<const uint4*>(resid + off), acc);
-    for (int r = 0; r < W; ++r) {
-      unpack8(ld_cv_v4(static_cast<const __nv_bfloat16*>(a.part[r]) + off), f);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] += f[j];
-    }
-    *reinterpret_cast<uint4*>(my_out + off) = pack8(acc);
-  }
-  if (!grid_sync(a.grid_counter, (E * 2 + 2) * G, limit_ns(a.timeout_ms), a.err)) return;
-  if (!rank_barrier(a, 1, E + 1)) return;
+  const uint64_t budget = limit_ns(a.timeout_ms);
+  __shared__ int give_up;
+  if (tid == 0) give_up = 0;
+  __syncthreads();
 
-  // 5. all-gather rows into the residual stream, then RMSNorm + MXFP8 quantization.
+  // 1. send local sums to the owners
+  for (int row = blockIdx.x; row < M; row += G) {
+    const int owner = min(row / per, W - 1);
+    uint2* dst = static_cast<uint2*>(a.part[owner]) + ((size_t)a.rank * per + (row - owner * per)) * words;
+    for (int w = tid; w < words; w += THREADS) st_ll(dst + w, local_word(a, row, w), E);
+  }
+  // 2. reduce the owned rows and broadcast them
+  const __nv_bfloat16* resid = static_cast<const __nv_bfloat16*>(a.residual);
+  for (int row = blockIdx.x; row < M; row += G) {
+    const int owner = min(row / per, W - 1);
+    if (owner != a.rank) continue;
+    const uint2* src = static_cast<const uint2*>(a.part[a.rank]) + (size_t)(row - owner * per) * words;
+    for (int w = tid; w < words; w += THREADS) {
+      float2 acc = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(resid + (size_t)row * H + 2 * w));
+      for (int q = 0; q < W; ++q) {
+        const float2 v = unpack_bf16x2(wait_ll(src + (size_t)q * per * words + w, E, budget, a.err, &give_up));
+        acc.x += v.x;
+        acc.y += v.y;
+      }
+      const uint32_t res = pack_bf16x2(acc.x, acc.y);
+      for (int q = 0; q < W; ++q) st_ll(static_cast<uint2*>(a.out[q]) + (size_t)row * words + w, res, E);
+    }
+  }
+  // 3. gather every row, then RMSNorm + MXFP8
   __shared__ float red[THREADS / 32];
   __nv_bfloat16* res_out = static_cast<__nv_bfloat16*>(a.residual);
   const __nv_bfloat16* wgt = static_cast<const __nv_bfloat16*>(a.weight);
+  const uint2* ag = static_cast<const uint2*>(a.out[a.rank]);
   for (int row = blockIdx.x; row < M; row += G) {
-    const int owner = min(row / per, W - 1);
-    const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(a.out[owner]) + (size_t)row * H;
     float x[4][8];
     float ss = 0.f;
     const int iters = H / (THREADS * 8);
     for (int it = 0; it < iters; ++it) {
       const int c = (it * THREADS + tid) * 8;
-      const uint4 u = ld_cv_v4(src + c);  // written this call by another SM or GPU
-      *reinterpret_cast<uint4*>(res_out + (size_t)row * H + c) = u;
-      unpack8(u, x[it]);
+      uint32_t u[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) ss += x[it][j] * x[it][j];
+      for (int j = 0; j < 4; ++j) {
+        u[j] = wait_ll(ag + (size_t)row * words + c / 2 + j, E, budget, a.err, &give_up);
+        const float2 f = unpack_bf16x2(u[j]);
+        x[it][2 * j] = f.x;
+        x[it][2 * j + 1] = f.y;
+        ss += f.x * f.x + f.y * f.y;
+      }
+      *reinterpret_cast<uint4*>(res_out + (size_t)row * H + c) = make_uint4(u[0], u[1], u[2], u[3]);
     }
     ss = warp_sum(ss);
     if ((tid & 31) == 0) red[tid >> 5] = ss;
@@ -235,10 +237,10 @@ __global__ void __launch_bounds__(THREADS) fused_allreduce_norm_kernel(const Fus
     const float rstd = rsqrtf(tot / H + a.eps);
     for (int it = 0; it < iters; ++it) {
       const int c = (it * THREADS + tid) * 8;
-      float w[8], y[8];
-      unpack8(*reinterpret_cast<const uint4*>(wgt + c), w);
+      float w8[8], y[8];
+      unpack8(*reinterpret_cast<const uint4*>(wgt + c), w8);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) y[j] = x[it][j] * rstd * (w[j] + a.w_offset);
+      for (int j = 0; j < 8; ++j) y[j] = x[it][j] * rstd * (w8[j] + a.w_offset);
       if (a.normed) *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.normed) + (size_t)row * H + c) = pack8(y);
       if (a.q) {
         float amax = 0.f;
@@ -261,6 +263,13 @@ __global__ void __launch_bounds__(THREADS) fused_allreduce_norm_kernel(const Fus
         }
       }
     }
+  }
+  // The last CTA to finish advances the epoch (every CTA has read it by then).
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const uint32_t done = atomicAdd(a.grid_counter, 1u) + 1;
+    if (done % (uint32_t)G == 0) *reinterpret_cast<volatile uint32_t*>(a.epoch) = E;
   }
 }
 

@@ -5,12 +5,13 @@ peers through CUDA IPC; every rank then holds device pointers to all W blocks an
 sm_100a kernels in csrc/kernels/collective.cu load and store peer memory directly.
 Block layout (all offsets 256-byte aligned)::
 
-    [flags: 32 x u32][argmax keys: R x u64][part: R x H bf16][out: R x H bf16]
+    [flags: 32 x u32][argmax keys: R x u64][rs words: (R+W) x H/2 x 8 B][ag words: R x H/2 x 8 B]
 
-Flags 0-15 belong to the fused all-reduce (two phases x 8 ranks), 16-31 to the argmax
-exchange.  The epoch words and the grid-barrier counter are rank-local device memory;
-the kernels advance them themselves, so every call (eager or CUDA-graph replay) uses
-fresh flag values and nothing needs resetting between steps.
+The all-reduce moves "flag-in-data" words (32 bits of payload + the call's epoch in one
+8-byte store), so it needs no separate barrier; flags 16-31 belong to the argmax
+exchange.  The epoch words and the completion counter are rank-local device memory; the
+kernels advance them themselves, so every call (eager or CUDA-graph replay) uses fresh
+flag values and nothing needs resetting between steps.
 
 The collectives are issued by every rank in the same order (the model's layer order),
 which is what the kernels' epochs rely on.  Waits are bounded: a peer that never
@@ -53,6 +54,10 @@ class FusedCollectives:
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.local_keys = None
         self.timeout_ms = runtime_config().coll_timeout_ms  # bound on every cross-rank wait
+        self.large_rows = 1024
+        from .collectives import NcclCollectives
+
+        self.nccl = NcclCollectives(group, self.device)
         if max_rows and hidden:
             self.reserve(max_rows, hidden)
 
@@ -63,10 +68,12 @@ class FusedCollectives:
             return
         self.close()
         R, H = max_rows, hidden
+        # Reduce-scatter and all-gather buffers hold flag-in-data words: 8 bytes per two
+        # bf16 values (the reduce-scatter side is [world][ceil(R/world)][H/2]).
         self.off_keys = _up(32 * 4)
         self.off_part = self.off_keys + _up(R * 8)
-        self.off_out = self.off_part + _up(R * H * 2)
-        self.nbytes = self.off_out + _up(R * H * 2)
+        self.off_out = self.off_part + _up((R + self.world) * H * 4)
+        self.nbytes = self.off_out + _up(R * H * 4)
         with torch.cuda.device(self.device):
             self._base = self.C.symm_alloc(self.nbytes)
             handle = self.C.ipc_handle(self._base)
@@ -105,6 +112,12 @@ class FusedCollectives:
         H = hidden_buf.shape[-1]
         if rows > self.max_rows or H != self.hidden:
             raise ValueError(f"fused all-reduce reserved for {self.max_rows}x{self.hidden}, got {rows}x{H}")
+        if rows > self.large_rows:
+            # Prefill-sized reductions are bandwidth-bound: the flag-in-data protocol moves
+            # twice the bytes, so large ones go through NCCL's ring/NVLS kernels.
+            self.nccl.allreduce_add_rmsnorm(delta, n_terms, row_stride, term_stride, hidden_buf, norm_w, eps, rows,
+                                            xq, xsf, term_index=term_index, term_scale=term_scale)
+            return
         self.C.fused_allreduce_norm(self.rank, self.world, delta, n_terms, row_stride, term_stride, self.part_ptrs,
                                     self.out_ptrs, self.flag_ptrs, self.epoch[0:1], self.grid, hidden_buf, norm_w,
                                     1.0, eps, rows, None, xq, xsf, self.err, term_index, term_scale,
