@@ -106,7 +106,10 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
   if (k_splits > 1)
     TORCH_CHECK(out.numel() >= (k_splits - 1) * split_stride + m_rows * ldo, "split-K out too small");
   TORCH_CHECK(p.chunk_prefix == nullptr || (p.group_count && p.group_offset), "grouped mode args");
-  if (p.chunk_prefix == nullptr) TORCH_CHECK(m_rows <= p.b_rows, "m_rows > rows of b");
+  if (p.chunk_prefix == nullptr) {
+    TORCH_CHECK(m_rows <= p.b_rows, "m_rows > rows of b");
+    if (k_splits <= 1) TORCH_CHECK(out.numel() >= m_rows * ldo, "out too small for m_rows x ldo");
+  }
   rc(zs_gemm_mxf8(&p, stream()), "zs_gemm_mxf8");
 }
 
@@ -168,7 +171,8 @@ void gdn(bool prefill, const Tensor& proj, int64_t num_k_heads, int64_t num_v_he
          const Tensor& a_log, const Tensor& dt_bias, const Tensor& norm_w, double eps,
          const Tensor& slots, const Tensor& positions, int64_t rows, const OptT& out_bf16,
          const OptT& out_q, const OptT& out_sf, const OptT& seq_start, int64_t num_seqs,
-         const OptT& ckpt_rows, const OptT& ckpt_slots, int64_t max_ckpt, const OptT& err) {
+         const OptT& ckpt_rows, const OptT& ckpt_slots, int64_t max_ckpt, const OptT& err,
+         const OptT& out_slots = std::nullopt) {
   check_cuda(proj, "proj");
   check_cuda(ssm_state, "ssm_state");
   check_cuda(conv_state, "conv_state");
@@ -201,6 +205,7 @@ void gdn(bool prefill, const Tensor& proj, int64_t num_k_heads, int64_t num_v_he
   g.ckpt_slots = optptr<const int>(ckpt_slots);
   g.max_ckpt = (int)max_ckpt;
   g.err = optptr<int>(err);
+  g.out_slots = optptr<const int>(out_slots);
   rc(prefill ? zs_gdn_prefill(&g, stream()) : zs_gdn_decode(&g, stream()), "zs_gdn");
 }
 
@@ -477,11 +482,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                           const Tensor& slots, const Tensor& positions, int64_t rows,
                           const OptT& out_bf16, const OptT& out_q, const OptT& out_sf,
                           const Tensor& seq_start, int64_t num_seqs, const OptT& ckpt_rows,
-                          const OptT& ckpt_slots, int64_t max_ckpt, const OptT& err) {
+                          const OptT& ckpt_slots, int64_t max_ckpt, const OptT& err, const OptT& out_slots) {
     gdn(true, proj, hk, hv, conv_w, conv_state, ssm_state, a_log, dt_bias, norm_w, eps, slots,
         positions, rows, out_bf16, out_q, out_sf, seq_start, num_seqs, ckpt_rows, ckpt_slots,
-        max_ckpt, err);
-  });
+        max_ckpt, err, out_slots);
+  }, py::arg("proj"), py::arg("hk"), py::arg("hv"), py::arg("conv_w"), py::arg("conv_state"), py::arg("ssm_state"),
+     py::arg("a_log"), py::arg("dt_bias"), py::arg("norm_w"), py::arg("eps"), py::arg("slots"), py::arg("positions"),
+     py::arg("rows"), py::arg("out_bf16"), py::arg("out_q"), py::arg("out_sf"), py::arg("seq_start"),
+     py::arg("num_seqs"), py::arg("ckpt_rows"), py::arg("ckpt_slots"), py::arg("max_ckpt"), py::arg("err"),
+     py::arg("out_slots") = py::none());
   m.def("attn_prologue", &attn_prologue);
   m.def("attn_decode", &attn_decode);
   m.def("moe_route", &moe_route, py::arg("logits"), py::arg("rows"), py::arg("num_experts"), py::arg("top_k"),

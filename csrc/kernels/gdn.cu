@@ -251,10 +251,14 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_kernel(const GdnArgs a
     }
     __syncthreads();
   }
+  // Final state: back to the input slot, or to out_slots[seq] (speculative verify keeps
+  // the pre-step state intact for the roll-back replay).
+  const int oslot = a.out_slots != nullptr ? a.out_slots[seq] : slot;
+  float* op = a.ssm_state + (((size_t)oslot * a.num_v_heads + vh) * DV + vr) * DK + kq * 32;
 #pragma unroll
   for (int i = 0; i < 8; ++i)
-    reinterpret_cast<float4*>(sp)[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
-  store_window(a, slot, pos0 + (r1 - r0), kh, vh, s, (vh % ratio) == 0);
+    reinterpret_cast<float4*>(op)[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
+  store_window(a, oslot, pos0 + (r1 - r0), kh, vh, s, (vh % ratio) == 0);
 }
 
 }  // namespace gdn

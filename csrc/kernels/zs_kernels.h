@@ -131,6 +131,8 @@ typedef struct GdnArgs {
   const int* ckpt_slots;   // prefill: matching checkpoint slot ids
   int max_ckpt;
   int* err;
+  const int* out_slots;    // prefill: optional [num_seqs] slot receiving the final state (and
+                           // conv window) instead of the input slot, which stays untouched
 } GdnArgs;
 
 int zs_gdn_decode(const GdnArgs* args, cudaStream_t stream);

@@ -92,7 +92,7 @@ class Qwen35Runner:
     def __init__(self, cfg: Qwen35Config, *, device="cuda", weights=None, max_seqs: int = 256,
                  max_prefill_tokens: int = 4096, num_pages: int = 4096, page_size: int = 16,
                  max_model_len: int = 4096, num_ckpt_slots: int = 0, tp_rank: int = 0, tp_size: int = 1,
-                 collectives=None, seed: int = 0):
+                 collectives=None, seed: int = 0, num_spec_tokens: int = 0):
         self.cfg = cfg
         self.dev = torch.device(device)
         self.C = _ext.load()
@@ -123,12 +123,22 @@ class Qwen35Runner:
         self.groups = self.e_local + 1
         self.top_k = cfg.num_experts_per_tok
         self.k1 = self.top_k + 1
-        self.num_slots = max_seqs + num_ckpt_slots + 1  # last slot = padding dummy
+        # Speculative decoding keeps one extra recurrent-state slot per request slot: a
+        # verify step writes its final state there and leaves the pre-step state intact.
+        self.num_spec = num_spec_tokens if cfg.mtp_num_hidden_layers > 0 else 0
+        self.spec_slot_base = max_seqs + num_ckpt_slots
+        self.num_slots = self.spec_slot_base + (max_seqs if self.num_spec else 0) + 1  # last = padding dummy
         self.dummy_slot = self.num_slots - 1
-        self._load_weights(weights or RandomWeights(cfg, seed=seed))
+        src = weights or RandomWeights(cfg, seed=seed)
+        self._load_weights(src)
         self._alloc_state()
         self._alloc_buffers()
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.spec = None
+        if self.num_spec:
+            from .qwen35_spec import SpecDecoder
+
+            self.spec = SpecDecoder(self, src)
 
     # ------------------------------------------------------------------ weights
     def _shard_rows(self, t: torch.Tensor, parts: list[int]) -> torch.Tensor:
@@ -295,12 +305,15 @@ class Qwen35Runner:
         b["pair_w"] = torch.zeros(R, self.k1, dtype=torch.float32, device=dev)
         vt = self.lm_head.n_pad // 128
         self.vocab_tiles = vt
-        b["lm_keys"] = torch.zeros(self.max_seqs, vt, dtype=torch.int64, device=dev)
-        b["out_ids"] = torch.zeros(self.max_seqs, **i32)
-        b["out_vals"] = torch.zeros(self.max_seqs, dtype=torch.float32, device=dev)
-        b["out_keys"] = torch.zeros(self.max_seqs, dtype=torch.int64, device=dev)
+        # lm_head rows: one per sequence; with speculative decoding every verify row and
+        # every MTP catch-up row (up to a whole step's rows).
+        self.lm_rows = R if self.num_spec else self.max_seqs
+        b["lm_keys"] = torch.zeros(self.lm_rows, vt, dtype=torch.int64, device=dev)
+        b["out_ids"] = torch.zeros(self.lm_rows, **i32)
+        b["out_vals"] = torch.zeros(self.lm_rows, dtype=torch.float32, device=dev)
+        b["out_keys"] = torch.zeros(self.lm_rows, dtype=torch.int64, device=dev)
         b["err"] = torch.zeros(1, **i32)
-        b["xq_last"] = torch.zeros(_pad128(self.max_seqs), H, dtype=torch.uint8, device=dev)
+        b["xq_last"] = torch.zeros(_pad128(self.lm_rows), H, dtype=torch.uint8, device=dev)
         # Step inputs (static so graphs can read them): ids, positions, slots, seq_lens,
         # packed as one [4, R] block so a step's inputs arrive in a single H2D copy.
         b["inputs"] = torch.zeros(4, R, **i32)
@@ -366,29 +379,34 @@ class Qwen35Runner:
         ctas = rows * self.hkv
         return int(max(1, min(self.max_splits, math.ceil(1200 / max(ctas, 1)))))
 
-    def _proj_out(self, w: PackedLinear, xq, xsf, rows: int, norm_w) -> None:
+    def _proj_out(self, w: PackedLinear, xq, xsf, rows: int, norm_w, hidden=None) -> None:
         """Row-parallel output projection (GDN out_proj / attention o_proj) into f32
         split-K partials, then residual add + RMSNorm (+ all-reduce across ranks)."""
         H = self.cfg.hidden_size
         s = self._k_splits(w, rows)
         self._gemm(w, xq, xsf, rows, self.buf["delta_f32"], H, EPI_F32, k_splits=s)
-        self._row_parallel_reduce(self.buf["delta_f32"], rows, s, norm_w, rows * H, H)
+        self._row_parallel_reduce(self.buf["delta_f32"], rows, s, norm_w, rows * H, H, hidden=hidden)
 
     def _row_parallel_reduce(self, delta_rows: torch.Tensor, rows: int, n_terms: int, norm_w, term_stride: int,
-                             row_stride: int, term_index=None, term_scale=None):
+                             row_stride: int, term_index=None, term_scale=None, hidden=None):
         """hidden += sum of delta terms (all-reduced across tp ranks), then RMSNorm -> xq.
         With ``term_index`` [rows, n_terms] the terms are gathered rows of delta (negative:
         not produced on this rank), scaled by ``term_scale``."""
         b, H = self.buf, self.cfg.hidden_size
+        hidden = b["hidden"] if hidden is None else hidden
         if self.tp > 1:
-            self.coll.allreduce_add_rmsnorm(delta_rows, n_terms, row_stride, term_stride, b["hidden"], norm_w,
+            self.coll.allreduce_add_rmsnorm(delta_rows, n_terms, row_stride, term_stride, hidden, norm_w,
                                             self.eps, rows, b["xq"], b["xsf"], term_index=term_index,
                                             term_scale=term_scale)
             return
-        self.C.add_rmsnorm_quant(b["hidden"], delta_rows, n_terms, row_stride, term_stride, norm_w, 1.0, self.eps,
+        self.C.add_rmsnorm_quant(hidden, delta_rows, n_terms, row_stride, term_stride, norm_w, 1.0, self.eps,
                                  rows, None, b["xq"], b["xsf"], term_index, term_scale)
 
-    def _layers(self, rows: int, decode: bool, num_seqs: int = 0, ckpt=None) -> None:
+    def _layers(self, rows: int, decode: bool, num_seqs: int = 0, ckpt=None, gdn_out_slots=None,
+                proj_store=None) -> None:
+        """All decoder layers over the staged rows.  Varlen (prefill / verify) steps may
+        redirect each sequence's final GDN state (`gdn_out_slots`) and keep every GDN layer's
+        input projection (`proj_store[layer]`) for a later replay."""
         cfg, C, b = self.cfg, self.C, self.buf
         H = cfg.hidden_size
         pos, slot, lens = b["in_pos"][:rows], b["in_slot"][:rows], b["in_len"][:rows]
@@ -397,7 +415,10 @@ class Qwen35Runner:
         for li, L in enumerate(self.layers):
             if L["type"] == "linear_attention":
                 gi = self.gdn_index[li]
-                proj = b["proj"][:rows * self.gdn_w].view(rows, self.gdn_w)
+                if proj_store is not None:
+                    proj = proj_store[gi][:rows]
+                else:
+                    proj = b["proj"][:rows * self.gdn_w].view(rows, self.gdn_w)
                 self._gemm(L["in_proj"], b["xq"], b["xsf"], rows, proj, self.gdn_w)
                 midq = self._mid(self.hv * 128)
                 args = (proj, self.hk, self.hv, L["conv_w"], self.conv_state[gi], self.ssm_state[gi], L["a_log"],
@@ -407,7 +428,7 @@ class Qwen35Runner:
                 else:
                     ck_rows, ck_slots, max_ck = ckpt if ckpt is not None else (None, None, 0)
                     C.gdn_prefill(*args, b["seq_start"][:num_seqs + 1], num_seqs, ck_rows, ck_slots, max_ck,
-                                  b["err"])
+                                  b["err"], gdn_out_slots)
                 self._proj_out(L["out_proj"], midq, b["midsf"], rows, L["post_norm"])
             else:
                 ai = self.attn_index[li]
@@ -444,6 +465,8 @@ class Qwen35Runner:
         self._gemm(L["down"], b["act"], b["act_sf"], rows, b["moe_y"], cfg.hidden_size, EPI_BF16, grouped=True)
 
     def _lm_head_argmax(self, rows: int, xq=None, xsf=None, pos=None) -> None:
+        if rows > self.lm_rows:
+            raise ValueError(f"lm_head over {rows} rows exceeds the {self.lm_rows}-row output buffers")
         """Greedy (temperature 0) or sampled next token of each row: the lm_head GEMM's
         epilogue reduces each vocab tile to one packed key of the (Gumbel-perturbed, for
         sampling rows) logits; the keys are then max-reduced locally or across ranks."""
@@ -473,14 +496,21 @@ class Qwen35Runner:
         self._layers(rows, decode=False, num_seqs=num_seqs, ckpt=ckpt)
         # lm_head only on each sequence's last row: gather those normed rows.
         last = b["seq_start"][1:num_seqs + 1].long() - 1
-        H = self.cfg.hidden_size
-        xq_last = b["xq_last"]
-        codes = self._gather_sf(b["xsf"], last, H)
-        xq_last[:num_seqs] = b["xq"][last]
-        sf_last = mx.atoms_from_codes(codes)
-        b["samp_pos"][:num_seqs] = b["in_pos"][last]
-        self._lm_head_argmax(num_seqs, xq_last, sf_last, pos=b["samp_pos"])
-        return b["out_ids"][:num_seqs]
+        return self.lm_head_rows(last, b["xq_last"])
+
+    def lm_head_rows(self, row_idx: torch.Tensor, xq_buf: torch.Tensor) -> torch.Tensor:
+        """Next token of the selected rows of the last forward (normed MXFP8 rows gathered
+        into `xq_buf`, then the lm_head GEMM + argmax / sampling)."""
+        b, H = self.buf, self.cfg.hidden_size
+        n = int(row_idx.numel())
+        if n > self.lm_rows or n > xq_buf.shape[0]:
+            raise ValueError(f"lm_head over {n} rows exceeds the {self.lm_rows}-row output buffers")
+        codes = self._gather_sf(b["xsf"], row_idx, H)
+        xq_buf[:n] = b["xq"][row_idx]
+        sf = mx.atoms_from_codes(codes)
+        b["samp_pos"][:n] = b["in_pos"][row_idx]
+        self._lm_head_argmax(n, xq_buf, sf, pos=b["samp_pos"])
+        return b["out_ids"][:n]
 
     def set_sampling(self, temperatures, seeds) -> None:
         """Per-sequence temperature (0 = greedy) and seed for the next steps' lm_head.

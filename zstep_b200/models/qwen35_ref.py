@@ -32,6 +32,9 @@ class SeqState:
     keys: list = field(default_factory=list)   # per attn layer: [T, Hkv, D]
     values: list = field(default_factory=list)
     pos: int = 0
+    hidden = None                              # residual stream after the last layer (pre final norm)
+    mtp_keys = None                            # MTP layer KV, indexed by position: [T, Hkv, D]
+    mtp_values = None
 
 
 class Qwen35Reference:
@@ -73,6 +76,18 @@ class Qwen35Reference:
                 L.update(self._attn(g, p))
             L.update(self._moe(g, p))
             self.layers.append(L)
+        self.mtp = None
+        if c.mtp_num_hidden_layers > 0:
+            try:
+                p = "mtp.layer."
+                M = {"fc": self._w(g("mtp.fc")), "norm_e": g("mtp.pre_fc_norm_embedding"),
+                     "norm_h": g("mtp.pre_fc_norm_hidden"), "norm": g("mtp.norm"),
+                     "input_norm": g(p + "input_norm"), "post_norm": g(p + "post_norm")}
+                M.update(self._attn(g, p))
+                M.update(self._moe(g, p))
+                self.mtp = M
+            except KeyError:
+                self.mtp = None
 
     # ------------------------------------------------------------------ weights
     def _w(self, w: torch.Tensor) -> torch.Tensor:
@@ -127,8 +142,12 @@ class Qwen35Reference:
         return s
 
     def clone_state(self, s: SeqState) -> SeqState:
-        return SeqState(gdn=[(a.clone(), b.clone()) for a, b in s.gdn], keys=[k.clone() for k in s.keys],
-                        values=[v.clone() for v in s.values], pos=s.pos)
+        n = SeqState(gdn=[(a.clone(), b.clone()) for a, b in s.gdn], keys=[k.clone() for k in s.keys],
+                     values=[v.clone() for v in s.values], pos=s.pos)
+        n.hidden = None if s.hidden is None else s.hidden.clone()
+        n.mtp_keys = None if s.mtp_keys is None else s.mtp_keys.clone()
+        n.mtp_values = None if s.mtp_values is None else s.mtp_values.clone()
+        return n
 
     # ------------------------------------------------------------------ forward
     def _q(self, x: torch.Tensor) -> torch.Tensor:
@@ -178,7 +197,36 @@ class Qwen35Reference:
             nw = self.layers[li + 1]["input_norm"] if li + 1 < len(self.layers) else self.final_norm
             res, normed = self._add_norm(res, self._reduce(moe), nw, eps)
         s.pos += 1
+        s.hidden = res
         return self.lm_head @ self._q(normed)
+
+    def mtp_step(self, s: SeqState, token: int, hidden: torch.Tensor, pos: int):
+        """One multi-token-prediction step: the next token's embedding and the hidden state
+        at `pos` (target's or the previous MTP step's) -> (draft logits shard, MTP hidden).
+        The MTP attention layer keeps its own KV at `pos` (entries past `pos` are dropped)."""
+        c, M = self.cfg, self.mtp
+        eps = c.rms_norm_eps
+        emb = R.bfr(self.embed[token]) if self.quant else self.embed[token]
+        fc_in = torch.cat([self._bf(R.rmsnorm(emb, M["norm_e"], eps)), self._bf(R.rmsnorm(hidden, M["norm_h"], eps))])
+        res = self._bf(M["fc"] @ self._q(fc_in))
+        normed = R.rmsnorm(res, M["input_norm"], eps)
+        qkv = self._bf(M["qkv"] @ self._q(normed))
+        q, gate, k, v = self._prologue(qkv, pos, M)
+        if s.mtp_keys is None:
+            s.mtp_keys = torch.zeros(0, self.hkv, self.D, device=self.dev)
+            s.mtp_values = torch.zeros(0, self.hkv, self.D, device=self.dev)
+        keys, values = s.mtp_keys[:pos], s.mtp_values[:pos]
+        if keys.shape[0] < pos:  # positions never filled (e.g. chunk boundaries) read as zeros
+            pad = torch.zeros(pos - keys.shape[0], self.hkv, self.D, device=self.dev)
+            keys, values = torch.cat([keys, pad]), torch.cat([values, pad])
+        s.mtp_keys = torch.cat([keys, k[None]], 0)
+        s.mtp_values = torch.cat([values, v[None]], 0)
+        out = self._attention(q, gate, s.mtp_keys, s.mtp_values)
+        delta = self._bf(M["o_proj"] @ self._q(out))
+        res, normed = self._add_norm(res, self._reduce(delta), M["post_norm"], eps)
+        moe = self._moe_fwd(self._q(normed), M)
+        res, normed = self._add_norm(res, self._reduce(moe), M["norm"], eps)
+        return self.lm_head @ self._q(normed), res
 
     def _add_norm(self, res, delta, w, eps):
         r = res + delta

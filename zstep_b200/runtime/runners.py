@@ -147,11 +147,12 @@ class GpuRunner:
         self.cfg = _resolve_config(args.model)
         self.dev = torch.device("cuda", torch.cuda.current_device())
         coll = make_collectives(self.dev) if world > 1 else None
+        num_spec = args.num_spec_tokens if args.spec_method == "mtp" else 0
         self.r = Qwen35Runner(self.cfg, device=self.dev, weights=_weights(self.cfg, args.model, args.seed),
                               max_seqs=geo.max_seqs, max_prefill_tokens=geo.max_step_tokens,
                               num_pages=args.num_pages, page_size=geo.page_size, max_model_len=args.max_model_len,
                               num_ckpt_slots=args.num_ckpt_slots, tp_rank=rank, tp_size=world, collectives=coll,
-                              seed=args.seed)
+                              seed=args.seed, num_spec_tokens=num_spec)
         self.rank = rank
 
     def execute(self, plan: dict) -> np.ndarray:
@@ -165,6 +166,8 @@ class GpuRunner:
             if src >= 0:
                 r.copy_recurrent_state(src, int(plan["seq_slot"][i]))
         rows = plan["num_rows"]
+        if r.spec is not None:
+            return self._execute_spec(plan, n, out)
         sampling = bool(plan["flags"] & wire.FLAG_SAMPLING)
         decode_only = bool(plan["flags"] & wire.FLAG_DECODE_ONLY)
         if sampling:
@@ -191,6 +194,86 @@ class GpuRunner:
             if int(plan["sample_row"][i]) >= 0:
                 out[i]["num_tokens"] = 1
                 out[i]["tokens"][0] = int(ids[i])
+        return out
+
+    def _execute_spec(self, plan: dict, n: int, out):
+        """Steps of an engine with MTP speculative decoding (eager): one varlen target forward
+        over all rows (verify rows of drafting sequences included), greedy acceptance,
+        recurrent-state replay of the accepted rows, then MTP drafts for the next step."""
+        r = self.r
+        rows = plan["num_rows"]
+        qs = plan["query_start"].tolist()
+        ids = plan["token_ids"][:rows].tolist()
+        pos = plan["positions"][:rows].tolist()
+        rslot = plan["row_slot"][:rows].tolist()
+        sw = plan["spec_width"][:n].tolist()
+        srow = plan["sample_row"][:n].tolist()
+        r.stage(ids, pos, rslot, seq_start=qs[:n + 1])
+        lm_rows, seq_lm, verify_slots = [], [], []
+        for i in range(n):
+            r0, r1 = qs[i], qs[i + 1]
+            if sw[i] > 0:
+                seq_lm.append((len(lm_rows), r1 - r0))
+                lm_rows.extend(range(r0, r1))
+                verify_slots.append(r.spec_slot_base + int(plan["seq_slot"][i]))
+            elif srow[i] >= 0:
+                seq_lm.append((len(lm_rows), 1))
+                lm_rows.append(r1 - 1)
+                verify_slots.append(None)
+            else:
+                seq_lm.append(None)
+                verify_slots.append(None)
+        ck = None
+        if len(plan["ckpt_row"]):
+            ck = r.checkpoint_args(plan["ckpt_row"], plan["ckpt_slot"], plan["query_start"])
+        lm_t = torch.tensor(lm_rows, dtype=torch.long, device=r.dev)
+        targets = r.spec.forward(rows, n, lm_t, verify_slots, ckpt=ck).cpu().tolist() if lm_rows else []
+        replay, replay_slots, replay_pos = [], [], []
+        m_ids, m_pos, m_slot, m_rows, last_of_seq, drafting = [], [], [], [], [], []
+        for i in range(n):
+            r0, r1 = qs[i], qs[i + 1]
+            out[i]["req_slot"] = int(plan["seq_slot"][i])
+            if seq_lm[i] is None:  # prefill chunk that does not sample: MTP catch-up only
+                for rr in range(r0, r1 - 1):
+                    m_ids.append(ids[rr + 1]), m_pos.append(pos[rr]), m_slot.append(rslot[rr]), m_rows.append(rr)
+                continue
+            st, cnt = seq_lm[i]
+            t = targets[st:st + cnt]
+            if sw[i] > 0:
+                drafts = ids[r0 + 1:r1]
+                acc = []
+                for j, d in enumerate(drafts):
+                    if t[j] != d:
+                        acc.append(t[j])
+                        break
+                    acc.append(d)
+                else:
+                    acc.append(t[len(drafts)])
+                replay.append((r0, len(acc)))
+                replay_slots.append(rslot[r0])
+                replay_pos.append(pos[r0])
+                for j, tok in enumerate(acc):  # the target token after row r0+j is acc[j]
+                    m_ids.append(tok), m_pos.append(pos[r0 + j]), m_slot.append(rslot[r0]), m_rows.append(r0 + j)
+            else:
+                acc = [t[0]]
+                for rr in range(r0, r1):
+                    nxt = ids[rr + 1] if rr + 1 < r1 else acc[0]
+                    m_ids.append(nxt), m_pos.append(pos[rr]), m_slot.append(rslot[rr]), m_rows.append(rr)
+            out[i]["num_tokens"] = len(acc)
+            out[i]["tokens"][:len(acc)] = acc
+            last_of_seq.append(len(m_ids) - 1)
+            drafting.append(i)
+        r.spec.replay(replay, replay_slots, replay_pos)
+        if m_ids:
+            rows_t = torch.tensor(m_rows, dtype=torch.long, device=r.dev)
+            if drafting:
+                drafts = r.spec.draft(m_ids, m_pos, m_slot, rows_t, last_of_seq)
+                for k, i in enumerate(drafting):
+                    out[i]["next_drafts"][:len(drafts[k])] = drafts[k]
+                    out[i]["num_drafts"] = len(drafts[k])
+            else:
+                r.spec.stage_mtp(m_ids, m_pos, m_slot, rows_t, r.buf["hidden"])
+                r.spec.mtp(len(m_ids))
         return out
 
     def close(self) -> None:
