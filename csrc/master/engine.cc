@@ -366,6 +366,7 @@ std::vector<TokenEvent> Engine::step() {
     const int32_t n_tok = std::max(1, std::min<int32_t>(out.num_tokens, wire::kMaxSpecTokens));
     if (s->rows > 1 && !was_prefill) {
       stats_.spec_verify_rows += s->rows;
+      stats_.spec_verify_steps += 1;
       stats_.spec_accepted += uint32_t(n_tok - 1);
       s->computed += uint32_t(n_tok);  // fed row 0 + accepted drafts
     } else {

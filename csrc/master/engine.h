@@ -123,6 +123,7 @@ struct EngineStats {
   uint64_t steps = 0, decode_steps = 0, prefill_tokens = 0, decode_tokens = 0, preemptions = 0;
   uint64_t prefix_queries = 0, prefix_query_tokens = 0, prefix_hit_tokens = 0, prefix_evictions = 0;
   uint64_t spec_drafts = 0, spec_accepted = 0, spec_verify_rows = 0;
+  uint64_t spec_verify_steps = 0;  // sequence-level verify steps (one per sequence per step)
   uint64_t last_gpu_us = 0;
 };
 

@@ -501,11 +501,11 @@ std::string HttpServer::render_metrics(serve::ServeLoop* loop, const ServerConfi
   for (const auto& kv : outcomes)
     o += "zstep:request_outcomes_total{" + model + ",outcome=\"" + kv.first + "\"} " + std::to_string(kv.second) + "\n";
   if (st.spec_drafts > 0 || st.spec_verify_rows > 0) {
-    counter("spec_decode_num_drafts_total", "Verify steps with drafts.", (double)st.spec_verify_rows);
+    counter("spec_decode_num_drafts_total", "Verify steps with drafts.", (double)st.spec_verify_steps);
     counter("spec_decode_num_draft_tokens_total", "Draft tokens proposed.", (double)st.spec_drafts);
     counter("spec_decode_num_accepted_tokens_total", "Draft tokens accepted.", (double)st.spec_accepted);
     gauge("spec_decode_mean_acceptance_length", "Mean tokens per verify step (accepted + bonus).",
-          st.spec_verify_rows ? 1.0 + (double)st.spec_accepted / (double)st.spec_verify_rows : 0.0);
+          st.spec_verify_steps ? 1.0 + (double)st.spec_accepted / (double)st.spec_verify_steps : 0.0);
   }
   hist("time_to_first_token_seconds", "Time to first token.", m.ttft);
   hist("time_per_output_token_seconds", "Time per output token after the first.", m.tpot);

@@ -87,7 +87,8 @@ const char* kRunUsage =
     "  --prompt TEXT                Generate from this text (chat template applied)\n"
     "  --max-tokens N               Tokens to generate (default 32)\n"
     "  --verify-greedy-json PATH    {\"prompts\": [[ids]], \"expected\": [[ids]]}: exit 1 on mismatch\n"
-    "  --bench-tiers SPEC[,SPEC]    label:concurrency:prompts:input_len:output_len\n"
+    "  --bench-tiers SPEC[,SPEC]    label:concurrency:prompts:input_len:output_len[:prefix_len:num_prefixes]\n"
+    "                               (with prefix fields, prompt i = shared prefix i % num_prefixes + input_len ids)\n"
     "  --bench-repeats N            Interleaved repeats per tier (default 1)\n"
     "  --seed N                     Prompt seed (default 0)\n";
 
@@ -438,10 +439,21 @@ double pct(std::vector<double> v, double q) {
 struct Tier {
   std::string label;
   int conc = 1, prompts = 1, in = 128, out = 128;
+  int prefix_len = 0, num_prefixes = 0;  // shared random prefixes: prompt i = prefix[i % n] + in random ids
 };
 
 json::Value run_tier(engine::Engine& e, const Tier& t, uint64_t seed, int32_t vocab, std::string* err) {
-  auto prompts = engine::random_prompts(seed, (size_t)t.prompts, (size_t)t.in, 10, std::max<int32_t>(11, vocab - 10));
+  const int32_t hi = std::max<int32_t>(11, vocab - 10);
+  auto prompts = engine::random_prompts(seed, (size_t)t.prompts, (size_t)t.in, 10, hi);
+  if (t.prefix_len > 0 && t.num_prefixes > 0) {
+    const auto prefixes = engine::random_prompts(seed ^ 0x5EC0DEull, (size_t)t.num_prefixes, (size_t)t.prefix_len, 10, hi);
+    for (size_t i = 0; i < prompts.size(); ++i) {
+      std::vector<int32_t> p = prefixes[i % prefixes.size()];
+      p.insert(p.end(), prompts[i].begin(), prompts[i].end());
+      prompts[i].swap(p);
+    }
+  }
+  const engine::EngineStats st0 = e.stats();
   std::map<uint64_t, double> t_submit, t_first, t_last;
   std::map<uint64_t, uint32_t> produced;
   size_t next = 0, done = 0;
@@ -496,6 +508,16 @@ json::Value run_tier(engine::Engine& e, const Tier& t, uint64_t seed, int32_t vo
   r.set("p99_ttft_ms", pct(ttft, 0.99));
   r.set("mean_tpot_ms", mean_of(tpot));
   r.set("p50_tpot_ms", pct(tpot, 0.5));
+  const engine::EngineStats st1 = e.stats();
+  if (t.prefix_len > 0) {
+    r.set("shared_prefix_len", t.prefix_len);
+    r.set("num_prefixes", t.num_prefixes);
+  }
+  const uint64_t steps = st1.spec_verify_steps - st0.spec_verify_steps;
+  if (steps > 0) {
+    r.set("spec_verify_steps", (int64_t)steps);
+    r.set("mean_acceptance_length", 1.0 + (double)(st1.spec_accepted - st0.spec_accepted) / (double)steps);
+  }
   return r;
 }
 
@@ -565,11 +587,20 @@ int cmd_run(const Args& a) {
       std::stringstream s2(spec);
       std::string part;
       while (std::getline(s2, part, ':')) f.push_back(part);
-      if (f.size() != 5) {
-        fprintf(stderr, "zstep run: tier `%s` is not label:conc:prompts:in:out\n", spec.c_str());
+      if (f.size() != 5 && f.size() != 7) {
+        fprintf(stderr, "zstep run: tier `%s` is not label:conc:prompts:in:out[:prefix_len:num_prefixes]\n",
+                spec.c_str());
         return 2;
       }
       Tier t{f[0], atoi(f[1].c_str()), atoi(f[2].c_str()), atoi(f[3].c_str()), atoi(f[4].c_str())};
+      if (f.size() == 7) {
+        t.prefix_len = atoi(f[5].c_str());
+        t.num_prefixes = atoi(f[6].c_str());
+        if (t.prefix_len < 1 || t.num_prefixes < 1) {
+          fprintf(stderr, "zstep run: tier `%s` has non-positive prefix fields\n", spec.c_str());
+          return 2;
+        }
+      }
       if (t.conc < 1 || t.prompts < 1 || t.in < 1 || t.out < 1) {
         fprintf(stderr, "zstep run: tier `%s` has non-positive fields\n", spec.c_str());
         return 2;

@@ -274,7 +274,8 @@ PYBIND11_MODULE(_master, m) {
       .def_readonly("prefix_query_tokens", &engine::EngineStats::prefix_query_tokens)
       .def_readonly("prefix_evictions", &engine::EngineStats::prefix_evictions)
       .def_readonly("spec_drafts", &engine::EngineStats::spec_drafts)
-      .def_readonly("spec_accepted", &engine::EngineStats::spec_accepted);
+      .def_readonly("spec_accepted", &engine::EngineStats::spec_accepted)
+      .def_readonly("spec_verify_steps", &engine::EngineStats::spec_verify_steps);
   py::class_<engine::Engine, std::shared_ptr<engine::Engine>>(m, "Engine")
       .def(py::init([](engine::Config cfg, py::function backend) {
              return std::make_shared<engine::Engine>(cfg, std::make_shared<PyBackend>(backend));

@@ -77,6 +77,15 @@ def test_bench_tiers_report(model_dir):
     assert "git_sha" in rep["provenance"]
 
 
+def test_bench_tiers_shared_prefix(model_dir):
+    r = run("run", "--mock", "--model-dir", model_dir, "--bench-tiers", "apc:2:6:8:4:48:2", "--max-seqs", "4",
+            "--max-step-tokens", "256", "--apc-node-pages", "1")
+    assert r.returncode == 0, r.stderr
+    run0 = json.loads(r.stdout)["tiers"][0]["runs"][0]
+    assert run0["shared_prefix_len"] == 48 and run0["num_prefixes"] == 2 and run0["output_tok_s"] > 0
+    assert run("run", "--mock", "--model-dir", model_dir, "--bench-tiers", "x:1:1:8:4:0:2").returncode == 2
+
+
 def test_strict_flags(model_dir):
     r = run("serve", "--mock", "--model-dir", model_dir, "--bogus", "1")
     assert r.returncode == 2 and "unknown flag --bogus" in r.stderr

@@ -1,0 +1,55 @@
+"""The native `zstep run` driving a B200 worker end to end: greedy generation through the
+shared-memory coordinator, and MTP speculative decoding producing the same tokens."""
+
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+from tests.test_tokenizer import build_hf_tokenizer
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+BIN = os.path.join(ROOT, "zstep_b200", "bin", "zstep")
+PROMPTS = [[11, 200, 3000, 45, 7], [900, 901, 902], list(range(100, 140))]
+
+
+@pytest.fixture(scope="module")
+def model_dir(tmp_path_factory):
+    if not os.path.exists(BIN):
+        subprocess.run(["make", "-C", os.path.join(ROOT, "csrc", "master")], check=True, capture_output=True)
+    d = str(tmp_path_factory.mktemp("model"))
+    build_hf_tokenizer(d)
+    return d
+
+
+def zstep_run(model_dir, *extra, timeout=900):
+    args = [BIN, "run", "--model-dir", model_dir, "--model", "qwen3.5-small", "--device", "cuda", "--max-seqs", "8",
+            "--max-model-len", "512", "--num-kv-pages", "256", "--max-step-tokens", "256", "--max-prefill-chunk",
+            "128", "--python", sys.executable, "--worker-root", ROOT, *extra]
+    r = subprocess.run(args, capture_output=True, text=True, timeout=timeout)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    return json.loads(r.stdout.strip().splitlines()[-1])
+
+
+def test_greedy_and_mtp_agree(model_dir):
+    outs = {}
+    for method in ("none", "mtp"):
+        res = []
+        for p in PROMPTS:
+            o = zstep_run(model_dir, "--prompt-ids", ",".join(map(str, p)), "--max-tokens", "16",
+                          "--speculative-method", method)
+            res.append(o["tokens"])
+        outs[method] = res
+    assert all(len(t) == 16 for t in outs["none"])
+    same = sum(a == b for a, b in zip(outs["none"], outs["mtp"]))
+    assert same >= len(PROMPTS) - 1, outs
+
+
+def test_bench_tier_with_mtp_and_shared_prefix(model_dir):
+    rep = zstep_run(model_dir, "--speculative-method", "mtp", "--bench-tiers", "mtp:4:8:32:16:64:2")
+    run0 = rep["tiers"][0]["runs"][0]
+    assert run0["output_tok_s"] > 0 and run0["shared_prefix_len"] == 64
+    assert run0["mean_acceptance_length"] >= 1.0
