@@ -1,0 +1,127 @@
+"""The DeepSeek-style reference model (MLA + DSA indexer + mHC + sigmoid grouped MoE):
+internal consistency checks on CPU, and the MXFP4 format."""
+
+import threading
+
+import torch
+
+from zstep_b200.config import deepseek_tiny
+from zstep_b200.models.deepseek_ref import DeepSeekReference, rope_halves, sinkhorn
+from zstep_b200.models.deepseek_weights import DeepSeekRandomWeights
+from zstep_b200.ops import mx
+
+
+def test_sinkhorn_is_doubly_stochastic():
+    g = torch.Generator().manual_seed(0)
+    p = sinkhorn(torch.randn(4, 4, generator=g) * 3, 20)
+    assert torch.allclose(p.sum(0), torch.ones(4), atol=1e-3)
+    assert torch.allclose(p.sum(1), torch.ones(4), atol=1e-6)
+    assert (p > 0).all()
+
+
+def test_mxfp4_round_trip_and_widening():
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(64, 128, generator=g)
+    packed, code = mx.quantize_fp4(x)
+    d = mx.dequantize_fp4(packed, code)
+    assert ((d - x).norm() / x.norm()) < 0.15
+    assert torch.equal(mx.dequantize(mx.fp4_to_e4m3(packed), code), d)  # widening is exact
+    ties = torch.tensor([[0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, -0.75] * 4])
+    assert mx.dequantize_fp4(*mx.quantize_fp4(ties))[0, :8].tolist() == [0, 1, 1, 2, 2, 4, 4, -1]
+
+
+def _explicit_mla(ref, L, q, kv_rows, pos):
+    """Non-absorbed MLA: per-head keys [W_UK c_kv | k_pe] and values W_UV c_kv."""
+    c = ref.cfg
+    kl, nope = c.kv_lora_rank, c.qk_nope_head_dim
+    ckv, kpe = kv_rows[:, :kl], kv_rows[:, kl:]
+    out = []
+    for h in range(ref.hl):
+        k = torch.cat([ckv @ L["w_uk"][h].T, kpe], dim=1)
+        v = ckv @ L["w_uv"][h].T
+        qh = torch.cat([q[h, :nope], rope_halves(q[h, nope:], pos, c.rope_theta)])
+        p = torch.softmax(k @ qh * c.qk_head_dim ** -0.5, dim=0)
+        out.append(p @ v)
+    return torch.cat(out)
+
+
+def test_absorbed_mla_equals_explicit():
+    cfg = deepseek_tiny()
+    ref = DeepSeekReference(cfg, DeepSeekRandomWeights(cfg, seed=3))
+    L = ref.layers[0]
+    g = torch.Generator().manual_seed(2)
+    T = 6
+    kv_rows = torch.randn(T, cfg.kv_cache_dim, generator=g)
+    q = torch.randn(ref.hl, cfg.qk_head_dim, generator=g)
+    exp = _explicit_mla(ref, L, q, kv_rows, T - 1)
+    # Absorbed path, as the reference's attention computes it.
+    kl, nope = cfg.kv_lora_rank, cfg.qk_nope_head_dim
+    q_lat = torch.einsum("hd,hdc->hc", q[:, :nope], L["w_uk"])
+    q_pe = rope_halves(q[:, nope:], T - 1, cfg.rope_theta)
+    p = torch.softmax((q_lat @ kv_rows[:, :kl].T + q_pe @ kv_rows[:, kl:].T) * cfg.qk_head_dim ** -0.5, -1)
+    got = torch.einsum("hc,hvc->hv", p @ kv_rows[:, :kl], L["w_uv"]).reshape(-1)
+    torch.testing.assert_close(got, exp, rtol=1e-4, atol=1e-5)
+
+
+def test_indexer_topk_switches_to_sparse():
+    cfg = deepseek_tiny()  # index_topk 8
+    src = DeepSeekRandomWeights(cfg, seed=4)
+    ref = DeepSeekReference(cfg, src)
+    big = DeepSeekReference(cfg.__class__(**{**cfg.to_dict(), "index_topk": 1000}), src)
+    s1, s2 = ref.new_state(), big.new_state()
+    toks = torch.randint(0, cfg.vocab_size, (14,), generator=torch.Generator().manual_seed(5)).tolist()
+    diffs = []
+    for t in toks:
+        a, b = ref.step(s1, t), big.step(s2, t)
+        diffs.append(float((a - b).abs().max()))
+    assert max(diffs[:cfg.index_topk]) == 0.0        # dense while the context fits in top-k
+    assert max(diffs[cfg.index_topk:]) > 0.0         # sparse afterwards
+
+
+def test_expert_parallel_shards_sum_to_single_rank():
+    cfg = deepseek_tiny()
+    src = DeepSeekRandomWeights(cfg, seed=6)
+    full = DeepSeekReference(cfg, src)
+    world = 2
+    bar = threading.Barrier(world)
+    slots = [None] * world
+
+    def make_allreduce(r):
+        def ar(x):
+            slots[r] = x.clone()
+            bar.wait()
+            tot = sum(slots)
+            bar.wait()
+            return tot
+        return ar
+
+    ranks = [DeepSeekReference(cfg, src, tp_rank=r, tp_size=world, allreduce=make_allreduce(r)) for r in range(world)]
+    toks = [3, 17, 200, 41, 9]
+    st = [m.new_state() for m in ranks]
+    out = [[] for _ in range(world)]
+
+    def run(r):
+        for t in toks:
+            out[r].append(ranks[r].step(st[r], t))
+
+    th = [threading.Thread(target=run, args=(r,)) for r in range(world)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    sf = full.new_state()
+    for i, t in enumerate(toks):
+        exp = full.step(sf, t)
+        got = torch.cat([out[0][i], out[1][i]])
+        torch.testing.assert_close(got, exp, rtol=1e-4, atol=1e-4)
+
+
+def test_quantized_reference_tracks_fp32():
+    cfg = deepseek_tiny()
+    src = DeepSeekRandomWeights(cfg, seed=7)
+    a, b = DeepSeekReference(cfg, src), DeepSeekReference(cfg, src, quant=True)
+    sa, sb = a.new_state(), b.new_state()
+    for t in [5, 6, 7, 8]:
+        la, lb = a.step(sa, t), b.step(sb, t)
+    cos = torch.nn.functional.cosine_similarity(la, lb, dim=0)
+    assert cos > 0.9

@@ -154,3 +154,112 @@ PRESETS = {
     "qwen3.5-tiny": qwen35_tiny,
     "qwen3.5-small": qwen35_small_gpu,
 }
+
+
+@dataclass(frozen=True)
+class DeepSeekConfig:
+    """DeepSeek-style MoE with multi-head latent attention (MLA), the DSA lightning indexer
+    (sparse attention over the top-k keys per query) and manifold-constrained hyper-
+    connections (mHC: ``hc_mult`` residual streams mixed by per-token sigmoid pre/post
+    weights and a Sinkhorn-normalised doubly-stochastic residual matrix).
+
+    The reference serves this family through vLLM (worker/zstep_worker/models/
+    deepseek_v41.py:408, DeepSeekV41StepRunner); the model math here is written from the
+    architecture's definition: MLA with absorbed k/v up-projections, a ReLU-weighted
+    multi-head index score, sigmoid grouped routing with a score-correction bias."""
+
+    vocab_size: int = 129280
+    hidden_size: int = 4096
+    num_hidden_layers: int = 48
+    first_k_dense_replace: int = 1
+    intermediate_size: int = 12288          # dense FFN layers
+    rms_norm_eps: float = 1e-6
+    num_attention_heads: int = 64
+    q_lora_rank: int = 1024
+    kv_lora_rank: int = 512
+    qk_nope_head_dim: int = 128
+    qk_rope_head_dim: int = 64
+    v_head_dim: int = 128
+    rope_theta: float = 10000.0
+    index_n_heads: int = 64
+    index_head_dim: int = 128
+    index_topk: int = 2048
+    n_routed_experts: int = 256
+    num_experts_per_tok: int = 8
+    n_group: int = 8
+    topk_group: int = 4
+    routed_scaling_factor: float = 2.5
+    moe_intermediate_size: int = 2048
+    n_shared_experts: int = 1
+    hc_mult: int = 4
+    hc_sinkhorn_iters: int = 20
+    hc_eps: float = 1e-6
+    expert_format: str = "mxfp4"            # routed and shared experts; everything else MXFP8
+    initializer_range: float = 0.02
+    name: str = "deepseek-mla-dsa-mhc"
+
+    @property
+    def qk_head_dim(self) -> int:
+        return self.qk_nope_head_dim + self.qk_rope_head_dim
+
+    @property
+    def kv_cache_dim(self) -> int:
+        """Latent cache row: normalised c_kv [kv_lora_rank] then roped k_pe [qk_rope_head_dim]."""
+        return self.kv_lora_rank + self.qk_rope_head_dim
+
+    @property
+    def hc_mix_dim(self) -> int:
+        """Per-token mixing logits of one mHC site: pre [n], post [n], residual [n*n]."""
+        n = self.hc_mult
+        return 2 * n + n * n
+
+    def is_dense(self, layer: int) -> bool:
+        return layer < self.first_k_dense_replace
+
+    def params(self) -> int:
+        h = self.hidden_size
+        nh = self.num_attention_heads
+        attn = (h * self.q_lora_rank + self.q_lora_rank * nh * self.qk_head_dim + h * self.kv_cache_dim
+                + self.kv_lora_rank * nh * (self.qk_nope_head_dim + self.v_head_dim) + nh * self.v_head_dim * h
+                + self.q_lora_rank * self.index_n_heads * self.index_head_dim + h * self.index_head_dim
+                + h * self.index_n_heads)
+        moe = (self.n_routed_experts + self.n_shared_experts) * 3 * h * self.moe_intermediate_size \
+            + h * self.n_routed_experts
+        dense = 3 * h * self.intermediate_size
+        nd = self.first_k_dense_replace
+        return self.num_hidden_layers * attn + nd * dense + (self.num_hidden_layers - nd) * moe \
+            + 2 * self.vocab_size * h
+
+    def to_dict(self) -> dict:
+        return asdict(self)
+
+
+def deepseek_full() -> DeepSeekConfig:
+    """The DeepSeek-style benchmark shape (48 layers, MLA 64 heads, DSA top-2048, mHC x4,
+    256 experts top-8 in MXFP4)."""
+    return DeepSeekConfig()
+
+
+def deepseek_tiny() -> DeepSeekConfig:
+    """CPU-sized DeepSeek-style model for the reference and plumbing tests."""
+    return DeepSeekConfig(vocab_size=512, hidden_size=128, num_hidden_layers=3, first_k_dense_replace=1,
+                          intermediate_size=256, num_attention_heads=4, q_lora_rank=64, kv_lora_rank=64,
+                          qk_nope_head_dim=32, qk_rope_head_dim=16, v_head_dim=32, index_n_heads=4,
+                          index_head_dim=32, index_topk=8, n_routed_experts=16, num_experts_per_tok=4, n_group=4,
+                          topk_group=2, moe_intermediate_size=64, name="deepseek-tiny")
+
+
+def deepseek_small_gpu(num_layers: int = 3, vocab: int = 8192, experts: int = 32, topk: int = 64) -> DeepSeekConfig:
+    """Reduced depth/width with the full per-head shapes the sm_100a kernels serve
+    (kv_lora 512, rope 64, nope/v 128, index heads 128-dim) for fast GPU tests."""
+    return DeepSeekConfig(vocab_size=vocab, hidden_size=1024, num_hidden_layers=num_layers, intermediate_size=2048,
+                          num_attention_heads=16, q_lora_rank=512, index_n_heads=16, index_topk=topk,
+                          n_routed_experts=experts, n_group=4, topk_group=2, moe_intermediate_size=512,
+                          name=f"deepseek-small-{num_layers}l")
+
+
+PRESETS.update({
+    "deepseek-mla-dsa-mhc": deepseek_full,
+    "deepseek-tiny": deepseek_tiny,
+    "deepseek-small": deepseek_small_gpu,
+})

@@ -108,3 +108,76 @@ def fake_quant(x: torch.Tensor) -> torch.Tensor:
     """Quantize-dequantize round trip (the value an MXFP8 GEMM actually multiplies)."""
     q, code = quantize(x)
     return dequantize(q, code).to(x.dtype) if x.dtype != torch.float32 else dequantize(q, code)
+
+
+# ------------------------------------------------------------------------------ MXFP4
+# OCP MXFP4: e2m1 elements (sign, 2 exponent bits with bias 1, 1 mantissa bit; magnitudes
+# 0, 0.5, 1, 1.5, 2, 3, 4, 6) with the same e8m0 scale per 32 elements.  The scale is
+# ``2**ceil(log2(amax / 6))``; elements round to the nearest e2m1 value, ties to the even
+# mantissa.  Two elements per byte: element 2i in the low nibble, 2i+1 in the high one.
+# Every e2m1 value times an e8m0 scale is exactly an e4m3 value times the same scale, so
+# the GEMM widens MXFP4 weights to MXFP8 in shared memory without changing a product.
+
+E2M1_MAX = 6.0
+E2M1_MAGS = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+
+
+def e8m0_codes_fp4(amax: torch.Tensor) -> torch.Tensor:
+    r = amax.float() / E2M1_MAX
+    mant, exp = torch.frexp(r)
+    e = torch.where(mant == 0.5, exp - 1, exp).clamp(-127, 127)
+    code = (e + 127).to(torch.int32)
+    return torch.where(amax > 0, code, torch.zeros_like(code)).to(torch.uint8)
+
+
+def quantize_fp4(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """``x [rows, k]`` (k % 32 == 0) -> (packed e2m1 uint8 [rows, k/2], codes uint8 [rows, k/32])."""
+    rows, k = x.shape
+    assert k % 32 == 0
+    xb = x.float().reshape(rows, k // 32, 32)
+    code = e8m0_codes_fp4(xb.abs().amax(dim=-1))
+    c = code.to(torch.int32)
+    inv = torch.where(c == 0, torch.full_like(c, 0, dtype=torch.float32) + 2.0 ** 127,
+                      torch.pow(2.0, (127 - c).float()))
+    y = (xb * inv.unsqueeze(-1)).clamp(-E2M1_MAX, E2M1_MAX)
+    # Distances in fp64 are exact for fp32 inputs; the 1e-12 bias on odd codes breaks exact
+    # ties toward the even mantissa and is far below any non-tie difference.
+    mags = torch.tensor(E2M1_MAGS, device=x.device, dtype=torch.float64)
+    d = (y.double().abs().unsqueeze(-1) - mags).abs() + 1e-12 * (torch.arange(8, device=x.device) & 1)
+    nib = d.argmin(-1).to(torch.uint8) | ((y < 0).to(torch.uint8) << 3)
+    nib = nib.reshape(rows, k)
+    packed = nib[:, 0::2] | (nib[:, 1::2] << 4)
+    return packed.contiguous(), code
+
+
+def dequantize_fp4(packed: torch.Tensor, code: torch.Tensor) -> torch.Tensor:
+    rows = packed.shape[0]
+    k = packed.shape[1] * 2
+    nib = torch.stack([packed & 0xF, packed >> 4], dim=-1).reshape(rows, k).long()
+    mags = torch.tensor(E2M1_MAGS, device=packed.device)
+    v = mags[nib & 7] * torch.where((nib & 8) != 0, -1.0, 1.0)
+    return (v.reshape(rows, k // 32, 32) * code_to_scale(code).unsqueeze(-1)).reshape(rows, k)
+
+
+def fake_quant_fp4(x: torch.Tensor) -> torch.Tensor:
+    p, c = quantize_fp4(x.reshape(-1, x.shape[-1]))
+    return dequantize_fp4(p, c).reshape(x.shape).to(x.dtype)
+
+
+def fp4_to_e4m3(packed: torch.Tensor) -> torch.Tensor:
+    """Widen packed e2m1 [rows, k/2] to e4m3 bytes [rows, k] (exact; same scales)."""
+    rows = packed.shape[0]
+    nib = torch.stack([packed & 0xF, packed >> 4], dim=-1).reshape(rows, -1).long()
+    mags = torch.tensor(E2M1_MAGS, device=packed.device)
+    v = mags[nib & 7] * torch.where((nib & 8) != 0, -1.0, 1.0)
+    return v.to(torch.float8_e4m3fn).view(torch.uint8)
+
+
+def tile_weight_fp4(packed: torch.Tensor) -> torch.Tensor:
+    """Packed e2m1 weight [rows, k/2] (rows % 128 == 0, k % 128 == 0) -> contiguous 8 KiB
+    chunks [rows/128][k/128][128 rows][64 bytes], one per (feature tile, K tile), in plain
+    row-major order; the GEMM's converter warps apply the 128-byte swizzle when they widen
+    a chunk to e4m3 in shared memory."""
+    rows, kh = packed.shape
+    t = packed.view(rows // 128, 128, kh // 64, 64).permute(0, 2, 1, 3)
+    return t.contiguous().view(rows, kh)
