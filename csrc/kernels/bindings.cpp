@@ -434,7 +434,228 @@ Tensor tensor_from_ptr(int64_t p, std::vector<int64_t> sizes, at::ScalarType dty
 
 }  // namespace
 
+
+// ------------------------------------------------------------------ DeepSeek-style layers
+void mhc_partial(const Tensor& x, int64_t rows, int64_t hidden, const Tensor& fn, int64_t mode, const OptT& y,
+                 const OptT& mix_prev, const OptT& ids, const OptT& embed, const Tensor& partial) {
+  check_cuda(x, "x");
+  check_cuda(fn, "fn");
+  check_cuda(partial, "partial");
+  TORCH_CHECK(x.scalar_type() == at::kFloat && fn.scalar_type() == at::kFloat, "mhc: x and fn must be fp32");
+  MhcPartialArgs a{};
+  a.x = ptr<float>(x);
+  a.rows = (int)rows;
+  a.hidden = (int)hidden;
+  a.m = (int)fn.size(0);
+  a.fn = ptr<const float>(fn);
+  a.mode = (int)mode;
+  a.y = optptr<const float>(y);
+  a.mix_prev = optptr<const float>(mix_prev);
+  a.ids = optptr<const int>(ids);
+  a.embed = optptr<const __nv_bfloat16>(embed);
+  a.partial = ptr<float>(partial);
+  TORCH_CHECK(mode != 1 || (a.y && a.mix_prev), "mhc_partial mode 1 needs y and mix_prev");
+  TORCH_CHECK(mode != 2 || (a.ids && a.embed), "mhc_partial mode 2 needs ids and embed");
+  TORCH_CHECK(x.numel() >= rows * 4 * hidden, "mhc_partial: x too small");
+  TORCH_CHECK(partial.numel() >= rows * zs_mhc_slices((int)hidden) * (a.m + 1), "mhc_partial: partial too small");
+  rc(zs_mhc_partial(&a, stream()), "zs_mhc_partial");
+}
+
+void mhc_finalize(const Tensor& x, int64_t rows, int64_t hidden, const Tensor& partial, const Tensor& base,
+                  const Tensor& scale, double eps, int64_t iters, const OptT& mix_out, const Tensor& weight,
+                  const Tensor& q, const Tensor& sf) {
+  check_cuda(x, "x");
+  check_cuda(q, "q");
+  MhcFinalizeArgs a{};
+  a.x = ptr<const float>(x);
+  a.rows = (int)rows;
+  a.hidden = (int)hidden;
+  a.m = (int)base.numel();
+  a.slices = zs_mhc_slices((int)hidden);
+  a.partial = ptr<const float>(partial);
+  a.base = ptr<const float>(base);
+  a.scale = ptr<const float>(scale);
+  a.eps = (float)eps;
+  a.sinkhorn_iters = (int)iters;
+  a.mix_out = optptr<float>(mix_out);
+  a.weight = ptr<const __nv_bfloat16>(weight);
+  a.q = ptr<uint8_t>(q);
+  a.sf = ptr<uint8_t>(sf);
+  TORCH_CHECK(a.m == 4 || a.mix_out, "mhc_finalize: a 24-logit site needs mix_out");
+  TORCH_CHECK(q.numel() >= rows * hidden, "mhc_finalize: q too small");
+  rc(zs_mhc_finalize(&a, stream()), "zs_mhc_finalize");
+}
+
+void rms_quant(const Tensor& x, int64_t width, const Tensor& w, double eps, int64_t rows, const Tensor& q,
+               const Tensor& sf) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "rms_quant: bf16 rows with unit stride");
+  TORCH_CHECK(q.numel() >= rows * width, "rms_quant: q too small");
+  rc(zs_rms_quant(ptr(x), (int)x.stride(0), (int)width, ptr(w), (float)eps, (int)rows, ptr<uint8_t>(q),
+                  ptr<uint8_t>(sf), stream()),
+     "zs_rms_quant");
+}
+
+void mla_prologue(const Tensor& proj, int64_t off_kva, int64_t off_ik, int64_t off_iw, const Tensor& qi,
+                  int64_t off_iq, int64_t rows, int64_t heads, int64_t nope, int64_t rope, int64_t kv_lora,
+                  int64_t index_heads, int64_t index_dim, const Tensor& kv_norm, const Tensor& ik_norm, double eps,
+                  double theta, const Tensor& slots, const Tensor& positions, const Tensor& page_table,
+                  int64_t page_size, const Tensor& ckv_cache, const Tensor& ik_cache, const Tensor& q_pe,
+                  const Tensor& iq, const Tensor& iw) {
+  check_cuda(proj, "proj");
+  check_cuda(ckv_cache, "ckv_cache");
+  check_cuda(ik_cache, "ik_cache");
+  TORCH_CHECK(page_table.scalar_type() == at::kInt, "page_table must be int32");
+  MlaPrologueArgs a{};
+  a.proj = ptr<const __nv_bfloat16>(proj);
+  a.ld_proj = (int)proj.stride(0);
+  a.off_kva = (int)off_kva;
+  a.off_ik = (int)off_ik;
+  a.off_iw = (int)off_iw;
+  a.qi = ptr<const __nv_bfloat16>(qi);
+  a.ld_qi = (int)qi.stride(0);
+  a.off_iq = (int)off_iq;
+  a.rows = (int)rows;
+  a.heads = (int)heads;
+  a.qk_dim = (int)(nope + rope);
+  a.nope = (int)nope;
+  a.rope = (int)rope;
+  a.kv_lora = (int)kv_lora;
+  a.index_heads = (int)index_heads;
+  a.index_dim = (int)index_dim;
+  a.kv_norm = ptr<const __nv_bfloat16>(kv_norm);
+  a.ik_norm = ptr<const __nv_bfloat16>(ik_norm);
+  a.eps = (float)eps;
+  a.theta = (float)theta;
+  a.iw_scale = (float)(1.0 / std::sqrt((double)index_heads));
+  a.slot = ptr<const int>(slots);
+  a.pos = ptr<const int>(positions);
+  a.page_table = ptr<const int>(page_table);
+  a.max_pages = (int)page_table.size(1);
+  a.page_size = (int)page_size;
+  a.ckv_cache = ptr<__nv_bfloat16>(ckv_cache);
+  a.ik_cache = ptr<__nv_bfloat16>(ik_cache);
+  a.q_pe = ptr<__nv_bfloat16>(q_pe);
+  a.iq = ptr<__nv_bfloat16>(iq);
+  a.iw = ptr<float>(iw);
+  rc(zs_mla_prologue(&a, stream()), "zs_mla_prologue");
+}
+
+void mla_absorb_q(const Tensor& qi, int64_t qk_dim, int64_t nope, const Tensor& w_uk, int64_t heads, int64_t rows,
+                  const Tensor& q_lat) {
+  check_cuda(qi, "qi");
+  check_cuda(w_uk, "w_uk");
+  const int kl = (int)w_uk.size(-1);
+  TORCH_CHECK(q_lat.numel() >= rows * heads * kl, "mla_absorb_q: q_lat too small");
+  rc(zs_mla_absorb_q(ptr(qi), (int)qi.stride(0), (int)qk_dim, (int)nope, ptr(w_uk), kl, (int)heads, (int)rows,
+                     ptr(q_lat), stream()),
+     "zs_mla_absorb_q");
+}
+
+void mla_attn(const Tensor& q_lat, const Tensor& q_pe, const Tensor& ckv_cache, const Tensor& page_table,
+              int64_t page_size, const Tensor& slots, const Tensor& sel, const Tensor& n_sel, int64_t rows,
+              int64_t heads, int64_t splits, double sm_scale, const Tensor& partial) {
+  check_cuda(q_lat, "q_lat");
+  check_cuda(partial, "partial");
+  MlaAttnArgs a{};
+  a.q_lat = ptr<const __nv_bfloat16>(q_lat);
+  a.q_pe = ptr<const __nv_bfloat16>(q_pe);
+  a.ckv_cache = ptr<const __nv_bfloat16>(ckv_cache);
+  a.page_table = ptr<const int>(page_table);
+  a.max_pages = (int)page_table.size(1);
+  a.page_size = (int)page_size;
+  a.slot = ptr<const int>(slots);
+  a.sel = ptr<const int>(sel);
+  a.ld_sel = (int)sel.stride(0);
+  a.n_sel = ptr<const int>(n_sel);
+  a.rows = (int)rows;
+  a.heads = (int)heads;
+  a.kv_lora = 512;
+  a.rope = (int)(ckv_cache.size(-1) - 512);
+  a.splits = (int)splits;
+  a.sm_scale = (float)sm_scale;
+  a.partial = ptr<float>(partial);
+  TORCH_CHECK(partial.numel() >= rows * heads * splits * (512 + 4), "mla_attn: partial too small");
+  rc(zs_mla_attn(&a, stream()), "zs_mla_attn");
+}
+
+void mla_up(const Tensor& partial, int64_t rows, int64_t heads, int64_t splits, const Tensor& w_uv_t, const Tensor& q,
+            const Tensor& sf) {
+  MlaUpArgs a{};
+  a.partial = ptr<const float>(partial);
+  a.rows = (int)rows;
+  a.heads = (int)heads;
+  a.splits = (int)splits;
+  a.v_dim = (int)w_uv_t.size(-1);
+  a.w_uv_t = ptr<const __nv_bfloat16>(w_uv_t);
+  a.q = ptr<uint8_t>(q);
+  a.sf = ptr<uint8_t>(sf);
+  TORCH_CHECK(q.numel() >= rows * heads * a.v_dim, "mla_up: q too small");
+  rc(zs_mla_up(&a, stream()), "zs_mla_up");
+}
+
+void dsa_index(const Tensor& iq, const Tensor& iw, const Tensor& ik_cache, const Tensor& page_table,
+               int64_t page_size, const Tensor& slots, const Tensor& ctx_len, int64_t rows, int64_t index_heads,
+               int64_t topk, int64_t max_ctx, const Tensor& scores, const Tensor& sel, const Tensor& n_sel) {
+  check_cuda(iq, "iq");
+  check_cuda(scores, "scores");
+  TORCH_CHECK(ik_cache.size(-1) == 128, "dsa_index: index dim must be 128");
+  TORCH_CHECK(max_ctx <= scores.size(1), "dsa_index: scores buffer narrower than the context");
+  TORCH_CHECK(topk <= sel.size(1), "dsa_index: sel buffer narrower than top-k");
+  DsaScoresArgs s{};
+  s.iq = ptr<const __nv_bfloat16>(iq);
+  s.iw = ptr<const float>(iw);
+  s.ik_cache = ptr<const __nv_bfloat16>(ik_cache);
+  s.page_table = ptr<const int>(page_table);
+  s.max_pages = (int)page_table.size(1);
+  s.page_size = (int)page_size;
+  s.slot = ptr<const int>(slots);
+  s.ctx_len = ptr<const int>(ctx_len);
+  s.rows = (int)rows;
+  s.index_heads = (int)index_heads;
+  s.topk = (int)topk;
+  s.scale = (float)(1.0 / std::sqrt(128.0));
+  s.scores = ptr<float>(scores);
+  s.ld_scores = (int)scores.stride(0);
+  rc(zs_dsa_scores(&s, (int)max_ctx, stream()), "zs_dsa_scores");
+  DsaTopkArgs k{};
+  k.scores = s.scores;
+  k.ld_scores = s.ld_scores;
+  k.ctx_len = s.ctx_len;
+  k.rows = (int)rows;
+  k.topk = (int)topk;
+  k.sel = ptr<int>(sel);
+  k.ld_sel = (int)sel.stride(0);
+  k.n_sel = ptr<int>(n_sel);
+  rc(zs_dsa_topk(&k, stream()), "zs_dsa_topk");
+}
+
+void gather_sum(const Tensor& rows_in, const Tensor& src, const Tensor& w, int64_t rows, const Tensor& y) {
+  check_cuda(rows_in, "rows_in");
+  const int k1 = (int)src.size(-1);
+  const int hidden = (int)rows_in.size(-1);
+  TORCH_CHECK(y.numel() >= rows * hidden, "gather_sum: y too small");
+  rc(zs_gather_sum(ptr(rows_in), ptr<const int>(src), ptr<const float>(w), k1, hidden, (int)rows, ptr<float>(y),
+                   stream()),
+     "zs_gather_sum");
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("mhc_partial", &mhc_partial, py::arg("x"), py::arg("rows"), py::arg("hidden"), py::arg("fn"), py::arg("mode"),
+        py::arg("y") = py::none(), py::arg("mix_prev") = py::none(), py::arg("ids") = py::none(),
+        py::arg("embed") = py::none(), py::arg("partial"));
+  m.def("mhc_slices", &zs_mhc_slices);
+  m.def("mhc_finalize", &mhc_finalize, py::arg("x"), py::arg("rows"), py::arg("hidden"), py::arg("partial"),
+        py::arg("base"), py::arg("scale"), py::arg("eps"), py::arg("iters"), py::arg("mix_out"), py::arg("weight"),
+        py::arg("q"), py::arg("sf"));
+  m.def("rms_quant", &rms_quant);
+  m.def("mla_prologue", &mla_prologue);
+  m.def("mla_absorb_q", &mla_absorb_q);
+  m.def("mla_attn", &mla_attn);
+  m.def("mla_up", &mla_up);
+  m.def("dsa_index", &dsa_index);
+  m.def("gather_sum", &gather_sum);
+
   m.def("fused_allreduce_norm", &fused_allreduce_norm, py::arg("rank"), py::arg("world"), py::arg("delta"),
         py::arg("n_terms"), py::arg("row_stride"), py::arg("term_stride"), py::arg("part"), py::arg("out"),
         py::arg("flags"), py::arg("epoch"), py::arg("grid_counter"), py::arg("residual"), py::arg("weight"),

@@ -7,6 +7,7 @@
 // that ran out, bad shapes seen on device) through the `err` word.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -282,6 +283,127 @@ typedef struct ArgmaxArArgs {
 // rebased by id_offset and max-reduced across ranks.
 int zs_allreduce_argmax(const ArgmaxArArgs* args, const unsigned long long* local_keys, int id_offset,
                         cudaStream_t stream);
+
+// ----------------------------------------------------------------------------------
+// DeepSeek-style layers: mHC, MLA, DSA indexer, MoE combine (deepseek.cu)
+// ----------------------------------------------------------------------------------
+typedef struct MhcPartialArgs {
+  float* x;                   // fp32 [rows, 4, hidden] residual streams (read; written in modes 1, 2)
+  int rows, hidden;
+  int m;                      // mixing logits of the site: 24 (pre|post|res) or 4 (final collapse)
+  const float* fn;            // fp32 [m, 4 * hidden]
+  int mode;                   // 0: X as is; 1: apply the previous site's update; 2: X = embed[ids]
+  const float* y;             // mode 1: fp32 [rows, hidden] sublayer output (bf16-rounded on use)
+  const float* mix_prev;      // mode 1: [rows, 4 + 16] post | res of the previous site
+  const int* ids;             // mode 2
+  const __nv_bfloat16* embed; // mode 2: [vocab, hidden]
+  float* partial;             // [rows, slices, m + 1]
+} MhcPartialArgs;
+
+typedef struct MhcFinalizeArgs {
+  const float* x;             // [rows, 4, hidden]
+  int rows, hidden, m, slices;
+  const float* partial;       // [rows, slices, m + 1]
+  const float* base;          // [m]
+  const float* scale;         // [3] (or [1] for the final collapse)
+  float eps;
+  int sinkhorn_iters;
+  float* mix_out;             // m == 24: [rows, 4 + 16] post | res
+  const __nv_bfloat16* weight;  // RMSNorm scale [hidden] (plain, no offset)
+  uint8_t* q;                 // MXFP8 [rows, hidden] of rmsnorm(pre @ X)
+  uint8_t* sf;
+} MhcFinalizeArgs;
+
+int zs_mhc_partial(const MhcPartialArgs* args, cudaStream_t stream);
+int zs_mhc_slices(int hidden);
+int zs_mhc_finalize(const MhcFinalizeArgs* args, cudaStream_t stream);
+
+// RMSNorm (plain scale) of a strided bf16 slice of `width` columns, then MXFP8.
+int zs_rms_quant(const void* x, int ld_x, int width, const void* w, float eps, int rows, uint8_t* q, uint8_t* sf,
+                 cudaStream_t stream);
+
+typedef struct MlaPrologueArgs {
+  const __nv_bfloat16* proj;  // [rows, ld_proj]: q_a | kv_a (kv_lora + rope) | index k | index weights
+  int ld_proj, off_kva, off_ik, off_iw;
+  const __nv_bfloat16* qi;    // [rows, ld_qi]: local heads x (nope | rope) then index queries
+  int ld_qi, off_iq;
+  int rows, heads, qk_dim, nope, rope, kv_lora, index_heads, index_dim;
+  const __nv_bfloat16* kv_norm;   // [kv_lora]
+  const __nv_bfloat16* ik_norm;   // [index_dim]
+  float eps, theta, iw_scale;
+  const int* slot;
+  const int* pos;
+  const int* page_table;
+  int max_pages, page_size;
+  __nv_bfloat16* ckv_cache;   // [pages, page_size, kv_lora + rope]
+  __nv_bfloat16* ik_cache;    // [pages, page_size, index_dim]
+  __nv_bfloat16* q_pe;        // [rows, heads, rope]
+  __nv_bfloat16* iq;          // [rows, index_heads, index_dim]
+  float* iw;                  // [rows, index_heads]
+} MlaPrologueArgs;
+
+int zs_mla_prologue(const MlaPrologueArgs* args, cudaStream_t stream);
+int zs_mla_absorb_q(const void* qi, int ld_qi, int qk_dim, int nope, const void* w_uk, int kv_lora, int heads,
+                    int rows, void* q_lat, cudaStream_t stream);
+
+typedef struct MlaAttnArgs {
+  const __nv_bfloat16* q_lat;  // [rows, heads, kv_lora]
+  const __nv_bfloat16* q_pe;   // [rows, heads, rope]
+  const __nv_bfloat16* ckv_cache;
+  const int* page_table;
+  int max_pages, page_size;
+  const int* slot;
+  const int* sel;              // [rows, ld_sel] selected positions (ascending)
+  int ld_sel;
+  const int* n_sel;            // [rows]
+  int rows, heads, kv_lora, rope, splits;
+  float sm_scale;
+  float* partial;              // [rows, heads, splits, kv_lora + 4]
+} MlaAttnArgs;
+
+size_t zs_mla_attn_smem(int heads);
+int zs_mla_attn(const MlaAttnArgs* args, cudaStream_t stream);
+
+typedef struct MlaUpArgs {
+  const float* partial;        // from zs_mla_attn
+  int rows, heads, splits, v_dim;
+  const __nv_bfloat16* w_uv_t; // [heads, kv_lora, v]
+  uint8_t* q;                  // MXFP8 [rows, heads * v]
+  uint8_t* sf;
+} MlaUpArgs;
+
+int zs_mla_up(const MlaUpArgs* args, cudaStream_t stream);
+
+typedef struct DsaScoresArgs {
+  const __nv_bfloat16* iq;     // [rows, index_heads, 128]
+  const float* iw;             // [rows, index_heads]
+  const __nv_bfloat16* ik_cache;
+  const int* page_table;
+  int max_pages, page_size;
+  const int* slot;
+  const int* ctx_len;          // [rows] keys visible to each row (position + 1)
+  int rows, index_heads, topk;
+  float scale;
+  float* scores;               // [rows, ld_scores]
+  int ld_scores;
+} DsaScoresArgs;
+
+typedef struct DsaTopkArgs {
+  const float* scores;
+  int ld_scores;
+  const int* ctx_len;
+  int rows, topk;
+  int* sel;                    // [rows, ld_sel]
+  int ld_sel;
+  int* n_sel;
+} DsaTopkArgs;
+
+int zs_dsa_scores(const DsaScoresArgs* args, int max_ctx, cudaStream_t stream);
+int zs_dsa_topk(const DsaTopkArgs* args, cudaStream_t stream);
+
+// y[t] = sum_j w[t, j] * rows_in[src[t, j]] (fp32; src -1 skipped; fixed order).
+int zs_gather_sum(const void* rows_in, const int* src, const float* w, int k1, int hidden, int rows, float* y,
+                  cudaStream_t stream);
 
 int zs_symm_alloc(size_t bytes, void** ptr);
 int zs_symm_free(void* ptr);

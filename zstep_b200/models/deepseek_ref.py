@@ -197,7 +197,8 @@ class DeepSeekReference:
         rs = torch.rsqrt(xf.pow(2).mean() + eps)
         h = torch.sigmoid(scale[0] * (fn @ xf) * rs + base) @ X
         s.pos += 1
-        return self.lm_head @ self._q(R.rmsnorm(h, self.final_norm, eps, 0.0))
+        self.last_normed = self._q(R.rmsnorm(h, self.final_norm, eps, 0.0))  # lm_head input (for tests)
+        return self.lm_head @ self.last_normed
 
     def _attention(self, s: DsState, li: int, L, xq):
         c = self.cfg

@@ -130,24 +130,32 @@ def e8m0_codes_fp4(amax: torch.Tensor) -> torch.Tensor:
     return torch.where(amax > 0, code, torch.zeros_like(code)).to(torch.uint8)
 
 
-def quantize_fp4(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+# Rounding boundaries between consecutive e2m1 magnitudes; at an exact boundary the
+# value goes to the neighbour with the even mantissa (the upper one after odd boundaries).
+_E2M1_BOUNDS = (0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0)
+
+
+def quantize_fp4(x: torch.Tensor, chunk_rows: int = 4096) -> tuple[torch.Tensor, torch.Tensor]:
     """``x [rows, k]`` (k % 32 == 0) -> (packed e2m1 uint8 [rows, k/2], codes uint8 [rows, k/32])."""
     rows, k = x.shape
     assert k % 32 == 0
-    xb = x.float().reshape(rows, k // 32, 32)
-    code = e8m0_codes_fp4(xb.abs().amax(dim=-1))
-    c = code.to(torch.int32)
-    inv = torch.where(c == 0, torch.full_like(c, 0, dtype=torch.float32) + 2.0 ** 127,
-                      torch.pow(2.0, (127 - c).float()))
-    y = (xb * inv.unsqueeze(-1)).clamp(-E2M1_MAX, E2M1_MAX)
-    # Distances in fp64 are exact for fp32 inputs; the 1e-12 bias on odd codes breaks exact
-    # ties toward the even mantissa and is far below any non-tie difference.
-    mags = torch.tensor(E2M1_MAGS, device=x.device, dtype=torch.float64)
-    d = (y.double().abs().unsqueeze(-1) - mags).abs() + 1e-12 * (torch.arange(8, device=x.device) & 1)
-    nib = d.argmin(-1).to(torch.uint8) | ((y < 0).to(torch.uint8) << 3)
-    nib = nib.reshape(rows, k)
-    packed = nib[:, 0::2] | (nib[:, 1::2] << 4)
-    return packed.contiguous(), code
+    packed = torch.empty(rows, k // 2, dtype=torch.uint8, device=x.device)
+    codes = torch.empty(rows, k // 32, dtype=torch.uint8, device=x.device)
+    for r0 in range(0, rows, chunk_rows):
+        xb = x[r0:r0 + chunk_rows].float().reshape(-1, k // 32, 32)
+        code = e8m0_codes_fp4(xb.abs().amax(dim=-1))
+        c = code.to(torch.int32)
+        inv = torch.where(c == 0, torch.full_like(c, 0, dtype=torch.float32) + 2.0 ** 127,
+                          torch.pow(2.0, (127 - c).float()))
+        y = (xb * inv.unsqueeze(-1)).clamp(-E2M1_MAX, E2M1_MAX)
+        a = y.abs()
+        mag = torch.zeros(a.shape, dtype=torch.uint8, device=x.device)
+        for i, b in enumerate(_E2M1_BOUNDS):
+            mag += (a > b) | ((a == b) & (i % 2 == 1))
+        nib = (mag | ((y < 0).to(torch.uint8) << 3)).reshape(-1, k)
+        packed[r0:r0 + chunk_rows] = nib[:, 0::2] | (nib[:, 1::2] << 4)
+        codes[r0:r0 + chunk_rows] = code
+    return packed, codes
 
 
 def dequantize_fp4(packed: torch.Tensor, code: torch.Tensor) -> torch.Tensor:

@@ -71,6 +71,10 @@ class NcclCollectives:
         dist.all_reduce(acc, group=self.group)
         self.C.add_rmsnorm_quant(hidden_buf, acc, 1, H, H, norm_w, 1.0, eps, rows, None, xq, xsf)
 
+    def allreduce_sum(self, t: torch.Tensor) -> None:
+        """In-place sum over ranks (the row-parallel sublayer output of the mHC model)."""
+        dist.all_reduce(t, group=self.group)
+
     def argmax_allreduce(self, keys, rows: int, tiles: int, id_offset: int, out_ids, out_vals) -> None:
         local = torch.empty(rows, dtype=torch.int64, device=keys.device)
         self.C.argmax_reduce(keys, rows, tiles, None, None, local)
@@ -102,6 +106,9 @@ class LocalCollectives:
                               norm_w, eps: float, rows: int, xq, xsf, term_index=None, term_scale=None) -> None:
         self.C.add_rmsnorm_quant(hidden_buf, delta, n_terms, row_stride, term_stride, norm_w, 1.0, eps, rows, None,
                                  xq, xsf, term_index, term_scale)
+
+    def allreduce_sum(self, t: torch.Tensor) -> None:
+        pass
 
     def argmax_allreduce(self, keys, rows: int, tiles: int, id_offset: int, out_ids, out_vals) -> None:
         self.C.argmax_reduce(keys, rows, tiles, out_ids, out_vals, None)

@@ -123,6 +123,10 @@ class FusedCollectives:
                                     1.0, eps, rows, None, xq, xsf, self.err, term_index, term_scale,
                                     self.timeout_ms)
 
+    def allreduce_sum(self, t: torch.Tensor) -> None:
+        """In-place fp32 sum over ranks (mHC sublayer outputs); NCCL carries it."""
+        self.nccl.allreduce_sum(t)
+
     def argmax_allreduce(self, keys, rows: int, tiles: int, id_offset: int, out_ids, out_vals) -> None:
         """Global greedy token per row from per-tile packed keys of this rank's vocab shard."""
         if rows > self.max_rows:
