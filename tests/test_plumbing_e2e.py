@@ -80,3 +80,43 @@ def test_worker_crash_is_detected():
         assert eng.poisoned()
     finally:
         coord.shutdown()
+
+
+@pytest.mark.timeout(600)
+@pytest.mark.parametrize("apc", [False, True])
+def test_deepseek_tp2_shm_engine_matches_reference(apc):
+    """The DeepSeek-style model (MLA + DSA indexer + mHC + expert-parallel MoE) through the
+    same engine and transport: 2 CPU ranks split heads and place experts by rank."""
+    from zstep_b200.config import deepseek_tiny
+    from zstep_b200.models.deepseek_ref import DeepSeekReference
+    from zstep_b200.models.deepseek_weights import DeepSeekRandomWeights
+
+    cfg = deepseek_tiny()
+    rng = random.Random(11)
+    base = [rng.randrange(cfg.vocab_size) for _ in range(32 if apc else 0)]
+    ps = [base + [rng.randrange(cfg.vocab_size) for _ in range(rng.randint(8, 24))] for _ in range(6)]
+    model = DeepSeekReference(cfg, DeepSeekRandomWeights(cfg, seed=0))
+    ref = []
+    for p in ps:
+        st = model.new_state()
+        for t in p:
+            lg = model.step(st, t)
+        gen = []
+        for _ in range(12):
+            gen.append(int(torch.argmax(lg)))
+            lg = model.step(st, gen[-1])
+        ref.append(gen)
+    eng, coord = launch(model="deepseek-tiny", world_size=2, device="cpu", max_seqs=2, max_step_tokens=64,
+                        page_size=16, num_pages=128, max_model_len=256, num_ckpt_slots=16 if apc else 0,
+                        engine={"max_prefill_chunk": 24, "prefix_caching": apc, "pages_per_node": 1,
+                                "recurrent_state": True})
+    try:
+        for i, p in enumerate(ps):
+            assert eng.submit(i, p, 12, True)
+        out = run_to_completion(eng)
+        for i in range(len(ps)):
+            assert out[i] == ref[i], f"request {i} diverged"
+        if apc:
+            assert eng.stats().prefix_hit_tokens >= 16
+    finally:
+        coord.shutdown()

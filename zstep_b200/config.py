@@ -233,6 +233,24 @@ class DeepSeekConfig:
     def to_dict(self) -> dict:
         return asdict(self)
 
+    @staticmethod
+    def is_hf_config(path: str | Path) -> bool:
+        p = Path(path)
+        f = p / "config.json" if p.is_dir() else p
+        if not f.is_file():
+            return False
+        return "kv_lora_rank" in json.loads(f.read_text(encoding="utf-8"))
+
+    @classmethod
+    def from_hf(cls, path: str | Path) -> "DeepSeekConfig":
+        """DeepSeek-V3-style ``config.json`` keys; mHC / index fields where present."""
+        p = Path(path)
+        raw = json.loads((p / "config.json" if p.is_dir() else p).read_text(encoding="utf-8"))
+        known = {f for f in cls.__dataclass_fields__}
+        kw = {k: v for k, v in raw.items() if k in known}
+        kw["name"] = str(raw.get("_name_or_path", raw.get("model_type", "deepseek")))
+        return cls(**kw)
+
 
 def deepseek_full() -> DeepSeekConfig:
     """The DeepSeek-style benchmark shape (48 layers, MLA 64 heads, DSA top-2048, mHC x4,

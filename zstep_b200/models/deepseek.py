@@ -371,6 +371,12 @@ class DeepSeekRunner:
             self._advance(rows, nxt)
         self._site(rows, self.hc_head, self.final_norm, mix_out=False)
 
+    def copy_recurrent_state(self, src_slot: int, dst_slot: int) -> None:
+        """No recurrent state: every cached quantity lives in the paged latent / index caches."""
+
+    def checkpoint_args(self, ckpt_rows, ckpt_slots, query_start):
+        return None
+
     # ------------------------------------------------------------------ public step API
     def decode_forward(self, rows: int) -> torch.Tensor:
         self._layers(rows, decode=True)

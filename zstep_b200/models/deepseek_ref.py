@@ -150,6 +150,9 @@ class DeepSeekReference:
             s.ik.append(torch.zeros(0, c.index_head_dim, device=self.dev))
         return s
 
+    def clone_state(self, s: DsState) -> DsState:
+        return DsState(ckv=[t.clone() for t in s.ckv], ik=[t.clone() for t in s.ik], pos=s.pos)
+
     def _q(self, x: torch.Tensor) -> torch.Tensor:
         if not self.quant:
             return x

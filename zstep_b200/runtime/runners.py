@@ -32,16 +32,29 @@ from ..sampling import sample_logits, verify_greedy
 
 
 def _resolve_config(name: str):
-    from ..config import PRESETS, Qwen35Config
+    from ..config import PRESETS, DeepSeekConfig, Qwen35Config
 
     if name in PRESETS:
         return PRESETS[name]()
+    if DeepSeekConfig.is_hf_config(name):
+        return DeepSeekConfig.from_hf(name)
     return Qwen35Config.from_hf(name)
 
 
+def _is_deepseek(cfg) -> bool:
+    from ..config import DeepSeekConfig
+
+    return isinstance(cfg, DeepSeekConfig)
+
+
 def _weights(cfg, name: str, seed: int):
+    from ..models.deepseek_weights import DeepSeekRandomWeights
     from ..models.weights import RandomWeights, SafetensorsWeights
 
+    if _is_deepseek(cfg):
+        if os.path.isdir(name):
+            raise NotImplementedError("DeepSeek-style checkpoints: only random-init weights are wired")
+        return DeepSeekRandomWeights(cfg, seed=seed)
     if os.path.isdir(name):
         return SafetensorsWeights(cfg, name)
     return RandomWeights(cfg, seed=seed)
@@ -67,14 +80,16 @@ class CpuReferenceRunner:
     """fp32 reference model, one ``SeqState`` per request slot (+ checkpoint slots)."""
 
     def __init__(self, args, rank: int, world: int, geo):
+        from ..models.deepseek_ref import DeepSeekReference
         from ..models.qwen35_ref import Qwen35Reference
 
         torch.set_num_threads(max(1, (os.cpu_count() or 2) // max(1, world)))
         self.cfg = _resolve_config(args.model)
         self.rank, self.world = rank, world
         ar = (lambda x: self._allreduce(x)) if world > 1 else None
-        self.model = Qwen35Reference(self.cfg, _weights(self.cfg, args.model, args.seed), device="cpu",
-                                     quant=False, tp_rank=rank, tp_size=world, allreduce=ar)
+        model_cls = DeepSeekReference if _is_deepseek(self.cfg) else Qwen35Reference
+        self.model = model_cls(self.cfg, _weights(self.cfg, args.model, args.seed), device="cpu",
+                               quant=False, tp_rank=rank, tp_size=world, allreduce=ar)
         self.states: dict[int, object] = {}
         self.ckpt: dict[int, object] = {}
 
@@ -141,6 +156,7 @@ class GpuRunner:
     """B200 runner: the kernels of models/qwen35.py driven by step plans."""
 
     def __init__(self, args, rank: int, world: int, geo):
+        from ..models.deepseek import DeepSeekRunner
         from ..models.qwen35 import Qwen35Runner
         from ..parallel import make_collectives
 
@@ -148,7 +164,12 @@ class GpuRunner:
         self.dev = torch.device("cuda", torch.cuda.current_device())
         coll = make_collectives(self.dev) if world > 1 else None
         num_spec = args.num_spec_tokens if args.spec_method == "mtp" else 0
-        self.r = Qwen35Runner(self.cfg, device=self.dev, weights=_weights(self.cfg, args.model, args.seed),
+        if _is_deepseek(self.cfg):
+            if num_spec:
+                raise NotImplementedError("MTP drafts are wired for the Qwen3.5 runner only")
+            num_spec = 0
+        runner_cls = DeepSeekRunner if _is_deepseek(self.cfg) else Qwen35Runner
+        self.r = runner_cls(self.cfg, device=self.dev, weights=_weights(self.cfg, args.model, args.seed),
                               max_seqs=geo.max_seqs, max_prefill_tokens=geo.max_step_tokens,
                               num_pages=args.num_pages, page_size=geo.page_size, max_model_len=args.max_model_len,
                               num_ckpt_slots=args.num_ckpt_slots, tp_rank=rank, tp_size=world, collectives=coll,
