@@ -44,7 +44,8 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
                const OptT& row_dst, const OptT& row_scale, const OptT& err, int64_t max_items,
                int64_t block_n, int64_t k_splits, int64_t split_stride, int64_t a_tiled,
                int64_t fix_splits, const OptT& ws, const OptT& tile_sem, const OptT& row_temp,
-               const OptT& row_seed, const OptT& row_pos, int64_t id_offset, const OptT& sample_any) {
+               const OptT& row_seed, const OptT& row_pos, int64_t id_offset, const OptT& sample_any,
+               int64_t a_fp4) {
   check_cuda(a, "a");
   check_cuda(sfa, "sfa");
   check_cuda(b, "b");
@@ -54,7 +55,8 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
   check_opt(group_offset, "group_offset");
   check_opt(chunk_prefix, "chunk_prefix");
   TORCH_CHECK(a.element_size() == 1 && b.element_size() == 1, "a/b must be 8-bit");
-  TORCH_CHECK(a.numel() >= groups * n_pad * k, "a too small");
+  TORCH_CHECK(a.numel() * (a_fp4 ? 2 : 1) >= groups * n_pad * k, "a too small");
+  TORCH_CHECK(!a_fp4 || a_tiled, "MXFP4 weights must be pre-tiled");
   TORCH_CHECK(b.numel() % k == 0, "b must be [rows, k]");
   GemmMxf8Args p{};
   p.a = ptr<const uint8_t>(a);
@@ -83,6 +85,7 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
   p.k_splits = (int)k_splits;
   p.split_stride = split_stride;
   p.a_tiled = (int)a_tiled;
+  p.a_fp4 = (int)a_fp4;
   p.fix_splits = (int)fix_splits;
   if (row_temp.has_value()) {
     TORCH_CHECK(row_seed.has_value() && row_pos.has_value(), "sampling needs row_temp, row_seed and row_pos");
@@ -596,7 +599,8 @@ void mla_up(const Tensor& partial, int64_t rows, int64_t heads, int64_t splits, 
 
 void dsa_index(const Tensor& iq, const Tensor& iw, const Tensor& ik_cache, const Tensor& page_table,
                int64_t page_size, const Tensor& slots, const Tensor& ctx_len, int64_t rows, int64_t index_heads,
-               int64_t topk, int64_t max_ctx, const Tensor& scores, const Tensor& sel, const Tensor& n_sel) {
+               int64_t topk, int64_t max_ctx, const Tensor& scores, const Tensor& sel, const Tensor& n_sel,
+               const OptT& err) {
   check_cuda(iq, "iq");
   check_cuda(scores, "scores");
   TORCH_CHECK(ik_cache.size(-1) == 128, "dsa_index: index dim must be 128");
@@ -617,6 +621,7 @@ void dsa_index(const Tensor& iq, const Tensor& iw, const Tensor& ik_cache, const
   s.scale = (float)(1.0 / std::sqrt(128.0));
   s.scores = ptr<float>(scores);
   s.ld_scores = (int)scores.stride(0);
+  s.err = optptr<int>(err);
   rc(zs_dsa_scores(&s, (int)max_ctx, stream()), "zs_dsa_scores");
   DsaTopkArgs k{};
   k.scores = s.scores;
@@ -653,7 +658,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_absorb_q", &mla_absorb_q);
   m.def("mla_attn", &mla_attn);
   m.def("mla_up", &mla_up);
-  m.def("dsa_index", &dsa_index);
+  m.def("dsa_index", &dsa_index, py::arg("iq"), py::arg("iw"), py::arg("ik_cache"), py::arg("page_table"),
+        py::arg("page_size"), py::arg("slots"), py::arg("ctx_len"), py::arg("rows"), py::arg("index_heads"),
+        py::arg("topk"), py::arg("max_ctx"), py::arg("scores"), py::arg("sel"), py::arg("n_sel"),
+        py::arg("err") = py::none());
   m.def("gather_sum", &gather_sum);
 
   m.def("fused_allreduce_norm", &fused_allreduce_norm, py::arg("rank"), py::arg("world"), py::arg("delta"),
@@ -679,7 +687,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("block_n"), py::arg("k_splits"), py::arg("split_stride"), py::arg("a_tiled"),
         py::arg("fix_splits") = 1, py::arg("ws") = py::none(), py::arg("tile_sem") = py::none(),
         py::arg("row_temp") = py::none(), py::arg("row_seed") = py::none(), py::arg("row_pos") = py::none(),
-        py::arg("id_offset") = 0, py::arg("sample_any") = py::none());
+        py::arg("id_offset") = 0, py::arg("sample_any") = py::none(), py::arg("a_fp4") = 0);
   m.def("quant_mxf8", &quant_mxf8);
   m.def("add_rmsnorm_quant", &add_rmsnorm_quant, py::arg("residual"), py::arg("delta"), py::arg("n_terms"),
         py::arg("d_row_stride"), py::arg("d_term_stride"), py::arg("weight"), py::arg("w_offset"), py::arg("eps"),

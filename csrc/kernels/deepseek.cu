@@ -399,7 +399,7 @@ mla_prologue_kernel(MlaPrologueArgs a) {
 // ------------------------------------------------------------------------------ absorb q
 // q_lat[t, h, :] = W_UK[h]^T q_nope[t, h]: CTA per (head, 16 tokens), thread per 2
 // latent columns.
-constexpr int kAbsTok = 16;
+constexpr int kAbsTok = 4;
 __global__ void __launch_bounds__(256)
 mla_absorb_q_kernel(const __nv_bfloat16* __restrict__ qi, int ld_qi, int qk_dim, int nope,
                     const __nv_bfloat16* __restrict__ w_uk, int kl, int heads, int rows,
@@ -418,6 +418,7 @@ mla_absorb_q_kernel(const __nv_bfloat16* __restrict__ qi, int ld_qi, int qk_dim,
 #pragma unroll
   for (int tt = 0; tt < kAbsTok; ++tt) acc[tt][0] = acc[tt][1] = 0.f;
   const __nv_bfloat16* wh = w_uk + (size_t)h * nope * kl;
+#pragma unroll 16
   for (int d = 0; d < nope; ++d) {
     const float2 w = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(wh + (size_t)d * kl + c));
 #pragma unroll
@@ -563,7 +564,7 @@ mla_attn_kernel(MlaAttnArgs a) {
 // Merge the split records of (token, head) into o_lat (bf16-rounded), then
 // o[t, h, :] = W_UV[h] o_lat (bf16) and MXFP8-quantize the row [heads * v] for o_proj.
 // CTA per (head, 8 tokens); 128 threads, thread per value dim.
-constexpr int kUpTok = 8;
+constexpr int kUpTok = 2;
 __global__ void __launch_bounds__(128)
 mla_up_kernel(MlaUpArgs a) {
   const int h = blockIdx.x;
@@ -605,6 +606,7 @@ mla_up_kernel(MlaUpArgs a) {
 #pragma unroll
   for (int tt = 0; tt < kUpTok; ++tt) acc[tt] = 0.f;
   const __nv_bfloat16* wh = a.w_uv_t + (size_t)h * kLat * V;
+#pragma unroll 16
   for (int c = 0; c < kLat; ++c) {
     const float w = __bfloat162float(wh[(size_t)c * V + d]);
 #pragma unroll
@@ -629,51 +631,133 @@ mla_up_kernel(MlaUpArgs a) {
 }
 
 // ------------------------------------------------------------------------------ DSA indexer
-// score[t, s] = sum_h w[t, h] relu(iq[t, h] . ik[s]) * id^-0.5 for s < ctx(t), only for
-// tokens whose context exceeds top-k.  CTA per (token, 128 keys), thread per key.
-constexpr int kIdxKeys = 128;
 constexpr int kIdxDim = 128;
-__global__ void __launch_bounds__(kIdxKeys)
-dsa_scores_kernel(DsaScoresArgs a) {
+
+// Tensor-core indexer scores: per (token, 1024-key chunk) CTA, 128-key tiles are staged
+// by cp.async into the K-major 128-byte-swizzled layout (two 64-dim chunks per row), one
+// thread issues 8 tcgen05.mma (kind::f16, bf16, M = 128 keys, N = index heads, K = 16
+// each) into TMEM, and each of the 4 warps reads its 32 keys' head scores back to form
+// sum_h w_h relu(q_h . k) * scale.  The next tile's copies overlap the MMA and epilogue.
+constexpr int kTcKeys = 128;
+constexpr int kTcTiles = 8;
+
+ZS_DEVICE void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+ZS_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+ZS_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Byte offset of 16-byte piece p (0..15) of row r in a K-major SW128 tile of `rows` rows
+// whose 256-byte rows are split into two 64-element chunks.
+ZS_DEVICE uint32_t sw128_off(int r, int p, int rows) {
+  return (uint32_t)((p >> 3) * rows * 128 + r * 128 + (((p & 7) ^ (r & 7)) << 4));
+}
+
+template <int IH>
+__global__ void __launch_bounds__(128)
+dsa_scores_tc_kernel(DsaScoresArgs a) {
   const int t = blockIdx.x;
   const int ctx = a.ctx_len[t];
-  const int s0 = blockIdx.y * kIdxKeys;
-  if (ctx <= a.topk || s0 >= ctx) return;
-  extern __shared__ __align__(16) float qsm[];  // [index_heads][kIdxDim] then w[index_heads]
-  float* wsm = qsm + a.index_heads * kIdxDim;
-  for (int i = threadIdx.x; i < a.index_heads * kIdxDim; i += blockDim.x)
-    qsm[i] = __bfloat162float(a.iq[(size_t)t * a.index_heads * kIdxDim + i]);
-  for (int i = threadIdx.x; i < a.index_heads; i += blockDim.x) wsm[i] = a.iw[(size_t)t * a.index_heads + i];
-  __syncthreads();
-  const int s = s0 + threadIdx.x;
-  if (s >= ctx) return;
+  const int s_begin = blockIdx.y * kTcKeys * kTcTiles;
+  if (ctx <= a.topk || s_begin >= ctx) return;  // uniform: before any barrier or TMEM use
+  const int n_tiles = min(kTcTiles, (ctx - s_begin + kTcKeys - 1) / kTcKeys);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* A = base;                                  // [2][2 chunks][128 rows][128 B]
+  uint8_t* B = base + 2 * 2 * kTcKeys * 128;          // [2 chunks][IH rows][128 B]
+  float* wsm = reinterpret_cast<float*>(B + 2 * IH * 128);
+  __shared__ uint64_t mbar;
+  __shared__ uint32_t tmem_base;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr uint32_t kCols = IH < 32 ? 32 : IH;
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, kCols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&mbar, 1);
+    fence_barrier_init();
+  }
+  // Index queries (B operand) and head weights.
+  const __nv_bfloat16* q = a.iq + (size_t)t * IH * kIdxDim;
+  for (int i = tid; i < IH * 16; i += blockDim.x) {
+    const int h = i >> 4, p = i & 15;
+    cp_async16(B + sw128_off(h, p, IH), q + (size_t)h * kIdxDim + p * 8);
+  }
+  for (int i = tid; i < IH; i += blockDim.x) wsm[i] = a.iw[(size_t)t * IH + i];
   const int slot = a.slot[t];
-  const int page = a.page_table[(size_t)slot * a.max_pages + s / a.page_size];
-  const uint4* kr = reinterpret_cast<const uint4*>(a.ik_cache + ((size_t)page * a.page_size + s % a.page_size) * kIdxDim);
-  float k[kIdxDim];
-#pragma unroll
-  for (int i = 0; i < kIdxDim / 8; ++i) {
-    const uint4 u = kr[i];
-    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = __bfloat1622float2(b[j]);
-      k[i * 8 + 2 * j] = f.x;
-      k[i * 8 + 2 * j + 1] = f.y;
+  auto stage_tile = [&](int tile, uint8_t* dst) {
+    const int s0 = s_begin + tile * kTcKeys;
+    for (int i = tid; i < kTcKeys * 16; i += blockDim.x) {
+      const int r = i >> 4, p = i & 15;
+      const int s = s0 + r;
+      uint8_t* d = dst + sw128_off(r, p, kTcKeys);
+      if (s < ctx) {
+        const int page = a.page_table[(size_t)slot * a.max_pages + s / a.page_size];
+        cp_async16(d, a.ik_cache + ((size_t)page * a.page_size + s % a.page_size) * kIdxDim + p * 8);
+      } else {
+        *reinterpret_cast<uint4*>(d) = make_uint4(0, 0, 0, 0);
+      }
     }
-  }
-  float score = 0.f;
-  for (int h = 0; h < a.index_heads; ++h) {
-    const float* q = qsm + h * kIdxDim;
-    float d = 0.f;
+  };
+  stage_tile(0, A);
+  cp_async_commit();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const uint32_t idesc = make_idesc_bf16(kTcKeys, IH, 0, 0);
+  bool ok = true;
+  for (int i = 0; i < n_tiles; ++i) {
+    cp_async_wait_all();
+    fence_proxy_async_shared();
+    __syncthreads();
+    uint8_t* Ai = A + (i & 1) * (2 * kTcKeys * 128);
+    if (tid == 0) {
+      tc_fence_after();
 #pragma unroll
-    for (int i = 0; i < kIdxDim; i += 4) {
-      const float4 qv = *reinterpret_cast<const float4*>(q + i);
-      d += qv.x * k[i] + qv.y * k[i + 1] + qv.z * k[i + 2] + qv.w * k[i + 3];
+      for (int kc = 0; kc < 2; ++kc)
+#pragma unroll
+        for (int kb = 0; kb < 4; ++kb) {
+          const uint64_t ad = make_smem_desc(smem_u32(Ai + kc * kTcKeys * 128) + kb * 32, 16, 1024, 2);
+          const uint64_t bd = make_smem_desc(smem_u32(B + kc * IH * 128) + kb * 32, 16, 1024, 2);
+          mma_bf16(tmem, ad, bd, idesc, (kc | kb) != 0 ? 1u : 0u);
+        }
+      tc_commit(&mbar);
     }
-    score += wsm[h] * fmaxf(d, 0.f) * a.scale;
+    if (i + 1 < n_tiles) {
+      stage_tile(i + 1, A + ((i + 1) & 1) * (2 * kTcKeys * 128));
+      cp_async_commit();
+    }
+    ok = mbar_wait(&mbar, (uint32_t)(i & 1), a.err);
+    if (!__syncthreads_and(ok)) break;  // bounded wait gave up: the error is recorded
+    tc_fence_after();
+    const uint32_t tq = tmem + ((uint32_t)(warp * 32) << 16);
+    float score = 0.f;
+#pragma unroll
+    for (int c0 = 0; c0 < IH; c0 += (IH < 32 ? 16 : 32)) {
+      if (IH < 32) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(tq + c0, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) score += wsm[c0 + j] * fmaxf(__uint_as_float(r[j]), 0.f);
+      } else {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tq + c0, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) score += wsm[c0 + j] * fmaxf(__uint_as_float(r[j]), 0.f);
+      }
+    }
+    const int s = s_begin + i * kTcKeys + warp * 32 + lane;
+    if (s < ctx) a.scores[(size_t)t * a.ld_scores + s] = score * a.scale;
+    tc_fence_before();
+    __syncthreads();
   }
-  a.scores[(size_t)t * a.ld_scores + s] = score;
+  cp_async_wait_all();  // no copy may still target shared memory when the CTA exits
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, kCols);
 }
 
 // Top-k selection per token (CTA of 1024 threads): positions 0..ctx-1 when ctx <= k, else
@@ -879,15 +963,18 @@ int zs_mla_up(const MlaUpArgs* a, cudaStream_t stream) {
 
 int zs_dsa_scores(const DsaScoresArgs* a, int max_ctx, cudaStream_t stream) {
   if (a->rows <= 0 || max_ctx <= a->topk) return 0;
-  if (a->index_heads > 128) return -2;
-  const size_t smem = (size_t)a->index_heads * ds::kIdxDim * 4 + (size_t)a->index_heads * 4;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(ds::dsa_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 80 * 1024);
-    attr_set = true;
-  }
-  dim3 grid(a->rows, (max_ctx + ds::kIdxKeys - 1) / ds::kIdxKeys);
-  ds::dsa_scores_kernel<<<grid, ds::kIdxKeys, smem, stream>>>(*a);
+  const int ih = a->index_heads;
+  if (ih != 16 && ih != 32 && ih != 64 && ih != 128) return -2;
+  const size_t smem = 1024 + 2 * 2 * ds::kTcKeys * 128 + 2 * (size_t)ih * 128 + (size_t)ih * 4;
+  dim3 grid(a->rows, (max_ctx + ds::kTcKeys * ds::kTcTiles - 1) / (ds::kTcKeys * ds::kTcTiles));
+  auto launch = [&](auto kern) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<grid, 128, smem, stream>>>(*a);
+  };
+  if (ih == 16) launch(ds::dsa_scores_tc_kernel<16>);
+  else if (ih == 32) launch(ds::dsa_scores_tc_kernel<32>);
+  else if (ih == 64) launch(ds::dsa_scores_tc_kernel<64>);
+  else launch(ds::dsa_scores_tc_kernel<128>);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

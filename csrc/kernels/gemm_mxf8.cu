@@ -49,7 +49,7 @@ constexpr int NUM_THREADS = 192;
 constexpr int kMaxGroups = 520;  // grouped mode: per-group tables are staged in smem
 constexpr int kMaxFixSplits = 8; // in-kernel split-K factor limit
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool FP4 = false>
 struct Cfg {
   // Each pipeline stage holds KT consecutive K tiles, so one bulk copy moves 32 KiB of
   // weights and one 3-D TMA box both tiles of activations: the producer issues half as
@@ -62,6 +62,8 @@ struct Cfg {
   static constexpr int SFA_COL = 2 * BN;           // + 8 * (kt & 1), 4 columns
   static constexpr int SFB_COL = 2 * BN + 4;       // + 8 * (kt & 1), 4 columns
   static constexpr int TMEM_COLS = (2 * BN + 16) <= 128 ? 128 : ((2 * BN + 16) <= 256 ? 256 : 512);
+  static constexpr int A4_BYTES = FP4 ? A_BYTES / 2 : 16;  // packed e2m1 staging per tile
+  static constexpr int THREADS = FP4 ? 320 : 192;          // + 4 converter warps for FP4
   struct Smem {
     uint8_t a[STAGES][KT][A_BYTES];
     uint8_t b[STAGES][KT][B_BYTES];
@@ -74,12 +76,16 @@ struct Cfg {
     int g_count[kMaxGroups];
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
+    uint64_t conv[STAGES];          // FP4: the converter warps widened stage's weights
     uint64_t acc_full[2];
     uint64_t acc_empty[2];
     uint64_t drain;
     uint32_t tmem_base;
     int abort_flag;
     int fix_last;                   // split-K: this CTA completed the current tile
+    // FP4 staging last, so the swizzled operand buffers above keep their 1024-byte
+    // alignment in every instantiation.
+    alignas(1024) uint8_t a4[FP4 ? STAGES : 1][KT][A4_BYTES];
   };
 };
 
@@ -179,12 +185,24 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t phase, int
   return false;
 }
 
-template <int BN, int STAGES>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+// Widen 8 packed e2m1 values (one 32-bit word, element i in nibble i) to 8 e4m3 bytes:
+// a byte permute picks each magnitude from an 8-entry table of the e4m3 images of
+// 0, 0.5, 1, 1.5, 2, 3, 4, 6; a second permute turns each sign bit into 0x00 / 0x80.
+__device__ __forceinline__ uint2 widen_e2m1x8(uint32_t w) {
+  const uint32_t lo = 0x3C383000u, hi = 0x4C484440u;
+  const uint32_t m0 = __byte_perm(lo, hi, w & 0x7777u);
+  const uint32_t s0 = __byte_perm(0x00008000u, 0u, (w >> 3) & 0x1111u);
+  const uint32_t m1 = __byte_perm(lo, hi, (w >> 16) & 0x7777u);
+  const uint32_t s1 = __byte_perm(0x00008000u, 0u, (w >> 19) & 0x1111u);
+  return make_uint2(m0 | s0, m1 | s1);
+}
+
+template <int BN, int STAGES, bool FP4>
+__global__ void __launch_bounds__(Cfg<BN, STAGES, FP4>::THREADS, 1)
 gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
                  const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_b_full,
                  const GemmMxf8Args p) {
-  using C = Cfg<BN, STAGES>;
+  using C = Cfg<BN, STAGES, FP4>;
   using Smem = typename C::Smem;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -196,6 +214,7 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], 1);
+      mbar_init(&s.conv[i], 4);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.acc_full[i], 1);
@@ -206,8 +225,8 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
     fence_barrier_init();
   }
   if (p.chunk_prefix != nullptr) {
-    for (int g = threadIdx.x; g <= p.groups; g += NUM_THREADS) s.g_prefix[g] = __ldg(p.chunk_prefix + g);
-    for (int g = threadIdx.x; g < p.groups; g += NUM_THREADS) {
+    for (int g = threadIdx.x; g <= p.groups; g += C::THREADS) s.g_prefix[g] = __ldg(p.chunk_prefix + g);
+    for (int g = threadIdx.x; g < p.groups; g += C::THREADS) {
       s.g_offset[g] = __ldg(p.group_offset + g);
       s.g_count[g] = __ldg(p.group_count + g);
     }
@@ -246,8 +265,12 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
           // A full-height B box spans KT tiles (a tile past the end of K is zero-filled);
           // short chunks load n16 16-row boxes per tile.
           const bool full_b = n16 * 16 == BN;
-          mbar_expect_tx(&s.full[st], n_sub * (A_BYTES + 2 * SF_BYTES) + (full_b ? C::KT : n_sub) * n16 * 16 * BK);
-          if (p.a_tiled) {  // pre-swizzled contiguous tiles: one plain bulk copy
+          const int a_bytes = FP4 ? C::A4_BYTES : A_BYTES;
+          mbar_expect_tx(&s.full[st], n_sub * (a_bytes + 2 * SF_BYTES) + (full_b ? C::KT : n_sub) * n16 * 16 * BK);
+          if (FP4) {  // packed e2m1 tiles into the staging buffer; the converter warps widen them
+            bulk_load(s.a4[st][0], p.a + ((size_t)(a_row / BM) * k_tiles + kt) * C::A4_BYTES, n_sub * C::A4_BYTES,
+                      &s.full[st]);
+          } else if (p.a_tiled) {  // pre-swizzled contiguous tiles: one plain bulk copy
             bulk_load(s.a[st][0], p.a + ((size_t)(a_row / BM) * k_tiles + kt) * A_BYTES, n_sub * A_BYTES,
                       &s.full[st]);
           } else {
@@ -303,6 +326,7 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
         const int n_sub = min(C::KT, it.kt1 - kt);
         const int st = consumed % STAGES;
         ok = wait_or_abort(&s.full[st], (consumed / STAGES) & 1, p.err, abort_flag);
+        if (FP4 && ok) ok = wait_or_abort(&s.conv[st], (consumed / STAGES) & 1, p.err, abort_flag);
         if (!__all_sync(0xffffffff, ok)) {
           ok = false;
           break;
@@ -347,6 +371,42 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
       if (!mbar_wait(&s.drain, 0, nullptr)) report_error(p.err, kErrDrainTimeout);
     }
     __syncwarp();
+  } else if (FP4 && warp >= 6) {
+    // ------------------------------------------------------------------ FP4 converters
+    // Walk the same stage sequence as the MMA warp: once a stage's copies landed, widen
+    // its packed weight tiles into the swizzled e4m3 image the MMA reads (piece c of row
+    // r at piece c ^ (r % 8)), make the writes visible to the tensor core, and arrive.
+    const int ct = threadIdx.x - 192;
+    uint32_t consumed = 0;
+    bool ok = true;
+    Item it;
+    for (int idx = blockIdx.x; ok && get_item<BN>(p, idx, it, s.g_prefix, s.g_offset, s.g_count) && !*abort_flag;
+         idx += gridDim.x) {
+      for (int kt = it.kt0; kt < it.kt1; kt += C::KT) {
+        const int n_sub = min(C::KT, it.kt1 - kt);
+        const int st = consumed % STAGES;
+        ok = wait_or_abort(&s.full[st], (consumed / STAGES) & 1, p.err, abort_flag);
+        if (!__all_sync(0xffffffff, ok)) {
+          ok = false;
+          break;
+        }
+        for (int j = 0; j < n_sub; ++j) {
+          const uint8_t* src = s.a4[st][j];
+          uint8_t* dst = s.a[st][j];
+#pragma unroll 4
+          for (int task = ct; task < BM * 8; task += 128) {
+            const int r = task >> 3, c = task & 7;
+            const uint2 v = *reinterpret_cast<const uint2*>(src + r * 64 + c * 8);
+            const uint2 w0 = widen_e2m1x8(v.x), w1 = widen_e2m1x8(v.y);
+            *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(w0.x, w0.y, w1.x, w1.y);
+          }
+        }
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.conv[st]);
+        ++consumed;
+      }
+    }
   } else {
     // ------------------------------------------------------------------ epilogue
     // Each thread owns one accumulator row (a weight feature) and walks the token
@@ -613,7 +673,7 @@ int num_sms() {
   return n;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool FP4>
 int launch(const GemmMxf8Args& p, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tbf,
            cudaStream_t stream) {
   using namespace zs::gemm;
@@ -626,10 +686,11 @@ int launch(const GemmMxf8Args& p, const CUtensorMap& ta, const CUtensorMap& tb, 
   } else if (p.max_items > 0 && p.max_items < grid) {
     grid = p.max_items;
   }
-  const size_t smem = sizeof(typename Cfg<BN, STAGES>::Smem) + 1024;
-  auto kern = gemm_mxf8_kernel<BN, STAGES>;
+  using CF = Cfg<BN, STAGES, FP4>;
+  const size_t smem = sizeof(typename CF::Smem) + 1024;
+  auto kern = gemm_mxf8_kernel<BN, STAGES, FP4>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  kern<<<grid, NUM_THREADS, smem, stream>>>(ta, tb, tbf, p);
+  kern<<<grid, CF::THREADS, smem, stream>>>(ta, tb, tbf, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -15;
 }
 
@@ -658,13 +719,19 @@ extern "C" int zs_gemm_mxf8(const GemmMxf8Args* args, cudaStream_t stream) {
   if (p.chunk_prefix != nullptr && p.chunk_rows != bn) return -17;
   if (p.chunk_prefix != nullptr && p.groups > kMaxGroups) return -18;
   CUtensorMap ta, tb;
-  if (p.a_tiled) {
+  if (p.a_fp4) {
+    // Packed e2m1 tiles (8 KiB each) reach shared memory by plain bulk copies; the map
+    // only has to be a valid descriptor of the buffer.
+    if (!p.a_tiled) return -22;
+    if (make_tmap_tiled(&ta, p.a, (int64_t)p.groups * (p.n_pad / BM) * (p.k / BK) / 2) != 0) return -13;
+  } else if (p.a_tiled) {
     if (make_tmap_tiled(&ta, p.a, (int64_t)p.groups * (p.n_pad / BM) * (p.k / BK)) != 0) return -13;
   } else if (make_tmap_u8(&ta, p.a, (int64_t)p.groups * p.n_pad, p.k, BM) != 0) {
     return -13;
   }
   if (make_tmap_u8(&tb, p.b, p.b_rows, p.k, 16) != 0) return -14;
   CUtensorMap tbf;
-  if (make_tmap_b3(&tbf, p.b, p.b_rows, p.k, bn, Cfg<32, 4>::KT) != 0) return -14;
-  return bn == 32 ? launch<32, 4>(p, ta, tb, tbf, stream) : launch<128, 3>(p, ta, tb, tbf, stream);
+  if (make_tmap_b3(&tbf, p.b, p.b_rows, p.k, bn, Cfg<32, 4, false>::KT) != 0) return -14;
+  if (p.a_fp4) return bn == 32 ? launch<32, 3, true>(p, ta, tb, tbf, stream) : launch<128, 2, true>(p, ta, tb, tbf, stream);
+  return bn == 32 ? launch<32, 4, false>(p, ta, tb, tbf, stream) : launch<128, 3, false>(p, ta, tb, tbf, stream);
 }

@@ -46,6 +46,8 @@ typedef struct GemmMxf8Args {
   int k_splits;            // dense mode, kEpiStoreF32 only: split K into this many partials
   long long split_stride;  // elements between split partials in out
   int a_tiled;             // 1: weights pre-tiled as [groups*n_pad/128][k/128][128 rows][128 B]
+  int a_fp4;               // 1: weights are packed e2m1 (MXFP4), pre-tiled [..][k/128][128 rows][64 B];
+                           //    widened to e4m3 in shared memory (scales unchanged)
                            //    (each TMA box one contiguous 16 KiB block); 0: row-major
   int epi_mode;
   void* out;
@@ -386,6 +388,7 @@ typedef struct DsaScoresArgs {
   float scale;
   float* scores;               // [rows, ld_scores]
   int ld_scores;
+  int* err;                    // bounded-wait failures
 } DsaScoresArgs;
 
 typedef struct DsaTopkArgs {

@@ -187,6 +187,46 @@ def test_gemm_tiled_weights(C, grouped):
         torch.testing.assert_close(out[o:o + cnt], s["xd"][o:o + cnt] @ s["wd"][gi, :n].T, rtol=1e-4, atol=1e-3)
 
 
+@pytest.mark.parametrize("bn", [32, 128])
+@pytest.mark.parametrize("grouped", [False, True])
+def test_gemm_fp4_weights(C, grouped, bn):
+    """MXFP4 weights stay packed in memory and are widened to e4m3 in shared memory by the
+    converter warps: results equal an fp32 GEMM on the dequantized MXFP4 weights."""
+    counts = [5, 40, 0, 129, 33]
+    k, n = 512, 384
+    s = _grouped_setup(counts if grouped else [200], k, n, seed=21)
+    g = len(counts) if grouped else 1
+    w = s["w"]
+    npad = s["npad"]
+    wp = torch.zeros(g, npad, k)
+    wp[:, :n] = w
+    packed, code = mx.quantize_fp4(wp.reshape(g * npad, k))
+    wd = mx.dequantize_fp4(packed, code).reshape(g, npad, k)
+    wq4 = mx.tile_weight_fp4(packed).cuda()
+    wsf = mx.atoms_from_codes(code).cuda()
+    out = torch.full((s["rows"], n), float("nan"), device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    if grouped:
+        pre, c = [0], 0
+        for cnt in counts:
+            c += (cnt + bn - 1) // bn
+            pre.append(c)
+        C.gemm_mxf8(wq4, wsf, s["xq"], s["xsf"], k, npad, n, g, 0, s["cnt"], s["off"],
+                    torch.tensor(pre, dtype=torch.int32, device="cuda"), EPI_F32, out, n, None, None, None, err, 0,
+                    bn, 1, 0, 1, a_fp4=1)
+    else:
+        C.gemm_mxf8(wq4, wsf, s["xq"], s["xsf"], k, npad, n, 1, 200, None, None, None, EPI_F32, out, n, None,
+                    None, None, err, 0, bn, 1, 0, 1, a_fp4=1)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    out = out.cpu()
+    for gi, cnt in enumerate(counts if grouped else [200]):
+        if cnt == 0:
+            continue
+        o = s["offsets"][gi]
+        torch.testing.assert_close(out[o:o + cnt], s["xd"][o:o + cnt] @ wd[gi, :n].T, rtol=1e-4, atol=1e-3)
+
+
 def test_gemm_silu_quant(C):
     counts = [5, 0, 140]
     k, inter = 256, 256  # 4 tiles of (64 gate + 64 up)

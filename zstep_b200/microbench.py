@@ -1,6 +1,7 @@
 """Kernel and step micro-benchmarks with roofline fractions.
 
     python -m zstep_b200.microbench breakdown [--layers 40] [--batch 256] [--ctx 1280]
+    python -m zstep_b200.microbench step --model deepseek --layers 48 --batch 64 --ctx 8192 --tp 8
     python -m zstep_b200.microbench step --eager 1        (one eager decode step; for ncu)
     python -m zstep_b200.microbench gemm --m 256 --n 12352 --k 2048 [--groups 1]
     python -m zstep_b200.microbench moe --m 256
@@ -111,9 +112,38 @@ def build_runner(layers: int, batch: int, ctx: int, experts: int = 256, vocab: i
     return r
 
 
+def build_ds_runner(layers: int, batch: int, ctx: int, tp: int = 1, expert_format: str = "mxfp4"):
+    """DeepSeek-style runner (full per-layer shapes, `layers` deep) holding rank 0's shard
+    of a tp-way attention / expert-parallel layout; reductions stay local.  Every row
+    decodes at position `ctx`, so the indexer scores `ctx + 1` keys and attention reads
+    the top-k (cache contents are left as allocated: the timing does not depend on them)."""
+    from .config import DeepSeekConfig
+    from .models.deepseek import DeepSeekRunner
+    from .parallel.collectives import LocalCollectives
+
+    cfg = DeepSeekConfig(num_hidden_layers=layers, expert_format=expert_format)
+    page = 16
+    pages_per_seq = (ctx + 64 + page - 1) // page
+    r = DeepSeekRunner(cfg, max_seqs=batch, max_prefill_tokens=batch, num_pages=batch * pages_per_seq + 1,
+                       page_size=page, max_model_len=ctx + 64, tp_rank=0, tp_size=tp,
+                       collectives=LocalCollectives() if tp > 1 else None)
+    for s in range(batch):
+        r.set_pages(s, list(range(1 + s * pages_per_seq, 1 + (s + 1) * pages_per_seq)))
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, cfg.vocab_size, (batch,), generator=g)
+    r.stage(ids, [ctx] * batch, list(range(batch)))
+    return r
+
+
+def _runner_for(a):
+    if a.model == "deepseek":
+        return build_ds_runner(a.layers, a.batch, a.ctx, tp=a.tp)
+    return build_runner(a.layers, a.batch, a.ctx, tp=a.tp)
+
+
 def cmd_breakdown(a):
     """Per-op device time of one eager decode step (events around every kernel call)."""
-    r = build_runner(a.layers, a.batch, a.ctx, tp=a.tp)
+    r = _runner_for(a)
     real = r.C
     events = []
 
@@ -157,7 +187,7 @@ def cmd_breakdown(a):
 
 
 def cmd_step(a):
-    r = build_runner(a.layers, a.batch, a.ctx, tp=a.tp)
+    r = _runner_for(a)
     if a.eager:
         for _ in range(a.warmup):
             r.decode_forward(a.batch)
@@ -301,6 +331,7 @@ def main():
     ap.add_argument("--groups", type=int, default=1)
     ap.add_argument("--flush", type=int, default=1, help="evict L2 before every timed call")
     ap.add_argument("--tp", type=int, default=1, help="time rank 0 of a tp-way layout (no communication)")
+    ap.add_argument("--model", default="qwen", choices=["qwen", "deepseek"])
     a = ap.parse_args()
     torch.manual_seed(0)
     {"breakdown": cmd_breakdown, "step": cmd_step, "gemm": cmd_gemm, "gdn": cmd_gdn, "attn": cmd_attn,

@@ -44,18 +44,19 @@ from .qwen35 import (DECODE_BUCKETS, EPI_BF16, EPI_F32, EPI_SILU, PackedLinear, 
 
 
 def pack_linear_fp4(w: torch.Tensor, C) -> PackedLinear:
-    """Expert weights in MXFP4 quantized on the host side of the reference rule, stored
-    as the MXFP8 GEMM consumes them (e2m1 values widened exactly to e4m3, same scales)."""
+    """Expert weights [G, N, K] -> MXFP4: packed e2m1 pre-tiled into 8 KiB chunks per
+    (128-row tile, 128-K tile) plus the usual e8m0 scale atoms.  The GEMM widens each
+    chunk to e4m3 in shared memory, so HBM carries half the bytes of MXFP8."""
     if w.dim() == 2:
         w = w.unsqueeze(0)
     g, n, k = w.shape
     npad = _pad128(n)
-    flat = torch.zeros(g, npad, k, dtype=torch.float32, device=w.device)
-    flat[:, :n] = w.float()
+    flat = torch.zeros(g, npad, k, dtype=torch.bfloat16, device=w.device)
+    flat[:, :n] = w
     flat = flat.reshape(g * npad, k)
     packed, code = mx.quantize_fp4(flat)
-    q = mx.fp4_to_e4m3(packed)
-    return PackedLinear(q=mx.tile_weight(q), sf=mx.atoms_from_codes(code), n=n, n_pad=npad, k=k, groups=g)
+    return PackedLinear(q=mx.tile_weight_fp4(packed), sf=mx.atoms_from_codes(code), n=n, n_pad=npad, k=k, groups=g,
+                        fp4=True)
 
 
 class DeepSeekRunner:
@@ -325,7 +326,7 @@ class DeepSeekRunner:
                        self.page_size, self.ckv_cache[li], self.ik_cache[li], b["q_pe"], b["iq"], b["iw"])
         C.mla_absorb_q(qi, c.qk_head_dim, c.qk_nope_head_dim, L["w_uk"], hl, rows, b["q_lat"])
         C.dsa_index(b["iq"], b["iw"], self.ik_cache[li], self.page_table, self.page_size, slot, lens, rows,
-                    c.index_n_heads, c.index_topk, self.max_model_len, b["scores"], b["sel"], b["n_sel"])
+                    c.index_n_heads, c.index_topk, self.max_model_len, b["scores"], b["sel"], b["n_sel"], b["err"])
         splits = self._attn_splits(rows) if decode else 1
         C.mla_attn(b["q_lat"], b["q_pe"], self.ckv_cache[li], self.page_table, self.page_size, slot, b["sel"],
                    b["n_sel"], rows, hl, splits, c.qk_head_dim ** -0.5, b["attn_part"])

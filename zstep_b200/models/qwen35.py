@@ -59,6 +59,7 @@ class PackedLinear:
     n_pad: int
     k: int
     groups: int = 1
+    fp4: bool = False   # q holds packed e2m1 tiles ([..][k/128][128 rows][64 B]); widened in the GEMM
 
 
 def pack_linear(w: torch.Tensor, C) -> PackedLinear:
@@ -330,14 +331,14 @@ class Qwen35Runner:
         if grouped:
             bn = self._moe_bn(rows)
             self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, w.groups, 0, b["gcount"], b["goff"], b["gpre"],
-                             epi, out, ldo, out_sf, row_dst, row_scale, b["err"], 0, bn, 1, 0, 1)
+                             epi, out, ldo, out_sf, row_dst, row_scale, b["err"], 0, bn, 1, 0, 1, a_fp4=int(w.fp4))
         else:
             bn = 32 if rows <= 32 else 128
             tiles = -(-rows // bn) * (w.n_pad // 128)
             fs = self._fix_splits(tiles, tiles, w.k // 128, bn) if (k_splits == 1 and self.use_fix_splits) else 1
             self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, 1, rows, None, None, None, epi, out, ldo,
                              out_sf, row_dst, row_scale, b["err"], 0, bn, k_splits, rows * ldo, 1,
-                             fs, b["gemm_ws"], b["gemm_sem"], **sampling)
+                             fs, b["gemm_ws"], b["gemm_sem"], a_fp4=int(w.fp4), **sampling)
 
     def _fix_splits(self, max_tiles: int, items: int, k_tiles: int, bn: int) -> int:
         """In-kernel split-K factor for a dense GEMM: double while all split items still fit
