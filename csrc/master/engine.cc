@@ -54,7 +54,79 @@ Engine::Engine(Config cfg, std::shared_ptr<Backend> backend)
       ckpt_slots_(int32_t(cfg_.num_ckpt_slots), int32_t(cfg_.max_seqs)) {
   if (cfg_.prefix_caching)
     tree_ = std::make_unique<kv::PrefixTree>(cfg_.page_size, cfg_.pages_per_node, cfg_.kv_hash_seed);
+  // The DRAM tier keeps one page per block and no recurrent checkpoint, so it needs
+  // APC nodes of one page and a model whose whole state is in the paged KV.
+  if (cfg_.dram_blocks > 0 && tree_ && cfg_.pages_per_node == 1 && !cfg_.recurrent_state)
+    dram_ = std::make_unique<kv::DramTier>(cfg_.dram_blocks, cfg_.page_size, cfg_.num_pages - 1,
+                                           cfg_.dram_loading_area);
   for (int32_t s = int32_t(cfg_.max_seqs) - 1; s >= 0; --s) free_slots_.push_back(s);
+}
+
+void Engine::evict_pages(size_t n) {
+  if (!tree_ || n == 0) return;
+  auto victims = tree_->evict_lru(n);
+  if (!dram_ || victims.empty()) return;
+  // The victims' pages are back in the pool but nothing has been allocated since, so
+  // their contents are intact until the copies below run.
+  std::vector<kv::KvTransferOp> ops;
+  std::vector<kv::Hash> keys;
+  for (const auto& v : victims) {
+    if (v.pages.size() != 1) continue;
+    if (auto op = dram_->admit(v.hash, v.pages[0])) {
+      ops.push_back(*op);
+      keys.push_back(v.hash);
+    }
+  }
+  if (!ops.empty() && !transfer(ops))
+    for (const auto& k : keys) dram_->rollback(k);
+}
+
+bool Engine::transfer(const std::vector<kv::KvTransferOp>& ops) {
+  const size_t per = std::max<size_t>(1, cfg_.max_step_tokens);
+  for (size_t i = 0; i < ops.size(); i += per) {
+    StepPlan p;
+    p.opcode = wire::kOpKvTransfer;
+    p.query_start = {0};
+    for (size_t j = i; j < std::min(ops.size(), i + per); ++j) {
+      p.token_ids.push_back(ops[j].hbm_page);
+      p.positions.push_back(ops[j].dram_slot);
+      p.row_slot.push_back(ops[j].h2d ? 1 : 0);
+    }
+    StepResult r;
+    if (!backend_->execute(p, &r) || r.status != 0) {
+      error_ = "KV transfer failed: " + backend_->error();
+      return false;
+    }
+  }
+  return true;
+}
+
+void Engine::reload_from_dram(const std::vector<int32_t>& key, kv::PrefixLease& lease) {
+  if (!dram_ || !tree_) return;
+  const uint32_t ps = cfg_.page_size;
+  const size_t first = lease.matched_nodes();
+  if ((first + 1) * ps > key.size()) return;
+  const auto hashes = kv::compute_block_hashes(key, ps, cfg_.kv_hash_seed);
+  size_t n = std::min(dram_->continuation(hashes, first), pages_.available());
+  if (n == 0) return;
+  auto got = pages_.allocate(n);
+  if (!got) return;
+  const auto slots = dram_->take(hashes, first, n);
+  std::vector<kv::KvTransferOp> ops;
+  for (size_t j = 0; j < slots.size(); ++j) ops.push_back(kv::KvTransferOp{got->ids()[j], slots[j], true});
+  const bool ok = transfer(ops);
+  dram_->release(slots);
+  if (!ok) return;  // the pages return to the pool; the blocks are recomputed instead
+  uint64_t parent = lease.leaf_node();
+  for (size_t j = 0; j < slots.size(); ++j) {
+    kv::BlockLease page = got->take_front(1);
+    kv::BlockLease aux;
+    const uint64_t id = tree_->insert(parent, key.data() + (first + j) * ps, page, aux);
+    if (id == 0) break;
+    parent = id;
+  }
+  lease.release();
+  lease = tree_->match(key);
 }
 
 Engine::~Engine() = default;
@@ -103,6 +175,15 @@ EngineStats Engine::stats() const {
     s.prefix_hit_tokens = t.hit_tokens;
     s.prefix_evictions = t.evictions;
   }
+  if (dram_) {
+    const auto d = dram_->stats();
+    s.dram_capacity = d.capacity_blocks;
+    s.dram_occupied = d.occupied_blocks;
+    s.dram_offloads = d.offloads;
+    s.dram_reloads = d.reloads;
+    s.dram_evictions = d.evictions;
+    s.dram_hit_tokens = d.hit_tokens;
+  }
   return s;
 }
 
@@ -142,11 +223,14 @@ bool Engine::admit_one() {
     std::vector<int32_t> key(r.prompt.begin(), r.prompt.end() - 1);
     lease = tree_->match(key);
     if (cfg_.recurrent_state && lease.matched_nodes() > 0 && lease.leaf_aux() < 0) lease.release();
+    if (dram_) reload_from_dram(key, lease);
   }
   const uint32_t matched_pages = uint32_t(lease.pages().size());
   const uint32_t own_needed = total_pages > matched_pages ? total_pages - matched_pages : 0;
-  if (pages_.available() < own_needed && tree_) tree_->evict_lru(own_needed - pages_.available());
-  if (pages_.available() < own_needed) return false;  // wait for running requests to finish
+  // With the DRAM tier, keep its loading area free (unless nothing else could run).
+  const size_t reserve = dram_ && !running_.empty() ? dram_->loading_area_pages() : 0;
+  if (pages_.available() < own_needed + reserve && tree_) evict_pages(own_needed + reserve - pages_.available());
+  if (pages_.available() < own_needed + reserve) return false;  // wait for running requests to finish
   auto own = pages_.allocate(own_needed);
   auto seq = make_seq(std::move(r));
   waiting_since_.erase(seq->req.id);
@@ -277,7 +361,7 @@ void Engine::stage(StepPlan& p, std::vector<Seq*>& order) {
         if (cfg_.recurrent_state) {
           auto a = ckpt_slots_.allocate(1);
           if (!a) {
-            tree_->evict_lru(1);
+            evict_pages(1);
             a = ckpt_slots_.allocate(1);
           }
           if (!a) break;  // no checkpoint slot: stop promoting this sequence

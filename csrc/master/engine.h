@@ -30,6 +30,7 @@
 #include <string>
 #include <vector>
 
+#include "dram_tier.h"
 #include "kv.h"
 #include "wire.h"
 
@@ -88,6 +89,9 @@ struct Config {
   uint32_t num_spec_tokens = 0;
   uint32_t ngram_n = 3;
   std::string kv_hash_seed = "42";
+  uint32_t dram_blocks = 0;            // host DRAM tier blocks (0: off); needs APC, 1 page per node,
+                                       // and a model without recurrent state
+  double dram_loading_area = 0.10;     // share of HBM pages kept free for DRAM reloads
 };
 
 // Host-side staged step (the coordinator copies it into a shared-memory plan slot).
@@ -125,6 +129,9 @@ struct EngineStats {
   uint64_t spec_drafts = 0, spec_accepted = 0, spec_verify_rows = 0;
   uint64_t spec_verify_steps = 0;  // sequence-level verify steps (one per sequence per step)
   uint64_t last_gpu_us = 0;
+  // Host DRAM tier of the prefix cache (zero when off).
+  uint64_t dram_capacity = 0, dram_occupied = 0, dram_offloads = 0, dram_reloads = 0, dram_evictions = 0;
+  uint64_t dram_hit_tokens = 0;
 };
 
 class Engine {
@@ -156,12 +163,19 @@ class Engine {
   void finish(Seq* s, Finish why, std::vector<TokenEvent>* out);
   void retire(Seq* s);
   std::vector<int32_t> ngram_drafts(const Seq& s) const;
+  // Evict LRU prefix leaves until n pages were freed, demoting them to the DRAM tier.
+  void evict_pages(size_t n);
+  // Run page copies between HBM and the DRAM tier as KvTransfer steps.
+  bool transfer(const std::vector<kv::KvTransferOp>& ops);
+  // Extend `lease` (the HBM match of `key`) with DRAM-resident continuation blocks.
+  void reload_from_dram(const std::vector<int32_t>& key, kv::PrefixLease& lease);
 
   Config cfg_;
   std::shared_ptr<Backend> backend_;
   kv::BlockPool pages_;
   kv::BlockPool ckpt_slots_;
   std::unique_ptr<kv::PrefixTree> tree_;
+  std::unique_ptr<kv::DramTier> dram_;
   std::deque<Request> waiting_;
   std::map<uint64_t, uint64_t> waiting_since_;  // request id -> step when queued
   std::vector<int32_t> free_slots_;

@@ -507,6 +507,14 @@ std::string HttpServer::render_metrics(serve::ServeLoop* loop, const ServerConfi
     gauge("spec_decode_mean_acceptance_length", "Mean tokens per verify step (accepted + bonus).",
           st.spec_verify_steps ? 1.0 + (double)st.spec_accepted / (double)st.spec_verify_steps : 0.0);
   }
+  if (st.dram_capacity > 0) {
+    gauge("dram_kv_capacity_blocks", "Host DRAM prefix-cache tier capacity.", (double)st.dram_capacity);
+    gauge("dram_kv_occupied_blocks", "Blocks resident in the host DRAM tier.", (double)st.dram_occupied);
+    counter("dram_kv_offloads_total", "Blocks demoted from HBM to host DRAM.", (double)st.dram_offloads);
+    counter("dram_kv_reloads_total", "Blocks reloaded from host DRAM into HBM.", (double)st.dram_reloads);
+    counter("dram_kv_evictions_total", "Blocks dropped from the full host DRAM tier.", (double)st.dram_evictions);
+    counter("dram_kv_hit_tokens_total", "Prompt tokens served from the host DRAM tier.", (double)st.dram_hit_tokens);
+  }
   hist("time_to_first_token_seconds", "Time to first token.", m.ttft);
   hist("time_per_output_token_seconds", "Time per output token after the first.", m.tpot);
   hist("e2e_request_latency_seconds", "End-to-end request latency.", m.e2e);

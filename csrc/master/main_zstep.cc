@@ -66,6 +66,9 @@ const char* kServeUsage =
     "  --enable-prefix-caching | --no-enable-prefix-caching   (default on)\n"
     "  --apc-node-pages N           Pages per prefix-cache node (default 8)\n"
     "  --num-ckpt-slots N           Recurrent-state checkpoint slots (default 64 with APC)\n"
+    "  --dram-kv-blocks N           Host DRAM tier of the prefix cache, in blocks (default 0 = off;\n"
+    "                               attention-only models; implies --apc-node-pages 1)\n"
+    "  --dram-loading-area-ratio R  Share of HBM pages kept free for DRAM reloads (default 0.10)\n"
     "  --max-waiting-requests N     Bounded waiting queue (default 1024)\n"
     "  --prefill-policy srpt|fifo   (default srpt)\n"
     "  --drain-timeout-secs N       SIGTERM drain grace period (default 30)\n"
@@ -116,10 +119,24 @@ struct Args {
 const std::set<std::string> kValueFlags = {
     "model-dir", "model", "served-model-name", "host", "port", "api-key", "admin-port", "world-size", "device",
     "max-model-len", "max-seqs", "max-step-tokens", "max-prefill-chunk", "page-block-tokens", "num-kv-pages",
-    "tokenizer-mode", "apc-node-pages", "num-ckpt-slots", "max-waiting-requests", "prefill-policy",
+    "tokenizer-mode", "apc-node-pages", "num-ckpt-slots", "dram-kv-blocks", "dram-loading-area-ratio", "max-waiting-requests", "prefill-policy",
     "drain-timeout-secs", "python", "worker-root", "ready-timeout-secs", "step-timeout-secs", "speculative-method",
     "num-speculative-tokens", "prompt-ids", "prompt", "max-tokens", "verify-greedy-json", "bench-tiers",
     "bench-repeats", "seed", "kv-events-endpoint", "kv-events-topic"};
+// Model families without per-slot recurrent state: DeepSeek-style presets, or an HF
+// directory whose config.json has MLA fields.
+bool attention_only_model(const std::string& model) {
+  if (model.rfind("deepseek", 0) == 0) return true;
+  FILE* f = fopen((model + "/config.json").c_str(), "rb");
+  if (!f) return false;
+  std::string text;
+  char buf[4096];
+  size_t n;
+  while ((n = fread(buf, 1, sizeof(buf), f)) > 0) text.append(buf, n);
+  fclose(f);
+  return text.find("\"kv_lora_rank\"") != std::string::npos;
+}
+
 const std::set<std::string> kBoolFlags = {"allow-remote-metrics", "no-allow-remote-metrics", "enable-prefix-caching",
                                           "no-enable-prefix-caching", "mock", "help"};
 
@@ -211,9 +228,22 @@ bool build_engine(const Args& a, Built* b, std::string* err) {
   c.num_pages = (uint32_t)a.num("num-kv-pages", 32768);
   c.max_model_len = (uint32_t)a.num("max-model-len", 32768);
   c.prefix_caching = !a.has("no-enable-prefix-caching");
-  c.pages_per_node = (uint32_t)a.num("apc-node-pages", 8);
-  c.recurrent_state = true;
-  c.num_ckpt_slots = (uint32_t)a.num("num-ckpt-slots", c.prefix_caching ? 64 : 0);
+  c.dram_blocks = (uint32_t)a.num("dram-kv-blocks", 0);
+  c.pages_per_node = (uint32_t)a.num("apc-node-pages", c.dram_blocks ? 1 : 8);
+  // Attention-only models (the DeepSeek-style family) keep no per-slot recurrent state.
+  c.recurrent_state = !attention_only_model(a.get("model", dir));
+  c.num_ckpt_slots = (uint32_t)a.num("num-ckpt-slots", c.prefix_caching && c.recurrent_state ? 64 : 0);
+  if (a.has("dram-loading-area-ratio")) c.dram_loading_area = strtod(a.get("dram-loading-area-ratio").c_str(), nullptr);
+  if (c.dram_blocks > 0) {
+    if (!c.prefix_caching || c.pages_per_node != 1 || c.recurrent_state) {
+      *err = "--dram-kv-blocks needs prefix caching, --apc-node-pages 1 and an attention-only model";
+      return false;
+    }
+    if (!(c.dram_loading_area > 0.0) || c.dram_loading_area > 0.5) {
+      *err = "--dram-loading-area-ratio must be in (0, 0.5]";
+      return false;
+    }
+  }
   c.prefill_policy = a.get("prefill-policy", "srpt");
   c.max_waiting = (uint32_t)a.num("max-waiting-requests", 1024);
   c.spec_method = a.get("speculative-method", "none");
@@ -269,7 +299,9 @@ bool build_engine(const Args& a, Built* b, std::string* err) {
                       "--spec-method",
                       c.spec_method,
                       "--num-spec-tokens",
-                      std::to_string(c.num_spec_tokens)};
+                      std::to_string(c.num_spec_tokens),
+                      "--dram-kv-blocks",
+                      std::to_string(c.dram_blocks)};
     const std::string root = a.get("worker-root", self_root());
     const char* pp = getenv("PYTHONPATH");
     cc.env["PYTHONPATH"] = root + (pp ? std::string(":") + pp : std::string());

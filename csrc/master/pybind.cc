@@ -260,7 +260,9 @@ PYBIND11_MODULE(_master, m) {
       .def_readwrite("spec_method", &engine::Config::spec_method)
       .def_readwrite("num_spec_tokens", &engine::Config::num_spec_tokens)
       .def_readwrite("ngram_n", &engine::Config::ngram_n)
-      .def_readwrite("kv_hash_seed", &engine::Config::kv_hash_seed);
+      .def_readwrite("kv_hash_seed", &engine::Config::kv_hash_seed)
+      .def_readwrite("dram_blocks", &engine::Config::dram_blocks)
+      .def_readwrite("dram_loading_area", &engine::Config::dram_loading_area);
   py::class_<engine::EngineStats>(m, "EngineStats")
       .def_readonly("waiting", &engine::EngineStats::waiting)
       .def_readonly("running", &engine::EngineStats::running)
@@ -275,7 +277,13 @@ PYBIND11_MODULE(_master, m) {
       .def_readonly("prefix_evictions", &engine::EngineStats::prefix_evictions)
       .def_readonly("spec_drafts", &engine::EngineStats::spec_drafts)
       .def_readonly("spec_accepted", &engine::EngineStats::spec_accepted)
-      .def_readonly("spec_verify_steps", &engine::EngineStats::spec_verify_steps);
+      .def_readonly("spec_verify_steps", &engine::EngineStats::spec_verify_steps)
+      .def_readonly("dram_capacity", &engine::EngineStats::dram_capacity)
+      .def_readonly("dram_occupied", &engine::EngineStats::dram_occupied)
+      .def_readonly("dram_offloads", &engine::EngineStats::dram_offloads)
+      .def_readonly("dram_reloads", &engine::EngineStats::dram_reloads)
+      .def_readonly("dram_evictions", &engine::EngineStats::dram_evictions)
+      .def_readonly("dram_hit_tokens", &engine::EngineStats::dram_hit_tokens);
   py::class_<engine::Engine, std::shared_ptr<engine::Engine>>(m, "Engine")
       .def(py::init([](engine::Config cfg, py::function backend) {
              return std::make_shared<engine::Engine>(cfg, std::make_shared<PyBackend>(backend));

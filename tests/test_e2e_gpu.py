@@ -53,3 +53,28 @@ def test_bench_tier_with_mtp_and_shared_prefix(model_dir):
     run0 = rep["tiers"][0]["runs"][0]
     assert run0["output_tok_s"] > 0 and run0["shared_prefix_len"] == 64
     assert run0["mean_acceptance_length"] >= 1.0
+
+
+def test_deepseek_dram_tier_keeps_greedy_tokens(model_dir, tmp_path):
+    """DeepSeek-style model on a B200 worker with a host DRAM tier and a small HBM page
+    pool: prefixes are demoted and reloaded between requests, and the generated tokens
+    equal a run without prefix caching."""
+    fam = [list(range(300, 364)), list(range(900, 964))]
+    prompts = [fam[k % 2] + [50 + 7 * k + j for j in range(8)] for k in range(6)]
+    path = tmp_path / "p.json"
+    path.write_text(json.dumps({"prompts": prompts}))  # no expectations: --max-tokens each
+    base = ["--model", "deepseek-small", "--max-seqs", "1", "--max-tokens", "8"]
+
+    def run(*extra):
+        args = [BIN, "run", "--model-dir", model_dir, "--device", "cuda", "--max-model-len", "256",
+                "--max-step-tokens", "256", "--max-prefill-chunk", "128", "--python", sys.executable,
+                "--worker-root", ROOT, "--verify-greedy-json", str(path), *base, *extra]
+        r = subprocess.run(args, capture_output=True, text=True, timeout=900)
+        return json.loads(r.stdout.strip().splitlines()[-1]), r
+
+    ref, r0 = run("--no-enable-prefix-caching", "--num-kv-pages", "64")
+    assert "verify_greedy" in ref, r0.stderr[-3000:]
+    want = [e["tokens"] for e in ref["verify_greedy"]]
+    path.write_text(json.dumps({"prompts": prompts, "expected": want}))
+    got, r1 = run("--num-kv-pages", "16", "--dram-kv-blocks", "32")
+    assert got.get("mismatches") == 0, (got, r1.stderr[-3000:])

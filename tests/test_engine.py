@@ -225,3 +225,84 @@ def test_overload_rejects_submit():
     eng = m.Engine(cfg, FakeBackend())
     assert eng.submit(1, [1], 1) and eng.submit(2, [1], 1)
     assert not eng.submit(3, [1], 1)
+
+
+class PagedFakeBackend:
+    """Fake model over a modelled paged KV: every row writes its token into the page the
+    plan's page table names; the next token is f(tokens read back from the pages for
+    positions 0..p).  Prefix reuse and DRAM demotion / reload are right only if the
+    engine's page bookkeeping and the KvTransfer copies are."""
+
+    def __init__(self, page_size):
+        self.ps = page_size
+        self.pages = {}
+        self.dram = {}
+        self.table = {}
+        self.transfers = []
+
+    def _history(self, slot, upto):
+        h = []
+        for pos in range(upto):
+            page = self.table[slot][pos // self.ps]
+            h.append(self.pages[page][pos % self.ps])
+        return h
+
+    def __call__(self, p):
+        if p["opcode"] == 3:  # KvTransfer: token_ids = pages, positions = DRAM slots, row_slot = direction
+            for page, slot, up in zip(p["token_ids"], p["positions"], p["row_slot"]):
+                self.transfers.append((page, slot, up))
+                if up:
+                    self.pages[page] = list(self.dram[slot])
+                else:
+                    self.dram[slot] = list(self.pages[page])
+            return []
+        for row, pages in zip(p["dirty_rows"], p["dirty_pages"]):
+            self.table[row] = list(pages)
+        outs = []
+        qs = p["query_start"]
+        for i, slot in enumerate(p["seq_slot"]):
+            r0, r1 = qs[i], qs[i + 1]
+            for r in range(r0, r1):
+                pos = p["positions"][r]
+                page = self.table[slot][pos // self.ps]
+                self.pages.setdefault(page, [None] * self.ps)[pos % self.ps] = p["token_ids"][r]
+            if p["sample_row"][i] < 0:
+                outs.append({"tokens": []})
+                continue
+            last = p["positions"][r1 - 1]
+            outs.append({"tokens": [f(self._history(slot, last + 1))]})
+        return outs
+
+
+@pytest.mark.parametrize("dram", [0, 48])
+def test_dram_tier_demotes_and_reloads_prefixes(dram):
+    cfg = m.EngineConfig()
+    cfg.max_seqs = 1
+    cfg.max_step_tokens = 64
+    cfg.max_prefill_chunk = 32
+    cfg.page_size = 4
+    cfg.num_pages = 21       # 20 usable pages: each request needs most of them
+    cfg.max_model_len = 128
+    cfg.prefix_caching = True
+    cfg.pages_per_node = 1
+    cfg.recurrent_state = False
+    cfg.dram_blocks = dram
+    be = PagedFakeBackend(4)
+    eng = m.Engine(cfg, be)
+    # Two families of prompts with long shared prefixes; alternating them evicts each
+    # family's prefix from HBM before it is needed again.
+    fam = [[(7 * i + 3) % V for i in range(40)], [(11 * i + 5) % V for i in range(40)]]
+    prompts = [fam[k % 2] + [(k * 13 + j) % V for j in range(5)] for k in range(6)]
+    for rid, pr in enumerate(prompts):
+        assert eng.submit(rid, pr, 6)
+    out, done = run(eng)
+    assert done == set(range(6)) and not eng.poisoned(), eng.error()
+    for rid, pr in enumerate(prompts):
+        assert out[rid] == expected(pr, 6), rid
+    st = eng.stats()
+    if dram:
+        assert st.dram_offloads > 0 and st.dram_reloads > 0 and st.dram_hit_tokens > 0
+        assert any(up for _, _, up in be.transfers) and any(not up for _, _, up in be.transfers)
+        assert st.prefix_hit_tokens > 0
+    else:
+        assert st.dram_capacity == 0 and not be.transfers

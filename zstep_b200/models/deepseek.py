@@ -372,6 +372,10 @@ class DeepSeekRunner:
             self._advance(rows, nxt)
         self._site(rows, self.hc_head, self.final_norm, mix_out=False)
 
+    def paged_caches(self) -> list[torch.Tensor]:
+        """Device tensors indexed [layer, page, ...]: what a host DRAM tier slot holds."""
+        return [self.ckv_cache, self.ik_cache]
+
     def copy_recurrent_state(self, src_slot: int, dst_slot: int) -> None:
         """No recurrent state: every cached quantity lives in the paged latent / index caches."""
 

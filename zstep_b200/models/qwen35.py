@@ -559,6 +559,10 @@ class Qwen35Runner:
         """Host->device bytes moved by the last stage() call."""
         return 4 * 4 * getattr(self, "_staged_rows", 0)
 
+    def paged_caches(self) -> list[torch.Tensor]:
+        """Device tensors indexed [layer, page, ...] (the attention layers' K and V)."""
+        return [self.k_cache, self.v_cache]
+
     def copy_recurrent_state(self, src_slot: int, dst_slot: int) -> None:
         """Restore a checkpoint: GDN state and both conv-window buffers of every layer."""
         self.ssm_state[:, dst_slot].copy_(self.ssm_state[:, src_slot])

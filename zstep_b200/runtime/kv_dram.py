@@ -1,0 +1,49 @@
+"""Host DRAM tier of the KV cache on a worker: a pinned host arena of demoted pages.
+
+One arena slot holds one device page of every paged cache tensor of the model (all
+layers), e.g. the latent and index-key caches of the DeepSeek-style model.  The master
+sends KvTransfer steps (page, slot, direction); D2H gathers the pages' rows on the device
+and lands them in the pinned slots, H2D scatters slots back into pages.  Copies run on
+the runner's stream, so a following step sees reloaded pages and a demoted page is read
+before any later step can overwrite it.  The arena is allocated after the worker pinned
+itself to its GPU's NUMA node, so its host pages are local to that GPU's root complex.
+
+Reference parity: worker/zstep_worker/kv_dram_tier.py:38 (HostDramKvTier),
+:157 (execute_transfers).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+
+class DramKvArena:
+    def __init__(self, caches: list[torch.Tensor], num_blocks: int):
+        """caches: device tensors [layers, pages, ...] (page is dim 1)."""
+        self.caches = caches
+        self.num_blocks = num_blocks
+        self.host = [torch.empty((num_blocks, c.shape[0]) + tuple(c.shape[2:]), dtype=c.dtype, pin_memory=True)
+                     for c in caches]
+        self.bytes_per_block = sum(h[0].numel() * h.element_size() for h in self.host)
+        self.d2h_blocks = 0
+        self.h2d_blocks = 0
+
+    def transfer(self, pages: np.ndarray, slots: np.ndarray, h2d: np.ndarray) -> None:
+        pages = np.asarray(pages, dtype=np.int64)
+        slots = np.asarray(slots, dtype=np.int64)
+        h2d = np.asarray(h2d).astype(bool)
+        if len(slots) and (slots.min() < 0 or slots.max() >= self.num_blocks):
+            raise ValueError(f"DRAM slot out of range (arena has {self.num_blocks} blocks)")
+        down, up = ~h2d, h2d
+        for c, host in zip(self.caches, self.host):
+            if down.any():
+                p = torch.from_numpy(pages[down]).to(c.device)
+                staged = c[:, p].transpose(0, 1).contiguous().cpu()
+                host[torch.from_numpy(slots[down])] = staged
+            if up.any():
+                p = torch.from_numpy(pages[up]).to(c.device)
+                staged = host[torch.from_numpy(slots[up])].pin_memory().to(c.device, non_blocking=True)
+                c[:, p] = staged.transpose(0, 1)
+        self.d2h_blocks += int(down.sum())
+        self.h2d_blocks += int(up.sum())

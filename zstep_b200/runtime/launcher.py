@@ -35,7 +35,7 @@ def launch(*, model: str = "qwen3.5-tiny", world_size: int = 1, device: str = "c
            max_seqs: int = 8, max_step_tokens: int = 512, page_size: int = 16, num_pages: int = 1024,
            max_model_len: int = 2048, num_ckpt_slots: int = 0, vocab_size: int = 0, engine: dict | None = None,
            ready_timeout_ms: int = 600000, step_timeout_ms: int = 300000, heartbeat_timeout_ms: int = 10000,
-           extra_env: dict | None = None):
+           extra_env: dict | None = None, dram_kv_blocks: int = 0):
     """Returns (engine, coordinator).  Call ``coordinator.shutdown()`` when done."""
     geo = _master.Geometry()
     geo.world_size = world_size
@@ -49,7 +49,7 @@ def launch(*, model: str = "qwen3.5-tiny", world_size: int = 1, device: str = "c
                          **(engine or {}))
     argv = [sys.executable, "-m", "zstep_b200.runtime.worker", "--model", model, "--device", device, "--seed",
             str(seed), "--num-pages", str(num_pages), "--max-model-len", str(max_model_len), "--num-ckpt-slots",
-            str(num_ckpt_slots)]
+            str(num_ckpt_slots), "--dram-kv-blocks", str(dram_kv_blocks)]
     root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     env = {"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(free_port()),
            "PYTHONPATH": root + os.pathsep + python_path()}

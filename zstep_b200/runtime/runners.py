@@ -106,6 +106,8 @@ class CpuReferenceRunner:
         return torch.cat(parts)
 
     def execute(self, plan: dict) -> np.ndarray:
+        if plan["opcode"] == wire.OP_KV_TRANSFER:
+            raise RuntimeError("the fp32 reference runner keeps unpaged per-slot state: no DRAM tier")
         n = plan["num_seqs"]
         out = _outputs(n)
         qs, toks, pos = plan["query_start"], plan["token_ids"], plan["positions"]
@@ -175,10 +177,20 @@ class GpuRunner:
                               num_ckpt_slots=args.num_ckpt_slots, tp_rank=rank, tp_size=world, collectives=coll,
                               seed=args.seed, num_spec_tokens=num_spec)
         self.rank = rank
+        self.dram = None
+        if getattr(args, "dram_kv_blocks", 0):
+            from .kv_dram import DramKvArena
+
+            self.dram = DramKvArena(self.r.paged_caches(), args.dram_kv_blocks)
 
     def execute(self, plan: dict) -> np.ndarray:
         r = self.r
         n = plan["num_seqs"]
+        if plan["opcode"] == wire.OP_KV_TRANSFER:
+            if self.dram is None:
+                raise RuntimeError("KvTransfer step without a DRAM arena (--dram-kv-blocks 0)")
+            self.dram.transfer(plan["token_ids"], plan["positions"], plan["row_slot"])
+            return _outputs(0)
         out = _outputs(n)
         for k, slot in enumerate(plan["dirty_rows"]):
             r.page_table[int(slot)].copy_(torch.from_numpy(plan["dirty_pages"][k][: r.max_pages]).to(r.dev))

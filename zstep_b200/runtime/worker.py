@@ -152,6 +152,7 @@ def parse_args(argv=None):
     ap.add_argument("--num-ckpt-slots", type=int, default=0)
     ap.add_argument("--spec-method", default="none")
     ap.add_argument("--num-spec-tokens", type=int, default=0)
+    ap.add_argument("--dram-kv-blocks", type=int, default=0, help="host DRAM tier blocks (pinned page arena)")
     ap.add_argument("--shm-fd", type=int, required=True)
     ap.add_argument("--shm-bytes", type=int, required=True)
     ap.add_argument("--plan-fd", type=int, required=True)
