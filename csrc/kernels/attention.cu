@@ -42,6 +42,8 @@ __device__ __forceinline__ size_t kv_offset(const AttnArgs& a, int page, int kvh
 
 // One CTA per row; one warp per head (q heads then k heads then v heads); lane owns 8 dims.
 __global__ void prologue_kernel(const AttnArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   const int row = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nh = a.num_q_heads + a.num_kv_heads;
@@ -153,6 +155,8 @@ __device__ __forceinline__ void load_row_piece(const __nv_bfloat16* row, int li,
 }
 
 __global__ void __launch_bounds__(256) decode_partial_kernel(const AttnArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   extern __shared__ __align__(128) uint8_t dec_smem_raw[];
   DecSmem& s = *reinterpret_cast<DecSmem*>((reinterpret_cast<uintptr_t>(dec_smem_raw) + 127) & ~uintptr_t(127));
   const int row = blockIdx.x;
@@ -294,6 +298,8 @@ __global__ void __launch_bounds__(256) decode_partial_kernel(const AttnArgs a) {
 // One CTA (256 threads, thread = dim) per (row, q head): merge splits, normalise,
 // apply sigmoid(gate), write bf16 and/or MXFP8.
 __global__ void decode_combine_kernel(const AttnArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   const int row = blockIdx.x, qh = blockIdx.y, d = threadIdx.x;
   const float* rec = a.partial + ((size_t)row * a.num_q_heads + qh) * a.num_splits * PREC;
   float m = -INFINITY;
@@ -330,7 +336,7 @@ extern "C" int zs_attn_prologue(const AttnArgs* args, cudaStream_t stream) {
   const AttnArgs& a = *args;
   if (a.head_dim != zs::attn::D || a.rotary_dim % 16 != 0 || a.rotary_dim > a.head_dim) return -1;
   if (a.rows == 0) return 0;
-  zs::attn::prologue_kernel<<<a.rows, 256, 0, stream>>>(a);
+  zs_launch(zs::attn::prologue_kernel, a.rows, 256, 0, stream, a);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
@@ -343,9 +349,9 @@ extern "C" int zs_attn_decode(const AttnArgs* args, cudaStream_t stream) {
   dim3 g1(a.rows, a.num_kv_heads, a.num_splits);
   const size_t smem = sizeof(zs::attn::DecSmem) + 128;
   cudaFuncSetAttribute(zs::attn::decode_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  zs::attn::decode_partial_kernel<<<g1, group * 32, smem, stream>>>(a);
+  zs_launch(zs::attn::decode_partial_kernel, g1, group * 32, smem, stream, a);
   dim3 g2(a.rows, a.num_q_heads);
-  zs::attn::decode_combine_kernel<<<g2, zs::attn::D, 0, stream>>>(a);
+  zs_launch(zs::attn::decode_combine_kernel, g2, zs::attn::D, 0, stream, a);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

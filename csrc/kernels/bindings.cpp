@@ -650,6 +650,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("y") = py::none(), py::arg("mix_prev") = py::none(), py::arg("ids") = py::none(),
         py::arg("embed") = py::none(), py::arg("partial"));
   m.def("mhc_slices", &zs_mhc_slices);
+  m.def("set_pdl", [](bool on) { zs_set_pdl(on ? 1 : 0); });
+  m.def("pdl_enabled", []() { return zs_pdl_enabled() != 0; });
   m.def("mhc_finalize", &mhc_finalize, py::arg("x"), py::arg("rows"), py::arg("hidden"), py::arg("partial"),
         py::arg("base"), py::arg("scale"), py::arg("eps"), py::arg("iters"), py::arg("mix_out"), py::arg("weight"),
         py::arg("q"), py::arg("sf"));

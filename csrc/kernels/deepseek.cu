@@ -82,6 +82,8 @@ ZS_DEVICE void quant8_store(const float (&v)[8], bool active, int row, int col, 
 template <int M>
 __global__ void __launch_bounds__(256)
 mhc_partial_kernel(MhcPartialArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   const int t0 = blockIdx.x * kPartTok;
   const int c0 = blockIdx.y * kPartCols;
   const int H = a.hidden;
@@ -171,6 +173,8 @@ mhc_partial_kernel(MhcPartialArgs a) {
 template <int M>
 __global__ void __launch_bounds__(256)
 mhc_finalize_kernel(MhcFinalizeArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   const int t = blockIdx.x;
   const int H = a.hidden;
   __shared__ float mix[M + 1];
@@ -264,6 +268,8 @@ mhc_finalize_kernel(MhcFinalizeArgs a) {
 __global__ void __launch_bounds__(256)
 rms_quant_kernel(const __nv_bfloat16* __restrict__ x, int ld_x, int width, const __nv_bfloat16* __restrict__ w,
                  float eps, uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   __shared__ float red[32];
   const int t = blockIdx.x;
   constexpr int kMaxPass = 4;
@@ -309,6 +315,8 @@ rms_quant_kernel(const __nv_bfloat16* __restrict__ x, int ld_x, int width, const
 // queries, and the scaled index-head weights.
 __global__ void __launch_bounds__(256)
 mla_prologue_kernel(MlaPrologueArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   __shared__ float red[32];
   const int t = blockIdx.x;
   const int pos = a.pos[t];
@@ -404,6 +412,8 @@ __global__ void __launch_bounds__(256)
 mla_absorb_q_kernel(const __nv_bfloat16* __restrict__ qi, int ld_qi, int qk_dim, int nope,
                     const __nv_bfloat16* __restrict__ w_uk, int kl, int heads, int rows,
                     __nv_bfloat16* __restrict__ q_lat) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   const int h = blockIdx.x;
   const int t0 = blockIdx.y * kAbsTok;
   __shared__ float qs[kAbsTok][128];
@@ -450,6 +460,8 @@ constexpr int kQPad = kLat + kRope + 4;    // floats per staged query row
 
 __global__ void __launch_bounds__(256)
 mla_attn_kernel(MlaAttnArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   float* qs = reinterpret_cast<float*>(smem_raw);                                   // [heads][kQPad]
   __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(qs + a.heads * kQPad);        // [kAttnKeys][kRowPad]
@@ -567,6 +579,8 @@ mla_attn_kernel(MlaAttnArgs a) {
 constexpr int kUpTok = 2;
 __global__ void __launch_bounds__(128)
 mla_up_kernel(MlaUpArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   const int h = blockIdx.x;
   const int t0 = blockIdx.y * kUpTok;
   const int HL = a.heads, S = a.splits, V = a.v_dim;
@@ -656,6 +670,8 @@ ZS_DEVICE uint32_t sw128_off(int r, int p, int rows) {
 template <int IH>
 __global__ void __launch_bounds__(128)
 dsa_scores_tc_kernel(DsaScoresArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   const int t = blockIdx.x;
   const int ctx = a.ctx_len[t];
   const int s_begin = blockIdx.y * kTcKeys * kTcTiles;
@@ -771,6 +787,8 @@ ZS_DEVICE uint32_t ord_key(float f) {
 
 __global__ void __launch_bounds__(1024)
 dsa_topk_kernel(DsaTopkArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   const int t = blockIdx.x;
   const int ctx = a.ctx_len[t];
   const int K = a.topk;
@@ -858,6 +876,8 @@ dsa_topk_kernel(DsaTopkArgs a) {
 __global__ void __launch_bounds__(256)
 gather_sum_kernel(const __nv_bfloat16* __restrict__ rows_in, const int* __restrict__ src,
                   const float* __restrict__ w, int k1, int hidden, float* __restrict__ y) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   const int t = blockIdx.x;
   for (int c = threadIdx.x * 8; c < hidden; c += blockDim.x * 8) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -890,8 +910,8 @@ int zs_mhc_partial(const MhcPartialArgs* a, cudaStream_t stream) {
   if (a->rows <= 0) return 0;
   if (a->hidden % 8 != 0 || (a->m != ds::kHcM && a->m != ds::kHcN)) return -2;
   dim3 grid((a->rows + ds::kPartTok - 1) / ds::kPartTok, (a->hidden + ds::kPartCols - 1) / ds::kPartCols);
-  if (a->m == ds::kHcM) ds::mhc_partial_kernel<ds::kHcM><<<grid, 256, 0, stream>>>(*a);
-  else ds::mhc_partial_kernel<ds::kHcN><<<grid, 256, 0, stream>>>(*a);
+  if (a->m == ds::kHcM) zs_launch(ds::mhc_partial_kernel<ds::kHcM>, grid, 256, 0, stream, *a);
+  else zs_launch(ds::mhc_partial_kernel<ds::kHcN>, grid, 256, 0, stream, *a);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -900,8 +920,8 @@ int zs_mhc_slices(int hidden) { return (hidden + ds::kPartCols - 1) / ds::kPartC
 int zs_mhc_finalize(const MhcFinalizeArgs* a, cudaStream_t stream) {
   if (a->rows <= 0) return 0;
   if (a->hidden % 32 != 0 || a->hidden > 8192) return -2;
-  if (a->m == ds::kHcM) ds::mhc_finalize_kernel<ds::kHcM><<<a->rows, 256, 0, stream>>>(*a);
-  else if (a->m == ds::kHcN) ds::mhc_finalize_kernel<ds::kHcN><<<a->rows, 256, 0, stream>>>(*a);
+  if (a->m == ds::kHcM) zs_launch(ds::mhc_finalize_kernel<ds::kHcM>, a->rows, 256, 0, stream, *a);
+  else if (a->m == ds::kHcN) zs_launch(ds::mhc_finalize_kernel<ds::kHcN>, a->rows, 256, 0, stream, *a);
   else return -2;
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
@@ -910,7 +930,7 @@ int zs_rms_quant(const void* x, int ld_x, int width, const void* w, float eps, i
                  cudaStream_t stream) {
   if (rows <= 0) return 0;
   if (width % 32 != 0 || width > 8192 || ld_x % 8 != 0) return -2;
-  ds::rms_quant_kernel<<<rows, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), ld_x, width,
+  zs_launch(ds::rms_quant_kernel, rows, 256, 0, stream, static_cast<const __nv_bfloat16*>(x), ld_x, width,
                                                  static_cast<const __nv_bfloat16*>(w), eps, q, sf);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
@@ -918,7 +938,7 @@ int zs_rms_quant(const void* x, int ld_x, int width, const void* w, float eps, i
 int zs_mla_prologue(const MlaPrologueArgs* a, cudaStream_t stream) {
   if (a->rows <= 0) return 0;
   if (a->kv_lora > 512 || a->index_dim > 256 || a->rope > 2 * 256 || a->rope % 2 != 0) return -2;
-  ds::mla_prologue_kernel<<<a->rows, 256, 0, stream>>>(*a);
+  zs_launch(ds::mla_prologue_kernel, a->rows, 256, 0, stream, *a);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -927,7 +947,7 @@ int zs_mla_absorb_q(const void* qi, int ld_qi, int qk_dim, int nope, const void*
   if (rows <= 0) return 0;
   if (nope > 128 || kl > 512 || kl % 2 != 0) return -2;
   dim3 grid(heads, (rows + ds::kAbsTok - 1) / ds::kAbsTok);
-  ds::mla_absorb_q_kernel<<<grid, 256, 0, stream>>>(
+  zs_launch(ds::mla_absorb_q_kernel, grid, 256, 0, stream,
       static_cast<const __nv_bfloat16*>(qi), ld_qi, qk_dim, nope, static_cast<const __nv_bfloat16*>(w_uk), kl, heads,
       rows, static_cast<__nv_bfloat16*>(q_lat));
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
@@ -949,7 +969,7 @@ int zs_mla_attn(const MlaAttnArgs* a, cudaStream_t stream) {
     attr_set = true;
   }
   dim3 grid(a->rows, a->splits);
-  ds::mla_attn_kernel<<<grid, 256, smem, stream>>>(*a);
+  zs_launch(ds::mla_attn_kernel, grid, 256, smem, stream, *a);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -957,7 +977,7 @@ int zs_mla_up(const MlaUpArgs* a, cudaStream_t stream) {
   if (a->rows <= 0) return 0;
   if (a->v_dim != 128 || a->splits > 64 || (a->heads * a->v_dim) % 128 != 0) return -2;
   dim3 grid(a->heads, (a->rows + ds::kUpTok - 1) / ds::kUpTok);
-  ds::mla_up_kernel<<<grid, 128, 0, stream>>>(*a);
+  zs_launch(ds::mla_up_kernel, grid, 128, 0, stream, *a);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -969,7 +989,7 @@ int zs_dsa_scores(const DsaScoresArgs* a, int max_ctx, cudaStream_t stream) {
   dim3 grid(a->rows, (max_ctx + ds::kTcKeys * ds::kTcTiles - 1) / (ds::kTcKeys * ds::kTcTiles));
   auto launch = [&](auto kern) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<grid, 128, smem, stream>>>(*a);
+    zs_launch(kern, grid, 128, smem, stream, *a);
   };
   if (ih == 16) launch(ds::dsa_scores_tc_kernel<16>);
   else if (ih == 32) launch(ds::dsa_scores_tc_kernel<32>);
@@ -980,7 +1000,7 @@ int zs_dsa_scores(const DsaScoresArgs* a, int max_ctx, cudaStream_t stream) {
 
 int zs_dsa_topk(const DsaTopkArgs* a, cudaStream_t stream) {
   if (a->rows <= 0) return 0;
-  ds::dsa_topk_kernel<<<a->rows, 1024, 0, stream>>>(*a);
+  zs_launch(ds::dsa_topk_kernel, a->rows, 1024, 0, stream, *a);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
@@ -988,6 +1008,6 @@ int zs_gather_sum(const void* rows_in, const int* src, const float* w, int k1, i
                   cudaStream_t stream) {
   if (rows <= 0) return 0;
   if (hidden % 8 != 0) return -2;
-  ds::gather_sum_kernel<<<rows, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(rows_in), src, w, k1, hidden, y);
+  zs_launch(ds::gather_sum_kernel, rows, 256, 0, stream, static_cast<const __nv_bfloat16*>(rows_in), src, w, k1, hidden, y);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }

@@ -204,6 +204,8 @@ __device__ __forceinline__ float delta_step(float (&st)[32], int vr, int kq, con
 }
 
 __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_kernel(const GdnArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   __shared__ Smem s;
   const int seq = blockIdx.x;
   const int vh = blockIdx.y;
@@ -271,6 +273,6 @@ extern "C" int zs_gdn_prefill(const GdnArgs* args, cudaStream_t stream) {
     return -1;
   if (a.num_seqs == 0) return 0;
   dim3 grid(a.num_seqs, a.num_v_heads);
-  zs::gdn::gdn_prefill_kernel<<<grid, zs::gdn::THREADS, 0, stream>>>(a);
+  zs_launch(zs::gdn::gdn_prefill_kernel, grid, zs::gdn::THREADS, 0, stream, a);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }

@@ -106,6 +106,8 @@ __device__ __forceinline__ void store_stage(const GdnArgs& a, Stage& st, const I
 }
 
 __global__ void __launch_bounds__(THREADS, 1) gdn_decode_tma_kernel(const GdnArgs a, int total_items) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   extern __shared__ __align__(128) uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -314,6 +316,6 @@ extern "C" int zs_gdn_decode(const GdnArgs* args, cudaStream_t stream) {
   const int grid = items < sms ? items : sms;
   const size_t smem = sizeof(Smem) + 128;
   cudaFuncSetAttribute(gdn_decode_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  gdn_decode_tma_kernel<<<grid, THREADS, smem, stream>>>(a, items);
+  zs_launch(gdn_decode_tma_kernel, grid, THREADS, smem, stream, a, items);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }

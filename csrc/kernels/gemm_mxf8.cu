@@ -202,6 +202,8 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES, FP4>::THREADS, 1)
 gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
                  const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_b_full,
                  const GemmMxf8Args p) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   using C = Cfg<BN, STAGES, FP4>;
   using Smem = typename C::Smem;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -690,7 +692,7 @@ int launch(const GemmMxf8Args& p, const CUtensorMap& ta, const CUtensorMap& tb, 
   const size_t smem = sizeof(typename CF::Smem) + 1024;
   auto kern = gemm_mxf8_kernel<BN, STAGES, FP4>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  kern<<<grid, CF::THREADS, smem, stream>>>(ta, tb, tbf, p);
+  zs_launch(kern, grid, CF::THREADS, smem, stream, ta, tb, tbf, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -15;
 }
 

@@ -50,6 +50,8 @@ __device__ __forceinline__ float logit(const MoeRouteArgs& a, int row, int col) 
 // compile-time constant so scores, selection keys and the chosen top-k stay in registers.
 template <int PER>
 __global__ void route_topk_kernel(const MoeRouteArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= a.rows) return;
@@ -185,6 +187,8 @@ __global__ void route_topk_kernel(const MoeRouteArgs a) {
 }
 
 __global__ void offsets_kernel(const MoeRouteArgs a, int groups) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   // Single CTA of 1024 threads (one group each, groups <= 1024): exclusive scans of the
   // 128-aligned segment sizes and of the per-group chunk counts, warp scans + one
   // warp over the 32 warp totals.
@@ -234,6 +238,8 @@ __global__ void offsets_kernel(const MoeRouteArgs a, int groups) {
 
 // One warp per (row, pair): copy hidden bytes + hidden/32 scale bytes.
 __global__ void scatter_kernel(const MoeRouteArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   const int K1 = a.top_k + 1;
   const int pair = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -290,19 +296,19 @@ extern "C" int zs_moe_route(const MoeRouteArgs* args, cudaStream_t stream) {
   if (groups > 1024) return -1;
   if (cudaMemsetAsync(a.group_count, 0, sizeof(int) * groups, stream) != cudaSuccess) return -2;
   if (a.rows == 0) {
-    zs::moe::offsets_kernel<<<1, 1024, 0, stream>>>(a, groups);
+    zs_launch(zs::moe::offsets_kernel, 1, 1024, 0, stream, a, groups);
     return cudaGetLastError() == cudaSuccess ? 0 : -2;
   }
   int wpb = 8;
   {
     const dim3 grid((a.rows + 1) / 2), block(64);  // 2 rows per block: more SMs busy
-    if (a.num_experts <= 64) zs::moe::route_topk_kernel<2><<<grid, block, 0, stream>>>(a);
-    else if (a.num_experts <= 128) zs::moe::route_topk_kernel<4><<<grid, block, 0, stream>>>(a);
-    else if (a.num_experts <= 256) zs::moe::route_topk_kernel<8><<<grid, block, 0, stream>>>(a);
-    else zs::moe::route_topk_kernel<16><<<grid, block, 0, stream>>>(a);
+    if (a.num_experts <= 64) zs_launch(zs::moe::route_topk_kernel<2>, grid, block, 0, stream, a);
+    else if (a.num_experts <= 128) zs_launch(zs::moe::route_topk_kernel<4>, grid, block, 0, stream, a);
+    else if (a.num_experts <= 256) zs_launch(zs::moe::route_topk_kernel<8>, grid, block, 0, stream, a);
+    else zs_launch(zs::moe::route_topk_kernel<16>, grid, block, 0, stream, a);
   }
-  zs::moe::offsets_kernel<<<1, 1024, 0, stream>>>(a, groups);
+  zs_launch(zs::moe::offsets_kernel, 1, 1024, 0, stream, a, groups);
   const int pairs = a.rows * (a.top_k + 1);
-  zs::moe::scatter_kernel<<<(pairs + wpb - 1) / wpb, wpb * 32, 0, stream>>>(a);
+  zs_launch(zs::moe::scatter_kernel, (pairs + wpb - 1) / wpb, wpb * 32, 0, stream, a);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }

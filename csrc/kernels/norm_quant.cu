@@ -14,6 +14,8 @@ namespace zs {
 // One thread per 32-element block: 64 B in, 32 B + 1 scale byte out.
 __global__ void quant_mxf8_kernel(const __nv_bfloat16* __restrict__ x, int rows, int k, int ld_x,
                                   uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   const int blocks_per_row = k / 32;
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (gid >= (long long)rows * blocks_per_row) return;
@@ -66,6 +68,8 @@ add_rmsnorm_quant_kernel(__nv_bfloat16* __restrict__ residual, const void* __res
                          const __nv_bfloat16* __restrict__ weight, float w_offset, float eps,
                          int hidden, __nv_bfloat16* __restrict__ normed, uint8_t* __restrict__ q,
                          uint8_t* __restrict__ sf) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
   const int iters = hidden / (kNormThreads * 8);
@@ -204,6 +208,8 @@ add_rmsnorm_quant_kernel(__nv_bfloat16* __restrict__ residual, const void* __res
 
 __global__ void argmax_reduce_kernel(const unsigned long long* __restrict__ keys, int rows, int tiles,
                                      int* out_ids, float* out_vals, unsigned long long* out_keys) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -226,6 +232,11 @@ __global__ void argmax_reduce_kernel(const unsigned long long* __restrict__ keys
 
 }  // namespace zs
 
+// Programmatic dependent launch switch (see sm100_common.cuh); the runtime config sets it.
+static int g_pdl = 1;
+extern "C" void zs_set_pdl(int on) { g_pdl = on ? 1 : 0; }
+extern "C" int zs_pdl_enabled() { return g_pdl; }
+
 extern "C" int zs_quant_mxf8(const void* x, int rows, int k, int ld_x, uint8_t* q, uint8_t* sf,
                              cudaStream_t stream) {
   if (k % 128 != 0 || rows < 0) return -1;
@@ -233,7 +244,7 @@ extern "C" int zs_quant_mxf8(const void* x, int rows, int k, int ld_x, uint8_t* 
   const long long total = (long long)rows * (k / 32);
   const int threads = 256;
   const long long grid = (total + threads - 1) / threads;
-  zs::quant_mxf8_kernel<<<(unsigned)grid, threads, 0, stream>>>(
+  zs_launch(zs::quant_mxf8_kernel, (unsigned)grid, threads, 0, stream,
       static_cast<const __nv_bfloat16*>(x), rows, k, ld_x, q, sf);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
@@ -247,7 +258,7 @@ extern "C" int zs_add_rmsnorm_quant(void* residual, const void* delta, int n_ter
   if (hidden % (zs::kNormThreads * 8) != 0 || hidden > zs::kNormThreads * 8 * zs::kNormMaxIter)
     return -1;
   if (rows == 0) return 0;
-  zs::add_rmsnorm_quant_kernel<false><<<rows, zs::kNormThreads, 0, stream>>>(
+  zs_launch(zs::add_rmsnorm_quant_kernel<false>, rows, zs::kNormThreads, 0, stream,
       static_cast<__nv_bfloat16*>(residual), delta, n_terms, d_row_stride, d_term_stride, delta_f32,
       term_index, term_scale, nullptr, nullptr, static_cast<const __nv_bfloat16*>(weight),
       w_offset, eps, hidden, static_cast<__nv_bfloat16*>(normed), q, sf);
@@ -262,7 +273,7 @@ extern "C" int zs_embed_rmsnorm_quant(const int* ids, const void* embed, void* h
       hidden_size > zs::kNormThreads * 8 * zs::kNormMaxIter)
     return -1;
   if (rows == 0) return 0;
-  zs::add_rmsnorm_quant_kernel<true><<<rows, zs::kNormThreads, 0, stream>>>(
+  zs_launch(zs::add_rmsnorm_quant_kernel<true>, rows, zs::kNormThreads, 0, stream,
       static_cast<__nv_bfloat16*>(hidden), nullptr, 0, 0, 0, 0, nullptr, nullptr, ids,
       static_cast<const __nv_bfloat16*>(embed), static_cast<const __nv_bfloat16*>(weight),
       w_offset, eps, hidden_size, static_cast<__nv_bfloat16*>(normed), q, sf);
@@ -273,7 +284,7 @@ extern "C" int zs_argmax_reduce(const unsigned long long* keys, int rows, int ti
                                 float* out_vals, unsigned long long* out_keys, cudaStream_t stream) {
   if (rows == 0) return 0;
   const int warps = 8;
-  zs::argmax_reduce_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, stream>>>(
+  zs_launch(zs::argmax_reduce_kernel, (rows + warps - 1) / warps, warps * 32, 0, stream,
       keys, rows, tiles, out_ids, out_vals, out_keys);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }

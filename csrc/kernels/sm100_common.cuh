@@ -14,6 +14,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #define ZS_DEVICE __device__ __forceinline__
 
 namespace zs {
@@ -361,4 +363,34 @@ ZS_DEVICE int sf_atom_offset(int row_in_atom, int kblk_in_atom) {
   return (row_in_atom & 31) * 16 + (row_in_atom >> 5) * 4 + kblk_in_atom;
 }
 
+// ---------------------------------------------------------------------------------
+// Programmatic dependent launch.  Kernels started by zs_launch may begin while the
+// previous kernel of the stream is still running (its CTAs free SMs one by one), so the
+// launch, the CTA ramp and a kernel's local set-up overlap the predecessor's tail.  Every
+// such kernel calls pdl_wait() before it touches global memory that an earlier kernel
+// writes or reads, and pdl_trigger() to let its own successor launch early.  Both are
+// no-ops for a kernel launched without the attribute.
+// ---------------------------------------------------------------------------------
+ZS_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+ZS_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace zs
+
+// Host switch (zs_set_pdl) and the launcher used by every kernel that waits with pdl_wait.
+extern "C" int zs_pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t zs_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                             Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = zs_pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}

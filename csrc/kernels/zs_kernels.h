@@ -408,6 +408,10 @@ int zs_dsa_topk(const DsaTopkArgs* args, cudaStream_t stream);
 int zs_gather_sum(const void* rows_in, const int* src, const float* w, int k1, int hidden, int rows, float* y,
                   cudaStream_t stream);
 
+// Programmatic dependent launch of the compute kernels (on by default).
+void zs_set_pdl(int on);
+int zs_pdl_enabled();
+
 int zs_symm_alloc(size_t bytes, void** ptr);
 int zs_symm_free(void* ptr);
 int zs_ipc_handle(void* ptr, void* handle_out);

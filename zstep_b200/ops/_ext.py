@@ -24,7 +24,11 @@ def load():
     with _lock:
         if _mod is None:
             try:
-                _mod = importlib.import_module("zstep_b200._C")
+                mod = importlib.import_module("zstep_b200._C")
+                from ..utils.env import runtime_config
+
+                mod.set_pdl(runtime_config().pdl)
+                _mod = mod
             except BaseException as e:  # noqa: BLE001 - re-raised with context below
                 _err = e
                 raise RuntimeError(

@@ -55,6 +55,7 @@ class RuntimeConfig:
     coll_timeout_ms: int = 5000           # ZSTEP_COLL_TIMEOUT_MS: bound on cross-rank waits
     gemm_fix_splits: bool = False         # ZSTEP_GEMM_FIX_SPLITS: in-kernel split-K for small GEMMs
     decode_graphs: bool = True            # ZSTEP_DECODE_GRAPHS: CUDA-graph decode buckets
+    pdl: bool = True                      # ZSTEP_PDL: programmatic dependent launch of the kernels
     spec_method: str = "none"             # ZSTEP_SPEC_METHOD: none | ngram | mtp
     num_spec_tokens: int = 0              # ZSTEP_NUM_SPEC_TOKENS: 0..7
     num_recurrent_checkpoints: int = 0    # ZSTEP_NUM_RECURRENT_CHECKPOINTS
@@ -68,6 +69,7 @@ class RuntimeConfig:
         "ZSTEP_COLL_TIMEOUT_MS": ("coll_timeout_ms", lambda n, r: _int(n, r, 1, 600000)),
         "ZSTEP_GEMM_FIX_SPLITS": ("gemm_fix_splits", _bool),
         "ZSTEP_DECODE_GRAPHS": ("decode_graphs", _bool),
+        "ZSTEP_PDL": ("pdl", _bool),
         "ZSTEP_SPEC_METHOD": ("spec_method", lambda n, r: _choice(n, r, ("none", "ngram", "mtp"))),
         "ZSTEP_NUM_SPEC_TOKENS": ("num_spec_tokens", lambda n, r: _int(n, r, 0, 7)),
         "ZSTEP_NUM_RECURRENT_CHECKPOINTS": ("num_recurrent_checkpoints", lambda n, r: _int(n, r, 0, 1 << 20)),
