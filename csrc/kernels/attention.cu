@@ -295,6 +295,287 @@ __global__ void __launch_bounds__(256) decode_partial_kernel(const AttnArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------------
+// Tensor-core split-KV decode (tcgen05).  One CTA of 4 warps per (row, kv head, split);
+// the split's keys go through 128-key tiles (8 pages):
+//   * TMA copies each (page, 64-dim chunk) box of K and V into a K-major 128-byte
+//     swizzled tile image: chunk c holds the tile's 128 key rows of dims 64c..64c+63.
+//   * S^T = K Q^T: one thread issues 16 tcgen05.mma (kind::f16 bf16, M = 128 keys,
+//     N = 16 query-head slots of the GQA group, K = 16 dims each) into TMEM columns 0-15.
+//   * Online softmax in the exp2 domain: thread t owns key t (TMEM lane t); per-head
+//     maxima and sums reduce through shared memory; P = exp2(S - m) is stored bf16 as
+//     the [16 heads x 128 keys] K-major operand of the second product, and O is rescaled
+//     in TMEM (tcgen05.ld / st) by exp2(m_old - m_new).
+//   * O^T += V^T P^T: the V tile image read as an MN-major operand (M = 128 head dims per
+//     MMA: 64-dim chunks LBO = 16 KiB apart, 8-key groups SBO = 1 KiB apart), N = 16,
+//     K = 16 keys per MMA, accumulated in TMEM columns 16-47.
+// K is reloaded as soon as S is in TMEM; V images are double-buffered and requested two
+// tiles ahead, so both copies overlap the dependent chain of a tile.  Output
+// records (o, m, l) have the layout of the SIMT kernel, so the same combine kernel runs.
+constexpr int TC_KEYS = 128;
+constexpr int TC_PAGES = TC_KEYS / PAGE;
+constexpr int TC_N = 16;
+constexpr int TC_NCHUNK = D / 64;
+constexpr int TC_CHUNK_BYTES = TC_KEYS * 128;
+constexpr int TC_TILE_BYTES = TC_NCHUNK * TC_CHUNK_BYTES;
+constexpr int TC_THREADS = 128;
+
+struct TcSmem {
+  uint8_t k[TC_TILE_BYTES];           // K tile image (reloaded as soon as S is computed)
+  uint8_t v[2][TC_TILE_BYTES];        // double-buffered V tile images (prefetched two tiles ahead)
+  uint8_t q[TC_NCHUNK][TC_N * 128];   // Q: [16 slots][256] K-major, slots >= group are zero
+  uint8_t p[2][TC_N * 128];           // P: [16 slots][128 keys] K-major, 2 chunks of 64 keys
+  float red_max[4][TC_N];
+  float red_sum[4][TC_N];
+  float m[TC_N], l[TC_N], r[TC_N];
+  uint64_t kfull, vfull[2], mma1, mma2;
+  uint32_t tmem_base;
+};
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+decode_partial_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
+                         const AttnArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
+  extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
+  TcSmem& s = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+  const int row = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = a.num_q_heads / a.num_kv_heads;
+  const int ctx = a.seq_lens[row];
+  const int pages = (ctx + PAGE - 1) / PAGE;
+  const int pps = (pages + a.num_splits - 1) / a.num_splits;
+  const int p0 = split * pps;
+  const int p1 = min(pages, p0 + pps);
+  const int npg = max(0, p1 - p0);
+  const int ntiles = (npg + TC_PAGES - 1) / TC_PAGES;
+  const int tok_end = min(ctx, p1 * PAGE);
+  const int* pt = a.page_table + (size_t)a.slots[row] * a.max_pages;
+  const float qscale = a.sm_scale * 1.4426950408889634f;  // exp2 domain
+
+  if (warp == 0) {
+    tmem_alloc(&s.tmem_base, 64);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&s.kfull, 1);
+    mbar_init(&s.vfull[0], 1);
+    mbar_init(&s.vfull[1], 1);
+    mbar_init(&s.mma1, 1);
+    mbar_init(&s.mma2, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+  }
+  if (tid < TC_N) {
+    s.m[tid] = -INFINITY;
+    s.l[tid] = 0.f;
+  }
+  // Q slots of this kv head's GQA group (rows >= G stay zero).
+  const __nv_bfloat16* qsrc = static_cast<const __nv_bfloat16*>(a.q_out) + ((size_t)row * a.num_q_heads + kvh * G) * D;
+  for (int i = tid; i < TC_N * 32; i += TC_THREADS) {
+    const int h = i >> 5, pc = i & 31, c = pc >> 3, piece = pc & 7;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (h < G) v = *reinterpret_cast<const uint4*>(qsrc + (size_t)h * D + pc * 8);
+    *reinterpret_cast<uint4*>(s.q[c] + h * 128 + ((piece ^ (h & 7)) << 4)) = v;
+  }
+  fence_proxy_async_shared();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const uint32_t t_s = tmem, t_o = tmem + 16;
+
+  // Producer state (thread 0 only): loads issued but not yet observed, per barrier.
+  int k_pend = 0, v_pend[2] = {0, 0};
+  int k_uses = 0, v_uses[2] = {0, 0};
+  auto issue = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* bar, int tile) {
+    const int pg0 = p0 + tile * TC_PAGES;
+    const int n = min(TC_PAGES, p1 - pg0);
+    mbar_expect_tx(bar, n * TC_NCHUNK * PAGE * 128);
+    for (int j = 0; j < n; ++j) {
+      const int y = (__ldg(pt + pg0 + j) * a.num_kv_heads + kvh) * PAGE;
+      for (int c = 0; c < TC_NCHUNK; ++c) tma_load_2d(dst + c * TC_CHUNK_BYTES + j * PAGE * 128, map, bar, c * 64, y);
+    }
+  };
+  if (tid == 0 && ntiles > 0) {
+    issue(&tk, s.k, &s.kfull, 0);
+    k_pend = 1;
+    for (int j = 0; j < 2 && j < ntiles; ++j) {
+      issue(&tv, s.v[j], &s.vfull[j], j);
+      v_pend[j] = 1;
+    }
+  }
+  bool ok = true;
+  for (int t = 0; t < ntiles; ++t) {
+    const int vb = t & 1;
+    const int pg0 = p0 + t * TC_PAGES;
+    const int n = min(TC_PAGES, p1 - pg0);
+    if (n < TC_PAGES) {
+      // Last, partial tile: zero the rows of the absent pages in both images (no copy
+      // targets them), so the products see finite values there.
+      const int per_chunk = (TC_PAGES - n) * PAGE * 8;  // 16-byte pieces per chunk
+      for (int i = tid; i < per_chunk * TC_NCHUNK; i += TC_THREADS) {
+        const int off = (i / per_chunk) * TC_CHUNK_BYTES + n * PAGE * 128 + (i % per_chunk) * 16;
+        *reinterpret_cast<uint4*>(s.k + off) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(s.v[vb] + off) = make_uint4(0, 0, 0, 0);
+      }
+      fence_proxy_async_shared();
+    }
+    ok = mbar_wait(&s.kfull, (uint32_t)(k_uses & 1), a.err);
+    if (!__syncthreads_and(ok)) break;
+    if (tid == 0) {
+      k_pend = 0;
+      tc_fence_after();
+      const uint32_t idesc = make_idesc_bf16(TC_KEYS, TC_N, 0, 0);
+#pragma unroll
+      for (int c = 0; c < TC_NCHUNK; ++c)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t ad = make_smem_desc(smem_u32(s.k + c * TC_CHUNK_BYTES) + k * 32, 16, 1024, 2);
+          const uint64_t bd = make_smem_desc(smem_u32(s.q[c]) + k * 32, 16, 1024, 2);
+          mma_bf16(t_s, ad, bd, idesc, (c | k) ? 1u : 0u);
+        }
+      tc_commit(&s.mma1);
+    }
+    ++k_uses;
+    ok = mbar_wait(&s.mma1, (uint32_t)(t & 1), a.err);
+    if (!__syncthreads_and(ok)) break;
+    tc_fence_after();
+    // S is in TMEM: the K image is free, so the next tile's K copy overlaps the rest of
+    // this tile (softmax, rescale, second product).
+    if (tid == 0 && t + 1 < ntiles) {
+      issue(&tk, s.k, &s.kfull, t + 1);
+      k_pend = 1;
+    }
+    // ---- online softmax: thread tid owns key tid of the tile
+    uint32_t sr[16];
+    tmem_ld_32x32b_x16(t_s + lane_off, sr);
+    tmem_ld_wait();
+    const int tok = pg0 * PAGE + tid;
+    const bool valid = tok < tok_end;
+    float sv[TC_N];
+#pragma unroll
+    for (int h = 0; h < TC_N; ++h) sv[h] = (valid && h < G) ? __uint_as_float(sr[h]) * qscale : -INFINITY;
+#pragma unroll
+    for (int h = 0; h < TC_N; ++h) {
+      const float v = warp_max(sv[h]);
+      if (lane == 0) s.red_max[warp][h] = v;
+    }
+    __syncthreads();
+    float mnew[TC_N];
+#pragma unroll
+    for (int h = 0; h < TC_N; ++h)
+      mnew[h] = fmaxf(fmaxf(s.m[h], fmaxf(s.red_max[0][h], s.red_max[1][h])), fmaxf(s.red_max[2][h], s.red_max[3][h]));
+    {
+      const int chunk = tid >> 6, within = tid & 63, piece = within >> 3, sub = (within & 7) * 2;
+#pragma unroll
+      for (int h = 0; h < TC_N; ++h) {
+        const float pv = sv[h] == -INFINITY ? 0.f : exp2f(sv[h] - mnew[h]);
+        const __nv_bfloat16 pb = __float2bfloat16_rn(pv);
+        *reinterpret_cast<__nv_bfloat16*>(s.p[chunk] + h * 128 + ((piece ^ (h & 7)) << 4) + sub) = pb;
+        const float sum = warp_sum(__bfloat162float(pb));
+        if (lane == 0) s.red_sum[warp][h] = sum;
+      }
+    }
+    fence_proxy_async_shared();
+    __syncthreads();
+    if (tid < TC_N) {
+      const int h = tid;
+      const float mo = s.m[h];
+      const float rr = mo == -INFINITY ? 0.f : exp2f(mo - mnew[h]);
+      s.l[h] = s.l[h] * rr + (s.red_sum[0][h] + s.red_sum[1][h] + s.red_sum[2][h] + s.red_sum[3][h]);
+      s.m[h] = mnew[h];
+      s.r[h] = rr;
+    }
+    __syncthreads();
+    if (t > 0) {  // rescale the running O^T (TMEM lane = head dim, column = head slot)
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        uint32_t o[16];
+        tmem_ld_32x32b_x16(t_o + mt * 16 + lane_off, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int h = 0; h < 16; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * s.r[h]);
+        tmem_st_32x32b_x16(t_o + mt * 16 + lane_off, o);
+      }
+      tmem_st_wait();
+    }
+    ok = mbar_wait(&s.vfull[vb], (uint32_t)(v_uses[vb] & 1), a.err);
+    if (ok && !valid && tok < (pg0 + n) * PAGE) {
+      // Cache rows past the context inside a loaded page: zero them (P is 0 there).
+#pragma unroll
+      for (int c = 0; c < TC_NCHUNK; ++c) {
+        uint4* rowp = reinterpret_cast<uint4*>(s.v[vb] + c * TC_CHUNK_BYTES + tid * 128);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) rowp[j] = make_uint4(0, 0, 0, 0);
+      }
+      fence_proxy_async_shared();
+    }
+    tc_fence_before();
+    if (!__syncthreads_and(ok)) break;
+    if (tid == 0) {
+      v_pend[vb] = 0;
+      tc_fence_after();
+      const uint32_t idesc2 = make_idesc_bf16(128, TC_N, 1, 0);
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint64_t ad =
+              make_smem_desc(smem_u32(s.v[vb] + 2 * mt * TC_CHUNK_BYTES) + ks * 2048, TC_CHUNK_BYTES, 1024, 2);
+          const uint64_t bd = make_smem_desc(smem_u32(s.p[ks >> 2]) + (ks & 3) * 32, 16, 1024, 2);
+          mma_bf16(t_o + mt * 16, ad, bd, idesc2, (t > 0 || ks > 0) ? 1u : 0u);
+        }
+      tc_commit(&s.mma2);
+    }
+    ++v_uses[vb];
+    ok = mbar_wait(&s.mma2, (uint32_t)(t & 1), a.err);
+    if (!__syncthreads_and(ok)) break;
+    tc_fence_after();
+    if (tid == 0 && t + 2 < ntiles) {  // this V image is free: the tile after next
+      issue(&tv, s.v[vb], &s.vfull[vb], t + 2);
+      v_pend[vb] = 1;
+    }
+  }
+  if (ok) {
+    const int h_lim = G < TC_N ? G : TC_N;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      uint32_t o[16];
+      if (ntiles > 0) {
+        tmem_ld_32x32b_x16(t_o + mt * 16 + lane_off, o);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int h = 0; h < 16; ++h) o[h] = 0u;
+      }
+      const int dim = mt * 128 + tid;
+#pragma unroll
+      for (int h = 0; h < 16; ++h) {
+        if (h >= h_lim) break;
+        a.partial[(((size_t)row * a.num_q_heads + kvh * G + h) * a.num_splits + split) * PREC + dim] =
+            __uint_as_float(o[h]);
+      }
+    }
+    if (tid < h_lim) {
+      float* rec = a.partial + (((size_t)row * a.num_q_heads + kvh * G + tid) * a.num_splits + split) * PREC;
+      rec[D] = s.m[tid];
+      rec[D + 1] = s.l[tid];
+    }
+  } else if (tid == 0) {
+    // Abort: let every copy still in flight land before the CTA releases shared memory.
+    if (k_pend) mbar_wait(&s.kfull, (uint32_t)(k_uses & 1), nullptr);
+    for (int b = 0; b < 2; ++b)
+      if (v_pend[b]) mbar_wait(&s.vfull[b], (uint32_t)(v_uses[b] & 1), nullptr);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 64);
+}
+
 // One CTA (256 threads, thread = dim) per (row, q head): merge splits, normalise,
 // apply sigmoid(gate), write bf16 and/or MXFP8.
 __global__ void decode_combine_kernel(const AttnArgs a) {
@@ -340,13 +621,62 @@ extern "C" int zs_attn_prologue(const AttnArgs* args, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// A paged K or V cache [pages, kv_heads, 16, 256] bf16 as a 2-D tensor of 256-dim rows;
+// one box is 16 rows (one page of one kv head) x 64 dims, 128-byte swizzled.
+int make_cache_map(CUtensorMap* m, void* base, long long rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return -1;
+  cuuint64_t dims[2] = {(cuuint64_t)zs::attn::D, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)zs::attn::D * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)zs::attn::PAGE};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+}  // namespace
+
 extern "C" int zs_attn_decode(const AttnArgs* args, cudaStream_t stream) {
   const AttnArgs& a = *args;
   if (a.head_dim != zs::attn::D || a.num_kv_heads <= 0 || a.num_q_heads % a.num_kv_heads != 0) return -1;
   const int group = a.num_q_heads / a.num_kv_heads;
-  if (group > 8 || a.num_splits < 1 || a.partial == nullptr || a.page_size != zs::attn::PAGE) return -1;
+  if (a.num_splits < 1 || a.partial == nullptr || a.page_size != zs::attn::PAGE) return -1;
   if (a.rows == 0) return 0;
   dim3 g1(a.rows, a.num_kv_heads, a.num_splits);
+  // Tensor cores pay off from 4 query heads per kv head; smaller groups (a GQA group
+  // split over many ranks) stay on the SIMT kernel, which runs one warp per head.
+  if (a.impl == 0 && group >= 4 && group <= zs::attn::TC_N && a.num_pages > 0) {
+    // Tensor-core path: TMA boxes of the paged caches (the maps cover all pages).
+    CUtensorMap tk, tv;
+    const long long rows = (long long)a.num_pages * a.num_kv_heads * zs::attn::PAGE;
+    if (make_cache_map(&tk, a.k_cache, rows) != 0 || make_cache_map(&tv, a.v_cache, rows) != 0) return -5;
+    const size_t smem = sizeof(zs::attn::TcSmem) + 1024;
+    cudaFuncSetAttribute(zs::attn::decode_partial_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    zs_launch(zs::attn::decode_partial_tc_kernel, g1, zs::attn::TC_THREADS, smem, stream, tk, tv, a);
+    dim3 g2(a.rows, a.num_q_heads);
+    zs_launch(zs::attn::decode_combine_kernel, g2, zs::attn::D, 0, stream, a);
+    return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  }
+  if (group > 8) return -1;
   const size_t smem = sizeof(zs::attn::DecSmem) + 128;
   cudaFuncSetAttribute(zs::attn::decode_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   zs_launch(zs::attn::decode_partial_kernel, g1, group * 32, smem, stream, a);

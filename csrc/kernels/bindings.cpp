@@ -263,9 +263,11 @@ void attn_decode(const Tensor& q_out, const Tensor& gate_out, int64_t num_q_head
                  int64_t num_kv_heads, const Tensor& k_cache, const Tensor& v_cache,
                  int64_t page_size, const Tensor& page_table, const Tensor& slots,
                  const Tensor& seq_lens, int64_t rows, const Tensor& partial, int64_t num_splits,
-                 double sm_scale, const OptT& out_bf16, const OptT& out_q, const OptT& out_sf) {
+                 double sm_scale, const OptT& out_bf16, const OptT& out_q, const OptT& out_sf, int64_t impl,
+                 const OptT& err) {
   check_cuda(q_out, "q_out");
   check_cuda(partial, "partial");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(2) == page_size, "k_cache must be [pages, kv_heads, page, 256]");
   TORCH_CHECK(partial.numel() >= rows * num_q_heads * num_splits * 260, "partial too small");
   AttnArgs a{};
   a.num_q_heads = (int)num_q_heads;
@@ -287,6 +289,9 @@ void attn_decode(const Tensor& q_out, const Tensor& gate_out, int64_t num_q_head
   a.out_bf16 = optptr(out_bf16);
   a.out_q = optptr<uint8_t>(out_q);
   a.out_sf = optptr<uint8_t>(out_sf);
+  a.num_pages = (int)k_cache.size(0);
+  a.impl = (int)impl;
+  a.err = optptr<int>(err);
   rc(zs_attn_decode(&a, stream()), "zs_attn_decode");
 }
 
@@ -723,7 +728,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
      py::arg("num_seqs"), py::arg("ckpt_rows"), py::arg("ckpt_slots"), py::arg("max_ckpt"), py::arg("err"),
      py::arg("out_slots") = py::none());
   m.def("attn_prologue", &attn_prologue);
-  m.def("attn_decode", &attn_decode);
+  m.def("attn_decode", &attn_decode, py::arg("q_out"), py::arg("gate_out"), py::arg("num_q_heads"),
+        py::arg("num_kv_heads"), py::arg("k_cache"), py::arg("v_cache"), py::arg("page_size"), py::arg("page_table"),
+        py::arg("slots"), py::arg("seq_lens"), py::arg("rows"), py::arg("partial"), py::arg("num_splits"),
+        py::arg("sm_scale"), py::arg("out_bf16"), py::arg("out_q"), py::arg("out_sf"), py::arg("impl") = 0,
+        py::arg("err") = py::none());
   m.def("moe_route", &moe_route, py::arg("logits"), py::arg("rows"), py::arg("num_experts"), py::arg("top_k"),
         py::arg("norm_topk"), py::arg("scoring"), py::arg("bias"), py::arg("n_group"), py::arg("topk_group"),
         py::arg("routed_scale"), py::arg("shared_gate_col"), py::arg("expert_begin"), py::arg("expert_end"),

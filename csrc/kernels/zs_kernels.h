@@ -177,6 +177,8 @@ typedef struct AttnArgs {
   const int* seq_start;    // [num_seqs+1]
   int num_seqs;
   int* err;
+  int num_pages;           // pages of k_cache / v_cache (the tensor-core path maps them all)
+  int impl;                // 0: tensor-core decode when supported (group <= 16), 1: SIMT decode
 } AttnArgs;
 
 int zs_attn_prologue(const AttnArgs* args, cudaStream_t stream);

@@ -609,6 +609,47 @@ def test_attention_prologue_and_decode(C):
         torch.testing.assert_close(out[r].cpu().float(), expect, rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("hq,hkv,splits", [(16, 2, 1), (16, 2, 3), (2, 1, 2), (16, 1, 1)])
+def test_attention_decode_tensor_core(C, hq, hkv, splits):
+    """The tcgen05 split-KV decode (128-key tiles, TMA page boxes, online softmax with
+    TMEM rescale) against the fp32 reference, over contexts that end mid-page, mid-tile,
+    on tile boundaries and inside one page; group sizes 8, 2 and 16."""
+    g = torch.Generator().manual_seed(7)
+    d, page = 256, 16
+    ctx = [1, 16, 37, 128, 129, 300, 511]
+    rows = len(ctx)
+    max_pages = 33
+    pages_total = rows * max_pages + 1
+    perm = torch.randperm(pages_total - 1, generator=g) + 1
+    table = perm.view(rows, max_pages).to(torch.int32)
+    kc = (torch.randn(pages_total, hkv, page, d, generator=g) * 0.5).to(torch.bfloat16)
+    vc = (torch.randn(pages_total, hkv, page, d, generator=g) * 0.5).to(torch.bfloat16)
+    q = torch.randn(rows, hq, d, generator=g).to(torch.bfloat16)
+    gate = torch.randn(rows, hq, d, generator=g).to(torch.bfloat16)
+    sm = 1 / math.sqrt(d)
+    dev = lambda t: t.cuda()  # noqa: E731
+    outs = {}
+    for impl in ((0, 1) if hq // hkv <= 8 else (0,)):
+        partial = torch.zeros(rows * hq * splits * 260, device="cuda")
+        out = torch.zeros(rows, hq * d, dtype=torch.bfloat16, device="cuda")
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        C.attn_decode(dev(q), dev(gate), hq, hkv, dev(kc), dev(vc), page, dev(table),
+                      torch.arange(rows, dtype=torch.int32, device="cuda"), torch.tensor(ctx, dtype=torch.int32).cuda(),
+                      rows, partial, splits, sm, out, None, None, impl=impl, err=err)
+        torch.cuda.synchronize()
+        assert err.item() == 0
+        outs[impl] = out.cpu().float()
+    grp = hq // hkv
+    for r in range(rows):
+        keys = torch.stack([kc[table[r, t // page], :, t % page].float() for t in range(ctx[r])])
+        vals = torch.stack([vc[table[r, t // page], :, t % page].float() for t in range(ctx[r])])
+        expect = ref.gated_attention(q[r].float(), gate[r].float(), keys, vals, sm)
+        torch.testing.assert_close(outs[0][r], expect, rtol=2e-2, atol=2e-2)
+    if 1 in outs:
+        torch.testing.assert_close(outs[0], outs[1], rtol=2e-2, atol=2e-2)
+    del grp
+
+
 def test_moe_route_softmax_shared(C):
     torch.manual_seed(0)
     rows, E, k, hidden = 50, 64, 4, 256
