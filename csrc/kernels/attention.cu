@@ -1,7 +1,10 @@
 // Gated GQA attention over a paged KV cache (Qwen3.5 full-attention layers).
 //
-// KV cache layout: [pages][kv_heads][page_size][head_dim] bf16, so the 16 tokens of one
-// (page, kv head) are one contiguous 8 KiB block that a single cp.async.bulk stages.
+// KV cache layout: [pages][kv_heads][16 tokens x 256 dims] bf16 blocks of 8 KiB, stored
+// pre-swizzled for the tensor cores: a block holds two halves of 8 tokens, each half four
+// 64-dim chunks of 8 rows x 128 B, and the 16-byte pieces of token row r sit at piece
+// index ^ (r % 8) (see swz()).  One cp.async.bulk copies a block into shared memory where
+// it is directly a K-major operand (8-row groups 4 KiB apart) or, for V, an MN-major one.
 //
 //  * prologue: per row, zero-centered RMSNorm of every q and k head ((1 + w) scale),
 //    partial rotary embedding (rotate-half over the first `rotary_dim` dims, cos/sin
@@ -36,8 +39,14 @@ constexpr int BLOCK_BYTES = PAGE * D * 2;  // one (page, kv head) block: 8 KiB
 
 __device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-__device__ __forceinline__ size_t kv_offset(const AttnArgs& a, int page, int kvh, int off) {
-  return (((size_t)page * a.num_kv_heads + kvh) * a.page_size + off) * D;
+// Element offset of the (page, kv head) block.
+__device__ __forceinline__ size_t kv_offset(const AttnArgs& a, int page, int kvh) {
+  return ((size_t)page * a.num_kv_heads + kvh) * PAGE * D;
+}
+
+// Element offset of (token row r, dims d..d+7) inside a block (d a multiple of 8).
+__device__ __forceinline__ int swz(int r, int d) {
+  return (r >> 3) * 2048 + (d >> 6) * 512 + (r & 7) * 64 + ((((d & 63) >> 3) ^ (r & 7)) << 3);
 }
 
 // One CTA per row; one warp per head (q heads then k heads then v heads); lane owns 8 dims.
@@ -57,7 +66,8 @@ __global__ void prologue_kernel(const AttnArgs a) {
       // V head: straight copy into the cache.
       const int kvh = h - nh;
       const uint4* src = reinterpret_cast<const uint4*>(qkv + a.num_q_heads * 2 * D + a.num_kv_heads * D + kvh * D);
-      reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.v_cache) + kv_offset(a, page, kvh, pos % a.page_size))[lane] =
+      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.v_cache) + kv_offset(a, page, kvh) +
+                                swz(pos % a.page_size, lane * 8)) =
           src[lane];
       continue;
     }
@@ -121,7 +131,8 @@ __global__ void prologue_kernel(const AttnArgs a) {
       reinterpret_cast<uint4*>(go)[lane] = reinterpret_cast<const uint4*>(src + D)[lane];
     } else {
       const int kvh = h - a.num_q_heads;
-      reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.k_cache) + kv_offset(a, page, kvh, pos % a.page_size))[lane] =
+      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.k_cache) + kv_offset(a, page, kvh) +
+                                swz(pos % a.page_size, lane * 8)) =
           pv;
     }
   }
@@ -144,6 +155,20 @@ __device__ __forceinline__ void load_row_piece(const __nv_bfloat16* row, int li,
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     const uint4 u = *reinterpret_cast<const uint4*>(row + c * 64 + li * 8);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 v = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(&u)[j]);
+      f[c * 8 + 2 * j] = v.x;
+      f[c * 8 + 2 * j + 1] = v.y;
+    }
+  }
+}
+
+// The same pieces of token row t of a swizzled (page, kv head) block.
+__device__ __forceinline__ void load_block_row_piece(const __nv_bfloat16* blk, int t, int li, float (&f)[32]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 u = *reinterpret_cast<const uint4*>(blk + swz(t, c * 64 + li * 8));
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -193,8 +218,8 @@ __global__ void __launch_bounds__(256) decode_partial_kernel(const AttnArgs a) {
     const int st = pi % RING;
     const int page = __ldg(pt + p0 + pi);
     mbar_expect_tx(&s.full[st], 2 * BLOCK_BYTES);
-    bulk_load(s.k[st], kc + kv_offset(a, page, kvh, 0), BLOCK_BYTES, &s.full[st]);
-    bulk_load(s.v[st], vc + kv_offset(a, page, kvh, 0), BLOCK_BYTES, &s.full[st]);
+    bulk_load(s.k[st], kc + kv_offset(a, page, kvh), BLOCK_BYTES, &s.full[st]);
+    bulk_load(s.v[st], vc + kv_offset(a, page, kvh), BLOCK_BYTES, &s.full[st]);
   };
   if (threadIdx.x == 0)
     for (int pi = 0; pi < min(RING, npg); ++pi) issue(pi);
@@ -226,7 +251,7 @@ __global__ void __launch_bounds__(256) decode_partial_kernel(const AttnArgs a) {
     for (int t = grp; t < PAGE; t += 4) {
       const bool valid = tok0 + t < ctx;
       float kf[32];
-      load_row_piece(s.k[st] + t * D, li, kf);
+      load_block_row_piece(s.k[st], t, li, kf);
       float sc = 0.f;
 #pragma unroll
       for (int j = 0; j < 32; ++j) sc += q[j] * kf[j];
@@ -235,7 +260,7 @@ __global__ void __launch_bounds__(256) decode_partial_kernel(const AttnArgs a) {
       sc += __shfl_xor_sync(0xffffffff, sc, 4);
       if (!valid) continue;
       float vf[32];
-      load_row_piece(s.v[st] + t * D, li, vf);
+      load_block_row_piece(s.v[st], t, li, vf);
       if (sc > m) {
         const float r = exp2f(m - sc);
         l *= r;
@@ -298,8 +323,9 @@ __global__ void __launch_bounds__(256) decode_partial_kernel(const AttnArgs a) {
 // ---------------------------------------------------------------------------------
 // Tensor-core split-KV decode (tcgen05).  One CTA of 4 warps per (row, kv head, split);
 // the split's keys go through 128-key tiles (8 pages):
-//   * TMA copies each (page, 64-dim chunk) box of K and V into a K-major 128-byte
-//     swizzled tile image: chunk c holds the tile's 128 key rows of dims 64c..64c+63.
+//   * One cp.async.bulk per page copies each pre-swizzled (page, kv head) block of K and V
+//     into the tile image: page j at 8 KiB * j, so for every 64-dim chunk the tile's
+//     128 key rows form 16 groups of 8 rows, 4 KiB apart (the operand's SBO).
 //   * S^T = K Q^T: one thread issues 16 tcgen05.mma (kind::f16 bf16, M = 128 keys,
 //     N = 16 query-head slots of the GQA group, K = 16 dims each) into TMEM columns 0-15.
 //   * Online softmax in the exp2 domain: thread t owns key t (TMEM lane t); per-head
@@ -307,8 +333,8 @@ __global__ void __launch_bounds__(256) decode_partial_kernel(const AttnArgs a) {
 //     the [16 heads x 128 keys] K-major operand of the second product, and O is rescaled
 //     in TMEM (tcgen05.ld / st) by exp2(m_old - m_new).
 //   * O^T += V^T P^T: the V tile image read as an MN-major operand (M = 128 head dims per
-//     MMA: 64-dim chunks LBO = 16 KiB apart, 8-key groups SBO = 1 KiB apart), N = 16,
-//     K = 16 keys per MMA, accumulated in TMEM columns 16-47.
+//     MMA: 64-dim chunks LBO = 1 KiB apart, 8-key groups SBO = 4 KiB apart), N = 16,
+//     K = 16 keys (one page) per MMA, accumulated in TMEM columns 16-47.
 // K is reloaded as soon as S is in TMEM; V images are double-buffered and requested two
 // tiles ahead, so both copies overlap the dependent chain of a tile.  Output
 // records (o, m, l) have the layout of the SIMT kernel, so the same combine kernel runs.
@@ -316,8 +342,7 @@ constexpr int TC_KEYS = 128;
 constexpr int TC_PAGES = TC_KEYS / PAGE;
 constexpr int TC_N = 16;
 constexpr int TC_NCHUNK = D / 64;
-constexpr int TC_CHUNK_BYTES = TC_KEYS * 128;
-constexpr int TC_TILE_BYTES = TC_NCHUNK * TC_CHUNK_BYTES;
+constexpr int TC_TILE_BYTES = TC_PAGES * BLOCK_BYTES;
 constexpr int TC_THREADS = 128;
 
 struct TcSmem {
@@ -333,8 +358,7 @@ struct TcSmem {
 };
 
 __global__ void __launch_bounds__(TC_THREADS, 1)
-decode_partial_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
-                         const AttnArgs a) {
+decode_partial_tc_kernel(const AttnArgs a) {
   pdl_wait();  // predecessor kernel done: its outputs are visible
   pdl_trigger();
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
@@ -364,8 +388,6 @@ decode_partial_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_co
     mbar_init(&s.mma1, 1);
     mbar_init(&s.mma2, 1);
     fence_barrier_init();
-    tma_prefetch_desc(&tk);
-    tma_prefetch_desc(&tv);
   }
   if (tid < TC_N) {
     s.m[tid] = -INFINITY;
@@ -390,20 +412,20 @@ decode_partial_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_co
   // Producer state (thread 0 only): loads issued but not yet observed, per barrier.
   int k_pend = 0, v_pend[2] = {0, 0};
   int k_uses = 0, v_uses[2] = {0, 0};
-  auto issue = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* bar, int tile) {
+  const __nv_bfloat16* kc = static_cast<const __nv_bfloat16*>(a.k_cache);
+  const __nv_bfloat16* vc = static_cast<const __nv_bfloat16*>(a.v_cache);
+  auto issue = [&](const __nv_bfloat16* cache, uint8_t* dst, uint64_t* bar, int tile) {
     const int pg0 = p0 + tile * TC_PAGES;
     const int n = min(TC_PAGES, p1 - pg0);
-    mbar_expect_tx(bar, n * TC_NCHUNK * PAGE * 128);
-    for (int j = 0; j < n; ++j) {
-      const int y = (__ldg(pt + pg0 + j) * a.num_kv_heads + kvh) * PAGE;
-      for (int c = 0; c < TC_NCHUNK; ++c) tma_load_2d(dst + c * TC_CHUNK_BYTES + j * PAGE * 128, map, bar, c * 64, y);
-    }
+    mbar_expect_tx(bar, n * BLOCK_BYTES);
+    for (int j = 0; j < n; ++j)
+      bulk_load(dst + j * BLOCK_BYTES, cache + kv_offset(a, __ldg(pt + pg0 + j), kvh), BLOCK_BYTES, bar);
   };
   if (tid == 0 && ntiles > 0) {
-    issue(&tk, s.k, &s.kfull, 0);
+    issue(kc, s.k, &s.kfull, 0);
     k_pend = 1;
     for (int j = 0; j < 2 && j < ntiles; ++j) {
-      issue(&tv, s.v[j], &s.vfull[j], j);
+      issue(vc, s.v[j], &s.vfull[j], j);
       v_pend[j] = 1;
     }
   }
@@ -413,13 +435,11 @@ decode_partial_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_co
     const int pg0 = p0 + t * TC_PAGES;
     const int n = min(TC_PAGES, p1 - pg0);
     if (n < TC_PAGES) {
-      // Last, partial tile: zero the rows of the absent pages in both images (no copy
-      // targets them), so the products see finite values there.
-      const int per_chunk = (TC_PAGES - n) * PAGE * 8;  // 16-byte pieces per chunk
-      for (int i = tid; i < per_chunk * TC_NCHUNK; i += TC_THREADS) {
-        const int off = (i / per_chunk) * TC_CHUNK_BYTES + n * PAGE * 128 + (i % per_chunk) * 16;
-        *reinterpret_cast<uint4*>(s.k + off) = make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(s.v[vb] + off) = make_uint4(0, 0, 0, 0);
+      // Last, partial tile: zero the absent pages in both images (no copy targets them),
+      // so the products see finite values there.
+      for (int i = n * (BLOCK_BYTES / 16) + tid; i < TC_PAGES * (BLOCK_BYTES / 16); i += TC_THREADS) {
+        reinterpret_cast<uint4*>(s.k)[i] = make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(s.v[vb])[i] = make_uint4(0, 0, 0, 0);
       }
       fence_proxy_async_shared();
     }
@@ -433,7 +453,7 @@ decode_partial_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_co
       for (int c = 0; c < TC_NCHUNK; ++c)
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const uint64_t ad = make_smem_desc(smem_u32(s.k + c * TC_CHUNK_BYTES) + k * 32, 16, 1024, 2);
+          const uint64_t ad = make_smem_desc(smem_u32(s.k + c * 1024) + k * 32, 16, 4096, 2);
           const uint64_t bd = make_smem_desc(smem_u32(s.q[c]) + k * 32, 16, 1024, 2);
           mma_bf16(t_s, ad, bd, idesc, (c | k) ? 1u : 0u);
         }
@@ -446,7 +466,7 @@ decode_partial_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_co
     // S is in TMEM: the K image is free, so the next tile's K copy overlaps the rest of
     // this tile (softmax, rescale, second product).
     if (tid == 0 && t + 1 < ntiles) {
-      issue(&tk, s.k, &s.kfull, t + 1);
+      issue(kc, s.k, &s.kfull, t + 1);
       k_pend = 1;
     }
     // ---- online softmax: thread tid owns key tid of the tile
@@ -505,9 +525,11 @@ decode_partial_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_co
     ok = mbar_wait(&s.vfull[vb], (uint32_t)(v_uses[vb] & 1), a.err);
     if (ok && !valid && tok < (pg0 + n) * PAGE) {
       // Cache rows past the context inside a loaded page: zero them (P is 0 there).
+      const int r = tid & 15;
+      uint8_t* blk = s.v[vb] + (tid >> 4) * BLOCK_BYTES + (r >> 3) * 4096 + (r & 7) * 128;
 #pragma unroll
       for (int c = 0; c < TC_NCHUNK; ++c) {
-        uint4* rowp = reinterpret_cast<uint4*>(s.v[vb] + c * TC_CHUNK_BYTES + tid * 128);
+        uint4* rowp = reinterpret_cast<uint4*>(blk + c * 1024);
 #pragma unroll
         for (int j = 0; j < 8; ++j) rowp[j] = make_uint4(0, 0, 0, 0);
       }
@@ -523,8 +545,7 @@ decode_partial_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_co
       for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
-          const uint64_t ad =
-              make_smem_desc(smem_u32(s.v[vb] + 2 * mt * TC_CHUNK_BYTES) + ks * 2048, TC_CHUNK_BYTES, 1024, 2);
+          const uint64_t ad = make_smem_desc(smem_u32(s.v[vb] + 2 * mt * 1024) + ks * BLOCK_BYTES, 1024, 4096, 2);
           const uint64_t bd = make_smem_desc(smem_u32(s.p[ks >> 2]) + (ks & 3) * 32, 16, 1024, 2);
           mma_bf16(t_o + mt * 16, ad, bd, idesc2, (t > 0 || ks > 0) ? 1u : 0u);
         }
@@ -535,7 +556,7 @@ decode_partial_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_co
     if (!__syncthreads_and(ok)) break;
     tc_fence_after();
     if (tid == 0 && t + 2 < ntiles) {  // this V image is free: the tile after next
-      issue(&tv, s.v[vb], &s.vfull[vb], t + 2);
+      issue(vc, s.v[vb], &s.vfull[vb], t + 2);
       v_pend[vb] = 1;
     }
   }
@@ -621,40 +642,6 @@ extern "C" int zs_attn_prologue(const AttnArgs* args, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
-namespace {
-
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (fn == nullptr) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
-  return fn;
-}
-
-// A paged K or V cache [pages, kv_heads, 16, 256] bf16 as a 2-D tensor of 256-dim rows;
-// one box is 16 rows (one page of one kv head) x 64 dims, 128-byte swizzled.
-int make_cache_map(CUtensorMap* m, void* base, long long rows) {
-  EncodeTiledFn enc = encode_fn();
-  if (enc == nullptr) return -1;
-  cuuint64_t dims[2] = {(cuuint64_t)zs::attn::D, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)zs::attn::D * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)zs::attn::PAGE};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? 0 : -2;
-}
-
-}  // namespace
-
 extern "C" int zs_attn_decode(const AttnArgs* args, cudaStream_t stream) {
   const AttnArgs& a = *args;
   if (a.head_dim != zs::attn::D || a.num_kv_heads <= 0 || a.num_q_heads % a.num_kv_heads != 0) return -1;
@@ -664,14 +651,10 @@ extern "C" int zs_attn_decode(const AttnArgs* args, cudaStream_t stream) {
   dim3 g1(a.rows, a.num_kv_heads, a.num_splits);
   // Tensor cores pay off from 4 query heads per kv head; smaller groups (a GQA group
   // split over many ranks) stay on the SIMT kernel, which runs one warp per head.
-  if (a.impl == 0 && group >= 4 && group <= zs::attn::TC_N && a.num_pages > 0) {
-    // Tensor-core path: TMA boxes of the paged caches (the maps cover all pages).
-    CUtensorMap tk, tv;
-    const long long rows = (long long)a.num_pages * a.num_kv_heads * zs::attn::PAGE;
-    if (make_cache_map(&tk, a.k_cache, rows) != 0 || make_cache_map(&tv, a.v_cache, rows) != 0) return -5;
+  if (a.impl == 0 && group >= 4 && group <= zs::attn::TC_N) {
     const size_t smem = sizeof(zs::attn::TcSmem) + 1024;
     cudaFuncSetAttribute(zs::attn::decode_partial_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    zs_launch(zs::attn::decode_partial_tc_kernel, g1, zs::attn::TC_THREADS, smem, stream, tk, tv, a);
+    zs_launch(zs::attn::decode_partial_tc_kernel, g1, zs::attn::TC_THREADS, smem, stream, a);
     dim3 g2(a.rows, a.num_q_heads);
     zs_launch(zs::attn::decode_combine_kernel, g2, zs::attn::D, 0, stream, a);
     return cudaGetLastError() == cudaSuccess ? 0 : -2;

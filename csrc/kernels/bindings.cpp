@@ -289,7 +289,6 @@ void attn_decode(const Tensor& q_out, const Tensor& gate_out, int64_t num_q_head
   a.out_bf16 = optptr(out_bf16);
   a.out_q = optptr<uint8_t>(out_q);
   a.out_sf = optptr<uint8_t>(out_sf);
-  a.num_pages = (int)k_cache.size(0);
   a.impl = (int)impl;
   a.err = optptr<int>(err);
   rc(zs_attn_decode(&a, stream()), "zs_attn_decode");

@@ -155,7 +155,7 @@ typedef struct AttnArgs {
   const void* q_norm_w;    // bf16 [head_dim] (zero-centered: scale = 1 + w)
   const void* k_norm_w;
   float eps;
-  void* k_cache;           // bf16 [pages, page_size, kv_heads, head_dim]
+  void* k_cache;           // bf16 [pages, kv_heads, 16 x 256] pre-swizzled blocks (attention.cu)
   void* v_cache;
   int page_size;
   const int* page_table;   // [slots, max_pages]
@@ -177,8 +177,7 @@ typedef struct AttnArgs {
   const int* seq_start;    // [num_seqs+1]
   int num_seqs;
   int* err;
-  int num_pages;           // pages of k_cache / v_cache (the tensor-core path maps them all)
-  int impl;                // 0: tensor-core decode when supported (group <= 16), 1: SIMT decode
+  int impl;                // 0: tensor-core decode for GQA groups of 4..16 heads, 1: SIMT decode
 } AttnArgs;
 
 int zs_attn_prologue(const AttnArgs* args, cudaStream_t stream);

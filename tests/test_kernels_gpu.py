@@ -7,6 +7,7 @@ import torch
 import torch.nn.functional as F
 
 from zstep_b200.ops import mx
+from zstep_b200.ops.kv_layout import swizzle_pages, unswizzle_pages
 from zstep_b200.ops import reference as ref
 
 pytestmark = pytest.mark.gpu
@@ -583,7 +584,7 @@ def test_attention_prologue_and_decode(C):
     qn = (0.1 * torch.randn(d)).to(torch.bfloat16)
     kn = (0.1 * torch.randn(d)).to(torch.bfloat16)
     pos = torch.tensor([c - 1 for c in ctx], dtype=torch.int32)
-    kc_g, vc_g = kc.cuda(), vc.cuda()
+    kc_g, vc_g = swizzle_pages(kc).cuda(), swizzle_pages(vc).cuda()
     q_out = torch.zeros(rows, hq, d, dtype=torch.bfloat16, device="cuda")
     g_out = torch.zeros(rows, hq, d, dtype=torch.bfloat16, device="cuda")
     C.attn_prologue(qkv.cuda(), hq, hkv, 64, 1e7, qn.cuda(), kn.cuda(), 1e-6, kc_g, vc_g, page,
@@ -595,6 +596,7 @@ def test_attention_prologue_and_decode(C):
     C.attn_decode(q_out, g_out, hq, hkv, kc_g, vc_g, page, page_table.cuda(), slots.cuda(),
                   torch.tensor(ctx, dtype=torch.int32).cuda(), rows, partial, splits, sm, out, None, None)
     torch.cuda.synchronize()
+    kc_rows, vc_rows = unswizzle_pages(kc_g.cpu()), unswizzle_pages(vc_g.cpu())
     for r in range(rows):
         q, gate, k_new, v_new = ref.attn_prologue_row(qkv[r].float(), pos[r].item(), hq=hq, hkv=hkv,
                                                       q_norm_w=qn, k_norm_w=kn, eps=1e-6, rotary_dim=64,
@@ -602,18 +604,19 @@ def test_attention_prologue_and_decode(C):
         torch.testing.assert_close(q_out[r].cpu().float(), q, rtol=2e-2, atol=2e-2)
         p_last = pos[r].item()
         pg = page_table[r, p_last // page].item()
-        torch.testing.assert_close(kc_g[pg, :, p_last % page].cpu().float(), k_new, rtol=2e-2, atol=2e-2)
-        keys = torch.stack([kc_g[page_table[r, t // page], :, t % page].cpu().float() for t in range(ctx[r])])
-        vals = torch.stack([vc_g[page_table[r, t // page], :, t % page].cpu().float() for t in range(ctx[r])])
+        torch.testing.assert_close(kc_rows[pg, :, p_last % page].float(), k_new, rtol=2e-2, atol=2e-2)
+        keys = torch.stack([kc_rows[page_table[r, t // page], :, t % page].float() for t in range(ctx[r])])
+        vals = torch.stack([vc_rows[page_table[r, t // page], :, t % page].float() for t in range(ctx[r])])
         expect = ref.gated_attention(q_out[r].cpu().float(), g_out[r].cpu().float(), keys, vals, sm)
         torch.testing.assert_close(out[r].cpu().float(), expect, rtol=2e-2, atol=2e-2)
 
 
 @pytest.mark.parametrize("hq,hkv,splits", [(16, 2, 1), (16, 2, 3), (2, 1, 2), (16, 1, 1)])
 def test_attention_decode_tensor_core(C, hq, hkv, splits):
-    """The tcgen05 split-KV decode (128-key tiles, TMA page boxes, online softmax with
-    TMEM rescale) against the fp32 reference, over contexts that end mid-page, mid-tile,
-    on tile boundaries and inside one page; group sizes 8, 2 and 16."""
+    """The tcgen05 split-KV decode (128-key tiles of bulk-copied pre-swizzled pages, online
+    softmax with TMEM rescale) and the SIMT kernel against the fp32 reference, over
+    contexts that end mid-page, mid-tile, on tile boundaries and inside one page; group
+    sizes 8, 2 (SIMT) and 16."""
     g = torch.Generator().manual_seed(7)
     d, page = 256, 16
     ctx = [1, 16, 37, 128, 129, 300, 511]
@@ -633,7 +636,7 @@ def test_attention_decode_tensor_core(C, hq, hkv, splits):
         partial = torch.zeros(rows * hq * splits * 260, device="cuda")
         out = torch.zeros(rows, hq * d, dtype=torch.bfloat16, device="cuda")
         err = torch.zeros(1, dtype=torch.int32, device="cuda")
-        C.attn_decode(dev(q), dev(gate), hq, hkv, dev(kc), dev(vc), page, dev(table),
+        C.attn_decode(dev(q), dev(gate), hq, hkv, dev(swizzle_pages(kc)), dev(swizzle_pages(vc)), page, dev(table),
                       torch.arange(rows, dtype=torch.int32, device="cuda"), torch.tensor(ctx, dtype=torch.int32).cuda(),
                       rows, partial, splits, sm, out, None, None, impl=impl, err=err)
         torch.cuda.synchronize()

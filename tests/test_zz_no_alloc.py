@@ -26,7 +26,7 @@ class AttnArgs(ctypes.Structure):
                 ("k_cache", P), ("v_cache", P), ("page_size", I), ("page_table", P), ("max_pages", I),
                 ("slots", P), ("positions", P), ("rows", I), ("q_out", P), ("gate_out", P), ("seq_lens", P),
                 ("partial", P), ("num_splits", I), ("sm_scale", F), ("out_bf16", P), ("out_q", P), ("out_sf", P),
-                ("seq_start", P), ("num_seqs", I), ("err", P), ("num_pages", I), ("impl", I)]
+                ("seq_start", P), ("num_seqs", I), ("err", P), ("impl", I)]
 
 
 def _lib():
@@ -62,7 +62,6 @@ def _args(t, c, out):
     a = AttnArgs()
     a.num_q_heads, a.num_kv_heads, a.head_dim = c["hq"], c["hkv"], 256
     a.k_cache, a.v_cache = t["kc"].data_ptr(), t["vc"].data_ptr()
-    a.num_pages = t["kc"].shape[0]
     a.page_size, a.page_table, a.max_pages = c["page"], t["table"].data_ptr(), c["max_pages"]
     a.slots, a.seq_lens, a.rows = t["slots"].data_ptr(), t["lens"].data_ptr(), c["rows"]
     a.q_out, a.gate_out = t["q"].data_ptr(), t["gate"].data_ptr()

@@ -287,15 +287,17 @@ def cmd_attn(a):
     r.k_cache.normal_()
     r.v_cache.normal_()
     ai = 0
-    splits = r._attn_splits(a.m, True)
+    splits = a.splits or r._attn_splits(a.m, True)
     midq = r._mid(r.hq * 256)
+    if b["partial"].numel() < a.m * r.hq * splits * 260:
+        b["partial"] = torch.zeros(a.m * r.hq * splits * 260, device=r.dev)
     fn = lambda: r.C.attn_decode(b["q_out"], b["gate_out"], r.hq, r.hkv, r.k_cache[ai], r.v_cache[ai], r.page_size,  # noqa
                                  r.page_table, b["in_slot"][:a.m], b["in_len"][:a.m], a.m, b["partial"], splits,
-                                 1 / 16.0, None, midq, b["midsf"])
+                                 1 / 16.0, None, midq, b["midsf"], impl=a.impl)
     ms = time_fn(fn, flush=True)
     kv_bytes = a.m * (a.ctx + 1) * r.hkv * 256 * 2 * 2
     pk = peaks()
-    print(json.dumps({"op": "attn_decode", "rows": a.m, "ctx": a.ctx, "splits": splits, "ms": round(ms, 4),
+    print(json.dumps({"op": "attn_decode", "impl": a.impl, "rows": a.m, "ctx": a.ctx, "splits": splits, "ms": round(ms, 4),
                       "gbs": round(kv_bytes / ms / 1e6, 1), "frac_hbm": round(kv_bytes / ms / 1e6 / pk["hbm_gbs"], 3),
                       "peaks": pk["src"]}))
 
@@ -332,6 +334,8 @@ def main():
     ap.add_argument("--flush", type=int, default=1, help="evict L2 before every timed call")
     ap.add_argument("--tp", type=int, default=1, help="time rank 0 of a tp-way layout (no communication)")
     ap.add_argument("--model", default="qwen", choices=["qwen", "deepseek"])
+    ap.add_argument("--splits", type=int, default=0, help="attn: split-KV factor (0 = the runner's choice)")
+    ap.add_argument("--impl", type=int, default=0, help="attn: 0 tensor-core decode, 1 SIMT decode")
     a = ap.parse_args()
     torch.manual_seed(0)
     {"breakdown": cmd_breakdown, "step": cmd_step, "gemm": cmd_gemm, "gdn": cmd_gdn, "attn": cmd_attn,

@@ -374,11 +374,16 @@ class Qwen35Runner:
         rp = _pad128(self.R)
         return self.buf["midq"][: rp * width].view(rp, width)
 
-    def _attn_splits(self, rows: int, decode: bool) -> int:
+    def _attn_splits(self, rows: int, decode: bool, ctx: int | None = None) -> int:
         if not decode:
             return 1
-        ctas = rows * self.hkv
-        return int(max(1, min(self.max_splits, math.ceil(1200 / max(ctas, 1)))))
+        ctas = max(rows * self.hkv, 1)
+        if self.hq // self.hkv >= 4:
+            # Tensor-core decode (one CTA per SM, a dependent chain per 128-key tile): about
+            # two waves of CTAs, each split keeping >= 8 tiles to amortise its first load.
+            ctx = ctx or self.max_pages * self.page_size
+            return int(max(1, min(self.max_splits, math.ceil(296 / ctas), max(1, ctx // 1024))))
+        return int(max(1, min(self.max_splits, math.ceil(1200 / ctas))))
 
     def _proj_out(self, w: PackedLinear, xq, xsf, rows: int, norm_w, hidden=None) -> None:
         """Row-parallel output projection (GDN out_proj / attention o_proj) into f32
