@@ -93,6 +93,10 @@ const char* kRunUsage =
     "  --bench-tiers SPEC[,SPEC]    label:concurrency:prompts:input_len:output_len[:prefix_len:num_prefixes]\n"
     "                               (with prefix fields, prompt i = shared prefix i % num_prefixes + input_len ids)\n"
     "  --bench-repeats N            Interleaved repeats per tier (default 1)\n"
+    "  --micro-steps N              Control-plane benchmark: N synthetic micro-steps per token count on the\n"
+    "                               `micro` worker model (no --model-dir needed); reports round-trip latency\n"
+    "  --token-counts LIST          Rows per micro-step, comma separated (default 6,48,192)\n"
+    "  --micro-hidden N / --micro-features N / --micro-experts N / --micro-topk N   micro-step model shape\n"
     "  --seed N                     Prompt seed (default 0)\n";
 
 struct Args {
@@ -119,7 +123,8 @@ struct Args {
 const std::set<std::string> kValueFlags = {
     "model-dir", "model", "served-model-name", "host", "port", "api-key", "admin-port", "world-size", "device",
     "max-model-len", "max-seqs", "max-step-tokens", "max-prefill-chunk", "page-block-tokens", "num-kv-pages",
-    "tokenizer-mode", "apc-node-pages", "num-ckpt-slots", "dram-kv-blocks", "dram-loading-area-ratio", "max-waiting-requests", "prefill-policy",
+    "tokenizer-mode", "apc-node-pages", "num-ckpt-slots", "dram-kv-blocks", "dram-loading-area-ratio",
+    "micro-steps", "token-counts", "micro-hidden", "micro-features", "micro-experts", "micro-topk", "max-waiting-requests", "prefill-policy",
     "drain-timeout-secs", "python", "worker-root", "ready-timeout-secs", "step-timeout-secs", "speculative-method",
     "num-speculative-tokens", "prompt-ids", "prompt", "max-tokens", "verify-greedy-json", "bench-tiers",
     "bench-repeats", "seed", "kv-events-endpoint", "kv-events-topic"};
@@ -209,12 +214,15 @@ struct Built {
 
 // Engine + backend from the common flags.
 bool build_engine(const Args& a, Built* b, std::string* err) {
+  const bool micro = a.has("micro-steps");
   const std::string dir = a.get("model-dir");
-  if (dir.empty()) {
+  if (dir.empty() && !micro) {
     *err = "--model-dir is required";
     return false;
   }
-  if (b->tokenizer.load_dir(dir, err)) {
+  if (micro) {
+    // the micro-step model needs no checkpoint or tokenizer
+  } else if (b->tokenizer.load_dir(dir, err)) {
     b->has_tokenizer = true;
   } else if (!a.has("prompt-ids") && !a.has("bench-tiers") && !a.has("verify-greedy-json")) {
     return false;  // text serving needs the tokenizer
@@ -287,7 +295,7 @@ bool build_engine(const Args& a, Built* b, std::string* err) {
                       "-m",
                       "zstep_b200.runtime.worker",
                       "--model",
-                      a.get("model", dir),
+                      micro ? std::string("micro") : a.get("model", dir),
                       "--device",
                       a.get("device", "cuda"),
                       "--num-pages",
@@ -302,6 +310,12 @@ bool build_engine(const Args& a, Built* b, std::string* err) {
                       std::to_string(c.num_spec_tokens),
                       "--dram-kv-blocks",
                       std::to_string(c.dram_blocks)};
+    if (micro)
+      for (const char* k : {"micro-hidden", "micro-features", "micro-experts", "micro-topk"})
+        if (a.has(k)) {
+          cc.worker_argv.push_back(std::string("--") + k);
+          cc.worker_argv.push_back(a.get(k));
+        }
     const std::string root = a.get("worker-root", self_root());
     const char* pp = getenv("PYTHONPATH");
     cc.env["PYTHONPATH"] = root + (pp ? std::string(":") + pp : std::string());
@@ -568,6 +582,82 @@ int cmd_run(const Args& a) {
   int rc = 0;
   engine::Engine& e = *b.engine;
   const std::string root = a.get("worker-root", self_root());
+  if (a.has("micro-steps")) {
+    // Control-plane benchmark: synthetic plans (one 1-row sequence per token) straight
+    // through the coordinator; the host clock measures publish -> all ranks done -> result.
+    if (!b.coord) {
+      fprintf(stderr, "zstep run: --micro-steps needs workers (not --mock)\n");
+      return 2;
+    }
+    const int steps = (int)a.num("micro-steps", 200);
+    std::vector<int> counts;
+    {
+      std::string list = a.get("token-counts", "6,48,192");
+      size_t p0 = 0;
+      while (p0 <= list.size()) {
+        const size_t p1 = list.find(',', p0);
+        const std::string item = list.substr(p0, p1 == std::string::npos ? std::string::npos : p1 - p0);
+        if (!item.empty()) counts.push_back(atoi(item.c_str()));
+        if (p1 == std::string::npos) break;
+        p0 = p1 + 1;
+      }
+    }
+    json::Value tiers = json::Value::array();
+    for (int m : counts) {
+      if (m < 1 || (uint32_t)m > b.cfg.max_seqs || (uint32_t)m > b.cfg.max_step_tokens) {
+        fprintf(stderr, "zstep run: token count %d must be within 1..min(--max-seqs, --max-step-tokens)\n", m);
+        rc = 2;
+        break;
+      }
+      engine::StepPlan p;
+      p.query_start.push_back(0);
+      for (int i = 0; i < m; ++i) {
+        p.token_ids.push_back(i + 1);
+        p.positions.push_back(i);
+        p.row_slot.push_back(i);
+        p.query_start.push_back(i + 1);
+        p.seq_slot.push_back(i);
+        p.seq_len.push_back(1);
+        p.sample_row.push_back(i);
+        p.sampling.push_back(wire::SamplingParams{});
+        p.restore_slot.push_back(-1);
+        p.spec_width.push_back(0);
+      }
+      std::vector<double> lat_us, gpu_us;
+      for (int s = 0; s < steps + 5 && err.empty(); ++s) {
+        engine::StepResult res;
+        const uint64_t t0 = monotonic_ns();
+        if (!b.coord->execute(p, &res)) {
+          err = b.coord->error();
+          break;
+        }
+        const uint64_t t1 = monotonic_ns();
+        if (s >= 5) {  // warm-up steps excluded
+          lat_us.push_back((t1 - t0) * 1e-3);
+          gpu_us.push_back((double)res.gpu_exec_us);
+        }
+      }
+      if (!err.empty()) break;
+      json::Value t = json::Value::object();
+      t.set("token_count", m);
+      t.set("steps", steps);
+      t.set("p50_step_us", pct(lat_us, 0.5));
+      t.set("p99_step_us", pct(lat_us, 0.99));
+      t.set("mean_step_us", mean_of(lat_us));
+      t.set("mean_gpu_us", mean_of(gpu_us));
+      t.set("mean_overhead_us", mean_of(lat_us) - mean_of(gpu_us));
+      t.set("steps_per_s", 1e6 / std::max(mean_of(lat_us), 1e-9));
+      tiers.push(t);
+    }
+    json::Value report = json::Value::object();
+    report.set("micro_steps", tiers);
+    report.set("world_size", (int64_t)a.num("world-size", 1));
+    report.set("provenance", provenance(root));
+    if (!err.empty()) report.set("error", err);
+    printf("%s\n", report.dump().c_str());
+    if (b.coord) b.coord->shutdown();
+    return err.empty() && rc == 0 ? 0 : 1;
+  }
   if (a.has("verify-greedy-json")) {
     std::ifstream f(a.get("verify-greedy-json"));
     std::stringstream ss;

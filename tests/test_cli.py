@@ -117,3 +117,19 @@ def test_serve_lifecycle_and_sigterm(model_dir):
         if p.poll() is None:
             p.kill()
             p.wait()
+
+
+def test_micro_steps_control_plane_benchmark():
+    """`zstep run --micro-steps` drives synthetic plans through the shared-memory coordinator
+    to two CPU workers running the micro-step model (tensor-parallel sum over gloo)."""
+    import sys
+
+    r = run("run", "--micro-steps", "12", "--token-counts", "4,16", "--device", "cpu", "--world-size", "2",
+            "--max-seqs", "32", "--max-step-tokens", "64", "--micro-hidden", "256", "--micro-features", "256",
+            "--micro-experts", "64", "--micro-topk", "4", "--python", sys.executable, "--worker-root", ROOT,
+            timeout=300)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
+    rep = json.loads(r.stdout.strip().splitlines()[-1])
+    tiers = rep["micro_steps"]
+    assert [t["token_count"] for t in tiers] == [4, 16]
+    assert all(t["steps"] == 12 and t["steps_per_s"] > 0 and t["p99_step_us"] >= t["p50_step_us"] for t in tiers)

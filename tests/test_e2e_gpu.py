@@ -81,3 +81,14 @@ def test_deepseek_dram_tier_keeps_greedy_tokens(model_dir, tmp_path):
     path.write_text(json.dumps({"prompts": prompts, "expected": want}))
     got, r1 = run("--num-kv-pages", "16", "--dram-kv-blocks", "32")
     assert got.get("mismatches") == 0, (got, r1.stderr[-3000:])
+
+
+def test_micro_steps_on_gpu():
+    """The micro-step model on a B200 worker (RMSNorm + MXFP8 + tcgen05 GEMM + router)."""
+    args = [BIN, "run", "--micro-steps", "20", "--token-counts", "6,48,192", "--device", "cuda", "--max-seqs", "192",
+            "--max-step-tokens", "256", "--python", sys.executable, "--worker-root", ROOT]
+    r = subprocess.run(args, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
+    tiers = json.loads(r.stdout.strip().splitlines()[-1])["micro_steps"]
+    assert [t["token_count"] for t in tiers] == [6, 48, 192]
+    assert all(t["mean_gpu_us"] > 0 and t["steps_per_s"] > 0 for t in tiers)

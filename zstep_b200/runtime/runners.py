@@ -66,6 +66,15 @@ def make_runner(args, rank: int, world: int, geo):
         if args.device == "cuda":
             torch.cuda.set_device(rank % max(1, torch.cuda.device_count()))
         dist.init_process_group(backend, rank=rank, world_size=world)
+    if args.model == "micro":
+        from ..models.micro import MicroStepRunner
+
+        coll = None
+        if args.device == "cuda" and world > 1:
+            from ..parallel import make_collectives
+
+            coll = make_collectives(torch.device("cuda", torch.cuda.current_device()))
+        return MicroStepRunner(args, rank, world, geo, device=args.device, collectives=coll)
     if args.device == "cpu":
         return CpuReferenceRunner(args, rank, world, geo)
     return GpuRunner(args, rank, world, geo)

@@ -133,7 +133,7 @@ class WorkerLoop:
                 outputs = self.runner.execute(plan)
             except Exception:  # noqa: BLE001
                 self.fail(ERR_EXCEPTION, f"step {step} failed:\n" + traceback.format_exc())
-            gpu_us = int((time.perf_counter() - t0) * 1e6)
+            gpu_us = getattr(self.runner, "last_gpu_us", 0) or int((time.perf_counter() - t0) * 1e6)
             if self.rank == 0:
                 self.view.write_result(step, outputs, 0, gpu_us)
             self.view.set_worker(self.rank, ready_step=step, status=wire.WORKER_READY, gpu_us=gpu_us)
@@ -153,6 +153,10 @@ def parse_args(argv=None):
     ap.add_argument("--spec-method", default="none")
     ap.add_argument("--num-spec-tokens", type=int, default=0)
     ap.add_argument("--dram-kv-blocks", type=int, default=0, help="host DRAM tier blocks (pinned page arena)")
+    ap.add_argument("--micro-hidden", type=int, default=5120, help="micro-step model: RMSNorm / GEMM input width")
+    ap.add_argument("--micro-features", type=int, default=2048, help="micro-step model: GEMM output columns")
+    ap.add_argument("--micro-experts", type=int, default=384, help="micro-step model: router experts")
+    ap.add_argument("--micro-topk", type=int, default=6, help="micro-step model: router top-k")
     ap.add_argument("--shm-fd", type=int, required=True)
     ap.add_argument("--shm-bytes", type=int, required=True)
     ap.add_argument("--plan-fd", type=int, required=True)
