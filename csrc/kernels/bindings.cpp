@@ -649,7 +649,44 @@ void gather_sum(const Tensor& rows_in, const Tensor& src, const Tensor& w, int64
      "zs_gather_sum");
 }
 
+
+void sample_rows(const Tensor& logits, int64_t vocab, int64_t rows, const Tensor& temperature, const OptT& top_k,
+                 const OptT& top_p, const OptT& presence, const OptT& frequency, const OptT& repetition,
+                 const Tensor& seed, const OptT& hist, const OptT& hist_len, int64_t top_n, const Tensor& out_token,
+                 const OptT& out_logprob, const OptT& out_top_ids, const OptT& out_top_lp) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(-1) == 1, "sample: fp32 logits rows");
+  TORCH_CHECK(seed.scalar_type() == at::kLong, "sample: int64 seeds");
+  SampleArgs a{};
+  a.logits = ptr<float>(logits);
+  a.ld = (int)logits.stride(0);
+  a.vocab = (int)vocab;
+  a.rows = (int)rows;
+  a.temperature = ptr<const float>(temperature);
+  a.top_k = optptr<const int>(top_k);
+  a.top_p = optptr<const float>(top_p);
+  a.presence = optptr<const float>(presence);
+  a.frequency = optptr<const float>(frequency);
+  a.repetition = optptr<const float>(repetition);
+  a.seed = ptr<const unsigned long long>(seed);
+  a.hist = optptr<const int>(hist);
+  a.hist_ld = hist.has_value() ? (int)hist->stride(0) : 0;
+  a.hist_len = optptr<const int>(hist_len);
+  a.want_logprobs = out_logprob.has_value() ? 1 : 0;
+  a.top_n = (int)top_n;
+  a.out_token = ptr<int>(out_token);
+  a.out_logprob = optptr<float>(out_logprob);
+  a.out_top_ids = optptr<int>(out_top_ids);
+  a.out_top_lp = optptr<float>(out_top_lp);
+  TORCH_CHECK(!a.want_logprobs || top_n == 0 || (a.out_top_ids && a.out_top_lp), "sample: top-N outputs");
+  rc(zs_sample(&a, stream()), "zs_sample");
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("sample", &sample_rows, py::arg("logits"), py::arg("vocab"), py::arg("rows"), py::arg("temperature"),
+        py::arg("top_k"), py::arg("top_p"), py::arg("presence"), py::arg("frequency"), py::arg("repetition"),
+        py::arg("seed"), py::arg("hist"), py::arg("hist_len"), py::arg("top_n"), py::arg("out_token"),
+        py::arg("out_logprob"), py::arg("out_top_ids"), py::arg("out_top_lp"));
   m.def("mhc_partial", &mhc_partial, py::arg("x"), py::arg("rows"), py::arg("hidden"), py::arg("fn"), py::arg("mode"),
         py::arg("y") = py::none(), py::arg("mix_prev") = py::none(), py::arg("ids") = py::none(),
         py::arg("embed") = py::none(), py::arg("partial"));

@@ -409,6 +409,32 @@ int zs_dsa_topk(const DsaTopkArgs* args, cudaStream_t stream);
 int zs_gather_sum(const void* rows_in, const int* src, const float* w, int k1, int hidden, int rows, float* y,
                   cudaStream_t stream);
 
+// ----------------------------------------------------------------------------------
+// Full-distribution sampling (sampling.cu)
+// ----------------------------------------------------------------------------------
+typedef struct SampleArgs {
+  float* logits;               // fp32 [rows, ld], whole vocabulary (penalties are applied in place)
+  int ld, vocab, rows;
+  const float* temperature;    // [rows]; <= 0: greedy
+  const int* top_k;            // [rows]; 0: off (may be NULL)
+  const float* top_p;          // [rows]; 1: off (may be NULL)
+  const float* presence;       // [rows] (may be NULL)
+  const float* frequency;      // [rows] (may be NULL)
+  const float* repetition;     // [rows] (may be NULL; 1 = off)
+  const unsigned long long* seed;  // [rows] draw seed
+  const int* hist;             // [rows, hist_ld] generated-token history (may be NULL)
+  int hist_ld;
+  const int* hist_len;         // [rows]
+  int want_logprobs;           // 1: chosen-token logprob and top_n logprobs of the raw logits
+  int top_n;                   // <= 5
+  int* out_token;              // [rows]
+  float* out_logprob;          // [rows]
+  int* out_top_ids;            // [rows, 5]
+  float* out_top_lp;           // [rows, 5]
+} SampleArgs;
+
+int zs_sample(const SampleArgs* args, cudaStream_t stream);
+
 // Programmatic dependent launch of the compute kernels (on by default).
 void zs_set_pdl(int on);
 int zs_pdl_enabled();

@@ -653,6 +653,80 @@ def test_attention_decode_tensor_core(C, hq, hkv, splits):
     del grp
 
 
+def _sample(C, logits, temp, top_k, top_p, seeds, hist=None, pres=None, freq=None, rep=None, top_n=0):
+    n, v = logits.shape
+    dev = "cuda"
+    f = lambda x, d=0.0: torch.full((n,), d, dtype=torch.float32, device=dev) if x is None else \
+        torch.as_tensor(x, dtype=torch.float32, device=dev)  # noqa: E731
+    lg = logits.clone().float().to(dev)
+    tok = torch.zeros(n, dtype=torch.int32, device=dev)
+    lp = torch.zeros(n, device=dev) if top_n else None
+    tids = torch.zeros(n, 5, dtype=torch.int32, device=dev) if top_n else None
+    tlps = torch.zeros(n, 5, device=dev) if top_n else None
+    if hist is None:
+        h, hl = None, None
+    else:
+        h = torch.zeros(n, 4096, dtype=torch.int32, device=dev)
+        hl = torch.zeros(n, dtype=torch.int32, device=dev)
+        for i, row in enumerate(hist):
+            h[i, :len(row)] = torch.tensor(row, dtype=torch.int32)
+            hl[i] = len(row)
+    C.sample(lg, v, n, f(temp), torch.as_tensor(top_k, dtype=torch.int32, device=dev), f(top_p, 1.0), f(pres),
+             f(freq), f(rep, 1.0), torch.as_tensor(seeds, dtype=torch.int64, device=dev), h, hl, top_n, tok, lp, tids,
+             tlps)
+    torch.cuda.synchronize()
+    return tok.cpu(), (lp.cpu() if top_n else None), (tids.cpu() if top_n else None), (tlps.cpu() if top_n else None)
+
+
+def test_sample_kernel_exact_cases(C):
+    """Greedy (with penalties), top-k = 1, a tiny top-p and log-probabilities are exact."""
+    from zstep_b200.sampling import apply_penalties
+
+    g = torch.Generator().manual_seed(3)
+    n, v = 6, 50000
+    logits = torch.randn(n, v, generator=g) * 3
+    hist = [[1, 2, 2, 7], [], [int(logits[2].argmax())] * 3, [5], [9, 9], [int(logits[5].argmax())]]
+    pres, freq, rep = [0.5, 0, 2.0, 0, 0.3, 0], [0.3, 0, 1.0, 0, 0.2, 0], [1.2, 1, 1, 1.5, 1, 2.0]
+    tok, lp, tids, tlps = _sample(C, logits, [0.0] * n, [0] * n, [1.0] * n, list(range(n)), hist=hist, pres=pres,
+                                  freq=freq, rep=rep, top_n=5)
+    for i in range(n):
+        pen = apply_penalties(logits[i], hist[i], pres[i], freq[i], rep[i])
+        assert int(tok[i]) == int(pen.argmax()), i
+        ref_lp = torch.log_softmax(logits[i].double(), 0)
+        assert abs(float(lp[i]) - float(ref_lp[int(tok[i])])) < 1e-4
+        top = torch.topk(logits[i], 5)
+        assert tids[i].tolist() == top.indices.tolist()
+        torch.testing.assert_close(tlps[i].double(), ref_lp[top.indices], rtol=0, atol=1e-4)
+    tok, *_ = _sample(C, logits, [0.8] * n, [1] * n, [1.0] * n, list(range(n)))
+    assert tok.tolist() == logits.argmax(-1).tolist()
+    tok, *_ = _sample(C, logits, [0.8] * n, [0] * n, [1e-6] * n, list(range(n)))
+    assert tok.tolist() == logits.argmax(-1).tolist()
+
+
+def test_sample_kernel_distribution_and_determinism(C):
+    """Many seeds over one row: every draw lies in the top-k / top-p kept set and the
+    frequencies follow the renormalised truncated softmax; a seed reproduces its draw."""
+    g = torch.Generator().manual_seed(4)
+    v, n = 300, 6000
+    row = torch.randn(v, generator=g) * 2
+    temp, k, p = 0.7, 20, 0.8
+    logits = row.expand(n, v).contiguous()
+    seeds = torch.arange(n, dtype=torch.int64) * 7919 + 11
+    tok, *_ = _sample(C, logits, [temp] * n, [k] * n, [p] * n, seeds)
+    tok2, *_ = _sample(C, logits, [temp] * n, [k] * n, [p] * n, seeds)
+    assert torch.equal(tok, tok2)
+    s = row / temp
+    vals, idx = torch.sort(s, descending=True)
+    probs = torch.softmax(vals[:k].double(), 0)
+    prior = torch.cumsum(probs, 0) - probs
+    keep = int((prior < p).sum())
+    kept = set(idx[:keep].tolist())
+    assert set(tok.tolist()) <= kept
+    want = probs[:keep] / probs[:keep].sum()
+    counts = torch.bincount(tok.long(), minlength=v).double()[idx[:keep]] / n
+    assert float((counts - want).abs().max()) < 0.03, (counts, want)
+
+
 def test_moe_route_softmax_shared(C):
     torch.manual_seed(0)
     rows, E, k, hidden = 50, 64, 4, 256

@@ -514,6 +514,7 @@ class Qwen35Runner:
         codes = self._gather_sf(b["xsf"], row_idx, H)
         xq_buf[:n] = b["xq"][row_idx]
         sf = mx.atoms_from_codes(codes)
+        self.last_lm_sf = sf  # scale atoms of the gathered rows (the full sampling head reuses them)
         b["samp_pos"][:n] = b["in_pos"][row_idx]
         self._lm_head_argmax(n, xq_buf, sf, pos=b["samp_pos"])
         return b["out_ids"][:n]

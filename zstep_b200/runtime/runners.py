@@ -28,6 +28,7 @@ import torch
 import torch.distributed as dist
 
 from . import wire
+from ..models import sampling_head
 from ..sampling import sample_logits, verify_greedy
 
 
@@ -101,6 +102,7 @@ class CpuReferenceRunner:
                                quant=False, tp_rank=rank, tp_size=world, allreduce=ar)
         self.states: dict[int, object] = {}
         self.ckpt: dict[int, object] = {}
+        self.generated: dict[int, list[int]] = {}  # per slot: generated tokens (penalties)
 
     def _allreduce(self, x: torch.Tensor) -> torch.Tensor:
         x = x.contiguous()
@@ -128,6 +130,7 @@ class CpuReferenceRunner:
                 self.states[slot] = self.model.clone_state(self.ckpt[int(plan["restore_slot"][i])])
             if r1 > r0 and int(pos[r0]) == 0:
                 self.states[slot] = self.model.new_state()
+                self.generated[slot] = []
             st = self.states[slot]
             width = int(plan["spec_width"][i])
             row_logits, row_states = [], []
@@ -153,7 +156,17 @@ class CpuReferenceRunner:
                 self.states[slot] = row_states[len(acc) - 1]
                 tokens = acc
             else:
-                tokens = [sample_logits(row_logits[-1], sp)]
+                hist = self.generated.setdefault(slot, [])[-4096:]
+                tokens = [sample_logits(row_logits[-1], sp, hist)]
+                if int(sp["logprobs"]) >= 0:
+                    lsm = torch.log_softmax(row_logits[-1].double(), dim=0)
+                    out[i]["logprobs"][0] = float(lsm[tokens[0]])
+                    k = min(int(sp["logprobs"]), len(out[i]["top_ids"]))
+                    if k > 0:
+                        top = torch.topk(row_logits[-1].float(), k)
+                        out[i]["top_ids"][:k] = top.indices.numpy()
+                        out[i]["top_logprobs"][:k] = lsm[top.indices].numpy()
+            self.generated.setdefault(slot, []).extend(tokens)
             out[i]["num_tokens"] = len(tokens)
             out[i]["tokens"][:len(tokens)] = tokens
         return out
@@ -186,6 +199,7 @@ class GpuRunner:
                               num_ckpt_slots=args.num_ckpt_slots, tp_rank=rank, tp_size=world, collectives=coll,
                               seed=args.seed, num_spec_tokens=num_spec)
         self.rank = rank
+        self.head = None  # full-distribution sampling head, created on first use
         self.dram = None
         if getattr(args, "dram_kv_blocks", 0):
             from .kv_dram import DramKvArena
@@ -221,9 +235,17 @@ class GpuRunner:
         elif getattr(self, "_sampling_set", False):
             r.clear_sampling()
             self._sampling_set = False
+        qs, pos = plan["query_start"], plan["positions"]
+        starting = [int(plan["seq_slot"][i]) for i in range(n) if qs[i + 1] > qs[i] and int(pos[qs[i]]) == 0]
+        full = sampling_head.needs_full(plan["sampling"], n)
+        if full and self.head is None:
+            self.head = sampling_head.SamplingHead(r)
+        if self.head is not None:
+            self.head.reset(starting)
         if decode_only:
             r.stage(plan["token_ids"], plan["positions"], plan["row_slot"])
             ids = r.decode_step(rows).cpu().numpy()
+            lm_in = (r.buf["xq"], r.buf["xsf"])
         else:
             seq_start = plan["query_start"].tolist()
             r.stage(plan["token_ids"], plan["positions"], plan["row_slot"], seq_start=seq_start)
@@ -231,11 +253,25 @@ class GpuRunner:
             if len(plan["ckpt_row"]):
                 ck = r.checkpoint_args(plan["ckpt_row"], plan["ckpt_slot"], plan["query_start"])
             ids = r.prefill_forward(rows, n, ckpt=ck).cpu().numpy()
+            lm_in = (r.buf["xq_last"], r.last_lm_sf)
+        lp = tids = tlps = None
+        if full:
+            # Top-k / top-p / penalties / logprobs: f32 lm_head over the same normed rows and
+            # the full-distribution sampling kernel.
+            record = [int(plan["sample_row"][i]) >= 0 for i in range(n)]
+            top_n = int(max(0, plan["sampling"]["logprobs"][:n].max()))
+            ids, lp, tids, tlps = self.head.sample(n, lm_in[0], lm_in[1], plan["seq_slot"], plan["sampling"],
+                                                   top_n=top_n, record=record)
         for i in range(n):
             out[i]["req_slot"] = int(plan["seq_slot"][i])
             if int(plan["sample_row"][i]) >= 0:
                 out[i]["num_tokens"] = 1
                 out[i]["tokens"][0] = int(ids[i])
+                if lp is not None:
+                    out[i]["logprobs"][0] = float(lp[i])
+                    k = max(0, int(plan["sampling"]["logprobs"][i]))
+                    out[i]["top_ids"][:k] = tids[i, :k]
+                    out[i]["top_logprobs"][:k] = tlps[i, :k]
         return out
 
     def _execute_spec(self, plan: dict, n: int, out):

@@ -51,14 +51,14 @@ def sample_logits(logits: torch.Tensor, sp, history: list[int] | None = None) ->
     repetition, seed, logprobs)."""
     logits = logits.float().reshape(-1)
     temperature = float(sp["temperature"]) if hasattr(sp, "dtype") or isinstance(sp, dict) else float(sp[0])
+    if history:  # penalties shape greedy and stochastic choices alike
+        logits = apply_penalties(logits, history, float(sp["presence"]), float(sp["frequency"]),
+                                 float(sp["repetition"]))
     if temperature <= 0.0:
         return int(torch.argmax(logits))
     top_p = float(sp["top_p"])
     top_k = int(sp["top_k"])
     seed = int(sp["seed"])
-    if history:
-        logits = apply_penalties(logits, history, float(sp["presence"]), float(sp["frequency"]),
-                                 float(sp["repetition"]))
     logits = logits / temperature
     vals, idx = torch.sort(logits, descending=True, stable=True)
     if top_k > 0:
