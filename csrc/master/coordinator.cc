@@ -203,8 +203,12 @@ void Coordinator::write_plan(const engine::StepPlan& plan, uint8_t* slot, uint64
   write_plan_slot(layout_, plan, slot, step_id);
 }
 
-bool Coordinator::execute(const engine::StepPlan& plan, engine::StepResult* result) {
+bool Coordinator::submit(const engine::StepPlan& plan) {
   if (!launched_ || !error_.empty()) return false;
+  if (inflight_.size() >= (size_t)wire::kPlanSlots) {
+    error_ = "more steps in flight than plan slots";
+    return false;
+  }
   const uint64_t t0 = monotonic_ns();
   const uint64_t step = ++step_id_;
   uint8_t* slot = arena_.base() + layout_.plan_offset + (step % wire::kPlanSlots) * layout_.plan.bytes;
@@ -215,11 +219,18 @@ bool Coordinator::execute(const engine::StepPlan& plan, engine::StepResult* resu
     return false;
   }
   for (auto& e : plan_efd_) e.signal();
+  publish_ns_total += monotonic_ns() - t0;
+  inflight_.push_back(step);
+  return true;
+}
+
+bool Coordinator::collect(engine::StepResult* result) {
+  if (inflight_.empty()) return false;
+  const uint64_t step = inflight_.front();
+  inflight_.pop_front();
   const uint64_t t1 = monotonic_ns();
   if (!wait_all(step, cfg_.step_timeout_ms)) return false;
-  const uint64_t t2 = monotonic_ns();
-  publish_ns_total += t1 - t0;
-  wait_ns_total += t2 - t1;
+  wait_ns_total += monotonic_ns() - t1;
   ++steps;
   const uint8_t* rs = arena_.base() + layout_.result_offset + (step % wire::kResultSlots) * layout_.result.bytes;
   auto rh = reinterpret_cast<const wire::StepResultHeader*>(rs);
@@ -232,6 +243,10 @@ bool Coordinator::execute(const engine::StepPlan& plan, engine::StepResult* resu
   const auto* outs = reinterpret_cast<const wire::SeqStepOutput*>(rs + layout_.result.outputs);
   result->outputs.assign(outs, outs + rh->num_seqs);
   return true;
+}
+
+bool Coordinator::execute(const engine::StepPlan& plan, engine::StepResult* result) {
+  return submit(plan) && collect(result);
 }
 
 void Coordinator::shutdown() {

@@ -12,6 +12,7 @@
 #include <sys/types.h>
 
 #include <map>
+#include <deque>
 #include <string>
 #include <vector>
 
@@ -38,6 +39,10 @@ class Coordinator : public engine::Backend {
   // Create the segment, spawn the workers and wait until all report READY.
   void launch();
   bool execute(const engine::StepPlan& plan, engine::StepResult* result) override;
+  // Publish a step and return; collect() waits for the oldest published step's result.
+  bool submit(const engine::StepPlan& plan) override;
+  bool collect(engine::StepResult* result) override;
+  bool async_capable() const override { return true; }
   std::string error() const override { return error_; }
   void shutdown();
   // Check every worker (alive, no error status, fresh heartbeat while busy).
@@ -60,6 +65,7 @@ class Coordinator : public engine::Backend {
   std::vector<EventFd> plan_efd_, done_efd_;
   std::vector<pid_t> pids_;
   uint64_t step_id_ = 0;
+  std::deque<uint64_t> inflight_;  // published step ids, oldest first
   std::string error_;
   bool launched_ = false;
 };

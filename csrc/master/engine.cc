@@ -29,6 +29,7 @@ struct Engine::Seq {
   bool sampled = false;
   std::vector<std::pair<uint32_t, kv::BlockLease>> promote;  // (node index, checkpoint lease)
   bool first_emitted = false;
+  bool finished = false;        // finished while a later in-flight step still covers it
 };
 
 uint64_t splitmix64(uint64_t& state) {
@@ -152,7 +153,12 @@ bool Engine::cancel(uint64_t id) {
   }
   for (auto& kvp : running_) {
     if (kvp.second->req.id == id) {
-      retire(kvp.second.get());
+      if (!inflight_.empty()) {  // an in-flight step still covers it: retire once that completes
+        kvp.second->finished = true;
+        zombies_.push_back(std::move(kvp.second));
+      } else {
+        retire(kvp.second.get());
+      }
       running_.erase(kvp.first);
       return true;
     }
@@ -160,7 +166,7 @@ bool Engine::cancel(uint64_t id) {
   return false;
 }
 
-bool Engine::has_work() const { return !waiting_.empty() || !running_.empty(); }
+bool Engine::has_work() const { return !waiting_.empty() || !running_.empty() || !inflight_.empty(); }
 
 EngineStats Engine::stats() const {
   EngineStats s = stats_;
@@ -393,6 +399,7 @@ void Engine::stage(StepPlan& p, std::vector<Seq*>& order) {
 
 // ---------------------------------------------------------------------------- step
 std::vector<TokenEvent> Engine::step() {
+  if (cfg_.in_flight_depth > 0 && backend_->async_capable()) return step_async();
   std::vector<TokenEvent> events;
   if (poisoned_) return events;
   while (admit_one()) {
@@ -408,22 +415,37 @@ std::vector<TokenEvent> Engine::step() {
   if (plan_.flags & wire::kFlagDecodeOnly) ++stats_.decode_steps;
   StepResult res;
   if (!backend_->execute(plan_, &res) || res.status != 0 || res.outputs.size() < order.size()) {
-    poisoned_ = true;
-    error_ = backend_->error().empty() ? "worker step failed" : backend_->error();
-    for (auto& kvp : running_) {
-      TokenEvent ev;
-      ev.request_id = kvp.second->req.id;
-      ev.finish = Finish::kError;
-      events.push_back(ev);
-      retire(kvp.second.get());
-    }
-    running_.clear();
+    fail_all(&events);
     return events;
   }
+  process(order, res, &events, false);
+  return events;
+}
+
+void Engine::fail_all(std::vector<TokenEvent>* events) {
+  poisoned_ = true;
+  error_ = backend_->error().empty() ? "worker step failed" : backend_->error();
+  for (auto& kvp : running_) {
+    TokenEvent ev;
+    ev.request_id = kvp.second->req.id;
+    ev.finish = Finish::kError;
+    events->push_back(ev);
+    retire(kvp.second.get());
+  }
+  running_.clear();
+  for (auto& z : zombies_) retire(z.get());
+  zombies_.clear();
+  inflight_.clear();
+}
+
+void Engine::process(std::vector<Seq*>& order, const StepResult& res, std::vector<TokenEvent>* events_out,
+                     bool defer) {
+  std::vector<TokenEvent>& events = *events_out;
   stats_.last_gpu_us = res.gpu_exec_us;
   std::vector<int32_t> done;
   for (size_t i = 0; i < order.size(); ++i) {
     Seq* s = order[i];
+    if (s->finished) continue;  // output of a run-ahead step past the sequence's end
     const wire::SeqStepOutput& out = res.outputs[i];
     // Promote the prefix nodes completed by this step.
     for (auto& pr : s->promote) {
@@ -495,8 +517,88 @@ std::vector<TokenEvent> Engine::step() {
     if (fin != Finish::kNone) done.push_back(s->slot);
   }
   for (int32_t slot : done) {
-    retire(running_.at(slot).get());
-    running_.erase(slot);
+    auto it = running_.find(slot);
+    if (defer) {  // a later in-flight step still reads this slot and its pages
+      it->second->finished = true;
+      zombies_.push_back(std::move(it->second));
+    } else {
+      retire(it->second.get());
+    }
+    running_.erase(it);
+  }
+}
+
+
+// ---------------------------------------------------------------------------- in-flight depth 1
+// While the running set is a stable pure-decode batch, the step after the one in flight
+// is published before the in-flight step's results are processed: its inputs are the
+// tokens the workers just sampled (kept per slot on the worker side, flag DEVICE_TOKENS),
+// so result processing and plan staging here overlap the GPU.  A sequence that finishes
+// in the processed step still appears in the step already published; it is kept (slot
+// and pages reserved) until that step completes and its extra output is dropped.
+bool Engine::can_run_ahead(const Inflight& cur) const {
+  if (!(cur.plan.flags & wire::kFlagDecodeOnly) || !waiting_.empty() || !zombies_.empty()) return false;
+  if (cur.order.size() != running_.size()) return false;
+  for (size_t i = 0; i < cur.order.size(); ++i) {
+    const Seq* s = cur.order[i];
+    if (s->finished || s->rows != 1 || !s->sampled || !s->drafts.empty()) return false;
+    // The step in flight produces token generated + 1; the ahead step token generated + 2.
+    if (s->generated + 2 > s->req.max_tokens || s->tokens.size() + 2 >= cfg_.max_model_len) return false;
+  }
+  return true;
+}
+
+std::vector<TokenEvent> Engine::step_async() {
+  std::vector<TokenEvent> events;
+  if (poisoned_) return events;
+  if (inflight_.empty()) {
+    while (admit_one()) {
+    }
+    if (running_.empty()) return events;
+    std::vector<Seq*> order;
+    stage(plan_, order);
+    if (order.empty()) return events;
+    ++stats_.steps;
+    if (plan_.flags & wire::kFlagDecodeOnly) ++stats_.decode_steps;
+    if (!backend_->submit(plan_)) {
+      fail_all(&events);
+      return events;
+    }
+    inflight_.push_back(Inflight{plan_, order});
+  }
+  if (inflight_.size() == 1 && can_run_ahead(inflight_.front())) {
+    Inflight next{inflight_.front().plan, inflight_.front().order};
+    StepPlan& p = next.plan;
+    p.flags |= wire::kFlagDeviceTokens;
+    for (auto& t : p.token_ids) t = -1;
+    for (auto& x : p.positions) ++x;
+    for (auto& x : p.seq_len) ++x;
+    for (auto& sp : p.sampling) ++sp.seed;  // seed = request seed + generated index
+    p.dirty_rows.clear();
+    p.dirty_pages.clear();
+    p.ckpt_row.clear();
+    p.ckpt_slot.clear();
+    for (auto& r : p.restore_slot) r = -1;
+    ++stats_.steps;
+    ++stats_.decode_steps;
+    ++stats_.run_ahead_steps;
+    if (!backend_->submit(p)) {
+      fail_all(&events);
+      return events;
+    }
+    inflight_.push_back(std::move(next));
+  }
+  StepResult res;
+  Inflight cur = std::move(inflight_.front());
+  inflight_.pop_front();
+  if (!backend_->collect(&res) || res.status != 0 || res.outputs.size() < cur.order.size()) {
+    fail_all(&events);
+    return events;
+  }
+  process(cur.order, res, &events, !inflight_.empty());
+  if (inflight_.empty()) {
+    for (auto& z : zombies_) retire(z.get());
+    zombies_.clear();
   }
   return events;
 }

@@ -92,6 +92,7 @@ struct Config {
   uint32_t dram_blocks = 0;            // host DRAM tier blocks (0: off); needs APC, 1 page per node,
                                        // and a model without recurrent state
   double dram_loading_area = 0.10;     // share of HBM pages kept free for DRAM reloads
+  uint32_t in_flight_depth = 0;        // 1: publish the next decode step before processing this one
 };
 
 // Host-side staged step (the coordinator copies it into a shared-memory plan slot).
@@ -119,6 +120,25 @@ class Backend {
   virtual ~Backend() = default;
   virtual bool execute(const StepPlan& plan, StepResult* result) = 0;
   virtual std::string error() const { return {}; }
+  // Asynchronous pair for in-flight pipelining: publish a step now, collect its result
+  // later (in submission order).  The default runs the step at submit time.
+  virtual bool submit(const StepPlan& plan) {
+    pending_.emplace_back();
+    return execute(plan, &pending_.back());
+  }
+  virtual bool collect(StepResult* result) {
+    if (pending_.empty()) return false;
+    *result = std::move(pending_.front());
+    pending_.pop_front();
+    return true;
+  }
+  // True when submit() returns before the step ran (the engine then runs ahead).
+  virtual bool async_capable() const { return async_; }
+  void set_async(bool on) { async_ = on; }
+
+ protected:
+  std::deque<StepResult> pending_;
+  bool async_ = false;
 };
 
 struct EngineStats {
@@ -132,6 +152,7 @@ struct EngineStats {
   // Host DRAM tier of the prefix cache (zero when off).
   uint64_t dram_capacity = 0, dram_occupied = 0, dram_offloads = 0, dram_reloads = 0, dram_evictions = 0;
   uint64_t dram_hit_tokens = 0;
+  uint64_t run_ahead_steps = 0;  // decode steps published before the previous one was processed
 };
 
 class Engine {
@@ -163,6 +184,14 @@ class Engine {
   void finish(Seq* s, Finish why, std::vector<TokenEvent>* out);
   void retire(Seq* s);
   std::vector<int32_t> ngram_drafts(const Seq& s) const;
+  struct Inflight {
+    StepPlan plan;
+    std::vector<Seq*> order;
+  };
+  void process(std::vector<Seq*>& order, const StepResult& res, std::vector<TokenEvent>* events, bool defer);
+  void fail_all(std::vector<TokenEvent>* events);
+  bool can_run_ahead(const Inflight& cur) const;
+  std::vector<TokenEvent> step_async();
   // Evict LRU prefix leaves until n pages were freed, demoting them to the DRAM tier.
   void evict_pages(size_t n);
   // Run page copies between HBM and the DRAM tier as KvTransfer steps.
@@ -180,6 +209,8 @@ class Engine {
   std::map<uint64_t, uint64_t> waiting_since_;  // request id -> step when queued
   std::vector<int32_t> free_slots_;
   std::map<int32_t, std::unique_ptr<Seq>> running_;  // by request slot
+  std::deque<Inflight> inflight_;                     // published, not yet processed steps
+  std::vector<std::unique_ptr<Seq>> zombies_;         // finished, still covered by an in-flight step
   StepPlan plan_;
   EngineStats stats_;
   bool poisoned_ = false;

@@ -69,6 +69,7 @@ const char* kServeUsage =
     "  --dram-kv-blocks N           Host DRAM tier of the prefix cache, in blocks (default 0 = off;\n"
     "                               attention-only models; implies --apc-node-pages 1)\n"
     "  --dram-loading-area-ratio R  Share of HBM pages kept free for DRAM reloads (default 0.10)\n"
+    "  --in-flight-depth 0|1        Publish the next decode step before processing the current one (default 1)\n"
     "  --max-waiting-requests N     Bounded waiting queue (default 1024)\n"
     "  --prefill-policy srpt|fifo   (default srpt)\n"
     "  --drain-timeout-secs N       SIGTERM drain grace period (default 30)\n"
@@ -124,7 +125,7 @@ const std::set<std::string> kValueFlags = {
     "model-dir", "model", "served-model-name", "host", "port", "api-key", "admin-port", "world-size", "device",
     "max-model-len", "max-seqs", "max-step-tokens", "max-prefill-chunk", "page-block-tokens", "num-kv-pages",
     "tokenizer-mode", "apc-node-pages", "num-ckpt-slots", "dram-kv-blocks", "dram-loading-area-ratio",
-    "micro-steps", "token-counts", "micro-hidden", "micro-features", "micro-experts", "micro-topk", "max-waiting-requests", "prefill-policy",
+    "micro-steps", "token-counts", "in-flight-depth", "micro-hidden", "micro-features", "micro-experts", "micro-topk", "max-waiting-requests", "prefill-policy",
     "drain-timeout-secs", "python", "worker-root", "ready-timeout-secs", "step-timeout-secs", "speculative-method",
     "num-speculative-tokens", "prompt-ids", "prompt", "max-tokens", "verify-greedy-json", "bench-tiers",
     "bench-repeats", "seed", "kv-events-endpoint", "kv-events-topic"};
@@ -237,6 +238,11 @@ bool build_engine(const Args& a, Built* b, std::string* err) {
   c.max_model_len = (uint32_t)a.num("max-model-len", 32768);
   c.prefix_caching = !a.has("no-enable-prefix-caching");
   c.dram_blocks = (uint32_t)a.num("dram-kv-blocks", 0);
+  c.in_flight_depth = (uint32_t)a.num("in-flight-depth", 1);
+  if (c.in_flight_depth > 1) {
+    *err = "--in-flight-depth must be 0 or 1";
+    return false;
+  }
   c.pages_per_node = (uint32_t)a.num("apc-node-pages", c.dram_blocks ? 1 : 8);
   // Attention-only models (the DeepSeek-style family) keep no per-slot recurrent state.
   c.recurrent_state = !attention_only_model(a.get("model", dir));

@@ -262,7 +262,8 @@ PYBIND11_MODULE(_master, m) {
       .def_readwrite("ngram_n", &engine::Config::ngram_n)
       .def_readwrite("kv_hash_seed", &engine::Config::kv_hash_seed)
       .def_readwrite("dram_blocks", &engine::Config::dram_blocks)
-      .def_readwrite("dram_loading_area", &engine::Config::dram_loading_area);
+      .def_readwrite("dram_loading_area", &engine::Config::dram_loading_area)
+      .def_readwrite("in_flight_depth", &engine::Config::in_flight_depth);
   py::class_<engine::EngineStats>(m, "EngineStats")
       .def_readonly("waiting", &engine::EngineStats::waiting)
       .def_readonly("running", &engine::EngineStats::running)
@@ -283,12 +284,15 @@ PYBIND11_MODULE(_master, m) {
       .def_readonly("dram_offloads", &engine::EngineStats::dram_offloads)
       .def_readonly("dram_reloads", &engine::EngineStats::dram_reloads)
       .def_readonly("dram_evictions", &engine::EngineStats::dram_evictions)
-      .def_readonly("dram_hit_tokens", &engine::EngineStats::dram_hit_tokens);
+      .def_readonly("dram_hit_tokens", &engine::EngineStats::dram_hit_tokens)
+      .def_readonly("run_ahead_steps", &engine::EngineStats::run_ahead_steps);
   py::class_<engine::Engine, std::shared_ptr<engine::Engine>>(m, "Engine")
-      .def(py::init([](engine::Config cfg, py::function backend) {
-             return std::make_shared<engine::Engine>(cfg, std::make_shared<PyBackend>(backend));
+      .def(py::init([](engine::Config cfg, py::function backend, bool async_backend) {
+             auto be = std::make_shared<PyBackend>(backend);
+             be->set_async(async_backend);  // tests: let the engine run ahead (steps still run at submit)
+             return std::make_shared<engine::Engine>(cfg, be);
            }),
-           py::arg("config"), py::arg("backend"))
+           py::arg("config"), py::arg("backend"), py::arg("async_backend") = false)
       .def("submit",
            [](engine::Engine& e, uint64_t id, std::vector<int32_t> prompt, uint32_t max_tokens, bool ignore_eos,
               std::vector<int32_t> eos, float temperature, float top_p, int32_t top_k, uint64_t seed) {

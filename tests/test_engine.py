@@ -306,3 +306,49 @@ def test_dram_tier_demotes_and_reloads_prefixes(dram):
         assert st.prefix_hit_tokens > 0
     else:
         assert st.dram_capacity == 0 and not be.transfers
+
+
+class DeviceTokenFake(FakeBackend):
+    """FakeBackend that also serves run-ahead steps: rows flagged DEVICE_TOKENS continue
+    their slot with the last token this backend produced for it."""
+
+    def __init__(self):
+        super().__init__()
+        self.last = {}
+        self.ahead = 0
+
+    def __call__(self, p):
+        if p["flags"] & 2:  # DEVICE_TOKENS
+            self.ahead += 1
+            p = dict(p)
+            p["token_ids"] = [self.last[s] for s in p["row_slot"]]
+        outs = super().__call__(p)
+        for s, o in zip(p["seq_slot"], outs):
+            if o["tokens"]:
+                self.last[s] = o["tokens"][-1]
+        return outs
+
+
+@pytest.mark.parametrize("depth", [0, 1])
+def test_in_flight_depth_one_matches_synchronous(depth):
+    cfg = m.EngineConfig()
+    cfg.max_seqs = 4
+    cfg.max_step_tokens = 64
+    cfg.max_prefill_chunk = 32
+    cfg.page_size = 4
+    cfg.num_pages = 256
+    cfg.max_model_len = 512
+    cfg.in_flight_depth = depth
+    be = DeviceTokenFake()
+    eng = m.Engine(cfg, be, async_backend=True)
+    eos_tok = f(list(range(7)))  # some request will emit it mid-way
+    reqs = {i: ([(i * 31 + j) % V for j in range(3 + 5 * i)], 4 + 3 * i) for i in range(7)}
+    for rid, (p, mt) in reqs.items():
+        assert eng.submit(rid, p, mt, False, [eos_tok])
+    out, done = run(eng)
+    assert done == set(reqs) and not eng.poisoned(), eng.error()
+    for rid, (p, mt) in reqs.items():
+        assert out[rid] == expected(p, mt, eos=(eos_tok,)), rid
+    st = eng.stats()
+    assert (st.run_ahead_steps > 0) == (depth == 1)
+    assert eng.free_slots() == 4

@@ -41,14 +41,16 @@ def prompts(n=8, seed=7, shared=0):
 
 
 @pytest.mark.timeout(600)
-@pytest.mark.parametrize("apc", [False, True])
-def test_tp2_shm_engine_matches_reference(apc):
+@pytest.mark.parametrize("apc,depth", [(False, 0), (True, 0), (True, 1)])
+def test_tp2_shm_engine_matches_reference(apc, depth):
+    """depth 1: decode steps are published one step ahead of result processing; workers
+    continue each slot with the token they sampled (device tokens)."""
     ps = prompts(shared=48 if apc else 0)
     ref = reference_generate(ps, 32)
     eng, coord = launch(model="qwen3.5-tiny", world_size=2, device="cpu", max_seqs=4, max_step_tokens=96,
                         page_size=16, num_pages=256, max_model_len=512, num_ckpt_slots=32 if apc else 0,
                         engine={"max_prefill_chunk": 40, "prefix_caching": apc, "pages_per_node": 1,
-                                "recurrent_state": True})
+                                "recurrent_state": True, "in_flight_depth": depth})
     try:
         for i, p in enumerate(ps):
             assert eng.submit(i, p, 32, True)
@@ -57,6 +59,7 @@ def test_tp2_shm_engine_matches_reference(apc):
             assert out[i] == ref[i], f"request {i} diverged"
         if apc:
             assert eng.stats().prefix_hit_tokens >= 48
+        assert (eng.stats().run_ahead_steps > 0) == (depth == 1)
         # Every page is free or held by a cached prefix node (1 page per node here).
         assert eng.free_pages() + eng.cached_prefix_nodes() == 255 and eng.free_slots() == 4
     finally:

@@ -19,6 +19,8 @@ plan-eventfd wait :442, run :480, report_error :668, main :734).
 from __future__ import annotations
 
 import argparse
+
+import numpy as np
 import gc
 import mmap
 import os
@@ -78,6 +80,7 @@ class WorkerLoop:
         self.geo = wire.Geometry(world_size=sb[3], max_seqs=sb[4], max_step_tokens=sb[5], max_pages_per_seq=sb[6],
                                  page_size=sb[7], vocab_size=sb[8])
         self.view = wire.SegmentView(self.mm, self.geo)
+        self.last_tok = np.zeros(self.geo.max_seqs + 64, dtype=np.int32)  # last sampled token per slot
         self.plan_efd = EventFd(args.plan_fd)
         self.done_efd = EventFd(args.done_fd)
         self._stop = threading.Event()
@@ -129,10 +132,17 @@ class WorkerLoop:
                 break
             self.view.set_worker(self.rank, status=wire.WORKER_RUNNING)
             t0 = time.perf_counter()
+            if plan["flags"] & wire.FLAG_DEVICE_TOKENS:
+                # Run-ahead step: every row continues its slot with the token this worker
+                # sampled for it in the previous step (identical on all ranks).
+                plan["token_ids"] = self.last_tok[plan["row_slot"]]
             try:
                 outputs = self.runner.execute(plan)
             except Exception:  # noqa: BLE001
                 self.fail(ERR_EXCEPTION, f"step {step} failed:\n" + traceback.format_exc())
+            for o in outputs:
+                if o["num_tokens"] > 0:
+                    self.last_tok[o["req_slot"]] = o["tokens"][o["num_tokens"] - 1]
             gpu_us = getattr(self.runner, "last_gpu_us", 0) or int((time.perf_counter() - t0) * 1e6)
             if self.rank == 0:
                 self.view.write_result(step, outputs, 0, gpu_us)
