@@ -69,7 +69,7 @@ const char* kServeUsage =
     "  --dram-kv-blocks N           Host DRAM tier of the prefix cache, in blocks (default 0 = off;\n"
     "                               attention-only models; implies --apc-node-pages 1)\n"
     "  --dram-loading-area-ratio R  Share of HBM pages kept free for DRAM reloads (default 0.10)\n"
-    "  --in-flight-depth 0|1        Publish the next decode step before processing the current one (default 1)\n"
+    "  --in-flight-depth 0|1        Publish the next decode step before processing the current one (default 0)\n"
     "  --max-waiting-requests N     Bounded waiting queue (default 1024)\n"
     "  --prefill-policy srpt|fifo   (default srpt)\n"
     "  --drain-timeout-secs N       SIGTERM drain grace period (default 30)\n"
@@ -238,7 +238,7 @@ bool build_engine(const Args& a, Built* b, std::string* err) {
   c.max_model_len = (uint32_t)a.num("max-model-len", 32768);
   c.prefix_caching = !a.has("no-enable-prefix-caching");
   c.dram_blocks = (uint32_t)a.num("dram-kv-blocks", 0);
-  c.in_flight_depth = (uint32_t)a.num("in-flight-depth", 1);
+  c.in_flight_depth = (uint32_t)a.num("in-flight-depth", 0);
   if (c.in_flight_depth > 1) {
     *err = "--in-flight-depth must be 0 or 1";
     return false;
@@ -565,6 +565,8 @@ json::Value run_tier(engine::Engine& e, const Tier& t, uint64_t seed, int32_t vo
     r.set("shared_prefix_len", t.prefix_len);
     r.set("num_prefixes", t.num_prefixes);
   }
+  r.set("engine_steps", (int64_t)(st1.steps - st0.steps));
+  r.set("run_ahead_steps", (int64_t)(st1.run_ahead_steps - st0.run_ahead_steps));
   const uint64_t steps = st1.spec_verify_steps - st0.spec_verify_steps;
   if (steps > 0) {
     r.set("spec_verify_steps", (int64_t)steps);

@@ -285,7 +285,8 @@ PYBIND11_MODULE(_master, m) {
       .def_readonly("dram_reloads", &engine::EngineStats::dram_reloads)
       .def_readonly("dram_evictions", &engine::EngineStats::dram_evictions)
       .def_readonly("dram_hit_tokens", &engine::EngineStats::dram_hit_tokens)
-      .def_readonly("run_ahead_steps", &engine::EngineStats::run_ahead_steps);
+      .def_readonly("run_ahead_steps", &engine::EngineStats::run_ahead_steps)
+      .def_readonly("last_gpu_us", &engine::EngineStats::last_gpu_us);
   py::class_<engine::Engine, std::shared_ptr<engine::Engine>>(m, "Engine")
       .def(py::init([](engine::Config cfg, py::function backend, bool async_backend) {
              auto be = std::make_shared<PyBackend>(backend);

@@ -24,6 +24,8 @@ def load():
     with _lock:
         if _mod is None:
             try:
+                import torch  # noqa: F401 - loads libc10/libtorch that the extension links against
+
                 mod = importlib.import_module("zstep_b200._C")
                 from ..utils.env import runtime_config
 
