@@ -413,6 +413,74 @@ void allreduce_argmax(int64_t rank, int64_t world, int64_t rows, const std::vect
      "zs_allreduce_argmax");
 }
 
+// Expert-parallel dispatch (which = 0) or combine (which = 1); offs = the six byte
+// offsets of the symmetric block (flags, counts, q, sf, meta, comb).
+void ep_call(int64_t which, int64_t rank, int64_t world, int64_t tokens, int64_t max_tokens, int64_t hidden,
+             int64_t top_k, int64_t num_experts, int64_t recv_cap, int64_t chunk_rows, const Tensor& topk_ids,
+             const Tensor& topk_w, const OptT& x, const std::vector<int64_t>& sym, const std::vector<int64_t>& offs,
+             const Tensor& cnt, const Tensor& pair_slot, const Tensor& bar, const Tensor& epoch,
+             const Tensor& group_count, const Tensor& group_offset, const Tensor& chunk_prefix,
+             const Tensor& recv_rows, const OptT& y, int64_t ldy, const OptT& residual, const OptT& out,
+             const OptT& err, int64_t timeout_ms) {
+  TORCH_CHECK(world >= 1 && world <= EP_MAX_WORLD && (int64_t)sym.size() == world, "bad world ", world,
+              " or symmetric pointer list of ", sym.size());
+  TORCH_CHECK(offs.size() == 6, "offs: flags, counts, q, sf, meta, comb");
+  check_cuda(topk_ids, "topk_ids");
+  TORCH_CHECK(topk_ids.scalar_type() == at::kInt && topk_w.scalar_type() == at::kFloat, "topk ids int32, weights f32");
+  TORCH_CHECK(topk_ids.is_contiguous() && topk_w.is_contiguous(), "topk tensors must be contiguous");
+  EpArgs a{};
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.tokens = (int)tokens;
+  a.max_tokens = (int)max_tokens;
+  a.hidden = (int)hidden;
+  a.top_k = (int)top_k;
+  a.num_experts = (int)num_experts;
+  a.recv_cap = (int)recv_cap;
+  a.chunk_rows = (int)chunk_rows;
+  a.topk_ids = ptr<const int>(topk_ids);
+  a.topk_w = ptr<const float>(topk_w);
+  if (x) {
+    TORCH_CHECK(x->scalar_type() == at::kBFloat16 && x->is_contiguous() && x->size(-1) == hidden, "x: bf16 [tokens, hidden]");
+    a.x = ptr(*x);
+  }
+  for (int r = 0; r < world; ++r) a.sym[r] = reinterpret_cast<char*>(sym[r]);
+  a.off_flags = offs[0];
+  a.off_counts = offs[1];
+  a.off_q = offs[2];
+  a.off_sf = offs[3];
+  a.off_meta = offs[4];
+  a.off_comb = offs[5];
+  a.cnt = ptr<int>(cnt);
+  a.pair_slot = ptr<int>(pair_slot);
+  a.bar = ptr<unsigned long long>(bar);
+  a.epoch = ptr<uint32_t>(epoch);
+  a.group_count = ptr<int>(group_count);
+  a.group_offset = ptr<int>(group_offset);
+  a.chunk_prefix = ptr<int>(chunk_prefix);
+  a.recv_rows = ptr<int>(recv_rows);
+  if (y) {
+    TORCH_CHECK(y->scalar_type() == at::kBFloat16 && y->stride(-1) == 1, "y: bf16 rows");
+    a.y = ptr(*y);
+    a.y_rows = (int)y->size(0);
+  }
+  a.ldy = ldy;
+  if (residual) {
+    TORCH_CHECK(residual->scalar_type() == at::kBFloat16 && residual->is_contiguous(), "residual: bf16 [tokens, hidden]");
+    a.residual = ptr(*residual);
+  }
+  if (out) {
+    TORCH_CHECK(out->scalar_type() == at::kBFloat16 && out->is_contiguous(), "out: bf16 [tokens, hidden]");
+    a.out = ptr(*out);
+  }
+  a.err = optptr<int>(err);
+  a.timeout_ms = (unsigned int)timeout_ms;
+  if (which == 0)
+    rc(zs_ep_dispatch(&a, stream()), "zs_ep_dispatch");
+  else
+    rc(zs_ep_combine(&a, stream()), "zs_ep_combine");
+}
+
 int64_t symm_alloc(int64_t bytes) {
   void* p = nullptr;
   rc(zs_symm_alloc((size_t)bytes, &p), "zs_symm_alloc");
@@ -716,6 +784,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("allreduce_argmax", &allreduce_argmax, py::arg("rank"), py::arg("world"), py::arg("rows"), py::arg("keys"),
         py::arg("flags"), py::arg("epoch"), py::arg("local_keys"), py::arg("id_offset"), py::arg("out_ids"),
         py::arg("out_vals"), py::arg("err"), py::arg("timeout_ms") = 0);
+  m.def("ep_call", &ep_call, py::arg("which"), py::arg("rank"), py::arg("world"), py::arg("tokens"),
+        py::arg("max_tokens"), py::arg("hidden"), py::arg("top_k"), py::arg("num_experts"), py::arg("recv_cap"),
+        py::arg("chunk_rows"), py::arg("topk_ids"), py::arg("topk_w"), py::arg("x"), py::arg("sym"), py::arg("offs"),
+        py::arg("cnt"), py::arg("pair_slot"), py::arg("bar"), py::arg("epoch"), py::arg("group_count"),
+        py::arg("group_offset"), py::arg("chunk_prefix"), py::arg("recv_rows"), py::arg("y"), py::arg("ldy"),
+        py::arg("residual"), py::arg("out"), py::arg("err"), py::arg("timeout_ms") = 0);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_free", [](int64_t p) { rc(zs_symm_free(reinterpret_cast<void*>(p)), "zs_symm_free"); });
   m.def("ipc_handle", &ipc_handle);

@@ -288,6 +288,63 @@ int zs_allreduce_argmax(const ArgmaxArArgs* args, const unsigned long long* loca
                         cudaStream_t stream);
 
 // ----------------------------------------------------------------------------------
+// Expert-parallel MoE all-to-all over NVLink peer memory (ep.cu)
+// ----------------------------------------------------------------------------------
+// Rank r owns the routed experts [r * E / W, (r + 1) * E / W).  Every rank's symmetric
+// block holds (byte offsets below, identical on every rank):
+//   flags  u32 [64]                    arrival words: [0, 8) dispatch, [8, 16) combine (by source)
+//   counts uint2 [W][E]                (pair count, epoch) of every source for every expert
+//   q      e4m3 [recv_cap][hidden]     received rows, grouped by local expert (128-row aligned)
+//   sf     scale atoms of q            tcgen05 block-scale layout of the grouped GEMM
+//   meta   int2 [recv_cap]             (source << 24 | token * top_k + k, weight bits); -1 = padding
+//   comb   bf16 [max_tokens * top_k][hidden]  expert outputs returned to their source
+#define EP_MAX_WORLD 8
+#define EP_MAX_EXPERTS 1024
+
+typedef struct EpArgs {
+  int rank, world;
+  int tokens;                  // local tokens of this call (<= max_tokens, may be 0)
+  int max_tokens;              // per-rank capacity (same on every rank)
+  int hidden;                  // multiple of 512
+  int top_k;                   // <= 16
+  int num_experts;             // global routed experts, a multiple of world, <= EP_MAX_EXPERTS
+  int recv_cap;                // rows of q / meta (multiple of 128)
+  int chunk_rows;              // 32 or 128: work chunk of the consuming grouped GEMM
+  const int* topk_ids;         // [tokens, top_k] global expert ids (-1: no expert)
+  const float* topk_w;         // [tokens, top_k]
+  const void* x;               // bf16 [tokens, hidden]: quantized to MXFP8 on the way out
+  char* sym[EP_MAX_WORLD];     // every rank's symmetric block
+  long long off_flags, off_counts, off_q, off_sf, off_meta, off_comb;
+  // rank-local scratch (zeroed once at allocation; the kernels keep it consistent)
+  int* cnt;                    // [num_experts]
+  int* pair_slot;              // [max_tokens * top_k]
+  unsigned long long* bar;     // grid-barrier counter
+  uint32_t* epoch;             // [2]: dispatch, combine (advanced by the kernels)
+  // dispatch outputs for the local grouped GEMM (the format of zs_moe_route)
+  int* group_count;            // [E / W]
+  int* group_offset;           // [E / W]
+  int* chunk_prefix;           // [E / W + 1]
+  int* recv_rows;              // [1]: padded rows of the grouped buffer
+  // combine
+  const void* y;               // bf16 [y_rows, ldy]: expert outputs in receive order
+  long long ldy;
+  int y_rows;                  // rows of y (a combine with more received rows reports kErrBadShape)
+  const void* residual;        // optional bf16 [tokens, hidden] added to the weighted sum
+  void* out;                   // bf16 [tokens, hidden]
+  int* err;
+  unsigned int timeout_ms;     // bound on every cross-rank wait (0: 5 s)
+} EpArgs;
+
+// Dispatch: MXFP8-quantize each token row once and store it over NVLink into the grouped
+// receive buffer of every rank that owns one of its top-k experts; counts travel first
+// so every sender knows every receiver's segment layout.  Returns when this rank's
+// receive buffer is complete.  One cooperative launch.
+int zs_ep_dispatch(const EpArgs* args, cudaStream_t stream);
+// Combine: return every received row's expert output to its source, then each source
+// sums its tokens' top-k outputs in k order with their routing weights (+ residual).
+int zs_ep_combine(const EpArgs* args, cudaStream_t stream);
+
+// ----------------------------------------------------------------------------------
 // DeepSeek-style layers: mHC, MLA, DSA indexer, MoE combine (deepseek.cu)
 // ----------------------------------------------------------------------------------
 typedef struct MhcPartialArgs {

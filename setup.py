@@ -11,11 +11,35 @@ The stand-alone `zstep` executable is built by zstep_b200/build_native.py.
 """
 
 import os
+import subprocess
 
 from setuptools import setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+
+
+def _links_shared_libstdcxx(cxx: str) -> bool:
+    """True if `cxx` finds a shared libstdc++ (it prints a bare name when it has none)."""
+    try:
+        out = subprocess.run([cxx, "-print-file-name=libstdc++.so"], capture_output=True, text=True,
+                             timeout=30).stdout.strip()
+    except (OSError, subprocess.SubprocessError):
+        return False
+    return os.path.isabs(out) and os.path.exists(out)
+
+
+# A compiler that links libstdc++ statically gives each extension its own copy of the C++
+# stream code next to the process's shared one; torch's error formatting (TORCH_CHECK
+# with numbers) then crashes inside the extension instead of raising.  Prefer a compiler
+# (and nvcc host compiler, via CC) that links the shared libstdc++.
+if not _links_shared_libstdcxx(os.environ.get("CXX", "c++")):
+    for var, name in (("CC", "gcc"), ("CXX", "g++")):
+        for d in ("/usr/bin", "/usr/local/bin"):
+            cand = os.path.join(d, name)
+            if os.path.exists(cand) and (var == "CC" or _links_shared_libstdcxx(cand)):
+                os.environ[var] = cand
+                break
 KDIR = os.path.join("csrc", "kernels")
 MDIR = os.path.join("csrc", "master")
 

@@ -1,5 +1,6 @@
-"""Collective microbenchmark: fused NVLink all-reduce + residual + RMSNorm + MXFP8 and the
-cross-rank argmax, against the NCCL baseline, at hidden 2048 over a range of row counts.
+"""Collective microbenchmark: fused NVLink all-reduce + residual + RMSNorm + MXFP8, the
+cross-rank argmax, and the expert-parallel dispatch / combine all-to-all, against the NCCL
+baseline over a range of row counts.
 
 Run one rank per GPU::
 
@@ -9,7 +10,11 @@ Run one rank per GPU::
 Each case captures `calls` back-to-back calls in one CUDA graph, replays it `reps` times
 between CUDA events and reports the median per call, max over ranks.  Roofline for the
 all-reduce: a two-shot all-reduce moves 2 (W-1)/W * M * H * 2 bytes out of every GPU, so
-the bound is that over the measured 770 GB/s per-direction peer bandwidth.
+the bound is that over the measured 770 GB/s per-direction peer bandwidth.  Expert
+all-to-all (hidden 4096, top-8 of 256 experts, uniform random routing): every pair whose
+expert lives on another rank moves one MXFP8 row (hidden + hidden/32 + 8 bytes) out on
+dispatch and one bf16 row (2 * hidden bytes) back on combine; the NCCL baseline is
+``all_to_all_single`` with per-rank splits (host-synchronised, timed eagerly).
 """
 
 from __future__ import annotations
@@ -101,12 +106,83 @@ def main():
         row["speedup_vs_nccl"] = round(row["nccl_us"] / row["fused_us"], 3)
         results.append(row)
     assert fused.check_error() == 0, fused.check_error()
+    results += bench_ep(rank, world, dev)
     if rank == 0:
         for r in results:
             print(json.dumps(r), flush=True)
     fused.close()
     dist.destroy_process_group()
     del C
+
+
+def _time_eager(body, reps: int) -> float:
+    body()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ts = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        body()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b))
+    t = torch.tensor([statistics.median(ts)], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def bench_ep(rank: int, world: int, dev, H: int = 4096, E: int = 256, K: int = 8,
+             token_counts=(1, 8, 64, 256, 1024, 4096)) -> list[dict]:
+    from .ep import EpAllToAll, NcclEp
+
+    T_max = max(token_counts)
+    # Receive capacity: twice the average load plus every segment's alignment (overflow is
+    # reported, never written past); y covers all of it.
+    ep = EpAllToAll(dev, num_experts=E, hidden=H, top_k=K, max_tokens=T_max, recv_cap=2 * T_max * K + E * 128)
+    nccl = NcclEp(E)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    x_all = torch.randn(T_max, H, device=dev, generator=g).to(torch.bfloat16)
+    ids_all = torch.rand(T_max, E, device=dev, generator=g).topk(K, dim=1).indices.to(torch.int32).contiguous()
+    w_all = torch.rand(T_max, K, device=dev, generator=g).contiguous()
+    y = torch.randn(ep.recv_cap, H, device=dev, dtype=torch.bfloat16)
+    out = torch.empty(T_max, H, dtype=torch.bfloat16, device=dev)
+    results = []
+    for T in token_counts:
+        x, ids, w = x_all[:T], ids_all[:T].contiguous(), w_all[:T].contiguous()
+        remote = int(((ids // (E // world)) != rank).sum())
+        pairs = torch.tensor([remote], device=dev)
+        dist.all_reduce(pairs, op=dist.ReduceOp.MAX)  # the busiest rank bounds the step
+        remote = int(pairs.item())
+        row = {"op": "ep_dispatch_combine", "world": world, "tokens": T, "hidden": H, "experts": E, "top_k": K}
+        calls = 20 if T <= 256 else 5
+        row["fused_dispatch_us"] = round(1000 * _time_graph(lambda: ep.dispatch(x, ids, w), calls, 10), 2)
+        ep.dispatch(x, ids, w)
+        row["fused_combine_us"] = round(1000 * _time_graph(
+            lambda: ep.combine(y, ids, w, out[:T]), calls, 10), 2)
+        if world > 1:
+            xq, xc = mx.quantize(x.float())
+            state = {}
+
+            def nd():
+                state["r"] = nccl.dispatch(xq, xc, ids)
+
+            row["nccl_dispatch_us"] = round(1000 * _time_eager(nd, 10), 2)
+            recv, order, sc, rc = state["r"]
+            yb = torch.randn(recv.shape[0], H, device=dev).to(torch.bfloat16)
+            row["nccl_combine_us"] = round(1000 * _time_eager(lambda: nccl.combine(yb, order, sc, rc, w), 10), 2)
+        d_bytes = remote * (H + H // 32 + 8)
+        c_bytes = remote * 2 * H
+        row["nvlink_bytes_dispatch"] = d_bytes
+        row["nvlink_bytes_combine"] = c_bytes
+        if d_bytes:
+            row["dispatch_frac_of_roofline"] = round(d_bytes / (LINK_GBS * 1e3) / row["fused_dispatch_us"], 4)
+            row["combine_frac_of_roofline"] = round(c_bytes / (LINK_GBS * 1e3) / row["fused_combine_us"], 4)
+        results.append(row)
+    torch.cuda.synchronize()
+    assert ep.check_error() == 0, ep.check_error()
+    ep.close()
+    return results
 
 
 if __name__ == "__main__":
