@@ -175,7 +175,7 @@ void gdn(bool prefill, const Tensor& proj, int64_t num_k_heads, int64_t num_v_he
          const Tensor& slots, const Tensor& positions, int64_t rows, const OptT& out_bf16,
          const OptT& out_q, const OptT& out_sf, const OptT& seq_start, int64_t num_seqs,
          const OptT& ckpt_rows, const OptT& ckpt_slots, int64_t max_ckpt, const OptT& err,
-         const OptT& out_slots = std::nullopt) {
+         const OptT& out_slots = std::nullopt, int64_t impl = 0) {
   check_cuda(proj, "proj");
   check_cuda(ssm_state, "ssm_state");
   check_cuda(conv_state, "conv_state");
@@ -209,6 +209,7 @@ void gdn(bool prefill, const Tensor& proj, int64_t num_k_heads, int64_t num_v_he
   g.max_ckpt = (int)max_ckpt;
   g.err = optptr<int>(err);
   g.out_slots = optptr<const int>(out_slots);
+  g.impl = (int)impl;
   rc(prefill ? zs_gdn_prefill(&g, stream()) : zs_gdn_decode(&g, stream()), "zs_gdn");
 }
 
@@ -828,15 +829,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                           const Tensor& slots, const Tensor& positions, int64_t rows,
                           const OptT& out_bf16, const OptT& out_q, const OptT& out_sf,
                           const Tensor& seq_start, int64_t num_seqs, const OptT& ckpt_rows,
-                          const OptT& ckpt_slots, int64_t max_ckpt, const OptT& err, const OptT& out_slots) {
+                          const OptT& ckpt_slots, int64_t max_ckpt, const OptT& err, const OptT& out_slots,
+                          int64_t impl) {
     gdn(true, proj, hk, hv, conv_w, conv_state, ssm_state, a_log, dt_bias, norm_w, eps, slots,
         positions, rows, out_bf16, out_q, out_sf, seq_start, num_seqs, ckpt_rows, ckpt_slots,
-        max_ckpt, err, out_slots);
+        max_ckpt, err, out_slots, impl);
   }, py::arg("proj"), py::arg("hk"), py::arg("hv"), py::arg("conv_w"), py::arg("conv_state"), py::arg("ssm_state"),
      py::arg("a_log"), py::arg("dt_bias"), py::arg("norm_w"), py::arg("eps"), py::arg("slots"), py::arg("positions"),
      py::arg("rows"), py::arg("out_bf16"), py::arg("out_q"), py::arg("out_sf"), py::arg("seq_start"),
      py::arg("num_seqs"), py::arg("ckpt_rows"), py::arg("ckpt_slots"), py::arg("max_ckpt"), py::arg("err"),
-     py::arg("out_slots") = py::none());
+     py::arg("out_slots") = py::none(), py::arg("impl") = 0);
   m.def("attn_prologue", &attn_prologue);
   m.def("attn_decode", &attn_decode, py::arg("q_out"), py::arg("gate_out"), py::arg("num_q_heads"),
         py::arg("num_kv_heads"), py::arg("k_cache"), py::arg("v_cache"), py::arg("page_size"), py::arg("page_table"),

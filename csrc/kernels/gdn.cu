@@ -263,6 +263,329 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_kernel(const GdnArgs a
   store_window(a, oslot, pos0 + (r1 - r0), kh, vh, s, (vh % ratio) == 0);
 }
 
+// ------------------------------------------------------------------------------------
+// Chunked prefill.  Within a chunk of L <= 64 tokens (cumulative log decay gam_t, state
+// S0 at the chunk start) the delta rule unrolls to
+//     S_t = exp(gam_t) S0 + sum_{i<=t} exp(gam_t - gam_i) u_i k_i^T
+// with pseudo-values u solving the unit lower-triangular system
+//     u_t + sum_{i<t} A[t][i] u_i = beta_t (v_t - exp(gam_t) S0 k_t),
+//     A[t][i] = beta_t exp(gam_t - gam_i) (k_t . k_i),
+// so the chunk's outputs and final state are
+//     o_t = exp(gam_t) S0 q_t + sum_{i<=t} exp(gam_t - gam_i) (q_t . k_i) u_i,
+//     S_L = exp(gam_L) S0 + sum_i exp(gam_L - gam_i) u_i k_i^T.
+// All token-pair terms are dense products over the chunk; only S crosses chunks.  Every
+// exponent is a difference gam_t - gam_i <= 0 (decays), so nothing overflows.
+// The CTA layout matches the token kernel: one CTA per (sequence, value head), the
+// 128 x 128 fp32 state in registers (thread = value row vr, k-quarter kq).  Chunks end
+// early at checkpoint rows so snapshots land on chunk boundaries.
+// ------------------------------------------------------------------------------------
+namespace chunk {
+
+constexpr int C = 64;
+constexpr int RS = 148;  // row stride in floats: four 32-float quarters padded to 36, + 4
+
+// Quarter padding keeps the 16-byte accesses of the four k-quarters of one row, and of
+// eight consecutive rows at one column, in distinct bank groups.
+__device__ __forceinline__ int ix(int t, int d) { return t * RS + (d >> 5) * 36 + (d & 31); }
+
+struct Smem {
+  float q[C * RS];   // normalised, scaled q
+  float k[C * RS];   // normalised k
+  float u[C * RS];   // v -> right-hand side -> pseudo-values
+  float o[C * RS];   // outputs before the gated norm
+  float A[C][C + 1];
+  float P[C][C + 1];
+  float gam[C];
+  float beta[C];
+};
+
+__device__ __forceinline__ float4 ld4(const float* base, int t, int d) {
+  return *reinterpret_cast<const float4*>(base + ix(t, d));
+}
+__device__ __forceinline__ float dot4(const float4& a, const float4& b) {
+  return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+}
+
+__global__ void __launch_bounds__(THREADS, 1) gdn_prefill_chunk_kernel(const GdnArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>(smem_raw);
+  const int seq = blockIdx.x;
+  const int vh = blockIdx.y;
+  const int r0 = a.seq_start[seq], r1 = a.seq_start[seq + 1];
+  if (r0 >= r1) return;
+  const int ratio = a.num_v_heads / a.num_k_heads;
+  const int kh = vh / ratio;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int vr = t >> 2, kq = t & 3;
+  const int slot = a.slots[r0];
+  const int pos0 = a.positions[r0];
+  const bool fresh = pos0 == 0;
+  const __nv_bfloat16* proj = static_cast<const __nv_bfloat16*>(a.proj);
+  const int conv_dim = 2 * a.num_k_heads * DK + a.num_v_heads * DV;
+  const int zoff = 2 * a.num_k_heads * DK + a.num_v_heads * DV;
+  const int boff = zoff + a.num_v_heads * DV;
+  const int aoff = boff + a.num_v_heads;
+
+  float st[32];
+  if (!fresh) {
+    const float* sp = a.ssm_state + (((size_t)slot * a.num_v_heads + vh) * DV + vr) * DK + kq * 32;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 f = reinterpret_cast<const float4*>(sp)[i];
+      st[4 * i] = f.x; st[4 * i + 1] = f.y; st[4 * i + 2] = f.z; st[4 * i + 3] = f.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) st[i] = 0.f;
+  }
+  // Conv channel of threads 0..383 (q | k | v of this head), window in registers.
+  int ch = 0;
+  float w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f, win0 = 0.f, win1 = 0.f, win2 = 0.f;
+  if (t < 2 * DK + DV) {
+    if (t < DK) ch = kh * DK + t;
+    else if (t < 2 * DK) ch = a.num_k_heads * DK + kh * DK + (t - DK);
+    else ch = 2 * a.num_k_heads * DK + vh * DV + (t - 2 * DK);
+    const __nv_bfloat16* w = static_cast<const __nv_bfloat16*>(a.conv_w) + (size_t)ch * 4;
+    w0 = bf(w); w1 = bf(w + 1); w2 = bf(w + 2); w3 = bf(w + 3);
+    if (!fresh) {
+      const __nv_bfloat16* cs = static_cast<const __nv_bfloat16*>(a.conv_state) +
+                                (((size_t)slot * 2 + (pos0 & 1)) * conv_dim + ch) * 3;
+      win0 = bf(cs); win1 = bf(cs + 1); win2 = bf(cs + 2);
+    }
+  }
+  const float decay_rate = -__expf(a.a_log[vh]);
+  const float dtb = a.dt_bias[vh];
+  const bool owns_qk = (vh % ratio) == 0;
+  auto store_win = [&](int dst_slot, int pos) {
+    if (t < 2 * DK + DV && (t >= 2 * DK || owns_qk)) {
+      __nv_bfloat16* cs = static_cast<__nv_bfloat16*>(a.conv_state) +
+                          (((size_t)dst_slot * 2 + (pos & 1)) * conv_dim + ch) * 3;
+      cs[0] = __float2bfloat16_rn(win0);
+      cs[1] = __float2bfloat16_rn(win1);
+      cs[2] = __float2bfloat16_rn(win2);
+    }
+  };
+  auto store_state = [&](int dst_slot) {
+    float* op = a.ssm_state + (((size_t)dst_slot * a.num_v_heads + vh) * DV + vr) * DK + kq * 32;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      reinterpret_cast<float4*>(op)[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
+  };
+
+  int ck = 0;
+  for (int c0 = r0; c0 < r1;) {
+    int c1 = min(r1, c0 + C);
+    if (a.ckpt_rows != nullptr && ck < a.max_ckpt) {
+      const int cr = a.ckpt_rows[seq * a.max_ckpt + ck];
+      if (cr >= c0 && cr < c1 - 1) c1 = cr + 1;
+    }
+    const int L = c1 - c0;
+
+    // 1. conv + SiLU per channel (bf16-rounded like the token kernel); gates per token
+    if (t < 2 * DK + DV) {
+      float* dst = t < DK ? s.q : (t < 2 * DK ? s.k : s.u);
+      const int d = t & (DK - 1);
+      for (int j = 0; j < C; ++j) {
+        float yb = 0.f;
+        if (j < L) {
+          const float x = bf(proj + (size_t)(c0 + j) * a.ld_proj + ch);
+          const float acc = w0 * win0 + w1 * win1 + w2 * win2 + w3 * x;
+          win0 = win1;
+          win1 = win2;
+          win2 = x;
+          yb = __bfloat162float(__float2bfloat16_rn(siluf_(acc)));
+        }
+        dst[ix(j, d)] = yb;
+      }
+    } else if (t < 2 * DK + DV + C) {
+      const int j = t - (2 * DK + DV);
+      float beta = 0.f, lg = 0.f;
+      if (j < L) {
+        const __nv_bfloat16* pr = proj + (size_t)(c0 + j) * a.ld_proj;
+        const float sp_in = bf(pr + aoff + vh) + dtb;
+        const float softplus = sp_in > 20.f ? sp_in : log1pf(__expf(sp_in));
+        beta = sigmoidf_(bf(pr + boff + vh));
+        lg = decay_rate * softplus;
+      }
+      s.beta[j] = beta;
+      s.gam[j] = lg;
+    }
+    __syncthreads();
+
+    // 2. cumulative log decay (warp 0), L2 norms of q and k (a warp per token)
+    if (warp == 0) {
+      float v0 = s.gam[lane], v1 = s.gam[lane + 32];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float n0 = __shfl_up_sync(0xffffffff, v0, o);
+        const float n1 = __shfl_up_sync(0xffffffff, v1, o);
+        if (lane >= o) { v0 += n0; v1 += n1; }
+      }
+      v1 += __shfl_sync(0xffffffff, v0, 31);
+      s.gam[lane] = v0;
+      s.gam[lane + 32] = v1;
+    }
+    for (int j = warp; j < C; j += THREADS / 32) {
+      float4 qv = ld4(s.q, j, lane * 4), kv = ld4(s.k, j, lane * 4);
+      const float sq = warp_sum(dot4(qv, qv));
+      const float sk = warp_sum(dot4(kv, kv));
+      const float fq = rsqrtf(sq + 1e-6f) * rsqrtf((float)DK), fk = rsqrtf(sk + 1e-6f);
+      qv.x *= fq; qv.y *= fq; qv.z *= fq; qv.w *= fq;
+      kv.x *= fk; kv.y *= fk; kv.z *= fk; kv.w *= fk;
+      *reinterpret_cast<float4*>(s.q + ix(j, lane * 4)) = qv;
+      *reinterpret_cast<float4*>(s.k + ix(j, lane * 4)) = kv;
+    }
+    __syncthreads();
+
+    // 3. A (strictly lower) and P (lower incl. diagonal); consecutive threads take
+    //    consecutive key rows i of one query row t
+    for (int p = t; p < C * C; p += THREADS) {
+      const int ti = p >> 6, ii = p & (C - 1);
+      float kk = 0.f, qk = 0.f;
+      if (ii <= ti) {
+#pragma unroll 8
+        for (int d = 0; d < DK; d += 4) {
+          const float4 ki = ld4(s.k, ii, d);
+          kk += dot4(ld4(s.k, ti, d), ki);
+          qk += dot4(ld4(s.q, ti, d), ki);
+        }
+      }
+      const float dec = ii <= ti ? __expf(s.gam[ti] - s.gam[ii]) : 0.f;
+      s.A[ti][ii] = ii < ti ? s.beta[ti] * dec * kk : 0.f;
+      s.P[ti][ii] = dec * qk;
+    }
+    // 4. right-hand side u_j = beta_j (v_j - exp(gam_j) S0 k_j) (reads only q/k/gam/beta)
+    for (int j = 0; j < C; ++j) {
+      float part = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 kv = ld4(s.k, j, kq * 32 + 4 * i);
+        part += st[4 * i] * kv.x + st[4 * i + 1] * kv.y + st[4 * i + 2] * kv.z + st[4 * i + 3] * kv.w;
+      }
+      part += __shfl_xor_sync(0xffffffff, part, 1);
+      part += __shfl_xor_sync(0xffffffff, part, 2);
+      if (kq == 0) {
+        float* u = s.u + ix(j, vr);
+        *u = s.beta[j] * (*u - __expf(s.gam[j]) * part);
+      }
+    }
+    __syncthreads();
+
+    // 5. forward substitution per value column: the four lanes of column vr split the
+    //    i-sum (i = kq mod 4) and meet through shuffles, so no block barrier is needed
+    for (int j = 1; j < L; ++j) {
+      float acc = 0.f;
+      for (int i = kq; i < j; i += 4) acc += s.A[j][i] * s.u[ix(i, vr)];
+      acc += __shfl_xor_sync(0xffffffff, acc, 1);
+      acc += __shfl_xor_sync(0xffffffff, acc, 2);
+      if (kq == 0) s.u[ix(j, vr)] -= acc;
+      __syncwarp();
+    }
+    __syncwarp();
+
+    // 6. outputs: inter-chunk term through S0, then the intra-chunk term (rows j = kq mod 4)
+    for (int j = 0; j < L; ++j) {
+      float part = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 qv = ld4(s.q, j, kq * 32 + 4 * i);
+        part += st[4 * i] * qv.x + st[4 * i + 1] * qv.y + st[4 * i + 2] * qv.z + st[4 * i + 3] * qv.w;
+      }
+      part += __shfl_xor_sync(0xffffffff, part, 1);
+      part += __shfl_xor_sync(0xffffffff, part, 2);
+      if ((j & 3) == kq) s.o[ix(j, vr)] = __expf(s.gam[j]) * part;
+    }
+    for (int j = kq; j < L; j += 4) {
+      float o = s.o[ix(j, vr)];
+      for (int i = 0; i <= j; ++i) o += s.P[j][i] * s.u[ix(i, vr)];
+      s.o[ix(j, vr)] = o;
+    }
+    // 7. carry the state to the chunk end (own 32 coefficients)
+    {
+      const float gl = s.gam[L - 1];
+      const float dl = __expf(gl);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) st[i] *= dl;
+      for (int j = 0; j < L; ++j) {
+        const float w = __expf(gl - s.gam[j]) * s.u[ix(j, vr)];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 kv = ld4(s.k, j, kq * 32 + 4 * i);
+          st[4 * i] += w * kv.x;
+          st[4 * i + 1] += w * kv.y;
+          st[4 * i + 2] += w * kv.z;
+          st[4 * i + 3] += w * kv.w;
+        }
+      }
+    }
+    __syncthreads();
+
+    // 8. gated RMSNorm + output, a warp per token (lane = 4 consecutive columns)
+    const int width = a.num_v_heads * DV;
+    for (int j = warp; j < L; j += THREADS / 32) {
+      const int row = c0 + j;
+      const int d = lane * 4;
+      const float4 ov = ld4(s.o, j, d);
+      const float ss = warp_sum(dot4(ov, ov));
+      const float rstd = rsqrtf(ss / DV + a.eps);
+      const __nv_bfloat16* pr = proj + (size_t)row * a.ld_proj + zoff + vh * DV + d;
+      const __nv_bfloat16* nw = static_cast<const __nv_bfloat16*>(a.norm_w) + d;
+      const float of[4] = {ov.x, ov.y, ov.z, ov.w};
+      float y[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float nrm = __bfloat162float(__float2bfloat16_rn(of[e] * rstd)) * bf(nw + e);
+        y[e] = nrm * siluf_(bf(pr + e));
+      }
+      const int col = vh * DV + d;
+      if (a.out_bf16 != nullptr) {
+        __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(a.out_bf16) + (size_t)row * width + col;
+        __nv_bfloat162 lo = __floats2bfloat162_rn(y[0], y[1]), hi = __floats2bfloat162_rn(y[2], y[3]);
+        uint2 pk;
+        pk.x = *reinterpret_cast<uint32_t*>(&lo);
+        pk.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(ob) = pk;
+      }
+      if (a.out_q != nullptr) {
+        float yb[4], amax = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          yb[e] = __bfloat162float(__float2bfloat16_rn(y[e]));
+          amax = fmaxf(amax, fabsf(yb[e]));
+        }
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffff, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffff, amax, 2));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffff, amax, 4));  // 8 lanes = one 32-column block
+        const uint8_t code = mx_scale_e8m0(amax);
+        const float inv = mx_inv_scale(code);
+        const uint32_t qw = uint32_t(f32_to_e4m3(yb[0] * inv)) | (uint32_t(f32_to_e4m3(yb[1] * inv)) << 8) |
+                            (uint32_t(f32_to_e4m3(yb[2] * inv)) << 16) | (uint32_t(f32_to_e4m3(yb[3] * inv)) << 24);
+        *reinterpret_cast<uint32_t*>(a.out_q + (size_t)row * width + col) = qw;
+        if ((lane & 7) == 0) {
+          const int kb = col >> 5;
+          a.out_sf[((size_t)(row >> 7) * (width >> 7) + (kb >> 2)) * 512 + sf_atom_offset(row & 127, kb & 3)] = code;
+        }
+      }
+    }
+    // 9. checkpoints requested at the chunk's last row
+    while (a.ckpt_rows != nullptr && ck < a.max_ckpt && a.ckpt_rows[seq * a.max_ckpt + ck] == c1 - 1) {
+      const int cslot = a.ckpt_slots[seq * a.max_ckpt + ck];
+      store_state(cslot);
+      store_win(cslot, pos0 + (c1 - r0));
+      ++ck;
+    }
+    c0 = c1;
+    __syncthreads();  // shared tiles are rewritten by the next chunk
+  }
+  const int oslot = a.out_slots != nullptr ? a.out_slots[seq] : slot;
+  store_state(oslot);
+  store_win(oslot, pos0 + (r1 - r0));
+}
+
+}  // namespace chunk
+
 }  // namespace gdn
 }  // namespace zs
 
@@ -273,6 +596,21 @@ extern "C" int zs_gdn_prefill(const GdnArgs* args, cudaStream_t stream) {
     return -1;
   if (a.num_seqs == 0) return 0;
   dim3 grid(a.num_seqs, a.num_v_heads);
-  zs_launch(zs::gdn::gdn_prefill_kernel, grid, zs::gdn::THREADS, 0, stream, a);
+  const bool chunked = a.impl == 2 || (a.impl == 0 && a.rows >= 16 * a.num_seqs);
+  if (chunked) {
+    const int smem = (int)sizeof(zs::gdn::chunk::Smem);
+    static bool attr_set[16] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 16 && !attr_set[dev]) {
+      if (cudaFuncSetAttribute(zs::gdn::chunk::gdn_prefill_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem) != cudaSuccess)
+        return -2;
+      attr_set[dev] = true;
+    }
+    zs_launch(zs::gdn::chunk::gdn_prefill_chunk_kernel, grid, zs::gdn::THREADS, smem, stream, a);
+  } else {
+    zs_launch(zs::gdn::gdn_prefill_kernel, grid, zs::gdn::THREADS, 0, stream, a);
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }

@@ -136,6 +136,8 @@ typedef struct GdnArgs {
   int* err;
   const int* out_slots;    // prefill: optional [num_seqs] slot receiving the final state (and
                            // conv window) instead of the input slot, which stays untouched
+  int impl;                // prefill: 0 = by length (chunked for >= 16 rows per sequence on
+                           // average), 1 = token-sequential, 2 = chunked
 } GdnArgs;
 
 int zs_gdn_decode(const GdnArgs* args, cudaStream_t stream);

@@ -527,9 +527,11 @@ def test_gdn_decode(C):
         torch.testing.assert_close(cs[sl, (p + 1) & 1].cpu().float(), win2, rtol=1e-2, atol=1e-2)
 
 
-def test_gdn_prefill_matches_decode_and_checkpoints(C):
+@pytest.mark.parametrize("impl,lens", [(1, [5, 1, 9]), (2, [5, 1, 9]), (2, [150, 1, 70]), (1, [150, 1, 70])])
+def test_gdn_prefill_matches_decode_and_checkpoints(C, impl, lens):
+    """Token-sequential (impl 1) and chunked (impl 2) prefill against the fp32 per-token
+    reference, with a continued sequence and checkpoints inside and across chunks."""
     hk, hv = 2, 4
-    lens = [5, 1, 9]
     rows = sum(lens)
     s = _gdn_setup(hk, hv, rows, 8, seed=1)
     seq_slots = [2, 4, 6]
@@ -543,14 +545,16 @@ def test_gdn_prefill_matches_decode_and_checkpoints(C):
     ck_rows = torch.full((3, max_ckpt), -1, dtype=torch.int32)
     ck_slots = torch.zeros(3, max_ckpt, dtype=torch.int32)
     ck_rows[0, 0], ck_slots[0, 0] = 2, 7   # after row 2 of seq 0
-    ck_rows[2, 0], ck_slots[2, 0] = 6 + 3, 1  # seq 2 starts at row 6; after its 4th token
+    ck_rows[2, 0], ck_slots[2, 0] = seq_start[2] + 3, 1  # after the 4th token of seq 2
+    if lens[0] > 100:
+        ck_rows[0, 1], ck_slots[0, 1] = 127, 5  # a chunk-aligned checkpoint as well
     cs, ssm = s["conv_state"].cuda(), s["ssm"].cuda()
     out = torch.zeros(rows, hv * 128, dtype=torch.bfloat16, device="cuda")
     C.gdn_prefill(s["proj"].cuda(), hk, hv, s["conv_w"].cuda(), cs, ssm, s["a_log"].cuda(),
                   s["dt_bias"].cuda(), s["norm_w"].cuda(), 1e-6, torch.tensor(slots, dtype=torch.int32).cuda(),
                   torch.tensor(pos, dtype=torch.int32).cuda(), rows, out, None, None,
                   torch.tensor(seq_start, dtype=torch.int32).cuda(), 3, ck_rows.cuda(), ck_slots.cuda(),
-                  max_ckpt, None)
+                  max_ckpt, None, impl=impl)
     torch.cuda.synchronize()
     for si, (sl, st0, ln) in enumerate(zip(seq_slots, starts, lens)):
         win = s["conv_state"][sl, st0 & 1].float() if st0 > 0 else torch.zeros(s["conv_dim"], 3)

@@ -90,7 +90,8 @@ def time_fn(fn, iters=20, warmup=3, flush=False, reps=8) -> float:
     return (total - base) / reps
 
 
-def build_runner(layers: int, batch: int, ctx: int, experts: int = 256, vocab: int = 248320, tp: int = 1):
+def build_runner(layers: int, batch: int, ctx: int, experts: int = 256, vocab: int = 248320, tp: int = 1,
+                 prefill_tokens: int = 0):
     """Runner on one GPU; with tp > 1 it holds rank 0's shard of a tp-way layout and its
     reductions stay local (LocalCollectives), so timings are one rank's compute only."""
     from .config import Qwen35Config
@@ -101,7 +102,8 @@ def build_runner(layers: int, batch: int, ctx: int, experts: int = 256, vocab: i
     cfg = Qwen35Config(num_hidden_layers=layers, layer_types=types, num_experts=experts, vocab_size=vocab)
     page = 16
     pages_per_seq = (ctx + 64 + page - 1) // page
-    r = Qwen35Runner(cfg, max_seqs=batch, max_prefill_tokens=batch, num_pages=batch * pages_per_seq + 1,
+    r = Qwen35Runner(cfg, max_seqs=batch, max_prefill_tokens=max(batch, prefill_tokens),
+                     num_pages=batch * pages_per_seq + 1,
                      page_size=page, max_model_len=ctx + 64, tp_rank=0, tp_size=tp,
                      collectives=LocalCollectives() if tp > 1 else None)
     for s in range(batch):
@@ -138,13 +140,27 @@ def build_ds_runner(layers: int, batch: int, ctx: int, tp: int = 1, expert_forma
 def _runner_for(a):
     if a.model == "deepseek":
         return build_ds_runner(a.layers, a.batch, a.ctx, tp=a.tp)
-    return build_runner(a.layers, a.batch, a.ctx, tp=a.tp)
+    return build_runner(a.layers, a.batch, a.ctx, tp=a.tp, prefill_tokens=a.prefill_seqs * a.ctx)
 
 
 def cmd_breakdown(a):
-    """Per-op device time of one eager decode step (events around every kernel call)."""
+    """Per-op device time of one eager decode step (events around every kernel call); with
+    --prefill-seqs N, of one varlen prefill of N sequences of --ctx tokens instead."""
     r = _runner_for(a)
     real = r.C
+    if a.prefill_seqs:
+        n, L = a.prefill_seqs, a.ctx
+        g = torch.Generator().manual_seed(1)
+        ids = torch.randint(0, r.cfg.vocab_size, (n * L,), generator=g).tolist()
+        pos = [p for _ in range(n) for p in range(L)]
+        slots = [s for s in range(n) for _ in range(L)]
+
+        def step():
+            r.stage(ids, pos, slots, seq_start=[s * L for s in range(n + 1)])
+            r.prefill_forward(n * L, n)
+    else:
+        def step():
+            r.decode_forward(a.batch)
     events = []
 
     class Proxy:
@@ -164,13 +180,13 @@ def cmd_breakdown(a):
             return wrapped
 
     for _ in range(2):
-        r.decode_forward(a.batch)
+        step()
     torch.cuda.synchronize()
     r.C = Proxy()
     events.clear()
     st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     st.record()
-    r.decode_forward(a.batch)
+    step()
     en.record()
     torch.cuda.synchronize()
     r.C = real
@@ -179,11 +195,12 @@ def cmd_breakdown(a):
     for tag, s, e in events:
         tot[tag] += s.elapsed_time(e)
         cnt[tag] += 1
-    step = st.elapsed_time(en)
+    step_ms = st.elapsed_time(en)
     rows = sorted(tot.items(), key=lambda kv: -kv[1])
-    print(f"eager decode step: {step:.3f} ms  (batch {a.batch}, ctx {a.ctx}, layers {a.layers})")
+    kind = f"prefill of {a.prefill_seqs} x {a.ctx} tokens" if a.prefill_seqs else f"decode step (batch {a.batch}, ctx {a.ctx})"
+    print(f"eager {kind}: {step_ms:.3f} ms, layers {a.layers}")
     for tag, ms in rows:
-        print(f"  {ms:8.3f} ms  {100 * ms / step:5.1f}%  x{cnt[tag]:<4d} {tag}")
+        print(f"  {ms:8.3f} ms  {100 * ms / step_ms:5.1f}%  x{cnt[tag]:<4d} {tag}")
 
 
 def cmd_step(a):
@@ -323,6 +340,7 @@ def main():
     ap.add_argument("--layers", type=int, default=40)
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--ctx", type=int, default=1280)
+    ap.add_argument("--prefill-seqs", type=int, default=0, help="breakdown: time a varlen prefill of this many sequences of --ctx tokens")
     ap.add_argument("--eager", type=int, default=0)
     ap.add_argument("--profile-replay", type=int, default=0)
     ap.add_argument("--warmup", type=int, default=2)
