@@ -306,6 +306,30 @@ __device__ __forceinline__ float dot4(const float4& a, const float4& b) {
   return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
 }
 
+// Sums each of p[0..7] over the warp's 32 lanes with 9 shuffles (three halving exchanges,
+// then two butterflies); lane l returns the sum of value (l >> 2) & 7.
+__device__ __forceinline__ float reduce8(const float (&p)[8], int lane) {
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+  float q[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = b4 ? p[i] : p[i + 4];
+    const float keep = b4 ? p[i + 4] : p[i];
+    q[i] = keep + __shfl_xor_sync(0xffffffff, send, 16);
+  }
+  float z[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = b3 ? q[i] : q[i + 2];
+    const float keep = b3 ? q[i + 2] : q[i];
+    z[i] = keep + __shfl_xor_sync(0xffffffff, send, 8);
+  }
+  float y = (b2 ? z[1] : z[0]) + __shfl_xor_sync(0xffffffff, b2 ? z[0] : z[1], 4);
+  y += __shfl_xor_sync(0xffffffff, y, 1);
+  y += __shfl_xor_sync(0xffffffff, y, 2);
+  return y;
+}
+
 __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_chunk_kernel(const GdnArgs a) {
   pdl_wait();
   pdl_trigger();
@@ -318,7 +342,11 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_chunk_kernel(const Gdn
   const int ratio = a.num_v_heads / a.num_k_heads;
   const int kh = vh / ratio;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  // Triangular solve and intra-chunk outputs: column vr, i-residue kq.  State products:
+  // warp w owns value rows 8w..8w+7 (the same rows as its vr columns), lane owns k
+  // columns 4*lane..4*lane+3, so one 16-byte load of a k or q row feeds 32 FMAs.
   const int vr = t >> 2, kq = t & 3;
+  const int row0 = warp * 8;
   const int slot = a.slots[r0];
   const int pos0 = a.positions[r0];
   const bool fresh = pos0 == 0;
@@ -328,13 +356,13 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_chunk_kernel(const Gdn
   const int boff = zoff + a.num_v_heads * DV;
   const int aoff = boff + a.num_v_heads;
 
-  float st[32];
+  float st[32];  // st[4r + c] = S[row0 + r][4 lane + c]
   if (!fresh) {
-    const float* sp = a.ssm_state + (((size_t)slot * a.num_v_heads + vh) * DV + vr) * DK + kq * 32;
+    const float* sp = a.ssm_state + ((size_t)slot * a.num_v_heads + vh) * DV * DK;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 f = reinterpret_cast<const float4*>(sp)[i];
-      st[4 * i] = f.x; st[4 * i + 1] = f.y; st[4 * i + 2] = f.z; st[4 * i + 3] = f.w;
+    for (int r = 0; r < 8; ++r) {
+      const float4 f = *reinterpret_cast<const float4*>(sp + (size_t)(row0 + r) * DK + lane * 4);
+      st[4 * r] = f.x; st[4 * r + 1] = f.y; st[4 * r + 2] = f.z; st[4 * r + 3] = f.w;
     }
   } else {
 #pragma unroll
@@ -368,10 +396,11 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_chunk_kernel(const Gdn
     }
   };
   auto store_state = [&](int dst_slot) {
-    float* op = a.ssm_state + (((size_t)dst_slot * a.num_v_heads + vh) * DV + vr) * DK + kq * 32;
+    float* op = a.ssm_state + ((size_t)dst_slot * a.num_v_heads + vh) * DV * DK;
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      reinterpret_cast<float4*>(op)[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
+    for (int r = 0; r < 8; ++r)
+      *reinterpret_cast<float4*>(op + (size_t)(row0 + r) * DK + lane * 4) =
+          make_float4(st[4 * r], st[4 * r + 1], st[4 * r + 2], st[4 * r + 3]);
   };
 
   int ck = 0;
@@ -387,17 +416,24 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_chunk_kernel(const Gdn
     if (t < 2 * DK + DV) {
       float* dst = t < DK ? s.q : (t < 2 * DK ? s.k : s.u);
       const int d = t & (DK - 1);
-      for (int j = 0; j < C; ++j) {
-        float yb = 0.f;
-        if (j < L) {
-          const float x = bf(proj + (size_t)(c0 + j) * a.ld_proj + ch);
-          const float acc = w0 * win0 + w1 * win1 + w2 * win2 + w3 * x;
-          win0 = win1;
-          win1 = win2;
-          win2 = x;
-          yb = __bfloat162float(__float2bfloat16_rn(siluf_(acc)));
+      const __nv_bfloat16* src = proj + (size_t)c0 * a.ld_proj + ch;
+      for (int j0 = 0; j0 < C; j0 += 16) {
+        float xs[16];  // 16 independent loads in flight before the sequential window update
+#pragma unroll
+        for (int u = 0; u < 16; ++u) xs[u] = j0 + u < L ? bf(src + (size_t)(j0 + u) * a.ld_proj) : 0.f;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          float yb = 0.f;
+          if (j0 + u < L) {
+            const float x = xs[u];
+            const float acc = w0 * win0 + w1 * win1 + w2 * win2 + w3 * x;
+            win0 = win1;
+            win1 = win2;
+            win2 = x;
+            yb = __bfloat162float(__float2bfloat16_rn(siluf_(acc)));
+          }
+          dst[ix(j0 + u, d)] = yb;
         }
-        dst[ix(j, d)] = yb;
       }
     } else if (t < 2 * DK + DV + C) {
       const int j = t - (2 * DK + DV);
@@ -439,36 +475,77 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_chunk_kernel(const Gdn
     }
     __syncthreads();
 
-    // 3. A (strictly lower) and P (lower incl. diagonal); consecutive threads take
-    //    consecutive key rows i of one query row t
-    for (int p = t; p < C * C; p += THREADS) {
-      const int ti = p >> 6, ii = p & (C - 1);
-      float kk = 0.f, qk = 0.f;
-      if (ii <= ti) {
-#pragma unroll 8
-        for (int d = 0; d < DK; d += 4) {
-          const float4 ki = ld4(s.k, ii, d);
-          kk += dot4(ld4(s.k, ti, d), ki);
-          qk += dot4(ld4(s.q, ti, d), ki);
+    // 3. A (strictly lower) and P (lower incl. diagonal) on 4 x 4 tiles of the lower
+    //    triangle: 136 tiles, two adjacent lanes per tile splitting the 128 dims.  Only
+    //    entries with i < t (A) and i <= t (P) are read later.  Warps 0-8 take the tiles;
+    //    the rest go straight on to step 4.
+    if (t < 288) {
+      const int x = t >> 1, half = t & 1;
+      const bool live = x < 136;
+      int bi = (int)((sqrtf(8.f * x + 1.f) - 1.f) * 0.5f);
+      while ((bi + 1) * (bi + 2) / 2 <= x) ++bi;
+      while (bi > 0 && bi * (bi + 1) / 2 > x) --bi;
+      const int bj = x - bi * (bi + 1) / 2;
+      const int ti0 = bi * 4, ii0 = bj * 4;
+      float kk[4][4], qk[4][4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) kk[i][j] = qk[i][j] = 0.f;
+      if (live) {
+        for (int d = half * 64; d < half * 64 + 64; d += 4) {
+          float4 ki[4];
+#pragma unroll
+          for (int b = 0; b < 4; ++b) ki[b] = ld4(s.k, ii0 + b, d);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const float4 kt = ld4(s.k, ti0 + r, d), qt = ld4(s.q, ti0 + r, d);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              kk[r][b] += dot4(kt, ki[b]);
+              qk[r][b] += dot4(qt, ki[b]);
+            }
+          }
         }
       }
-      const float dec = ii <= ti ? __expf(s.gam[ti] - s.gam[ii]) : 0.f;
-      s.A[ti][ii] = ii < ti ? s.beta[ti] * dec * kk : 0.f;
-      s.P[ti][ii] = dec * qk;
-    }
-    // 4. right-hand side u_j = beta_j (v_j - exp(gam_j) S0 k_j) (reads only q/k/gam/beta)
-    for (int j = 0; j < C; ++j) {
-      float part = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 kv = ld4(s.k, j, kq * 32 + 4 * i);
-        part += st[4 * i] * kv.x + st[4 * i + 1] * kv.y + st[4 * i + 2] * kv.z + st[4 * i + 3] * kv.w;
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          kk[r][b] += __shfl_xor_sync(0xffffffff, kk[r][b], 1);
+          qk[r][b] += __shfl_xor_sync(0xffffffff, qk[r][b], 1);
+        }
+      if (live) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const int ti = ti0 + r, ii = ii0 + b;
+            const float dec = ii <= ti ? __expf(s.gam[ti] - s.gam[ii]) : 0.f;
+            if (half == 0) s.A[ti][ii] = ii < ti ? s.beta[ti] * dec * kk[r][b] : 0.f;
+            else s.P[ti][ii] = dec * qk[r][b];
+          }
       }
-      part += __shfl_xor_sync(0xffffffff, part, 1);
-      part += __shfl_xor_sync(0xffffffff, part, 2);
-      if (kq == 0) {
-        float* u = s.u + ix(j, vr);
-        *u = s.beta[j] * (*u - __expf(s.gam[j]) * part);
+    }
+    // 4. through S0: right-hand side u_j = beta_j (v_j - exp(gam_j) S0 k_j) and the
+    //    inter-chunk output term o_j = exp(gam_j) S0 q_j (rows of this warp only)
+    for (int j = 0; j < L; ++j) {
+      const float4 kv = ld4(s.k, j, lane * 4);
+      const float4 qv = ld4(s.q, j, lane * 4);
+      float pk[8], pq[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        pk[r] = st[4 * r] * kv.x + st[4 * r + 1] * kv.y + st[4 * r + 2] * kv.z + st[4 * r + 3] * kv.w;
+        pq[r] = st[4 * r] * qv.x + st[4 * r + 1] * qv.y + st[4 * r + 2] * qv.z + st[4 * r + 3] * qv.w;
+      }
+      const float xk = reduce8(pk, lane);
+      const float xq = reduce8(pq, lane);
+      if ((lane & 3) == 0) {
+        const int v = row0 + ((lane >> 2) & 7);
+        const float e = __expf(s.gam[j]);
+        float* u = s.u + ix(j, v);
+        *u = s.beta[j] * (*u - e * xk);
+        s.o[ix(j, v)] = e * xq;
       }
     }
     __syncthreads();
@@ -485,18 +562,7 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_chunk_kernel(const Gdn
     }
     __syncwarp();
 
-    // 6. outputs: inter-chunk term through S0, then the intra-chunk term (rows j = kq mod 4)
-    for (int j = 0; j < L; ++j) {
-      float part = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 qv = ld4(s.q, j, kq * 32 + 4 * i);
-        part += st[4 * i] * qv.x + st[4 * i + 1] * qv.y + st[4 * i + 2] * qv.z + st[4 * i + 3] * qv.w;
-      }
-      part += __shfl_xor_sync(0xffffffff, part, 1);
-      part += __shfl_xor_sync(0xffffffff, part, 2);
-      if ((j & 3) == kq) s.o[ix(j, vr)] = __expf(s.gam[j]) * part;
-    }
+    // 6. intra-chunk output term (rows j = kq mod 4 of column vr)
     for (int j = kq; j < L; j += 4) {
       float o = s.o[ix(j, vr)];
       for (int i = 0; i <= j; ++i) o += s.P[j][i] * s.u[ix(i, vr)];
@@ -509,14 +575,16 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_chunk_kernel(const Gdn
 #pragma unroll
       for (int i = 0; i < 32; ++i) st[i] *= dl;
       for (int j = 0; j < L; ++j) {
-        const float w = __expf(gl - s.gam[j]) * s.u[ix(j, vr)];
+        const float e = __expf(gl - s.gam[j]);
+        const float4 kv = ld4(s.k, j, lane * 4);
+        const float4 u0 = ld4(s.u, j, row0), u1 = ld4(s.u, j, row0 + 4);
+        const float uw[8] = {u0.x * e, u0.y * e, u0.z * e, u0.w * e, u1.x * e, u1.y * e, u1.z * e, u1.w * e};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 kv = ld4(s.k, j, kq * 32 + 4 * i);
-          st[4 * i] += w * kv.x;
-          st[4 * i + 1] += w * kv.y;
-          st[4 * i + 2] += w * kv.z;
-          st[4 * i + 3] += w * kv.w;
+        for (int r = 0; r < 8; ++r) {
+          st[4 * r] += uw[r] * kv.x;
+          st[4 * r + 1] += uw[r] * kv.y;
+          st[4 * r + 2] += uw[r] * kv.z;
+          st[4 * r + 3] += uw[r] * kv.w;
         }
       }
     }
@@ -524,20 +592,30 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_chunk_kernel(const Gdn
 
     // 8. gated RMSNorm + output, a warp per token (lane = 4 consecutive columns)
     const int width = a.num_v_heads * DV;
-    for (int j = warp; j < L; j += THREADS / 32) {
+    float zg[C / (THREADS / 32)][4];  // gate inputs of this warp's tokens, loaded together
+#pragma unroll
+    for (int u = 0; u < C / (THREADS / 32); ++u) {
+      const int j = warp + u * (THREADS / 32);
+      const __nv_bfloat16* pr = proj + (size_t)(c0 + j) * a.ld_proj + zoff + vh * DV + lane * 4;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) zg[u][e] = j < L ? bf(pr + e) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < C / (THREADS / 32); ++u) {
+      const int j = warp + u * (THREADS / 32);
+      if (j >= L) break;
       const int row = c0 + j;
       const int d = lane * 4;
       const float4 ov = ld4(s.o, j, d);
       const float ss = warp_sum(dot4(ov, ov));
       const float rstd = rsqrtf(ss / DV + a.eps);
-      const __nv_bfloat16* pr = proj + (size_t)row * a.ld_proj + zoff + vh * DV + d;
       const __nv_bfloat16* nw = static_cast<const __nv_bfloat16*>(a.norm_w) + d;
       const float of[4] = {ov.x, ov.y, ov.z, ov.w};
       float y[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float nrm = __bfloat162float(__float2bfloat16_rn(of[e] * rstd)) * bf(nw + e);
-        y[e] = nrm * siluf_(bf(pr + e));
+        y[e] = nrm * siluf_(zg[u][e]);
       }
       const int col = vh * DV + d;
       if (a.out_bf16 != nullptr) {

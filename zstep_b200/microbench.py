@@ -280,6 +280,8 @@ def _pad128_(n):
 
 
 def cmd_gdn(a):
+    if a.prefill_seqs:
+        return _gdn_prefill(a)
     r = build_runner(4, a.m, 64, experts=32, vocab=8192)
     b = r.buf
     L = r.layers[0]
@@ -294,6 +296,30 @@ def cmd_gdn(a):
     pk = peaks()
     print(json.dumps({"op": "gdn_decode", "rows": a.m, "ms": round(ms, 4), "gbs": round(state_bytes / ms / 1e6, 1),
                       "frac_hbm": round(state_bytes / ms / 1e6 / pk["hbm_gbs"], 3), "peaks": pk["src"]}))
+
+
+def _gdn_prefill(a):
+    """Varlen GDN prefill of --prefill-seqs fresh sequences sharing --m rows (--impl 0 auto,
+    1 token-sequential, 2 chunked)."""
+    n = a.prefill_seqs
+    L = a.m // n
+    rows = n * L
+    r = build_runner(4, n, L, experts=32, vocab=8192, prefill_tokens=rows)
+    b = r.buf
+    lay = r.layers[0]
+    r.stage([1] * rows, [p for _ in range(n) for p in range(L)], [s for s in range(n) for _ in range(L)],
+            seq_start=[s * L for s in range(n + 1)])
+    proj = b["proj"][: rows * r.gdn_w].view(rows, r.gdn_w)
+    proj.normal_()
+    midq = r._mid(r.hv * 128)
+    fn = lambda: r.C.gdn_prefill(proj, r.hk, r.hv, lay["conv_w"], r.conv_state[0], r.ssm_state[0],  # noqa
+                                 lay["a_log"], lay["dt_bias"], lay["gnorm"], r.eps, b["in_slot"][:rows],
+                                 b["in_pos"][:rows], rows, None, midq, b["midsf"], b["seq_start"][:n + 1], n,
+                                 None, None, 0, b["err"], None, impl=a.impl)
+    ms = time_fn(fn, flush=True)
+    flops = 2 * 4.2e6 * (rows / 64) * r.hv  # ~4.2M FMAs per 64-token chunk and value head
+    print(json.dumps({"op": "gdn_prefill", "rows": rows, "seqs": n, "impl": a.impl, "ms": round(ms, 4),
+                      "tflops_fp32": round(flops / ms / 1e9, 2)}))
 
 
 def cmd_attn(a):
