@@ -354,9 +354,10 @@ void fused_allreduce_norm(int64_t rank, int64_t world, const Tensor& delta, int6
                           const std::vector<int64_t>& flags, const Tensor& epoch, const Tensor& grid_counter,
                           const Tensor& residual, const Tensor& weight, double w_offset, double eps, int64_t rows,
                           const OptT& normed, const OptT& q, const OptT& sf, const OptT& err,
-                          const OptT& term_index, const OptT& term_scale, int64_t timeout_ms) {
+                          const OptT& term_index, const OptT& term_scale, int64_t timeout_ms,
+                          const std::vector<int64_t>& oneshot) {
   TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)part.size() == world && (int64_t)out.size() == world &&
-                  (int64_t)flags.size() == world,
+                  (int64_t)flags.size() == world && (oneshot.empty() || (int64_t)oneshot.size() == world),
               "bad world / pointer lists");
   check_cuda(delta, "delta");
   check_cuda(residual, "residual");
@@ -388,7 +389,29 @@ void fused_allreduce_norm(int64_t rank, int64_t world, const Tensor& delta, int6
   a.term_index = optptr<const int>(term_index);
   a.term_scale = optptr<const float>(term_scale);
   a.timeout_ms = (unsigned int)timeout_ms;
+  for (size_t r = 0; r < oneshot.size(); ++r) a.oneshot[r] = reinterpret_cast<void*>(oneshot[r]);
   rc(zs_fused_allreduce_norm(&a, stream()), "zs_fused_allreduce_norm");
+}
+
+void allreduce_sum_f32(int64_t rank, int64_t world, const Tensor& data, int64_t rows, int64_t max_rows,
+                       const std::vector<int64_t>& buf, const Tensor& epoch, const Tensor& grid_counter,
+                       const OptT& err, int64_t timeout_ms) {
+  TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)buf.size() == world, "bad world ", world, " / buffer list");
+  check_cuda(data, "data");
+  TORCH_CHECK(data.scalar_type() == at::kFloat && data.dim() == 2, "data: f32 [rows, cols]");
+  SumArArgs a{};
+  a.rank = (int)rank;
+  a.world = (int)world;
+  a.data = ptr<float>(data);
+  a.rows = (int)rows;
+  a.cols = (int)data.size(1);
+  a.max_rows = (int)max_rows;
+  for (int r = 0; r < world; ++r) a.buf[r] = reinterpret_cast<void*>(buf[r]);
+  a.epoch = ptr<uint32_t>(epoch);
+  a.grid_counter = ptr<uint32_t>(grid_counter);
+  a.err = optptr<int>(err);
+  a.timeout_ms = (unsigned int)timeout_ms;
+  rc(zs_allreduce_sum_f32(&a, stream()), "zs_allreduce_sum_f32");
 }
 
 void allreduce_argmax(int64_t rank, int64_t world, int64_t rows, const std::vector<int64_t>& keys,
@@ -781,6 +804,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("flags"), py::arg("epoch"), py::arg("grid_counter"), py::arg("residual"), py::arg("weight"),
         py::arg("w_offset"), py::arg("eps"), py::arg("rows"), py::arg("normed"), py::arg("q"), py::arg("sf"),
         py::arg("err"), py::arg("term_index") = py::none(), py::arg("term_scale") = py::none(),
+        py::arg("timeout_ms") = 0, py::arg("oneshot") = std::vector<int64_t>{});
+  m.def("allreduce_sum_f32", &allreduce_sum_f32, py::arg("rank"), py::arg("world"), py::arg("data"), py::arg("rows"),
+        py::arg("max_rows"), py::arg("buf"), py::arg("epoch"), py::arg("grid_counter"), py::arg("err"),
         py::arg("timeout_ms") = 0);
   m.def("allreduce_argmax", &allreduce_argmax, py::arg("rank"), py::arg("world"), py::arg("rows"), py::arg("keys"),
         py::arg("flags"), py::arg("epoch"), py::arg("local_keys"), py::arg("id_offset"), py::arg("out_ids"),

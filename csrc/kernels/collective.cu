@@ -11,12 +11,20 @@
 // (a counter in device memory advanced by the kernel itself), so there is no separate
 // barrier round trip and the kernel stays CUDA-graph safe.
 //
+// fused_allreduce_norm_small (rows <= 8): one-shot instead of two-shot (one NVLink hop),
+// one 8-CTA cluster per row splitting its columns; the RMSNorm sum of squares is combined
+// through distributed shared memory.
+//
 // allreduce_argmax: per-row packed (logit, ~id) keys of each rank's vocab shard are
 // exchanged the same way and max-reduced, giving the global greedy token on every rank.
+//
+// allreduce_sum_f32: one-shot in-place fp32 sum (the mHC model's sublayer outputs).
 //
 // Reference parity: replaces worker/zstep_worker/kernels_sm120/csrc/shm_allreduce_kernels.cu
 // (shm_v5 all-reduce :472, fused AR + add + RMSNorm :1376, spin-wait with abort :31-83)
 // and the TP=8 argmax exchange (csrc/qwen35_ops_kernels.cu:202).
+#include <cooperative_groups.h>
+
 #include "peer.cuh"
 #include "sm100_common.cuh"
 #include "zs_kernels.h"
@@ -173,6 +181,160 @@ __global__ void __launch_bounds__(THREADS) fused_allreduce_norm_kernel(const Fus
   }
 }
 
+// One-shot fused all-reduce for rows <= FAR_SMALL_ROWS.  Cluster = one row; CTA `part`
+// owns words [part * cw, (part + 1) * cw) of it.  Every rank pushes its local words of
+// the slice to every rank (parity E & 1 of the one-shot buffer, so call E+1 never
+// overwrites words a slower rank still waits for in call E: a rank starts call E+2 only
+// after every rank finished pushing call E+1, i.e. finished reading call E), then sums
+// residual + all ranks' words in rank order, like the two-shot owner does.
+constexpr int SMALL_CTAS = 8;
+
+__global__ void __cluster_dims__(SMALL_CTAS, 1, 1) __launch_bounds__(THREADS)
+    fused_allreduce_norm_small_kernel(const FusedArArgs a) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int H = a.hidden, W = a.world;
+  const int words = H / 2, cw = words / SMALL_CTAS;
+  const int row = blockIdx.x / SMALL_CTAS;
+  const int part = (int)cluster.block_rank();
+  const int tid = threadIdx.x, lane = tid & 31;
+  const uint32_t E = *reinterpret_cast<volatile uint32_t*>(a.epoch) + 1;
+  const int par = E & 1;
+  const uint64_t budget = limit_ns(a.timeout_ms);
+  __shared__ int give_up;
+  __shared__ float red[THREADS / 32];
+  __shared__ float cta_ss, tot_ss;
+  if (tid == 0) give_up = 0;
+  __syncthreads();
+  // The grid always has FAR_SMALL_ROWS clusters (a fixed CTA count keeps the completion
+  // counter a multiple of the grid); clusters past `rows` only count themselves.
+  if (row >= a.rows) {
+    if (tid == 0) {
+      const uint32_t done = atomicAdd(a.grid_counter, 1u) + 1;
+      if (done % gridDim.x == 0) *reinterpret_cast<volatile uint32_t*>(a.epoch) = E;
+    }
+    return;
+  }
+  auto slot = [&](int q, int src, int w) {
+    return static_cast<uint2*>(a.oneshot[q]) + ((((size_t)par * W + src) * FAR_SMALL_ROWS + row) * words + w);
+  };
+  // 1. push
+  for (int w = part * cw + tid; w < (part + 1) * cw; w += THREADS) {
+    const uint32_t v = local_word(a, row, w);
+    for (int q = 0; q < W; ++q) st_ll(slot(q, a.rank, w), v, E);
+  }
+  // 2. reduce (residual first, then ranks in order), write the residual
+  constexpr int MAXW = 4;  // words per thread: hidden <= 8 * 2 * THREADS * MAXW
+  float2 x[MAXW];
+  float ss = 0.f;
+  __nv_bfloat16* res = static_cast<__nv_bfloat16*>(a.residual);
+#pragma unroll
+  for (int i = 0; i < MAXW; ++i) {
+    x[i] = make_float2(0.f, 0.f);
+    const int w = part * cw + tid + i * THREADS;
+    if (w >= (part + 1) * cw) continue;
+    float2 acc = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(res + (size_t)row * H + 2 * w));
+    for (int q = 0; q < W; ++q) {
+      const float2 v = unpack_bf16x2(wait_ll(slot(a.rank, q, w), E, budget, a.err, &give_up));
+      acc.x += v.x;
+      acc.y += v.y;
+    }
+    const uint32_t r = pack_bf16x2(acc.x, acc.y);
+    *reinterpret_cast<uint32_t*>(res + (size_t)row * H + 2 * w) = r;
+    x[i] = unpack_bf16x2(r);
+    ss += x[i].x * x[i].x + x[i].y * x[i].y;
+  }
+  // 3. row sum of squares: CTA partials exchanged through distributed shared memory
+  ss = warp_sum(ss);
+  if (lane == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  if (tid == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < THREADS / 32; ++i) t += red[i];
+    cta_ss = t;
+  }
+  cluster.sync();
+  if (tid == 0) {
+    float t = 0.f;
+    for (int r = 0; r < SMALL_CTAS; ++r) t += *cluster.map_shared_rank(&cta_ss, r);
+    tot_ss = t;
+  }
+  cluster.sync();  // no CTA leaves while a peer may still read its cta_ss
+  const float rstd = rsqrtf(tot_ss / H + a.eps);
+  // 4. RMSNorm + MXFP8 of the slice (16 consecutive threads = one 32-column block)
+  const __nv_bfloat16* wgt = static_cast<const __nv_bfloat16*>(a.weight);
+#pragma unroll
+  for (int i = 0; i < MAXW; ++i) {
+    const int w = part * cw + tid + i * THREADS;
+    if (part * cw + (tid & ~15) + i * THREADS >= (part + 1) * cw) continue;  // whole block outside
+    const bool in = w < (part + 1) * cw;
+    const int c = 2 * w;
+    float y0 = 0.f, y1 = 0.f;
+    if (in) {
+      const float2 wv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(wgt + c));
+      y0 = x[i].x * rstd * (wv.x + a.w_offset);
+      y1 = x[i].y * rstd * (wv.y + a.w_offset);
+      if (a.normed) *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(a.normed) + (size_t)row * H + c) =
+          pack_bf16x2(y0, y1);
+    }
+    if (a.q) {
+      float amax = fmaxf(fabsf(y0), fabsf(y1));
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffff, amax, o));
+      const uint8_t code = mx_scale_e8m0(amax);
+      const float inv = mx_inv_scale(code);
+      if (in) {
+        const uint16_t pk = uint16_t(f32_to_e4m3(y0 * inv)) | (uint16_t(f32_to_e4m3(y1 * inv)) << 8);
+        *reinterpret_cast<uint16_t*>(a.q + (size_t)row * H + c) = pk;
+        if ((tid & 15) == 0) {
+          const int kb = c >> 5;
+          a.sf[((size_t)(row >> 7) * (H >> 7) + (kb >> 2)) * 512 + sf_atom_offset(row & 127, kb & 3)] = code;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const uint32_t done = atomicAdd(a.grid_counter, 1u) + 1;
+    if (done % gridDim.x == 0) *reinterpret_cast<volatile uint32_t*>(a.epoch) = E;
+  }
+}
+
+// One-shot fp32 sum: each thread pushes its elements to every rank, then sums exactly the
+// elements it pushed, so a thread only ever waits for peers.
+__global__ void __launch_bounds__(THREADS) allreduce_sum_f32_kernel(const SumArArgs a) {
+  const int W = a.world;
+  const uint32_t E = *reinterpret_cast<volatile uint32_t*>(a.epoch) + 1;
+  const int par = E & 1;
+  const size_t n = (size_t)a.rows * a.cols;
+  const size_t stride = (size_t)a.max_rows * a.cols;
+  const uint64_t budget = limit_ns(a.timeout_ms);
+  __shared__ int give_up;
+  if (threadIdx.x == 0) give_up = 0;
+  __syncthreads();
+  const size_t step = (size_t)gridDim.x * THREADS;
+  for (size_t i = (size_t)blockIdx.x * THREADS + threadIdx.x; i < n; i += step) {
+    const uint32_t v = __float_as_uint(a.data[i]);
+    for (int q = 0; q < W; ++q)
+      st_ll(static_cast<uint2*>(a.buf[q]) + ((size_t)par * W + a.rank) * stride + i, v, E);
+  }
+  for (size_t i = (size_t)blockIdx.x * THREADS + threadIdx.x; i < n; i += step) {
+    float acc = 0.f;
+    for (int q = 0; q < W; ++q)
+      acc += __uint_as_float(wait_ll(static_cast<const uint2*>(a.buf[a.rank]) + ((size_t)par * W + q) * stride + i, E,
+                                     budget, a.err, &give_up));
+    a.data[i] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t done = atomicAdd(a.grid_counter, 1u) + 1;
+    if (done % gridDim.x == 0) *reinterpret_cast<volatile uint32_t*>(a.epoch) = E;
+  }
+}
+
 // Global argmax over vocab shards: keys[r] = per-row best packed key of rank r's shard
 // (ids already global).  Every rank max-reduces all W keys per row.
 __global__ void allreduce_argmax_kernel(const ArgmaxArArgs a) {
@@ -235,6 +397,17 @@ extern "C" int zs_fused_allreduce_norm(const FusedArArgs* args, cudaStream_t str
   if (a.world < 1 || a.world > 8 || a.hidden % (zs::coll::THREADS * 8) != 0 || a.hidden > zs::coll::THREADS * 8 * 4)
     return -1;
   if (a.rows <= 0) return 0;
+  if (a.oneshot[0] != nullptr && a.rows <= FAR_SMALL_ROWS) {
+    // Slices of whole warps (words per CTA a multiple of 32) keep every shuffle warp-uniform.
+    if ((a.hidden / 2) % zs::coll::SMALL_CTAS != 0 || (a.hidden / 2) / zs::coll::SMALL_CTAS > zs::coll::THREADS * 4 ||
+        ((a.hidden / 2) / zs::coll::SMALL_CTAS) % 32 != 0)
+      return -1;
+    for (int r = 0; r < a.world; ++r)
+      if (a.oneshot[r] == nullptr) return -1;
+    zs::coll::fused_allreduce_norm_small_kernel<<<FAR_SMALL_ROWS * zs::coll::SMALL_CTAS, zs::coll::THREADS, 0, stream>>>(
+        a);
+    return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  }
   // Cooperative launch: the grid barrier needs all FAR_CTAS CTAs co-resident.
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(FAR_CTAS);
@@ -256,6 +429,17 @@ extern "C" int zs_allreduce_argmax(const ArgmaxArArgs* args, const unsigned long
   zs::coll::rebase_keys_kernel<<<(a.rows + 255) / 256, 256, 0, stream>>>(
       local_keys, a.rows, id_offset, static_cast<unsigned long long*>(const_cast<void*>(a.keys[a.rank])));
   zs::coll::allreduce_argmax_kernel<<<1, 256, 0, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+extern "C" int zs_allreduce_sum_f32(const SumArArgs* args, cudaStream_t stream) {
+  const SumArArgs& a = *args;
+  if (a.world < 1 || a.world > 8 || a.rows < 0 || a.rows > a.max_rows || a.cols <= 0) return -1;
+  for (int r = 0; r < a.world; ++r)
+    if (a.buf[r] == nullptr) return -1;
+  if (a.rows == 0) return 0;
+  // A fixed grid keeps the completion counter a multiple of the grid across calls.
+  zs::coll::allreduce_sum_f32_kernel<<<SUM_CTAS, zs::coll::THREADS, 0, stream>>>(a);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 

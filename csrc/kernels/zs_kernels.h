@@ -269,9 +269,34 @@ typedef struct FusedArArgs {
   uint8_t* sf;
   int* err;
   unsigned int timeout_ms;   // bound on every cross-rank wait (0: 5000 ms)
+  // One-shot path for rows <= FAR_SMALL_ROWS (optional): symmetric flag-in-data words
+  // [2 parities][world][FAR_SMALL_ROWS][hidden/2] per rank; one 8-CTA cluster per row
+  // splits the columns and combines the RMSNorm sum of squares through distributed
+  // shared memory.  epoch / grid_counter must then be this path's own counters.
+  void* oneshot[8];
 } FusedArArgs;
 
+#define FAR_SMALL_ROWS 8
+
 int zs_fused_allreduce_norm(const FusedArArgs* args, cudaStream_t stream);
+
+// In-place fp32 sum over ranks of data[rows, cols] (one-shot push over NVLink, summed in
+// rank order so every rank gets the same bits).  buf: symmetric flag-in-data words
+// [2 parities][world][max_rows][cols] per rank.
+typedef struct SumArArgs {
+  int rank, world;
+  float* data;
+  int rows, cols, max_rows;
+  void* buf[8];
+  uint32_t* epoch;
+  uint32_t* grid_counter;
+  int* err;
+  unsigned int timeout_ms;
+} SumArArgs;
+
+#define SUM_CTAS 148  // fixed grid of zs_allreduce_sum_f32
+
+int zs_allreduce_sum_f32(const SumArArgs* args, cudaStream_t stream);
 
 typedef struct ArgmaxArArgs {
   int rank, world, rows;

@@ -28,7 +28,7 @@ def check_allreduce(coll, C, rank, world, dev):
     # Each rank's split-K partials, [terms, R, H] f32 (rank-specific data).
     allp = [torch.randn(terms, R, H, generator=g, device=dev) for _ in range(world)]
     delta = allp[rank].contiguous()
-    for rows in (R, 37, 1):
+    for rows in (R, 37, 1, 5, 8):  # <= 8 rows take the one-shot cluster kernel
         hidden = resid0.clone()
         xq = torch.zeros(128 * ((R + 127) // 128), H, dtype=torch.uint8, device=dev)
         xsf = torch.zeros(mx.atoms_bytes(xq.shape[0], H), dtype=torch.uint8, device=dev)
@@ -85,6 +85,42 @@ def check_graph_replay(coll, rank, world, dev):
     torch.cuda.synchronize()
     assert coll.check_error() == 0
     assert torch.equal(hidden, exp), "graph replay mismatch"
+    del graph
+
+
+def check_allreduce_sum(coll, rank, world, dev):
+    """fp32 in-place sum: the one-shot kernel (<= sum_rows rows, repeated and under graph
+    replay) and the NCCL path above, against the rank-ordered fp32 sum."""
+    H = coll.hidden
+    for rows in (1, 3, coll.sum_rows, coll.sum_rows + 5):
+        g = torch.Generator(device=dev).manual_seed(400 + rows)
+        allx = [torch.randn(rows, H, generator=g, device=dev) for _ in range(world)]
+        for _ in range(3):
+            t = allx[rank].clone()
+            coll.allreduce_sum(t)
+            torch.cuda.synchronize()
+            assert coll.check_error() == 0
+            exp = allx[0].clone()
+            for r in range(1, world):
+                exp = exp + allx[r]
+            torch.testing.assert_close(t, exp, rtol=1e-6, atol=1e-6)
+    t = allx[rank][:3].clone()
+    src = allx[rank][:3].clone()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        t.copy_(src)
+        coll.allreduce_sum(t)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        t.copy_(src)
+        coll.allreduce_sum(t)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    exp = sum(x[:3] for x in allx)
+    torch.testing.assert_close(t, exp, rtol=1e-6, atol=1e-6)
     del graph
 
 
@@ -186,6 +222,7 @@ def main():
         check_allreduce(coll, C, rank, world, dev)
         check_graph_replay(coll, rank, world, dev)
         check_argmax(coll, rank, world, dev)
+        check_allreduce_sum(coll, rank, world, dev)
         what = os.environ.get("ZSTEP_MP_CHECKS", "all")
         if what == "all":
             coll.close()

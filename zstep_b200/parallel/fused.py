@@ -6,6 +6,12 @@ sm_100a kernels in csrc/kernels/collective.cu load and store peer memory directl
 Block layout (all offsets 256-byte aligned)::
 
     [flags: 32 x u32][argmax keys: R x u64][rs words: (R+W) x H/2 x 8 B][ag words: R x H/2 x 8 B]
+    [one-shot words: 2 x W x 8 x H/2 x 8 B][fp32 sum words: 2 x W x S x H x 8 B]
+
+Reductions of at most 8 rows take the one-shot cluster kernel (one NVLink hop instead
+of two; an 8-CTA cluster per row shares the RMSNorm statistics through distributed
+shared memory).  ``allreduce_sum`` (the mHC model's fp32 sublayer outputs) is a one-shot
+push of flag-in-data words for up to S = ``sum_rows`` rows and NCCL above that.
 
 The all-reduce moves "flag-in-data" words (32 bits of payload + the call's epoch in one
 8-byte store), so it needs no separate barrier; flags 16-31 belong to the argmax
@@ -37,7 +43,7 @@ def _up(x: int, a: int = _ALIGN) -> int:
 
 
 class FusedCollectives:
-    def __init__(self, device, group=None, max_rows: int = 0, hidden: int = 0):
+    def __init__(self, device, group=None, max_rows: int = 0, hidden: int = 0, sum_rows: int = 64):
         self.C = _ext.load()
         self.group = group
         self.world = dist.get_world_size(group)
@@ -49,8 +55,9 @@ class FusedCollectives:
         self.hidden = 0
         self._base = 0
         self._peers: list[int] = []
-        self.epoch = torch.zeros(4, dtype=torch.int32, device=self.device)  # [ar, argmax, -, -]
-        self.grid = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.epoch = torch.zeros(4, dtype=torch.int32, device=self.device)  # [ar, argmax, one-shot ar, sum]
+        self.grid = torch.zeros(3, dtype=torch.int32, device=self.device)  # completion counters per kernel
+        self.sum_rows = sum_rows
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.local_keys = None
         self.timeout_ms = runtime_config().coll_timeout_ms  # bound on every cross-rank wait
@@ -73,7 +80,9 @@ class FusedCollectives:
         self.off_keys = _up(32 * 4)
         self.off_part = self.off_keys + _up(R * 8)
         self.off_out = self.off_part + _up((R + self.world) * H * 4)
-        self.nbytes = self.off_out + _up(R * H * 4)
+        self.off_small = self.off_out + _up(R * H * 4)
+        self.off_sum = self.off_small + _up(2 * self.world * 8 * H * 4)
+        self.nbytes = self.off_sum + _up(2 * self.world * self.sum_rows * H * 8)
         with torch.cuda.device(self.device):
             self._base = self.C.symm_alloc(self.nbytes)
             handle = self.C.ipc_handle(self._base)
@@ -87,6 +96,8 @@ class FusedCollectives:
         self.key_ptrs = [p + self.off_keys for p in self._peers]
         self.part_ptrs = [p + self.off_part for p in self._peers]
         self.out_ptrs = [p + self.off_out for p in self._peers]
+        self.small_ptrs = [p + self.off_small for p in self._peers]
+        self.sum_ptrs = [p + self.off_sum for p in self._peers]
         self.local_keys = torch.zeros(R, dtype=torch.int64, device=self.device)
 
     def close(self) -> None:
@@ -118,13 +129,25 @@ class FusedCollectives:
             self.nccl.allreduce_add_rmsnorm(delta, n_terms, row_stride, term_stride, hidden_buf, norm_w, eps, rows,
                                             xq, xsf, term_index=term_index, term_scale=term_scale)
             return
+        if rows <= 8 and (H // 16) % 32 == 0:
+            self.C.fused_allreduce_norm(self.rank, self.world, delta, n_terms, row_stride, term_stride,
+                                        self.part_ptrs, self.out_ptrs, self.flag_ptrs, self.epoch[2:3], self.grid[1:2],
+                                        hidden_buf, norm_w, 1.0, eps, rows, None, xq, xsf, self.err, term_index,
+                                        term_scale, self.timeout_ms, oneshot=self.small_ptrs)
+            return
         self.C.fused_allreduce_norm(self.rank, self.world, delta, n_terms, row_stride, term_stride, self.part_ptrs,
-                                    self.out_ptrs, self.flag_ptrs, self.epoch[0:1], self.grid, hidden_buf, norm_w,
+                                    self.out_ptrs, self.flag_ptrs, self.epoch[0:1], self.grid[0:1], hidden_buf, norm_w,
                                     1.0, eps, rows, None, xq, xsf, self.err, term_index, term_scale,
                                     self.timeout_ms)
 
     def allreduce_sum(self, t: torch.Tensor) -> None:
-        """In-place fp32 sum over ranks (mHC sublayer outputs); NCCL carries it."""
+        """In-place fp32 sum over ranks of t [rows, hidden] (mHC sublayer outputs): one-shot
+        over NVLink up to ``sum_rows`` rows, NCCL above (bandwidth-bound sizes)."""
+        if t.dim() == 2 and t.shape[1] == self.hidden and t.shape[0] <= self.sum_rows and t.dtype == torch.float32 \
+                and t.is_contiguous():
+            self.C.allreduce_sum_f32(self.rank, self.world, t, t.shape[0], self.sum_rows, self.sum_ptrs,
+                                     self.epoch[3:4], self.grid[2:3], self.err, self.timeout_ms)
+            return
         self.nccl.allreduce_sum(t)
 
     def argmax_allreduce(self, keys, rows: int, tiles: int, id_offset: int, out_ids, out_vals) -> None:
