@@ -334,8 +334,8 @@ void Engine::stage(StepPlan& p, std::vector<Seq*>& order) {
       while (s->drafts.size() > room) s->drafts.pop_back();
       const uint32_t left = s->req.max_tokens - s->generated;
       while (!s->drafts.empty() && s->drafts.size() + 1 > left) s->drafts.pop_back();
-    } else if (cfg_.spec_method == "mtp") {
-      // drafts were proposed by the worker in the previous step's result
+    } else if (model_drafts()) {
+      // drafts were proposed by the worker (MTP or DSpark head) in the previous step's result
     } else {
       s->drafts.clear();
     }
@@ -508,7 +508,7 @@ void Engine::process(std::vector<Seq*>& order, const StepResult& res, std::vecto
         break;
       }
     }
-    if (cfg_.spec_method == "mtp") {
+    if (model_drafts()) {
       s->drafts.assign(out.next_drafts, out.next_drafts + std::max(0, std::min<int32_t>(out.num_drafts, wire::kMaxSpecTokens)));
     }
     ev.completion_tokens = s->generated;

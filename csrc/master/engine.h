@@ -85,7 +85,7 @@ struct Config {
   std::string prefill_policy = "fifo"; // "fifo" | "srpt"
   uint32_t starvation_steps = 64;
   uint32_t max_waiting = 4096;
-  std::string spec_method = "none";    // "none" | "ngram" | "mtp"
+  std::string spec_method = "none";    // "none" | "ngram" | "mtp" | "dspark" (last two: drafts from the worker)
   uint32_t num_spec_tokens = 0;
   uint32_t ngram_n = 3;
   std::string kv_hash_seed = "42";
@@ -191,6 +191,8 @@ class Engine {
   void process(std::vector<Seq*>& order, const StepResult& res, std::vector<TokenEvent>* events, bool defer);
   void fail_all(std::vector<TokenEvent>* events);
   bool can_run_ahead(const Inflight& cur) const;
+  // Drafts come from the worker's model head (MTP for Qwen, DSpark for DeepSeek).
+  bool model_drafts() const { return cfg_.spec_method == "mtp" || cfg_.spec_method == "dspark"; }
   std::vector<TokenEvent> step_async();
   // Evict LRU prefix leaves until n pages were freed, demoting them to the DRAM tier.
   void evict_pages(size_t n);

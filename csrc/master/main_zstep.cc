@@ -77,7 +77,7 @@ const char* kServeUsage =
     "  --worker-root PATH           Directory containing the zstep_b200 package\n"
     "  --ready-timeout-secs N       Worker start-up timeout (default 1800)\n"
     "  --step-timeout-secs N        Per-step timeout (default 300)\n"
-    "  --speculative-method none|ngram|mtp\n"
+    "  --speculative-method none|ngram|mtp|dspark\n"
     "  --num-speculative-tokens K   Draft tokens per verify step 1..7\n"
     "  --kv-events-endpoint ADDR    Publish prefix-cache events: tcp://host:port (ZMTP PUB) or file://path\n"
     "  --kv-events-topic TOPIC      Topic of published events (default <served-model-name>/0)\n"
@@ -270,8 +270,8 @@ bool build_engine(const Args& a, Built* b, std::string* err) {
     *err = "--prefill-policy must be srpt or fifo";
     return false;
   }
-  if (c.spec_method != "none" && c.spec_method != "ngram" && c.spec_method != "mtp") {
-    *err = "--speculative-method must be none, ngram or mtp";
+  if (c.spec_method != "none" && c.spec_method != "ngram" && c.spec_method != "mtp" && c.spec_method != "dspark") {
+    *err = "--speculative-method must be none, ngram, mtp or dspark";
     return false;
   }
   if (c.spec_method != "none" && (c.num_spec_tokens < 1 || c.num_spec_tokens > 7)) {

@@ -51,6 +51,28 @@ def test_greedy_and_mtp_agree(model_dir):
     assert any(a == b for a, b in zip(outs["none"], outs["mtp"])), outs
 
 
+def test_deepseek_greedy_and_dspark_agree(model_dir):
+    """DeepSeek-style model with the DSpark draft head: verify steps accept drafts only
+    where they equal the target's greedy tokens, so the output matches plain decoding
+    (leading tokens everywhere, at least one continuation in full: verify rows run the
+    varlen attention path while plain decode runs the split-KV one)."""
+    outs = {}
+    for method in ("none", "dspark"):
+        res = []
+        for p in PROMPTS:
+            args = [BIN, "run", "--model-dir", model_dir, "--model", "deepseek-small", "--device", "cuda",
+                    "--max-seqs", "4", "--max-model-len", "256", "--num-kv-pages", "128", "--max-step-tokens", "128",
+                    "--max-prefill-chunk", "128", "--python", sys.executable, "--worker-root", ROOT,
+                    "--prompt-ids", ",".join(map(str, p)), "--max-tokens", "12", "--speculative-method", method]
+            r = subprocess.run(args, capture_output=True, text=True, timeout=900)
+            assert r.returncode == 0, r.stderr[-3000:]
+            res.append(json.loads(r.stdout.strip().splitlines()[-1])["tokens"])
+        outs[method] = res
+    assert all(len(t) == 12 for t in outs["dspark"])
+    assert all(a[:4] == b[:4] for a, b in zip(outs["none"], outs["dspark"])), outs
+    assert any(a == b for a, b in zip(outs["none"], outs["dspark"])), outs
+
+
 def test_bench_tier_with_mtp_and_shared_prefix(model_dir):
     rep = zstep_run(model_dir, "--speculative-method", "mtp", "--bench-tiers", "mtp:4:8:32:16:64:2")
     run0 = rep["tiers"][0]["runs"][0]

@@ -197,6 +197,18 @@ class DeepSeekConfig:
     expert_format: str = "mxfp4"            # routed and shared experts; everything else MXFP8
     initializer_range: float = 0.02
     name: str = "deepseek-mla-dsa-mhc"
+    # DSpark draft head: target layers whose FFN-site inputs feed it (empty: 1, L/2, L-1),
+    # the rank of its Markov (previous-token) logit correction, and the filler token of
+    # the draft block's non-anchor rows (-1: vocab_size - 1).
+    dspark_aux_layers: tuple = ()
+    dspark_markov_rank: int = 256
+    dspark_noise_token: int = -1
+
+    def dspark_aux(self) -> tuple:
+        if self.dspark_aux_layers:
+            return tuple(self.dspark_aux_layers)
+        L = self.num_hidden_layers
+        return tuple(sorted({min(1, L - 1), L // 2, L - 1}))
 
     @property
     def qk_head_dim(self) -> int:

@@ -107,12 +107,17 @@ class DeepSeekRunner:
         self.k1 = self.top_k + 1
         self.num_slots = max_seqs + 1
         self.dummy_slot = max_seqs
-        self.num_spec = 0
+        self.num_spec = num_spec_tokens
         self.spec = None
+        self.spec_slot_base = 0  # no recurrent state: verify needs no spare slots
         src = weights or DeepSeekRandomWeights(cfg, seed=seed)
         self._load_weights(src)
         self._alloc_state()
         self._alloc_buffers()
+        if self.num_spec:
+            from .deepseek_spark import DSparkDrafter
+
+            self.spec = DSparkDrafter(self, src)
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
 
     # ------------------------------------------------------------------ weights
@@ -121,42 +126,51 @@ class DeepSeekRunner:
         get = lambda n: src.get(n, dev)  # noqa: E731
         f32 = lambda n: get(n).float().contiguous()  # noqa: E731
         bf = lambda n: get(n).to(torch.bfloat16).contiguous()  # noqa: E731
-        H, hl = c.hidden_size, self.hl
         self.embed = bf("embed")
         self.final_norm = bf("final_norm")
         vs = c.vocab_size // tp
         self.vocab_local = vs
         self.lm_head = pack_linear(get("lm_head")[r * vs:(r + 1) * vs], C)
         self.hc_head = (f32("hc_head.fn"), f32("hc_head.base"), f32("hc_head.scale"))
-        nope, vd, qk = c.qk_nope_head_dim, c.v_head_dim, c.qk_head_dim
         self.layers = []
         for i in range(c.num_hidden_layers):
             p = f"layers.{i}."
-            L = {"attn_norm": bf(p + "attn_norm"), "ffn_norm": bf(p + "ffn_norm"),
-                 "hc_attn": (f32(p + "hc_attn.fn"), f32(p + "hc_attn.base"), f32(p + "hc_attn.scale")),
+            L = {"hc_attn": (f32(p + "hc_attn.fn"), f32(p + "hc_attn.base"), f32(p + "hc_attn.scale")),
                  "hc_ffn": (f32(p + "hc_ffn.fn"), f32(p + "hc_ffn.base"), f32(p + "hc_ffn.scale"))}
-            L["proj_a"] = pack_linear(torch.cat([get(p + "mla.q_a"), get(p + "mla.kv_a"), get(p + "idx.wk"),
-                                                 get(p + "idx.w")], 0), C)
-            q_b = get(p + "mla.q_b")[r * hl * qk:(r + 1) * hl * qk]
-            L["proj_q"] = pack_linear(torch.cat([q_b, get(p + "idx.wq")], 0), C)
-            L["q_a_norm"], L["kv_a_norm"], L["idx_k_norm"] = bf(p + "mla.q_a_norm"), bf(p + "mla.kv_a_norm"), \
-                bf(p + "idx.k_norm")
-            kv_b = get(p + "mla.kv_b").reshape(c.num_attention_heads, nope + vd, c.kv_lora_rank)[r * hl:(r + 1) * hl]
-            L["w_uk"] = kv_b[:, :nope].to(torch.bfloat16).contiguous()                   # [hl, nope, kl]
-            L["w_uv_t"] = kv_b[:, nope:].transpose(1, 2).to(torch.bfloat16).contiguous()  # [hl, kl, v]
-            L["o_proj"] = pack_linear(get(p + "mla.o_proj")[:, r * hl * vd:(r + 1) * hl * vd].contiguous(), C)
-            if c.is_dense(i):
-                Fl = c.intermediate_size // tp
-                sl = slice(r * Fl, (r + 1) * Fl)
-                L["dense"] = True
-                L["gate_up"] = pack_linear(interleave_gate_up(get(p + "mlp.gate")[sl][None],
-                                                              get(p + "mlp.up")[sl][None]), C)
-                L["down"] = pack_linear(get(p + "mlp.down")[:, sl].contiguous(), C)
-            else:
-                L["dense"] = False
-                L.update(self._load_moe(src, p))
+            L.update(self._load_layer(src, p, c.is_dense(i)))
             self.layers.append(L)
             torch.cuda.synchronize(dev)
+
+    def _load_layer(self, src, p: str, dense: bool) -> dict:
+        """MLA attention (this rank's heads), indexer and FFN (dense slice or local experts)
+        of the layer with name prefix `p`."""
+        c, C, dev, r, tp = self.cfg, self.C, self.dev, self.tp_rank, self.tp
+        get = lambda n: src.get(n, dev)  # noqa: E731
+        bf = lambda n: get(n).to(torch.bfloat16).contiguous()  # noqa: E731
+        hl = self.hl
+        nope, vd, qk = c.qk_nope_head_dim, c.v_head_dim, c.qk_head_dim
+        L = {"attn_norm": bf(p + "attn_norm"), "ffn_norm": bf(p + "ffn_norm")}
+        L["proj_a"] = pack_linear(torch.cat([get(p + "mla.q_a"), get(p + "mla.kv_a"), get(p + "idx.wk"),
+                                             get(p + "idx.w")], 0), C)
+        q_b = get(p + "mla.q_b")[r * hl * qk:(r + 1) * hl * qk]
+        L["proj_q"] = pack_linear(torch.cat([q_b, get(p + "idx.wq")], 0), C)
+        L["q_a_norm"], L["kv_a_norm"], L["idx_k_norm"] = bf(p + "mla.q_a_norm"), bf(p + "mla.kv_a_norm"), \
+            bf(p + "idx.k_norm")
+        kv_b = get(p + "mla.kv_b").reshape(c.num_attention_heads, nope + vd, c.kv_lora_rank)[r * hl:(r + 1) * hl]
+        L["w_uk"] = kv_b[:, :nope].to(torch.bfloat16).contiguous()                   # [hl, nope, kl]
+        L["w_uv_t"] = kv_b[:, nope:].transpose(1, 2).to(torch.bfloat16).contiguous()  # [hl, kl, v]
+        L["o_proj"] = pack_linear(get(p + "mla.o_proj")[:, r * hl * vd:(r + 1) * hl * vd].contiguous(), C)
+        if dense:
+            Fl = c.intermediate_size // tp
+            sl = slice(r * Fl, (r + 1) * Fl)
+            L["dense"] = True
+            L["gate_up"] = pack_linear(interleave_gate_up(get(p + "mlp.gate")[sl][None],
+                                                          get(p + "mlp.up")[sl][None]), C)
+            L["down"] = pack_linear(get(p + "mlp.down")[:, sl].contiguous(), C)
+        else:
+            L["dense"] = False
+            L.update(self._load_moe(src, p))
+        return L
 
     def _load_moe(self, src, p: str) -> dict:
         c, C, dev = self.cfg, self.C, self.dev
@@ -260,7 +274,7 @@ class DeepSeekRunner:
             b["pair_w"] = torch.zeros(R, self.k1, **f32)
         vt = self.lm_head.n_pad // 128
         self.vocab_tiles = vt
-        self.lm_rows = self.max_seqs
+        self.lm_rows = self.max_seqs * (1 + self.num_spec)  # verify steps score every verify row
         b["samp_temp"] = torch.zeros(R, **f32)
         b["samp_seed"] = torch.zeros(R, dtype=torch.int64, device=dev)
         b["samp_pos"] = torch.zeros(R, **i32)
@@ -311,9 +325,12 @@ class DeepSeekRunner:
         b, c = self.buf, self.cfg
         self.C.mhc_partial(b["X"], rows, c.hidden_size, next_fn, 1, y=b["y"], mix_prev=b["mix"], partial=b["hcp"])
 
-    def _attention(self, li: int, L, rows: int, decode: bool) -> None:
+    def _attention(self, li: int, L, rows: int, decode: bool, caches=None) -> None:
+        """MLA + DSA sublayer -> buf["y"] (fp32, reduced over ranks).  `caches` (latent,
+        index) overrides layer li's paged caches (the DSpark head keeps its own)."""
         c, C, b = self.cfg, self.C, self.buf
         hl = self.hl
+        ckv, ik = caches if caches is not None else (self.ckv_cache[li], self.ik_cache[li])
         pos, slot, lens = b["in_pos"][:rows], b["in_slot"][:rows], b["in_len"][:rows]
         proj_a = b["proj_a"][:rows]
         self._gemm(L["proj_a"], b["xq"], b["xsf"], rows, proj_a, self.wa)
@@ -323,12 +340,12 @@ class DeepSeekRunner:
         C.mla_prologue(proj_a, self.off_kva, self.off_ik, self.off_iw, qi, self.off_iq, rows, hl,
                        c.qk_nope_head_dim, c.qk_rope_head_dim, c.kv_lora_rank, c.index_n_heads, c.index_head_dim,
                        L["kv_a_norm"], L["idx_k_norm"], self.eps, c.rope_theta, slot, pos, self.page_table,
-                       self.page_size, self.ckv_cache[li], self.ik_cache[li], b["q_pe"], b["iq"], b["iw"])
+                       self.page_size, ckv, ik, b["q_pe"], b["iq"], b["iw"])
         C.mla_absorb_q(qi, c.qk_head_dim, c.qk_nope_head_dim, L["w_uk"], hl, rows, b["q_lat"])
-        C.dsa_index(b["iq"], b["iw"], self.ik_cache[li], self.page_table, self.page_size, slot, lens, rows,
+        C.dsa_index(b["iq"], b["iw"], ik, self.page_table, self.page_size, slot, lens, rows,
                     c.index_n_heads, c.index_topk, self.max_model_len, b["scores"], b["sel"], b["n_sel"], b["err"])
         splits = self._attn_splits(rows) if decode else 1
-        C.mla_attn(b["q_lat"], b["q_pe"], self.ckv_cache[li], self.page_table, self.page_size, slot, b["sel"],
+        C.mla_attn(b["q_lat"], b["q_pe"], ckv, self.page_table, self.page_size, slot, b["sel"],
                    b["n_sel"], rows, hl, splits, c.qk_head_dim ** -0.5, b["attn_part"])
         C.mla_up(b["attn_part"], rows, hl, splits, L["w_uv_t"], b["o_q"], b["o_sf"])
         self._gemm(L["o_proj"], b["o_q"], b["o_sf"], rows, b["y"], c.hidden_size, EPI_F32)
@@ -362,11 +379,14 @@ class DeepSeekRunner:
         H = c.hidden_size
         C.mhc_partial(b["X"], rows, H, self.layers[0]["hc_attn"][0], 2, ids=b["in_ids"][:rows], embed=self.embed,
                       partial=b["hcp"])
+        aux = {li: j for j, li in enumerate(self.spec.aux)} if self.spec is not None and not decode else {}
         for li, L in enumerate(self.layers):
             self._site(rows, L["hc_attn"], L["attn_norm"])
             self._attention(li, L, rows, decode)
             self._advance(rows, L["hc_ffn"][0])
             self._site(rows, L["hc_ffn"], L["ffn_norm"])
+            if li in aux:
+                self.spec.capture(aux[li], rows)
             self._ffn(L, rows)
             nxt = self.layers[li + 1]["hc_attn"][0] if li + 1 < len(self.layers) else self.hc_head[0]
             self._advance(rows, nxt)

@@ -15,6 +15,9 @@ Canonical names (per layer prefix ``layers.{i}.``):
               moe.down [E, H, I]; moe.shared.gate, moe.shared.up [Is, H]; moe.shared.down [H, Is]
 Globals: embed [V, H]; hc_head.fn [n, n*H], hc_head.base [n], hc_head.scale [1] (fp32);
 final_norm [H]; lm_head [V, H].
+DSpark draft head: dspark.fc [H, a*H] (a = number of auxiliary target layers);
+layers.dspark.* (one dense MLA layer, names as above); dspark.final_norm [H];
+dspark.markov_w1, dspark.markov_w2 [V, r] (r = dspark_markov_rank).
 
 mHC initialisation: the mixing projections start small (scale 0.01) around a base that
 gives pre = post-gate = sigmoid(0) and a residual matrix close to the identity (diagonal
@@ -52,6 +55,9 @@ def shape_of(cfg: DeepSeekConfig, name: str) -> tuple[int, ...]:
         "moe.shared.gate": (Is, H), "moe.shared.up": (Is, H), "moe.shared.down": (H, Is),
         "embed": (cfg.vocab_size, H), "final_norm": (H,), "lm_head": (cfg.vocab_size, H),
         "hc_head.fn": (n, n * H), "hc_head.base": (n,), "hc_head.scale": (1,),
+        "dspark.fc": (H, len(cfg.dspark_aux()) * H), "dspark.final_norm": (H,),
+        "dspark.markov_w1": (cfg.vocab_size, cfg.dspark_markov_rank),
+        "dspark.markov_w2": (cfg.vocab_size, cfg.dspark_markov_rank),
     }
     return table[leaf]
 

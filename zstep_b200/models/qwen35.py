@@ -470,7 +470,7 @@ class Qwen35Runner:
         self._gemm(L["gate_up"], b["xg"], b["xg_sf"], rows, b["act"], I, EPI_SILU, grouped=True, out_sf=b["act_sf"])
         self._gemm(L["down"], b["act"], b["act_sf"], rows, b["moe_y"], cfg.hidden_size, EPI_BF16, grouped=True)
 
-    def _lm_head_argmax(self, rows: int, xq=None, xsf=None, pos=None) -> None:
+    def _lm_head_argmax(self, rows: int, xq=None, xsf=None, pos=None, head=None) -> None:
         if rows > self.lm_rows:
             raise ValueError(f"lm_head over {rows} rows exceeds the {self.lm_rows}-row output buffers")
         """Greedy (temperature 0) or sampled next token of each row: the lm_head GEMM's
@@ -479,7 +479,7 @@ class Qwen35Runner:
         b = self.buf
         xq = b["xq"] if xq is None else xq
         xsf = b["xsf"] if xsf is None else xsf
-        self._gemm(self.lm_head, xq, xsf, rows, b["lm_keys"], self.vocab_tiles, EPI_ARGMAX,
+        self._gemm(self.lm_head if head is None else head, xq, xsf, rows, b["lm_keys"], self.vocab_tiles, EPI_ARGMAX,
                    row_temp=b["samp_temp"], row_seed=b["samp_seed"], row_pos=b["in_pos"] if pos is None else pos,
                    id_offset=self.tp_rank * self.vocab_local, sample_any=b["samp_any"])
         if self.tp > 1:

@@ -172,6 +172,12 @@ class SpecDecoder:
             torch.index_select(hidden_src, 0, hidden_rows, out=self.hid[:n])
         return n
 
+    def catch_up(self, ids, positions, slots, hidden_rows: torch.Tensor) -> None:
+        """Steps without drafting sequences: run the head over the accepted rows so its KV
+        cache stays complete."""
+        self.stage_mtp(ids, positions, slots, hidden_rows, self.r.buf["hidden"])
+        self.mtp(len(ids))
+
     def draft(self, ids, positions, slots, hidden_rows: torch.Tensor, last_of_seq: list[int]) -> list[list[int]]:
         """Catch-up rows (one per accepted target row) then K-1 chained steps.  Returns the K
         drafts of each sequence; `last_of_seq[i]` is the catch-up row of sequence i's newest

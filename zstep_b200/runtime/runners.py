@@ -187,11 +187,11 @@ class GpuRunner:
         self.cfg = _resolve_config(args.model)
         self.dev = torch.device("cuda", torch.cuda.current_device())
         coll = make_collectives(self.dev) if world > 1 else None
-        num_spec = args.num_spec_tokens if args.spec_method == "mtp" else 0
-        if _is_deepseek(self.cfg):
-            if num_spec:
-                raise NotImplementedError("MTP drafts are wired for the Qwen3.5 runner only")
-            num_spec = 0
+        # Model-drafted speculation: the MTP head for Qwen3.5, the DSpark head for DeepSeek.
+        want = "dspark" if _is_deepseek(self.cfg) else "mtp"
+        if args.spec_method in ("mtp", "dspark") and args.spec_method != want:
+            raise ValueError(f"--speculative-method {args.spec_method} does not fit this model (use {want})")
+        num_spec = args.num_spec_tokens if args.spec_method == want else 0
         runner_cls = DeepSeekRunner if _is_deepseek(self.cfg) else Qwen35Runner
         self.r = runner_cls(self.cfg, device=self.dev, weights=_weights(self.cfg, args.model, args.seed),
                               max_seqs=geo.max_seqs, max_prefill_tokens=geo.max_step_tokens,
@@ -350,8 +350,7 @@ class GpuRunner:
                     out[i]["next_drafts"][:len(drafts[k])] = drafts[k]
                     out[i]["num_drafts"] = len(drafts[k])
             else:
-                r.spec.stage_mtp(m_ids, m_pos, m_slot, rows_t, r.buf["hidden"])
-                r.spec.mtp(len(m_ids))
+                r.spec.catch_up(m_ids, m_pos, m_slot, rows_t)
         return out
 
     def close(self) -> None:
