@@ -100,7 +100,7 @@ class DSparkDrafter:
         sf = mx.atoms_from_codes(codes)
         self.fc_sf[:sf.numel()].copy_(sf)
         r._gemm(self.fc, self.fc_q, self.fc_sf, n, self.h, H, EPI_BF16)
-        C.add_rmsnorm_quant(self.h, None, 0, H, H, L["attn_norm"], 0.0, r.eps, n, None, b["xq"], b["xsf"])
+        C.rms_quant(self.h, H, L["attn_norm"], r.eps, n, b["xq"], b["xsf"])
         r.stage([0] * n, positions, slots)
         proj_a = b["proj_a"][:n]
         r._gemm(L["proj_a"], b["xq"], b["xsf"], n, proj_a, r.wa)
@@ -124,15 +124,18 @@ class DSparkDrafter:
             lens += [p + K] * K  # every block row sees the whole block (and the context)
         rows = len(ids)
         r.stage(ids, pos, sl, seq_lens=lens)
-        C.embed_rmsnorm_quant(b["in_ids"][:rows], r.embed, self.h, L["attn_norm"], 0.0, r.eps, rows, None, b["xq"],
-                              b["xsf"])
+        h = self.h[:rows]
+        torch.index_select(r.embed, 0, b["in_ids"][:rows].long(), out=h)
+        C.rms_quant(h, H, L["attn_norm"], r.eps, rows, b["xq"], b["xsf"])
         r._attention(-1, L, rows, False, caches=(self.ckv, self.ik))
-        C.add_rmsnorm_quant(self.h, b["y"], 1, H, H, L["ffn_norm"], 0.0, r.eps, rows, None, b["xq"], b["xsf"])
+        h.copy_(h.float() + b["y"][:rows])  # residual add in fp32, stored bf16
+        C.rms_quant(h, H, L["ffn_norm"], r.eps, rows, b["xq"], b["xsf"])
         Fl = c.intermediate_size // r.tp
         r._gemm(L["gate_up"], b["xq"], b["xsf"], rows, b["act_d"], Fl, EPI_SILU, out_sf=b["act_d_sf"])
         r._gemm(L["down"], b["act_d"], b["act_d_sf"], rows, b["y"], H, EPI_F32)
         r._reduce(rows)
-        C.add_rmsnorm_quant(self.h, b["y"], 1, H, H, self.final_norm, 0.0, r.eps, rows, None, b["xq"], b["xsf"])
+        h.copy_(h.float() + b["y"][:rows])
+        C.rms_quant(h, H, self.final_norm, r.eps, rows, b["xq"], b["xsf"])
         return rows
 
     def _step(self, n: int, k: int, prev: torch.Tensor) -> torch.Tensor:
