@@ -298,8 +298,15 @@ __global__ void __launch_bounds__(THREADS) combine_kernel(const EpArgs a) {
     if (code < 0) continue;
     __nv_bfloat16* dst = comb_of(a, code >> 24) + (size_t)(code & 0xFFFFFF) * H;
     const __nv_bfloat16* src = y + (size_t)i * a.ldy;
-    for (int c = lane * 8; c < H; c += 256)
-      *reinterpret_cast<uint4*>(dst + c) = *reinterpret_cast<const uint4*>(src + c);
+    for (int c0 = lane * 8; c0 < H; c0 += 256 * 8) {  // 8 loads in flight, then 8 stores
+      uint4 buf[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (c0 + u * 256 < H) buf[u] = *reinterpret_cast<const uint4*>(src + c0 + u * 256);
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (c0 + u * 256 < H) *reinterpret_cast<uint4*>(dst + c0 + u * 256) = buf[u];
+    }
   }
   __threadfence_system();
   grid_sync(a.bar, G, budget, a.err, &give_up);
@@ -330,7 +337,17 @@ __global__ void __launch_bounds__(THREADS) combine_kernel(const EpArgs a) {
       my_ok = (e >= 0 && e < NE && a.pair_slot[t * K + lane] >= 0) ? 1 : 0;
       my_w = a.topk_w[t * K + lane];
     }
+    const unsigned okm = __ballot_sync(kFull, my_ok);  // bit k: pair k returned a row
+    float wk[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) wk[k] = __shfl_sync(kFull, my_w, k);
+    const __nv_bfloat16* crow = comb + (size_t)t * K * H;
     for (int c = lane * 8; c < H; c += 256) {
+      // All top-k loads first (uncached: peers wrote them), then the sum in k order.
+      uint4 v[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k)
+        if (k < K && ((okm >> k) & 1u)) v[k] = __ldcv(reinterpret_cast<const uint4*>(crow + (size_t)k * H + c));
       float acc[8];
       if (res != nullptr) {
         unpack8(*reinterpret_cast<const uint4*>(res + (size_t)t * H + c), acc);
@@ -338,14 +355,13 @@ __global__ void __launch_bounds__(THREADS) combine_kernel(const EpArgs a) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[j] = 0.f;
       }
-      for (int k = 0; k < K; ++k) {
-        const int ok = __shfl_sync(kFull, my_ok, k);
-        const float w = __shfl_sync(kFull, my_w, k);
-        if (!ok) continue;
-        float v[8];
-        unpack8(ld_cv_v4(comb + ((size_t)t * K + k) * H + c), v);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] += w * v[j];
+      for (int k = 0; k < 16; ++k) {
+        if (k >= K || !((okm >> k) & 1u)) continue;
+        float f[8];
+        unpack8(v[k], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += wk[k] * f[j];
       }
       *reinterpret_cast<uint4*>(out + (size_t)t * H + c) = pack8(acc);
     }

@@ -322,6 +322,65 @@ def _gdn_prefill(a):
                       "tflops_fp32": round(flops / ms / 1e9, 2)}))
 
 
+def cmd_coll(a):
+    """NVLink collective kernels as one rank on one GPU (peers = this GPU): the one-shot
+    cluster all-reduce + RMSNorm + MXFP8 (8 rows), the fp32 sum (64 rows) and the expert
+    all-to-all dispatch + combine (--m tokens, hidden 4096, top-8 of 256).  With --iters 1
+    every kernel launches exactly once (for a profiler capture); otherwise CUDA-event medians."""
+    import os
+
+    import torch.distributed as dist
+
+    from .ops import mx
+    from .parallel.ep import EpAllToAll
+    from .parallel.fused import FusedCollectives
+
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29613")
+        dist.init_process_group("gloo", rank=0, world_size=1)
+    dev = torch.device("cuda", 0)
+    H = 2048
+    coll = FusedCollectives(dev, max_rows=256, hidden=H)
+    rows = 8
+    delta = (0.01 * torch.randn(rows, H, device=dev)).to(torch.bfloat16)
+    hid = torch.zeros(rows, H, dtype=torch.bfloat16, device=dev)
+    w = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    xq = torch.zeros(128, H, dtype=torch.uint8, device=dev)
+    xsf = torch.zeros(mx.atoms_bytes(128, H), dtype=torch.uint8, device=dev)
+    t = torch.randn(64, H, device=dev)
+    ep = EpAllToAll(dev, num_experts=256, hidden=4096, top_k=8, max_tokens=a.m, recv_cap=2 * a.m * 8 + 256 * 128)
+    x = torch.randn(a.m, 4096, device=dev, dtype=torch.bfloat16)
+    ids = torch.rand(a.m, 256, device=dev).topk(8, dim=1).indices.to(torch.int32).contiguous()
+    wt = torch.rand(a.m, 8, device=dev)
+    y = torch.randn(ep.recv_cap, 4096, device=dev, dtype=torch.bfloat16)
+    out = torch.empty(a.m, 4096, dtype=torch.bfloat16, device=dev)
+    ops = {"allreduce_norm_small_8rows": lambda: coll.allreduce_add_rmsnorm(delta, 1, H, 0, hid, w, 1e-6, rows, xq, xsf),
+           "allreduce_sum_f32_64rows": lambda: coll.allreduce_sum(t),
+           "ep_dispatch": lambda: ep.dispatch(x, ids, wt),
+           "ep_combine": lambda: ep.combine(y, ids, wt, out)}
+    res = {"op": "coll_single_rank", "tokens": a.m}
+    for name, fn in ops.items():
+        if a.iters == 1:
+            fn()
+            continue
+        ts = []
+        for _ in range(a.iters):
+            s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_.record()
+            fn()
+            e_.record()
+            e_.synchronize()
+            ts.append(s_.elapsed_time(e_) * 1000)
+        res[name + "_us"] = round(statistics.median(ts), 2)
+    torch.cuda.synchronize()
+    res["err"] = coll.check_error() | ep.check_error()
+    print(json.dumps(res))
+    ep.close()
+    coll.close()
+    dist.destroy_process_group()
+
+
 def cmd_attn(a):
     r = build_runner(4, a.m, a.ctx, experts=32, vocab=8192)
     b = r.buf
@@ -362,7 +421,7 @@ def cmd_moe(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("cmd", choices=["breakdown", "step", "gemm", "gdn", "attn", "moe"])
+    ap.add_argument("cmd", choices=["breakdown", "step", "gemm", "gdn", "attn", "moe", "coll"])
     ap.add_argument("--layers", type=int, default=40)
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--ctx", type=int, default=1280)
@@ -382,7 +441,7 @@ def main():
     ap.add_argument("--impl", type=int, default=0, help="attn: 0 tensor-core decode, 1 SIMT decode")
     a = ap.parse_args()
     torch.manual_seed(0)
-    {"breakdown": cmd_breakdown, "step": cmd_step, "gemm": cmd_gemm, "gdn": cmd_gdn, "attn": cmd_attn,
+    {"breakdown": cmd_breakdown, "step": cmd_step, "gemm": cmd_gemm, "gdn": cmd_gdn, "attn": cmd_attn, "coll": cmd_coll,
      "moe": cmd_moe}[a.cmd](a)
 
 
