@@ -69,7 +69,7 @@ struct Cfg {
     uint8_t b[STAGES][KT][B_BYTES];
     uint8_t sfa[STAGES][KT][SF_BYTES];
     uint8_t sfb[STAGES][KT][SF_BYTES];
-    float xch[32][64];              // epilogue exchange (gate/up pairing)
+    float xch[32][65];              // epilogue exchange (gate/up pairing, then the transpose)
     unsigned long long red[4][32];  // epilogue exchange (argmax)
     int g_prefix[kMaxGroups + 1];   // grouped mode: chunk prefix, offsets, counts
     int g_offset[kMaxGroups];
@@ -495,23 +495,38 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
             }
             asm volatile("bar.sync 1, 128;" ::: "memory");
             if (q < 2) {
-              const int feat = it.m * 64 + q * 32 + lane;  // intermediate column
-              uint8_t* act = reinterpret_cast<uint8_t*>(p.out);
+              // h = silu(gate) * up for 32 token columns of this lane's feature, written
+              // back over the up values this lane read (own column of the padded tile),
+              // then read transposed: lane L owns token column L and its 32 consecutive
+              // features, so the MXFP8 block maximum needs no shuffles and the row
+              // leaves as two 16-byte stores.
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int col = col0 + j;
-                const float h = siluf_(v[j]) * s.xch[j][q * 32 + lane];
-                const float amax = warp_max(fabsf(h));
-                const uint8_t code = mx_scale_e8m0(amax);
-                if (j < ncols) {
-                  const int row = seg_row0 + col;
-                  act[(size_t)row * p.ldo + feat] = f32_to_e4m3(h * mx_inv_scale(code));
-                  if (lane == 0) {
-                    const int kb = feat >> 5;
-                    uint8_t* sf = p.out_sf + ((size_t)(row >> 7) * (p.ldo >> 7) + (kb >> 2)) * 512;
-                    sf[sf_atom_offset(row & 127, kb & 3)] = code;
-                  }
+              for (int j = 0; j < 32; ++j) s.xch[j][q * 32 + lane] = siluf_(v[j]) * s.xch[j][q * 32 + lane];
+              __syncwarp();
+              if (lane < ncols) {
+                float h[32];
+                float amax = 0.f;
+#pragma unroll
+                for (int f = 0; f < 32; ++f) {
+                  h[f] = s.xch[lane][q * 32 + f];
+                  amax = fmaxf(amax, fabsf(h[f]));
                 }
+                const uint8_t code = mx_scale_e8m0(amax);
+                const float inv = mx_inv_scale(code);
+                uint32_t w8[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  w8[i] = uint32_t(f32_to_e4m3(h[4 * i] * inv)) | (uint32_t(f32_to_e4m3(h[4 * i + 1] * inv)) << 8) |
+                          (uint32_t(f32_to_e4m3(h[4 * i + 2] * inv)) << 16) |
+                          (uint32_t(f32_to_e4m3(h[4 * i + 3] * inv)) << 24);
+                const int row = seg_row0 + col0 + lane;
+                const int feat0 = it.m * 64 + q * 32;  // first intermediate column of the block
+                uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) + (size_t)row * p.ldo + feat0);
+                dst[0] = make_uint4(w8[0], w8[1], w8[2], w8[3]);
+                dst[1] = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+                const int kb = feat0 >> 5;
+                uint8_t* sf = p.out_sf + ((size_t)(row >> 7) * (p.ldo >> 7) + (kb >> 2)) * 512;
+                sf[sf_atom_offset(row & 127, kb & 3)] = code;
               }
             }
             asm volatile("bar.sync 2, 128;" ::: "memory");
@@ -706,6 +721,8 @@ extern "C" int zs_gemm_mxf8(const GemmMxf8Args* args, cudaStream_t stream) {
       (reinterpret_cast<uintptr_t>(p.sfa) & 15) || (reinterpret_cast<uintptr_t>(p.sfb) & 15))
     return -11;
   if (p.b_rows % BM != 0) return -12;
+  // The SiLU epilogue stores 32-byte rows of MXFP8 output.
+  if (p.epi_mode == kEpiSiluQuant && ((p.ldo & 15) || (reinterpret_cast<uintptr_t>(p.out) & 15))) return -23;
   if (p.k_splits > 1 && (p.chunk_prefix != nullptr || p.epi_mode != kEpiStoreF32)) return -16;
   if (p.fix_splits > 1) {
     if (p.k_splits > 1 || p.fix_splits > kMaxFixSplits || (p.k / BK) % p.fix_splits != 0 || p.ws == nullptr ||
