@@ -148,6 +148,8 @@ def cmd_breakdown(a):
     --prefill-seqs N, of one varlen prefill of N sequences of --ctx tokens instead."""
     r = _runner_for(a)
     real = r.C
+    if hasattr(r, "prefill_attn_impl"):
+        r.prefill_attn_impl = a.impl
     if a.prefill_seqs:
         n, L = a.prefill_seqs, a.ctx
         g = torch.Generator().manual_seed(1)

@@ -267,6 +267,8 @@ class Qwen35Runner:
         # In-kernel split-K for dense GEMMs with few output tiles.  Off by default: on the
         # decode shapes measured so far it did not beat the unsplit kernel.
         self.use_fix_splits = runtime_config().gemm_fix_splits
+        # Varlen prefill attention: 0 = tensor-core kernel, 1 = SIMT kernel (per-row causal lengths).
+        self.prefill_attn_impl = 0
         b["xq"] = torch.zeros(Rp, H, dtype=torch.uint8, device=dev)
         b["xsf"] = torch.zeros(mx.atoms_bytes(Rp, H), dtype=torch.uint8, device=dev)
         b["proj"] = torch.zeros(R * max(self.gdn_w, self.qkv_w), dtype=torch.bfloat16, device=dev)
@@ -447,7 +449,8 @@ class Qwen35Runner:
                 splits = self._attn_splits(rows, decode)
                 C.attn_decode(b["q_out"], b["gate_out"], self.hq, self.hkv, self.k_cache[ai], self.v_cache[ai],
                               self.page_size, self.page_table, slot, lens, rows, b["partial"], splits,
-                              1.0 / math.sqrt(cfg.head_dim), None, midq, b["midsf"])
+                              1.0 / math.sqrt(cfg.head_dim), None, midq, b["midsf"],
+                              impl=0 if decode else self.prefill_attn_impl)
                 self._proj_out(L["o_proj"], midq, b["midsf"], rows, L["post_norm"])
             self._moe(L, rows)
             next_w = self.layers[li + 1]["input_norm"] if li + 1 < len(self.layers) else self.final_norm
