@@ -340,7 +340,7 @@ def cmd_coll(a):
     cluster all-reduce + RMSNorm + MXFP8 (8 rows), the fp32 sum (64 rows) and the expert
     all-to-all dispatch + combine (--m tokens, hidden 4096, top-8 of 256).  With --iters 1
     every kernel launches exactly once (for a profiler capture); otherwise CUDA-event medians."""
-    import os
+    import socket
 
     import torch.distributed as dist
 
@@ -349,9 +349,10 @@ def cmd_coll(a):
     from .parallel.fused import FusedCollectives
 
     if not dist.is_initialized():
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        os.environ.setdefault("MASTER_PORT", "29613")
-        dist.init_process_group("gloo", rank=0, world_size=1)
+        with socket.socket() as sk:
+            sk.bind(("127.0.0.1", 0))
+            port = sk.getsockname()[1]
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
     dev = torch.device("cuda", 0)
     H = 2048
     coll = FusedCollectives(dev, max_rows=256, hidden=H)
