@@ -30,6 +30,7 @@ import torch.distributed as dist
 from . import wire
 from ..models import sampling_head
 from ..sampling import sample_logits, verify_greedy
+from ..utils.env import runtime_config
 
 
 def _resolve_config(name: str):
@@ -186,6 +187,7 @@ class GpuRunner:
 
         self.cfg = _resolve_config(args.model)
         self.dev = torch.device("cuda", torch.cuda.current_device())
+        self.nvtx = runtime_config().nvtx
         coll = make_collectives(self.dev) if world > 1 else None
         # Model-drafted speculation: the MTP head for Qwen3.5, the DSpark head for DeepSeek.
         want = "dspark" if _is_deepseek(self.cfg) else "mtp"
@@ -207,6 +209,20 @@ class GpuRunner:
             self.dram = DramKvArena(self.r.paged_caches(), args.dram_kv_blocks)
 
     def execute(self, plan: dict) -> np.ndarray:
+        """One step plan.  With ZSTEP_NVTX=1 the step is an NVTX range named after its kind
+        (decode / prefill / verify / kv-transfer), for Nsight timelines."""
+        if not self.nvtx:
+            return self._execute(plan)
+        kind = ("kv-transfer" if plan["opcode"] == wire.OP_KV_TRANSFER else
+                "verify" if plan["flags"] & wire.FLAG_SPEC_VERIFY else
+                "decode" if plan["flags"] & wire.FLAG_DECODE_ONLY else "prefill")
+        torch.cuda.nvtx.range_push(f"zstep {kind} rows={int(plan['num_rows'])}")
+        try:
+            return self._execute(plan)
+        finally:
+            torch.cuda.nvtx.range_pop()
+
+    def _execute(self, plan: dict) -> np.ndarray:
         r = self.r
         n = plan["num_seqs"]
         if plan["opcode"] == wire.OP_KV_TRANSFER:
