@@ -585,11 +585,22 @@ decode_partial_tc_kernel(const AttnArgs a) {
       rec[D] = s.m[tid];
       rec[D + 1] = s.l[tid];
     }
-  } else if (tid == 0) {
-    // Abort: let every copy still in flight land before the CTA releases shared memory.
-    if (k_pend) mbar_wait(&s.kfull, (uint32_t)(k_uses & 1), nullptr);
-    for (int b = 0; b < 2; ++b)
-      if (v_pend[b]) mbar_wait(&s.vfull[b], (uint32_t)(v_uses[b] & 1), nullptr);
+  } else {
+    // Abort (the error word is set): still write an empty record (m = -inf, l = 0) for each
+    // head of this split, so the combine kernel skips the split instead of reading whatever
+    // an earlier call left in the scratch buffer.
+    const int h_lim = G < TC_N ? G : TC_N;
+    if (tid < h_lim) {
+      float* rec = a.partial + (((size_t)row * a.num_q_heads + kvh * G + tid) * a.num_splits + split) * PREC;
+      rec[D] = -INFINITY;
+      rec[D + 1] = 0.f;
+    }
+    // Let every copy still in flight land before the CTA releases shared memory.
+    if (tid == 0) {
+      if (k_pend) mbar_wait(&s.kfull, (uint32_t)(k_uses & 1), nullptr);
+      for (int b = 0; b < 2; ++b)
+        if (v_pend[b]) mbar_wait(&s.vfull[b], (uint32_t)(v_uses[b] & 1), nullptr);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -689,8 +700,9 @@ extern "C" int zs_attn_prefill(const AttnArgs* args, cudaStream_t stream) {
 // rows * num_q_heads * num_splits * 260 floats; above that it returns -3 and launches nothing.
 // Sharing: every call on a device uses the same array, so calls that overlap in time (two
 // streams, or two host threads without ordering between their streams) race on it; issue
-// them on one stream.  Nothing in the array has to start at zero: each record a call reads
-// was written earlier in the same call.
+// them on one stream.  Nothing in the array has to start at zero: every split record the
+// combine step reads is written earlier in the same call (an aborted split writes an empty
+// record), so contents left by a previous call are never mixed in.
 // Set-up: the first call on each device looks up the array's address with that device
 // current and caches it; make the first call on a device before any stream capture.
 static __device__ __align__(256) float g_attn_noalloc_scratch[ZS_ATTN_NOALLOC_SCRATCH_FLOATS];
@@ -702,10 +714,19 @@ float* g_noalloc_ptr[64] = {};
 
 extern "C" int zs_attn_decode_noalloc(const AttnArgs* args, cudaStream_t stream) {
   const AttnArgs& in = *args;
-  const size_t need = (size_t)in.rows * (size_t)in.num_q_heads * (size_t)in.num_splits * zs::attn::PREC;
-  if (in.rows < 0 || in.num_q_heads < 0 || in.num_splits < 0 || need > (size_t)ZS_ATTN_NOALLOC_SCRATCH_FLOATS) {
-    fprintf(stderr, "zs_attn_decode_noalloc: needs %zu scratch floats, the fixed limit is %zu\n", need,
-            (size_t)ZS_ATTN_NOALLOC_SCRATCH_FLOATS);
+  // Size check without overflow: divide the limit by each factor in turn instead of
+  // multiplying the caller's ints together.
+  const size_t limit = (size_t)ZS_ATTN_NOALLOC_SCRATCH_FLOATS;
+  bool fits = in.rows >= 0 && in.num_q_heads >= 0 && in.num_splits >= 0;
+  if (fits && in.rows > 0 && in.num_q_heads > 0 && in.num_splits > 0) {
+    size_t room = limit / zs::attn::PREC;
+    room /= (size_t)in.rows;
+    room /= (size_t)in.num_q_heads;
+    fits = (size_t)in.num_splits <= room;
+  }
+  if (!fits) {
+    fprintf(stderr, "zs_attn_decode_noalloc: rows %d x q heads %d x splits %d x %d floats exceed the fixed "
+            "scratch of %zu floats\n", in.rows, in.num_q_heads, in.num_splits, zs::attn::PREC, limit);
     return -3;
   }
   int dev = -1;

@@ -19,8 +19,7 @@ def g():
     cfg = qwen35_small_gpu(num_layers=4, vocab=8192, experts=32)
     r = Qwen35Runner(cfg, weights=RandomWeights(cfg, seed=5), max_seqs=8, max_prefill_tokens=128, num_pages=64,
                      max_model_len=256)
-    gr = GpuRunner.__new__(GpuRunner)
-    gr.r, gr.head, gr.dram, gr.rank = r, None, None, 0
+    gr = GpuRunner.wrap(r)
     for s in range(4):
         r.set_pages(s, list(range(1 + 8 * s, 1 + 8 * (s + 1))))
     return gr

@@ -24,8 +24,7 @@ def setup():
     runner = Qwen35Runner(cfg, weights=src, max_seqs=8, max_prefill_tokens=256, num_pages=64, max_model_len=256,
                           num_spec_tokens=K)
     ref = Qwen35Reference(cfg, src, device="cuda", quant=True)
-    g = GpuRunner.__new__(GpuRunner)
-    g.r = runner
+    g = GpuRunner.wrap(runner)
     return cfg, runner, ref, g
 
 

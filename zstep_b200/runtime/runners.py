@@ -180,6 +180,26 @@ class CpuReferenceRunner:
 class GpuRunner:
     """B200 runner: the kernels of models/qwen35.py driven by step plans."""
 
+    # Defaults for every attribute ``execute`` reads, so a runner built by ``wrap`` (no CLI
+    # arguments) behaves like one built by the worker.
+    nvtx = False
+    head = None
+    dram = None
+    rank = 0
+
+    @classmethod
+    def wrap(cls, model_runner, rank: int = 0, nvtx: bool = False) -> "GpuRunner":
+        """A step-plan runner around an already built model runner (Qwen35Runner or
+        DeepSeekRunner): what the worker builds, minus argument parsing, weight loading and
+        the DRAM arena.  Tests and embedders drive plans through this."""
+        g = cls.__new__(cls)
+        g.r, g.rank, g.nvtx = model_runner, rank, nvtx
+        g.head = None
+        g.dram = None
+        g.dev = model_runner.dev
+        g.cfg = model_runner.cfg
+        return g
+
     def __init__(self, args, rank: int, world: int, geo):
         from ..models.deepseek import DeepSeekRunner
         from ..models.qwen35 import Qwen35Runner
