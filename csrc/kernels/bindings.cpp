@@ -349,21 +349,21 @@ void moe_route(const Tensor& logits, int64_t rows, int64_t num_experts, int64_t 
   rc(zs_moe_route(&a, stream()), "zs_moe_route");
 }
 
-void fused_allreduce_norm(int64_t rank, int64_t world, const Tensor& delta, int64_t n_terms, int64_t row_stride,
-                          int64_t term_stride, const std::vector<int64_t>& part, const std::vector<int64_t>& out,
-                          const std::vector<int64_t>& flags, const Tensor& epoch, const Tensor& grid_counter,
-                          const Tensor& residual, const Tensor& weight, double w_offset, double eps, int64_t rows,
-                          const OptT& normed, const OptT& q, const OptT& sf, const OptT& err,
-                          const OptT& term_index, const OptT& term_scale, int64_t timeout_ms,
-                          const std::vector<int64_t>& oneshot) {
-  TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)part.size() == world && (int64_t)out.size() == world &&
-                  (int64_t)flags.size() == world && (oneshot.empty() || (int64_t)oneshot.size() == world),
+void fused_allreduce_norm(int64_t rank, int64_t world, int64_t protocol, const Tensor& delta, int64_t n_terms,
+                          int64_t row_stride, int64_t term_stride, const std::vector<int64_t>& part,
+                          const std::vector<int64_t>& out, const std::vector<int64_t>& flags, const Tensor& epoch,
+                          const Tensor& grid_counter, const Tensor& residual, const Tensor& weight, double w_offset,
+                          double eps, int64_t rows, const OptT& normed, const OptT& q, const OptT& sf, const OptT& err,
+                          const OptT& term_index, const OptT& term_scale, int64_t timeout_ms) {
+  TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)part.size() == world &&
+                  (out.empty() || (int64_t)out.size() == world) && (flags.empty() || (int64_t)flags.size() == world),
               "bad world / pointer lists");
   check_cuda(delta, "delta");
   check_cuda(residual, "residual");
   FusedArArgs a{};
   a.rank = (int)rank;
   a.world = (int)world;
+  a.protocol = (int)protocol;
   a.delta = ptr(delta);
   a.n_terms = (int)n_terms;
   a.row_stride = row_stride;
@@ -371,8 +371,8 @@ void fused_allreduce_norm(int64_t rank, int64_t world, const Tensor& delta, int6
   a.delta_f32 = delta.scalar_type() == at::kFloat ? 1 : 0;
   for (int r = 0; r < world; ++r) {
     a.part[r] = reinterpret_cast<void*>(part[r]);
-    a.out[r] = reinterpret_cast<void*>(out[r]);
-    a.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
+    if (!out.empty()) a.out[r] = reinterpret_cast<void*>(out[r]);
+    if (!flags.empty()) a.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
   }
   a.epoch = ptr<uint32_t>(epoch);
   a.grid_counter = ptr<uint32_t>(grid_counter);
@@ -389,7 +389,6 @@ void fused_allreduce_norm(int64_t rank, int64_t world, const Tensor& delta, int6
   a.term_index = optptr<const int>(term_index);
   a.term_scale = optptr<const float>(term_scale);
   a.timeout_ms = (unsigned int)timeout_ms;
-  for (size_t r = 0; r < oneshot.size(); ++r) a.oneshot[r] = reinterpret_cast<void*>(oneshot[r]);
   rc(zs_fused_allreduce_norm(&a, stream()), "zs_fused_allreduce_norm");
 }
 
@@ -414,27 +413,29 @@ void allreduce_sum_f32(int64_t rank, int64_t world, const Tensor& data, int64_t 
   rc(zs_allreduce_sum_f32(&a, stream()), "zs_allreduce_sum_f32");
 }
 
-void allreduce_argmax(int64_t rank, int64_t world, int64_t rows, const std::vector<int64_t>& keys,
-                      const std::vector<int64_t>& flags, const Tensor& epoch, const Tensor& local_keys,
-                      int64_t id_offset, const OptT& out_ids, const OptT& out_vals, const OptT& err,
+void allreduce_argmax(int64_t rank, int64_t world, int64_t rows, int64_t max_rows, const Tensor& tile_keys,
+                      int64_t tiles, int64_t id_offset, const std::vector<int64_t>& lines, const Tensor& epoch,
+                      const Tensor& grid_counter, const OptT& out_ids, const OptT& out_vals, const OptT& err,
                       int64_t timeout_ms) {
-  TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)keys.size() == world && (int64_t)flags.size() == world,
-              "bad world / pointer lists");
+  TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)lines.size() == world, "bad world / pointer lists");
+  check_cuda(tile_keys, "tile_keys");
+  TORCH_CHECK(tile_keys.scalar_type() == at::kLong && tile_keys.numel() >= rows * tiles, "tile_keys: i64 [rows, tiles]");
   ArgmaxArArgs a{};
   a.rank = (int)rank;
   a.world = (int)world;
   a.rows = (int)rows;
-  for (int r = 0; r < world; ++r) {
-    a.keys[r] = reinterpret_cast<const void*>(keys[r]);
-    a.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
-  }
+  a.max_rows = (int)max_rows;
+  a.tile_keys = ptr<const unsigned long long>(tile_keys);
+  a.tiles = (int)tiles;
+  a.id_offset = (int)id_offset;
+  for (int r = 0; r < world; ++r) a.lines[r] = reinterpret_cast<void*>(lines[r]);
   a.epoch = ptr<uint32_t>(epoch);
+  a.grid_counter = ptr<uint32_t>(grid_counter);
   a.out_ids = optptr<int>(out_ids);
   a.out_vals = optptr<float>(out_vals);
   a.err = optptr<int>(err);
   a.timeout_ms = (unsigned int)timeout_ms;
-  rc(zs_allreduce_argmax(&a, ptr<const unsigned long long>(local_keys), (int)id_offset, stream()),
-     "zs_allreduce_argmax");
+  rc(zs_allreduce_argmax(&a, stream()), "zs_allreduce_argmax");
 }
 
 // Expert-parallel dispatch (which = 0) or combine (which = 1); offs = the six byte
@@ -799,18 +800,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("err") = py::none());
   m.def("gather_sum", &gather_sum);
 
-  m.def("fused_allreduce_norm", &fused_allreduce_norm, py::arg("rank"), py::arg("world"), py::arg("delta"),
-        py::arg("n_terms"), py::arg("row_stride"), py::arg("term_stride"), py::arg("part"), py::arg("out"),
-        py::arg("flags"), py::arg("epoch"), py::arg("grid_counter"), py::arg("residual"), py::arg("weight"),
-        py::arg("w_offset"), py::arg("eps"), py::arg("rows"), py::arg("normed"), py::arg("q"), py::arg("sf"),
-        py::arg("err"), py::arg("term_index") = py::none(), py::arg("term_scale") = py::none(),
-        py::arg("timeout_ms") = 0, py::arg("oneshot") = std::vector<int64_t>{});
+  m.def("fused_allreduce_norm", &fused_allreduce_norm, py::arg("rank"), py::arg("world"), py::arg("protocol"),
+        py::arg("delta"), py::arg("n_terms"), py::arg("row_stride"), py::arg("term_stride"), py::arg("part"),
+        py::arg("out"), py::arg("flags"), py::arg("epoch"), py::arg("grid_counter"), py::arg("residual"),
+        py::arg("weight"), py::arg("w_offset"), py::arg("eps"), py::arg("rows"), py::arg("normed"), py::arg("q"),
+        py::arg("sf"), py::arg("err"), py::arg("term_index") = py::none(), py::arg("term_scale") = py::none(),
+        py::arg("timeout_ms") = 0);
   m.def("allreduce_sum_f32", &allreduce_sum_f32, py::arg("rank"), py::arg("world"), py::arg("data"), py::arg("rows"),
         py::arg("max_rows"), py::arg("buf"), py::arg("epoch"), py::arg("grid_counter"), py::arg("err"),
         py::arg("timeout_ms") = 0);
-  m.def("allreduce_argmax", &allreduce_argmax, py::arg("rank"), py::arg("world"), py::arg("rows"), py::arg("keys"),
-        py::arg("flags"), py::arg("epoch"), py::arg("local_keys"), py::arg("id_offset"), py::arg("out_ids"),
-        py::arg("out_vals"), py::arg("err"), py::arg("timeout_ms") = 0);
+  m.def("allreduce_argmax", &allreduce_argmax, py::arg("rank"), py::arg("world"), py::arg("rows"),
+        py::arg("max_rows"), py::arg("tile_keys"), py::arg("tiles"), py::arg("id_offset"), py::arg("lines"),
+        py::arg("epoch"), py::arg("grid_counter"), py::arg("out_ids"), py::arg("out_vals"), py::arg("err"),
+        py::arg("timeout_ms") = 0);
   m.def("ep_call", &ep_call, py::arg("which"), py::arg("rank"), py::arg("world"), py::arg("tokens"),
         py::arg("max_tokens"), py::arg("hidden"), py::arg("top_k"), py::arg("num_experts"), py::arg("recv_cap"),
         py::arg("chunk_rows"), py::arg("topk_ids"), py::arg("topk_w"), py::arg("x"), py::arg("sym"), py::arg("offs"),
@@ -819,6 +821,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("residual"), py::arg("out"), py::arg("err"), py::arg("timeout_ms") = 0);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_free", [](int64_t p) { rc(zs_symm_free(reinterpret_cast<void*>(p)), "zs_symm_free"); });
+  m.def("symm_memset", [](int64_t p, int64_t bytes) {
+    TORCH_CHECK(cudaMemsetAsync(reinterpret_cast<void*>(p), 0, (size_t)bytes, stream()) == cudaSuccess,
+                "cudaMemsetAsync failed");
+  });
   m.def("ipc_handle", &ipc_handle);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", [](int64_t p) { rc(zs_ipc_close(reinterpret_cast<void*>(p)), "zs_ipc_close"); });

@@ -1,30 +1,46 @@
 // Tensor-parallel collectives fused with their consumers, over NVLink peer memory.
 //
 // Symmetric memory: every rank allocates the same buffers with cudaMalloc and maps its
-// peers' copies through CUDA IPC (cudaIpcOpenMemHandle), so a kernel on rank r can load
-// from and store to rank q's buffer directly over NVLink / NVSwitch.  No host memory
-// and no library collective sits on the data path.
+// peers' copies through CUDA IPC (cudaIpcOpenMemHandle), so a kernel on rank r stores
+// straight into rank q's buffer over NVLink / NVSwitch.  Every protocol here is
+// push-based: a kernel only ever stores to peers and loads its own memory, so each
+// NVLink crossing is one posted write and no load waits on a remote round trip.
 //
-// fused_allreduce_norm (one cooperative launch): push-based two-shot all-reduce of the
-// row-parallel partial sums with flag-in-data words, fused with the residual add, RMSNorm
-// and MXFP8 quantization (details at the kernel).  Every word carries the call's epoch
-// (a counter in device memory advanced by the kernel itself), so there is no separate
-// barrier round trip and the kernel stays CUDA-graph safe.
+// LL lines.  Decode-sized messages move as 16-byte "LL lines" {d0, epoch, d1, epoch}: two
+// 32-bit payload words (four bf16, or two f32), each paired with the call's epoch in one
+// 8-byte half.  A reader accepts a line only when both halves carry the current epoch,
+// so data and flag arrive in the same store and no separate barrier round trip is paid.
+// Readers issue the loads of every source before checking any (up to 8 in flight per
+// thread), then re-poll only the stale ones: a wait costs one memory latency, not one per
+// source.  Epochs are per-protocol device counters advanced by the last CTA of each call,
+// so every call (eager or CUDA-graph replay) carries fresh flag values.
 //
-// fused_allreduce_norm_small (rows <= 8): one-shot instead of two-shot (one NVLink hop),
-// one 8-CTA cluster per row splitting its columns; the RMSNorm sum of squares is combined
-// through distributed shared memory.
+// fused_allreduce_norm, three protocols (host chooses by row count):
+//   one-shot : every rank pushes its local rows to every rank (parity-double-buffered);
+//              each rank sums residual + the W contributions in rank order.  One hop.
+//   two-shot : reduce-scatter to the row's owner + all-gather of the owner's bf16 result,
+//              both as LL lines.  Two hops, 2(W-1)/W of the bytes of the one-shot.
+//   plain    : the two-shot data flow with plain bf16 rows and per-(source, CTA) flags
+//              released after a system-scope fence, for prefill-sized reductions where
+//              the LL format's doubled bytes would dominate.
+// All three then apply residual add, RMSNorm and MXFP8 quantization in the same kernel.
+// Every rank computes every row's sum in the same order, so all ranks hold identical
+// bf16 residual streams.
 //
-// allreduce_argmax: per-row packed (logit, ~id) keys of each rank's vocab shard are
-// exchanged the same way and max-reduced, giving the global greedy token on every rank.
+// allreduce_argmax: the lm_head's per-tile keys -> per-row key -> global ids -> one LL
+// line per (row, rank) pushed to every rank -> max over ranks, in one kernel.
 //
-// allreduce_sum_f32: one-shot in-place fp32 sum (the mHC model's sublayer outputs).
+// allreduce_sum_f32: one-shot LL fp32 sum (the mHC model's sublayer outputs).
+//
+// Launch: all kernels use programmatic dependent launch (set-up overlaps the producer's
+// tail; each waits before its first read of predecessor output).  A two-shot CTA c only
+// waits for CTA c of other ranks (same row -> CTA map everywhere) and never for another
+// CTA of its own rank, and FAR_CTAS CTAs of 256 threads with a few KB of shared memory fit
+// beside any kernel of this library, so they are all resident without a cooperative launch.
 //
 // Reference parity: replaces worker/zstep_worker/kernels_sm120/csrc/shm_allreduce_kernels.cu
 // (shm_v5 all-reduce :472, fused AR + add + RMSNorm :1376, spin-wait with abort :31-83)
 // and the TP=8 argmax exchange (csrc/qwen35_ops_kernels.cu:202).
-#include <cooperative_groups.h>
-
 #include "peer.cuh"
 #include "sm100_common.cuh"
 #include "zs_kernels.h"
@@ -33,359 +49,485 @@ namespace zs {
 namespace coll {
 
 constexpr int THREADS = 256;
+constexpr int MAX_LPT = 4;  // LL lines (4 columns each) per thread per row: hidden <= 4096
 
 using namespace peer;
 
+__device__ __forceinline__ void st_ll16(void* p, uint32_t d0, uint32_t d1, uint32_t e) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(d0), "r"(e), "r"(d1), "r"(e)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_ll16(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool ll_ok(const uint4& v, uint32_t e) { return v.y == e && v.w == e; }
 
-// Local contribution to word w (elements 2w, 2w+1) of `row`: the rank's terms summed in
-// term order, rounded to bf16 (what the other ranks receive).
-__device__ __forceinline__ uint32_t local_word(const FusedArArgs& a, int row, int w) {
-  float s0 = 0.f, s1 = 0.f;
-  const int c = 2 * w;
+// Loads the n (<= N) lines p[0], p[stride], ... and waits until every one carries epoch e.
+// All loads are issued before any is checked; stale lines are re-polled until the time
+// budget runs out (then kErrPeerTimeout, and the CTA-wide give_up word stops the others).
+template <int N>
+__device__ __forceinline__ bool wait_lines(const uint4* p, size_t stride, int n, uint32_t e, uint4 (&v)[N],
+                                           uint64_t budget, int* err, volatile int* give_up) {
+  uint32_t pend = 0;
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+    if (i < n) v[i] = ld_ll16(p + i * stride);
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+    if (i < n && !ll_ok(v[i], e)) pend |= 1u << i;
+  if (pend == 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      if ((pend >> i) & 1u) {
+        v[i] = ld_ll16(p + i * stride);
+        if (ll_ok(v[i], e)) pend &= ~(1u << i);
+      }
+    if (pend == 0) return true;
+    if (*give_up) return false;
+    if ((it & 15) == 15) {
+      if (globaltimer_ns() - t0 > budget) {
+        report_error(err, kErrPeerTimeout);
+        *give_up = 1;
+        return false;
+      }
+      __nanosleep(32);
+    }
+  }
+}
+
+__device__ __forceinline__ float4 bf16x4_to_f4(uint32_t lo, uint32_t hi) {
+  const float2 a = unpack_bf16x2(lo), b = unpack_bf16x2(hi);
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// This rank's contribution to columns [4l, 4l + 4) of `row`: its terms summed in term order
+// (fp32), as the caller will round it (bf16 on the wire).
+__device__ __forceinline__ float4 local_line(const FusedArArgs& a, int row, int l) {
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int c = 4 * l;
   for (int t = 0; t < a.n_terms; ++t) {
     long long off = row * a.row_stride + t * a.term_stride + c;
     float sc = 1.f;
     if (a.term_index != nullptr) {  // gathered term; negative = not produced on this rank
-      const int src = a.term_index[row * a.n_terms + t];
+      const int src = __ldg(a.term_index + row * a.n_terms + t);
       if (src < 0) continue;
       off = (long long)src * a.row_stride + c;
     }
-    if (a.term_scale != nullptr) sc = a.term_scale[row * a.n_terms + t];
+    if (a.term_scale != nullptr) sc = __ldg(a.term_scale + row * a.n_terms + t);
+    float4 v;
     if (a.delta_f32) {
-      const float2 v = *reinterpret_cast<const float2*>(static_cast<const float*>(a.delta) + off);
-      s0 += sc * v.x;
-      s1 += sc * v.y;
+      v = *reinterpret_cast<const float4*>(static_cast<const float*>(a.delta) + off);
     } else {
-      const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(static_cast<const __nv_bfloat16*>(a.delta) + off));
-      s0 += sc * v.x;
-      s1 += sc * v.y;
+      const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.delta) + off);
+      v = bf16x4_to_f4(u.x, u.y);
     }
+    s.x += sc * v.x;
+    s.y += sc * v.y;
+    s.z += sc * v.z;
+    s.w += sc * v.w;
   }
-  return pack_bf16x2(s0, s1);
+  return s;
 }
 
-// Push-based two-shot all-reduce with flag-in-data words (no grid barrier, no remote loads):
-//  1. send   : every rank pushes its bf16 local sum of each row to the row's owner
-//              (rs buffer slot [sender][row - owner_first_row])
-//  2. reduce : the owner waits for the W contributions of its rows, adds residual + the
-//              contributions in rank order (identical on every rank) and pushes the bf16
-//              result to every rank's ag buffer
-//  3. gather : every rank waits for each row's result, writes it to its residual stream
-//              and applies RMSNorm + MXFP8 quantization
-// CTA c handles rows c, c+G, ... in all three phases on every rank, so a CTA only waits for
-// words that other CTAs (same index, other ranks) produce before they wait themselves.
-// Buffers are reused across calls without extra barriers: a rank writes call E+1's words
-// only after it finished call E, which needed every peer's call-E words it is about to
-// overwrite to have been consumed (an owner sends its results only after reading all
-// contributions; a sender starts the next call only after reading all results).
-__global__ void __launch_bounds__(THREADS) fused_allreduce_norm_kernel(const FusedArArgs a) {
-  const int H = a.hidden, M = a.rows, W = a.world;
-  const int words = H / 2;
-  const int tid = threadIdx.x;
-  const uint32_t E = *reinterpret_cast<volatile uint32_t*>(a.epoch) + 1;  // this call's flag value (never 0)
-  const int G = gridDim.x;
-  const int per = (M + W - 1) / W;
+// Finishing step shared by every protocol, for one row whose reduced bf16 values this
+// thread holds as lines l = tid + i * THREADS (i < lpt): write the residual, RMSNorm over
+// the row (block reduction), then the bf16 and/or MXFP8 outputs.  An MXFP8 block of 32
+// columns is 8 consecutive lines = 8 consecutive threads.
+__device__ __forceinline__ void finish_row(const FusedArArgs& a, int row, int lpt, const uint2 (&res)[MAX_LPT],
+                                           float* red) {
+  const int H = a.hidden, tid = threadIdx.x;
+  __nv_bfloat16* res_out = static_cast<__nv_bfloat16*>(a.residual) + (size_t)row * H;
+  float x[MAX_LPT][4];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAX_LPT; ++i) {
+    if (i >= lpt) break;
+    const int c = 4 * (tid + i * THREADS);
+    *reinterpret_cast<uint2*>(res_out + c) = res[i];
+    const float4 f = bf16x4_to_f4(res[i].x, res[i].y);
+    x[i][0] = f.x;
+    x[i][1] = f.y;
+    x[i][2] = f.z;
+    x[i][3] = f.w;
+    ss += f.x * f.x + f.y * f.y + f.z * f.z + f.w * f.w;
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < THREADS / 32; ++i) tot += red[i];
+  __syncthreads();  // red is reused by the next row
+  const float rstd = rsqrtf(tot / H + a.eps);
+  const __nv_bfloat16* wgt = static_cast<const __nv_bfloat16*>(a.weight);
+#pragma unroll
+  for (int i = 0; i < MAX_LPT; ++i) {
+    if (i >= lpt) break;
+    const int c = 4 * (tid + i * THREADS);
+    const uint2 wu = *reinterpret_cast<const uint2*>(wgt + c);
+    const float4 w4 = bf16x4_to_f4(wu.x, wu.y);
+    float y[4] = {x[i][0] * rstd * (w4.x + a.w_offset), x[i][1] * rstd * (w4.y + a.w_offset),
+                  x[i][2] * rstd * (w4.z + a.w_offset), x[i][3] * rstd * (w4.w + a.w_offset)};
+    if (a.normed)
+      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.normed) + (size_t)row * H + c) =
+          make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
+    if (a.q) {
+      float amax = fmaxf(fmaxf(fabsf(y[0]), fabsf(y[1])), fmaxf(fabsf(y[2]), fabsf(y[3])));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffff, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffff, amax, 2));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffff, amax, 4));
+      const uint8_t code = mx_scale_e8m0(amax);
+      const float inv = mx_inv_scale(code);
+      uint32_t pk = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) pk |= uint32_t(f32_to_e4m3(y[j] * inv)) << (8 * j);
+      *reinterpret_cast<uint32_t*>(a.q + (size_t)row * H + c) = pk;
+      if ((tid & 7) == 0) {
+        const int kb = c >> 5;
+        a.sf[((size_t)(row >> 7) * (H >> 7) + (kb >> 2)) * 512 + sf_atom_offset(row & 127, kb & 3)] = code;
+      }
+    }
+  }
+}
+
+// The last CTA of a call re-arms the completion counter and advances the epoch (every CTA
+// read the epoch at its start; the next call starts after this kernel completes).
+__device__ __forceinline__ void finish_call(uint32_t* counter, uint32_t* epoch, uint32_t E) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(counter, 1u) == gridDim.x - 1) {
+      *reinterpret_cast<volatile uint32_t*>(counter) = 0u;
+      *reinterpret_cast<volatile uint32_t*>(epoch) = E;
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t read_epoch(const uint32_t* epoch) {
+  return *reinterpret_cast<const volatile uint32_t*>(epoch) + 1u;  // this call's flag value
+}
+
+// ---------------------------------------------------------------------------------
+// One-shot: CTA = row.  Push lines of the row to every rank's slot [parity][rank][row],
+// then sum residual + the W slots in rank order.
+__global__ void __launch_bounds__(THREADS, 3) ar_oneshot_kernel(const FusedArArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int H = a.hidden, W = a.world, L = H / 4, lpt = L / THREADS;
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const uint32_t E = read_epoch(a.epoch);
+  const int par = E & 1;
   const uint64_t budget = limit_ns(a.timeout_ms);
   __shared__ int give_up;
+  __shared__ float red[THREADS / 32];
   if (tid == 0) give_up = 0;
   __syncthreads();
+  auto slot = [&](int dst_rank, int src) {
+    return static_cast<uint4*>(a.part[dst_rank]) + (((size_t)par * W + src) * FAR_ONESHOT_ROWS + row) * L;
+  };
+  for (int i = 0; i < lpt; ++i) {
+    const int l = tid + i * THREADS;
+    const float4 f = local_line(a, row, l);
+    const uint32_t d0 = pack_bf16x2(f.x, f.y), d1 = pack_bf16x2(f.z, f.w);
+    for (int q = 0; q < W; ++q) st_ll16(slot(q, a.rank) + l, d0, d1, E);
+  }
+  const __nv_bfloat16* resid = static_cast<const __nv_bfloat16*>(a.residual) + (size_t)row * H;
+  const size_t src_stride = (size_t)FAR_ONESHOT_ROWS * L;
+  uint2 res[MAX_LPT];
+  bool ok = true;
+#pragma unroll
+  for (int i = 0; i < MAX_LPT; ++i) {
+    if (i >= lpt) break;
+    const int l = tid + i * THREADS;
+    uint4 v[8];
+    ok = ok && wait_lines<8>(slot(a.rank, 0) + l, src_stride, W, E, v, budget, a.err, &give_up);
+    const uint2 ru = *reinterpret_cast<const uint2*>(resid + 4 * l);
+    float4 acc = bf16x4_to_f4(ru.x, ru.y);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      if (q >= W) break;
+      const float4 f = bf16x4_to_f4(v[q].x, v[q].z);
+      acc.x += f.x;
+      acc.y += f.y;
+      acc.z += f.z;
+      acc.w += f.w;
+    }
+    res[i] = make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
+  }
+  if (__syncthreads_or(!ok) == 0) finish_row(a, row, lpt, res, red);
+  finish_call(a.grid_counter, a.epoch, E);
+}
 
-  // 1. send local sums to the owners
+// ---------------------------------------------------------------------------------
+// Two-shot with LL lines.  CTA c handles rows c, c + G, ... in every phase on every rank.
+//  1. send   : local lines of each row to the row's owner, slot [rank][row - owner_first]
+//  2. reduce : the owner sums residual + W slots in rank order, pushes the bf16 result
+//              line to every rank's gather buffer
+//  3. gather : every rank waits for each row's result lines, then finish_row
+// Buffer reuse needs no extra barrier: a rank writes call E+1's lines only after it
+// finished call E, and finishing call E required every owner to have read all of call E's
+// reduce-scatter slots (an owner sends results only after reading them) and every rank to
+// have read call E's results for all rows (its own gather).
+__global__ void __launch_bounds__(THREADS, 4) ar_twoshot_kernel(const FusedArArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int H = a.hidden, M = a.rows, W = a.world, L = H / 4, lpt = L / THREADS;
+  const int tid = threadIdx.x, G = gridDim.x;
+  const int per = (M + W - 1) / W;
+  const uint32_t E = read_epoch(a.epoch);
+  const uint64_t budget = limit_ns(a.timeout_ms);
+  __shared__ int give_up;
+  __shared__ float red[THREADS / 32];
+  if (tid == 0) give_up = 0;
+  __syncthreads();
+  // 1. send
   for (int row = blockIdx.x; row < M; row += G) {
     const int owner = min(row / per, W - 1);
-    uint2* dst = static_cast<uint2*>(a.part[owner]) + ((size_t)a.rank * per + (row - owner * per)) * words;
-    for (int w = tid; w < words; w += THREADS) st_ll(dst + w, local_word(a, row, w), E);
+    uint4* dst = static_cast<uint4*>(a.part[owner]) + ((size_t)a.rank * per + (row - owner * per)) * L;
+    for (int l = tid; l < L; l += THREADS) {
+      const float4 f = local_line(a, row, l);
+      st_ll16(dst + l, pack_bf16x2(f.x, f.y), pack_bf16x2(f.z, f.w), E);
+    }
   }
-  // 2. reduce the owned rows and broadcast them
-  const __nv_bfloat16* resid = static_cast<const __nv_bfloat16*>(a.residual);
+  // 2. reduce the owned rows, broadcast the results
+  const size_t src_stride = (size_t)per * L;
   for (int row = blockIdx.x; row < M; row += G) {
     const int owner = min(row / per, W - 1);
     if (owner != a.rank) continue;
-    const uint2* src = static_cast<const uint2*>(a.part[a.rank]) + (size_t)(row - owner * per) * words;
-    for (int w = tid; w < words; w += THREADS) {
-      float2 acc = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(resid + (size_t)row * H + 2 * w));
-      for (int q = 0; q < W; ++q) {
-        const float2 v = unpack_bf16x2(wait_ll(src + (size_t)q * per * words + w, E, budget, a.err, &give_up));
-        acc.x += v.x;
-        acc.y += v.y;
+    const uint4* src = static_cast<const uint4*>(a.part[a.rank]) + (size_t)(row - owner * per) * L;
+    const __nv_bfloat16* resid = static_cast<const __nv_bfloat16*>(a.residual) + (size_t)row * H;
+    for (int l = tid; l < L; l += THREADS) {
+      uint4 v[8];
+      if (!wait_lines<8>(src + l, src_stride, W, E, v, budget, a.err, &give_up)) break;
+      const uint2 ru = *reinterpret_cast<const uint2*>(resid + 4 * l);
+      float4 acc = bf16x4_to_f4(ru.x, ru.y);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (q >= W) break;
+        const float4 f = bf16x4_to_f4(v[q].x, v[q].z);
+        acc.x += f.x;
+        acc.y += f.y;
+        acc.z += f.z;
+        acc.w += f.w;
       }
-      const uint32_t res = pack_bf16x2(acc.x, acc.y);
-      for (int q = 0; q < W; ++q) st_ll(static_cast<uint2*>(a.out[q]) + (size_t)row * words + w, res, E);
+      const uint32_t r0 = pack_bf16x2(acc.x, acc.y), r1 = pack_bf16x2(acc.z, acc.w);
+      for (int q = 0; q < W; ++q) st_ll16(static_cast<uint4*>(a.out[q]) + (size_t)row * L + l, r0, r1, E);
     }
   }
-  // 3. gather every row, then RMSNorm + MXFP8
-  __shared__ float red[THREADS / 32];
-  __nv_bfloat16* res_out = static_cast<__nv_bfloat16*>(a.residual);
-  const __nv_bfloat16* wgt = static_cast<const __nv_bfloat16*>(a.weight);
-  const uint2* ag = static_cast<const uint2*>(a.out[a.rank]);
+  // 3. gather + RMSNorm + MXFP8
   for (int row = blockIdx.x; row < M; row += G) {
-    float x[4][8];
-    float ss = 0.f;
-    const int iters = H / (THREADS * 8);
-    for (int it = 0; it < iters; ++it) {
-      const int c = (it * THREADS + tid) * 8;
-      uint32_t u[4];
+    const uint4* ag = static_cast<const uint4*>(a.out[a.rank]) + (size_t)row * L;
+    uint4 v[MAX_LPT];
+    const bool ok = wait_lines<MAX_LPT>(ag + tid, THREADS, lpt, E, v, budget, a.err, &give_up);
+    if (__syncthreads_or(!ok)) break;
+    uint2 res[MAX_LPT];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        u[j] = wait_ll(ag + (size_t)row * words + c / 2 + j, E, budget, a.err, &give_up);
-        const float2 f = unpack_bf16x2(u[j]);
-        x[it][2 * j] = f.x;
-        x[it][2 * j + 1] = f.y;
-        ss += f.x * f.x + f.y * f.y;
-      }
-      *reinterpret_cast<uint4*>(res_out + (size_t)row * H + c) = make_uint4(u[0], u[1], u[2], u[3]);
-    }
-    ss = warp_sum(ss);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
-    __syncthreads();
-    float tot = 0.f;
-#pragma unroll
-    for (int i = 0; i < THREADS / 32; ++i) tot += red[i];
-    __syncthreads();
-    const float rstd = rsqrtf(tot / H + a.eps);
-    for (int it = 0; it < iters; ++it) {
-      const int c = (it * THREADS + tid) * 8;
-      float w8[8], y[8];
-      unpack8(*reinterpret_cast<const uint4*>(wgt + c), w8);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) y[j] = x[it][j] * rstd * (w8[j] + a.w_offset);
-      if (a.normed) *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.normed) + (size_t)row * H + c) = pack8(y);
-      if (a.q) {
-        float amax = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(y[j]));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffff, amax, 1));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffff, amax, 2));
-        const uint8_t code = mx_scale_e8m0(amax);
-        const float inv = mx_inv_scale(code);
-        uint32_t lo = 0, hi = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          lo |= uint32_t(f32_to_e4m3(y[j] * inv)) << (8 * j);
-          hi |= uint32_t(f32_to_e4m3(y[4 + j] * inv)) << (8 * j);
-        }
-        *reinterpret_cast<uint2*>(a.q + (size_t)row * H + c) = make_uint2(lo, hi);
-        if ((tid & 3) == 0) {
-          const int kb = c >> 5;
-          a.sf[((size_t)(row >> 7) * (H >> 7) + (kb >> 2)) * 512 + sf_atom_offset(row & 127, kb & 3)] = code;
-        }
-      }
-    }
+    for (int i = 0; i < MAX_LPT; ++i) res[i] = make_uint2(v[i].x, v[i].z);
+    finish_row(a, row, lpt, res, red);
   }
-  // The last CTA to finish advances the epoch (every CTA has read it by then).
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    const uint32_t done = atomicAdd(a.grid_counter, 1u) + 1;
-    if (done % (uint32_t)G == 0) *reinterpret_cast<volatile uint32_t*>(a.epoch) = E;
+  finish_call(a.grid_counter, a.epoch, E);
+}
+
+// ---------------------------------------------------------------------------------
+// Two-shot with plain bf16 rows (prefill sizes).  Flags: [phase][source][CTA] u32 per rank.
+// After a CTA's stores of a phase, every thread fences at system scope, then thread q
+// releases flag [phase][rank][c] on rank q; a consumer CTA c acquires the W flags of CTA
+// c on every rank before it reads.  Reuse across calls follows the two-shot argument.
+__device__ __forceinline__ void publish(const FusedArArgs& a, int phase, uint32_t E) {
+  __syncthreads();  // every store of this CTA precedes the fences below
+  if (threadIdx.x < a.world) {
+    __threadfence_system();
+    st_release_sys(a.flags[threadIdx.x] + ((size_t)phase * 8 + a.rank) * FAR_CTAS + blockIdx.x, E);
   }
 }
 
-// One-shot fused all-reduce for rows <= FAR_SMALL_ROWS.  Cluster = one row; CTA `part`
-// owns words [part * cw, (part + 1) * cw) of it.  Every rank pushes its local words of
-// the slice to every rank (parity E & 1 of the one-shot buffer, so call E+1 never
-// overwrites words a slower rank still waits for in call E: a rank starts call E+2 only
-// after every rank finished pushing call E+1, i.e. finished reading call E), then sums
-// residual + all ranks' words in rank order, like the two-shot owner does.
-constexpr int SMALL_CTAS = 8;
+__device__ __forceinline__ bool await(const FusedArArgs& a, int phase, uint32_t E, uint64_t budget,
+                                      volatile int* give_up) {
+  if (threadIdx.x < a.world) {
+    const uint32_t* f = a.flags[a.rank] + ((size_t)phase * 8 + threadIdx.x) * FAR_CTAS + blockIdx.x;
+    if (!wait_flag_sys(f, E, budget, nullptr)) {
+      report_error(a.err, kErrPeerTimeout);
+      *give_up = 1;
+    }
+  }
+  __syncthreads();
+  return *give_up == 0;
+}
 
-__global__ void __cluster_dims__(SMALL_CTAS, 1, 1) __launch_bounds__(THREADS)
-    fused_allreduce_norm_small_kernel(const FusedArArgs a) {
-  namespace cg = cooperative_groups;
-  cg::cluster_group cluster = cg::this_cluster();
-  const int H = a.hidden, W = a.world;
-  const int words = H / 2, cw = words / SMALL_CTAS;
-  const int row = blockIdx.x / SMALL_CTAS;
-  const int part = (int)cluster.block_rank();
-  const int tid = threadIdx.x, lane = tid & 31;
-  const uint32_t E = *reinterpret_cast<volatile uint32_t*>(a.epoch) + 1;
-  const int par = E & 1;
+__global__ void __launch_bounds__(THREADS, 4) ar_plain_kernel(const FusedArArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int H = a.hidden, M = a.rows, W = a.world, L = H / 4, lpt = L / THREADS;
+  const int tid = threadIdx.x, G = gridDim.x;
+  const int per = (M + W - 1) / W;
+  const uint32_t E = read_epoch(a.epoch);
   const uint64_t budget = limit_ns(a.timeout_ms);
   __shared__ int give_up;
   __shared__ float red[THREADS / 32];
-  __shared__ float cta_ss, tot_ss;
   if (tid == 0) give_up = 0;
   __syncthreads();
-  // The grid always has FAR_SMALL_ROWS clusters (a fixed CTA count keeps the completion
-  // counter a multiple of the grid); clusters past `rows` only count themselves.
-  if (row >= a.rows) {
-    if (tid == 0) {
-      const uint32_t done = atomicAdd(a.grid_counter, 1u) + 1;
-      if (done % gridDim.x == 0) *reinterpret_cast<volatile uint32_t*>(a.epoch) = E;
+  // 1. send (8 columns per 16-byte store)
+  const int L8 = H / 8;
+  for (int row = blockIdx.x; row < M; row += G) {
+    const int owner = min(row / per, W - 1);
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.part[owner]) +
+                                          ((size_t)a.rank * per + (row - owner * per)) * H);
+    for (int j = tid; j < L8; j += THREADS) {
+      const float4 f0 = local_line(a, row, 2 * j), f1 = local_line(a, row, 2 * j + 1);
+      dst[j] = make_uint4(pack_bf16x2(f0.x, f0.y), pack_bf16x2(f0.z, f0.w), pack_bf16x2(f1.x, f1.y),
+                          pack_bf16x2(f1.z, f1.w));
     }
-    return;
   }
-  auto slot = [&](int q, int src, int w) {
-    return static_cast<uint2*>(a.oneshot[q]) + ((((size_t)par * W + src) * FAR_SMALL_ROWS + row) * words + w);
-  };
-  // 1. push
-  for (int w = part * cw + tid; w < (part + 1) * cw; w += THREADS) {
-    const uint32_t v = local_word(a, row, w);
-    for (int q = 0; q < W; ++q) st_ll(slot(q, a.rank, w), v, E);
-  }
-  // 2. reduce (residual first, then ranks in order), write the residual
-  constexpr int MAXW = 4;  // words per thread: hidden <= 8 * 2 * THREADS * MAXW
-  float2 x[MAXW];
-  float ss = 0.f;
-  __nv_bfloat16* res = static_cast<__nv_bfloat16*>(a.residual);
+  publish(a, 0, E);
+  // 2. reduce the owned rows, push them to every rank
+  if (await(a, 0, E, budget, &give_up)) {
+    for (int row = blockIdx.x; row < M; row += G) {
+      const int owner = min(row / per, W - 1);
+      if (owner != a.rank) continue;
+      const __nv_bfloat16* src = static_cast<const __nv_bfloat16*>(a.part[a.rank]) + (size_t)(row - owner * per) * H;
+      const __nv_bfloat16* resid = static_cast<const __nv_bfloat16*>(a.residual) + (size_t)row * H;
+      for (int j = tid; j < L8; j += THREADS) {
+        uint4 v[8];
 #pragma unroll
-  for (int i = 0; i < MAXW; ++i) {
-    x[i] = make_float2(0.f, 0.f);
-    const int w = part * cw + tid + i * THREADS;
-    if (w >= (part + 1) * cw) continue;
-    float2 acc = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(res + (size_t)row * H + 2 * w));
-    for (int q = 0; q < W; ++q) {
-      const float2 v = unpack_bf16x2(wait_ll(slot(a.rank, q, w), E, budget, a.err, &give_up));
-      acc.x += v.x;
-      acc.y += v.y;
-    }
-    const uint32_t r = pack_bf16x2(acc.x, acc.y);
-    *reinterpret_cast<uint32_t*>(res + (size_t)row * H + 2 * w) = r;
-    x[i] = unpack_bf16x2(r);
-    ss += x[i].x * x[i].x + x[i].y * x[i].y;
-  }
-  // 3. row sum of squares: CTA partials exchanged through distributed shared memory
-  ss = warp_sum(ss);
-  if (lane == 0) red[tid >> 5] = ss;
-  __syncthreads();
-  if (tid == 0) {
-    float t = 0.f;
+        for (int q = 0; q < 8; ++q)
+          if (q < W) v[q] = __ldcg(reinterpret_cast<const uint4*>(src + (size_t)q * per * H) + j);
+        const uint4 ru = *reinterpret_cast<const uint4*>(resid + 8 * j);
+        float4 lo = bf16x4_to_f4(ru.x, ru.y), hi = bf16x4_to_f4(ru.z, ru.w);
 #pragma unroll
-    for (int i = 0; i < THREADS / 32; ++i) t += red[i];
-    cta_ss = t;
-  }
-  cluster.sync();
-  if (tid == 0) {
-    float t = 0.f;
-    for (int r = 0; r < SMALL_CTAS; ++r) t += *cluster.map_shared_rank(&cta_ss, r);
-    tot_ss = t;
-  }
-  cluster.sync();  // no CTA leaves while a peer may still read its cta_ss
-  const float rstd = rsqrtf(tot_ss / H + a.eps);
-  // 4. RMSNorm + MXFP8 of the slice (16 consecutive threads = one 32-column block)
-  const __nv_bfloat16* wgt = static_cast<const __nv_bfloat16*>(a.weight);
-#pragma unroll
-  for (int i = 0; i < MAXW; ++i) {
-    const int w = part * cw + tid + i * THREADS;
-    if (part * cw + (tid & ~15) + i * THREADS >= (part + 1) * cw) continue;  // whole block outside
-    const bool in = w < (part + 1) * cw;
-    const int c = 2 * w;
-    float y0 = 0.f, y1 = 0.f;
-    if (in) {
-      const float2 wv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(wgt + c));
-      y0 = x[i].x * rstd * (wv.x + a.w_offset);
-      y1 = x[i].y * rstd * (wv.y + a.w_offset);
-      if (a.normed) *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(a.normed) + (size_t)row * H + c) =
-          pack_bf16x2(y0, y1);
-    }
-    if (a.q) {
-      float amax = fmaxf(fabsf(y0), fabsf(y1));
-#pragma unroll
-      for (int o = 1; o < 16; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffff, amax, o));
-      const uint8_t code = mx_scale_e8m0(amax);
-      const float inv = mx_inv_scale(code);
-      if (in) {
-        const uint16_t pk = uint16_t(f32_to_e4m3(y0 * inv)) | (uint16_t(f32_to_e4m3(y1 * inv)) << 8);
-        *reinterpret_cast<uint16_t*>(a.q + (size_t)row * H + c) = pk;
-        if ((tid & 15) == 0) {
-          const int kb = c >> 5;
-          a.sf[((size_t)(row >> 7) * (H >> 7) + (kb >> 2)) * 512 + sf_atom_offset(row & 127, kb & 3)] = code;
+        for (int q = 0; q < 8; ++q) {
+          if (q >= W) break;
+          const float4 a0 = bf16x4_to_f4(v[q].x, v[q].y), a1 = bf16x4_to_f4(v[q].z, v[q].w);
+          lo.x += a0.x;
+          lo.y += a0.y;
+          lo.z += a0.z;
+          lo.w += a0.w;
+          hi.x += a1.x;
+          hi.y += a1.y;
+          hi.z += a1.z;
+          hi.w += a1.w;
         }
+        const uint4 r = make_uint4(pack_bf16x2(lo.x, lo.y), pack_bf16x2(lo.z, lo.w), pack_bf16x2(hi.x, hi.y),
+                                   pack_bf16x2(hi.z, hi.w));
+        for (int q = 0; q < W; ++q)
+          reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out[q]) + (size_t)row * H)[j] = r;
       }
     }
   }
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    const uint32_t done = atomicAdd(a.grid_counter, 1u) + 1;
-    if (done % gridDim.x == 0) *reinterpret_cast<volatile uint32_t*>(a.epoch) = E;
+  publish(a, 1, E);
+  // 3. gather + RMSNorm + MXFP8
+  if (await(a, 1, E, budget, &give_up)) {
+    for (int row = blockIdx.x; row < M; row += G) {
+      const uint2* ag = reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.out[a.rank]) +
+                                                       (size_t)row * H);
+      uint2 res[MAX_LPT];
+#pragma unroll
+      for (int i = 0; i < MAX_LPT; ++i)
+        if (i < lpt) res[i] = __ldcg(ag + tid + i * THREADS);
+      finish_row(a, row, lpt, res, red);
+    }
   }
+  finish_call(a.grid_counter, a.epoch, E);
 }
 
-// One-shot fp32 sum: each thread pushes its elements to every rank, then sums exactly the
-// elements it pushed, so a thread only ever waits for peers.
-__global__ void __launch_bounds__(THREADS) allreduce_sum_f32_kernel(const SumArArgs a) {
+// ---------------------------------------------------------------------------------
+// One-shot fp32 sum: line i = elements (2i, 2i+1); each thread pushes its lines to every
+// rank, then sums exactly the lines it pushed in rank order (so it only waits for peers).
+__global__ void __launch_bounds__(THREADS, 4) allreduce_sum_f32_kernel(const SumArArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int W = a.world;
-  const uint32_t E = *reinterpret_cast<volatile uint32_t*>(a.epoch) + 1;
+  const uint32_t E = read_epoch(a.epoch);
   const int par = E & 1;
-  const size_t n = (size_t)a.rows * a.cols;
-  const size_t stride = (size_t)a.max_rows * a.cols;
+  const size_t n = (size_t)a.rows * a.cols / 2;
+  const size_t stride = (size_t)a.max_rows * a.cols / 2;
   const uint64_t budget = limit_ns(a.timeout_ms);
   __shared__ int give_up;
   if (threadIdx.x == 0) give_up = 0;
   __syncthreads();
   const size_t step = (size_t)gridDim.x * THREADS;
+  const float2* data2 = reinterpret_cast<const float2*>(a.data);
   for (size_t i = (size_t)blockIdx.x * THREADS + threadIdx.x; i < n; i += step) {
-    const uint32_t v = __float_as_uint(a.data[i]);
+    const float2 v = data2[i];
     for (int q = 0; q < W; ++q)
-      st_ll(static_cast<uint2*>(a.buf[q]) + ((size_t)par * W + a.rank) * stride + i, v, E);
+      st_ll16(static_cast<uint4*>(a.buf[q]) + ((size_t)par * W + a.rank) * stride + i, __float_as_uint(v.x),
+              __float_as_uint(v.y), E);
   }
   for (size_t i = (size_t)blockIdx.x * THREADS + threadIdx.x; i < n; i += step) {
-    float acc = 0.f;
-    for (int q = 0; q < W; ++q)
-      acc += __uint_as_float(wait_ll(static_cast<const uint2*>(a.buf[a.rank]) + ((size_t)par * W + q) * stride + i, E,
-                                     budget, a.err, &give_up));
-    a.data[i] = acc;
+    uint4 v[8];
+    if (!wait_lines<8>(static_cast<const uint4*>(a.buf[a.rank]) + (size_t)par * W * stride + i, stride, W, E, v,
+                       budget, a.err, &give_up))
+      break;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      if (q >= W) break;
+      s0 += __uint_as_float(v[q].x);
+      s1 += __uint_as_float(v[q].z);
+    }
+    reinterpret_cast<float2*>(a.data)[i] = make_float2(s0, s1);
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const uint32_t done = atomicAdd(a.grid_counter, 1u) + 1;
-    if (done % gridDim.x == 0) *reinterpret_cast<volatile uint32_t*>(a.epoch) = E;
-  }
+  finish_call(a.grid_counter, a.epoch, E);
 }
 
-// Global argmax over vocab shards: keys[r] = per-row best packed key of rank r's shard
-// (ids already global).  Every rank max-reduces all W keys per row.
-__global__ void allreduce_argmax_kernel(const ArgmaxArArgs a) {
-  const uint32_t E = *reinterpret_cast<volatile uint32_t*>(a.epoch);
-  const int tid = threadIdx.x;
-  // Publish this rank's keys (already in its symmetric buffer), then barrier.
-  __shared__ int ok;
-  __threadfence_system();  // keys written by rebase_keys_kernel before the release
-  if (tid < a.world) st_release_sys(a.flags[tid] + 16 + a.rank, E + 1);
-  if (tid == 0) {
-    ok = 1;
-    for (int r = 0; r < a.world && ok; ++r) {
-      if (!wait_flag_sys(a.flags[a.rank] + 16 + r, E + 1, limit_ns(a.timeout_ms), nullptr)) {
-        ok = 0;
-        report_error(a.err, kErrPeerTimeout);
-      }
-    }
-  }
+// ---------------------------------------------------------------------------------
+// Global argmax: one warp per row reduces the row's tile keys, rebases the id to the
+// global vocabulary, and lane 0 pushes the key as one LL line to every rank's slot
+// [parity][rank][row]; then the warp waits for the W lines of the row and max-reduces.
+constexpr int ARGMAX_WARPS = 8;
+
+__global__ void __launch_bounds__(ARGMAX_WARPS * 32) allreduce_argmax_kernel(const ArgmaxArArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int W = a.world;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * ARGMAX_WARPS + warp;
+  const uint32_t E = read_epoch(a.epoch);
+  const int par = E & 1;
+  const uint64_t budget = limit_ns(a.timeout_ms);
+  __shared__ int give_up;
+  if (threadIdx.x == 0) give_up = 0;
   __syncthreads();
-  if (!ok) return;
-  for (int row = tid; row < a.rows; row += blockDim.x) {
+  if (row < a.rows) {
     unsigned long long best = 0;
-    for (int r = 0; r < a.world; ++r) {
-      const unsigned long long* kp = static_cast<const unsigned long long*>(a.keys[r]) + row;
-      unsigned long long k;
-      asm volatile("ld.global.cv.u64 %0, [%1];" : "=l"(k) : "l"(kp) : "memory");
+    for (int t = lane; t < a.tiles; t += 32) {
+      const unsigned long long k = a.tile_keys[(size_t)row * a.tiles + t];
       best = k > best ? k : best;
     }
-    if (a.out_ids) a.out_ids[row] = unpack_argmax_id(best);
-    if (a.out_vals) a.out_vals[row] = unpack_argmax_value(best);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffff, best, o);
+      best = other > best ? other : best;
+    }
+    // Rebase the local id (the logit half of the key is unchanged).
+    const int gid = unpack_argmax_id(best) + a.id_offset;
+    best = (best & 0xFFFFFFFF00000000ull) | static_cast<uint32_t>(~gid);
+    const size_t src_stride = (size_t)a.max_rows;
+    if (lane < W)
+      st_ll16(static_cast<uint4*>(a.lines[lane]) + ((size_t)par * W + a.rank) * src_stride + row,
+              static_cast<uint32_t>(best), static_cast<uint32_t>(best >> 32), E);
+    unsigned long long g = 0;
+    if (lane < W) {
+      uint4 v[1];
+      if (wait_lines<1>(static_cast<const uint4*>(a.lines[a.rank]) + ((size_t)par * W + lane) * src_stride + row, 0,
+                        1, E, v, budget, a.err, &give_up))
+        g = (static_cast<unsigned long long>(v[0].z) << 32) | v[0].x;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffff, g, o);
+      g = other > g ? other : g;
+    }
+    if (lane == 0) {
+      if (a.out_ids) a.out_ids[row] = unpack_argmax_id(g);
+      if (a.out_vals) a.out_vals[row] = unpack_argmax_value(g);
+    }
   }
-  __syncthreads();
-  // Second barrier: no rank may overwrite its keys before every peer has read them.
-  if (tid < a.world) st_release_sys(a.flags[tid] + 24 + a.rank, E + 1);
-  if (tid == 0) {
-    for (int r = 0; r < a.world; ++r)
-      if (!wait_flag_sys(a.flags[a.rank] + 24 + r, E + 1, limit_ns(a.timeout_ms), nullptr))
-        report_error(a.err, kErrPeerTimeout);
-    *reinterpret_cast<volatile uint32_t*>(a.epoch) = E + 1;
-  }
-}
-
-// Rebase per-row local argmax keys to global ids and store them in the symmetric
-// key buffer of this rank.
-__global__ void rebase_keys_kernel(const unsigned long long* __restrict__ local, int rows, int id_offset,
-                                   unsigned long long* __restrict__ out) {
-  const int row = blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= rows) return;
-  const unsigned long long k = local[row];
-  const int lid = unpack_argmax_id(k);
-  out[row] = (k & 0xFFFFFFFF00000000ull) | static_cast<uint32_t>(~(lid + id_offset));
+  finish_call(a.grid_counter, a.epoch, E);
 }
 
 }  // namespace coll
@@ -393,54 +535,49 @@ __global__ void rebase_keys_kernel(const unsigned long long* __restrict__ local,
 
 // ----------------------------------------------------------------------------------- host
 extern "C" int zs_fused_allreduce_norm(const FusedArArgs* args, cudaStream_t stream) {
+  using namespace zs::coll;
   const FusedArArgs& a = *args;
-  if (a.world < 1 || a.world > 8 || a.hidden % (zs::coll::THREADS * 8) != 0 || a.hidden > zs::coll::THREADS * 8 * 4)
-    return -1;
-  if (a.rows <= 0) return 0;
-  if (a.oneshot[0] != nullptr && a.rows <= FAR_SMALL_ROWS) {
-    // Slices of whole warps (words per CTA a multiple of 32) keep every shuffle warp-uniform.
-    if ((a.hidden / 2) % zs::coll::SMALL_CTAS != 0 || (a.hidden / 2) / zs::coll::SMALL_CTAS > zs::coll::THREADS * 4 ||
-        ((a.hidden / 2) / zs::coll::SMALL_CTAS) % 32 != 0)
+  if (a.world < 1 || a.world > 8 || a.hidden % (THREADS * 4) != 0 || a.hidden > THREADS * 4 * MAX_LPT) return -1;
+  for (int r = 0; r < a.world; ++r)
+    if (a.part[r] == nullptr || (a.protocol != FAR_ONESHOT && a.out[r] == nullptr) ||
+        (a.protocol == FAR_PLAIN && a.flags[r] == nullptr))
       return -1;
-    for (int r = 0; r < a.world; ++r)
-      if (a.oneshot[r] == nullptr) return -1;
-    zs::coll::fused_allreduce_norm_small_kernel<<<FAR_SMALL_ROWS * zs::coll::SMALL_CTAS, zs::coll::THREADS, 0, stream>>>(
-        a);
-    return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  if (a.rows <= 0) return 0;
+  cudaError_t e;
+  if (a.protocol == FAR_ONESHOT) {
+    if (a.rows > FAR_ONESHOT_ROWS) return -1;
+    e = zs_launch(ar_oneshot_kernel, a.rows, THREADS, 0, stream, a);
+  } else if (a.protocol == FAR_TWOSHOT) {
+    e = zs_launch(ar_twoshot_kernel, FAR_CTAS, THREADS, 0, stream, a);
+  } else if (a.protocol == FAR_PLAIN) {
+    e = zs_launch(ar_plain_kernel, FAR_CTAS, THREADS, 0, stream, a);
+  } else {
+    return -1;
   }
-  // Cooperative launch: the grid barrier needs all FAR_CTAS CTAs co-resident.
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(FAR_CTAS);
-  cfg.blockDim = dim3(zs::coll::THREADS);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, zs::coll::fused_allreduce_norm_kernel, a) == cudaSuccess ? 0 : -2;
+  return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
-extern "C" int zs_allreduce_argmax(const ArgmaxArArgs* args, const unsigned long long* local_keys, int id_offset,
-                                   cudaStream_t stream) {
+extern "C" int zs_allreduce_argmax(const ArgmaxArArgs* args, cudaStream_t stream) {
+  using namespace zs::coll;
   const ArgmaxArArgs& a = *args;
-  if (a.world < 1 || a.world > 8) return -1;
+  if (a.world < 1 || a.world > 8 || a.rows > a.max_rows || a.tiles <= 0) return -1;
+  for (int r = 0; r < a.world; ++r)
+    if (a.lines[r] == nullptr) return -1;
   if (a.rows <= 0) return 0;
-  zs::coll::rebase_keys_kernel<<<(a.rows + 255) / 256, 256, 0, stream>>>(
-      local_keys, a.rows, id_offset, static_cast<unsigned long long*>(const_cast<void*>(a.keys[a.rank])));
-  zs::coll::allreduce_argmax_kernel<<<1, 256, 0, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  const cudaError_t e =
+      zs_launch(allreduce_argmax_kernel, (a.rows + ARGMAX_WARPS - 1) / ARGMAX_WARPS, ARGMAX_WARPS * 32, 0, stream, a);
+  return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
 extern "C" int zs_allreduce_sum_f32(const SumArArgs* args, cudaStream_t stream) {
+  using namespace zs::coll;
   const SumArArgs& a = *args;
-  if (a.world < 1 || a.world > 8 || a.rows < 0 || a.rows > a.max_rows || a.cols <= 0) return -1;
+  if (a.world < 1 || a.world > 8 || a.rows < 0 || a.rows > a.max_rows || a.cols <= 0 || (a.cols & 1)) return -1;
   for (int r = 0; r < a.world; ++r)
     if (a.buf[r] == nullptr) return -1;
   if (a.rows == 0) return 0;
-  // A fixed grid keeps the completion counter a multiple of the grid across calls.
-  zs::coll::allreduce_sum_f32_kernel<<<SUM_CTAS, zs::coll::THREADS, 0, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  const cudaError_t e = zs_launch(allreduce_sum_f32_kernel, SUM_CTAS, THREADS, 0, stream, a);
+  return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
 // Symmetric memory helpers: raw cudaMalloc blocks shared through CUDA IPC.

@@ -10,9 +10,11 @@
 //   warp 4    : TMA / bulk-copy producer
 //   warp 5    : MMA issuer (one thread) + scale-factor TMEM staging (tcgen05.cp)
 // Accumulators are double-buffered in TMEM so the epilogue of tile i overlaps the
-// main loop of tile i+1.  Two instantiations: BN=128 (6 stages) for prefill-sized
-// token counts, BN=32 (9 stages) for decode, where each expert sees a few tokens and
-// the kernel is a weight stream that wants as many bytes in flight as possible.
+// main loop of tile i+1.  Each pipeline stage holds two K tiles (KT = 2).  Instantiations:
+// BN=128 with 3 stages for prefill-sized token counts, BN=32 with 4 stages for decode,
+// where each expert sees a few tokens and the kernel is a weight stream that wants as many
+// bytes in flight as shared memory allows; the MXFP4 variants use 2 and 3 stages (their
+// packed staging buffers take the rest).
 //
 // Operand formats (all produced by this library's quantizers):
 //   A  weights      e4m3 [G * Npad, K], K contiguous; Npad % 128 == 0, K % 128 == 0
@@ -202,8 +204,6 @@ __global__ void __launch_bounds__(Cfg<BN, STAGES, FP4>::THREADS, 1)
 gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
                  const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_b_full,
                  const GemmMxf8Args p) {
-  pdl_wait();  // predecessor kernel done: its outputs are visible
-  pdl_trigger();
   using C = Cfg<BN, STAGES, FP4>;
   using Smem = typename C::Smem;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -211,7 +211,10 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
   const int warp = warp_id();
   const int lane = lane_id();
   volatile int* abort_flag = &s.abort_flag;
+  const int k_tiles = p.k / BK;
 
+  // Set-up that reads nothing a predecessor kernel writes runs before the dependency wait,
+  // so under programmatic dependent launch it overlaps the previous kernel's tail.
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&s.full[i], 1);
@@ -226,13 +229,6 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
     s.abort_flag = 0;
     fence_barrier_init();
   }
-  if (p.chunk_prefix != nullptr) {
-    for (int g = threadIdx.x; g <= p.groups; g += C::THREADS) s.g_prefix[g] = __ldg(p.chunk_prefix + g);
-    for (int g = threadIdx.x; g < p.groups; g += C::THREADS) {
-      s.g_offset[g] = __ldg(p.group_offset + g);
-      s.g_count[g] = __ldg(p.group_count + g);
-    }
-  }
   if (warp == 0) {
     tmem_alloc(&s.tmem_base, C::TMEM_COLS);
     tmem_relinquish();
@@ -242,11 +238,64 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
     tma_prefetch_desc(&tmap_b);
     tma_prefetch_desc(&tmap_b_full);
   }
+  __syncthreads();  // barriers initialised before the producer arms them
+  // Weights never change during a step, so in dense mode the producer starts streaming
+  // the first item's weight stages (and their scales) before the dependency wait; the
+  // activation half of those stages is issued after it.  `pre` stages are armed here.
+  int pre = 0;
+  auto stage_bytes = [&](const Item& it, int n_sub) -> uint32_t {
+    const int n16 = (it.count + 15) >> 4;
+    const bool full_b = n16 * 16 == BN;
+    const int a_bytes = FP4 ? C::A4_BYTES : A_BYTES;
+    return n_sub * (a_bytes + 2 * SF_BYTES) + (full_b ? C::KT : n_sub) * n16 * 16 * BK;
+  };
+  auto issue_a = [&](const Item& it, int st, int kt, int n_sub) {
+    const int a_row = it.g * p.n_pad + it.m * BM;
+    if (FP4) {  // packed e2m1 tiles into the staging buffer; the converter warps widen them
+      bulk_load(s.a4[st][0], p.a + ((size_t)(a_row / BM) * k_tiles + kt) * C::A4_BYTES, n_sub * C::A4_BYTES,
+                &s.full[st]);
+    } else if (p.a_tiled) {  // pre-swizzled contiguous tiles: one plain bulk copy
+      bulk_load(s.a[st][0], p.a + ((size_t)(a_row / BM) * k_tiles + kt) * A_BYTES, n_sub * A_BYTES, &s.full[st]);
+    } else {
+      for (int j = 0; j < n_sub; ++j) tma_load_2d(s.a[st][j], &tmap_a, &s.full[st], (kt + j) * BK, a_row);
+    }
+    const uint8_t* sfa_src = p.sfa + ((size_t)(it.g * (p.n_pad / BM) + it.m) * k_tiles) * SF_BYTES;
+    bulk_load(s.sfa[st][0], sfa_src + (size_t)kt * SF_BYTES, n_sub * SF_BYTES, &s.full[st]);
+  };
+  // Activation half of a stage (after the dependency wait).
+  auto issue_b = [&](const Item& it, int st, int kt, int n_sub, int n16, int b_row, const uint8_t* sfb_src) {
+    if (n16 * 16 == BN) {
+      tma_load_3d(s.b[st][0], &tmap_b_full, &s.full[st], 0, b_row, kt);  // one BN-row x KT box
+    } else {
+      for (int t = 0; t < n_sub; ++t)
+        for (int j = 0; j < n16; ++j)
+          tma_load_2d(s.b[st][t] + j * 16 * BK, &tmap_b, &s.full[st], (kt + t) * BK, b_row + j * 16);
+    }
+    bulk_load(s.sfb[st][0], sfb_src + (size_t)kt * SF_BYTES, n_sub * SF_BYTES, &s.full[st]);
+  };
+  if (warp == 4 && lane == 0 && p.chunk_prefix == nullptr) {
+    Item it0;
+    if (get_item<BN>(p, blockIdx.x, it0, nullptr, nullptr, nullptr)) {
+      for (int kt = it0.kt0; kt < it0.kt1 && pre < STAGES; kt += C::KT, ++pre) {
+        const int n_sub = min(C::KT, it0.kt1 - kt);
+        mbar_expect_tx(&s.full[pre], stage_bytes(it0, n_sub));
+        issue_a(it0, pre, kt, n_sub);
+      }
+    }
+  }
+  pdl_wait();  // predecessor kernel done: its outputs (activations, group tables) are visible
+  pdl_trigger();
+  if (p.chunk_prefix != nullptr) {
+    for (int g = threadIdx.x; g <= p.groups; g += C::THREADS) s.g_prefix[g] = __ldg(p.chunk_prefix + g);
+    for (int g = threadIdx.x; g < p.groups; g += C::THREADS) {
+      s.g_offset[g] = __ldg(p.group_offset + g);
+      s.g_count[g] = __ldg(p.group_count + g);
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
-  const int k_tiles = p.k / BK;
 
   if (warp == 4) {
     // ------------------------------------------------------------------ producer
@@ -255,9 +304,7 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
       Item it;
       for (int idx = blockIdx.x; get_item<BN>(p, idx, it, s.g_prefix, s.g_offset, s.g_count) && !*abort_flag; idx += gridDim.x) {
         const int n16 = (it.count + 15) >> 4;
-        const int a_row = it.g * p.n_pad + it.m * BM;
         const int b_row = it.seg_off + it.c * BN;
-        const uint8_t* sfa_src = p.sfa + ((size_t)(it.g * (p.n_pad / BM) + it.m) * k_tiles) * SF_BYTES;
         const uint8_t* sfb_src = p.sfb + ((size_t)(b_row / BM) * k_tiles) * SF_BYTES;
         for (int kt = it.kt0; kt < it.kt1; kt += C::KT) {
           const int n_sub = min(C::KT, it.kt1 - kt);
@@ -266,28 +313,24 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
           if (issued >= STAGES && !wait_or_abort(&s.empty[st], ph, p.err, abort_flag)) break;
           // A full-height B box spans KT tiles (a tile past the end of K is zero-filled);
           // short chunks load n16 16-row boxes per tile.
-          const bool full_b = n16 * 16 == BN;
-          const int a_bytes = FP4 ? C::A4_BYTES : A_BYTES;
-          mbar_expect_tx(&s.full[st], n_sub * (a_bytes + 2 * SF_BYTES) + (full_b ? C::KT : n_sub) * n16 * 16 * BK);
-          if (FP4) {  // packed e2m1 tiles into the staging buffer; the converter warps widen them
-            bulk_load(s.a4[st][0], p.a + ((size_t)(a_row / BM) * k_tiles + kt) * C::A4_BYTES, n_sub * C::A4_BYTES,
-                      &s.full[st]);
-          } else if (p.a_tiled) {  // pre-swizzled contiguous tiles: one plain bulk copy
-            bulk_load(s.a[st][0], p.a + ((size_t)(a_row / BM) * k_tiles + kt) * A_BYTES, n_sub * A_BYTES,
-                      &s.full[st]);
-          } else {
-            for (int j = 0; j < n_sub; ++j) tma_load_2d(s.a[st][j], &tmap_a, &s.full[st], (kt + j) * BK, a_row);
+          if ((int)issued >= pre) {  // else: armed, weights requested before the dependency wait
+            mbar_expect_tx(&s.full[st], stage_bytes(it, n_sub));
+            issue_a(it, st, kt, n_sub);
           }
-          if (full_b) {
-            tma_load_3d(s.b[st][0], &tmap_b_full, &s.full[st], 0, b_row, kt);  // one BN-row x KT box
-          } else {
-            for (int t = 0; t < n_sub; ++t)
-              for (int j = 0; j < n16; ++j)
-                tma_load_2d(s.b[st][t] + j * 16 * BK, &tmap_b, &s.full[st], (kt + t) * BK, b_row + j * 16);
-          }
-          bulk_load(s.sfa[st][0], sfa_src + (size_t)kt * SF_BYTES, n_sub * SF_BYTES, &s.full[st]);
-          bulk_load(s.sfb[st][0], sfb_src + (size_t)kt * SF_BYTES, n_sub * SF_BYTES, &s.full[st]);
+          issue_b(it, st, kt, n_sub, n16, b_row, sfb_src);
           ++issued;
+        }
+      }
+      if ((int)issued < pre) {
+        // Aborted before reaching every armed stage: complete their activation halves too,
+        // so each copy in flight finishes its barrier and the drain below can see it land.
+        Item it0;
+        get_item<BN>(p, blockIdx.x, it0, nullptr, nullptr, nullptr);
+        for (; (int)issued < pre; ++issued) {
+          const int kt = it0.kt0 + (int)issued * C::KT;
+          const int b_row = it0.seg_off + it0.c * BN;
+          issue_b(it0, issued, kt, min(C::KT, it0.kt1 - kt), (it0.count + 15) >> 4, b_row,
+                  p.sfb + ((size_t)(b_row / BM) * k_tiles) * SF_BYTES);
         }
       }
       if (blockIdx.x == 0 && p.fix_splits > 1 && p.chunk_prefix != nullptr &&

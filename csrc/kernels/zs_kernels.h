@@ -244,22 +244,38 @@ int zs_moe_route(const MoeRouteArgs* args, cudaStream_t stream);
 // ----------------------------------------------------------------------------------
 // Fused tensor-parallel collectives over NVLink peer memory (symmetric buffers)
 // ----------------------------------------------------------------------------------
-#define FAR_CTAS 128  // persistent grid of the fused all-reduce (must be co-resident)
+#define FAR_CTAS 128  // grid of the two-shot all-reduces (co-resident; CTA c pairs with CTA c of every rank)
+
+// Protocols of zs_fused_allreduce_norm (the host picks one per call from the row count):
+//   FAR_ONESHOT  : every rank pushes its rows to every rank as 16-byte LL lines (two bf16
+//                  pairs + the call's epoch twice); one NVLink hop, parity-double-buffered.
+//   FAR_TWOSHOT  : LL lines to the row's owner, owner reduces and pushes the result to all.
+//   FAR_PLAIN    : two-shot with plain bf16 rows (no flag words: full link bandwidth); per
+//                  (source, CTA) flags published with a system-scope release after the
+//                  data, for prefill-sized reductions.
+#define FAR_ONESHOT 0
+#define FAR_TWOSHOT 1
+#define FAR_PLAIN 2
+#define FAR_ONESHOT_ROWS 64  // capacity (rows) of the one-shot buffers
 
 typedef struct FusedArArgs {
   int rank, world;
+  int protocol;              // FAR_ONESHOT / FAR_TWOSHOT / FAR_PLAIN
   const void* delta;         // local partial terms: delta[row*row_stride + t*term_stride + col]
   int n_terms;
   const int* term_index;     // optional gathered terms (as in zs_add_rmsnorm_quant)
   const float* term_scale;
   long long row_stride, term_stride;
   int delta_f32;             // terms are f32 (split-K partials) or bf16 (MoE pair rows)
-  void* part[8];             // symmetric bf16 [rows, hidden] per rank (local sum)
-  void* out[8];              // symmetric bf16 [rows, hidden] per rank (reduced owned rows)
-  uint32_t* flags[8];        // symmetric u32 [32] per rank (barrier slots)
-  uint32_t* epoch;           // local device counter (same sequence on every rank)
-  uint32_t* grid_counter;    // local device counter for the in-kernel grid barrier
-  const int* abort_word;     // optional device-visible abort flag (nonzero: give up waits)
+  // Symmetric buffers (per rank, this protocol's area):
+  //   ONESHOT: part = LL lines [2 parities][world][FAR_ONESHOT_ROWS][hidden/4]
+  //   TWOSHOT: part = LL lines [world][ceil(rows/world)][hidden/4], out = LL lines [rows][hidden/4]
+  //   PLAIN  : part = bf16 [world][ceil(rows/world)][hidden],       out = bf16 [rows][hidden]
+  void* part[8];
+  void* out[8];
+  uint32_t* flags[8];        // PLAIN: u32 [2][world][FAR_CTAS] per rank (phase, source, CTA)
+  uint32_t* epoch;           // local device counter of this protocol (same sequence on every rank)
+  uint32_t* grid_counter;    // local device counter: the last CTA of a call advances the epoch
   void* residual;            // bf16 [rows, hidden], replicated residual stream (in/out)
   const void* weight;        // RMSNorm weight
   float w_offset, eps;
@@ -269,20 +285,13 @@ typedef struct FusedArArgs {
   uint8_t* sf;
   int* err;
   unsigned int timeout_ms;   // bound on every cross-rank wait (0: 5000 ms)
-  // One-shot path for rows <= FAR_SMALL_ROWS (optional): symmetric flag-in-data words
-  // [2 parities][world][FAR_SMALL_ROWS][hidden/2] per rank; one 8-CTA cluster per row
-  // splits the columns and combines the RMSNorm sum of squares through distributed
-  // shared memory.  epoch / grid_counter must then be this path's own counters.
-  void* oneshot[8];
 } FusedArArgs;
-
-#define FAR_SMALL_ROWS 8
 
 int zs_fused_allreduce_norm(const FusedArArgs* args, cudaStream_t stream);
 
 // In-place fp32 sum over ranks of data[rows, cols] (one-shot push over NVLink, summed in
-// rank order so every rank gets the same bits).  buf: symmetric flag-in-data words
-// [2 parities][world][max_rows][cols] per rank.
+// rank order so every rank gets the same bits).  buf: symmetric LL lines (two floats +
+// epoch twice, 16 bytes) [2 parities][world][max_rows * cols / 2] per rank.
 typedef struct SumArArgs {
   int rank, world;
   float* data;
@@ -294,25 +303,29 @@ typedef struct SumArArgs {
   unsigned int timeout_ms;
 } SumArArgs;
 
-#define SUM_CTAS 148  // fixed grid of zs_allreduce_sum_f32
+#define SUM_CTAS 148  // grid of zs_allreduce_sum_f32
 
 int zs_allreduce_sum_f32(const SumArArgs* args, cudaStream_t stream);
 
+// Global greedy / sampled token over vocab shards in one kernel: each row's per-tile keys
+// of this rank's shard are max-reduced, rebased to global ids, pushed to every rank as one
+// LL line ([2 parities][world][max_rows] lines of 16 bytes per rank) and max-reduced over
+// the ranks.  Every rank ends with the same ids.
 typedef struct ArgmaxArArgs {
-  int rank, world, rows;
-  const void* keys[8];       // symmetric u64 [rows] per rank (global ids)
-  uint32_t* flags[8];
-  uint32_t* epoch;           // its own counter (not shared with the all-reduce)
+  int rank, world, rows, max_rows;
+  const unsigned long long* tile_keys;  // this rank's [rows, tiles] packed keys (local ids)
+  int tiles;
+  int id_offset;             // global id of this rank's first vocab entry
+  void* lines[8];            // symmetric LL line buffers
+  uint32_t* epoch;           // its own counter
+  uint32_t* grid_counter;
   int* out_ids;
   float* out_vals;
   int* err;
   unsigned int timeout_ms;   // bound on every cross-rank wait (0: 5000 ms)
 } ArgmaxArArgs;
 
-// local_keys: this rank's per-row best key over its vocab shard (local ids); ids are
-// rebased by id_offset and max-reduced across ranks.
-int zs_allreduce_argmax(const ArgmaxArArgs* args, const unsigned long long* local_keys, int id_offset,
-                        cudaStream_t stream);
+int zs_allreduce_argmax(const ArgmaxArArgs* args, cudaStream_t stream);
 
 // ----------------------------------------------------------------------------------
 // Expert-parallel MoE all-to-all over NVLink peer memory (ep.cu)

@@ -8,6 +8,7 @@ Exit code 0 = every check passed on this rank."""
 import datetime
 import os
 import sys
+import time
 
 import torch
 import torch.distributed as dist
@@ -18,7 +19,22 @@ from zstep_b200.ops import mx  # noqa: E402
 from zstep_b200.parallel.fused import FusedCollectives  # noqa: E402
 
 
+def _expected_residual(resid0, allp, rows, world, terms):
+    """bf16(resid + sum_r bf16(sum_t part_r[t])) summed in rank order."""
+    acc = resid0[:rows].float()
+    for r in range(world):
+        s = allp[r][0, :rows].clone()
+        for t in range(1, terms):
+            s = s + allp[r][t, :rows]
+        acc = acc + s.to(torch.bfloat16).float()
+    return acc.to(torch.bfloat16)
+
+
 def check_allreduce(coll, C, rank, world, dev):
+    """Every protocol (one-shot / two-shot LL / plain) at several row counts, against the
+    rank-ordered sum; rows past `rows` must stay untouched."""
+    from zstep_b200.parallel.fused import ONESHOT, PLAIN, TWOSHOT
+
     H, R = 2048, 96
     coll.reserve(R, H)
     g = torch.Generator(device=dev).manual_seed(100)
@@ -28,35 +44,66 @@ def check_allreduce(coll, C, rank, world, dev):
     # Each rank's split-K partials, [terms, R, H] f32 (rank-specific data).
     allp = [torch.randn(terms, R, H, generator=g, device=dev) for _ in range(world)]
     delta = allp[rank].contiguous()
-    for rows in (R, 37, 1, 5, 8):  # <= 8 rows take the one-shot cluster kernel
-        hidden = resid0.clone()
-        xq = torch.zeros(128 * ((R + 127) // 128), H, dtype=torch.uint8, device=dev)
-        xsf = torch.zeros(mx.atoms_bytes(xq.shape[0], H), dtype=torch.uint8, device=dev)
-        coll.allreduce_add_rmsnorm(delta, terms, H, R * H, hidden, w, 1e-6, rows, xq, xsf)
-        torch.cuda.synchronize()
-        assert coll.check_error() == 0
-        # Expected: bf16(resid + sum_r bf16(sum_t part_r[t])) in rank order.
-        acc = resid0[:rows].float()
-        for r in range(world):
-            s = allp[r][0, :rows].clone()
-            for t in range(1, terms):
-                s = s + allp[r][t, :rows]
-            acc = acc + s.to(torch.bfloat16).float()
-        exp = acc.to(torch.bfloat16)
-        assert torch.equal(hidden[:rows], exp), f"residual mismatch rows={rows}"
-        assert torch.equal(hidden[rows:], resid0[rows:]), "rows beyond `rows` were touched"
-        # Normed + quantized output vs the single-GPU norm kernel on the expected residual.
-        h2 = exp.clone()
-        xq2, xsf2 = torch.zeros_like(xq), torch.zeros_like(xsf)
-        C.add_rmsnorm_quant(h2, None, 0, H, H, w, 1.0, 1e-6, rows, None, xq2, xsf2)
-        d1 = mx.dequantize(xq[:rows], mx.codes_from_atoms(xsf, rows, H))
-        d2 = mx.dequantize(xq2[:rows], mx.codes_from_atoms(xsf2, rows, H))
-        torch.testing.assert_close(d1, d2, rtol=0.07, atol=1e-2)
+    for rows in (R, 37, 1, 5, 8, 64):
+        for proto in (ONESHOT, TWOSHOT, PLAIN):
+            if proto == ONESHOT and rows > 64:
+                continue
+            for rep in range(2):  # the second call reuses the buffers with the next epoch
+                hidden = resid0.clone()
+                xq = torch.zeros(128 * ((R + 127) // 128), H, dtype=torch.uint8, device=dev)
+                xsf = torch.zeros(mx.atoms_bytes(xq.shape[0], H), dtype=torch.uint8, device=dev)
+                coll.allreduce_add_rmsnorm(delta, terms, H, R * H, hidden, w, 1e-6, rows, xq, xsf, protocol=proto)
+                torch.cuda.synchronize()
+                assert coll.check_error() == 0, (rows, proto)
+                exp = _expected_residual(resid0, allp, rows, world, terms)
+                assert torch.equal(hidden[:rows], exp), f"residual mismatch rows={rows} protocol={proto}"
+                assert torch.equal(hidden[rows:], resid0[rows:]), "rows beyond `rows` were touched"
+            # Normed + quantized output vs the single-GPU norm kernel on the expected residual.
+            h2 = exp.clone()
+            xq2, xsf2 = torch.zeros_like(xq), torch.zeros_like(xsf)
+            C.add_rmsnorm_quant(h2, None, 0, H, H, w, 1.0, 1e-6, rows, None, xq2, xsf2)
+            assert torch.equal(xq[:rows], xq2[:rows]), f"MXFP8 rows differ rows={rows} protocol={proto}"
+            assert torch.equal(mx.codes_from_atoms(xsf, rows, H), mx.codes_from_atoms(xsf2, rows, H))
+
+
+def check_prefill_sized(coll, rank, world, dev):
+    """A prefill-sized reduction (2048 rows, hidden 4096 as in the DeepSeek shape) takes the
+    plain two-shot protocol; gathered MoE-style terms with weights."""
+    H, R = 4096, 2048
+    coll.close()
+    coll.reserve(R, H)
+    g = torch.Generator(device=dev).manual_seed(500)
+    resid0 = torch.randn(R, H, generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.rand(H, generator=g, device=dev) + 0.5).to(torch.bfloat16)
+    rows_y = 3 * R
+    ally = [torch.randn(rows_y, H, generator=g, device=dev).to(torch.bfloat16) for _ in range(world)]
+    idx = torch.randint(0, rows_y, (R, 2), generator=g, device=dev).to(torch.int32)
+    idx[::7, 1] = -1  # terms this rank did not produce
+    scale = torch.rand(R, 2, generator=g, device=dev)
+    hidden = resid0.clone()
+    xq = torch.zeros(R, H, dtype=torch.uint8, device=dev)
+    xsf = torch.zeros(mx.atoms_bytes(R, H), dtype=torch.uint8, device=dev)
+    assert coll.protocol_for(R) == 2
+    coll.allreduce_add_rmsnorm(ally[rank], 2, H, 0, hidden, w, 1e-6, R, xq, xsf, term_index=idx, term_scale=scale)
+    torch.cuda.synchronize()
+    assert coll.check_error() == 0
+    acc = resid0.float()
+    for r in range(world):
+        y = ally[r].float()
+        s = torch.zeros(R, H, device=dev)
+        for t in range(2):
+            ok = (idx[:, t] >= 0).unsqueeze(1)
+            s = s + torch.where(ok, y[idx[:, t].clamp(min=0).long()] * scale[:, t:t + 1], torch.zeros_like(s))
+        acc = acc + s.to(torch.bfloat16).float()
+    torch.testing.assert_close(hidden.float(), acc.to(torch.bfloat16).float(), rtol=1e-2, atol=1e-2)
+    coll.close()
 
 
 def check_graph_replay(coll, rank, world, dev):
-    """The kernels advance their own epochs: several replays of one graph stay correct."""
+    """The kernels advance their own epochs: several replays of one graph (one call of each
+    protocol in it) stay correct."""
     H, R = 2048, 64
+    coll.reserve(96, H)
     g = torch.Generator(device=dev).manual_seed(200 + rank)
     delta = torch.randn(R, H, generator=g, device=dev).to(torch.bfloat16)
     hidden = torch.zeros(R, H, dtype=torch.bfloat16, device=dev)
@@ -73,15 +120,17 @@ def check_graph_replay(coll, rank, world, dev):
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        coll.allreduce_add_rmsnorm(delta, 1, H, 0, hidden, w, 1e-6, R, xq, xsf)
+        for proto in (0, 1, 2):
+            coll.allreduce_add_rmsnorm(delta, 1, H, 0, hidden, w, 1e-6, R, xq, xsf, protocol=proto)
     hidden.zero_()
     exp = torch.zeros(R, H, device=dev).to(torch.bfloat16)
     for _ in range(4):
         graph.replay()
-        acc = exp.float()
-        for d in all_d:
-            acc = acc + d.float()
-        exp = acc.to(torch.bfloat16)
+        for _ in range(3):  # the graph holds three all-reduces
+            acc = exp.float()
+            for d in all_d:
+                acc = acc + d.float()
+            exp = acc.to(torch.bfloat16)
     torch.cuda.synchronize()
     assert coll.check_error() == 0
     assert torch.equal(hidden, exp), "graph replay mismatch"
@@ -127,6 +176,7 @@ def check_allreduce_sum(coll, rank, world, dev):
 def check_argmax(coll, rank, world, dev):
     from zstep_b200.ops import _ext
 
+    coll.reserve(96, 2048)
     rows, tiles, vloc = 50, 7, 7 * 128
     g = torch.Generator(device=dev).manual_seed(300)
     logits = [torch.randn(rows, vloc, generator=g, device=dev) for _ in range(world)]
@@ -149,6 +199,19 @@ def check_argmax(coll, rank, world, dev):
     assert torch.equal(out_ids.long(), i), "argmax ids"
     assert torch.equal(out_vals, v), "argmax values"
     del _ext
+
+
+TIE_MARGIN = 0.1  # two logits that each move by up to ~5e-2 (MXFP8 activations, bf16 rounding) can swap
+
+
+def _same_or_near_tie(got, want, ref_logits):
+    """Greedy tokens must equal the fp32 reference's, except where the reference itself
+    nearly ties: the token chosen must then be within TIE_MARGIN of the reference's best."""
+    for g_tok, w_tok, lg in zip(got, want, ref_logits):
+        if g_tok == w_tok:
+            continue
+        gap = float(lg[w_tok] - lg[g_tok])
+        assert gap < TIE_MARGIN, f"token {g_tok} != reference {w_tok} with reference margin {gap:.4f}"
 
 
 def check_model(coll, rank, world, dev):
@@ -177,12 +240,13 @@ def check_model(coll, rank, world, dev):
     first = runner.prefill_forward(len(ids), len(lens)).cpu().tolist()
     assert runner.check_error() == 0
     states = [ref.new_state() for _ in lens]
-    ref_next = []
+    ref_next, first_logits = [], []
     for s, p in enumerate(prompts):
         for t in p:
             lg = ref.step(states[s], t)
         ref_next.append(int(lg.argmax()))
-    assert sum(int(a == b) for a, b in zip(first, ref_next)) >= 2, (first, ref_next)
+        first_logits.append(lg)
+    _same_or_near_tie(first, ref_next, first_logits)
     # Every rank must produce the same tokens (the fused reductions are rank-order fixed).
     gathered = [None] * world
     dist.all_gather_object(gathered, first)
@@ -193,18 +257,49 @@ def check_model(coll, rank, world, dev):
         runner.stage(toks, p_now, list(range(3)))
         out = runner.decode_step(3).cpu().tolist()
         assert runner.check_error() == 0
-        ref_out, ref_l = [], []
+        ref_out, ref_l, ref_lg = [], [], []
         for s in range(3):
             lg = ref.step(states[s], toks[s])
             ref_out.append(int(lg.argmax()))
             ref_l.append(lg.max().item())
+            ref_lg.append(lg)
         vals = runner.buf["out_vals"][:3].cpu()
         torch.testing.assert_close(vals, torch.tensor(ref_l), rtol=3e-2, atol=3e-2)
-        assert sum(int(a == b) for a, b in zip(out, ref_out)) >= 2, (step, out, ref_out)
+        _same_or_near_tie(out, ref_out, ref_lg)
         dist.all_gather_object(gathered, out)
         assert all(x == out for x in gathered), gathered
         toks = ref_out
     runner.graphs.clear()
+
+
+def check_peer_timeout(coll, rank, world, dev):
+    """Bounded device waits: rank 1 skips one all-reduce between steps (its GPU runs
+    nothing), so rank 0's kernel must give up after timeout_ms, report kErrPeerTimeout (2)
+    and return.  After a collective reset every rank's next call succeeds again."""
+    H, R = 2048, 32
+    coll.reserve(R, H)
+    coll.timeout_ms = 50
+    delta = torch.ones(R, H, dtype=torch.bfloat16, device=dev)
+    hidden = torch.zeros(R, H, dtype=torch.bfloat16, device=dev)
+    w = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    xq = torch.zeros(128, H, dtype=torch.uint8, device=dev)
+    xsf = torch.zeros(mx.atoms_bytes(128, H), dtype=torch.uint8, device=dev)
+    for proto in (0, 1, 2):
+        dist.barrier()
+        if rank != 1:
+            t0 = time.time()
+            coll.allreduce_add_rmsnorm(delta, 1, H, 0, hidden, w, 1e-6, R, xq, xsf, protocol=proto)
+            torch.cuda.synchronize()
+            assert time.time() - t0 < 5.0
+            assert coll.check_error() == 2, (proto, coll.check_error())
+        dist.barrier()
+        coll.reset()
+        hidden.zero_()
+        coll.allreduce_add_rmsnorm(delta, 1, H, 0, hidden, w, 1e-6, R, xq, xsf, protocol=proto)
+        torch.cuda.synchronize()
+        assert coll.check_error() == 0
+        assert torch.equal(hidden, torch.full_like(hidden, float(world))), proto
+    coll.close()
 
 
 def main():
@@ -223,6 +318,10 @@ def main():
         check_graph_replay(coll, rank, world, dev)
         check_argmax(coll, rank, world, dev)
         check_allreduce_sum(coll, rank, world, dev)
+        check_prefill_sized(coll, rank, world, dev)
+        coll = FusedCollectives(dev)
+        if world > 1:
+            check_peer_timeout(coll, rank, world, dev)
         what = os.environ.get("ZSTEP_MP_CHECKS", "all")
         if what == "all":
             coll.close()

@@ -21,7 +21,7 @@ def _port() -> int:
 
 
 @pytest.mark.timeout(900)
-@pytest.mark.parametrize("world", [1, 2])  # one rank still runs every kernel, pushing to itself
+@pytest.mark.parametrize("world", [1, 2, 4, 8])  # one rank still runs every kernel, pushing to itself
 def test_fused_collectives_and_tp_model(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")

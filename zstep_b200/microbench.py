@@ -267,21 +267,26 @@ def cmd_gemm(a):
         out = torch.empty(rows_out, a.n, dtype=torch.bfloat16, device="cuda")
     ldo = out.shape[1]
     if a.groups == 1:
-        bn = 32 if a.m <= 32 else 128
+        bn = a.bn or (32 if a.m <= 32 else 128)
+        ws = torch.zeros(8 << 20, dtype=torch.float32, device="cuda")
+        sem = torch.zeros(16384, dtype=torch.int32, device="cuda")
         fn = lambda: C.gemm_mxf8(pw.q, pw.sf, xq, xsf, a.k, pw.n_pad, a.n, 1, a.m, None, None, None, a.epi, out,  # noqa
-                                 ldo, out_sf, None, None, None, 0, bn, 1, 0, 1)
+                                 ldo, out_sf, None, None, None, 0, bn, 1, 0, 1, a.fix_splits, ws, sem)
     else:
         cnt = torch.full((a.groups,), a.m, dtype=torch.int32, device="cuda")
         off = torch.arange(a.groups, dtype=torch.int32, device="cuda") * _pad128_(a.m)
         bn = 32 if a.m <= 32 else 128
         pre = torch.arange(a.groups + 1, dtype=torch.int32, device="cuda") * ((a.m + bn - 1) // bn)
+        ws = torch.zeros(8 << 20, dtype=torch.float32, device="cuda")
+        sem = torch.zeros(16384, dtype=torch.int32, device="cuda")
         fn = lambda: C.gemm_mxf8(pw.q, pw.sf, xq, xsf, a.k, pw.n_pad, a.n, a.groups, 0, cnt, off, pre, a.epi,  # noqa
-                                 out, ldo, out_sf, None, None, None, 0, bn, 1, 0, 1)
+                                 out, ldo, out_sf, None, None, None, 0, bn, 1, 0, 1, a.fix_splits, ws, sem)
     ms = time_fn(fn, flush=bool(a.flush))
     pk = peaks()
     flops = 2.0 * a.m * a.n * a.k * a.groups
     bytes_ = a.n * a.k * a.groups * (1 + 1 / 32) + a.m * a.k * a.groups + a.m * a.n * 2 * a.groups
-    res = {"op": "gemm_mxf8", "m": a.m, "n": a.n, "k": a.k, "groups": a.groups, "epi": a.epi, "ms": round(ms, 4),
+    res = {"op": "gemm_mxf8", "m": a.m, "n": a.n, "k": a.k, "groups": a.groups, "epi": a.epi,
+           "fix_splits": a.fix_splits, "ms": round(ms, 4),
            "tflops": round(flops / ms / 1e9, 1), "gbs": round(bytes_ / ms / 1e6, 1),
            "frac_fp8_peak": round(flops / ms / 1e9 / (2 * pk["bf16_tflops"]), 3),
            "frac_hbm": round(bytes_ / ms / 1e6 / pk["hbm_gbs"], 3), "peaks": pk["src"]}
@@ -453,6 +458,8 @@ def main():
     ap.add_argument("--model", default="qwen", choices=["qwen", "deepseek"])
     ap.add_argument("--splits", type=int, default=0, help="attn: split-KV factor (0 = the runner's choice)")
     ap.add_argument("--epi", type=int, default=0, help="gemm: 0 bf16 store, 2 SiLU(gate)*up + MXFP8")
+    ap.add_argument("--fix-splits", type=int, default=1, help="gemm (dense): in-kernel split-K factor")
+    ap.add_argument("--bn", type=int, default=0, help="gemm (dense): token tile 32 or 128 (0 = by rows)")
     ap.add_argument("--impl", type=int, default=0, help="attn: 0 tensor-core decode, 1 SIMT decode")
     a = ap.parse_args()
     torch.manual_seed(0)

@@ -210,6 +210,8 @@ class DeepSeekRunner:
         R = max(self.max_seqs, self.max_prefill_tokens)
         Rp = _pad128(R)
         self.R = R
+        if self.tp > 1 and hasattr(self.coll, "reserve"):
+            self.coll.reserve(R, H)  # symmetric buffers of the NVLink sublayer sums
         i32 = dict(dtype=torch.int32, device=dev)
         f32 = dict(dtype=torch.float32, device=dev)
         u8 = dict(dtype=torch.uint8, device=dev)

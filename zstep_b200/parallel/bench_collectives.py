@@ -10,7 +10,9 @@ Run one rank per GPU::
 Each case captures `calls` back-to-back calls in one CUDA graph, replays it `reps` times
 between CUDA events and reports the median per call, max over ranks.  Roofline for the
 all-reduce: a two-shot all-reduce moves 2 (W-1)/W * M * H * 2 bytes out of every GPU, so
-the bound is that over the measured 770 GB/s per-direction peer bandwidth.  Expert
+the bound is that over the measured 770 GB/s per-direction peer bandwidth.  Every protocol
+of the fused kernel (one-shot LL, two-shot LL, two-shot plain) is timed where it applies;
+``fused_us`` is the one the runner picks for that row count.  Expert
 all-to-all (hidden 4096, top-8 of 256 experts, uniform random routing): every pair whose
 expert lives on another rank moves one MXFP8 row (hidden + hidden/32 + 8 bytes) out on
 dispatch and one bf16 row (2 * hidden bytes) back on combine; the NCCL baseline is
@@ -29,7 +31,7 @@ import torch.distributed as dist
 from ..ops import _ext, mx
 from .collectives import NcclCollectives
 from ..utils.env import dist_env
-from .fused import FusedCollectives
+from .fused import FAR_ONESHOT_ROWS, ONESHOT, PLAIN, TWOSHOT, FusedCollectives
 
 LINK_GBS = 770.0  # measured peer copy bandwidth per direction per GPU on this pool
 
@@ -71,28 +73,38 @@ def main():
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     C = _ext.load()
-    H, R = 2048, 4096
-    fused = FusedCollectives(dev, max_rows=R, hidden=H)
+    R = 4096
+    fused = FusedCollectives(dev)
     nccl = NcclCollectives(None, dev)
-    w = torch.randn(H, device=dev).to(torch.bfloat16)
-    hidden = torch.zeros(R, H, dtype=torch.bfloat16, device=dev)
-    delta = (0.01 * torch.randn(R, H, device=dev)).to(torch.bfloat16)
-    xq = torch.zeros(R, H, dtype=torch.uint8, device=dev)
-    xsf = torch.zeros(mx.atoms_bytes(R, H), dtype=torch.uint8, device=dev)
     results = []
-    for m in (1, 8, 32, 128, 256, 1024, 4096):
-        row = {"op": "allreduce_add_rmsnorm_mxfp8", "world": world, "rows": m, "hidden": H}
-        calls = 50 if m <= 256 else 10
-        for name, coll in (("fused", fused), ("nccl", nccl)):
-            row[f"{name}_us"] = round(1000 * _time_graph(
-                lambda: coll.allreduce_add_rmsnorm(delta, 1, H, 0, hidden, w, 1e-6, m, xq, xsf), calls, 10), 2)
-        link_bytes = 2 * (world - 1) / world * m * H * 2
-        bound_us = link_bytes / (LINK_GBS * 1e3)
-        row["nvlink_bytes_per_gpu"] = int(link_bytes)
-        row["roofline_us"] = round(bound_us, 3)
-        row["fused_frac_of_roofline"] = round(bound_us / row["fused_us"], 4)
-        row["speedup_vs_nccl"] = round(row["nccl_us"] / row["fused_us"], 3)
-        results.append(row)
+    names = {ONESHOT: "oneshot", TWOSHOT: "twoshot_ll", PLAIN: "twoshot_plain"}
+    for H in (2048, 4096):
+        fused.reserve(R, H)
+        w = torch.randn(H, device=dev).to(torch.bfloat16)
+        hidden = torch.zeros(R, H, dtype=torch.bfloat16, device=dev)
+        delta = (0.01 * torch.randn(R, H, device=dev)).to(torch.bfloat16)
+        xq = torch.zeros(R, H, dtype=torch.uint8, device=dev)
+        xsf = torch.zeros(mx.atoms_bytes(R, H), dtype=torch.uint8, device=dev)
+        for m in (1, 8, 32, 64, 128, 256, 512, 1024, 4096):
+            row = {"op": "allreduce_add_rmsnorm_mxfp8", "world": world, "rows": m, "hidden": H,
+                   "auto_protocol": names[fused.protocol_for(m)]}
+            calls = 50 if m <= 256 else 10
+            for proto in (ONESHOT, TWOSHOT, PLAIN):
+                if (proto == ONESHOT and m > FAR_ONESHOT_ROWS) or (proto == TWOSHOT and m > fused.ll_cap):
+                    continue
+                row[f"{names[proto]}_us"] = round(1000 * _time_graph(
+                    lambda: fused.allreduce_add_rmsnorm(delta, 1, H, 0, hidden, w, 1e-6, m, xq, xsf, protocol=proto),
+                    calls, 10), 2)
+            row["fused_us"] = row[f"{row['auto_protocol']}_us"]
+            row["nccl_us"] = round(1000 * _time_graph(
+                lambda: nccl.allreduce_add_rmsnorm(delta, 1, H, 0, hidden, w, 1e-6, m, xq, xsf), calls, 10), 2)
+            link_bytes = 2 * (world - 1) / world * m * H * 2
+            bound_us = link_bytes / (LINK_GBS * 1e3)
+            row["nvlink_bytes_per_gpu"] = int(link_bytes)
+            row["roofline_us"] = round(bound_us, 3)
+            row["fused_frac_of_roofline"] = round(bound_us / row["fused_us"], 4)
+            row["speedup_vs_nccl"] = round(row["nccl_us"] / row["fused_us"], 3)
+            results.append(row)
     # Vocab-sharded lm_head argmax exchange (256 rows, 8 local tiles of 128 ids).
     for rows in (1, 256):
         tiles = 8

@@ -6,9 +6,10 @@ Two implementations share one interface:
   then the residual-add + RMSNorm + MXFP8 kernel; global argmax via an int64 MAX
   all-reduce of packed (logit, ~id) keys.
 * ``FusedCollectives`` (parallel/fused.py) -- the product path: one sm_100a kernel
-  that pulls the peers' partial sums over NVLink (P2P loads from symmetric memory),
-  reduces them in a fixed rank order (bit-identical on every rank), and applies the
-  residual add, RMSNorm and MXFP8 quantization in the same pass.
+  that pushes each rank's partial sums into its peers' symmetric memory over NVLink
+  (P2P stores of flag-carrying LL lines; every load is local), reduces them in a fixed
+  rank order (bit-identical on every rank), and applies the residual add, RMSNorm and
+  MXFP8 quantization in the same pass.
 
 ``allreduce_add_rmsnorm`` takes the local contribution as ``n_terms`` partial terms
 (split-K partials or MoE pair rows) addressed as ``delta[row*row_stride + t*term_stride

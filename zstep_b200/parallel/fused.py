@@ -2,26 +2,27 @@
 
 Each rank allocates one symmetric block with ``cudaMalloc`` and shares it with its
 peers through CUDA IPC; every rank then holds device pointers to all W blocks and the
-sm_100a kernels in csrc/kernels/collective.cu load and store peer memory directly.
-Block layout (all offsets 256-byte aligned)::
+sm_100a kernels in csrc/kernels/collective.cu store into peer memory directly (every
+protocol is push-based: kernels load only their own memory).  Block layout (all offsets
+256-byte aligned; R = reserved rows, H = hidden, S = ``sum_rows``, Rl = LL two-shot rows)::
 
-    [flags: 32 x u32][argmax keys: R x u64][rs words: (R+W) x H/2 x 8 B][ag words: R x H/2 x 8 B]
-    [one-shot words: 2 x W x 8 x H/2 x 8 B][fp32 sum words: 2 x W x S x H x 8 B]
+    [plain flags: 2 x 8 x FAR_CTAS u32][argmax lines: 2 x W x R x 16 B]
+    [one-shot lines: 2 x W x 64 x H/4 x 16 B]
+    [two-shot LL: (Rl + W) x H/4 x 16 B  +  Rl x H/4 x 16 B]
+    [plain two-shot: (R + W) x H x 2 B  +  R x H x 2 B][fp32 sum lines: 2 x W x S x H/2 x 16 B]
 
-Reductions of at most 8 rows take the one-shot cluster kernel (one NVLink hop instead
-of two; an 8-CTA cluster per row shares the RMSNorm statistics through distributed
-shared memory).  ``allreduce_sum`` (the mHC model's fp32 sublayer outputs) is a one-shot
-push of flag-in-data words for up to S = ``sum_rows`` rows and NCCL above that.
+Protocol by row count (``allreduce_add_rmsnorm``): up to ``ZSTEP_COLL_ONESHOT_ROWS``
+rows one-shot (one NVLink hop), up to ``ZSTEP_COLL_LL_ROWS`` two-shot with LL lines
+(data and epoch in one store, no barrier), above that two-shot with plain bf16 rows and
+per-CTA release/acquire flags (full link bandwidth for prefill-sized reductions).  NCCL
+is only used when ``ZSTEP_COLLECTIVES=nccl`` selects the baseline.
 
-The all-reduce moves "flag-in-data" words (32 bits of payload + the call's epoch in one
-8-byte store), so it needs no separate barrier; flags 16-31 belong to the argmax
-exchange.  The epoch words and the completion counter are rank-local device memory; the
-kernels advance them themselves, so every call (eager or CUDA-graph replay) uses fresh
-flag values and nothing needs resetting between steps.
-
-The collectives are issued by every rank in the same order (the model's layer order),
-which is what the kernels' epochs rely on.  Waits are bounded: a peer that never
-arrives makes the kernel record ``kErrPeerTimeout`` (2) in ``err`` and return.
+Epoch words and completion counters are rank-local device memory, one pair per protocol;
+the kernels advance them themselves, so every call (eager or CUDA-graph replay) uses
+fresh flag values and nothing needs resetting between steps.  The collectives are issued
+by every rank in the same order (the model's layer order), which is what the epochs rely
+on.  Waits are bounded: a peer that never arrives makes the kernel record
+``kErrPeerTimeout`` (2) in ``err`` and return.
 
 Reference parity: worker/zstep_worker/kernels_sm120/shm_allreduce.py:437 (host-SHM
 all-reduce + residual + RMSNorm) and csrc/qwen35_ops_kernels.cu:202 (TP argmax).
@@ -42,6 +43,13 @@ def _up(x: int, a: int = _ALIGN) -> int:
     return (x + a - 1) // a * a
 
 
+FAR_CTAS = 128          # csrc/kernels/zs_kernels.h
+FAR_ONESHOT_ROWS = 64   # csrc/kernels/zs_kernels.h
+ONESHOT, TWOSHOT, PLAIN = 0, 1, 2
+# Epoch / completion-counter slots, one per kernel family.
+_E_ONE, _E_TWO, _E_PLAIN, _E_ARGMAX, _E_SUM = range(5)
+
+
 class FusedCollectives:
     def __init__(self, device, group=None, max_rows: int = 0, hidden: int = 0, sum_rows: int = 64):
         self.C = _ext.load()
@@ -55,13 +63,14 @@ class FusedCollectives:
         self.hidden = 0
         self._base = 0
         self._peers: list[int] = []
-        self.epoch = torch.zeros(4, dtype=torch.int32, device=self.device)  # [ar, argmax, one-shot ar, sum]
-        self.grid = torch.zeros(3, dtype=torch.int32, device=self.device)  # completion counters per kernel
+        self.epoch = torch.zeros(5, dtype=torch.int32, device=self.device)
+        self.grid = torch.zeros(5, dtype=torch.int32, device=self.device)
         self.sum_rows = sum_rows
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
-        self.local_keys = None
-        self.timeout_ms = runtime_config().coll_timeout_ms  # bound on every cross-rank wait
-        self.large_rows = 1024
+        cfg = runtime_config()
+        self.timeout_ms = cfg.coll_timeout_ms  # bound on every cross-rank wait
+        self.oneshot_rows = min(cfg.coll_oneshot_rows, FAR_ONESHOT_ROWS)
+        self.ll_rows = cfg.coll_ll_rows
         from .collectives import NcclCollectives
 
         self.nccl = NcclCollectives(group, self.device)
@@ -74,15 +83,27 @@ class FusedCollectives:
         if max_rows <= self.max_rows and hidden == self.hidden:
             return
         self.close()
-        R, H = max_rows, hidden
-        # Reduce-scatter and all-gather buffers hold flag-in-data words: 8 bytes per two
-        # bf16 values (the reduce-scatter side is [world][ceil(R/world)][H/2]).
-        self.off_keys = _up(32 * 4)
-        self.off_part = self.off_keys + _up(R * 8)
-        self.off_out = self.off_part + _up((R + self.world) * H * 4)
-        self.off_small = self.off_out + _up(R * H * 4)
-        self.off_sum = self.off_small + _up(2 * self.world * 8 * H * 4)
-        self.nbytes = self.off_sum + _up(2 * self.world * self.sum_rows * H * 8)
+        R, H, W = max_rows, hidden, self.world
+        Rl = min(R, self.ll_rows)
+        self.ll_cap = Rl
+        off = 0
+        self.off_flags = off
+        off += _up(2 * 8 * FAR_CTAS * 4)
+        self.off_argmax = off
+        off += _up(2 * W * R * 16)
+        self.off_one = off
+        off += _up(2 * W * FAR_ONESHOT_ROWS * H * 4)
+        self.off_ll_part = off
+        off += _up((Rl + W) * H * 4)
+        self.off_ll_out = off
+        off += _up(Rl * H * 4)
+        self.off_plain_part = off
+        off += _up((R + W) * H * 2)
+        self.off_plain_out = off
+        off += _up(R * H * 2)
+        self.off_sum = off
+        off += _up(2 * W * self.sum_rows * H * 8)
+        self.nbytes = off
         with torch.cuda.device(self.device):
             self._base = self.C.symm_alloc(self.nbytes)
             handle = self.C.ipc_handle(self._base)
@@ -92,13 +113,13 @@ class FusedCollectives:
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
         self.max_rows, self.hidden = R, H
-        self.flag_ptrs = [p for p in self._peers]
-        self.key_ptrs = [p + self.off_keys for p in self._peers]
-        self.part_ptrs = [p + self.off_part for p in self._peers]
-        self.out_ptrs = [p + self.off_out for p in self._peers]
-        self.small_ptrs = [p + self.off_small for p in self._peers]
-        self.sum_ptrs = [p + self.off_sum for p in self._peers]
-        self.local_keys = torch.zeros(R, dtype=torch.int64, device=self.device)
+        at = lambda o: [p + o for p in self._peers]  # noqa: E731
+        self.flag_ptrs = at(self.off_flags)
+        self.argmax_ptrs = at(self.off_argmax)
+        self.one_ptrs = at(self.off_one)
+        self.ll_part_ptrs, self.ll_out_ptrs = at(self.off_ll_part), at(self.off_ll_out)
+        self.plain_part_ptrs, self.plain_out_ptrs = at(self.off_plain_part), at(self.off_plain_out)
+        self.sum_ptrs = at(self.off_sum)
 
     def close(self) -> None:
         if not self._base:
@@ -116,44 +137,65 @@ class FusedCollectives:
         return int(self.err.item())
 
     # ---------------------------------------------------------------- ops
+    def protocol_for(self, rows: int) -> int:
+        if rows <= self.oneshot_rows:
+            return ONESHOT
+        if rows <= self.ll_cap:
+            return TWOSHOT
+        return PLAIN
+
     def allreduce_add_rmsnorm(self, delta, n_terms: int, row_stride: int, term_stride: int, hidden_buf,
-                              norm_w, eps: float, rows: int, xq, xsf, term_index=None, term_scale=None) -> None:
+                              norm_w, eps: float, rows: int, xq, xsf, term_index=None, term_scale=None,
+                              protocol: int | None = None) -> None:
         """hidden_buf[:rows] += sum over ranks of the local term sums; then RMSNorm(norm_w)
         -> MXFP8 (xq, xsf).  Every rank ends with the same bf16 residual stream."""
         H = hidden_buf.shape[-1]
         if rows > self.max_rows or H != self.hidden:
             raise ValueError(f"fused all-reduce reserved for {self.max_rows}x{self.hidden}, got {rows}x{H}")
-        if rows > self.large_rows:
-            # Prefill-sized reductions are bandwidth-bound: the flag-in-data protocol moves
-            # twice the bytes, so large ones go through NCCL's ring/NVLS kernels.
-            self.nccl.allreduce_add_rmsnorm(delta, n_terms, row_stride, term_stride, hidden_buf, norm_w, eps, rows,
-                                            xq, xsf, term_index=term_index, term_scale=term_scale)
-            return
-        if rows <= 8 and (H // 16) % 32 == 0:
-            self.C.fused_allreduce_norm(self.rank, self.world, delta, n_terms, row_stride, term_stride,
-                                        self.part_ptrs, self.out_ptrs, self.flag_ptrs, self.epoch[2:3], self.grid[1:2],
-                                        hidden_buf, norm_w, 1.0, eps, rows, None, xq, xsf, self.err, term_index,
-                                        term_scale, self.timeout_ms, oneshot=self.small_ptrs)
-            return
-        self.C.fused_allreduce_norm(self.rank, self.world, delta, n_terms, row_stride, term_stride, self.part_ptrs,
-                                    self.out_ptrs, self.flag_ptrs, self.epoch[0:1], self.grid[0:1], hidden_buf, norm_w,
-                                    1.0, eps, rows, None, xq, xsf, self.err, term_index, term_scale,
-                                    self.timeout_ms)
+        proto = self.protocol_for(rows) if protocol is None else protocol
+        if proto == ONESHOT:
+            part, out, flags, e = self.one_ptrs, [], [], _E_ONE
+        elif proto == TWOSHOT:
+            if rows > self.ll_cap:
+                raise ValueError(f"LL two-shot buffers hold {self.ll_cap} rows, got {rows}")
+            part, out, flags, e = self.ll_part_ptrs, self.ll_out_ptrs, [], _E_TWO
+        else:
+            part, out, flags, e = self.plain_part_ptrs, self.plain_out_ptrs, self.flag_ptrs, _E_PLAIN
+        self.C.fused_allreduce_norm(self.rank, self.world, proto, delta, n_terms, row_stride, term_stride, part, out,
+                                    flags, self.epoch[e:e + 1], self.grid[e:e + 1], hidden_buf, norm_w, 1.0, eps,
+                                    rows, None, xq, xsf, self.err, term_index, term_scale, self.timeout_ms)
 
     def allreduce_sum(self, t: torch.Tensor) -> None:
         """In-place fp32 sum over ranks of t [rows, hidden] (mHC sublayer outputs): one-shot
-        over NVLink up to ``sum_rows`` rows, NCCL above (bandwidth-bound sizes)."""
+        LL lines over NVLink up to ``sum_rows`` rows, NCCL above (bandwidth-bound sizes)."""
         if t.dim() == 2 and t.shape[1] == self.hidden and t.shape[0] <= self.sum_rows and t.dtype == torch.float32 \
                 and t.is_contiguous():
             self.C.allreduce_sum_f32(self.rank, self.world, t, t.shape[0], self.sum_rows, self.sum_ptrs,
-                                     self.epoch[3:4], self.grid[2:3], self.err, self.timeout_ms)
+                                     self.epoch[_E_SUM:_E_SUM + 1], self.grid[_E_SUM:_E_SUM + 1], self.err,
+                                     self.timeout_ms)
             return
         self.nccl.allreduce_sum(t)
 
     def argmax_allreduce(self, keys, rows: int, tiles: int, id_offset: int, out_ids, out_vals) -> None:
-        """Global greedy token per row from per-tile packed keys of this rank's vocab shard."""
+        """Global greedy token per row from per-tile packed keys of this rank's vocab shard
+        (one kernel: tile reduction, id rebase, LL exchange, max over ranks)."""
         if rows > self.max_rows:
             raise ValueError(f"fused argmax reserved for {self.max_rows} rows, got {rows}")
-        self.C.argmax_reduce(keys, rows, tiles, None, None, self.local_keys)
-        self.C.allreduce_argmax(self.rank, self.world, rows, self.key_ptrs, self.flag_ptrs, self.epoch[1:2],
-                                self.local_keys, id_offset, out_ids, out_vals, self.err, self.timeout_ms)
+        self.C.allreduce_argmax(self.rank, self.world, rows, self.max_rows, keys, tiles, id_offset, self.argmax_ptrs,
+                                self.epoch[_E_ARGMAX:_E_ARGMAX + 1], self.grid[_E_ARGMAX:_E_ARGMAX + 1], out_ids,
+                                out_vals, self.err, self.timeout_ms)
+
+    def reset(self) -> None:
+        """Collective: bring every rank's protocol state back to the start (after a call
+        that timed out left the ranks' epochs apart).  Waits for all local work, clears
+        the symmetric block, epochs, counters and the error word, then barriers so no rank
+        pushes into a peer's block before that peer has cleared it."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        if self._base:
+            self.C.symm_memset(self._base, self.nbytes)
+        self.epoch.zero_()
+        self.grid.zero_()
+        self.err.zero_()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)

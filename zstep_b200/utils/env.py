@@ -53,6 +53,8 @@ def _choice(name: str, raw: str, choices: tuple[str, ...]) -> str:
 class RuntimeConfig:
     collectives: str = "fused"            # ZSTEP_COLLECTIVES: fused | nccl
     coll_timeout_ms: int = 5000           # ZSTEP_COLL_TIMEOUT_MS: bound on cross-rank waits
+    coll_oneshot_rows: int = 16           # ZSTEP_COLL_ONESHOT_ROWS: all-reduces up to this many rows go one-shot
+    coll_ll_rows: int = 1024              # ZSTEP_COLL_LL_ROWS: two-shot LL lines up to this many rows, plain above
     gemm_fix_splits: bool = False         # ZSTEP_GEMM_FIX_SPLITS: in-kernel split-K for small GEMMs
     decode_graphs: bool = True            # ZSTEP_DECODE_GRAPHS: CUDA-graph decode buckets
     pdl: bool = True                      # ZSTEP_PDL: programmatic dependent launch of the kernels
@@ -67,6 +69,8 @@ class RuntimeConfig:
     _VARS = {
         "ZSTEP_COLLECTIVES": ("collectives", lambda n, r: _choice(n, r, ("fused", "nccl"))),
         "ZSTEP_COLL_TIMEOUT_MS": ("coll_timeout_ms", lambda n, r: _int(n, r, 1, 600000)),
+        "ZSTEP_COLL_ONESHOT_ROWS": ("coll_oneshot_rows", lambda n, r: _int(n, r, 0, 64)),
+        "ZSTEP_COLL_LL_ROWS": ("coll_ll_rows", lambda n, r: _int(n, r, 0, 1 << 16)),
         "ZSTEP_GEMM_FIX_SPLITS": ("gemm_fix_splits", _bool),
         "ZSTEP_DECODE_GRAPHS": ("decode_graphs", _bool),
         "ZSTEP_PDL": ("pdl", _bool),
