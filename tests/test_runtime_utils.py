@@ -92,3 +92,48 @@ def test_topology_decision():
                        multicast_supported=lambda i: False)
     assert t.fully_peer and not t.nvlink_fabric and t.recommended_collectives() == "nccl"
     assert "collectives=" in t.summary()
+
+
+def test_runahead_guard_caps_in_flight_steps():
+    from zstep_b200.runtime.runahead import RunAheadGuard
+
+    class FakeEvents:
+        """Events that complete only when the test says so; wait() completes one."""
+
+        def __init__(self):
+            self.created, self.pending, self.waited = 0, set(), []
+
+        def create(self):
+            self.created += 1
+            return self.created
+
+        def record(self, ev):
+            self.pending.add(ev)
+
+        def done(self, ev):
+            return ev not in self.pending
+
+        def wait(self, ev):
+            self.waited.append(ev)
+            self.pending.discard(ev)
+
+    be = FakeEvents()
+    g = RunAheadGuard(2, be)
+    for _ in range(2):
+        g.before_launch()
+        g.after_launch()
+    assert g.depth == 2 and not be.waited
+    g.before_launch()  # third step: must wait for the oldest
+    assert be.waited == [1] and g.depth == 1
+    g.after_launch()
+    be.pending.clear()  # everything finished on the device
+    g.before_launch()
+    assert g.depth == 0 and g.waits == 1
+    g.after_launch()
+    assert be.created == 2  # events are pooled, not re-created
+    g.drain()
+    assert g.depth == 0
+    off = RunAheadGuard(0, be)
+    off.before_launch()
+    off.after_launch()
+    assert off.depth == 0 and not off.enabled

@@ -260,6 +260,8 @@ class DeepSeekConfig:
         raw = json.loads((p / "config.json" if p.is_dir() else p).read_text(encoding="utf-8"))
         known = {f for f in cls.__dataclass_fields__}
         kw = {k: v for k, v in raw.items() if k in known}
+        if "dspark_aux_layers" in kw:
+            kw["dspark_aux_layers"] = tuple(kw["dspark_aux_layers"])
         kw["name"] = str(raw.get("_name_or_path", raw.get("model_type", "deepseek")))
         return cls(**kw)
 

@@ -36,14 +36,24 @@ class DramKvArena:
         if len(slots) and (slots.min() < 0 or slots.max() >= self.num_blocks):
             raise ValueError(f"DRAM slot out of range (arena has {self.num_blocks} blocks)")
         down, up = ~h2d, h2d
+        # Every copy is asynchronous on the runner's stream: D2H gathers the demoted pages
+        # into a device staging block and copies each page's block into its pinned slot;
+        # H2D copies the slots into a staging block and scatters it into the pages.  Stream
+        # order makes a later step see reloaded pages and keeps a demoted page's rows from
+        # being overwritten before they are copied out; the host never waits.
+        d_slots = slots[down].tolist()
+        u_slots = slots[up].tolist()
         for c, host in zip(self.caches, self.host):
-            if down.any():
-                p = torch.from_numpy(pages[down]).to(c.device)
-                staged = c[:, p].transpose(0, 1).contiguous().cpu()
-                host[torch.from_numpy(slots[down])] = staged
-            if up.any():
-                p = torch.from_numpy(pages[up]).to(c.device)
-                staged = host[torch.from_numpy(slots[up])].pin_memory().to(c.device, non_blocking=True)
+            if d_slots:
+                p = torch.from_numpy(pages[down]).to(c.device, non_blocking=True)
+                staged = c[:, p].transpose(0, 1).contiguous()
+                for j, sl in enumerate(d_slots):
+                    host[sl].copy_(staged[j], non_blocking=True)
+            if u_slots:
+                p = torch.from_numpy(pages[up]).to(c.device, non_blocking=True)
+                staged = torch.empty((len(u_slots),) + tuple(host.shape[1:]), dtype=c.dtype, device=c.device)
+                for j, sl in enumerate(u_slots):
+                    staged[j].copy_(host[sl], non_blocking=True)
                 c[:, p] = staged.transpose(0, 1)
-        self.d2h_blocks += int(down.sum())
-        self.h2d_blocks += int(up.sum())
+        self.d2h_blocks += len(d_slots)
+        self.h2d_blocks += len(u_slots)

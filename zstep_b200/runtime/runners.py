@@ -28,6 +28,7 @@ import torch
 import torch.distributed as dist
 
 from . import wire
+from .runahead import RunAheadGuard, TorchEventBackend
 from ..models import sampling_head
 from ..sampling import sample_logits, verify_greedy
 from ..utils.env import runtime_config
@@ -55,7 +56,9 @@ def _weights(cfg, name: str, seed: int):
 
     if _is_deepseek(cfg):
         if os.path.isdir(name):
-            raise NotImplementedError("DeepSeek-style checkpoints: only random-init weights are wired")
+            from ..models.hf_checkpoint import DeepSeekSafetensorsWeights
+
+            return DeepSeekSafetensorsWeights(cfg, name)
         return DeepSeekRandomWeights(cfg, seed=seed)
     if os.path.isdir(name):
         return SafetensorsWeights(cfg, name)
@@ -186,6 +189,7 @@ class GpuRunner:
     head = None
     dram = None
     rank = 0
+    guard = RunAheadGuard(0)  # eager-step run-ahead cap (off unless the worker sets one)
 
     @classmethod
     def wrap(cls, model_runner, rank: int = 0, nvtx: bool = False) -> "GpuRunner":
@@ -208,6 +212,7 @@ class GpuRunner:
         self.cfg = _resolve_config(args.model)
         self.dev = torch.device("cuda", torch.cuda.current_device())
         self.nvtx = runtime_config().nvtx
+        self.guard = RunAheadGuard(runtime_config().runahead_depth, TorchEventBackend(self.dev))
         coll = make_collectives(self.dev) if world > 1 else None
         # Model-drafted speculation: the MTP head for Qwen3.5, the DSpark head for DeepSeek.
         want = "dspark" if _is_deepseek(self.cfg) else "mtp"
@@ -288,7 +293,10 @@ class GpuRunner:
             ck = None
             if len(plan["ckpt_row"]):
                 ck = r.checkpoint_args(plan["ckpt_row"], plan["ckpt_slot"], plan["query_start"])
-            ids = r.prefill_forward(rows, n, ckpt=ck).cpu().numpy()
+            self.guard.before_launch()
+            dev_ids = r.prefill_forward(rows, n, ckpt=ck)
+            self.guard.after_launch()
+            ids = dev_ids.cpu().numpy()
             lm_in = (r.buf["xq_last"], r.last_lm_sf)
         lp = tids = tlps = None
         if full:

@@ -64,6 +64,7 @@ class RuntimeConfig:
     dram_kv_blocks: int = 0               # ZSTEP_DRAM_KV_BLOCKS: host DRAM KV tier size (pages)
     numa_pin: bool = True                 # ZSTEP_NUMA_PIN: pin workers to their GPU's NUMA node
     nvtx: bool = False                    # ZSTEP_NVTX: NVTX ranges around runner phases
+    runahead_depth: int = 2               # ZSTEP_RUNAHEAD_DEPTH: eager steps in flight per worker (0: no cap)
     log_level: str = "info"               # ZSTEP_LOG_LEVEL: debug | info | warning | error
 
     _VARS = {
@@ -80,6 +81,7 @@ class RuntimeConfig:
         "ZSTEP_DRAM_KV_BLOCKS": ("dram_kv_blocks", lambda n, r: _int(n, r, 0, 1 << 26)),
         "ZSTEP_NUMA_PIN": ("numa_pin", _bool),
         "ZSTEP_NVTX": ("nvtx", _bool),
+        "ZSTEP_RUNAHEAD_DEPTH": ("runahead_depth", lambda n, r: _int(n, r, 0, 64)),
         "ZSTEP_LOG_LEVEL": ("log_level", lambda n, r: _choice(n, r, ("debug", "info", "warning", "error"))),
     }
 
