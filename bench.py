@@ -48,6 +48,10 @@ def parse_args():
     ap.add_argument("--mid-context", type=int, default=1,
                     help="prefill prompt + gen/2 tokens so timed steps sit at the mean decode context")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--engine-path", type=int, default=1,
+                    help="also time decode through the native master (zstep run, SHM + eventfd) at N GPUs")
+    ap.add_argument("--engine-gen", type=int, default=48, help="engine path: output tokens per request")
+    ap.add_argument("--nccl-arm", type=int, default=1, help="N>1: also time the same decode step with NCCL collectives")
     return ap.parse_args()
 
 
@@ -140,7 +144,7 @@ def main():
     B, P, gen = args.batch, args.prompt, args.gen
     ctx0 = P + (gen // 2 if args.mid_context else 0)
     steps, warm = args.steps, args.warmup
-    assert ctx0 + warm + 2 * steps + 4 <= P + gen + 64
+    assert ctx0 + 2 * warm + 3 * steps + 4 <= P + gen + 64
     page = 16
     max_len = P + gen + 64
     pages_per_seq = (max_len + page - 1) // page
@@ -248,6 +252,39 @@ def main():
     # Kernel launches per decode step: count our kernels in one eager step.
     launches = count_launches(runner, B)
 
+    # ------------------------------------------------------------------ NCCL baseline arm
+    # The same runner and CUDA-graph decode step with the tensor-parallel reductions and the
+    # argmax exchange on NCCL (ZSTEP_COLLECTIVES=nccl): the fused NVLink kernels' end-to-end
+    # gain on the same box.
+    nccl_ms = None
+    if world > 1 and args.nccl_arm:
+        from zstep_b200.parallel.collectives import NcclCollectives
+
+        del graph
+        runner.graphs.clear()
+        fused_coll = runner.coll
+        runner.coll = NcclCollectives(None, dev)
+        runner.stage(host_tok, [pos_now + steps] * B, list(range(B)))
+        runner.capture_decode_graph(bucket)
+        graph = runner.graphs[bucket]
+        for _ in range(warm):
+            graph.replay()
+            advance()
+        dist.barrier()
+        torch.cuda.synchronize()
+        n0, n1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n0.record()
+        for _ in range(steps):
+            graph.replay()
+            advance()
+        n1.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        t = torch.tensor([n0.elapsed_time(n1)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        nccl_ms = float(t.item())
+        runner.coll = fused_coll
+
     if world > 1:
         t = torch.tensor([dev_ms, e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -275,13 +312,88 @@ def main():
             "gpu_launches_per_step": launches,
             "clocks": clocks,
             "init_s": round(init_s, 1),
+            "vs_baseline_note": "cross-hardware: divides by the reference's published 8x RTX 6000D number "
+                                "(in1024->256, c=128); no same-box reference run exists",
         }
-        print(json.dumps(res), flush=True)
+        if nccl_ms is not None:
+            res["nccl_arm"] = {"value": round(B * steps / (nccl_ms / 1000.0), 2), "unit": "tok/s",
+                               "ms_per_step": round(nccl_ms / steps, 4),
+                               "what": "same decode graph, TP reductions + argmax exchange on NCCL"}
     del graph
     runner.graphs.clear()  # release graphs before the process group goes away
+    if args.engine_path:
+        # Free this process's model before the native engine's workers load theirs.
+        runner.buf.clear()
+        runner.layers.clear()
+        del runner, b, advance, out
+        import gc
+
+        gc.collect()
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        eng = None
+        if world > 1:
+            dist.barrier()
+            store = dist.distributed_c10d._get_default_store()
+            if rank == 0:
+                eng = engine_path(args, world)
+                store.set("zstep_bench_engine_done", "1")
+            else:
+                # Wait on the store (host only): a collective here would park a kernel on
+                # every GPU while the engine's workers run on them.
+                store.wait(["zstep_bench_engine_done"], datetime.timedelta(seconds=900))
+        else:
+            eng = engine_path(args, world)
+        if rank == 0:
+            res["engine_path"] = eng
+    if rank == 0:
+        print(json.dumps(res), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def engine_path(args, world: int) -> dict:
+    """Decode through the product's serving path: the native master (`zstep run`) with
+    `world` worker processes over shared memory + eventfds, the scheduler, the KV block
+    pool and CUDA-graph decode steps, on the benchmark's shape (256 concurrent random
+    1024-token prompts, greedy).  Reports the master's own p50 TPOT / TTFT and the decode
+    throughput they imply (256 / p50 TPOT), wall-clock on the host (the master's clock)."""
+    import tempfile
+
+    root = os.path.dirname(os.path.abspath(__file__))
+    binary = os.path.join(root, "zstep_b200", "bin", "zstep")
+    if not os.path.exists(binary):
+        return {"error": f"{binary} not built"}
+    B, P, G = args.batch, args.prompt, args.engine_gen
+    with tempfile.TemporaryDirectory() as d:
+        cmd = [binary, "run", "--model-dir", d, "--model", "qwen3.5-35b-a3b", "--device", "cuda",
+               "--world-size", str(world), "--max-seqs", str(B), "--max-model-len", str(P + G + 64),
+               "--num-kv-pages", str(max(32768, B * ((P + G + 64 + 15) // 16) + 1)), "--max-step-tokens", "8192",
+               "--max-prefill-chunk", "8192", "--no-enable-prefix-caching", "--python", sys.executable,
+               "--worker-root", root, "--bench-tiers", f"engine:{B}:{B}:{P}:{G}", "--seed", str(args.seed)]
+        env = {k: v for k, v in os.environ.items()
+               if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "LOCAL_WORLD_SIZE", "GROUP_RANK", "MASTER_ADDR",
+                            "MASTER_PORT", "TORCHELASTIC_RUN_ID", "ROLE_RANK", "ROLE_WORLD_SIZE")}
+        t0 = time.time()
+        try:
+            r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
+        except subprocess.TimeoutExpired:
+            return {"error": "zstep run timed out after 600 s"}
+        wall = time.time() - t0
+    if r.returncode != 0:
+        return {"error": f"zstep run exited {r.returncode}", "stderr_tail": r.stderr[-600:]}
+    try:
+        rep = json.loads(r.stdout.strip().splitlines()[-1])
+        run0 = rep["tiers"][0]["runs"][0]
+    except (ValueError, KeyError, IndexError) as e:
+        return {"error": f"unparsable report: {e}", "stdout_tail": r.stdout[-600:]}
+    tpot = float(run0["p50_tpot_ms"])
+    return {"decode_tok_s": round(B / (tpot / 1000.0), 2) if tpot > 0 else None, "p50_tpot_ms": round(tpot, 4),
+            "p50_ttft_ms": round(float(run0["p50_ttft_ms"]), 2),
+            "output_tok_s_incl_prefill": round(float(run0["output_tok_s"]), 2), "requests": B, "input_len": P,
+            "output_len": G, "n_gpus": world, "wall_s": round(wall, 1),
+            "what": "zstep run --bench-tiers through the C++ master, SHM transport and worker processes"}
 
 
 def count_launches(runner, rows: int) -> int:

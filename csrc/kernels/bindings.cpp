@@ -45,7 +45,8 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
                int64_t block_n, int64_t k_splits, int64_t split_stride, int64_t a_tiled,
                int64_t fix_splits, const OptT& ws, const OptT& tile_sem, const OptT& row_temp,
                const OptT& row_seed, const OptT& row_pos, int64_t id_offset, const OptT& sample_any,
-               int64_t a_fp4) {
+               int64_t a_fp4, const std::vector<int64_t>& push_part, const OptT& push_epoch, int64_t push_rank,
+               int64_t push_mode) {
   check_cuda(a, "a");
   check_cuda(sfa, "sfa");
   check_cuda(b, "b");
@@ -98,6 +99,13 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
   }
   p.id_offset = (int)id_offset;
   p.sample_any = optptr<const float>(sample_any);
+  TORCH_CHECK(push_part.size() <= 8, "at most 8 push targets");
+  for (size_t q = 0; q < push_part.size(); ++q) p.push_part[q] = reinterpret_cast<void*>(push_part[q]);
+  p.push_world = (int)push_part.size();
+  p.push_epoch = optptr<const uint32_t>(push_epoch);
+  p.push_rank = (int)push_rank;
+  p.push_rows = (int)m_rows;
+  p.push_mode = (int)push_mode;
   if (fix_splits > 1) {
     TORCH_CHECK(ws.has_value() && tile_sem.has_value(), "split-K needs ws and tile_sem");
     TORCH_CHECK(ws->scalar_type() == at::kFloat && tile_sem->scalar_type() == at::kInt, "ws f32, tile_sem i32");
@@ -111,7 +119,9 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
   TORCH_CHECK(p.chunk_prefix == nullptr || (p.group_count && p.group_offset), "grouped mode args");
   if (p.chunk_prefix == nullptr) {
     TORCH_CHECK(m_rows <= p.b_rows, "m_rows > rows of b");
-    if (k_splits <= 1) TORCH_CHECK(out.numel() >= m_rows * ldo, "out too small for m_rows x ldo");
+    // kEpiPushLL stores into the all-reduce's receive buffers, never into `out`.
+    if (k_splits <= 1 && epi_mode != kEpiPushLL)
+      TORCH_CHECK(out.numel() >= m_rows * ldo, "out too small for m_rows x ldo");
   }
   rc(zs_gemm_mxf8(&p, stream()), "zs_gemm_mxf8");
 }
@@ -354,7 +364,7 @@ void fused_allreduce_norm(int64_t rank, int64_t world, int64_t protocol, const T
                           const std::vector<int64_t>& out, const std::vector<int64_t>& flags, const Tensor& epoch,
                           const Tensor& grid_counter, const Tensor& residual, const Tensor& weight, double w_offset,
                           double eps, int64_t rows, const OptT& normed, const OptT& q, const OptT& sf, const OptT& err,
-                          const OptT& term_index, const OptT& term_scale, int64_t timeout_ms) {
+                          const OptT& term_index, const OptT& term_scale, int64_t timeout_ms, bool pushed) {
   TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)part.size() == world &&
                   (out.empty() || (int64_t)out.size() == world) && (flags.empty() || (int64_t)flags.size() == world),
               "bad world / pointer lists");
@@ -389,6 +399,7 @@ void fused_allreduce_norm(int64_t rank, int64_t world, int64_t protocol, const T
   a.term_index = optptr<const int>(term_index);
   a.term_scale = optptr<const float>(term_scale);
   a.timeout_ms = (unsigned int)timeout_ms;
+  a.pushed = pushed ? 1 : 0;
   rc(zs_fused_allreduce_norm(&a, stream()), "zs_fused_allreduce_norm");
 }
 
@@ -436,6 +447,44 @@ void allreduce_argmax(int64_t rank, int64_t world, int64_t rows, int64_t max_row
   a.err = optptr<int>(err);
   a.timeout_ms = (unsigned int)timeout_ms;
   rc(zs_allreduce_argmax(&a, stream()), "zs_allreduce_argmax");
+}
+
+void spec_verify(int64_t n, int64_t k, int64_t dummy_slot, const Tensor& ids, const Tensor& targets,
+                 const Tensor& pos, const Tensor& slot, const Tensor& record, const Tensor& rep_start,
+                 const Tensor& rep_idx, const Tensor& rep_slot, const Tensor& rep_pos, const Tensor& mtp_ids,
+                 const Tensor& mtp_pos, const Tensor& mtp_slot, const Tensor& mtp_len, const Tensor& last_row) {
+  const int64_t rows = n * (k + 1);
+  for (const Tensor* t : {&ids, &targets, &pos, &slot, &rep_slot, &rep_pos, &mtp_ids, &mtp_pos, &mtp_slot, &mtp_len}) {
+    check_cuda(*t, "spec_verify operand");
+    TORCH_CHECK(t->scalar_type() == at::kInt && t->numel() >= rows, "spec_verify: int32 [n*(k+1)] operands");
+  }
+  check_cuda(record, "record");
+  check_cuda(rep_start, "rep_start");
+  check_cuda(rep_idx, "rep_idx");
+  check_cuda(last_row, "last_row");
+  TORCH_CHECK(record.scalar_type() == at::kInt && record.numel() >= n * (k + 2), "record: int32 [n, k+2]");
+  TORCH_CHECK(rep_start.scalar_type() == at::kInt && rep_start.numel() >= n + 1, "rep_start: int32 [n+1]");
+  TORCH_CHECK(rep_idx.scalar_type() == at::kLong && rep_idx.numel() >= rows, "rep_idx: int64 [n*(k+1)]");
+  TORCH_CHECK(last_row.scalar_type() == at::kLong && last_row.numel() >= n, "last_row: int64 [n]");
+  SpecVerifyArgs a{};
+  a.n = (int)n;
+  a.k = (int)k;
+  a.dummy_slot = (int)dummy_slot;
+  a.ids = ptr<const int>(ids);
+  a.targets = ptr<const int>(targets);
+  a.pos = ptr<const int>(pos);
+  a.slot = ptr<const int>(slot);
+  a.record = ptr<int>(record);
+  a.rep_start = ptr<int>(rep_start);
+  a.rep_idx = ptr<long long>(rep_idx);
+  a.rep_slot = ptr<int>(rep_slot);
+  a.rep_pos = ptr<int>(rep_pos);
+  a.mtp_ids = ptr<int>(mtp_ids);
+  a.mtp_pos = ptr<int>(mtp_pos);
+  a.mtp_slot = ptr<int>(mtp_slot);
+  a.mtp_len = ptr<int>(mtp_len);
+  a.last_row = ptr<long long>(last_row);
+  rc(zs_spec_verify(&a, stream()), "zs_spec_verify");
 }
 
 // Expert-parallel dispatch (which = 0) or combine (which = 1); offs = the six byte
@@ -805,7 +854,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out"), py::arg("flags"), py::arg("epoch"), py::arg("grid_counter"), py::arg("residual"),
         py::arg("weight"), py::arg("w_offset"), py::arg("eps"), py::arg("rows"), py::arg("normed"), py::arg("q"),
         py::arg("sf"), py::arg("err"), py::arg("term_index") = py::none(), py::arg("term_scale") = py::none(),
-        py::arg("timeout_ms") = 0);
+        py::arg("timeout_ms") = 0, py::arg("pushed") = false);
   m.def("allreduce_sum_f32", &allreduce_sum_f32, py::arg("rank"), py::arg("world"), py::arg("data"), py::arg("rows"),
         py::arg("max_rows"), py::arg("buf"), py::arg("epoch"), py::arg("grid_counter"), py::arg("err"),
         py::arg("timeout_ms") = 0);
@@ -837,8 +886,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("block_n"), py::arg("k_splits"), py::arg("split_stride"), py::arg("a_tiled"),
         py::arg("fix_splits") = 1, py::arg("ws") = py::none(), py::arg("tile_sem") = py::none(),
         py::arg("row_temp") = py::none(), py::arg("row_seed") = py::none(), py::arg("row_pos") = py::none(),
-        py::arg("id_offset") = 0, py::arg("sample_any") = py::none(), py::arg("a_fp4") = 0);
+        py::arg("id_offset") = 0, py::arg("sample_any") = py::none(), py::arg("a_fp4") = 0,
+        py::arg("push_part") = std::vector<int64_t>{}, py::arg("push_epoch") = py::none(), py::arg("push_rank") = 0,
+        py::arg("push_mode") = 1);
   m.def("quant_mxf8", &quant_mxf8);
+  m.def("spec_verify", &spec_verify);
   m.def("add_rmsnorm_quant", &add_rmsnorm_quant, py::arg("residual"), py::arg("delta"), py::arg("n_terms"),
         py::arg("d_row_stride"), py::arg("d_term_stride"), py::arg("weight"), py::arg("w_offset"), py::arg("eps"),
         py::arg("rows"), py::arg("normed"), py::arg("q"), py::arg("sf"), py::arg("term_index") = py::none(),

@@ -53,17 +53,6 @@ constexpr int MAX_LPT = 4;  // LL lines (4 columns each) per thread per row: hid
 
 using namespace peer;
 
-__device__ __forceinline__ void st_ll16(void* p, uint32_t d0, uint32_t d1, uint32_t e) {
-  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(d0), "r"(e), "r"(d1), "r"(e)
-               : "memory");
-}
-__device__ __forceinline__ uint4 ld_ll16(const void* p) {
-  uint4 v;
-  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ bool ll_ok(const uint4& v, uint32_t e) { return v.y == e && v.w == e; }
 
 // Loads the n (<= N) lines p[0], p[stride], ... and waits until every one carries epoch e.
 // All loads are issued before any is checked; stale lines are re-polled until the time
@@ -230,7 +219,7 @@ __global__ void __launch_bounds__(THREADS, 3) ar_oneshot_kernel(const FusedArArg
   auto slot = [&](int dst_rank, int src) {
     return static_cast<uint4*>(a.part[dst_rank]) + (((size_t)par * W + src) * FAR_ONESHOT_ROWS + row) * L;
   };
-  for (int i = 0; i < lpt; ++i) {
+  for (int i = 0; i < lpt && !a.pushed; ++i) {
     const int l = tid + i * THREADS;
     const float4 f = local_line(a, row, l);
     const uint32_t d0 = pack_bf16x2(f.x, f.y), d1 = pack_bf16x2(f.z, f.w);
@@ -285,8 +274,8 @@ __global__ void __launch_bounds__(THREADS, 4) ar_twoshot_kernel(const FusedArArg
   __shared__ float red[THREADS / 32];
   if (tid == 0) give_up = 0;
   __syncthreads();
-  // 1. send
-  for (int row = blockIdx.x; row < M; row += G) {
+  // 1. send (unless the producing GEMM's epilogue already pushed these lines)
+  for (int row = blockIdx.x; row < M && !a.pushed; row += G) {
     const int owner = min(row / per, W - 1);
     uint4* dst = static_cast<uint4*>(a.part[owner]) + ((size_t)a.rank * per + (row - owner * per)) * L;
     for (int l = tid; l < L; l += THREADS) {
@@ -543,6 +532,7 @@ extern "C" int zs_fused_allreduce_norm(const FusedArArgs* args, cudaStream_t str
         (a.protocol == FAR_PLAIN && a.flags[r] == nullptr))
       return -1;
   if (a.rows <= 0) return 0;
+  if (a.pushed && a.protocol == FAR_PLAIN) return -1;
   cudaError_t e;
   if (a.protocol == FAR_ONESHOT) {
     if (a.rows > FAR_ONESHOT_ROWS) return -1;

@@ -37,6 +37,7 @@
 // Reference parity: replaces the reference's Triton grouped MoE GEMMs and skinny
 // linears (worker/zstep_worker/kernels_sm120/qwen35_ops.py:1226-1438) and the
 // b12x MXFP8 linears (kernels_sm120/b12x_dsv41.py:370) with one tcgen05 kernel.
+#include "peer.cuh"
 #include "sm100_common.cuh"
 #include "zs_kernels.h"
 
@@ -623,6 +624,35 @@ gemm_mxf8_kernel(const __grid_constant__ CUtensorMap tmap_a,
 #pragma unroll
             for (int j = 0; j < 32; ++j)
               if (valid_n && j < ncols) o[(size_t)dst[j] * p.ldo] = __float2bfloat16_rn(v[j] * scl[j]);
+          } else if (p.epi_mode == kEpiPushLL) {
+            // Row-parallel partial sums straight into the fused all-reduce's receive slots:
+            // lanes 4i..4i+3 hold features 4i..4i+3 of every token column; two shuffles
+            // gather them into lane 4i, which stores one LL line per token (8 lanes x 16 B
+            // = 128 contiguous bytes per store instruction).
+            const uint32_t E = *reinterpret_cast<const volatile uint32_t*>(p.push_epoch) + 1u;
+            const int W = p.push_world, L = p.n_valid >> 2;
+            const int per = (p.push_rows + W - 1) / W;
+            const size_t line = (size_t)(n_glob >> 2);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float nx = __shfl_down_sync(0xffffffff, v[j], 1);
+              const uint32_t pk = peer::pack_bf16x2(v[j], nx);
+              const uint32_t pk2 = __shfl_down_sync(0xffffffff, pk, 2);
+              const int row = seg_row0 + col0 + j;
+              if ((lane & 3) == 0 && j < ncols && valid_n) {
+                if (p.push_mode == FAR_TWOSHOT) {
+                  const int owner = min(row / per, W - 1);
+                  peer::st_ll16(static_cast<uint4*>(p.push_part[owner]) +
+                                    ((size_t)p.push_rank * per + (row - owner * per)) * L + line, pk, pk2, E);
+                } else {
+                  const int par = E & 1;
+                  for (int q = 0; q < W; ++q)
+                    peer::st_ll16(static_cast<uint4*>(p.push_part[q]) +
+                                      (((size_t)par * W + p.push_rank) * FAR_ONESHOT_ROWS + row) * L + line,
+                                  pk, pk2, E);
+                }
+              }
+            }
           } else if (p.epi_mode == kEpiStoreF32) {
             float* o = reinterpret_cast<float*>(p.out) + it.ks * p.split_stride * split_off +
                        (size_t)(seg_row0 + col0) * p.ldo + n_glob;
@@ -778,6 +808,17 @@ extern "C" int zs_gemm_mxf8(const GemmMxf8Args* args, cudaStream_t stream) {
     if (p.chunk_prefix == nullptr && tiles * p.fix_splits > num_sms()) return -21;
   }
   const int bn = p.block_n == 32 ? 32 : 128;
+  if (p.epi_mode == kEpiPushLL) {
+    // Whole-K items, dense, hidden a multiple of 4, every receive buffer present, rows
+    // within the one-shot capacity when pushing to every rank.
+    if (p.chunk_prefix != nullptr || p.k_splits > 1 || p.fix_splits > 1 || (p.n_valid & 3) || p.push_epoch == nullptr ||
+        p.push_world < 1 || p.push_world > 8 || p.push_rank < 0 || p.push_rank >= p.push_world ||
+        p.push_rows != p.m_rows || (p.push_mode != FAR_TWOSHOT && p.push_mode != FAR_ONESHOT) ||
+        (p.push_mode == FAR_ONESHOT && p.m_rows > FAR_ONESHOT_ROWS))
+      return -24;
+    for (int q = 0; q < p.push_world; ++q)
+      if (p.push_part[q] == nullptr) return -24;
+  }
   if (p.chunk_prefix != nullptr && p.chunk_rows != bn) return -17;
   if (p.chunk_prefix != nullptr && p.groups > kMaxGroups) return -18;
   CUtensorMap ta, tb;

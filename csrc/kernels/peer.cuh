@@ -1,8 +1,8 @@
 // Device helpers for kernels that load and store other GPUs' memory over NVLink:
 // bounded waits on flags written by peers (global timer budget), system-scope
-// release/acquire, uncached loads of peer-written data, and "flag-in-data" words
-// (32-bit payload + call epoch in one 8-byte store, so a reader never pairs the payload
-// of one call with the flag of another).
+// release/acquire, uncached loads of peer-written data, and "flag-in-data" words and
+// lines (32-bit payloads each paired with the call's epoch in one 8-byte half, so a reader
+// never pairs the payload of one call with the flag of another).
 #pragma once
 #include "sm100_common.cuh"
 
@@ -104,6 +104,21 @@ __device__ __forceinline__ uint32_t wait_ll(const uint2* p, uint32_t epoch, uint
     }
   }
 }
+
+// 16-byte LL line {d0, epoch, d1, epoch}: two 32-bit payload words, each paired with the
+// call's epoch in one 8-byte half, stored with one vector store.  A reader accepts the line
+// only when both halves carry the current epoch.
+__device__ __forceinline__ void st_ll16(void* p, uint32_t d0, uint32_t d1, uint32_t e) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(d0), "r"(e), "r"(d1), "r"(e)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_ll16(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool ll_ok(const uint4& v, uint32_t e) { return v.y == e && v.w == e; }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);

@@ -351,3 +351,75 @@ extern "C" int zs_sample(const SampleArgs* args, cudaStream_t stream) {
   zs_launch(zs::smp::sample_kernel, a.rows, zs::smp::T, 0, stream, a);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
+
+// ---------------------------------------------------------------------------------------
+// On-device greedy verify of a speculative step (one CTA, one thread per sequence).
+//
+// Sequence i owns rows [i*(K+1), (i+1)*(K+1)): its last accepted token then K drafts.
+// targets[row] is the target model's greedy token after that row.  The accepted prefix is
+// the longest run j = 0.. with targets[i*(K+1)+j] == ids[i*(K+1)+j+1], plus the target token
+// that follows it (the bonus), so 1 <= acc_len <= K+1 and the accepted tokens are
+// targets[i*(K+1) .. i*(K+1)+acc_len).  The kernel also lays out what the rest of the step
+// needs, all on the device:
+//   * the recurrent-state replay over the accepted rows: a compacted row list with its
+//     per-sequence starts (an exclusive prefix sum of acc_len), slots and positions;
+//   * the draft head's catch-up rows (fixed size n*(K+1): row j of sequence i carries the
+//     token that followed it if j < acc_len, else points at the padding slot);
+//   * the catch-up row of each sequence's newest token (where the next drafts start);
+//   * the host-visible record: acc_len then the K+1 token slots (-1 past acc_len).
+// Reference parity: worker/zstep_worker/spec_decode.py:41 (verify_greedy), :55 (verify_batch).
+namespace zs {
+__global__ void __launch_bounds__(1024) spec_verify_kernel(const SpecVerifyArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int scan[1024];
+  const int i = threadIdx.x, K1 = a.k + 1;
+  int acc = 0;
+  if (i < a.n) {
+    const int r0 = i * K1;
+    acc = 1;
+    while (acc < K1 && a.targets[r0 + acc - 1] == a.ids[r0 + acc]) ++acc;
+    int* rec = a.record + (size_t)i * (K1 + 1);
+    rec[0] = acc;
+    for (int j = 0; j < K1; ++j) {
+      const int r = r0 + j;
+      const bool ok = j < acc;
+      rec[1 + j] = ok ? a.targets[r] : -1;
+      a.mtp_ids[r] = ok ? a.targets[r] : 0;
+      a.mtp_pos[r] = ok ? a.pos[r] : 1;
+      a.mtp_slot[r] = ok ? a.slot[r] : a.dummy_slot;
+      a.mtp_len[r] = ok ? a.pos[r] + 1 : 2;
+    }
+    a.last_row[i] = r0 + acc - 1;
+  }
+  // Exclusive prefix sum of acc over the sequences (Hillis-Steele in shared memory).
+  scan[i] = acc;
+  __syncthreads();
+  for (int off = 1; off < (int)blockDim.x; off <<= 1) {
+    const int v = i >= off ? scan[i - off] : 0;
+    __syncthreads();
+    scan[i] += v;
+    __syncthreads();
+  }
+  if (i < a.n) {
+    const int start = scan[i] - acc;
+    a.rep_start[i] = start;
+    if (i == a.n - 1) a.rep_start[a.n] = scan[i];
+    const int r0 = i * K1;
+    for (int j = 0; j < acc; ++j) {
+      a.rep_idx[start + j] = r0 + j;
+      a.rep_slot[start + j] = a.slot[r0];
+      a.rep_pos[start + j] = a.pos[r0 + j];
+    }
+  }
+}
+}  // namespace zs
+
+extern "C" int zs_spec_verify(const SpecVerifyArgs* args, cudaStream_t stream) {
+  const SpecVerifyArgs& a = *args;
+  if (a.n < 1 || a.n > 1024 || a.k < 1 || a.k > 7) return -1;
+  return zs_launch(zs::spec_verify_kernel, 1, 1024, 0, stream, a) == cudaSuccess &&
+                 cudaGetLastError() == cudaSuccess
+             ? 0
+             : -2;
+}

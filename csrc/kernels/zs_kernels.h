@@ -24,6 +24,7 @@ enum GemmEpilogue {
   kEpiSiluQuant = 2,      // gate/up tile pairs -> silu(g)*u -> MXFP8 out (e4m3 [rows, ldo]) + out_sf atoms
   kEpiScatterScaled = 3,  // out bf16 [row_dst[row], ldo] = acc * row_scale[row]
   kEpiArgmaxPartial = 4,  // out u64 [rows, ldo = Npad/128]: per-tile packed argmax key
+  kEpiPushLL = 5,         // row-parallel partials pushed to the fused all-reduce (push_* fields)
 };
 
 typedef struct GemmMxf8Args {
@@ -71,6 +72,15 @@ typedef struct GemmMxf8Args {
   const int* row_pos;
   int id_offset;           // global id of feature 0 (vocab shard offset)
   const float* sample_any; // optional scalar: <= 0 means no row samples (skips the per-row loads)
+  // kEpiPushLL: the GEMM is the producer of a tensor-parallel all-reduce (row-parallel
+  // projection).  Each output value leaves the epilogue as bf16 inside an LL line (4
+  // features of one token + the all-reduce call's epoch) stored straight into the receive
+  // slots of zs_fused_allreduce_norm over NVLink: the row's owner (FAR_TWOSHOT) or every
+  // rank (FAR_ONESHOT).  The all-reduce then runs with `pushed` set.  No fp32 partials
+  // touch HBM.  Whole K per item (no split-K); n_valid = hidden, a multiple of 4.
+  void* push_part[8];      // the protocol's symmetric receive buffers of every rank
+  const uint32_t* push_epoch;  // that protocol's epoch counter (read, not advanced)
+  int push_world, push_rank, push_rows, push_mode;
 } GemmMxf8Args;
 
 int zs_gemm_mxf8(const GemmMxf8Args* args, cudaStream_t stream);
@@ -280,6 +290,7 @@ typedef struct FusedArArgs {
   const void* weight;        // RMSNorm weight
   float w_offset, eps;
   int rows, hidden;
+  int pushed;                // 1: a kEpiPushLL GEMM already delivered this rank's lines (ONESHOT / TWOSHOT)
   void* normed;              // optional bf16 output
   uint8_t* q;                // optional MXFP8 output + scale atoms
   uint8_t* sf;
@@ -531,6 +542,27 @@ typedef struct SampleArgs {
 } SampleArgs;
 
 int zs_sample(const SampleArgs* args, cudaStream_t stream);
+
+// On-device greedy verify of a speculative step (n sequences x (k+1) rows); see sampling.cu.
+typedef struct SpecVerifyArgs {
+  int n, k, dummy_slot;
+  const int* ids;       // [n*(k+1)] row tokens: last accepted token, then k drafts
+  const int* targets;   // [n*(k+1)] target greedy token after each row
+  const int* pos;       // [n*(k+1)] row positions
+  const int* slot;      // [n*(k+1)] row slots
+  int* record;          // [n, k+2] out: acc_len, then k+1 accepted tokens (-1 padded)
+  int* rep_start;       // [n+1] out: replay row ranges (compacted)
+  long long* rep_idx;   // [n*(k+1)] out: source row of each replay row
+  int* rep_slot;        // [n*(k+1)] out
+  int* rep_pos;         // [n*(k+1)] out
+  int* mtp_ids;         // [n*(k+1)] out: draft-head catch-up rows (padding rows -> dummy slot)
+  int* mtp_pos;
+  int* mtp_slot;
+  int* mtp_len;
+  long long* last_row;  // [n] out: catch-up row of each sequence's newest token
+} SpecVerifyArgs;
+
+int zs_spec_verify(const SpecVerifyArgs* args, cudaStream_t stream);
 
 // Programmatic dependent launch of the compute kernels (on by default).
 void zs_set_pdl(int on);

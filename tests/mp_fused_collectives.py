@@ -66,6 +66,50 @@ def check_allreduce(coll, C, rank, world, dev):
             assert torch.equal(mx.codes_from_atoms(xsf, rows, H), mx.codes_from_atoms(xsf2, rows, H))
 
 
+def check_gemm_push(coll, C, rank, world, dev):
+    """Row-parallel GEMM whose epilogue pushes bf16 LL lines into the all-reduce's receive
+    slots (one-shot and two-shot), then the all-reduce without its send phase: equal to
+    residual + the rank-ordered sum of each rank's bf16 GEMM output."""
+    from zstep_b200.models.qwen35 import EPI_BF16, EPI_PUSH, pack_linear
+
+    H, K = 2048, 512
+    coll.reserve(96, H)
+    g = torch.Generator(device=dev).manual_seed(600)
+    ws = [(0.02 * torch.randn(H, K, generator=g, device=dev)).to(torch.bfloat16) for _ in range(world)]
+    xs = [torch.randn(96, K, generator=g, device=dev).to(torch.bfloat16) for _ in range(world)]
+    resid0 = torch.randn(96, H, generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.rand(H, generator=g, device=dev) + 0.5).to(torch.bfloat16)
+    pw = pack_linear(ws[rank], C)
+    xq = torch.zeros(128, K, dtype=torch.uint8, device=dev)
+    xsf = torch.zeros(mx.atoms_bytes(128, K), dtype=torch.uint8, device=dev)
+    C.quant_mxf8(xs[rank], xq[:96], xsf)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    # Each rank's plain bf16 GEMM output (same kernel, local store) for the expectation.
+    mine = torch.zeros(96, H, dtype=torch.bfloat16, device=dev)
+    C.gemm_mxf8(pw.q, pw.sf, xq, xsf, K, pw.n_pad, H, 1, 96, None, None, None, EPI_BF16, mine, H, None, None, None,
+                err, 0, 32, 1, 0, 1)
+    outs = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(outs, mine)
+    for rows in (5, 37, 96):
+        tgt = coll.push_target(rows)
+        assert tgt is not None
+        proto, parts, ep = tgt
+        hidden = resid0.clone()
+        oq = torch.zeros(128, H, dtype=torch.uint8, device=dev)
+        osf = torch.zeros(mx.atoms_bytes(128, H), dtype=torch.uint8, device=dev)
+        dummy = torch.zeros(1, dtype=torch.float32, device=dev)
+        C.gemm_mxf8(pw.q, pw.sf, xq, xsf, K, pw.n_pad, H, 1, rows, None, None, None, EPI_PUSH, dummy, H, None, None,
+                    None, err, 0, 32, 1, 0, 1, push_part=parts, push_epoch=ep, push_rank=rank, push_mode=proto)
+        coll.allreduce_add_rmsnorm(dummy, 1, H, 0, hidden, w, 1e-6, rows, oq, osf, protocol=proto, pushed=True)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0 and coll.check_error() == 0, (rows, proto)
+        acc = resid0[:rows].float()
+        for r in range(world):
+            acc = acc + outs[r][:rows].float()
+        assert torch.equal(hidden[:rows], acc.to(torch.bfloat16)), f"pushed all-reduce rows={rows} protocol={proto}"
+        assert torch.equal(hidden[rows:], resid0[rows:])
+
+
 def check_prefill_sized(coll, rank, world, dev):
     """A prefill-sized reduction (2048 rows, hidden 4096 as in the DeepSeek shape) takes the
     plain two-shot protocol; gathered MoE-style terms with weights."""
@@ -201,7 +245,7 @@ def check_argmax(coll, rank, world, dev):
     del _ext
 
 
-TIE_MARGIN = 0.1  # two logits that each move by up to ~5e-2 (MXFP8 activations, bf16 rounding) can swap
+TIE_MARGIN = 0.15  # the logit check allows 3e-2 + 3e-2|v| per logit (|v| ~ 1): two logits can swap across 0.15
 
 
 def _same_or_near_tie(got, want, ref_logits):
@@ -318,6 +362,7 @@ def main():
         check_graph_replay(coll, rank, world, dev)
         check_argmax(coll, rank, world, dev)
         check_allreduce_sum(coll, rank, world, dev)
+        check_gemm_push(coll, C, rank, world, dev)
         check_prefill_sized(coll, rank, world, dev)
         coll = FusedCollectives(dev)
         if world > 1:

@@ -76,11 +76,25 @@ def runner_greedy(runner, prompts, slots, n):
     return out
 
 
-def test_verify_with_oracle_drafts_matches_greedy(setup):
+@pytest.mark.parametrize("graphs", [True, False], ids=["graph", "eager"])
+def test_verify_with_oracle_drafts_matches_greedy(setup, graphs, monkeypatch):
     """Verify steps fed the runner's own greedy continuation (corrupted at chosen places)
     accept exactly the uncorrupted prefix, reproduce greedy decoding, and leave the same
-    recurrent state as plain decoding (the roll-back replay)."""
+    recurrent state as plain decoding (the roll-back replay).  `graph`: the steady-state
+    verify steps take the CUDA-graph path (on-device verify, roll-back and drafting);
+    `eager`: the host-driven path."""
+    import dataclasses
+
+    from zstep_b200.runtime import runners
+    from zstep_b200.utils.env import runtime_config
+
+    monkeypatch.setattr(runners, "runtime_config",
+                        lambda: dataclasses.replace(runtime_config(), decode_graphs=graphs))
     cfg, runner, ref, g = setup
+    if graphs:
+        calls = []
+        real = g._execute_spec_graph
+        monkeypatch.setattr(g, "_execute_spec_graph", lambda *a: calls.append(1) or real(*a))
     gen = torch.Generator().manual_seed(5)
     prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=gen).tolist() for n in (9, 23, 14)]
     for s in range(6):
@@ -113,6 +127,8 @@ def test_verify_with_oracle_drafts_matches_greedy(setup):
             produced[s] += [int(t) for t in out[s]["tokens"][:n]]
             ok[s] = ok[s] and produced[s] == truth[s][:len(produced[s])]
     assert sum(ok) >= 2, (produced, truth)
+    if graphs:
+        assert len(calls) == 3  # every verify step took the graph path
     # Recurrent state after the accepted tokens equals plain decoding's state after the
     # same inputs (prompt plus every produced token but the newest).
     for s in range(3):

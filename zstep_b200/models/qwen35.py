@@ -39,7 +39,7 @@ from ..utils.env import runtime_config
 from ..ops import mx
 from .weights import RandomWeights
 
-EPI_BF16, EPI_F32, EPI_SILU, EPI_SCATTER, EPI_ARGMAX = 0, 1, 2, 3, 4
+EPI_BF16, EPI_F32, EPI_SILU, EPI_SCATTER, EPI_ARGMAX, EPI_PUSH = 0, 1, 2, 3, 4, 5
 
 DECODE_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256, 320, 384, 448, 512)
 
@@ -388,9 +388,22 @@ class Qwen35Runner:
         return int(max(1, min(self.max_splits, math.ceil(1200 / ctas))))
 
     def _proj_out(self, w: PackedLinear, xq, xsf, rows: int, norm_w, hidden=None) -> None:
-        """Row-parallel output projection (GDN out_proj / attention o_proj) into f32
-        split-K partials, then residual add + RMSNorm (+ all-reduce across ranks)."""
+        """Row-parallel output projection (GDN out_proj / attention o_proj), then residual
+        add + RMSNorm (+ all-reduce across ranks).  Tensor parallel at decode sizes: the
+        GEMM epilogue pushes its bf16 partial tiles straight into the fused all-reduce's
+        receive slots over NVLink, and the all-reduce only reduces and normalises.
+        Otherwise: f32 split-K partials, reduced by the next kernel."""
         H = self.cfg.hidden_size
+        b = self.buf
+        tgt = self.coll.push_target(rows) if self.tp > 1 and hasattr(self.coll, "push_target") else None
+        if tgt is not None:
+            proto, parts, ep = tgt
+            self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, 1, rows, None, None, None, EPI_PUSH,
+                             b["delta_f32"], H, None, None, None, b["err"], 0, 32, 1, 0, 1,
+                             push_part=parts, push_epoch=ep, push_rank=self.tp_rank, push_mode=proto)
+            self.coll.allreduce_add_rmsnorm(b["delta_f32"], 1, H, 0, b["hidden"] if hidden is None else hidden,
+                                            norm_w, self.eps, rows, b["xq"], b["xsf"], protocol=proto, pushed=True)
+            return
         s = self._k_splits(w, rows)
         self._gemm(w, xq, xsf, rows, self.buf["delta_f32"], H, EPI_F32, k_splits=s)
         self._row_parallel_reduce(self.buf["delta_f32"], rows, s, norm_w, rows * H, H, hidden=hidden)

@@ -120,6 +120,102 @@ class SpecDecoder:
                             None, midq, r.buf["midsf"], self.fix_seq_start[:len(starts)], len(row_groups), None, None,
                             0, r.buf["err"])
 
+    # ------------------------------------------------------------------ graph path
+    # A steady-state verify step (every sequence carries K drafts, greedy, no checkpoint)
+    # runs as one CUDA graph per sequence bucket: target forward, lm_head argmax, on-device
+    # verify (csrc/kernels/sampling.cu spec_verify), replay of the accepted rows, draft-head
+    # catch-up and the K-1 chained drafts, with no host round trip inside the step.
+    def _graph_buffers(self) -> None:
+        if hasattr(self, "g_record"):
+            return
+        r, K, dev = self.r, self.K, self.r.dev
+        ms, R = r.max_seqs, r.R
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.g_record = torch.zeros(ms, 2 * K + 2, **i32)  # acc_len | K+1 accepted tokens | K next drafts
+        self.g_verify = torch.zeros(ms, K + 2, **i32)
+        self.g_rep_start = torch.zeros(ms + 1, **i32)
+        self.g_rep_idx = torch.zeros(R, dtype=torch.long, device=dev)
+        self.g_rep_slot = torch.zeros(R, **i32)
+        self.g_rep_pos = torch.zeros(R, **i32)
+        self.g_last = torch.zeros(ms, dtype=torch.long, device=dev)
+        self.g_graphs: dict[int, torch.cuda.CUDAGraph] = {}
+
+    def graph_bucket(self, n: int) -> int | None:
+        """Smallest decode bucket holding n verify sequences (None: too many rows)."""
+        r = self.r
+        bk = r.bucket_for(n)
+        if bk < n or bk * (self.K + 1) > r.R or bk * (self.K + 1) > r.lm_rows:
+            return None
+        return bk
+
+    def verify_step(self, nb: int) -> None:
+        """One speculative step over nb sequences x (K+1) staged rows (seq_start and
+        out_slots staged), device-only.  Result rows: self.g_record[:nb]."""
+        r, C, b, K = self.r, self.r.C, self.r.buf, self.K
+        R = nb * (K + 1)
+        r._layers(R, decode=False, num_seqs=nb, gdn_out_slots=self.out_slots[:nb], proj_store=self.proj_store)
+        r._lm_head_argmax(R)
+        C.spec_verify(nb, K, r.dummy_slot, b["in_ids"], b["out_ids"], b["in_pos"], b["in_slot"], self.g_verify,
+                      self.g_rep_start, self.g_rep_idx, self.g_rep_slot, self.g_rep_pos, self.ids, self.pos, self.slot,
+                      self.lens, self.g_last)
+        # Replay the GDN recurrence over the accepted rows, in place on the pre-step slots.
+        midq = r._mid(r.hv * 128)
+        for li in r.cfg.gdn_layers:
+            gi = r.gdn_index[li]
+            L = r.layers[li]
+            torch.index_select(self.proj_store[gi], 0, self.g_rep_idx[:R], out=self.fix_proj[:R])
+            C.gdn_prefill(self.fix_proj[:R], r.hk, r.hv, L["conv_w"], r.conv_state[gi], r.ssm_state[gi], L["a_log"],
+                          L["dt_bias"], L["gnorm"], r.eps, self.g_rep_slot[:R], self.g_rep_pos[:R], R, None, midq,
+                          b["midsf"], self.g_rep_start[:nb + 1], nb, None, None, 0, b["err"])
+        # Draft head: catch-up over every verify row (rows past a sequence's accepted
+        # prefix point at the padding slot), then K-1 chained single-row steps.
+        self.hid[:R].copy_(b["hidden"][:R])
+        first = self.mtp(R)
+        last = self.g_last[:nb]
+        drafts = [first.index_select(0, last)]
+        prev = self.res.index_select(0, last)
+        pos0 = self.pos.index_select(0, last)
+        slot0 = self.slot.index_select(0, last)
+        for s in range(1, K):
+            self.ids[:nb].copy_(drafts[-1])
+            self.pos[:nb].copy_(pos0 + s)
+            self.slot[:nb].copy_(slot0)
+            self.lens[:nb].copy_(pos0 + s + 1)
+            self.hid[:nb].copy_(prev)
+            drafts.append(self.mtp(nb).clone())
+            prev = self.res[:nb].clone()
+        self.g_record[:nb, :K + 2].copy_(self.g_verify[:nb])
+        self.g_record[:nb, K + 2:].copy_(torch.stack(drafts, 1))
+
+    def run_verify_graph(self, nb: int) -> None:
+        """Replay (capturing on first use) the verify-step graph of bucket nb."""
+        self._graph_buffers()
+        if nb not in self.g_graphs:
+            r, b = self.r, self.r.buf
+            saved = (b["inputs"].clone(), b["seq_start"].clone(), self.out_slots.clone())
+            # Capture on padding rows only: every row and state slot is the dummy one.
+            R = nb * (self.K + 1)
+            b["in_ids"][:R] = 0
+            b["in_pos"][:R] = 1
+            b["in_slot"][:R] = r.dummy_slot
+            b["in_len"][:R] = 2
+            b["seq_start"][:nb + 1].copy_(torch.arange(nb + 1, device=r.dev, dtype=torch.int32) * (self.K + 1))
+            self.out_slots[:nb] = r.dummy_slot
+            s = torch.cuda.Stream(r.dev)
+            s.wait_stream(torch.cuda.current_stream(r.dev))
+            with torch.cuda.stream(s):
+                for _ in range(2):
+                    self.verify_step(nb)
+            torch.cuda.current_stream(r.dev).wait_stream(s)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self.verify_step(nb)
+            self.g_graphs[nb] = g
+            b["inputs"].copy_(saved[0])
+            b["seq_start"].copy_(saved[1])
+            self.out_slots.copy_(saved[2])
+        self.g_graphs[nb].replay()
+
     # ------------------------------------------------------------------ MTP head
     def mtp(self, rows: int) -> torch.Tensor:
         """MTP head over `rows` staged rows (self.ids / pos / slot / lens and self.hid).

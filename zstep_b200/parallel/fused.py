@@ -71,6 +71,7 @@ class FusedCollectives:
         self.timeout_ms = cfg.coll_timeout_ms  # bound on every cross-rank wait
         self.oneshot_rows = min(cfg.coll_oneshot_rows, FAR_ONESHOT_ROWS)
         self.ll_rows = cfg.coll_ll_rows
+        self.push = cfg.coll_push
         from .collectives import NcclCollectives
 
         self.nccl = NcclCollectives(group, self.device)
@@ -144,11 +145,26 @@ class FusedCollectives:
             return TWOSHOT
         return PLAIN
 
+    def push_target(self, rows: int):
+        """Where a row-parallel GEMM's epilogue pushes its partial sums for an all-reduce of
+        `rows` rows: (protocol, receive buffers of every rank, epoch counter), or None when
+        that row count takes the plain protocol (the GEMM then writes its output locally)."""
+        if rows > self.max_rows or not self.push:
+            return None
+        proto = self.protocol_for(rows)
+        if proto == ONESHOT:
+            return proto, self.one_ptrs, self.epoch[_E_ONE:_E_ONE + 1]
+        if proto == TWOSHOT:
+            return proto, self.ll_part_ptrs, self.epoch[_E_TWO:_E_TWO + 1]
+        return None
+
     def allreduce_add_rmsnorm(self, delta, n_terms: int, row_stride: int, term_stride: int, hidden_buf,
                               norm_w, eps: float, rows: int, xq, xsf, term_index=None, term_scale=None,
-                              protocol: int | None = None) -> None:
+                              protocol: int | None = None, pushed: bool = False) -> None:
         """hidden_buf[:rows] += sum over ranks of the local term sums; then RMSNorm(norm_w)
-        -> MXFP8 (xq, xsf).  Every rank ends with the same bf16 residual stream."""
+        -> MXFP8 (xq, xsf).  Every rank ends with the same bf16 residual stream.  With
+        ``pushed`` the local sums were already delivered by a GEMM epilogue
+        (``push_target``) and ``delta`` is not read."""
         H = hidden_buf.shape[-1]
         if rows > self.max_rows or H != self.hidden:
             raise ValueError(f"fused all-reduce reserved for {self.max_rows}x{self.hidden}, got {rows}x{H}")
@@ -163,7 +179,8 @@ class FusedCollectives:
             part, out, flags, e = self.plain_part_ptrs, self.plain_out_ptrs, self.flag_ptrs, _E_PLAIN
         self.C.fused_allreduce_norm(self.rank, self.world, proto, delta, n_terms, row_stride, term_stride, part, out,
                                     flags, self.epoch[e:e + 1], self.grid[e:e + 1], hidden_buf, norm_w, 1.0, eps,
-                                    rows, None, xq, xsf, self.err, term_index, term_scale, self.timeout_ms)
+                                    rows, None, xq, xsf, self.err, term_index, term_scale, self.timeout_ms,
+                                    pushed=pushed)
 
     def allreduce_sum(self, t: torch.Tensor) -> None:
         """In-place fp32 sum over ranks of t [rows, hidden] (mHC sublayer outputs): one-shot

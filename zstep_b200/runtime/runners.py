@@ -324,6 +324,15 @@ class GpuRunner:
         recurrent-state replay of the accepted rows, then MTP drafts for the next step."""
         r = self.r
         rows = plan["num_rows"]
+        K = r.num_spec
+        if (runtime_config().decode_graphs and n > 0 and rows == n * (K + 1) and not len(plan["ckpt_row"])
+                and not plan["flags"] & wire.FLAG_SAMPLING
+                and all(int(w) == K + 1 for w in plan["spec_width"][:n])
+                and all(int(q) == i * (K + 1) for i, q in enumerate(plan["query_start"][:n + 1]))
+                and all(int(sr) == (i + 1) * (K + 1) - 1 for i, sr in enumerate(plan["sample_row"][:n]))):
+            nb = r.spec.graph_bucket(n)
+            if nb is not None:
+                return self._execute_spec_graph(plan, n, nb, out)
         qs = plan["query_start"].tolist()
         ids = plan["token_ids"][:rows].tolist()
         pos = plan["positions"][:rows].tolist()
@@ -395,6 +404,34 @@ class GpuRunner:
                     out[i]["num_drafts"] = len(drafts[k])
             else:
                 r.spec.catch_up(m_ids, m_pos, m_slot, rows_t)
+        return out
+
+    def _execute_spec_graph(self, plan: dict, n: int, nb: int, out):
+        """A steady-state verify step (every sequence: last token + K drafts, greedy) as one
+        CUDA-graph replay: verify, acceptance, state roll-back and the next drafts all run on
+        the device; the host reads one [n, 2K+2] record per step."""
+        r = self.r
+        K = r.num_spec
+        K1 = K + 1
+        R, rows = nb * K1, plan["num_rows"]
+        ids = np.zeros(R, np.int32)
+        pos = np.ones(R, np.int32)
+        slot = np.full(R, r.dummy_slot, np.int32)
+        ids[:rows] = plan["token_ids"][:rows]
+        pos[:rows] = plan["positions"][:rows]
+        slot[:rows] = plan["row_slot"][:rows]
+        r.stage(ids, pos, slot, seq_start=[i * K1 for i in range(nb + 1)])
+        spare = [r.spec_slot_base + int(plan["seq_slot"][i]) for i in range(n)] + [r.dummy_slot] * (nb - n)
+        r.spec.out_slots[:nb].copy_(torch.tensor(spare, dtype=torch.int32))
+        r.spec.run_verify_graph(nb)
+        rec = r.spec.g_record[:n].cpu().numpy()
+        for i in range(n):
+            acc = int(rec[i, 0])
+            out[i]["req_slot"] = int(plan["seq_slot"][i])
+            out[i]["num_tokens"] = acc
+            out[i]["tokens"][:acc] = rec[i, 1:1 + acc]
+            out[i]["next_drafts"][:K] = rec[i, K + 2:2 * K + 2]
+            out[i]["num_drafts"] = K
         return out
 
     def close(self) -> None:

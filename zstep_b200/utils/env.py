@@ -55,6 +55,7 @@ class RuntimeConfig:
     coll_timeout_ms: int = 5000           # ZSTEP_COLL_TIMEOUT_MS: bound on cross-rank waits
     coll_oneshot_rows: int = 16           # ZSTEP_COLL_ONESHOT_ROWS: all-reduces up to this many rows go one-shot
     coll_ll_rows: int = 1024              # ZSTEP_COLL_LL_ROWS: two-shot LL lines up to this many rows, plain above
+    coll_push: bool = True                # ZSTEP_COLL_PUSH: row-parallel GEMM epilogues push into the all-reduce
     gemm_fix_splits: bool = False         # ZSTEP_GEMM_FIX_SPLITS: in-kernel split-K for small GEMMs
     decode_graphs: bool = True            # ZSTEP_DECODE_GRAPHS: CUDA-graph decode buckets
     pdl: bool = True                      # ZSTEP_PDL: programmatic dependent launch of the kernels
@@ -72,6 +73,7 @@ class RuntimeConfig:
         "ZSTEP_COLL_TIMEOUT_MS": ("coll_timeout_ms", lambda n, r: _int(n, r, 1, 600000)),
         "ZSTEP_COLL_ONESHOT_ROWS": ("coll_oneshot_rows", lambda n, r: _int(n, r, 0, 64)),
         "ZSTEP_COLL_LL_ROWS": ("coll_ll_rows", lambda n, r: _int(n, r, 0, 1 << 16)),
+        "ZSTEP_COLL_PUSH": ("coll_push", _bool),
         "ZSTEP_GEMM_FIX_SPLITS": ("gemm_fix_splits", _bool),
         "ZSTEP_DECODE_GRAPHS": ("decode_graphs", _bool),
         "ZSTEP_PDL": ("pdl", _bool),
