@@ -333,10 +333,13 @@ bool Tokenizer::is_special(int32_t id) const {
 
 // ------------------------------------------------------------------ encode
 void Tokenizer::bpe(const std::string& piece, std::vector<int32_t>* out) const {
-  auto hit = cache_.find(piece);
-  if (hit != cache_.end()) {
-    out->insert(out->end(), hit->second.begin(), hit->second.end());
-    return;
+  {
+    std::shared_lock<std::shared_mutex> lk(cache_mu_);
+    auto hit = cache_.find(piece);
+    if (hit != cache_.end()) {
+      out->insert(out->end(), hit->second.begin(), hit->second.end());
+      return;
+    }
   }
   std::vector<std::string> sym;
   sym.reserve(piece.size());
@@ -383,7 +386,10 @@ void Tokenizer::bpe(const std::string& piece, std::vector<int32_t>* out) const {
       }
     }
   }
-  if (cache_.size() < 200000) cache_.emplace(piece, ids);
+  {
+    std::unique_lock<std::shared_mutex> lk(cache_mu_);
+    if (cache_.size() < 200000) cache_.emplace(piece, ids);
+  }
   out->insert(out->end(), ids.begin(), ids.end());
 }
 

@@ -16,6 +16,8 @@
 #include <stdint.h>
 
 #include <map>
+#include <mutex>
+#include <shared_mutex>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -60,6 +62,9 @@ class Tokenizer {
   std::vector<int32_t> eos_ids_;
   std::string byte_to_uni_[256];                     // byte -> UTF-8 of its alphabet char
   std::unordered_map<uint32_t, uint8_t> uni_to_byte_;
+  // Memo of finished BPE pieces.  encode() is const and runs on every HTTP connection
+  // thread at once, so the memo is guarded: lookups share the lock, inserts take it alone.
+  mutable std::shared_mutex cache_mu_;
   mutable std::unordered_map<std::string, std::vector<int32_t>> cache_;
 };
 

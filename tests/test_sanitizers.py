@@ -9,6 +9,7 @@ import http.client
 import json
 import os
 import signal
+import threading
 import subprocess
 
 import pytest
@@ -83,12 +84,15 @@ def test_serve_loop_under_tsan(model_dir):
             except Exception as e:  # noqa: BLE001
                 errors.append((i, repr(e)))
 
-        # One connection at a time: the acceptor, connection and engine threads still run
-        # concurrently (TSan's happens-before analysis does not depend on client timing).
-        # Simultaneous client connections stall the TSan build only (the plain and ASan
-        # builds serve them); that is an open item.
-        for i in range(6):
-            client(i)
+        # Simultaneous client connections: the connection threads tokenize, submit and
+        # stream at the same time as the acceptor and the engine thread.  (This run found
+        # the tokenizer's BPE memo being filled by several connection threads at once.)
+        threads = [threading.Thread(target=client, args=(i,)) for i in range(6)]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join(timeout=300)
+        assert not any(t.is_alive() for t in threads), "a client did not finish"
         assert not errors, errors
         p.send_signal(signal.SIGTERM)
         assert p.wait(timeout=120) == 0
