@@ -267,7 +267,9 @@ class Qwen35Runner:
         # In-kernel split-K for dense GEMMs with few output tiles.  Off by default: on the
         # decode shapes measured so far it did not beat the unsplit kernel.
         self.use_fix_splits = runtime_config().gemm_fix_splits
-        # Varlen prefill attention: 0 = tensor-core kernel, 1 = SIMT kernel (per-row causal lengths).
+        # Varlen prefill attention: 0 = query-tiled tensor-core kernel (split-KV tensor-core
+        # decode per row for short rows), 1 = SIMT decode kernel per row, 2 = tensor-core
+        # decode kernel per row (per-row causal lengths).
         self.prefill_attn_impl = 0
         b["xq"] = torch.zeros(Rp, H, dtype=torch.uint8, device=dev)
         b["xsf"] = torch.zeros(mx.atoms_bytes(Rp, H), dtype=torch.uint8, device=dev)
@@ -459,11 +461,19 @@ class Qwen35Runner:
                                 self.eps, self.k_cache[ai], self.v_cache[ai], self.page_size, self.page_table, slot,
                                 pos, rows, b["q_out"], b["gate_out"])
                 midq = self._mid(self.hq * cfg.head_dim)
-                splits = self._attn_splits(rows, decode)
-                C.attn_decode(b["q_out"], b["gate_out"], self.hq, self.hkv, self.k_cache[ai], self.v_cache[ai],
-                              self.page_size, self.page_table, slot, lens, rows, b["partial"], splits,
-                              1.0 / math.sqrt(cfg.head_dim), None, midq, b["midsf"],
-                              impl=0 if decode else self.prefill_attn_impl)
+                if not decode and self.prefill_attn_impl == 0 and rows >= 16 * max(1, num_seqs):
+                    # Query-tiled tensor-core prefill: 128-row tiles of each sequence.
+                    C.attn_prefill(b["q_out"], b["gate_out"], self.hq, self.hkv, self.k_cache[ai],
+                                   self.v_cache[ai], self.page_size, self.page_table, slot, pos, rows,
+                                   b["seq_start"][:num_seqs + 1], num_seqs, 1.0 / math.sqrt(cfg.head_dim), None,
+                                   midq, b["midsf"], b["err"])
+                else:
+                    # Decode, and short varlen rows (verify steps): split-KV per row.
+                    splits = self._attn_splits(rows, decode)
+                    C.attn_decode(b["q_out"], b["gate_out"], self.hq, self.hkv, self.k_cache[ai],
+                                  self.v_cache[ai], self.page_size, self.page_table, slot, lens, rows, b["partial"],
+                                  splits, 1.0 / math.sqrt(cfg.head_dim), None, midq, b["midsf"],
+                                  impl=1 if (not decode and self.prefill_attn_impl == 1) else 0)
                 self._proj_out(L["o_proj"], midq, b["midsf"], rows, L["post_norm"])
             self._moe(L, rows)
             next_w = self.layers[li + 1]["input_norm"] if li + 1 < len(self.layers) else self.final_norm
