@@ -46,7 +46,7 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
                int64_t fix_splits, const OptT& ws, const OptT& tile_sem, const OptT& row_temp,
                const OptT& row_seed, const OptT& row_pos, int64_t id_offset, const OptT& sample_any,
                int64_t a_fp4, const std::vector<int64_t>& push_part, const OptT& push_epoch, int64_t push_rank,
-               int64_t push_mode) {
+               int64_t push_mode, int64_t last_m0, int64_t last_mt) {
   check_cuda(a, "a");
   check_cuda(sfa, "sfa");
   check_cuda(b, "b");
@@ -106,6 +106,8 @@ void gemm_mxf8(const Tensor& a, const Tensor& sfa, const Tensor& b, const Tensor
   p.push_rank = (int)push_rank;
   p.push_rows = (int)m_rows;
   p.push_mode = (int)push_mode;
+  p.last_m0 = (int)last_m0;
+  p.last_mt = (int)last_mt;
   if (fix_splits > 1) {
     TORCH_CHECK(ws.has_value() && tile_sem.has_value(), "split-K needs ws and tile_sem");
     TORCH_CHECK(ws->scalar_type() == at::kFloat && tile_sem->scalar_type() == at::kInt, "ws f32, tile_sem i32");
@@ -922,7 +924,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("row_temp") = py::none(), py::arg("row_seed") = py::none(), py::arg("row_pos") = py::none(),
         py::arg("id_offset") = 0, py::arg("sample_any") = py::none(), py::arg("a_fp4") = 0,
         py::arg("push_part") = std::vector<int64_t>{}, py::arg("push_epoch") = py::none(), py::arg("push_rank") = 0,
-        py::arg("push_mode") = 1);
+        py::arg("push_mode") = 1, py::arg("last_m0") = 0, py::arg("last_mt") = 0);
   m.def("quant_mxf8", &quant_mxf8);
   m.def("attn_prefill", &attn_prefill, py::arg("q_out"), py::arg("gate_out"), py::arg("num_q_heads"),
         py::arg("num_kv_heads"), py::arg("k_cache"), py::arg("v_cache"), py::arg("page_size"), py::arg("page_table"),

@@ -123,13 +123,23 @@ __device__ __forceinline__ bool get_item(const GemmMxf8Args& p, int idx, Item& i
   }
   const int S = p.fix_splits > 1 ? p.fix_splits : 1;
   const int total_chunks = pre[p.groups];
-  if (idx >= total_chunks * m_tiles * S) return false;
+  // With last_mt > 0 the last group's chunks cover only tiles [last_m0, last_m0 + last_mt).
+  const int pre_last = p.last_mt > 0 ? pre[p.groups - 1] : total_chunks;
+  const int full_tiles = pre_last * m_tiles;
+  const int total_tiles = full_tiles + (total_chunks - pre_last) * (p.last_mt > 0 ? p.last_mt : 0);
+  if (idx >= total_tiles * S) return false;
   const int t = idx / S;
   if (S > 1 && t >= p.max_tiles) return false;  // workspace too small: the producer reports it
   it.ks = idx % S;
   it.tile = t;
-  const int chunk = t / m_tiles;
-  it.m = t % m_tiles;
+  int chunk;
+  if (t < full_tiles) {
+    chunk = t / m_tiles;
+    it.m = t % m_tiles;
+  } else {
+    chunk = pre_last + (t - full_tiles) / p.last_mt;
+    it.m = p.last_m0 + (t - full_tiles) % p.last_mt;
+  }
   int lo = 0, hi = p.groups;  // largest g with prefix[g] <= chunk
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
@@ -820,6 +830,8 @@ extern "C" int zs_gemm_mxf8(const GemmMxf8Args* args, cudaStream_t stream) {
       if (p.push_part[q] == nullptr) return -24;
   }
   if (p.chunk_prefix != nullptr && p.chunk_rows != bn) return -17;
+  if (p.last_mt < 0 || p.last_m0 < 0 || (p.last_mt > 0 && (p.chunk_prefix == nullptr || p.last_m0 + p.last_mt > p.n_pad / BM)))
+    return -25;
   if (p.chunk_prefix != nullptr && p.groups > kMaxGroups) return -18;
   CUtensorMap ta, tb;
   if (p.a_fp4) {

@@ -43,6 +43,8 @@ typedef struct GemmMxf8Args {
   const int* chunk_prefix; // grouped mode: [groups+1] prefix of ceil(count/chunk_rows); NULL = dense
   int chunk_rows;          // grouped mode: rows per chunk the prefix was built for (== block_n)
   int max_items;           // grouped mode: optional cap on CTAs (0 = one per SM)
+  int last_m0, last_mt;    // grouped mode: the last group computes only 128-row tiles [last_m0, last_m0 +
+                           // last_mt) (last_mt 0 = all tiles; a tensor-parallel rank's slice of the shared expert)
   int block_n;             // tokens per work item: 32 (decode) or 128
   int k_splits;            // dense mode, kEpiStoreF32 only: split K into this many partials
   long long split_stride;  // elements between split partials in out

@@ -186,13 +186,21 @@ class DeepSeekRunner:
         del gate, up
         sd = src.get(p + "moe.shared.down", dev)
         if self.tp > 1:
-            n = H // self.tp
-            mask = torch.zeros(H, 1, dtype=sd.dtype, device=dev)
-            mask[self.tp_rank * n:(self.tp_rank + 1) * n] = 1
+            # Tensor-parallel shared expert: this rank's intermediate columns only (its
+            # gate/up tiles are selected in the grouped GEMM, the other columns of the down
+            # projection are zero), summed over ranks by the sublayer all-reduce.
+            c0, c1 = self.shared_cols()
+            mask = torch.zeros(1, sd.shape[1], dtype=sd.dtype, device=dev)
+            mask[:, c0:c1] = 1
             sd = sd * mask
         down = torch.stack([ex("down", e) for e in range(eb, ee)] + [sd])
         out["down"] = packer(down, C)
         return out
+
+    def shared_cols(self) -> tuple[int, int]:
+        """This rank's intermediate columns of the shared expert."""
+        n = self.cfg.moe_intermediate_size * self.cfg.n_shared_experts // self.tp
+        return self.tp_rank * n, (self.tp_rank + 1) * n
 
     # ------------------------------------------------------------------ state
     def _alloc_state(self) -> None:
@@ -370,8 +378,9 @@ class DeepSeekRunner:
                         b["xq"], b["xsf"], b["xg"], b["xg_sf"], b["err"], nr, 1, rows * nr, self._moe_bn(rows),
                         b["pair_src"], b["pair_w"])
             I = c.moe_intermediate_size
+            c0, c1 = self.shared_cols()
             self._gemm(L["gate_up"], b["xg"], b["xg_sf"], rows, b["act"], I, EPI_SILU, grouped=True,
-                       out_sf=b["act_sf"])
+                       out_sf=b["act_sf"], last_tiles=(c0 // 64, (c1 - c0) // 64) if self.tp > 1 else None)
             self._gemm(L["down"], b["act"], b["act_sf"], rows, b["moe_y"], H, EPI_BF16, grouped=True)
             C.gather_sum(b["moe_y"], b["pair_src"], b["pair_w"], rows, b["y"])
         self._reduce(rows)

@@ -121,6 +121,7 @@ class Qwen35Runner:
         # Shared expert: replicated gate/up, down output-sharded by rank (only rank r writes
         # its 1/tp slice of the hidden dim; the all-reduce then sums the slices).
         assert cfg.shared_expert_intermediate_size == cfg.moe_intermediate_size
+        assert cfg.shared_expert_intermediate_size % (64 * tp_size) == 0, "shared expert tiles must split over ranks"
         self.groups = self.e_local + 1
         self.top_k = cfg.num_experts_per_tok
         self.k1 = self.top_k + 1
@@ -219,13 +220,21 @@ class Qwen35Runner:
         down = get(p + "moe.down")[eb:ee]
         sd = get(p + "moe.shared.down")
         if self.tp > 1:
-            # Output-sharded shared down-projection: zero the rows other ranks own.
-            n = H // self.tp
-            mask = torch.zeros(H, 1, dtype=sd.dtype, device=sd.device)
-            mask[self.tp_rank * n:(self.tp_rank + 1) * n] = 1
+            # Tensor-parallel shared expert: rank r computes the intermediate columns
+            # [r*I/tp, (r+1)*I/tp) (its 128-row tiles of the interleaved gate/up, selected in
+            # the grouped GEMM by last_m0/last_mt) and the down projection over those columns
+            # only (the other columns' weights are zero), so the all-reduce sums the slices.
+            sl = self.shared_cols()
+            mask = torch.zeros(1, sd.shape[1], dtype=sd.dtype, device=sd.device)
+            mask[:, sl[0]:sl[1]] = 1
             sd = sd * mask
         out["down"] = pack_linear(torch.cat([down, sd[None]], 0), C)
         return out
+
+    def shared_cols(self) -> tuple[int, int]:
+        """This rank's intermediate columns of the shared expert."""
+        n = self.cfg.shared_expert_intermediate_size // self.tp
+        return self.tp_rank * n, (self.tp_rank + 1) * n
 
     # ------------------------------------------------------------------ state
     def _alloc_state(self) -> None:
@@ -330,12 +339,14 @@ class Qwen35Runner:
 
     # ------------------------------------------------------------------ kernels
     def _gemm(self, w: PackedLinear, xq, xsf, rows: int, out, ldo: int, epi=EPI_BF16, grouped=False,
-              out_sf=None, row_dst=None, row_scale=None, k_splits: int = 1, **sampling):
+              out_sf=None, row_dst=None, row_scale=None, k_splits: int = 1, last_tiles=None, **sampling):
         b = self.buf
         if grouped:
             bn = self._moe_bn(rows)
+            m0, mt = last_tiles if last_tiles is not None else (0, 0)
             self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, w.groups, 0, b["gcount"], b["goff"], b["gpre"],
-                             epi, out, ldo, out_sf, row_dst, row_scale, b["err"], 0, bn, 1, 0, 1, a_fp4=int(w.fp4))
+                             epi, out, ldo, out_sf, row_dst, row_scale, b["err"], 0, bn, 1, 0, 1, a_fp4=int(w.fp4),
+                             last_m0=m0, last_mt=mt)
         else:
             bn = 32 if rows <= 32 else 128
             tiles = -(-rows // bn) * (w.n_pad // 128)
@@ -493,7 +504,10 @@ class Qwen35Runner:
                     b["goff"], b["gpre"], b["pair_slot"], b["row_dst"], b["row_scale"], b["xq"], b["xsf"], b["xg"],
                     b["xg_sf"], b["err"], nr, s, rows * nr, self._moe_bn(rows), b["pair_src"], b["pair_w"])
         I = cfg.moe_intermediate_size
-        self._gemm(L["gate_up"], b["xg"], b["xg_sf"], rows, b["act"], I, EPI_SILU, grouped=True, out_sf=b["act_sf"])
+        # Shared expert (last group): this rank's 128-row gate/up tiles only (64 columns each).
+        c0, c1 = self.shared_cols()
+        self._gemm(L["gate_up"], b["xg"], b["xg_sf"], rows, b["act"], I, EPI_SILU, grouped=True, out_sf=b["act_sf"],
+                   last_tiles=(c0 // 64, (c1 - c0) // 64) if self.tp > 1 else None)
         self._gemm(L["down"], b["act"], b["act_sf"], rows, b["moe_y"], cfg.hidden_size, EPI_BF16, grouped=True)
 
     def _lm_head_argmax(self, rows: int, xq=None, xsf=None, pos=None, head=None) -> None:
