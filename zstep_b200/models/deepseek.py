@@ -72,6 +72,7 @@ class DeepSeekRunner:
     check_error = Qwen35Runner.check_error
     _gemm = Qwen35Runner._gemm
     _fix_splits = Qwen35Runner._fix_splits
+    _dense_bn = Qwen35Runner._dense_bn
     _gather_sf = Qwen35Runner._gather_sf
     _lm_head_argmax = Qwen35Runner._lm_head_argmax
     lm_head_rows = Qwen35Runner.lm_head_rows

@@ -348,12 +348,25 @@ class Qwen35Runner:
                              epi, out, ldo, out_sf, row_dst, row_scale, b["err"], 0, bn, 1, 0, 1, a_fp4=int(w.fp4),
                              last_m0=m0, last_mt=mt)
         else:
-            bn = 32 if rows <= 32 else 128
+            bn = self._dense_bn(rows, w)
             tiles = -(-rows // bn) * (w.n_pad // 128)
             fs = self._fix_splits(tiles, tiles, w.k // 128, bn) if (k_splits == 1 and self.use_fix_splits) else 1
             self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, 1, rows, None, None, None, epi, out, ldo,
                              out_sf, row_dst, row_scale, b["err"], 0, bn, k_splits, rows * ldo, 1,
                              fs, b["gemm_ws"], b["gemm_sem"], a_fp4=int(w.fp4), **sampling)
+
+    def _dense_bn(self, rows: int, w: PackedLinear, k_splits: int = 1) -> int:
+        """Token tile of a dense GEMM.  One CTA streams its weight tiles at a bounded rate, so
+        a GEMM with few 128-token work items leaves most SMs idle; 32-token items multiply
+        the CTAs (the weight tile is re-read from L2 per item) until about half the SMs
+        have work.  ZSTEP_GEMM_DENSE_BN pins 32 or 128."""
+        forced = runtime_config().gemm_dense_bn
+        if forced:
+            return forced
+        if rows <= 32:
+            return 32
+        items128 = -(-rows // 128) * (w.n_pad // 128) * max(1, k_splits)
+        return 32 if rows <= 512 and items128 * 2 < self.num_sms else 128
 
     def _fix_splits(self, max_tiles: int, items: int, k_tiles: int, bn: int) -> int:
         """In-kernel split-K factor for a dense GEMM: double while all split items still fit
@@ -376,7 +389,7 @@ class Qwen35Runner:
         """Split K until the dense GEMM has about one wave of work items (decode only)."""
         if rows > self.max_seqs:
             return 1
-        bn = 32 if rows <= 32 else 128
+        bn = self._dense_bn(rows, w)
         items = ((rows + bn - 1) // bn) * (w.n_pad // 128)
         k_tiles = w.k // 128
         s = 1

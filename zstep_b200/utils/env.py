@@ -42,6 +42,13 @@ def _int(name: str, raw: str, lo: int | None = None, hi: int | None = None) -> i
     return v
 
 
+def _choice_int(name: str, raw: str, choices: tuple[int, ...]) -> int:
+    v = _int(name, raw)
+    if v not in choices:
+        raise EnvError(f"{name}={v}: expected one of {', '.join(map(str, choices))}")
+    return v
+
+
 def _choice(name: str, raw: str, choices: tuple[str, ...]) -> str:
     v = raw.strip().lower()
     if v not in choices:
@@ -57,6 +64,7 @@ class RuntimeConfig:
     coll_ll_rows: int = 1024              # ZSTEP_COLL_LL_ROWS: two-shot LL lines up to this many rows, plain above
     coll_push: bool = True                # ZSTEP_COLL_PUSH: row-parallel GEMM epilogues push into the all-reduce
     gemm_fix_splits: bool = False         # ZSTEP_GEMM_FIX_SPLITS: in-kernel split-K for small GEMMs
+    gemm_dense_bn: int = 0                # ZSTEP_GEMM_DENSE_BN: dense GEMM token tile 32 | 128 (0: by shape)
     decode_graphs: bool = True            # ZSTEP_DECODE_GRAPHS: CUDA-graph decode buckets
     pdl: bool = True                      # ZSTEP_PDL: programmatic dependent launch of the kernels
     spec_method: str = "none"             # ZSTEP_SPEC_METHOD: none | ngram | mtp
@@ -75,6 +83,7 @@ class RuntimeConfig:
         "ZSTEP_COLL_LL_ROWS": ("coll_ll_rows", lambda n, r: _int(n, r, 0, 1 << 16)),
         "ZSTEP_COLL_PUSH": ("coll_push", _bool),
         "ZSTEP_GEMM_FIX_SPLITS": ("gemm_fix_splits", _bool),
+        "ZSTEP_GEMM_DENSE_BN": ("gemm_dense_bn", lambda n, r: _choice_int(n, r, (0, 32, 128))),
         "ZSTEP_DECODE_GRAPHS": ("decode_graphs", _bool),
         "ZSTEP_PDL": ("pdl", _bool),
         "ZSTEP_SPEC_METHOD": ("spec_method", lambda n, r: _choice(n, r, ("none", "ngram", "mtp"))),
