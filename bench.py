@@ -50,7 +50,7 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--engine-path", type=int, default=1,
                     help="also time decode through the native master (zstep run, SHM + eventfd) at N GPUs")
-    ap.add_argument("--engine-gen", type=int, default=48, help="engine path: output tokens per request")
+    ap.add_argument("--engine-gen", type=int, default=256, help="engine path: output tokens per request")
     ap.add_argument("--nccl-arm", type=int, default=1, help="N>1: also time the same decode step with NCCL collectives")
     return ap.parse_args()
 

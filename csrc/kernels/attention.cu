@@ -642,300 +642,6 @@ __global__ void decode_combine_kernel(const AttnArgs a) {
   }
 }
 
-// ---------------------------------------------------------------------------------------
-// Query-tiled prefill attention (tcgen05, flash-style).  One CTA per (128-row query tile of
-// one sequence, q head); 128 threads, thread t owns query row t of the tile.
-//   * Q tile [128 rows x 256 dims] is staged once into shared memory as a 128-byte
-//     swizzled K-major operand (4 chunks of 64 dims, 8-row groups 1 KiB apart).
-//   * Keys stream in 64-key tiles (4 pages) by cp.async.bulk of the pre-swizzled cache
-//     blocks, K and V double-buffered, one tile ahead of the math.
-//   * S = Q K^T: 16 tcgen05.mma (M = 128 queries, N = 64 keys, K = 16 dims each) into TMEM
-//     columns [0, 64).  Each thread reads its row of S (tcgen05.ld), applies the causal
-//     mask (key position <= the row's position), and keeps an online softmax in the exp2
-//     domain; P = exp2(S - m) is written as bf16 into a swizzled K-major tile.
-//   * O += P V: 4 tcgen05.mma (M = 128, N = 256 dims, K = 16 keys) into TMEM columns
-//     [256, 512), V read MN-major straight from the page image.  When a row's maximum
-//     grows the row's O is rescaled in TMEM first (warps whose rows all kept their maximum
-//     skip it).
-//   * Key tiles past the tile's last query position are skipped (causal), so a chunk's
-//     work is quadratic in its own length only through its diagonal tiles.
-//   * Epilogue: O / l, sigmoid gate, bf16 and/or MXFP8 output (scale per 32 dims), the same
-//     rounding as the decode combine.
-// Rows of a prefill chunk may start at any position (chunked prefill): each row attends to
-// keys [0, position] of its sequence's pages, which the prologue has already written.
-constexpr int PF_Q = 128;                 // queries per tile
-constexpr int PF_KEYS = 64;               // keys per tile
-constexpr int PF_PAGES = PF_KEYS / PAGE;  // 4 pages
-constexpr int PF_THREADS = 128;
-
-struct PfSmem {
-  uint8_t q[4][PF_Q * 128];               // Q: 4 chunks of 64 dims x 128 rows (16 KiB each)
-  uint8_t k[2][PF_PAGES * BLOCK_BYTES];   // K tile images (32 KiB each)
-  uint8_t v[2][PF_PAGES * BLOCK_BYTES];   // V tile images
-  uint8_t p[PF_Q * 128];                  // P: 128 rows x 64 keys bf16, one 128-byte swizzle chunk
-  uint64_t kfull[2], vfull[2], mma_s, mma_pv;
-  uint32_t tmem_base;
-  int row_pos[PF_Q];
-};
-
-__global__ void __launch_bounds__(PF_THREADS, 1) prefill_tc_kernel(const AttnArgs a) {
-  pdl_wait();
-  pdl_trigger();
-  extern __shared__ __align__(1024) uint8_t pf_smem_raw[];
-  PfSmem& s = *reinterpret_cast<PfSmem*>((reinterpret_cast<uintptr_t>(pf_smem_raw) + 1023) & ~uintptr_t(1023));
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int qh = blockIdx.y;
-  const int G = a.num_q_heads / a.num_kv_heads, kvh = qh / G;
-  // Locate this CTA's (sequence, query tile): tiles are numbered sequence after sequence.
-  int seq = -1, tile = 0;
-  {
-    int acc = 0;
-    for (int i = 0; i < a.num_seqs; ++i) {
-      const int n = (a.seq_start[i + 1] - a.seq_start[i] + PF_Q - 1) / PF_Q;
-      if ((int)blockIdx.x < acc + n) {
-        seq = i;
-        tile = blockIdx.x - acc;
-        break;
-      }
-      acc += n;
-    }
-  }
-  if (seq < 0) return;  // past the last tile (the grid is an upper bound)
-  const int r_begin = a.seq_start[seq] + tile * PF_Q;
-  const int n_rows = min(PF_Q, a.seq_start[seq + 1] - r_begin);
-  const int slot = a.slots[r_begin];
-  const int* pt = a.page_table + (size_t)slot * a.max_pages;
-  if (tid < PF_Q) s.row_pos[tid] = tid < n_rows ? a.positions[r_begin + tid] : -1;
-  if (warp == 0) {
-    tmem_alloc(&s.tmem_base, 512);
-    tmem_relinquish();
-  }
-  if (tid == 0) {
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s.kfull[b], 1);
-      mbar_init(&s.vfull[b], 1);
-    }
-    mbar_init(&s.mma_s, 1);
-    mbar_init(&s.mma_pv, 1);
-    fence_barrier_init();
-  }
-  // Q tile -> swizzled K-major image (rows past the tile are zero).
-  const __nv_bfloat16* qsrc = static_cast<const __nv_bfloat16*>(a.q_out);
-  for (int i = tid; i < PF_Q * 32; i += PF_THREADS) {
-    const int r = i >> 5, pc = i & 31, c = pc >> 3, piece = pc & 7;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < n_rows) v = *reinterpret_cast<const uint4*>(qsrc + ((size_t)(r_begin + r) * a.num_q_heads + qh) * D + pc * 8);
-    *reinterpret_cast<uint4*>(s.q[c] + (r >> 3) * 1024 + (r & 7) * 128 + ((piece ^ (r & 7)) << 4)) = v;
-  }
-  fence_proxy_async_shared();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = s.tmem_base;
-  const uint32_t t_s = tmem, t_o = tmem + 256;
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-  // Keys [0, last_pos] cover every row of the tile (positions increase along a sequence).
-  const int last_pos = s.row_pos[n_rows - 1];
-  const int n_keys = last_pos + 1;
-  const int ntiles = (n_keys + PF_KEYS - 1) / PF_KEYS;
-  const int total_pages = (n_keys + PAGE - 1) / PAGE;
-  const __nv_bfloat16* kc = static_cast<const __nv_bfloat16*>(a.k_cache);
-  const __nv_bfloat16* vc = static_cast<const __nv_bfloat16*>(a.v_cache);
-  auto issue = [&](const __nv_bfloat16* cache, uint8_t* dst, uint64_t* bar, int t) {
-    const int pg0 = t * PF_PAGES;
-    const int n = min(PF_PAGES, total_pages - pg0);
-    mbar_expect_tx(bar, n * BLOCK_BYTES);
-    for (int j = 0; j < n; ++j)
-      bulk_load(dst + j * BLOCK_BYTES, cache + kv_offset(a, __ldg(pt + pg0 + j), kvh), BLOCK_BYTES, bar);
-  };
-  // Producer bookkeeping (thread 0): loads issued per buffer and whether one is unconsumed.
-  int k_pend[2] = {0, 0}, v_pend[2] = {0, 0}, k_iss[2] = {0, 0}, v_iss[2] = {0, 0};
-  if (tid == 0) {
-    for (int t = 0; t < 2 && t < ntiles; ++t) {
-      issue(kc, s.k[t], &s.kfull[t], t);
-      issue(vc, s.v[t], &s.vfull[t], t);
-      k_pend[t] = v_pend[t] = 1;
-      k_iss[t] = v_iss[t] = 1;
-    }
-  }
-  const float qscale = a.sm_scale * 1.4426950408889634f;
-  const int my_pos = s.row_pos[tid];
-  float m = -INFINITY, l = 0.f;
-  bool ok = true;
-  for (int t = 0; t < ntiles; ++t) {
-    const int b = t & 1;
-    const uint32_t ph = (uint32_t)((t >> 1) & 1);
-    const int pg0 = t * PF_PAGES;
-    const int n_pg = min(PF_PAGES, total_pages - pg0);
-    if (n_pg < PF_PAGES) {
-      // Partial last tile: zero the absent pages of both images so the products stay finite.
-      for (int i = n_pg * (BLOCK_BYTES / 16) + tid; i < PF_PAGES * (BLOCK_BYTES / 16); i += PF_THREADS) {
-        reinterpret_cast<uint4*>(s.k[b])[i] = make_uint4(0, 0, 0, 0);
-        reinterpret_cast<uint4*>(s.v[b])[i] = make_uint4(0, 0, 0, 0);
-      }
-      fence_proxy_async_shared();
-    }
-    ok = mbar_wait(&s.kfull[b], ph, a.err);
-    if (!__syncthreads_and(ok)) break;
-    if (tid == 0) {
-      k_pend[b] = 0;
-      tc_fence_after();
-      const uint32_t idesc = make_idesc_bf16(PF_Q, PF_KEYS, 0, 0);
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t ad = make_smem_desc(smem_u32(s.q[c]) + k * 32, 16, 1024, 2);
-          const uint64_t bd = make_smem_desc(smem_u32(s.k[b] + c * 1024) + k * 32, 16, 4096, 2);
-          mma_bf16(t_s, ad, bd, idesc, (c | k) ? 1u : 0u);
-        }
-      tc_commit(&s.mma_s);
-    }
-    ok = mbar_wait(&s.mma_s, (uint32_t)(t & 1), a.err);
-    if (!__syncthreads_and(ok)) break;
-    tc_fence_after();
-    if (tid == 0 && t + 2 < ntiles) {  // S is in TMEM: this K image is free
-      issue(kc, s.k[b], &s.kfull[b], t + 2);
-      k_pend[b] = 1;
-      ++k_iss[b];
-    }
-    // The previous P V product must be done before P and O are touched again.
-    if (t > 0) {
-      ok = mbar_wait(&s.mma_pv, (uint32_t)((t - 1) & 1), a.err);
-      if (!__syncthreads_and(ok)) break;
-      tc_fence_after();
-      if (tid == 0 && t + 1 < ntiles) {  // V image of tile t-1 is free: tile t+1 goes there
-        issue(vc, s.v[b ^ 1], &s.vfull[b ^ 1], t + 1);
-        v_pend[b ^ 1] = 1;
-        ++v_iss[b ^ 1];
-      }
-    }
-    // ---- online softmax over this thread's row of S
-    float sv[PF_KEYS];
-    {
-      uint32_t r0[32], r1[32];
-      tmem_ld_32x32b_x32(t_s + lane_off, r0);
-      tmem_ld_32x32b_x32(t_s + 32 + lane_off, r1);
-      tmem_ld_wait();
-      const int key0 = t * PF_KEYS;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        sv[j] = key0 + j <= my_pos ? __uint_as_float(r0[j]) * qscale : -INFINITY;
-        sv[32 + j] = key0 + 32 + j <= my_pos ? __uint_as_float(r1[j]) * qscale : -INFINITY;
-      }
-    }
-    float tmax = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < PF_KEYS; ++j) tmax = fmaxf(tmax, sv[j]);
-    const float m_new = fmaxf(m, tmax);
-    const float rr = (m == -INFINITY || m_new == -INFINITY) ? 0.f : exp2f(m - m_new);
-    float psum = 0.f;
-#pragma unroll
-    for (int piece = 0; piece < 8; ++piece) {
-      uint32_t w[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float p0 = sv[piece * 8 + 2 * e] == -INFINITY ? 0.f : exp2f(sv[piece * 8 + 2 * e] - m_new);
-        const float p1 = sv[piece * 8 + 2 * e + 1] == -INFINITY ? 0.f : exp2f(sv[piece * 8 + 2 * e + 1] - m_new);
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-        const float2 back = __bfloat1622float2(h2);
-        psum += back.x + back.y;
-        w[e] = *reinterpret_cast<uint32_t*>(&h2);
-      }
-      *reinterpret_cast<uint4*>(s.p + (tid >> 3) * 1024 + (tid & 7) * 128 + ((piece ^ (tid & 7)) << 4)) =
-          make_uint4(w[0], w[1], w[2], w[3]);
-    }
-    l = l * rr + psum;
-    const bool grew = t > 0 && m_new > m && m != -INFINITY;
-    m = m_new;
-    // Rescale this row's O when its maximum grew (whole warps skip when none did).
-    if (__any_sync(0xffffffff, grew)) {
-      const float f = grew ? rr : 1.f;
-#pragma unroll 1
-      for (int c0 = 0; c0 < 256; c0 += 16) {
-        uint32_t o[16];
-        tmem_ld_32x32b_x16(t_o + c0 + lane_off, o);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * f);
-        tmem_st_32x32b_x16(t_o + c0 + lane_off, o);
-      }
-      tmem_st_wait();
-    }
-    fence_proxy_async_shared();
-    tc_fence_before();
-    ok = mbar_wait(&s.vfull[b], ph, a.err);
-    if (!__syncthreads_and(ok)) break;
-    if (tid == 0) {
-      v_pend[b] = 0;
-      tc_fence_after();
-      const uint32_t idesc2 = make_idesc_bf16(PF_Q, 256, 0, 1);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {  // 16 keys (one page) per MMA
-        const uint64_t ad = make_smem_desc(smem_u32(s.p) + k * 32, 16, 1024, 2);
-        const uint64_t bd = make_smem_desc(smem_u32(s.v[b]) + k * BLOCK_BYTES, 1024, 4096, 2);
-        mma_bf16(t_o, ad, bd, idesc2, (t > 0 || k > 0) ? 1u : 0u);
-      }
-      tc_commit(&s.mma_pv);
-    }
-  }
-  if (ok && ntiles > 0) ok = mbar_wait(&s.mma_pv, (uint32_t)((ntiles - 1) & 1), a.err);
-  ok = __syncthreads_and(ok);
-  tc_fence_after();
-  if (ok && tid < n_rows) {
-    // ---- epilogue: O / l, gate, bf16 and/or MXFP8
-    const int row = r_begin + tid;
-    const float inv_l = l > 0.f ? 1.f / l : 0.f;
-    const __nv_bfloat16* gp = static_cast<const __nv_bfloat16*>(a.gate_out) + ((size_t)row * a.num_q_heads + qh) * D;
-    const int width = a.num_q_heads * D;
-#pragma unroll 1
-    for (int c0 = 0; c0 < 256; c0 += 32) {
-      uint32_t o[32];
-      tmem_ld_32x32b_x32(t_o + c0 + lane_off, o);
-      tmem_ld_wait();
-      float y[32];
-      float amax = 0.f;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float g = __bfloat162float(gp[c0 + j]);
-        y[j] = bfr(bfr(__uint_as_float(o[j]) * inv_l) * sigmoidf_(g));
-        amax = fmaxf(amax, fabsf(y[j]));
-      }
-      const int col = qh * D + c0;
-      if (a.out_bf16 != nullptr) {
-        __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(a.out_bf16) + (size_t)row * width + col;
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) *reinterpret_cast<__nv_bfloat162*>(ob + j) = __floats2bfloat162_rn(y[j], y[j + 1]);
-      }
-      if (a.out_q != nullptr) {
-        const uint8_t code = mx_scale_e8m0(amax);
-        const float inv = mx_inv_scale(code);
-        uint32_t w8[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          w8[i] = uint32_t(f32_to_e4m3(y[4 * i] * inv)) | (uint32_t(f32_to_e4m3(y[4 * i + 1] * inv)) << 8) |
-                  (uint32_t(f32_to_e4m3(y[4 * i + 2] * inv)) << 16) | (uint32_t(f32_to_e4m3(y[4 * i + 3] * inv)) << 24);
-        uint4* dq = reinterpret_cast<uint4*>(a.out_q + (size_t)row * width + col);
-        dq[0] = make_uint4(w8[0], w8[1], w8[2], w8[3]);
-        dq[1] = make_uint4(w8[4], w8[5], w8[6], w8[7]);
-        const int kb = col >> 5;
-        a.out_sf[((size_t)(row >> 7) * (width >> 7) + (kb >> 2)) * 512 + sf_atom_offset(row & 127, kb & 3)] = code;
-      }
-    }
-  }
-  if (!ok && tid == 0) {
-    // Abort: let every copy still in flight land before the CTA releases shared memory.
-    for (int b = 0; b < 2; ++b) {
-      if (k_pend[b]) mbar_wait(&s.kfull[b], (uint32_t)((k_iss[b] - 1) & 1), nullptr);
-      if (v_pend[b]) mbar_wait(&s.vfull[b], (uint32_t)((v_iss[b] - 1) & 1), nullptr);
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, 512);
-}
-
 }  // namespace attn
 }  // namespace zs
 
@@ -973,22 +679,10 @@ extern "C" int zs_attn_decode(const AttnArgs* args, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }
 
-// Varlen prefill.  With seq_start the query-tiled tensor-core kernel runs (rows of one
-// sequence are consecutive; every row's K/V was written by the prologue); without it (or
-// impl = 1) the decode kernels run once per row with per-row causal lengths.
+// Varlen prefill: identical math with per-row causal context lengths (seq_lens must
+// hold position + 1 for every row); the caller runs the prologue for all rows first.
 extern "C" int zs_attn_prefill(const AttnArgs* args, cudaStream_t stream) {
-  const AttnArgs& a = *args;
-  if (a.seq_start == nullptr || a.impl == 1) return zs_attn_decode(args, stream);
-  if (a.head_dim != zs::attn::D || a.num_kv_heads <= 0 || a.num_q_heads % a.num_kv_heads != 0 ||
-      a.page_size != zs::attn::PAGE || a.num_seqs < 1)
-    return -1;
-  if (a.rows == 0) return 0;
-  const size_t smem = sizeof(zs::attn::PfSmem) + 1024;
-  cudaFuncSetAttribute(zs::attn::prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  // Upper bound on the number of 128-row tiles: rows / 128 + one partial tile per sequence.
-  dim3 grid((a.rows + zs::attn::PF_Q - 1) / zs::attn::PF_Q + a.num_seqs, a.num_q_heads);
-  zs_launch(zs::attn::prefill_tc_kernel, grid, zs::attn::PF_THREADS, smem, stream, a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+  return zs_attn_decode(args, stream);
 }
 
 // ---------------------------------------------------------------------------------------

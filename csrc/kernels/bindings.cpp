@@ -307,40 +307,6 @@ void attn_decode(const Tensor& q_out, const Tensor& gate_out, int64_t num_q_head
   rc(zs_attn_decode(&a, stream()), "zs_attn_decode");
 }
 
-void attn_prefill(const Tensor& q_out, const Tensor& gate_out, int64_t num_q_heads, int64_t num_kv_heads,
-                  const Tensor& k_cache, const Tensor& v_cache, int64_t page_size, const Tensor& page_table,
-                  const Tensor& slots, const Tensor& positions, int64_t rows, const Tensor& seq_start,
-                  int64_t num_seqs, double sm_scale, const OptT& out_bf16, const OptT& out_q, const OptT& out_sf,
-                  const OptT& err) {
-  check_cuda(q_out, "q_out");
-  check_cuda(seq_start, "seq_start");
-  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(2) == page_size, "k_cache must be [pages, kv_heads, page, 256]");
-  TORCH_CHECK(seq_start.scalar_type() == at::kInt && seq_start.numel() >= num_seqs + 1, "seq_start: int32 [n+1]");
-  TORCH_CHECK(positions.scalar_type() == at::kInt && positions.numel() >= rows, "positions: int32 [rows]");
-  AttnArgs a{};
-  a.num_q_heads = (int)num_q_heads;
-  a.num_kv_heads = (int)num_kv_heads;
-  a.head_dim = 256;
-  a.k_cache = ptr(k_cache);
-  a.v_cache = ptr(v_cache);
-  a.page_size = (int)page_size;
-  a.page_table = ptr<const int>(page_table);
-  a.max_pages = (int)page_table.size(1);
-  a.slots = ptr<const int>(slots);
-  a.positions = ptr<const int>(positions);
-  a.rows = (int)rows;
-  a.q_out = ptr(q_out);
-  a.gate_out = ptr(gate_out);
-  a.seq_start = ptr<const int>(seq_start);
-  a.num_seqs = (int)num_seqs;
-  a.sm_scale = (float)sm_scale;
-  a.out_bf16 = optptr(out_bf16);
-  a.out_q = optptr<uint8_t>(out_q);
-  a.out_sf = optptr<uint8_t>(out_sf);
-  a.err = optptr<int>(err);
-  rc(zs_attn_prefill(&a, stream()), "zs_attn_prefill");
-}
-
 void moe_route(const Tensor& logits, int64_t rows, int64_t num_experts, int64_t top_k,
                bool norm_topk, int64_t scoring, const OptT& bias, int64_t n_group,
                int64_t topk_group, double routed_scale, int64_t shared_gate_col,
@@ -926,10 +892,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("push_part") = std::vector<int64_t>{}, py::arg("push_epoch") = py::none(), py::arg("push_rank") = 0,
         py::arg("push_mode") = 1, py::arg("last_m0") = 0, py::arg("last_mt") = 0);
   m.def("quant_mxf8", &quant_mxf8);
-  m.def("attn_prefill", &attn_prefill, py::arg("q_out"), py::arg("gate_out"), py::arg("num_q_heads"),
-        py::arg("num_kv_heads"), py::arg("k_cache"), py::arg("v_cache"), py::arg("page_size"), py::arg("page_table"),
-        py::arg("slots"), py::arg("positions"), py::arg("rows"), py::arg("seq_start"), py::arg("num_seqs"),
-        py::arg("sm_scale"), py::arg("out_bf16"), py::arg("out_q"), py::arg("out_sf"), py::arg("err") = py::none());
   m.def("spec_verify", &spec_verify);
   m.def("add_rmsnorm_quant", &add_rmsnorm_quant, py::arg("residual"), py::arg("delta"), py::arg("n_terms"),
         py::arg("d_row_stride"), py::arg("d_term_stride"), py::arg("weight"), py::arg("w_offset"), py::arg("eps"),

@@ -657,57 +657,6 @@ def test_attention_decode_tensor_core(C, hq, hkv, splits):
     del grp
 
 
-@pytest.mark.parametrize("hq,hkv", [(16, 2), (2, 1), (4, 1)])
-def test_attention_prefill_query_tiled(C, hq, hkv):
-    """The query-tiled tcgen05 prefill (128-query tiles, 64-key tiles of bulk-copied pages,
-    causal masking, online softmax with TMEM rescale) against the fp32 reference: varlen
-    sequences whose chunks start at position 0 and mid-sequence (chunked prefill over an
-    existing KV prefix), lengths that end mid-page and cross tile boundaries; bf16 and MXFP8
-    outputs (the MXFP8 one against the bf16 one through the same quantizer)."""
-    g = torch.Generator().manual_seed(11)
-    d, page = 256, 16
-    # (first position of the chunk, rows of the chunk) per sequence
-    seqs = [(0, 1), (0, 37), (0, 128), (0, 200), (70, 60), (300, 150), (5, 3)]
-    rows = sum(n for _, n in seqs)
-    max_pages = 32
-    pages_total = len(seqs) * max_pages + 1
-    perm = torch.randperm(pages_total - 1, generator=g) + 1
-    table = perm.view(len(seqs), max_pages).to(torch.int32)
-    kc = (torch.randn(pages_total, hkv, page, d, generator=g) * 0.5).to(torch.bfloat16)
-    vc = (torch.randn(pages_total, hkv, page, d, generator=g) * 0.5).to(torch.bfloat16)
-    q = torch.randn(rows, hq, d, generator=g).to(torch.bfloat16)
-    gate = torch.randn(rows, hq, d, generator=g).to(torch.bfloat16)
-    slots, pos, starts = [], [], [0]
-    for i, (p0, n) in enumerate(seqs):
-        slots += [i] * n
-        pos += list(range(p0, p0 + n))
-        starts.append(starts[-1] + n)
-    sm = 1 / math.sqrt(d)
-    rp = (rows + 127) // 128 * 128
-    out = torch.zeros(rows, hq * d, dtype=torch.bfloat16, device="cuda")
-    oq = torch.zeros(rp, hq * d, dtype=torch.uint8, device="cuda")
-    osf = torch.zeros(mx.atoms_bytes(rp, hq * d), dtype=torch.uint8, device="cuda")
-    err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device="cuda")  # noqa: E731
-    C.attn_prefill(q.cuda(), gate.cuda(), hq, hkv, swizzle_pages(kc).cuda(), swizzle_pages(vc).cuda(), page,
-                   table.cuda(), i32(slots), i32(pos), rows, i32(starts), len(seqs), sm, out, oq, osf, err)
-    torch.cuda.synchronize()
-    assert err.item() == 0
-    outc = out.cpu().float()
-    for r in range(rows):
-        sl, ctx = slots[r], pos[r] + 1
-        keys = torch.stack([kc[table[sl, t // page], :, t % page].float() for t in range(ctx)])
-        vals = torch.stack([vc[table[sl, t // page], :, t % page].float() for t in range(ctx)])
-        expect = ref.gated_attention(q[r].float(), gate[r].float(), keys, vals, sm)
-        torch.testing.assert_close(outc[r], expect, rtol=2e-2, atol=2e-2)
-    # MXFP8 output: the bf16 output quantized by the library's quantizer.
-    q2 = torch.zeros_like(oq)
-    sf2 = torch.zeros_like(osf)
-    C.quant_mxf8(out, q2[:rows], sf2)
-    assert torch.equal(oq[:rows], q2[:rows])
-    assert torch.equal(mx.codes_from_atoms(osf, rows, hq * d), mx.codes_from_atoms(sf2, rows, hq * d))
-
-
 def _sample(C, logits, temp, top_k, top_p, seeds, hist=None, pres=None, freq=None, rep=None, top_n=0):
     n, v = logits.shape
     dev = "cuda"

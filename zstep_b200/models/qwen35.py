@@ -276,9 +276,7 @@ class Qwen35Runner:
         # In-kernel split-K for dense GEMMs with few output tiles.  Off by default: on the
         # decode shapes measured so far it did not beat the unsplit kernel.
         self.use_fix_splits = runtime_config().gemm_fix_splits
-        # Varlen prefill attention: 0 = query-tiled tensor-core kernel (split-KV tensor-core
-        # decode per row for short rows), 1 = SIMT decode kernel per row, 2 = tensor-core
-        # decode kernel per row (per-row causal lengths).
+        # Varlen prefill attention: 0 = tensor-core kernel, 1 = SIMT kernel (per-row causal lengths).
         self.prefill_attn_impl = 0
         b["xq"] = torch.zeros(Rp, H, dtype=torch.uint8, device=dev)
         b["xsf"] = torch.zeros(mx.atoms_bytes(Rp, H), dtype=torch.uint8, device=dev)
@@ -348,7 +346,7 @@ class Qwen35Runner:
                              epi, out, ldo, out_sf, row_dst, row_scale, b["err"], 0, bn, 1, 0, 1, a_fp4=int(w.fp4),
                              last_m0=m0, last_mt=mt)
         else:
-            bn = self._dense_bn(rows, w)
+            bn = self._dense_bn(rows, w) if k_splits == 1 else (32 if rows <= 32 else 128)
             tiles = -(-rows // bn) * (w.n_pad // 128)
             fs = self._fix_splits(tiles, tiles, w.k // 128, bn) if (k_splits == 1 and self.use_fix_splits) else 1
             self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, 1, rows, None, None, None, epi, out, ldo,
@@ -365,8 +363,10 @@ class Qwen35Runner:
             return forced
         if rows <= 32:
             return 32
+        # Measured on B200 at 256 rows: 32-token items win up to ~32 128-token items
+        # (e.g. 15.4 vs 17.0 us at 1536 x 2048) and lose beyond (21.6 vs 17.4 us at 3088 x 2048).
         items128 = -(-rows // 128) * (w.n_pad // 128) * max(1, k_splits)
-        return 32 if rows <= 512 and items128 * 2 < self.num_sms else 128
+        return 32 if rows <= 512 and items128 * 4 <= self.num_sms else 128
 
     def _fix_splits(self, max_tiles: int, items: int, k_tiles: int, bn: int) -> int:
         """In-kernel split-K factor for a dense GEMM: double while all split items still fit
@@ -389,7 +389,7 @@ class Qwen35Runner:
         """Split K until the dense GEMM has about one wave of work items (decode only)."""
         if rows > self.max_seqs:
             return 1
-        bn = self._dense_bn(rows, w)
+        bn = 32 if rows <= 32 else 128  # split-K partials use the 128-token tile (see _gemm)
         items = ((rows + bn - 1) // bn) * (w.n_pad // 128)
         k_tiles = w.k // 128
         s = 1
@@ -485,19 +485,11 @@ class Qwen35Runner:
                                 self.eps, self.k_cache[ai], self.v_cache[ai], self.page_size, self.page_table, slot,
                                 pos, rows, b["q_out"], b["gate_out"])
                 midq = self._mid(self.hq * cfg.head_dim)
-                if not decode and self.prefill_attn_impl == 0 and rows >= 16 * max(1, num_seqs):
-                    # Query-tiled tensor-core prefill: 128-row tiles of each sequence.
-                    C.attn_prefill(b["q_out"], b["gate_out"], self.hq, self.hkv, self.k_cache[ai],
-                                   self.v_cache[ai], self.page_size, self.page_table, slot, pos, rows,
-                                   b["seq_start"][:num_seqs + 1], num_seqs, 1.0 / math.sqrt(cfg.head_dim), None,
-                                   midq, b["midsf"], b["err"])
-                else:
-                    # Decode, and short varlen rows (verify steps): split-KV per row.
-                    splits = self._attn_splits(rows, decode)
-                    C.attn_decode(b["q_out"], b["gate_out"], self.hq, self.hkv, self.k_cache[ai],
-                                  self.v_cache[ai], self.page_size, self.page_table, slot, lens, rows, b["partial"],
-                                  splits, 1.0 / math.sqrt(cfg.head_dim), None, midq, b["midsf"],
-                                  impl=1 if (not decode and self.prefill_attn_impl == 1) else 0)
+                splits = self._attn_splits(rows, decode)
+                C.attn_decode(b["q_out"], b["gate_out"], self.hq, self.hkv, self.k_cache[ai], self.v_cache[ai],
+                              self.page_size, self.page_table, slot, lens, rows, b["partial"], splits,
+                              1.0 / math.sqrt(cfg.head_dim), None, midq, b["midsf"],
+                              impl=0 if decode else self.prefill_attn_impl)
                 self._proj_out(L["o_proj"], midq, b["midsf"], rows, L["post_norm"])
             self._moe(L, rows)
             next_w = self.layers[li + 1]["input_norm"] if li + 1 < len(self.layers) else self.final_norm

@@ -330,7 +330,7 @@ class GpuRunner:
                 and all(int(w) == K + 1 for w in plan["spec_width"][:n])
                 and all(int(q) == i * (K + 1) for i, q in enumerate(plan["query_start"][:n + 1]))
                 and all(int(sr) == (i + 1) * (K + 1) - 1 for i, sr in enumerate(plan["sample_row"][:n]))):
-            nb = r.spec.graph_bucket(n)
+            nb = r.spec.graph_bucket(n) if hasattr(r.spec, "graph_bucket") else None
             if nb is not None:
                 return self._execute_spec_graph(plan, n, nb, out)
         qs = plan["query_start"].tolist()
