@@ -407,7 +407,8 @@ void fused_allreduce_norm(int64_t rank, int64_t world, int64_t protocol, const T
 
 void allreduce_sum_f32(int64_t rank, int64_t world, const Tensor& data, int64_t rows, int64_t max_rows,
                        const std::vector<int64_t>& buf, const Tensor& epoch, const Tensor& grid_counter,
-                       const OptT& err, int64_t timeout_ms) {
+                       const OptT& err, int64_t timeout_ms, const std::vector<int64_t>& part,
+                       const std::vector<int64_t>& out, const std::vector<int64_t>& flags) {
   TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)buf.size() == world, "bad world ", world, " / buffer list");
   check_cuda(data, "data");
   TORCH_CHECK(data.scalar_type() == at::kFloat && data.dim() == 2, "data: f32 [rows, cols]");
@@ -423,6 +424,16 @@ void allreduce_sum_f32(int64_t rank, int64_t world, const Tensor& data, int64_t 
   a.grid_counter = ptr<uint32_t>(grid_counter);
   a.err = optptr<int>(err);
   a.timeout_ms = (unsigned int)timeout_ms;
+  if (!part.empty()) {
+    TORCH_CHECK((int64_t)part.size() == world && (int64_t)out.size() == world && (int64_t)flags.size() == world,
+                "plain fp32 sum: part / out / flags per rank");
+    a.plain = 1;
+    for (int r = 0; r < world; ++r) {
+      a.part[r] = reinterpret_cast<void*>(part[r]);
+      a.out[r] = reinterpret_cast<void*>(out[r]);
+      a.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
+    }
+  }
   rc(zs_allreduce_sum_f32(&a, stream()), "zs_allreduce_sum_f32");
 }
 
@@ -859,7 +870,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("timeout_ms") = 0, py::arg("pushed") = false);
   m.def("allreduce_sum_f32", &allreduce_sum_f32, py::arg("rank"), py::arg("world"), py::arg("data"), py::arg("rows"),
         py::arg("max_rows"), py::arg("buf"), py::arg("epoch"), py::arg("grid_counter"), py::arg("err"),
-        py::arg("timeout_ms") = 0);
+        py::arg("timeout_ms") = 0, py::arg("part") = std::vector<int64_t>{}, py::arg("out") = std::vector<int64_t>{},
+        py::arg("flags") = std::vector<int64_t>{});
   m.def("allreduce_argmax", &allreduce_argmax, py::arg("rank"), py::arg("world"), py::arg("rows"),
         py::arg("max_rows"), py::arg("tile_keys"), py::arg("tiles"), py::arg("id_offset"), py::arg("lines"),
         py::arg("epoch"), py::arg("grid_counter"), py::arg("out_ids"), py::arg("out_vals"), py::arg("err"),

@@ -327,7 +327,8 @@ __global__ void __launch_bounds__(THREADS, 4) ar_twoshot_kernel(const FusedArArg
 // After a CTA's stores of a phase, every thread fences at system scope, then thread q
 // releases flag [phase][rank][c] on rank q; a consumer CTA c acquires the W flags of CTA
 // c on every rank before it reads.  Reuse across calls follows the two-shot argument.
-__device__ __forceinline__ void publish(const FusedArArgs& a, int phase, uint32_t E) {
+template <typename Args>
+__device__ __forceinline__ void publish(const Args& a, int phase, uint32_t E) {
   __syncthreads();  // every store of this CTA precedes the fences below
   if (threadIdx.x < a.world) {
     __threadfence_system();
@@ -335,7 +336,8 @@ __device__ __forceinline__ void publish(const FusedArArgs& a, int phase, uint32_
   }
 }
 
-__device__ __forceinline__ bool await(const FusedArArgs& a, int phase, uint32_t E, uint64_t budget,
+template <typename Args>
+__device__ __forceinline__ bool await(const Args& a, int phase, uint32_t E, uint64_t budget,
                                       volatile int* give_up) {
   if (threadIdx.x < a.world) {
     const uint32_t* f = a.flags[a.rank] + ((size_t)phase * 8 + threadIdx.x) * FAR_CTAS + blockIdx.x;
@@ -464,6 +466,56 @@ __global__ void __launch_bounds__(THREADS, 4) allreduce_sum_f32_kernel(const Sum
 }
 
 // ---------------------------------------------------------------------------------
+// Plain two-shot fp32 sum (rows above the one-shot capacity): the FAR_PLAIN data flow on
+// fp32 rows without the norm.  Owners sum the W contributions in rank order, so every
+// rank ends with the same bits.
+__global__ void __launch_bounds__(THREADS, 4) allreduce_sum_f32_plain_kernel(const SumArArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int M = a.rows, W = a.world, C4 = a.cols / 4, tid = threadIdx.x, G = gridDim.x;
+  const int per = (M + W - 1) / W;
+  const uint32_t E = read_epoch(a.epoch);
+  const uint64_t budget = limit_ns(a.timeout_ms);
+  __shared__ int give_up;
+  if (tid == 0) give_up = 0;
+  __syncthreads();
+  const float4* src4 = reinterpret_cast<const float4*>(a.data);
+  for (int row = blockIdx.x; row < M; row += G) {
+    const int owner = min(row / per, W - 1);
+    float4* dst = static_cast<float4*>(a.part[owner]) + ((size_t)a.rank * per + (row - owner * per)) * C4;
+    for (int j = tid; j < C4; j += THREADS) dst[j] = src4[(size_t)row * C4 + j];
+  }
+  publish(a, 0, E);
+  if (await(a, 0, E, budget, &give_up)) {
+    for (int row = blockIdx.x; row < M; row += G) {
+      const int owner = min(row / per, W - 1);
+      if (owner != a.rank) continue;
+      const float4* part = static_cast<const float4*>(a.part[a.rank]) + (size_t)(row - owner * per) * C4;
+      for (int j = tid; j < C4; j += THREADS) {
+        float4 acc = __ldcg(part + j);
+        for (int q = 1; q < W; ++q) {
+          const float4 v = __ldcg(part + (size_t)q * per * C4 + j);
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
+        for (int q = 0; q < W; ++q) (static_cast<float4*>(a.out[q]) + (size_t)row * C4)[j] = acc;
+      }
+    }
+  }
+  publish(a, 1, E);
+  if (await(a, 1, E, budget, &give_up)) {
+    float4* dst4 = reinterpret_cast<float4*>(a.data);
+    for (int row = blockIdx.x; row < M; row += G) {
+      const float4* res = static_cast<const float4*>(a.out[a.rank]) + (size_t)row * C4;
+      for (int j = tid; j < C4; j += THREADS) dst4[(size_t)row * C4 + j] = __ldcg(res + j);
+    }
+  }
+  finish_call(a.grid_counter, a.epoch, E);
+}
+
+// ---------------------------------------------------------------------------------
 // Global argmax: one warp per row reduces the row's tile keys, rebases the id to the
 // global vocabulary, and lane 0 pushes the key as one LL line to every rank's slot
 // [parity][rank][row]; then the warp waits for the W lines of the row and max-reduces.
@@ -562,6 +614,14 @@ extern "C" int zs_allreduce_argmax(const ArgmaxArArgs* args, cudaStream_t stream
 extern "C" int zs_allreduce_sum_f32(const SumArArgs* args, cudaStream_t stream) {
   using namespace zs::coll;
   const SumArArgs& a = *args;
+  if (a.plain) {
+    if (a.world < 1 || a.world > 8 || a.rows < 0 || a.cols <= 0 || (a.cols & 3)) return -1;
+    for (int r = 0; r < a.world; ++r)
+      if (a.part[r] == nullptr || a.out[r] == nullptr || a.flags[r] == nullptr) return -1;
+    if (a.rows == 0) return 0;
+    const cudaError_t e = zs_launch(allreduce_sum_f32_plain_kernel, FAR_CTAS, THREADS, 0, stream, a);
+    return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? 0 : -2;
+  }
   if (a.world < 1 || a.world > 8 || a.rows < 0 || a.rows > a.max_rows || a.cols <= 0 || (a.cols & 1)) return -1;
   for (int r = 0; r < a.world; ++r)
     if (a.buf[r] == nullptr) return -1;

@@ -314,6 +314,13 @@ typedef struct SumArArgs {
   uint32_t* grid_counter;
   int* err;
   unsigned int timeout_ms;
+  // Plain two-shot (rows above the one-shot capacity; set plain = 1): fp32 rows through
+  // part [world][ceil(rows/world)][cols] and out [rows][cols] per rank, with per-(source,
+  // CTA) release/acquire flags [2][8][FAR_CTAS] (the FAR_PLAIN scheme).
+  int plain;
+  void* part[8];
+  void* out[8];
+  uint32_t* flags[8];
 } SumArArgs;
 
 #define SUM_CTAS 148  // grid of zs_allreduce_sum_f32

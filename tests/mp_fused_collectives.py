@@ -183,9 +183,9 @@ def check_graph_replay(coll, rank, world, dev):
 
 def check_allreduce_sum(coll, rank, world, dev):
     """fp32 in-place sum: the one-shot kernel (<= sum_rows rows, repeated and under graph
-    replay) and the NCCL path above, against the rank-ordered fp32 sum."""
+    replay) and the plain two-shot above, against the rank-ordered fp32 sum."""
     H = coll.hidden
-    for rows in (1, 3, coll.sum_rows, coll.sum_rows + 5):
+    for rows in (1, 3, coll.sum_rows, coll.sum_rows + 5, min(coll.max_rows, 96)):  # > sum_rows: plain two-shot
         g = torch.Generator(device=dev).manual_seed(400 + rows)
         allx = [torch.randn(rows, H, generator=g, device=dev) for _ in range(world)]
         for _ in range(3):

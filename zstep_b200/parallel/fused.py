@@ -47,7 +47,7 @@ FAR_CTAS = 128          # csrc/kernels/zs_kernels.h
 FAR_ONESHOT_ROWS = 64   # csrc/kernels/zs_kernels.h
 ONESHOT, TWOSHOT, PLAIN = 0, 1, 2
 # Epoch / completion-counter slots, one per kernel family.
-_E_ONE, _E_TWO, _E_PLAIN, _E_ARGMAX, _E_SUM = range(5)
+_E_ONE, _E_TWO, _E_PLAIN, _E_ARGMAX, _E_SUM, _E_SUMP = range(6)
 
 
 class FusedCollectives:
@@ -63,8 +63,8 @@ class FusedCollectives:
         self.hidden = 0
         self._base = 0
         self._peers: list[int] = []
-        self.epoch = torch.zeros(5, dtype=torch.int32, device=self.device)
-        self.grid = torch.zeros(5, dtype=torch.int32, device=self.device)
+        self.epoch = torch.zeros(6, dtype=torch.int32, device=self.device)
+        self.grid = torch.zeros(6, dtype=torch.int32, device=self.device)
         self.sum_rows = sum_rows
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         cfg = runtime_config()
@@ -104,6 +104,13 @@ class FusedCollectives:
         off += _up(R * H * 2)
         self.off_sum = off
         off += _up(2 * W * self.sum_rows * H * 8)
+        # Plain two-shot fp32 sum (rows above sum_rows): its own flags, fp32 part and out.
+        self.off_sum_flags = off
+        off += _up(2 * 8 * FAR_CTAS * 4)
+        self.off_sum_part = off
+        off += _up((R + W) * H * 4)
+        self.off_sum_out = off
+        off += _up(R * H * 4)
         self.nbytes = off
         with torch.cuda.device(self.device):
             self._base = self.C.symm_alloc(self.nbytes)
@@ -121,6 +128,8 @@ class FusedCollectives:
         self.ll_part_ptrs, self.ll_out_ptrs = at(self.off_ll_part), at(self.off_ll_out)
         self.plain_part_ptrs, self.plain_out_ptrs = at(self.off_plain_part), at(self.off_plain_out)
         self.sum_ptrs = at(self.off_sum)
+        self.sum_flag_ptrs = at(self.off_sum_flags)
+        self.sum_part_ptrs, self.sum_out_ptrs = at(self.off_sum_part), at(self.off_sum_out)
 
     def close(self) -> None:
         if not self._base:
@@ -184,12 +193,18 @@ class FusedCollectives:
 
     def allreduce_sum(self, t: torch.Tensor) -> None:
         """In-place fp32 sum over ranks of t [rows, hidden] (mHC sublayer outputs): one-shot
-        LL lines over NVLink up to ``sum_rows`` rows, NCCL above (bandwidth-bound sizes)."""
-        if t.dim() == 2 and t.shape[1] == self.hidden and t.shape[0] <= self.sum_rows and t.dtype == torch.float32 \
-                and t.is_contiguous():
+        LL lines over NVLink up to ``sum_rows`` rows, the plain two-shot above (prefill)."""
+        ok = t.dim() == 2 and t.shape[1] == self.hidden and t.dtype == torch.float32 and t.is_contiguous()
+        if ok and t.shape[0] <= self.sum_rows:
             self.C.allreduce_sum_f32(self.rank, self.world, t, t.shape[0], self.sum_rows, self.sum_ptrs,
                                      self.epoch[_E_SUM:_E_SUM + 1], self.grid[_E_SUM:_E_SUM + 1], self.err,
                                      self.timeout_ms)
+            return
+        if ok and t.shape[0] <= self.max_rows:
+            self.C.allreduce_sum_f32(self.rank, self.world, t, t.shape[0], self.max_rows, self.sum_ptrs,
+                                     self.epoch[_E_SUMP:_E_SUMP + 1], self.grid[_E_SUMP:_E_SUMP + 1], self.err,
+                                     self.timeout_ms, part=self.sum_part_ptrs, out=self.sum_out_ptrs,
+                                     flags=self.sum_flag_ptrs)
             return
         self.nccl.allreduce_sum(t)
 
