@@ -337,7 +337,7 @@ class Qwen35Runner:
 
     # ------------------------------------------------------------------ kernels
     def _gemm(self, w: PackedLinear, xq, xsf, rows: int, out, ldo: int, epi=EPI_BF16, grouped=False,
-              out_sf=None, row_dst=None, row_scale=None, k_splits: int = 1, last_tiles=None, **sampling):
+              out_sf=None, row_dst=None, row_scale=None, k_splits: int = 1, last_tiles=None, bn=None, **sampling):
         b = self.buf
         if grouped:
             bn = self._moe_bn(rows)
@@ -346,7 +346,8 @@ class Qwen35Runner:
                              epi, out, ldo, out_sf, row_dst, row_scale, b["err"], 0, bn, 1, 0, 1, a_fp4=int(w.fp4),
                              last_m0=m0, last_mt=mt)
         else:
-            bn = self._dense_bn(rows, w) if k_splits == 1 else (32 if rows <= 32 else 128)
+            if bn is None:
+                bn = self._dense_bn(rows, w) if k_splits == 1 else (32 if rows <= 32 else 128)
             tiles = -(-rows // bn) * (w.n_pad // 128)
             fs = self._fix_splits(tiles, tiles, w.k // 128, bn) if (k_splits == 1 and self.use_fix_splits) else 1
             self.C.gemm_mxf8(w.q, w.sf, xq, xsf, w.k, w.n_pad, w.n, 1, rows, None, None, None, epi, out, ldo,
@@ -385,18 +386,25 @@ class Qwen35Runner:
         tokens (decode), 128 for prefill-sized batches."""
         return 32 if rows * self.top_k <= 32 * self.cfg.num_experts else 128
 
-    def _k_splits(self, w: PackedLinear, rows: int, cap: int | None = None) -> int:
-        """Split K until the dense GEMM has about one wave of work items (decode only)."""
+    def _split_plan(self, w: PackedLinear, rows: int, cap: int | None = None) -> tuple[int, int]:
+        """(token tile, K splits) of a dense GEMM whose consumer sums f32 split-K partials
+        (decode only): for each tile, split K until about one wave of work items; keep the
+        tile with more items, the 128-token one on a tie (fewer weight re-reads).  Measured
+        on B200: the router (384 x 2048) runs best as 32-token x 4 splits, a 2048 x 4096
+        projection as 128-token x 4 splits."""
         if rows > self.max_seqs:
-            return 1
-        bn = 32 if rows <= 32 else 128  # split-K partials use the 128-token tile (see _gemm)
-        items = ((rows + bn - 1) // bn) * (w.n_pad // 128)
+            return (32 if rows <= 32 else 128), 1
         k_tiles = w.k // 128
-        s = 1
         limit = min(self.max_ksplit, k_tiles, cap or self.max_ksplit)
-        while items * s * 2 <= 160 and s * 2 <= limit:
-            s *= 2
-        return s
+        best = None
+        for bn in ((32,) if rows <= 32 else (128, 32)):
+            items = ((rows + bn - 1) // bn) * (w.n_pad // 128)
+            s = 1
+            while items * s * 2 <= 160 and s * 2 <= limit:
+                s *= 2
+            if best is None or items * s > best[2]:
+                best = (bn, s, items * s)
+        return best[0], best[1]
 
     def _mid(self, width: int) -> torch.Tensor:
         rp = _pad128(self.R)
@@ -430,8 +438,8 @@ class Qwen35Runner:
             self.coll.allreduce_add_rmsnorm(b["delta_f32"], 1, H, 0, b["hidden"] if hidden is None else hidden,
                                             norm_w, self.eps, rows, b["xq"], b["xsf"], protocol=proto, pushed=True)
             return
-        s = self._k_splits(w, rows)
-        self._gemm(w, xq, xsf, rows, self.buf["delta_f32"], H, EPI_F32, k_splits=s)
+        bn, s = self._split_plan(w, rows)
+        self._gemm(w, xq, xsf, rows, self.buf["delta_f32"], H, EPI_F32, k_splits=s, bn=bn)
         self._row_parallel_reduce(self.buf["delta_f32"], rows, s, norm_w, rows * H, H, hidden=hidden)
 
     def _row_parallel_reduce(self, delta_rows: torch.Tensor, rows: int, n_terms: int, norm_w, term_stride: int,
@@ -502,8 +510,8 @@ class Qwen35Runner:
         nr = L["router"].n_pad
         # Router logits: split-K partials summed by the routing kernel (or one term when the
         # GEMM reduces its splits in-kernel).
-        s = 1 if self.use_fix_splits else self._k_splits(L["router"], rows, cap=4)
-        self._gemm(L["router"], b["xq"], b["xsf"], rows, b["logits"], nr, EPI_F32, k_splits=s)
+        bn, s = (None, 1) if self.use_fix_splits else self._split_plan(L["router"], rows, cap=4)
+        self._gemm(L["router"], b["xq"], b["xsf"], rows, b["logits"], nr, EPI_F32, k_splits=s, bn=bn)
         C.moe_route(b["logits"], rows, E, self.top_k, cfg.norm_topk_prob, 0, None, 1, 1, 1.0, E,
                     self.e_begin, self.e_begin + self.e_local, True, b["topk_ids"], b["topk_w"], b["gcount"],
                     b["goff"], b["gpre"], b["pair_slot"], b["row_dst"], b["row_scale"], b["xq"], b["xsf"], b["xg"],
