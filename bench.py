@@ -377,9 +377,9 @@ def engine_path(args, world: int) -> dict:
                             "MASTER_PORT", "TORCHELASTIC_RUN_ID", "ROLE_RANK", "ROLE_WORLD_SIZE")}
         t0 = time.time()
         try:
-            r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
+            r = subprocess.run(cmd, capture_output=True, text=True, timeout=300, env=env)
         except subprocess.TimeoutExpired:
-            return {"error": "zstep run timed out after 600 s"}
+            return {"error": "zstep run timed out after 300 s"}
         wall = time.time() - t0
     if r.returncode != 0:
         return {"error": f"zstep run exited {r.returncode}", "stderr_tail": r.stderr[-600:]}
