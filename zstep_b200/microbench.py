@@ -341,9 +341,10 @@ def _gdn_prefill(a):
 
 
 def cmd_coll(a):
-    """NVLink collective kernels as one rank on one GPU (peers = this GPU): the one-shot
-    cluster all-reduce + RMSNorm + MXFP8 (8 rows), the fp32 sum (64 rows) and the expert
-    all-to-all dispatch + combine (--m tokens, hidden 4096, top-8 of 256).  With --iters 1
+    """NVLink collective kernels as one rank on one GPU (peers = this GPU): the all-reduce +
+    RMSNorm + MXFP8 (one-shot at 8 rows, two-shot LL and plain at 256 rows), the argmax
+    exchange (256 rows x 243 vocab tiles), the fp32 sum (64 rows) and the expert all-to-all
+    dispatch + combine (--m tokens, hidden 4096, top-8 of 256).  With --iters 1
     every kernel launches exactly once (for a profiler capture); otherwise CUDA-event medians."""
     import socket
 
@@ -374,7 +375,20 @@ def cmd_coll(a):
     wt = torch.rand(a.m, 8, device=dev)
     y = torch.randn(ep.recv_cap, 4096, device=dev, dtype=torch.bfloat16)
     out = torch.empty(a.m, 4096, dtype=torch.bfloat16, device=dev)
+    big = 256
+    delta_b = (0.01 * torch.randn(big, H, device=dev)).to(torch.bfloat16)
+    hid_b = torch.zeros(big, H, dtype=torch.bfloat16, device=dev)
+    xq_b = torch.zeros(big, H, dtype=torch.uint8, device=dev)
+    xsf_b = torch.zeros(mx.atoms_bytes(big, H), dtype=torch.uint8, device=dev)
+    keys = torch.randint(0, 2 ** 62, (big, 243), dtype=torch.int64, device=dev)
+    ids_out = torch.zeros(big, dtype=torch.int32, device=dev)
+    vals_out = torch.zeros(big, dtype=torch.float32, device=dev)
+    ar = lambda proto, m: coll.allreduce_add_rmsnorm(delta_b, 1, H, 0, hid_b, w, 1e-6, m, xq_b, xsf_b,  # noqa: E731
+                                                     protocol=proto)
     ops = {"allreduce_norm_small_8rows": lambda: coll.allreduce_add_rmsnorm(delta, 1, H, 0, hid, w, 1e-6, rows, xq, xsf),
+           "allreduce_norm_twoshot_ll_256rows": lambda: ar(1, big),
+           "allreduce_norm_twoshot_plain_256rows": lambda: ar(2, big),
+           "argmax_exchange_256rows": lambda: coll.argmax_allreduce(keys, big, 243, 0, ids_out, vals_out),
            "allreduce_sum_f32_64rows": lambda: coll.allreduce_sum(t),
            "ep_dispatch": lambda: ep.dispatch(x, ids, wt),
            "ep_combine": lambda: ep.combine(y, ids, wt, out)}
