@@ -12,6 +12,17 @@ from zstep_b200.models.weights import RandomWeights
 
 pytestmark = pytest.mark.gpu
 
+TIE_MARGIN = 0.15  # the logit check allows 3e-2 + 3e-2|v| per logit (|v| ~ 1): two logits can swap across 0.15
+
+
+def _same_or_near_tie(got, want, ref_logits):
+    """Greedy tokens must equal the fp32 reference's, except where the reference itself
+    nearly ties: the chosen token must then be within TIE_MARGIN of the reference's best."""
+    for g_tok, w_tok, lg in zip(got, want, ref_logits):
+        if g_tok != w_tok:
+            gap = float(lg[w_tok] - lg[g_tok])
+            assert gap < TIE_MARGIN, f"token {g_tok} != reference {w_tok} with reference margin {gap:.4f}"
+
 
 @pytest.fixture(scope="module")
 def setup():
@@ -51,7 +62,8 @@ def test_prefill_then_decode_matches_reference(setup):
     vals = runner.buf["out_vals"][:3].cpu()
     for s in range(3):
         torch.testing.assert_close(vals[s], ref_logits[s].max().cpu(), rtol=3e-2, atol=3e-2)
-    assert agree >= 2, (first, ref_next)
+    _same_or_near_tie(first, ref_next, ref_logits)
+    del agree
 
     # Decode 4 steps (graph path) feeding the reference's own tokens to both sides.
     toks = ref_next
@@ -60,12 +72,13 @@ def test_prefill_then_decode_matches_reference(setup):
         runner.stage(toks, p_now, list(range(3)))
         out = runner.decode_step(3).cpu().tolist()
         assert runner.check_error() == 0
-        ref_out, ref_l = [], []
+        ref_out, ref_l, ref_lg = [], [], []
         for s in range(3):
             lg = ref.step(states[s], toks[s])
             ref_out.append(int(lg.argmax()))
             ref_l.append(lg.max().item())
+            ref_lg.append(lg)
         vals = runner.buf["out_vals"][:3].cpu()
         torch.testing.assert_close(vals, torch.tensor(ref_l), rtol=3e-2, atol=3e-2)
-        assert sum(int(a == b) for a, b in zip(out, ref_out)) >= 2, (step, out, ref_out)
+        _same_or_near_tie(out, ref_out, ref_lg)
         toks = ref_out
