@@ -799,3 +799,55 @@ def test_moe_route_sigmoid_grouped(C):
                                routed_scale=2.5)
     assert torch.equal(out[0].cpu().long(), ids_ref)
     torch.testing.assert_close(out[1].cpu(), w_ref, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("n,k", [(1, 1), (5, 3), (37, 7)])
+def test_spec_verify_kernel(C, n, k):
+    """On-device greedy verify: accept length, accepted tokens, compacted replay rows and
+    the draft head's catch-up rows against a host restatement."""
+    g = torch.Generator().manual_seed(n * 10 + k)
+    K1 = k + 1
+    R = n * K1
+    targets = torch.randint(0, 50, (R,), generator=g, dtype=torch.int32)
+    ids = torch.randint(0, 50, (R,), generator=g, dtype=torch.int32)
+    # Make sequence i's drafts match the targets for its first i % K1 positions.
+    for i in range(n):
+        m = i % K1
+        for j in range(m):
+            ids[i * K1 + j + 1] = targets[i * K1 + j]
+        if m < k:
+            ids[i * K1 + m + 1] = (targets[i * K1 + m] + 1) % 50
+    pos = torch.arange(R, dtype=torch.int32) + 100
+    slot = torch.tensor([i for i in range(n) for _ in range(K1)], dtype=torch.int32)
+    dev = lambda t: t.cuda()  # noqa: E731
+    i32 = lambda m: torch.full((m,), -7, dtype=torch.int32, device="cuda")  # noqa: E731
+    rec = torch.full((n, k + 2), -7, dtype=torch.int32, device="cuda")
+    rep_start, rep_idx = i32(n + 1), torch.full((R,), -7, dtype=torch.int64, device="cuda")
+    rep_slot, rep_pos = i32(R), i32(R)
+    m_ids, m_pos, m_slot, m_len = i32(R), i32(R), i32(R), i32(R)
+    last = torch.full((n,), -7, dtype=torch.int64, device="cuda")
+    dummy = 999
+    C.spec_verify(n, k, dummy, dev(ids), dev(targets), dev(pos), dev(slot), rec, rep_start, rep_idx, rep_slot,
+                  rep_pos, m_ids, m_pos, m_slot, m_len, last)
+    torch.cuda.synchronize()
+    rec, rep_start, rep_idx = rec.cpu(), rep_start.cpu(), rep_idx.cpu()
+    start = 0
+    for i in range(n):
+        acc = min(i % K1, k) + 1
+        assert int(rec[i, 0]) == acc
+        assert rec[i, 1:1 + acc].tolist() == targets[i * K1:i * K1 + acc].tolist()
+        assert all(int(x) == -1 for x in rec[i, 1 + acc:])
+        assert int(rep_start[i]) == start
+        assert rep_idx[start:start + acc].tolist() == list(range(i * K1, i * K1 + acc))
+        assert rep_slot.cpu()[start:start + acc].tolist() == [i] * acc
+        assert rep_pos.cpu()[start:start + acc].tolist() == pos[i * K1:i * K1 + acc].tolist()
+        for j in range(K1):
+            r = i * K1 + j
+            if j < acc:
+                assert (int(m_ids[r]), int(m_pos[r]), int(m_slot[r]), int(m_len[r])) == \
+                    (int(targets[r]), int(pos[r]), i, int(pos[r]) + 1)
+            else:
+                assert int(m_slot[r]) == dummy
+        assert int(last[i]) == i * K1 + acc - 1
+        start += acc
+    assert int(rep_start[n]) == start
