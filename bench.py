@@ -372,14 +372,17 @@ def engine_path(args, world: int) -> dict:
                "--num-kv-pages", str(max(32768, B * ((P + G + 64 + 15) // 16) + 1)), "--max-step-tokens", "8192",
                "--max-prefill-chunk", "8192", "--no-enable-prefix-caching", "--python", sys.executable,
                "--worker-root", root, "--bench-tiers", f"engine:{B}:{B}:{P}:{G}", "--seed", str(args.seed)]
-        env = {k: v for k, v in os.environ.items()
-               if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "LOCAL_WORLD_SIZE", "GROUP_RANK", "MASTER_ADDR",
-                            "MASTER_PORT", "TORCHELASTIC_RUN_ID", "ROLE_RANK", "ROLE_WORLD_SIZE")}
+        # Drop the launcher's rendezvous variables (torchrun's RANK, MASTER_*, TORCHELASTIC_*,
+        # ...): the master hosts its workers' own process group.
+        launcher = ("RANK", "WORLD_SIZE", "LOCAL_RANK", "LOCAL_WORLD_SIZE", "GROUP_RANK", "GROUP_WORLD_SIZE",
+                    "MASTER_ADDR", "MASTER_PORT", "ROLE_RANK", "ROLE_WORLD_SIZE", "ROLE_NAME")
+        env = {k: v for k, v in os.environ.items() if k not in launcher and not k.startswith("TORCHELASTIC_")}
         t0 = time.time()
         try:
             r = subprocess.run(cmd, capture_output=True, text=True, timeout=300, env=env)
-        except subprocess.TimeoutExpired:
-            return {"error": "zstep run timed out after 300 s"}
+        except subprocess.TimeoutExpired as e:
+            tail = e.stderr.decode(errors="replace") if isinstance(e.stderr, bytes) else (e.stderr or "")
+            return {"error": "zstep run timed out after 300 s", "stderr_tail": tail[-600:]}
         wall = time.time() - t0
     if r.returncode != 0:
         return {"error": f"zstep run exited {r.returncode}", "stderr_tail": r.stderr[-600:]}

@@ -116,6 +116,10 @@ void Coordinator::launch() {
       clear_cloexec(arena_.fd());
       clear_cloexec(plan_efd_[r].fd());
       clear_cloexec(done_efd_[r].fd());
+      // The workers' process group is hosted by their own rank 0.  A master started from
+      // inside a torchrun job inherits TORCHELASTIC_USE_AGENT_STORE=True, which would make
+      // every worker a store client of a server that never starts (a hang at init).
+      unsetenv("TORCHELASTIC_USE_AGENT_STORE");
       for (auto& kv : cfg_.env) setenv(kv.first.c_str(), kv.second.c_str(), 1);
       std::vector<char*> argv;
       for (auto& a : args) argv.push_back(const_cast<char*>(a.c_str()));

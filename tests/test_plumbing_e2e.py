@@ -123,3 +123,22 @@ def test_deepseek_tp2_shm_engine_matches_reference(apc):
             assert eng.stats().prefix_hit_tokens >= 16
     finally:
         coord.shutdown()
+
+
+@pytest.mark.timeout(300)
+def test_tp2_workers_ignore_an_inherited_torchrun_agent_store(monkeypatch):
+    """A master started inside a torchrun job inherits TORCHELASTIC_USE_AGENT_STORE=True.
+    Its workers must still host their own process group (rank 0 runs the store); before
+    the fix every worker became a store client and the group never formed."""
+    monkeypatch.setenv("TORCHELASTIC_USE_AGENT_STORE", "True")
+    ps = prompts(n=2)
+    ref = reference_generate(ps, 4)
+    eng, coord = launch(model="qwen3.5-tiny", world_size=2, device="cpu", max_seqs=2, max_step_tokens=96,
+                        page_size=16, num_pages=64, max_model_len=256, ready_timeout_ms=120000)
+    try:
+        for i, p in enumerate(ps):
+            assert eng.submit(i, p, 4, True)
+        out = run_to_completion(eng)
+        assert [out[i] for i in range(len(ps))] == ref
+    finally:
+        coord.shutdown()

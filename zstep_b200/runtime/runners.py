@@ -67,6 +67,10 @@ def _weights(cfg, name: str, seed: int):
 
 def make_runner(args, rank: int, world: int, geo):
     if world > 1 and not dist.is_initialized():
+        # This group is hosted by worker rank 0 at MASTER_ADDR/MASTER_PORT.  An inherited
+        # TORCHELASTIC_USE_AGENT_STORE=True (a master started under torchrun) would turn
+        # rank 0 into a client of a store that never starts.
+        os.environ.pop("TORCHELASTIC_USE_AGENT_STORE", None)
         backend = "nccl" if args.device == "cuda" else "gloo"
         if args.device == "cuda":
             torch.cuda.set_device(rank % max(1, torch.cuda.device_count()))
