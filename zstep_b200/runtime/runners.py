@@ -31,7 +31,7 @@ from . import wire
 from .runahead import RunAheadGuard, TorchEventBackend
 from ..models import sampling_head
 from ..sampling import sample_logits, verify_greedy
-from ..utils.env import runtime_config
+from ..utils.env import own_process_group_store, runtime_config
 
 
 def _resolve_config(name: str):
@@ -67,10 +67,9 @@ def _weights(cfg, name: str, seed: int):
 
 def make_runner(args, rank: int, world: int, geo):
     if world > 1 and not dist.is_initialized():
-        # This group is hosted by worker rank 0 at MASTER_ADDR/MASTER_PORT.  An inherited
-        # TORCHELASTIC_USE_AGENT_STORE=True (a master started under torchrun) would turn
-        # rank 0 into a client of a store that never starts.
-        os.environ.pop("TORCHELASTIC_USE_AGENT_STORE", None)
+        # This group is hosted by worker rank 0 at MASTER_ADDR/MASTER_PORT, also when the
+        # master itself was started under torchrun.
+        own_process_group_store()
         backend = "nccl" if args.device == "cuda" else "gloo"
         if args.device == "cuda":
             torch.cuda.set_device(rank % max(1, torch.cuda.device_count()))

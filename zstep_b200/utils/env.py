@@ -149,3 +149,12 @@ def dist_env(env: dict | None = None) -> DistEnv:
 
 def python_path() -> str:
     return os.environ.get("PYTHONPATH", "")
+
+
+def own_process_group_store(env: dict | None = None) -> None:
+    """Make this process group host its own rendezvous store (rank 0 serves it).  A process
+    started from inside a torchrun job inherits TORCHELASTIC_USE_AGENT_STORE=True, which
+    tells torch.distributed that the launcher's agent runs the store, so every rank,
+    rank 0 included, would connect as a client to a server that never starts."""
+    env = os.environ if env is None else env
+    env.pop("TORCHELASTIC_USE_AGENT_STORE", None)
