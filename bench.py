@@ -402,7 +402,7 @@ def engine_path(args, world: int) -> dict:
 def count_launches(runner, rows: int) -> int:
     """Number of zstep_b200 kernels one decode step launches (counted on an eager step)."""
     per_call = {"gemm_mxf8": 1, "quant_mxf8": 1, "add_rmsnorm_quant": 1, "embed_rmsnorm_quant": 1,
-                "argmax_reduce": 1, "gdn_decode": 1, "gdn_prefill": 1, "attn_prologue": 1, "attn_decode": 2,
+                "argmax_reduce": 1, "gdn_decode": 1, "gdn_prefill": 2, "attn_prologue": 1, "attn_decode": 2,
                 "moe_route": 3, "fused_allreduce_norm": 1, "allreduce_argmax": 1}
     counts = {"n": 0}
     real = runner.C

@@ -608,6 +608,428 @@ decode_partial_tc_kernel(const AttnArgs a) {
   if (warp == 0) tmem_dealloc(tmem, 64);
 }
 
+// ---------------------------------------------------------------------------------
+// Tensor-core attention over query rows grouped by sequence (varlen prefill, speculative
+// verify: seq_start given).  A work item is (query rows, kv head, split): up to NS / G
+// consecutive rows of one sequence (NS = 32 query slots = row x head of the GQA group:
+// 4 rows at G = 8, 16 at G = 2), so every K/V tile it loads serves all of them instead of
+// one row, each slot masked by its own causal length.  Per 128-key tile the steps are
+// those of the decode kernel above (page-image bulk copies, S^T = K Q^T with N = NS,
+// online softmax with the TMEM rescale, O^T += V^T P^T), with these differences:
+//   * each CTA walks items idx = blockIdx.x + j * gridDim.x and its copies run ahead over
+//     its whole tile stream (K one tile, V two tiles), across item boundaries;
+//   * a tile's page ids are read together, then its page copies issued back to back;
+//   * the item list is built in the CTA from seq_start: a scan of each sequence's row
+//     chunks into shared memory, then a binary search per item.
+// Records (o, m, l) per (row, head, split) feed the same combine kernel.
+constexpr int TC_NMR = 32;         // query slots of a work item
+constexpr int TC_MAX_SEQS = 1024;  // sequences whose chunk prefix fits in shared memory
+
+template <int NS>
+struct TcRowsSmem {
+  uint8_t k[TC_TILE_BYTES];           // K tile image (reloaded as soon as S is computed)
+  uint8_t v[2][TC_TILE_BYTES];        // double-buffered V tile images (prefetched two tiles ahead)
+  uint8_t q[TC_NCHUNK][NS * 128];     // Q: [NS slots][256] K-major, unused slots are zero
+  uint8_t p[2][NS * 128];             // P: [NS slots][128 keys] K-major, 2 chunks of 64 keys
+  float red_max[4][NS];
+  float red_sum[4][NS];
+  float m[NS], l[NS], r[NS];
+  int len[NS];                        // causal length of each slot's row (0: unused slot)
+  int cpre[TC_MAX_SEQS + 1];          // items (row chunks) before each sequence
+  int tsum[TC_THREADS + 1];
+  uint64_t kfull, vfull[2], mma1, mma2;
+  uint32_t tmem_base;
+};
+
+// One work item: query rows [r0, r0 + nr) of one sequence, a kv head and a split, whose
+// keys are the pages [p0, p1) (the split's share of the longest row's context).
+struct TcItem {
+  int r0, nr, kvh, split, p0, p1, ntiles, tok_end;
+  const int* pt;
+};
+
+// rpi = query rows per item; cpre = row-chunk prefix over the sequences.
+__device__ __forceinline__ bool tc_item(const AttnArgs& a, int idx, int rpi, const int* cpre, TcItem& it) {
+  if (idx >= cpre[a.num_seqs] * a.num_kv_heads * a.num_splits) return false;
+  it.split = idx % a.num_splits;
+  const int rk = idx / a.num_splits;
+  it.kvh = rk % a.num_kv_heads;
+  const int chunk = rk / a.num_kv_heads;
+  int lo = 0, hi = a.num_seqs;  // largest sequence with cpre[seq] <= chunk
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (cpre[mid] <= chunk) lo = mid; else hi = mid;
+  }
+  it.r0 = a.seq_start[lo] + (chunk - cpre[lo]) * rpi;
+  it.nr = min(rpi, a.seq_start[lo + 1] - it.r0);
+  int ctx = 0;
+  for (int i = 0; i < it.nr; ++i) ctx = max(ctx, a.seq_lens[it.r0 + i]);
+  const int pages = (ctx + PAGE - 1) / PAGE;
+  const int pps = (pages + a.num_splits - 1) / a.num_splits;
+  it.p0 = it.split * pps;
+  it.p1 = min(pages, it.p0 + pps);
+  it.ntiles = (max(0, it.p1 - it.p0) + TC_PAGES - 1) / TC_PAGES;
+  it.tok_end = min(ctx, it.p1 * PAGE);
+  it.pt = a.page_table + (size_t)a.slots[it.r0] * a.max_pages;
+  return true;
+}
+
+// Copy-side position in the CTA's tile stream (thread 0 only): item j, tile t.
+struct TcCursor {
+  int j, t;
+  bool valid;
+  TcItem it;
+};
+
+__device__ __forceinline__ void tc_settle(const AttnArgs& a, int rpi, const int* cpre, TcCursor& c) {
+  while (c.valid && c.t >= c.it.ntiles) {  // skip items without keys
+    ++c.j;
+    c.t = 0;
+    c.valid = tc_item(a, blockIdx.x + c.j * gridDim.x, rpi, cpre, c.it);
+  }
+}
+
+__device__ __forceinline__ void tc_start(const AttnArgs& a, int rpi, const int* cpre, TcCursor& c) {
+  c.j = 0;
+  c.t = 0;
+  c.valid = tc_item(a, blockIdx.x, rpi, cpre, c.it);
+  tc_settle(a, rpi, cpre, c);
+}
+
+__device__ __forceinline__ void tc_advance(const AttnArgs& a, int rpi, const int* cpre, TcCursor& c) {
+  ++c.t;
+  tc_settle(a, rpi, cpre, c);
+}
+
+__device__ __forceinline__ size_t tc_rec(const AttnArgs& a, int row, int head, int split) {
+  return (((size_t)row * a.num_q_heads + head) * a.num_splits + split) * PREC;
+}
+
+// Empty records (m = -inf, l = 0) for the slots of an item: the combine kernel skips them.
+__device__ __forceinline__ void tc_empty_record(const AttnArgs& a, const TcItem& it, int G, int tid) {
+  if (tid < it.nr * G) {
+    float* rec = a.partial + tc_rec(a, it.r0 + tid / G, it.kvh * G + tid % G, it.split);
+    rec[D] = -INFINITY;
+    rec[D + 1] = 0.f;
+  }
+}
+
+template <int NS>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+rows_partial_tc_kernel(const AttnArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
+  extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
+  using Smem = TcRowsSmem<NS>;
+  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = a.num_q_heads / a.num_kv_heads;
+  const float qscale = a.sm_scale * 1.4426950408889634f;  // exp2 domain
+  constexpr uint32_t tmem_cols = NS <= 16 ? 64 : 128;
+  const int rpi = NS / G;
+  const int* cpre = s.cpre;
+
+  if (warp == 0) {
+    tmem_alloc(&s.tmem_base, tmem_cols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&s.kfull, 1);
+    mbar_init(&s.vfull[0], 1);
+    mbar_init(&s.vfull[1], 1);
+    mbar_init(&s.mma1, 1);
+    mbar_init(&s.mma2, 1);
+    fence_barrier_init();
+  }
+  {
+    // Items before each sequence: thread t counts the row chunks of a contiguous block of
+    // sequences, the block sums are scanned, and each thread writes its block's prefix.
+    const int per = (a.num_seqs + TC_THREADS - 1) / TC_THREADS;
+    const int s0 = min(a.num_seqs, tid * per), s1 = min(a.num_seqs, s0 + per);
+    int sum = 0;
+    for (int q = s0; q < s1; ++q) sum += (a.seq_start[q + 1] - a.seq_start[q] + rpi - 1) / rpi;
+    s.tsum[tid] = sum;
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0;
+      for (int i = 0; i < TC_THREADS; ++i) {
+        const int v = s.tsum[i];
+        s.tsum[i] = acc;
+        acc += v;
+      }
+      s.tsum[TC_THREADS] = acc;
+      s.cpre[a.num_seqs] = acc;
+    }
+    __syncthreads();
+    int acc = s.tsum[tid];
+    for (int q = s0; q < s1; ++q) {
+      s.cpre[q] = acc;
+      acc += (a.seq_start[q + 1] - a.seq_start[q] + rpi - 1) / rpi;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const uint32_t t_s = tmem, t_o = tmem + NS;
+
+  // Copy state (thread 0 only): cursors over the tile stream (K one tile ahead of the
+  // consumer, V two) and the copies issued but not yet observed, per barrier.
+  TcCursor kcur, vcur;
+  int k_pend = 0, v_pend[2] = {0, 0};
+  int k_uses = 0, v_uses[2] = {0, 0};
+  const __nv_bfloat16* kc = static_cast<const __nv_bfloat16*>(a.k_cache);
+  const __nv_bfloat16* vc = static_cast<const __nv_bfloat16*>(a.v_cache);
+  auto issue = [&](const __nv_bfloat16* cache, uint8_t* dst, uint64_t* bar, const TcCursor& c) {
+    const int pg0 = c.it.p0 + c.t * TC_PAGES;
+    const int n = min(TC_PAGES, c.it.p1 - pg0);
+    int page[TC_PAGES];
+#pragma unroll
+    for (int j = 0; j < TC_PAGES; ++j) page[j] = j < n ? __ldg(c.it.pt + pg0 + j) : 0;
+    mbar_expect_tx(bar, n * BLOCK_BYTES);
+#pragma unroll
+    for (int j = 0; j < TC_PAGES; ++j)
+      if (j < n) bulk_load(dst + j * BLOCK_BYTES, cache + kv_offset(a, page[j], c.it.kvh), BLOCK_BYTES, bar);
+  };
+  if (tid == 0) {
+    tc_start(a, rpi, cpre, kcur);
+    if (kcur.valid) {
+      issue(kc, s.k, &s.kfull, kcur);
+      k_pend = 1;
+      tc_advance(a, rpi, cpre, kcur);
+    }
+    tc_start(a, rpi, cpre, vcur);
+    for (int b = 0; b < 2 && vcur.valid; ++b) {
+      issue(vc, s.v[b], &s.vfull[b], vcur);
+      v_pend[b] = 1;
+      tc_advance(a, rpi, cpre, vcur);
+    }
+  }
+
+  bool ok = true;
+  int f = 0;  // position in the tile stream: barrier phases and the V buffer
+  int j = 0;
+  TcItem it;
+  for (; tc_item(a, blockIdx.x + j * gridDim.x, rpi, cpre, it); ++j) {
+    // ---- item start: running max / sum, each slot's causal length and the Q slots
+    // (slot = row * G + head; unused slots stay zero).  The previous item's products and
+    // record reads are done.
+    const int nslots = it.nr * G;
+    if (tid < NS) {
+      s.m[tid] = -INFINITY;
+      s.l[tid] = 0.f;
+      s.len[tid] = tid < nslots ? a.seq_lens[it.r0 + tid / G] : 0;
+    }
+    for (int i = tid; i < NS * 32; i += TC_THREADS) {
+      const int h = i >> 5, pc = i & 31, c = pc >> 3, piece = pc & 7;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (h < nslots) {
+        const __nv_bfloat16* qrow = static_cast<const __nv_bfloat16*>(a.q_out) +
+                                    ((size_t)(it.r0 + h / G) * a.num_q_heads + it.kvh * G + h % G) * D;
+        v = *reinterpret_cast<const uint4*>(qrow + pc * 8);
+      }
+      *reinterpret_cast<uint4*>(s.q[c] + h * 128 + ((piece ^ (h & 7)) << 4)) = v;
+    }
+    fence_proxy_async_shared();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+
+    for (int t = 0; t < it.ntiles; ++t, ++f) {
+      const int vb = f & 1;
+      const int pg0 = it.p0 + t * TC_PAGES;
+      const int n = min(TC_PAGES, it.p1 - pg0);
+      if (n < TC_PAGES) {
+        // Last, partial tile: zero the absent pages in both images (no copy targets them),
+        // so the products see finite values there.
+        for (int i = n * (BLOCK_BYTES / 16) + tid; i < TC_PAGES * (BLOCK_BYTES / 16); i += TC_THREADS) {
+          reinterpret_cast<uint4*>(s.k)[i] = make_uint4(0, 0, 0, 0);
+          reinterpret_cast<uint4*>(s.v[vb])[i] = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_shared();
+      }
+      ok = mbar_wait(&s.kfull, (uint32_t)(k_uses & 1), a.err);
+      if (!__syncthreads_and(ok)) break;
+      if (tid == 0) {
+        k_pend = 0;
+        tc_fence_after();
+        const uint32_t idesc = make_idesc_bf16(TC_KEYS, NS, 0, 0);
+#pragma unroll
+        for (int c = 0; c < TC_NCHUNK; ++c)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = make_smem_desc(smem_u32(s.k + c * 1024) + k * 32, 16, 4096, 2);
+            const uint64_t bd = make_smem_desc(smem_u32(s.q[c]) + k * 32, 16, 1024, 2);
+            mma_bf16(t_s, ad, bd, idesc, (c | k) ? 1u : 0u);
+          }
+        tc_commit(&s.mma1);
+      }
+      ++k_uses;
+      ok = mbar_wait(&s.mma1, (uint32_t)(f & 1), a.err);
+      if (!__syncthreads_and(ok)) break;
+      tc_fence_after();
+      // S is in TMEM: the K image is free, so the next tile's K copy (possibly the next
+      // item's first) overlaps the rest of this tile.
+      if (tid == 0 && kcur.valid) {
+        issue(kc, s.k, &s.kfull, kcur);
+        k_pend = 1;
+        tc_advance(a, rpi, cpre, kcur);
+      }
+      // ---- online softmax: thread tid owns key tid of the tile
+      uint32_t sr[NS];
+#pragma unroll
+      for (int c0 = 0; c0 < NS; c0 += 16) {
+        uint32_t part[16];
+        tmem_ld_32x32b_x16(t_s + c0 + lane_off, part);
+#pragma unroll
+        for (int h = 0; h < 16; ++h) sr[c0 + h] = part[h];
+      }
+      tmem_ld_wait();
+      // Key tok counts for slot h when it lies in this split's pages (tok_end) and inside
+      // the slot's causal length.
+      const int tok = pg0 * PAGE + tid;
+      const bool in_split = tok < it.tok_end;
+      float sv[NS];
+#pragma unroll
+      for (int h = 0; h < NS; ++h)
+        sv[h] = (in_split && tok < s.len[h]) ? __uint_as_float(sr[h]) * qscale : -INFINITY;
+#pragma unroll
+      for (int h = 0; h < NS; ++h) {
+        const float v = warp_max(sv[h]);
+        if (lane == 0) s.red_max[warp][h] = v;
+      }
+      __syncthreads();
+      float mnew[NS];
+#pragma unroll
+      for (int h = 0; h < NS; ++h)
+        mnew[h] = fmaxf(fmaxf(s.m[h], fmaxf(s.red_max[0][h], s.red_max[1][h])), fmaxf(s.red_max[2][h], s.red_max[3][h]));
+      {
+        const int chunk = tid >> 6, within = tid & 63, piece = within >> 3, sub = (within & 7) * 2;
+#pragma unroll
+        for (int h = 0; h < NS; ++h) {
+          const float pv = sv[h] == -INFINITY ? 0.f : exp2f(sv[h] - mnew[h]);
+          const __nv_bfloat16 pb = __float2bfloat16_rn(pv);
+          *reinterpret_cast<__nv_bfloat16*>(s.p[chunk] + h * 128 + ((piece ^ (h & 7)) << 4) + sub) = pb;
+          const float sum = warp_sum(__bfloat162float(pb));
+          if (lane == 0) s.red_sum[warp][h] = sum;
+        }
+      }
+      fence_proxy_async_shared();
+      __syncthreads();
+      if (tid < NS) {
+        const int h = tid;
+        const float mo = s.m[h];
+        const float rr = mo == -INFINITY ? 0.f : exp2f(mo - mnew[h]);
+        s.l[h] = s.l[h] * rr + (s.red_sum[0][h] + s.red_sum[1][h] + s.red_sum[2][h] + s.red_sum[3][h]);
+        s.m[h] = mnew[h];
+        s.r[h] = rr;
+      }
+      __syncthreads();
+      if (t > 0) {  // rescale the running O^T (TMEM lane = head dim, column = query slot)
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int c0 = 0; c0 < NS; c0 += 16) {
+            uint32_t o[16];
+            tmem_ld_32x32b_x16(t_o + mt * NS + c0 + lane_off, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int h = 0; h < 16; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * s.r[c0 + h]);
+            tmem_st_32x32b_x16(t_o + mt * NS + c0 + lane_off, o);
+          }
+        tmem_st_wait();
+      }
+      ok = mbar_wait(&s.vfull[vb], (uint32_t)(v_uses[vb] & 1), a.err);
+      if (ok && !in_split && tok < (pg0 + n) * PAGE) {
+        // Cache rows past the context inside a loaded page: zero them (P is 0 there).
+        const int r = tid & 15;
+        uint8_t* blk = s.v[vb] + (tid >> 4) * BLOCK_BYTES + (r >> 3) * 4096 + (r & 7) * 128;
+#pragma unroll
+        for (int c = 0; c < TC_NCHUNK; ++c) {
+          uint4* rowp = reinterpret_cast<uint4*>(blk + c * 1024);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) rowp[q] = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_shared();
+      }
+      tc_fence_before();
+      if (!__syncthreads_and(ok)) break;
+      if (tid == 0) {
+        v_pend[vb] = 0;
+        tc_fence_after();
+        const uint32_t idesc2 = make_idesc_bf16(128, NS, 1, 0);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint64_t ad = make_smem_desc(smem_u32(s.v[vb] + 2 * mt * 1024) + ks * BLOCK_BYTES, 1024, 4096, 2);
+            const uint64_t bd = make_smem_desc(smem_u32(s.p[ks >> 2]) + (ks & 3) * 32, 16, 1024, 2);
+            mma_bf16(t_o + mt * NS, ad, bd, idesc2, (t > 0 || ks > 0) ? 1u : 0u);
+          }
+        tc_commit(&s.mma2);
+      }
+      ++v_uses[vb];
+      ok = mbar_wait(&s.mma2, (uint32_t)(f & 1), a.err);
+      if (!__syncthreads_and(ok)) break;
+      tc_fence_after();
+      if (tid == 0 && vcur.valid) {  // this V image is free: the tile two ahead in the stream
+        issue(vc, s.v[vb], &s.vfull[vb], vcur);
+        v_pend[vb] = 1;
+        tc_advance(a, rpi, cpre, vcur);
+      }
+    }
+    if (!ok) break;
+    // ---- item end: the record (o, m, l) of every used slot
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int c0 = 0; c0 < NS; c0 += 16) {
+        if (c0 >= nslots) break;
+        uint32_t o[16];
+        if (it.ntiles > 0) {
+          tmem_ld_32x32b_x16(t_o + mt * NS + c0 + lane_off, o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int h = 0; h < 16; ++h) o[h] = 0u;
+        }
+        const int dim = mt * 128 + tid;
+#pragma unroll
+        for (int h = 0; h < 16; ++h) {
+          const int sl = c0 + h;
+          if (sl >= nslots) break;
+          a.partial[tc_rec(a, it.r0 + sl / G, it.kvh * G + sl % G, it.split) + dim] = __uint_as_float(o[h]);
+        }
+      }
+    if (tid < nslots) {
+      float* rec = a.partial + tc_rec(a, it.r0 + tid / G, it.kvh * G + tid % G, it.split);
+      rec[D] = s.m[tid];
+      rec[D + 1] = s.l[tid];
+    }
+    // The next item's products overwrite S and O, and its set-up rewrites m / l / len.
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  }
+  if (!ok) {
+    // Abort (the error word is set): still write empty records (m = -inf, l = 0) for this
+    // item and every later one of this CTA, so the combine kernel skips them instead of
+    // reading whatever an earlier call left in the scratch buffer.
+    for (; tc_item(a, blockIdx.x + j * gridDim.x, rpi, cpre, it); ++j) tc_empty_record(a, it, G, tid);
+    // Let every copy still in flight land before the CTA releases shared memory.
+    if (tid == 0) {
+      if (k_pend) mbar_wait(&s.kfull, (uint32_t)(k_uses & 1), nullptr);
+      for (int b = 0; b < 2; ++b)
+        if (v_pend[b]) mbar_wait(&s.vfull[b], (uint32_t)(v_uses[b] & 1), nullptr);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, tmem_cols);
+}
+
 // One CTA (256 threads, thread = dim) per (row, q head): merge splits, normalise,
 // apply sigmoid(gate), write bf16 and/or MXFP8.
 __global__ void decode_combine_kernel(const AttnArgs a) {
@@ -660,12 +1082,25 @@ extern "C" int zs_attn_decode(const AttnArgs* args, cudaStream_t stream) {
   if (a.num_splits < 1 || a.partial == nullptr || a.page_size != zs::attn::PAGE) return -1;
   if (a.rows == 0) return 0;
   dim3 g1(a.rows, a.num_kv_heads, a.num_splits);
-  // Tensor cores pay off from 4 query heads per kv head; smaller groups (a GQA group
-  // split over many ranks) stay on the SIMT kernel, which runs one warp per head.
-  if (a.impl == 0 && group >= 4 && group <= zs::attn::TC_N) {
-    const size_t smem = sizeof(zs::attn::TcSmem) + 1024;
-    cudaFuncSetAttribute(zs::attn::decode_partial_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    zs_launch(zs::attn::decode_partial_tc_kernel, g1, zs::attn::TC_THREADS, smem, stream, a);
+  // impl 0 picks: tensor cores from 4 query heads per kv head; smaller groups (a GQA group
+  // split over many ranks) stay on the SIMT kernel, which runs one warp per head.  impl 1
+  // forces the SIMT kernel, impl 2 the tensor-core kernels for any group up to 16.
+  const bool tc = (a.impl == 0 && group >= 4 && group <= zs::attn::TC_N) || (a.impl == 2 && group <= zs::attn::TC_N);
+  if (tc) {
+    if (a.seq_start != nullptr && a.num_seqs > 0 && a.num_seqs <= zs::attn::TC_MAX_SEQS) {
+      // Rows grouped by sequence: multi-row items of 32 query slots, one CTA per item
+      // (the item count is bounded above: every sequence adds at most one partial chunk).
+      const int rpi = zs::attn::TC_NMR / group;
+      const long long items = ((long long)a.rows / rpi + a.num_seqs) * a.num_kv_heads * a.num_splits;
+      const size_t smem = sizeof(zs::attn::TcRowsSmem<zs::attn::TC_NMR>) + 1024;
+      auto kern = zs::attn::rows_partial_tc_kernel<zs::attn::TC_NMR>;
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      zs_launch(kern, (int)items, zs::attn::TC_THREADS, smem, stream, a);
+    } else {
+      const size_t smem = sizeof(zs::attn::TcSmem) + 1024;
+      cudaFuncSetAttribute(zs::attn::decode_partial_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      zs_launch(zs::attn::decode_partial_tc_kernel, g1, zs::attn::TC_THREADS, smem, stream, a);
+    }
     dim3 g2(a.rows, a.num_q_heads);
     zs_launch(zs::attn::decode_combine_kernel, g2, zs::attn::D, 0, stream, a);
     return cudaGetLastError() == cudaSuccess ? 0 : -2;

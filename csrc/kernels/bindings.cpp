@@ -187,7 +187,7 @@ void gdn(bool prefill, const Tensor& proj, int64_t num_k_heads, int64_t num_v_he
          const Tensor& slots, const Tensor& positions, int64_t rows, const OptT& out_bf16,
          const OptT& out_q, const OptT& out_sf, const OptT& seq_start, int64_t num_seqs,
          const OptT& ckpt_rows, const OptT& ckpt_slots, int64_t max_ckpt, const OptT& err,
-         const OptT& out_slots = std::nullopt, int64_t impl = 0) {
+         const OptT& out_slots = std::nullopt, int64_t impl = 0, int64_t max_seq_rows = 0) {
   check_cuda(proj, "proj");
   check_cuda(ssm_state, "ssm_state");
   check_cuda(conv_state, "conv_state");
@@ -222,6 +222,7 @@ void gdn(bool prefill, const Tensor& proj, int64_t num_k_heads, int64_t num_v_he
   g.err = optptr<int>(err);
   g.out_slots = optptr<const int>(out_slots);
   g.impl = (int)impl;
+  g.max_seq_rows = (int)max_seq_rows;
   rc(prefill ? zs_gdn_prefill(&g, stream()) : zs_gdn_decode(&g, stream()), "zs_gdn");
 }
 
@@ -277,9 +278,11 @@ void attn_decode(const Tensor& q_out, const Tensor& gate_out, int64_t num_q_head
                  int64_t page_size, const Tensor& page_table, const Tensor& slots,
                  const Tensor& seq_lens, int64_t rows, const Tensor& partial, int64_t num_splits,
                  double sm_scale, const OptT& out_bf16, const OptT& out_q, const OptT& out_sf, int64_t impl,
-                 const OptT& err) {
+                 const OptT& err, const OptT& seq_start, int64_t num_seqs) {
   check_cuda(q_out, "q_out");
   check_cuda(partial, "partial");
+  TORCH_CHECK(!seq_start.has_value() || (num_seqs >= 0 && seq_start->numel() > num_seqs),
+              "seq_start must hold num_seqs + 1 row offsets");
   TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(2) == page_size, "k_cache must be [pages, kv_heads, page, 256]");
   TORCH_CHECK(partial.numel() >= rows * num_q_heads * num_splits * 260, "partial too small");
   AttnArgs a{};
@@ -304,6 +307,8 @@ void attn_decode(const Tensor& q_out, const Tensor& gate_out, int64_t num_q_head
   a.out_sf = optptr<uint8_t>(out_sf);
   a.impl = (int)impl;
   a.err = optptr<int>(err);
+  a.seq_start = optptr<const int>(seq_start);
+  a.num_seqs = seq_start.has_value() ? (int)num_seqs : 0;
   rc(zs_attn_decode(&a, stream()), "zs_attn_decode");
 }
 
@@ -928,21 +933,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                           const OptT& out_bf16, const OptT& out_q, const OptT& out_sf,
                           const Tensor& seq_start, int64_t num_seqs, const OptT& ckpt_rows,
                           const OptT& ckpt_slots, int64_t max_ckpt, const OptT& err, const OptT& out_slots,
-                          int64_t impl) {
+                          int64_t impl, int64_t max_seq_rows) {
     gdn(true, proj, hk, hv, conv_w, conv_state, ssm_state, a_log, dt_bias, norm_w, eps, slots,
         positions, rows, out_bf16, out_q, out_sf, seq_start, num_seqs, ckpt_rows, ckpt_slots,
-        max_ckpt, err, out_slots, impl);
+        max_ckpt, err, out_slots, impl, max_seq_rows);
   }, py::arg("proj"), py::arg("hk"), py::arg("hv"), py::arg("conv_w"), py::arg("conv_state"), py::arg("ssm_state"),
      py::arg("a_log"), py::arg("dt_bias"), py::arg("norm_w"), py::arg("eps"), py::arg("slots"), py::arg("positions"),
      py::arg("rows"), py::arg("out_bf16"), py::arg("out_q"), py::arg("out_sf"), py::arg("seq_start"),
      py::arg("num_seqs"), py::arg("ckpt_rows"), py::arg("ckpt_slots"), py::arg("max_ckpt"), py::arg("err"),
-     py::arg("out_slots") = py::none(), py::arg("impl") = 0);
+     py::arg("out_slots") = py::none(), py::arg("impl") = 0, py::arg("max_seq_rows") = 0);
   m.def("attn_prologue", &attn_prologue);
   m.def("attn_decode", &attn_decode, py::arg("q_out"), py::arg("gate_out"), py::arg("num_q_heads"),
         py::arg("num_kv_heads"), py::arg("k_cache"), py::arg("v_cache"), py::arg("page_size"), py::arg("page_table"),
         py::arg("slots"), py::arg("seq_lens"), py::arg("rows"), py::arg("partial"), py::arg("num_splits"),
         py::arg("sm_scale"), py::arg("out_bf16"), py::arg("out_q"), py::arg("out_sf"), py::arg("impl") = 0,
-        py::arg("err") = py::none());
+        py::arg("err") = py::none(), py::arg("seq_start") = py::none(), py::arg("num_seqs") = 0);
   m.def("moe_route", &moe_route, py::arg("logits"), py::arg("rows"), py::arg("num_experts"), py::arg("top_k"),
         py::arg("norm_topk"), py::arg("scoring"), py::arg("bias"), py::arg("n_group"), py::arg("topk_group"),
         py::arg("routed_scale"), py::arg("shared_gate_col"), py::arg("expert_begin"), py::arg("expert_end"),

@@ -260,7 +260,9 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_kernel(const GdnArgs a
 #pragma unroll
   for (int i = 0; i < 8; ++i)
     reinterpret_cast<float4*>(op)[i] = make_float4(st[4 * i], st[4 * i + 1], st[4 * i + 2], st[4 * i + 3]);
-  store_window(a, oslot, pos0 + (r1 - r0), kh, vh, s, (vh % ratio) == 0);
+  // The q/k windows are shared by the value heads of a q/k group and written afterwards by
+  // gdn_qk_window_kernel; this CTA stores its own v window only.
+  store_window(a, oslot, pos0 + (r1 - r0), kh, vh, s, false);
 }
 
 // ------------------------------------------------------------------------------------
@@ -386,8 +388,8 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_chunk_kernel(const Gdn
   const float decay_rate = -__expf(a.a_log[vh]);
   const float dtb = a.dt_bias[vh];
   const bool owns_qk = (vh % ratio) == 0;
-  auto store_win = [&](int dst_slot, int pos) {
-    if (t < 2 * DK + DV && (t >= 2 * DK || owns_qk)) {
+  auto store_win = [&](int dst_slot, int pos, bool with_qk) {
+    if (t < 2 * DK + DV && (t >= 2 * DK || with_qk)) {
       __nv_bfloat16* cs = static_cast<__nv_bfloat16*>(a.conv_state) +
                           (((size_t)dst_slot * 2 + (pos & 1)) * conv_dim + ch) * 3;
       cs[0] = __float2bfloat16_rn(win0);
@@ -651,7 +653,7 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_chunk_kernel(const Gdn
     while (a.ckpt_rows != nullptr && ck < a.max_ckpt && a.ckpt_rows[seq * a.max_ckpt + ck] == c1 - 1) {
       const int cslot = a.ckpt_slots[seq * a.max_ckpt + ck];
       store_state(cslot);
-      store_win(cslot, pos0 + (c1 - r0));
+      store_win(cslot, pos0 + (c1 - r0), owns_qk);
       ++ck;
     }
     c0 = c1;
@@ -659,10 +661,49 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_prefill_chunk_kernel(const Gdn
   }
   const int oslot = a.out_slots != nullptr ? a.out_slots[seq] : slot;
   store_state(oslot);
-  store_win(oslot, pos0 + (r1 - r0));
+  store_win(oslot, pos0 + (r1 - r0), false);  // q/k windows: gdn_qk_window_kernel
 }
 
 }  // namespace chunk
+
+// ------------------------------------------------------------------------------------
+// Final q/k conv windows, one thread per q/k channel of each (sequence, q/k head).
+// Every value-head CTA of a q/k group reads the group's q/k window when it starts, and the
+// window after T new rows goes to parity buffer (pos0 + T) & 1: for even T that is the
+// buffer being read, and the grid orders sequences fastest, so a value head scheduled a
+// wave after its group's first one would read an already advanced window.  The prefill
+// kernels therefore store only their own v windows (checkpoint slots excepted: nothing
+// reads them during the call) and this kernel, stream-ordered after them, writes the
+// last three conv inputs of (old window, new rows) of each q/k channel.
+__global__ void gdn_qk_window_kernel(const GdnArgs a) {
+  pdl_wait();  // the prefill kernel (every reader of the old windows) has finished
+  pdl_trigger();
+  const int seq = blockIdx.x, kh = blockIdx.y, t = threadIdx.x;
+  const int r0 = a.seq_start[seq], r1 = a.seq_start[seq + 1];
+  if (r0 >= r1 || t >= 2 * DK) return;
+  const int Hk = a.num_k_heads;
+  const int conv_dim = 2 * Hk * DK + a.num_v_heads * DV;
+  const int ch = t < DK ? kh * DK + t : Hk * DK + kh * DK + (t - DK);
+  const int slot = a.slots[r0], pos0 = a.positions[r0];
+  const int oslot = a.out_slots != nullptr ? a.out_slots[seq] : slot;
+  const int T = r1 - r0;
+  const __nv_bfloat16* proj = static_cast<const __nv_bfloat16*>(a.proj);
+  const __nv_bfloat16* old_w = static_cast<const __nv_bfloat16*>(a.conv_state) +
+                               (((size_t)slot * 2 + (pos0 & 1)) * conv_dim + ch) * 3;
+  __nv_bfloat16 w[3];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const int src = T - 3 + i;  // new row index; negative: entry 3 + src of the old window
+    w[i] = src >= 0 ? proj[(size_t)(r0 + src) * a.ld_proj + ch]
+                    : (pos0 == 0 ? __float2bfloat16_rn(0.f) : old_w[3 + src]);
+  }
+  // All three old entries are in registers before the store (it may overwrite them).
+  __nv_bfloat16* new_w = static_cast<__nv_bfloat16*>(a.conv_state) +
+                         (((size_t)oslot * 2 + ((pos0 + T) & 1)) * conv_dim + ch) * 3;
+  new_w[0] = w[0];
+  new_w[1] = w[1];
+  new_w[2] = w[2];
+}
 
 }  // namespace gdn
 }  // namespace zs
@@ -675,7 +716,14 @@ extern "C" int zs_gdn_prefill(const GdnArgs* args, cudaStream_t stream) {
   if (a.num_seqs == 0) return 0;
   dim3 grid(a.num_seqs, a.num_v_heads);
   const bool chunked = a.impl == 2 || (a.impl == 0 && a.rows >= 16 * a.num_seqs);
-  if (chunked) {
+  const bool short_rows = a.impl == 0 && a.max_seq_rows >= 1 && a.max_seq_rows <= ZS_GDN_ROWS_MAX &&
+                          (a.ckpt_rows == nullptr || a.max_ckpt == 0);
+  if (short_rows) {
+    // A few rows per sequence (speculative verify / replay): the streaming decode kernel
+    // reads and writes each state once.
+    const int rc = zs_gdn_decode_rows(&a, stream);
+    if (rc != 0) return rc;
+  } else if (chunked) {
     const int smem = (int)sizeof(zs::gdn::chunk::Smem);
     static bool attr_set[16] = {false};
     int dev = 0;
@@ -690,5 +738,6 @@ extern "C" int zs_gdn_prefill(const GdnArgs* args, cudaStream_t stream) {
   } else {
     zs_launch(zs::gdn::gdn_prefill_kernel, grid, zs::gdn::THREADS, 0, stream, a);
   }
+  zs_launch(zs::gdn::gdn_qk_window_kernel, dim3(a.num_seqs, a.num_k_heads), 2 * zs::gdn::DK, 0, stream, a);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
 }

@@ -19,6 +19,13 @@
 // the value heads sharing a q/k head read the old q/k window while the owner (the
 // first value head of the group) writes the new one.
 //
+// Row groups (TMAX = 4: a speculative verify pass over the last token + K drafts, the
+// roll-back replay of the accepted rows): an item is (sequence, value head) with up to 4
+// consecutive rows; the state is read once, stepped through the rows in registers and
+// written once (to out_slots[seq] when given), each row's output emitted in turn.  The
+// q/k windows are left to the follow-up window kernel of the prefill path: with an even
+// row count the new window lands in the buffer the other value heads read.
+//
 // Reference parity: worker/zstep_worker/kernels_sm120/qwen35_ops.py:659-935 (conv,
 // delta rule, gated norm; state stored [V, K]) and the fused decode kernels of
 // kernels_sm120/csrc/qwen35_ops_kernels.cu:354-757.
@@ -34,20 +41,22 @@ constexpr int COMPUTE_WARPS = 16;
 constexpr int THREADS = COMPUTE_WARPS * 32 + 32;  // + producer warp
 constexpr uint32_t STATE_BYTES = DK * DV * 4;
 
+template <int TMAX>
 struct Stage {
-  float state[DV * DK];          // [v][k]
-  __nv_bfloat16 x[3 * 128];      // projected q | k | v channels of the item (conv inputs)
-  __nv_bfloat16 z[128];          // gate input z
-  __nv_bfloat16 win[3 * 128 * 3];  // conv windows (q | k | v), 3 taps per channel
-  __nv_bfloat16 w[3 * 128 * 4];    // conv weights (q | k | v), 4 taps per channel
+  float state[DV * DK];                // [v][k]
+  __nv_bfloat16 x[TMAX][3 * 128];      // projected q | k | v channels of each row (conv inputs)
+  __nv_bfloat16 z[TMAX][128];          // gate input z of each row
+  __nv_bfloat16 win[3 * 128 * 3];      // conv windows (q | k | v), 3 taps per channel
+  __nv_bfloat16 w[3 * 128 * 4];        // conv weights (q | k | v), 4 taps per channel
 };
 
+template <int TMAX>
 struct Smem {
-  Stage st[STAGES];
+  Stage<TMAX> st[STAGES];
   float conv_out[3 * 128];  // q | k | v after conv + SiLU (fp32)
   float o[DV];
   float red[COMPUTE_WARPS * 2];
-  float scal[4];
+  float gate[TMAX][2];      // beta and the decay g of each row of the item
   uint64_t full[STAGES];
   uint64_t computed[STAGES];
   int abort_flag;
@@ -75,29 +84,45 @@ __device__ __forceinline__ bool wait_flag(uint64_t* bar, uint32_t phase, int* er
   return false;
 }
 
+// An item's rows [row, row + nrows) (nrows 0: nothing to do), value head, q/k head, state
+// slot read, slot written, and the position of its first row.
 struct ItemInfo {
-  int row, vh, kh, slot, pos;
+  int row, nrows, vh, kh, slot, oslot, pos;
 };
 
+template <int TMAX>
 __device__ __forceinline__ ItemInfo item_info(const GdnArgs& a, int idx) {
   ItemInfo it;
-  it.row = idx / a.num_v_heads;
   it.vh = idx % a.num_v_heads;
   it.kh = it.vh / (a.num_v_heads / a.num_k_heads);
-  it.slot = a.slots[it.row];
-  it.pos = a.positions[it.row];
+  if (TMAX == 1) {
+    it.row = idx / a.num_v_heads;
+    it.nrows = 1;
+    it.slot = it.oslot = a.slots[it.row];
+  } else {
+    const int seq = idx / a.num_v_heads;
+    it.row = a.seq_start[seq];
+    it.nrows = a.seq_start[seq + 1] - it.row;
+    if (it.nrows > TMAX) it.nrows = 0;  // outside the contract: reported by the producer, skipped
+    it.slot = it.nrows > 0 ? a.slots[it.row] : 0;
+    it.oslot = a.out_slots != nullptr ? a.out_slots[seq] : it.slot;
+  }
+  it.pos = it.nrows > 0 ? a.positions[it.row] : 0;
   return it;
 }
 
 // Write back a finished stage: state, the new conv windows (q/k only by the first value
-// head of the q/k head's group), all as bulk stores from shared memory.
-__device__ __forceinline__ void store_stage(const GdnArgs& a, Stage& st, const ItemInfo& it, int conv_dim) {
+// head of the q/k head's group, and only for single-row items), all as bulk stores from
+// shared memory.
+template <int TMAX>
+__device__ __forceinline__ void store_stage(const GdnArgs& a, Stage<TMAX>& st, const ItemInfo& it, int conv_dim) {
+  if (it.nrows == 0) return;
   const int ratio = a.num_v_heads / a.num_k_heads;
-  float* gstate = a.ssm_state + ((size_t)it.slot * a.num_v_heads + it.vh) * DV * DK;
+  float* gstate = a.ssm_state + ((size_t)it.oslot * a.num_v_heads + it.vh) * DV * DK;
   bulk_store(gstate, st.state, STATE_BYTES);
   __nv_bfloat16* cs = static_cast<__nv_bfloat16*>(a.conv_state) +
-                      ((size_t)it.slot * 2 + ((it.pos + 1) & 1)) * conv_dim * 3;
-  if (it.vh % ratio == 0) {
+                      ((size_t)it.oslot * 2 + ((it.pos + it.nrows) & 1)) * conv_dim * 3;
+  if (TMAX == 1 && it.vh % ratio == 0) {
     bulk_store(cs + (size_t)it.kh * 128 * 3, st.win, 128 * 3 * 2);
     bulk_store(cs + (size_t)(a.num_k_heads + it.kh) * 128 * 3, st.win + 128 * 3, 128 * 3 * 2);
   }
@@ -105,11 +130,13 @@ __device__ __forceinline__ void store_stage(const GdnArgs& a, Stage& st, const I
   bulk_commit();
 }
 
+template <int TMAX>
 __global__ void __launch_bounds__(THREADS, 1) gdn_decode_tma_kernel(const GdnArgs a, int total_items) {
   pdl_wait();  // predecessor kernel done: its outputs are visible
   pdl_trigger();
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  using Sm = Smem<TMAX>;
+  Sm& s = *reinterpret_cast<Sm*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int Hk = a.num_k_heads, Hv = a.num_v_heads;
   const int conv_dim = 2 * Hk * DK + Hv * DV;
@@ -134,23 +161,31 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_decode_tma_kernel(const GdnArg
       const __nv_bfloat16* csg = static_cast<const __nv_bfloat16*>(a.conv_state);
       for (int idx = blockIdx.x; idx < total_items && !*abort_flag; idx += gridDim.x, ++n_local) {
         const int sidx = n_local % STAGES;
-        Stage& st = s.st[sidx];
+        Stage<TMAX>& st = s.st[sidx];
         if (n_local >= STAGES) {
           // Stage reuse: write back the item computed STAGES items ago first.
           if (!wait_flag(&s.computed[sidx], ((n_local - STAGES) / STAGES) & 1, a.err, abort_flag)) break;
-          store_stage(a, st, pend[sidx], conv_dim);
+          store_stage<TMAX>(a, st, pend[sidx], conv_dim);
           bulk_wait_read0();
         }
-        const ItemInfo it = item_info(a, idx);
+        const ItemInfo it = item_info<TMAX>(a, idx);
         pend[sidx] = it;
+        if (it.nrows == 0) {  // empty sequence (or too many rows: reported): arrive, no copies
+          if (TMAX > 1 && a.seq_start[idx / Hv + 1] - a.seq_start[idx / Hv] > TMAX) report_error(a.err, kErrBadShape);
+          mbar_expect_tx(&s.full[sidx], 0);
+          continue;
+        }
         const bool fresh = it.pos == 0;
-        const uint32_t bytes = (fresh ? 0u : STATE_BYTES + 3 * 128 * 3 * 2) + 4 * 128 * 2 + 3 * 128 * 4 * 2;
+        const uint32_t bytes =
+            (fresh ? 0u : STATE_BYTES + 3 * 128 * 3 * 2) + it.nrows * 4 * 128 * 2 + 3 * 128 * 4 * 2;
         mbar_expect_tx(&s.full[sidx], bytes);
-        const __nv_bfloat16* prow = proj + (size_t)it.row * a.ld_proj;
-        bulk_load(st.x, prow + it.kh * 128, 256, &s.full[sidx]);
-        bulk_load(st.x + 128, prow + (Hk + it.kh) * 128, 256, &s.full[sidx]);
-        bulk_load(st.x + 256, prow + 2 * Hk * 128 + it.vh * 128, 256, &s.full[sidx]);
-        bulk_load(st.z, prow + conv_dim + it.vh * 128, 256, &s.full[sidx]);
+        for (int r = 0; r < it.nrows; ++r) {
+          const __nv_bfloat16* prow = proj + (size_t)(it.row + r) * a.ld_proj;
+          bulk_load(st.x[r], prow + it.kh * 128, 256, &s.full[sidx]);
+          bulk_load(st.x[r] + 128, prow + (Hk + it.kh) * 128, 256, &s.full[sidx]);
+          bulk_load(st.x[r] + 256, prow + 2 * Hk * 128 + it.vh * 128, 256, &s.full[sidx]);
+          bulk_load(st.z[r], prow + conv_dim + it.vh * 128, 256, &s.full[sidx]);
+        }
         bulk_load(st.w, cw + (size_t)it.kh * 128 * 4, 1024, &s.full[sidx]);
         bulk_load(st.w + 512, cw + (size_t)(Hk + it.kh) * 128 * 4, 1024, &s.full[sidx]);
         bulk_load(st.w + 1024, cw + (size_t)(2 * Hk * 128 + it.vh * 128) * 4, 1024, &s.full[sidx]);
@@ -167,7 +202,7 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_decode_tma_kernel(const GdnArg
       for (int j = first; j < n_local && !*abort_flag; ++j) {
         const int sidx = j % STAGES;
         if (!wait_flag(&s.computed[sidx], (j / STAGES) & 1, a.err, abort_flag)) break;
-        store_stage(a, s.st[sidx], pend[sidx], conv_dim);
+        store_stage<TMAX>(a, s.st[sidx], pend[sidx], conv_dim);
       }
       bulk_wait_all0();
       // Loads that were issued but never consumed (abort): wait for them to land.
@@ -183,113 +218,131 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_decode_tma_kernel(const GdnArg
   int n_local = 0;
   for (int idx = blockIdx.x; idx < total_items; idx += gridDim.x, ++n_local) {
     const int sidx = n_local % STAGES;
-    Stage& st = s.st[sidx];
+    Stage<TMAX>& st = s.st[sidx];
     if (!wait_flag(&s.full[sidx], (n_local / STAGES) & 1, a.err, abort_flag)) break;
-    const ItemInfo it = item_info(a, idx);
+    const ItemInfo it = item_info<TMAX>(a, idx);
     const bool fresh = it.pos == 0;
-    // 1. conv + SiLU (threads 0..383, one channel each); new window written in place.
-    if (t < 384) {
-      const float x = __bfloat162float(st.x[t]);
-      __nv_bfloat16* win = st.win + t * 3;
-      const float w0 = fresh ? 0.f : __bfloat162float(win[0]);
-      const float w1 = fresh ? 0.f : __bfloat162float(win[1]);
-      const float w2 = fresh ? 0.f : __bfloat162float(win[2]);
-      const __nv_bfloat16* w = st.w + t * 4;
-      const float acc = __bfloat162float(w[0]) * w0 + __bfloat162float(w[1]) * w1 +
-                        __bfloat162float(w[2]) * w2 + __bfloat162float(w[3]) * x;
-      win[0] = __float2bfloat16_rn(w1);
-      win[1] = __float2bfloat16_rn(w2);
-      win[2] = st.x[t];
-      const float y = __bfloat162float(__float2bfloat16_rn(siluf_(acc)));
-      s.conv_out[t] = y;
-      // Partial sums of squares: warps 0-3 hold q, 4-7 hold k.
-      const float sq = warp_sum(y * y);
-      if (lane == 0) s.red[warp] = sq;
-    }
-    if (t == 0) {
-      const __nv_bfloat16* prow = static_cast<const __nv_bfloat16*>(a.proj) + (size_t)it.row * a.ld_proj;
+    // Gates of every row (threads 384.., idle during the conv): their loads and
+    // transcendentals overlap the first row's conv instead of sitting on each row's path.
+    if (t >= 384 && t < 384 + it.nrows) {
+      const int r = t - 384;
+      const __nv_bfloat16* prow = static_cast<const __nv_bfloat16*>(a.proj) + (size_t)(it.row + r) * a.ld_proj;
       const int boff = conv_dim + Hv * DV;
       const float b_raw = __bfloat162float(prow[boff + it.vh]);
       const float a_raw = __bfloat162float(prow[boff + Hv + it.vh]);
       const float sp_in = a_raw + a.dt_bias[it.vh];
       const float softplus = sp_in > 20.f ? sp_in : log1pf(__expf(sp_in));
-      s.scal[0] = sigmoidf_(b_raw);
-      s.scal[1] = __expf(-__expf(a.a_log[it.vh]) * softplus);
+      s.gate[r][0] = sigmoidf_(b_raw);
+      s.gate[r][1] = __expf(-__expf(a.a_log[it.vh]) * softplus);
     }
-    asm volatile("bar.sync 3, 512;" ::: "memory");  // compute warps only
-    const float rq = rsqrtf(s.red[0] + s.red[1] + s.red[2] + s.red[3] + 1e-6f) * rsqrtf((float)DK);
-    const float rk = rsqrtf(s.red[4] + s.red[5] + s.red[6] + s.red[7] + 1e-6f);
-    const float beta = s.scal[0], g = s.scal[1];
-    // 2. delta rule on 32 coefficients of state row vr.  The 4 threads of a row own
-    //    interleaved 16-byte pieces: piece i of thread kq covers k = seg(i)*16 + kq*4
-    //    + 0..3 with seg(i) = (i + vr) & 7, so each quarter-warp's 128-bit shared
-    //    accesses (2 rows x 4 threads) fall in distinct banks.
+    // State row vr, 32 coefficients per thread, held in registers across the item's rows.
+    // The 4 threads of a row own interleaved 16-byte pieces: piece i of thread kq covers
+    // k = seg(i)*16 + kq*4 + 0..3 with seg(i) = (i + vr) & 7, so each quarter-warp's
+    // 128-bit shared accesses (2 rows x 4 threads) fall in distinct banks.
     float* srow = st.state + vr * DK;
-    float c[32], qk[32], kk[32];
+    float c[32];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int k0 = ((i + vr) & 7) * 16 + kq * 4;
       const float4 f = fresh ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(srow + k0);
       c[4 * i] = f.x; c[4 * i + 1] = f.y; c[4 * i + 2] = f.z; c[4 * i + 3] = f.w;
-      const float4 q4 = *reinterpret_cast<const float4*>(s.conv_out + k0);
-      const float4 k4 = *reinterpret_cast<const float4*>(s.conv_out + 128 + k0);
-      qk[4 * i] = q4.x; qk[4 * i + 1] = q4.y; qk[4 * i + 2] = q4.z; qk[4 * i + 3] = q4.w;
-      kk[4 * i] = k4.x; kk[4 * i + 1] = k4.y; kk[4 * i + 2] = k4.z; kk[4 * i + 3] = k4.w;
     }
-    float kvm = 0.f;
+    for (int r = 0; r < it.nrows; ++r) {
+      const int row = it.row + r;
+      // 1. conv + SiLU (threads 0..383, one channel each); the window shifts in place.
+      if (t < 384) {
+        const float x = __bfloat162float(st.x[r][t]);
+        __nv_bfloat16* win = st.win + t * 3;
+        const bool zero_win = fresh && r == 0;  // a fresh sequence's window is all zeros
+        const float w0 = zero_win ? 0.f : __bfloat162float(win[0]);
+        const float w1 = zero_win ? 0.f : __bfloat162float(win[1]);
+        const float w2 = zero_win ? 0.f : __bfloat162float(win[2]);
+        const __nv_bfloat16* w = st.w + t * 4;
+        const float acc = __bfloat162float(w[0]) * w0 + __bfloat162float(w[1]) * w1 +
+                          __bfloat162float(w[2]) * w2 + __bfloat162float(w[3]) * x;
+        win[0] = __float2bfloat16_rn(w1);
+        win[1] = __float2bfloat16_rn(w2);
+        win[2] = st.x[r][t];
+        const float y = __bfloat162float(__float2bfloat16_rn(siluf_(acc)));
+        s.conv_out[t] = y;
+        // Partial sums of squares: warps 0-3 hold q, 4-7 hold k.
+        const float sq = warp_sum(y * y);
+        if (lane == 0 && warp < 8) s.red[warp] = sq;
+      }
+      asm volatile("bar.sync 3, 512;" ::: "memory");  // compute warps only
+      const float rq = rsqrtf(s.red[0] + s.red[1] + s.red[2] + s.red[3] + 1e-6f) * rsqrtf((float)DK);
+      const float rk = rsqrtf(s.red[4] + s.red[5] + s.red[6] + s.red[7] + 1e-6f);
+      const float beta = s.gate[r][0], g = s.gate[r][1];
+      // 2. delta rule on the 32 coefficients of state row vr.
+      float qk[32], kk[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      c[i] *= g;
-      kvm += c[i] * kk[i];
-    }
-    kvm *= rk;
-    kvm += __shfl_xor_sync(0xffffffff, kvm, 1);
-    kvm += __shfl_xor_sync(0xffffffff, kvm, 2);
-    const float delta = (s.conv_out[256 + vr] - kvm) * beta * rk;  // folds the k norm into delta
-    float o = 0.f;
+      for (int i = 0; i < 8; ++i) {
+        const int k0 = ((i + vr) & 7) * 16 + kq * 4;
+        const float4 q4 = *reinterpret_cast<const float4*>(s.conv_out + k0);
+        const float4 k4 = *reinterpret_cast<const float4*>(s.conv_out + 128 + k0);
+        qk[4 * i] = q4.x; qk[4 * i + 1] = q4.y; qk[4 * i + 2] = q4.z; qk[4 * i + 3] = q4.w;
+        kk[4 * i] = k4.x; kk[4 * i + 1] = k4.y; kk[4 * i + 2] = k4.z; kk[4 * i + 3] = k4.w;
+      }
+      float kvm = 0.f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      c[i] += kk[i] * delta;
-      o += c[i] * qk[i];
-    }
-    o *= rq;
-    o += __shfl_xor_sync(0xffffffff, o, 1);
-    o += __shfl_xor_sync(0xffffffff, o, 2);
+      for (int i = 0; i < 32; ++i) {
+        c[i] *= g;
+        kvm += c[i] * kk[i];
+      }
+      kvm *= rk;
+      kvm += __shfl_xor_sync(0xffffffff, kvm, 1);
+      kvm += __shfl_xor_sync(0xffffffff, kvm, 2);
+      const float delta = (s.conv_out[256 + vr] - kvm) * beta * rk;  // folds the k norm into delta
+      float o = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int k0 = ((i + vr) & 7) * 16 + kq * 4;
-      *reinterpret_cast<float4*>(srow + k0) = make_float4(c[4 * i], c[4 * i + 1], c[4 * i + 2], c[4 * i + 3]);
-    }
-    if (kq == 0) s.o[vr] = o;
-    // Make the generic-proxy smem writes (state, windows) visible to the bulk stores.
-    fence_proxy_async_shared();
-    asm volatile("bar.sync 3, 512;" ::: "memory");
-    // 3. gated RMSNorm + output (warps 0-3, one value each).
-    if (t < DV) {
-      const float ov = s.o[t];
-      const float ss = warp_sum(ov * ov);
-      if (lane == 0) s.red[8 + warp] = ss;
-      asm volatile("bar.sync 1, 128;" ::: "memory");  // warps 0-3 only
-      const float tot = s.red[8] + s.red[9] + s.red[10] + s.red[11];
-      const float rstd = rsqrtf(tot / DV + a.eps);
-      const float z = __bfloat162float(st.z[t]);
-      const float w = __bfloat162float(static_cast<const __nv_bfloat16*>(a.norm_w)[t]);
-      const float y = __bfloat162float(__float2bfloat16_rn(ov * rstd)) * w * siluf_(z);
-      const int width = Hv * DV;
-      const int col = it.vh * DV + t;
-      if (a.out_bf16 != nullptr)
-        static_cast<__nv_bfloat16*>(a.out_bf16)[(size_t)it.row * width + col] = __float2bfloat16_rn(y);
-      if (a.out_q != nullptr) {
-        const float yb = __bfloat162float(__float2bfloat16_rn(y));
-        const uint8_t code = mx_scale_e8m0(warp_max(fabsf(yb)));
-        a.out_q[(size_t)it.row * width + col] = f32_to_e4m3(yb * mx_inv_scale(code));
-        if (lane == 0) {
-          const int kb = col >> 5;
-          a.out_sf[((size_t)(it.row >> 7) * (width >> 7) + (kb >> 2)) * 512 +
-                   sf_atom_offset(it.row & 127, kb & 3)] = code;
+      for (int i = 0; i < 32; ++i) {
+        c[i] += kk[i] * delta;
+        o += c[i] * qk[i];
+      }
+      o *= rq;
+      o += __shfl_xor_sync(0xffffffff, o, 1);
+      o += __shfl_xor_sync(0xffffffff, o, 2);
+      if (kq == 0) s.o[vr] = o;
+      asm volatile("bar.sync 3, 512;" ::: "memory");
+      // 3. gated RMSNorm + output of this row (warps 0-3, one value each).
+      if (t < DV) {
+        const float ov = s.o[t];
+        const float ss = warp_sum(ov * ov);
+        if (lane == 0) s.red[8 + warp] = ss;
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // warps 0-3 only
+        const float tot = s.red[8] + s.red[9] + s.red[10] + s.red[11];
+        const float rstd = rsqrtf(tot / DV + a.eps);
+        const float z = __bfloat162float(st.z[r][t]);
+        const float w = __bfloat162float(static_cast<const __nv_bfloat16*>(a.norm_w)[t]);
+        const float y = __bfloat162float(__float2bfloat16_rn(ov * rstd)) * w * siluf_(z);
+        const int width = Hv * DV;
+        const int col = it.vh * DV + t;
+        if (a.out_bf16 != nullptr)
+          static_cast<__nv_bfloat16*>(a.out_bf16)[(size_t)row * width + col] = __float2bfloat16_rn(y);
+        if (a.out_q != nullptr) {
+          const float yb = __bfloat162float(__float2bfloat16_rn(y));
+          const uint8_t code = mx_scale_e8m0(warp_max(fabsf(yb)));
+          a.out_q[(size_t)row * width + col] = f32_to_e4m3(yb * mx_inv_scale(code));
+          if (lane == 0) {
+            const int kb = col >> 5;
+            a.out_sf[((size_t)(row >> 7) * (width >> 7) + (kb >> 2)) * 512 + sf_atom_offset(row & 127, kb & 3)] =
+                code;
+          }
         }
       }
+      // The next row rewrites conv_out, o and the reduction slots.
+      if (TMAX > 1) asm volatile("bar.sync 3, 512;" ::: "memory");
     }
+    // The stepped state back to shared memory for the producer's bulk store.
+    if (it.nrows > 0) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int k0 = ((i + vr) & 7) * 16 + kq * 4;
+        *reinterpret_cast<float4*>(srow + k0) = make_float4(c[4 * i], c[4 * i + 1], c[4 * i + 2], c[4 * i + 3]);
+      }
+    }
+    // Make the generic-proxy smem writes (state, windows) visible to the bulk stores.
+    fence_proxy_async_shared();
     // 4. hand the stage to the producer for write-back (all compute warps are past
     //    their last read of it once they reach this barrier).
     asm volatile("bar.sync 2, 512;" ::: "memory");
@@ -300,13 +353,11 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_decode_tma_kernel(const GdnArg
 }  // namespace gdn_dec
 }  // namespace zs
 
-extern "C" int zs_gdn_decode(const GdnArgs* args, cudaStream_t stream) {
+namespace {
+
+template <int TMAX>
+int launch_stream(const GdnArgs& a, int items, cudaStream_t stream) {
   using namespace zs::gdn_dec;
-  const GdnArgs& a = *args;
-  if (a.head_k != DK || a.head_v != DV || a.num_k_heads <= 0 || a.num_v_heads % a.num_k_heads != 0) return -1;
-  if (a.ld_proj % 8 != 0) return -1;  // 16-byte aligned projection rows for the bulk copies
-  if (a.rows == 0) return 0;
-  const int items = a.rows * a.num_v_heads;
   static int sms = 0;
   if (sms == 0) {
     int dev = 0;
@@ -314,8 +365,31 @@ extern "C" int zs_gdn_decode(const GdnArgs* args, cudaStream_t stream) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   }
   const int grid = items < sms ? items : sms;
-  const size_t smem = sizeof(Smem) + 128;
-  cudaFuncSetAttribute(gdn_decode_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  zs_launch(gdn_decode_tma_kernel, grid, THREADS, smem, stream, a, items);
+  const size_t smem = sizeof(Smem<TMAX>) + 128;
+  cudaFuncSetAttribute(gdn_decode_tma_kernel<TMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  zs_launch(gdn_decode_tma_kernel<TMAX>, grid, THREADS, smem, stream, a, items);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+}  // namespace
+
+extern "C" int zs_gdn_decode(const GdnArgs* args, cudaStream_t stream) {
+  using namespace zs::gdn_dec;
+  const GdnArgs& a = *args;
+  if (a.head_k != DK || a.head_v != DV || a.num_k_heads <= 0 || a.num_v_heads % a.num_k_heads != 0) return -1;
+  if (a.ld_proj % 8 != 0) return -1;  // 16-byte aligned projection rows for the bulk copies
+  if (a.rows == 0) return 0;
+  return launch_stream<1>(a, a.rows * a.num_v_heads, stream);
+}
+
+// Row groups of up to ZS_GDN_ROWS_MAX rows per sequence (seq_start), no checkpoints: the
+// streaming kernel over (sequence, value head) items.  The final q/k conv windows are
+// written by the caller's follow-up window kernel (zs_gdn_prefill).
+extern "C" int zs_gdn_decode_rows(const GdnArgs* args, cudaStream_t stream) {
+  using namespace zs::gdn_dec;
+  const GdnArgs& a = *args;
+  if (a.head_k != DK || a.head_v != DV || a.num_k_heads <= 0 || a.num_v_heads % a.num_k_heads != 0) return -1;
+  if (a.ld_proj % 8 != 0 || a.seq_start == nullptr) return -1;
+  if (a.num_seqs == 0) return 0;
+  return launch_stream<ZS_GDN_ROWS_MAX>(a, a.num_seqs * a.num_v_heads, stream);
 }

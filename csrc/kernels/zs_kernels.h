@@ -150,9 +150,15 @@ typedef struct GdnArgs {
                            // conv window) instead of the input slot, which stays untouched
   int impl;                // prefill: 0 = by length (chunked for >= 16 rows per sequence on
                            // average), 1 = token-sequential, 2 = chunked
+  int max_seq_rows;        // prefill: rows per sequence are at most this (0: unknown).  With
+                           // impl 0, 1..ZS_GDN_ROWS_MAX and no checkpoints the rows run on the
+                           // streaming decode kernel (speculative verify and replay)
 } GdnArgs;
 
+#define ZS_GDN_ROWS_MAX 4
+
 int zs_gdn_decode(const GdnArgs* args, cudaStream_t stream);
+int zs_gdn_decode_rows(const GdnArgs* args, cudaStream_t stream);
 int zs_gdn_prefill(const GdnArgs* args, cudaStream_t stream);
 
 // ----------------------------------------------------------------------------------
@@ -191,7 +197,7 @@ typedef struct AttnArgs {
   const int* seq_start;    // [num_seqs+1]
   int num_seqs;
   int* err;
-  int impl;                // 0: tensor-core decode for GQA groups of 4..16 heads, 1: SIMT decode
+  int impl;                // 0: tensor cores for GQA groups of 4..16 heads, else SIMT; 1: SIMT; 2: tensor cores
 } AttnArgs;
 
 int zs_attn_prologue(const AttnArgs* args, cudaStream_t stream);

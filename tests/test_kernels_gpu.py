@@ -572,6 +572,90 @@ def test_gdn_prefill_matches_decode_and_checkpoints(C, impl, lens):
         torch.testing.assert_close(ssm[sl].cpu(), st, rtol=1e-3, atol=1e-4)
 
 
+@pytest.mark.parametrize("impl", [1, 2, "rows"])
+def test_gdn_prefill_continuation_with_even_rows(C, impl):
+    """Sequences that continue from position 5 with an even number of new rows (a chunked
+    prefill continuation, a speculative replay of 2 or 4 rows).  Their q/k conv window ends
+    in the parity buffer it is read from; with 160 sequences the value heads of one q/k
+    group run waves apart, so a window written by the first of them before the others had
+    read it would show up here.  impl 1 token-sequential, 2 chunked, "rows" the streaming
+    kernel over row groups.  Outputs, final states and every final conv window against the
+    fp32 per-token reference."""
+    hk, hv = 2, 4
+    n, p0 = 160, 5
+    lens = [2 if i % 2 else 4 for i in range(n)]
+    rows = sum(lens)
+    s = _gdn_setup(hk, hv, rows, n, seed=3)
+    slots, pos, seq_start = [], [], [0]
+    for i, ln in enumerate(lens):
+        slots += [i] * ln
+        pos += list(range(p0, p0 + ln))
+        seq_start.append(seq_start[-1] + ln)
+    cs, ssm = s["conv_state"].cuda(), s["ssm"].cuda()
+    out = torch.zeros(rows, hv * 128, dtype=torch.bfloat16, device="cuda")
+    C.gdn_prefill(s["proj"].cuda(), hk, hv, s["conv_w"].cuda(), cs, ssm, s["a_log"].cuda(),
+                  s["dt_bias"].cuda(), s["norm_w"].cuda(), 1e-6, torch.tensor(slots, dtype=torch.int32).cuda(),
+                  torch.tensor(pos, dtype=torch.int32).cuda(), rows, out, None, None,
+                  torch.tensor(seq_start, dtype=torch.int32).cuda(), n, None, None, 0, None,
+                  impl=0 if impl == "rows" else impl, max_seq_rows=4 if impl == "rows" else 0)
+    torch.cuda.synchronize()
+    out, cs, ssm = out.cpu().float(), cs.cpu().float(), ssm.cpu()
+    for i, ln in enumerate(lens):
+        win = s["conv_state"][i, p0 & 1].float()
+        st = s["ssm"][i]
+        for j in range(ln):
+            r = seq_start[i] + j
+            y, win, st = ref.gdn_token(s["proj"][r].float(), win, st, hk=hk, hv=hv, conv_w=s["conv_w"],
+                                       a_log=s["a_log"], dt_bias=s["dt_bias"], norm_w=s["norm_w"], eps=1e-6)
+            torch.testing.assert_close(out[r], y, rtol=3e-2, atol=3e-2)
+        torch.testing.assert_close(ssm[i], st, rtol=1e-3, atol=1e-4)
+        torch.testing.assert_close(cs[i, (p0 + ln) & 1], win, rtol=1e-2, atol=1e-2)
+
+
+def test_gdn_rows_streaming_kernel_with_out_slots(C):
+    """The streaming GDN kernel over row groups (a speculative verify pass: the last token +
+    drafts of each sequence, 1 to 4 rows, some sequences fresh): outputs per row against the
+    fp32 reference, the final state and conv windows in out_slots[seq] for the sequences
+    that have one (the input slot untouched), in place for the others."""
+    hk, hv = 2, 4
+    lens = [1, 2, 3, 4] * 40
+    n = len(lens)
+    starts_pos = [0 if i % 7 == 0 else 3 + i % 5 for i in range(n)]
+    rows = sum(lens)
+    s = _gdn_setup(hk, hv, rows, 2 * n, seed=5)
+    slots, pos, seq_start = [], [], [0]
+    for i, ln in enumerate(lens):
+        slots += [i] * ln
+        pos += list(range(starts_pos[i], starts_pos[i] + ln))
+        seq_start.append(seq_start[-1] + ln)
+    out_slots = [n + i if i % 2 == 0 else i for i in range(n)]
+    cs, ssm = s["conv_state"].cuda(), s["ssm"].cuda()
+    out = torch.zeros(rows, hv * 128, dtype=torch.bfloat16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    C.gdn_prefill(s["proj"].cuda(), hk, hv, s["conv_w"].cuda(), cs, ssm, s["a_log"].cuda(),
+                  s["dt_bias"].cuda(), s["norm_w"].cuda(), 1e-6, torch.tensor(slots, dtype=torch.int32).cuda(),
+                  torch.tensor(pos, dtype=torch.int32).cuda(), rows, out, None, None,
+                  torch.tensor(seq_start, dtype=torch.int32).cuda(), n, None, None, 0, err,
+                  torch.tensor(out_slots, dtype=torch.int32).cuda(), impl=0, max_seq_rows=4)
+    torch.cuda.synchronize()
+    assert err.item() == 0
+    out, cs, ssm = out.cpu().float(), cs.cpu().float(), ssm.cpu()
+    for i, ln in enumerate(lens):
+        p0 = starts_pos[i]
+        win = s["conv_state"][i, p0 & 1].float() if p0 > 0 else torch.zeros(s["conv_dim"], 3)
+        st = s["ssm"][i] if p0 > 0 else torch.zeros(hv, 128, 128)
+        for j in range(ln):
+            r = seq_start[i] + j
+            y, win, st = ref.gdn_token(s["proj"][r].float(), win, st, hk=hk, hv=hv, conv_w=s["conv_w"],
+                                       a_log=s["a_log"], dt_bias=s["dt_bias"], norm_w=s["norm_w"], eps=1e-6)
+            torch.testing.assert_close(out[r], y, rtol=3e-2, atol=3e-2)
+        o = out_slots[i]
+        torch.testing.assert_close(ssm[o], st, rtol=1e-3, atol=1e-4)
+        torch.testing.assert_close(cs[o, (p0 + ln) & 1], win, rtol=1e-2, atol=1e-2)
+        if o != i:
+            torch.testing.assert_close(ssm[i], s["ssm"][i])
+
+
 def test_attention_prologue_and_decode(C):
     torch.manual_seed(0)
     hq, hkv, d, page = 8, 2, 256, 16
@@ -615,15 +699,17 @@ def test_attention_prologue_and_decode(C):
         torch.testing.assert_close(out[r].cpu().float(), expect, rtol=2e-2, atol=2e-2)
 
 
-@pytest.mark.parametrize("hq,hkv,splits", [(16, 2, 1), (16, 2, 3), (2, 1, 2), (16, 1, 1)])
-def test_attention_decode_tensor_core(C, hq, hkv, splits):
+@pytest.mark.parametrize("hq,hkv,splits,reps", [(16, 2, 1, 1), (16, 2, 3, 1), (2, 1, 2, 1), (16, 1, 1, 1),
+                                                 (16, 2, 1, 24), (16, 2, 3, 8), (2, 1, 1, 24)])
+def test_attention_decode_tensor_core(C, hq, hkv, splits, reps):
     """The tcgen05 split-KV decode (128-key tiles of bulk-copied pre-swizzled pages, online
-    softmax with TMEM rescale) and the SIMT kernel against the fp32 reference, over
-    contexts that end mid-page, mid-tile, on tile boundaries and inside one page; group
-    sizes 8, 2 (SIMT) and 16."""
+    softmax with TMEM rescale) and the SIMT kernel (impl 1; impl 2 forces tensor cores for
+    the 2-head group) against the fp32 reference, over contexts that end mid-page, mid-tile,
+    on tile boundaries and inside one page, and splits without pages; group sizes 8, 2 and
+    16.  reps > 1 repeats the context list for more CTAs than SMs."""
     g = torch.Generator().manual_seed(7)
     d, page = 256, 16
-    ctx = [1, 16, 37, 128, 129, 300, 511]
+    ctx = [1, 16, 37, 128, 129, 300, 511] * reps
     rows = len(ctx)
     max_pages = 33
     pages_total = rows * max_pages + 1
@@ -636,7 +722,7 @@ def test_attention_decode_tensor_core(C, hq, hkv, splits):
     sm = 1 / math.sqrt(d)
     dev = lambda t: t.cuda()  # noqa: E731
     outs = {}
-    for impl in ((0, 1) if hq // hkv <= 8 else (0,)):
+    for impl in ((0, 1, 2) if hq // hkv <= 8 else (0,)):
         partial = torch.zeros(rows * hq * splits * 260, device="cuda")
         out = torch.zeros(rows, hq * d, dtype=torch.bfloat16, device="cuda")
         err = torch.zeros(1, dtype=torch.int32, device="cuda")
@@ -651,10 +737,62 @@ def test_attention_decode_tensor_core(C, hq, hkv, splits):
         keys = torch.stack([kc[table[r, t // page], :, t % page].float() for t in range(ctx[r])])
         vals = torch.stack([vc[table[r, t // page], :, t % page].float() for t in range(ctx[r])])
         expect = ref.gated_attention(q[r].float(), gate[r].float(), keys, vals, sm)
-        torch.testing.assert_close(outs[0][r], expect, rtol=2e-2, atol=2e-2)
-    if 1 in outs:
-        torch.testing.assert_close(outs[0], outs[1], rtol=2e-2, atol=2e-2)
+        for impl in outs:
+            torch.testing.assert_close(outs[impl][r], expect, rtol=2e-2, atol=2e-2)
     del grp
+
+
+@pytest.mark.parametrize("hq,hkv,splits,impl", [(16, 2, 1, 0), (16, 2, 3, 0), (2, 1, 2, 2), (16, 1, 1, 0),
+                                                 (4, 1, 1, 0)])
+def test_attention_varlen_multi_row_items(C, hq, hkv, splits, impl):
+    """Varlen attention with sequence boundaries (prefill / speculative verify): the
+    tensor-core kernel packs up to 32 / G consecutive query rows of a sequence into one
+    work item (32 query slots sharing each K/V tile), each slot masked by its own causal
+    length.  Sequences of 1, 4, 5, 37 and 130 new rows after 0 to 300 cached tokens, and
+    more items than SMs, against the fp32 reference row by row, with and without the
+    sequence boundaries."""
+    g = torch.Generator().manual_seed(11)
+    d, page = 256, 16
+    seqs = [(0, 37), (300, 4), (17, 1), (128, 130), (5, 5)] * 3 + [(90, 4)] * 40  # (cached, new rows)
+    max_pages = 33
+    n = len(seqs)
+    pages_total = n * max_pages + 1
+    perm = torch.randperm(pages_total - 1, generator=g) + 1
+    table = perm.view(n, max_pages).to(torch.int32)
+    kc = (torch.randn(pages_total, hkv, page, d, generator=g) * 0.5).to(torch.bfloat16)
+    vc = (torch.randn(pages_total, hkv, page, d, generator=g) * 0.5).to(torch.bfloat16)
+    slots, lens, starts = [], [], [0]
+    for i, (cached, new) in enumerate(seqs):
+        slots += [i] * new
+        lens += [cached + j + 1 for j in range(new)]
+        starts.append(starts[-1] + new)
+    rows = len(lens)
+    q = torch.randn(rows, hq, d, generator=g).to(torch.bfloat16)
+    gate = torch.randn(rows, hq, d, generator=g).to(torch.bfloat16)
+    sm = 1 / math.sqrt(d)
+    dev = lambda x: x.cuda()  # noqa: E731
+    outs = {}
+    for mode in ("grouped", "per_row"):
+        partial = torch.zeros(rows * hq * splits * 260, device="cuda")
+        out = torch.zeros(rows, hq * d, dtype=torch.bfloat16, device="cuda")
+        err = torch.zeros(1, dtype=torch.int32, device="cuda")
+        ss = torch.tensor(starts, dtype=torch.int32, device="cuda") if mode == "grouped" else None
+        C.attn_decode(dev(q), dev(gate), hq, hkv, dev(swizzle_pages(kc)), dev(swizzle_pages(vc)), page, dev(table),
+                      torch.tensor(slots, dtype=torch.int32, device="cuda"), torch.tensor(lens, dtype=torch.int32).cuda(),
+                      rows, partial, splits, sm, out, None, None, impl=impl, err=err, seq_start=ss,
+                      num_seqs=n if ss is not None else 0)
+        torch.cuda.synchronize()
+        assert err.item() == 0
+        outs[mode] = out.cpu().float()
+    for i, (cached, new) in enumerate(seqs):
+        tot = cached + new
+        keys_all = torch.stack([kc[table[i, t // page], :, t % page].float() for t in range(tot)])
+        vals_all = torch.stack([vc[table[i, t // page], :, t % page].float() for t in range(tot)])
+        for r in range(starts[i], starts[i + 1]):
+            L = lens[r]
+            expect = ref.gated_attention(q[r].float(), gate[r].float(), keys_all[:L], vals_all[:L], sm)
+            torch.testing.assert_close(outs["grouped"][r], expect, rtol=2e-2, atol=2e-2)
+            torch.testing.assert_close(outs["per_row"][r], expect, rtol=2e-2, atol=2e-2)
 
 
 def _sample(C, logits, temp, top_k, top_p, seeds, hist=None, pres=None, freq=None, rep=None, top_n=0):

@@ -136,7 +136,13 @@ def test_verify_with_oracle_drafts_matches_greedy(setup, graphs, monkeypatch):
             continue
         plain = runner_greedy(runner, [prompts[s]], [s], len(produced[s]))[0]
         assert plain == produced[s]
-        torch.testing.assert_close(runner.ssm_state[:, spec_slots[s]], runner.ssm_state[:, s], rtol=2e-2, atol=1e-2)
+        # The verify pass computes the replayed rows' GDN inputs through the grouped-row
+        # kernels and the (K+1)-row GEMM tiles, plain decoding through one-row kernels: the
+        # inputs agree to the last bits, not bit for bit.  A replay over wrong rows moves
+        # whole state rows, which the mean difference catches.
+        spec_st, plain_st = runner.ssm_state[:, spec_slots[s]], runner.ssm_state[:, s]
+        torch.testing.assert_close(spec_st, plain_st, rtol=3e-2, atol=3e-2)
+        assert (spec_st - plain_st).abs().mean().item() < 1e-3
         par = (len(prompts[s]) + len(produced[s]) - 1) & 1  # conv window buffer of the next position
         torch.testing.assert_close(runner.conv_state[:, spec_slots[s], par], runner.conv_state[:, s, par], rtol=2e-2,
                                    atol=2e-3)

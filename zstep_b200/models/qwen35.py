@@ -458,10 +458,12 @@ class Qwen35Runner:
                                  rows, None, b["xq"], b["xsf"], term_index, term_scale)
 
     def _layers(self, rows: int, decode: bool, num_seqs: int = 0, ckpt=None, gdn_out_slots=None,
-                proj_store=None) -> None:
+                proj_store=None, max_seq_rows: int = 0) -> None:
         """All decoder layers over the staged rows.  Varlen (prefill / verify) steps may
         redirect each sequence's final GDN state (`gdn_out_slots`) and keep every GDN layer's
-        input projection (`proj_store[layer]`) for a later replay."""
+        input projection (`proj_store[layer]`) for a later replay; `max_seq_rows` (a bound
+        on the rows of any sequence, 0 if unknown) lets a verify step's few rows per
+        sequence run on the streaming GDN kernel."""
         cfg, C, b = self.cfg, self.C, self.buf
         H = cfg.hidden_size
         pos, slot, lens = b["in_pos"][:rows], b["in_slot"][:rows], b["in_len"][:rows]
@@ -483,7 +485,7 @@ class Qwen35Runner:
                 else:
                     ck_rows, ck_slots, max_ck = ckpt if ckpt is not None else (None, None, 0)
                     C.gdn_prefill(*args, b["seq_start"][:num_seqs + 1], num_seqs, ck_rows, ck_slots, max_ck,
-                                  b["err"], gdn_out_slots)
+                                  b["err"], gdn_out_slots, max_seq_rows=max_seq_rows)
                 self._proj_out(L["out_proj"], midq, b["midsf"], rows, L["post_norm"])
             else:
                 ai = self.attn_index[li]
@@ -494,10 +496,15 @@ class Qwen35Runner:
                                 pos, rows, b["q_out"], b["gate_out"])
                 midq = self._mid(self.hq * cfg.head_dim)
                 splits = self._attn_splits(rows, decode)
+                # Varlen steps pass their sequence boundaries: the tensor-core kernel then
+                # serves several query rows of a sequence from each K/V tile it loads.
+                grouped = not decode and num_seqs > 0
                 C.attn_decode(b["q_out"], b["gate_out"], self.hq, self.hkv, self.k_cache[ai], self.v_cache[ai],
                               self.page_size, self.page_table, slot, lens, rows, b["partial"], splits,
                               1.0 / math.sqrt(cfg.head_dim), None, midq, b["midsf"],
-                              impl=0 if decode else self.prefill_attn_impl)
+                              impl=0 if decode else self.prefill_attn_impl,
+                              seq_start=b["seq_start"][:num_seqs + 1] if grouped else None,
+                              num_seqs=num_seqs if grouped else 0)
                 self._proj_out(L["o_proj"], midq, b["midsf"], rows, L["post_norm"])
             self._moe(L, rows)
             next_w = self.layers[li + 1]["input_norm"] if li + 1 < len(self.layers) else self.final_norm

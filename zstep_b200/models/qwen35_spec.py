@@ -118,7 +118,7 @@ class SpecDecoder:
             r.C.gdn_prefill(self.fix_proj[:rows], r.hk, r.hv, L["conv_w"], r.conv_state[gi], r.ssm_state[gi],
                             L["a_log"], L["dt_bias"], L["gnorm"], r.eps, self.slot[:rows], self.pos[:rows], rows,
                             None, midq, r.buf["midsf"], self.fix_seq_start[:len(starts)], len(row_groups), None, None,
-                            0, r.buf["err"])
+                            0, r.buf["err"], max_seq_rows=max(n for _, n in row_groups))
 
     # ------------------------------------------------------------------ graph path
     # A steady-state verify step (every sequence carries K drafts, greedy, no checkpoint)
@@ -153,7 +153,8 @@ class SpecDecoder:
         out_slots staged), device-only.  Result rows: self.g_record[:nb]."""
         r, C, b, K = self.r, self.r.C, self.r.buf, self.K
         R = nb * (K + 1)
-        r._layers(R, decode=False, num_seqs=nb, gdn_out_slots=self.out_slots[:nb], proj_store=self.proj_store)
+        r._layers(R, decode=False, num_seqs=nb, gdn_out_slots=self.out_slots[:nb], proj_store=self.proj_store,
+                  max_seq_rows=K + 1)
         r._lm_head_argmax(R)
         C.spec_verify(nb, K, r.dummy_slot, b["in_ids"], b["out_ids"], b["in_pos"], b["in_slot"], self.g_verify,
                       self.g_rep_start, self.g_rep_idx, self.g_rep_slot, self.g_rep_pos, self.ids, self.pos, self.slot,
@@ -166,7 +167,7 @@ class SpecDecoder:
             torch.index_select(self.proj_store[gi], 0, self.g_rep_idx[:R], out=self.fix_proj[:R])
             C.gdn_prefill(self.fix_proj[:R], r.hk, r.hv, L["conv_w"], r.conv_state[gi], r.ssm_state[gi], L["a_log"],
                           L["dt_bias"], L["gnorm"], r.eps, self.g_rep_slot[:R], self.g_rep_pos[:R], R, None, midq,
-                          b["midsf"], self.g_rep_start[:nb + 1], nb, None, None, 0, b["err"])
+                          b["midsf"], self.g_rep_start[:nb + 1], nb, None, None, 0, b["err"], max_seq_rows=K + 1)
         # Draft head: catch-up over every verify row (rows past a sequence's accepted
         # prefix point at the padding slot), then K-1 chained single-row steps.
         self.hid[:R].copy_(b["hidden"][:R])
