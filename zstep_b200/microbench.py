@@ -91,7 +91,7 @@ def time_fn(fn, iters=20, warmup=3, flush=False, reps=8) -> float:
 
 
 def build_runner(layers: int, batch: int, ctx: int, experts: int = 256, vocab: int = 248320, tp: int = 1,
-                 prefill_tokens: int = 0):
+                 prefill_tokens: int = 0, num_spec: int = 0):
     """Runner on one GPU; with tp > 1 it holds rank 0's shard of a tp-way layout and its
     reductions stay local (LocalCollectives), so timings are one rank's compute only."""
     from .config import Qwen35Config
@@ -105,7 +105,7 @@ def build_runner(layers: int, batch: int, ctx: int, experts: int = 256, vocab: i
     r = Qwen35Runner(cfg, max_seqs=batch, max_prefill_tokens=max(batch, prefill_tokens),
                      num_pages=batch * pages_per_seq + 1,
                      page_size=page, max_model_len=ctx + 64, tp_rank=0, tp_size=tp,
-                     collectives=LocalCollectives() if tp > 1 else None)
+                     collectives=LocalCollectives() if tp > 1 else None, num_spec_tokens=num_spec)
     for s in range(batch):
         r.set_pages(s, list(range(1 + s * pages_per_seq, 1 + (s + 1) * pages_per_seq)))
     g = torch.Generator().manual_seed(0)
@@ -147,7 +147,6 @@ def cmd_breakdown(a):
     """Per-op device time of one eager decode step (events around every kernel call); with
     --prefill-seqs N, of one varlen prefill of N sequences of --ctx tokens instead."""
     r = _runner_for(a)
-    real = r.C
     if hasattr(r, "prefill_attn_impl"):
         r.prefill_attn_impl = a.impl
     if a.prefill_seqs:
@@ -163,6 +162,14 @@ def cmd_breakdown(a):
     else:
         def step():
             r.decode_forward(a.batch)
+    kind = f"prefill of {a.prefill_seqs} x {a.ctx} tokens" if a.prefill_seqs else f"decode step (batch {a.batch}, ctx {a.ctx})"
+    _op_breakdown(r, step, f"eager {kind}", a.layers)
+
+
+def _op_breakdown(r, step, label: str, layers: int) -> None:
+    """Run `step` twice, then once more with CUDA events around every extension call
+    (through a proxy of the runner's kernel module), and print the per-op device time."""
+    real = r.C
     events = []
 
     class Proxy:
@@ -199,10 +206,59 @@ def cmd_breakdown(a):
         cnt[tag] += 1
     step_ms = st.elapsed_time(en)
     rows = sorted(tot.items(), key=lambda kv: -kv[1])
-    kind = f"prefill of {a.prefill_seqs} x {a.ctx} tokens" if a.prefill_seqs else f"decode step (batch {a.batch}, ctx {a.ctx})"
-    print(f"eager {kind}: {step_ms:.3f} ms, layers {a.layers}")
+    print(f"{label}: {step_ms:.3f} ms, layers {layers}")
     for tag, ms in rows:
         print(f"  {ms:8.3f} ms  {100 * ms / step_ms:5.1f}%  x{cnt[tag]:<4d} {tag}")
+
+
+def _graph_ms(replay, warmup: int, iters: int) -> float:
+    for _ in range(warmup):
+        replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        replay()
+        e.record()
+        e.synchronize()
+        ts.append(s.elapsed_time(e))
+    return statistics.median(ts)
+
+
+def cmd_spec(a):
+    """Device time of one steady-state speculative step (one CUDA graph: target forward over
+    batch x (K+1) rows, lm_head argmax, on-device greedy verify, GDN replay of the accepted
+    rows, MTP catch-up and the chained drafts) next to a plain decode step of the same batch.
+    Random weights accept no drafts, so every replay is the acceptance-1 worst case.  With
+    --eager 1: the per-op device time of one eager verify step instead."""
+    K = a.spec_k
+    r = build_runner(a.layers, a.batch, a.ctx, tp=a.tp, prefill_tokens=a.batch * (K + 1), num_spec=K)
+    bk = r.bucket_for(a.batch)
+    n, K1 = a.batch, K + 1
+    nb = r.spec.graph_bucket(n)
+    g = torch.Generator().manual_seed(2)
+    ids = torch.randint(0, r.cfg.vocab_size, (nb * K1,), generator=g).tolist()
+    pos = [a.ctx + j for _ in range(nb) for j in range(K1)]
+    slot = [i for i in range(nb) for _ in range(K1)]
+
+    def stage_verify():
+        r.stage(ids, pos, slot, seq_start=[i * K1 for i in range(nb + 1)])
+        r.spec.out_slots[:nb].copy_(torch.arange(nb, dtype=torch.int32) + r.spec_slot_base)
+
+    if a.eager:
+        r.spec._graph_buffers()
+        stage_verify()
+        _op_breakdown(r, lambda: r.spec.verify_step(nb), f"eager verify step ({n} x {K1} rows, ctx {a.ctx})",
+                      a.layers)
+        return
+    r.capture_decode_graph(bk)
+    dec = _graph_ms(r.graphs[bk].replay, a.warmup, a.iters)
+    stage_verify()
+    r.spec.run_verify_graph(nb)
+    ver = _graph_ms(lambda: r.spec.g_graphs[nb].replay(), a.warmup, a.iters)
+    print(json.dumps({"op": "spec_step", "batch": n, "K": K, "ctx": a.ctx, "tp": a.tp, "decode_step_ms": round(dec, 4),
+                      "verify_step_ms": round(ver, 4), "ratio": round(ver / dec, 3)}))
 
 
 def cmd_step(a):
@@ -254,7 +310,8 @@ def _gemm_case(m, n, k, groups=1):
 
 def cmd_gemm(a):
     """Dense or uniform grouped MXFP8 GEMM; --epi 2 runs the SiLU(gate)*up + MXFP8 epilogue
-    of the MoE gate/up projection (n = 2 x intermediate, output e4m3 + scale atoms)."""
+    of the MoE gate/up projection (n = 2 x intermediate, output e4m3 + scale atoms), --epi 3
+    the scaled scatter of the MoE down projection."""
     from .ops import mx
 
     C, pw, xq, xsf = _gemm_case(a.m, a.n, a.k, a.groups)
@@ -279,8 +336,12 @@ def cmd_gemm(a):
         pre = torch.arange(a.groups + 1, dtype=torch.int32, device="cuda") * ((a.m + bn - 1) // bn)
         ws = torch.zeros(8 << 20, dtype=torch.float32, device="cuda")
         sem = torch.zeros(16384, dtype=torch.int32, device="cuda")
+        dst = scl = None
+        if a.epi == 3:  # MoE down projection: rows scattered to (token, k) slots, times the routing weight
+            dst = torch.randperm(rows_out, device="cuda").to(torch.int32)
+            scl = torch.rand(rows_out, device="cuda")
         fn = lambda: C.gemm_mxf8(pw.q, pw.sf, xq, xsf, a.k, pw.n_pad, a.n, a.groups, 0, cnt, off, pre, a.epi,  # noqa
-                                 out, ldo, out_sf, None, None, None, 0, bn, 1, 0, 1, a.fix_splits, ws, sem)
+                                 out, ldo, out_sf, dst, scl, None, 0, bn, 1, 0, 1, a.fix_splits, ws, sem)
     ms = time_fn(fn, flush=bool(a.flush))
     pk = peaks()
     flops = 2.0 * a.m * a.n * a.k * a.groups
@@ -415,7 +476,7 @@ def cmd_coll(a):
 
 
 def cmd_attn(a):
-    r = build_runner(4, a.m, a.ctx, experts=32, vocab=8192)
+    r = build_runner(4, a.m, a.ctx, experts=32, vocab=8192, tp=a.tp)
     b = r.buf
     b["q_out"].normal_()
     b["gate_out"].normal_()
@@ -432,7 +493,8 @@ def cmd_attn(a):
     ms = time_fn(fn, flush=True)
     kv_bytes = a.m * (a.ctx + 1) * r.hkv * 256 * 2 * 2
     pk = peaks()
-    print(json.dumps({"op": "attn_decode", "impl": a.impl, "rows": a.m, "ctx": a.ctx, "splits": splits, "ms": round(ms, 4),
+    print(json.dumps({"op": "attn_decode", "impl": a.impl, "tp": a.tp, "rows": a.m, "ctx": a.ctx, "splits": splits,
+                      "ms": round(ms, 4),
                       "gbs": round(kv_bytes / ms / 1e6, 1), "frac_hbm": round(kv_bytes / ms / 1e6 / pk["hbm_gbs"], 3),
                       "peaks": pk["src"]}))
 
@@ -454,13 +516,14 @@ def cmd_moe(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("cmd", choices=["breakdown", "step", "gemm", "gdn", "attn", "moe", "coll"])
+    ap.add_argument("cmd", choices=["breakdown", "step", "spec", "gemm", "gdn", "attn", "moe", "coll"])
     ap.add_argument("--layers", type=int, default=40)
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--ctx", type=int, default=1280)
     ap.add_argument("--prefill-seqs", type=int, default=0, help="breakdown: time a varlen prefill of this many sequences of --ctx tokens")
     ap.add_argument("--eager", type=int, default=0)
     ap.add_argument("--profile-replay", type=int, default=0)
+    ap.add_argument("--spec-k", type=int, default=3, help="spec: draft tokens per verify step")
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--m", type=int, default=256)
@@ -471,13 +534,15 @@ def main():
     ap.add_argument("--tp", type=int, default=1, help="time rank 0 of a tp-way layout (no communication)")
     ap.add_argument("--model", default="qwen", choices=["qwen", "deepseek"])
     ap.add_argument("--splits", type=int, default=0, help="attn: split-KV factor (0 = the runner's choice)")
-    ap.add_argument("--epi", type=int, default=0, help="gemm: 0 bf16 store, 2 SiLU(gate)*up + MXFP8")
+    ap.add_argument("--epi", type=int, default=0,
+                    help="gemm: 0 bf16 store, 2 SiLU(gate)*up + MXFP8, 3 scaled scatter (grouped MoE down)")
     ap.add_argument("--fix-splits", type=int, default=1, help="gemm (dense): in-kernel split-K factor")
     ap.add_argument("--bn", type=int, default=0, help="gemm (dense): token tile 32 or 128 (0 = by rows)")
-    ap.add_argument("--impl", type=int, default=0, help="attn: 0 tensor-core decode, 1 SIMT decode")
+    ap.add_argument("--impl", type=int, default=0,
+                    help="attn: 0 auto (tensor cores from 4 q heads per kv head), 1 SIMT, 2 tensor cores")
     a = ap.parse_args()
     torch.manual_seed(0)
-    {"breakdown": cmd_breakdown, "step": cmd_step, "gemm": cmd_gemm, "gdn": cmd_gdn, "attn": cmd_attn, "coll": cmd_coll,
+    {"breakdown": cmd_breakdown, "step": cmd_step, "spec": cmd_spec, "gemm": cmd_gemm, "gdn": cmd_gdn, "attn": cmd_attn, "coll": cmd_coll,
      "moe": cmd_moe}[a.cmd](a)
 
 
