@@ -414,12 +414,18 @@ decode_partial_tc_kernel(const AttnArgs a) {
   int k_uses = 0, v_uses[2] = {0, 0};
   const __nv_bfloat16* kc = static_cast<const __nv_bfloat16*>(a.k_cache);
   const __nv_bfloat16* vc = static_cast<const __nv_bfloat16*>(a.v_cache);
+  // The tile's page ids are loaded together (independent loads, one latency), then its
+  // page copies are issued back to back.
   auto issue = [&](const __nv_bfloat16* cache, uint8_t* dst, uint64_t* bar, int tile) {
     const int pg0 = p0 + tile * TC_PAGES;
     const int n = min(TC_PAGES, p1 - pg0);
+    int page[TC_PAGES];
+#pragma unroll
+    for (int j = 0; j < TC_PAGES; ++j) page[j] = j < n ? __ldg(pt + pg0 + j) : 0;
     mbar_expect_tx(bar, n * BLOCK_BYTES);
-    for (int j = 0; j < n; ++j)
-      bulk_load(dst + j * BLOCK_BYTES, cache + kv_offset(a, __ldg(pt + pg0 + j), kvh), BLOCK_BYTES, bar);
+#pragma unroll
+    for (int j = 0; j < TC_PAGES; ++j)
+      if (j < n) bulk_load(dst + j * BLOCK_BYTES, cache + kv_offset(a, page[j], kvh), BLOCK_BYTES, bar);
   };
   if (tid == 0 && ntiles > 0) {
     issue(kc, s.k, &s.kfull, 0);
