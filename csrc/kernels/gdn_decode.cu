@@ -53,10 +53,11 @@ struct Stage {
 template <int TMAX>
 struct Smem {
   Stage<TMAX> st[STAGES];
-  float conv_out[3 * 128];  // q | k | v after conv + SiLU (fp32)
-  float o[DV];
-  float red[COMPUTE_WARPS * 2];
-  float gate[TMAX][2];      // beta and the decay g of each row of the item
+  __nv_bfloat16 conv_out[TMAX][3 * 128];  // q | k | v after conv + SiLU of each row (bf16-rounded values)
+  float o[TMAX][DV];                      // delta-rule outputs of each row, before the gated norm
+  float red[TMAX][8];                     // per row: sums of squares of q (warps 0-3) and k (4-7)
+  float red_o[TMAX][4];                   // per row: sums of squares of o (4 warps)
+  float gate[TMAX][2];                    // beta and the decay g of each row of the item
   uint64_t full[STAGES];
   uint64_t computed[STAGES];
   int abort_flag;
@@ -247,41 +248,55 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_decode_tma_kernel(const GdnArg
       const float4 f = fresh ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(srow + k0);
       c[4 * i] = f.x; c[4 * i + 1] = f.y; c[4 * i + 2] = f.z; c[4 * i + 3] = f.w;
     }
-    for (int r = 0; r < it.nrows; ++r) {
-      const int row = it.row + r;
-      // 1. conv + SiLU (threads 0..383, one channel each); the window shifts in place.
-      if (t < 384) {
+    // 1. conv + SiLU of every row (threads 0..383, one channel each, rows in order: the
+    //    window shifts in place).  It does not depend on the state, so all rows go before
+    //    the first barrier.
+    if (t < 384) {
+      __nv_bfloat16* win = st.win + t * 3;
+      const __nv_bfloat16* w = st.w + t * 4;
+      const float c0 = __bfloat162float(w[0]), c1 = __bfloat162float(w[1]), c2 = __bfloat162float(w[2]),
+                  c3 = __bfloat162float(w[3]);
+      float w0 = fresh ? 0.f : __bfloat162float(win[0]);  // a fresh sequence's window is all zeros
+      float w1 = fresh ? 0.f : __bfloat162float(win[1]);
+      float w2 = fresh ? 0.f : __bfloat162float(win[2]);
+      for (int r = 0; r < it.nrows; ++r) {
         const float x = __bfloat162float(st.x[r][t]);
-        __nv_bfloat16* win = st.win + t * 3;
-        const bool zero_win = fresh && r == 0;  // a fresh sequence's window is all zeros
-        const float w0 = zero_win ? 0.f : __bfloat162float(win[0]);
-        const float w1 = zero_win ? 0.f : __bfloat162float(win[1]);
-        const float w2 = zero_win ? 0.f : __bfloat162float(win[2]);
-        const __nv_bfloat16* w = st.w + t * 4;
-        const float acc = __bfloat162float(w[0]) * w0 + __bfloat162float(w[1]) * w1 +
-                          __bfloat162float(w[2]) * w2 + __bfloat162float(w[3]) * x;
-        win[0] = __float2bfloat16_rn(w1);
-        win[1] = __float2bfloat16_rn(w2);
-        win[2] = st.x[r][t];
-        const float y = __bfloat162float(__float2bfloat16_rn(siluf_(acc)));
-        s.conv_out[t] = y;
+        const float acc = c0 * w0 + c1 * w1 + c2 * w2 + c3 * x;
+        w0 = w1;
+        w1 = w2;
+        w2 = x;
+        const __nv_bfloat16 yb = __float2bfloat16_rn(siluf_(acc));
+        s.conv_out[r][t] = yb;
+        const float y = __bfloat162float(yb);
         // Partial sums of squares: warps 0-3 hold q, 4-7 hold k.
         const float sq = warp_sum(y * y);
-        if (lane == 0 && warp < 8) s.red[warp] = sq;
+        if (lane == 0 && warp < 8) s.red[r][warp] = sq;
       }
-      asm volatile("bar.sync 3, 512;" ::: "memory");  // compute warps only
-      const float rq = rsqrtf(s.red[0] + s.red[1] + s.red[2] + s.red[3] + 1e-6f) * rsqrtf((float)DK);
-      const float rk = rsqrtf(s.red[4] + s.red[5] + s.red[6] + s.red[7] + 1e-6f);
+      if (it.nrows > 0) {
+        win[0] = __float2bfloat16_rn(w0);
+        win[1] = __float2bfloat16_rn(w1);
+        win[2] = __float2bfloat16_rn(w2);
+      }
+    }
+    asm volatile("bar.sync 3, 512;" ::: "memory");  // compute warps only
+    // 2. delta rule over the rows, the 32 coefficients of state row vr in registers; the
+    //    only exchanges are within the 4 threads of a row (shuffles), so no block barrier.
+    for (int r = 0; r < it.nrows; ++r) {
+      const float rq = rsqrtf(s.red[r][0] + s.red[r][1] + s.red[r][2] + s.red[r][3] + 1e-6f) * rsqrtf((float)DK);
+      const float rk = rsqrtf(s.red[r][4] + s.red[r][5] + s.red[r][6] + s.red[r][7] + 1e-6f);
       const float beta = s.gate[r][0], g = s.gate[r][1];
-      // 2. delta rule on the 32 coefficients of state row vr.
       float qk[32], kk[32];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int k0 = ((i + vr) & 7) * 16 + kq * 4;
-        const float4 q4 = *reinterpret_cast<const float4*>(s.conv_out + k0);
-        const float4 k4 = *reinterpret_cast<const float4*>(s.conv_out + 128 + k0);
-        qk[4 * i] = q4.x; qk[4 * i + 1] = q4.y; qk[4 * i + 2] = q4.z; qk[4 * i + 3] = q4.w;
-        kk[4 * i] = k4.x; kk[4 * i + 1] = k4.y; kk[4 * i + 2] = k4.z; kk[4 * i + 3] = k4.w;
+        const uint2 q4 = *reinterpret_cast<const uint2*>(&s.conv_out[r][k0]);
+        const uint2 k4 = *reinterpret_cast<const uint2*>(&s.conv_out[r][128 + k0]);
+        const float2 qa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q4.x));
+        const float2 qb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q4.y));
+        const float2 ka = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&k4.x));
+        const float2 kb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&k4.y));
+        qk[4 * i] = qa.x; qk[4 * i + 1] = qa.y; qk[4 * i + 2] = qb.x; qk[4 * i + 3] = qb.y;
+        kk[4 * i] = ka.x; kk[4 * i + 1] = ka.y; kk[4 * i + 2] = kb.x; kk[4 * i + 3] = kb.y;
       }
       float kvm = 0.f;
 #pragma unroll
@@ -292,7 +307,8 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_decode_tma_kernel(const GdnArg
       kvm *= rk;
       kvm += __shfl_xor_sync(0xffffffff, kvm, 1);
       kvm += __shfl_xor_sync(0xffffffff, kvm, 2);
-      const float delta = (s.conv_out[256 + vr] - kvm) * beta * rk;  // folds the k norm into delta
+      const float vv = __bfloat162float(s.conv_out[r][256 + vr]);
+      const float delta = (vv - kvm) * beta * rk;  // folds the k norm into delta
       float o = 0.f;
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
@@ -302,21 +318,33 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_decode_tma_kernel(const GdnArg
       o *= rq;
       o += __shfl_xor_sync(0xffffffff, o, 1);
       o += __shfl_xor_sync(0xffffffff, o, 2);
-      if (kq == 0) s.o[vr] = o;
-      asm volatile("bar.sync 3, 512;" ::: "memory");
-      // 3. gated RMSNorm + output of this row (warps 0-3, one value each).
-      if (t < DV) {
-        const float ov = s.o[t];
+      if (kq == 0) s.o[r][vr] = o;
+    }
+    // The stepped state back to shared memory for the producer's bulk store.
+    if (it.nrows > 0) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int k0 = ((i + vr) & 7) * 16 + kq * 4;
+        *reinterpret_cast<float4*>(srow + k0) = make_float4(c[4 * i], c[4 * i + 1], c[4 * i + 2], c[4 * i + 3]);
+      }
+    }
+    asm volatile("bar.sync 3, 512;" ::: "memory");  // every row's o is in shared memory
+    // 3. gated RMSNorm + output, all rows at once: warps 4r..4r+3 own row r (one value each).
+    {
+      const int r = t >> 7, vi = t & 127;
+      if (r < it.nrows) {
+        const int row = it.row + r;
+        const float ov = s.o[r][vi];
         const float ss = warp_sum(ov * ov);
-        if (lane == 0) s.red[8 + warp] = ss;
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // warps 0-3 only
-        const float tot = s.red[8] + s.red[9] + s.red[10] + s.red[11];
+        if (lane == 0) s.red_o[r][warp & 3] = ss;
+        asm volatile("bar.sync %0, 128;" ::"r"(4 + r) : "memory");  // the 4 warps of row r
+        const float tot = s.red_o[r][0] + s.red_o[r][1] + s.red_o[r][2] + s.red_o[r][3];
         const float rstd = rsqrtf(tot / DV + a.eps);
-        const float z = __bfloat162float(st.z[r][t]);
-        const float w = __bfloat162float(static_cast<const __nv_bfloat16*>(a.norm_w)[t]);
+        const float z = __bfloat162float(st.z[r][vi]);
+        const float w = __bfloat162float(static_cast<const __nv_bfloat16*>(a.norm_w)[vi]);
         const float y = __bfloat162float(__float2bfloat16_rn(ov * rstd)) * w * siluf_(z);
         const int width = Hv * DV;
-        const int col = it.vh * DV + t;
+        const int col = it.vh * DV + vi;
         if (a.out_bf16 != nullptr)
           static_cast<__nv_bfloat16*>(a.out_bf16)[(size_t)row * width + col] = __float2bfloat16_rn(y);
         if (a.out_q != nullptr) {
@@ -329,16 +357,6 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_decode_tma_kernel(const GdnArg
                 code;
           }
         }
-      }
-      // The next row rewrites conv_out, o and the reduction slots.
-      if (TMAX > 1) asm volatile("bar.sync 3, 512;" ::: "memory");
-    }
-    // The stepped state back to shared memory for the producer's bulk store.
-    if (it.nrows > 0) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int k0 = ((i + vr) & 7) * 16 + kq * 4;
-        *reinterpret_cast<float4*>(srow + k0) = make_float4(c[4 * i], c[4 * i + 1], c[4 * i + 2], c[4 * i + 3]);
       }
     }
     // Make the generic-proxy smem writes (state, windows) visible to the bulk stores.
