@@ -285,35 +285,73 @@ __global__ void __launch_bounds__(THREADS, 1) gdn_decode_tma_kernel(const GdnArg
       const float rq = rsqrtf(s.red[r][0] + s.red[r][1] + s.red[r][2] + s.red[r][3] + 1e-6f) * rsqrtf((float)DK);
       const float rk = rsqrtf(s.red[r][4] + s.red[r][5] + s.red[r][6] + s.red[r][7] + 1e-6f);
       const float beta = s.gate[r][0], g = s.gate[r][1];
-      float qk[32], kk[32];
+      float kvm = 0.f, o = 0.f;
+      float delta;
+      if constexpr (TMAX == 1) {
+        // One row: q and k in registers (measured faster for the decode step).
+        float qk[32], kk[32];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int k0 = ((i + vr) & 7) * 16 + kq * 4;
-        const uint2 q4 = *reinterpret_cast<const uint2*>(&s.conv_out[r][k0]);
-        const uint2 k4 = *reinterpret_cast<const uint2*>(&s.conv_out[r][128 + k0]);
-        const float2 qa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q4.x));
-        const float2 qb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&q4.y));
-        const float2 ka = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&k4.x));
-        const float2 kb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&k4.y));
-        qk[4 * i] = qa.x; qk[4 * i + 1] = qa.y; qk[4 * i + 2] = qb.x; qk[4 * i + 3] = qb.y;
-        kk[4 * i] = ka.x; kk[4 * i + 1] = ka.y; kk[4 * i + 2] = kb.x; kk[4 * i + 3] = kb.y;
-      }
-      float kvm = 0.f;
+        for (int i = 0; i < 8; ++i) {
+          const int k0 = ((i + vr) & 7) * 16 + kq * 4;
+          const uint2 qu = *reinterpret_cast<const uint2*>(&s.conv_out[r][k0]);
+          const uint2 ku = *reinterpret_cast<const uint2*>(&s.conv_out[r][128 + k0]);
+          const float2 qa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qu.x));
+          const float2 qb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&qu.y));
+          const float2 ka = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ku.x));
+          const float2 kb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ku.y));
+          qk[4 * i] = qa.x; qk[4 * i + 1] = qa.y; qk[4 * i + 2] = qb.x; qk[4 * i + 3] = qb.y;
+          kk[4 * i] = ka.x; kk[4 * i + 1] = ka.y; kk[4 * i + 2] = kb.x; kk[4 * i + 3] = kb.y;
+        }
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        c[i] *= g;
-        kvm += c[i] * kk[i];
-      }
-      kvm *= rk;
-      kvm += __shfl_xor_sync(0xffffffff, kvm, 1);
-      kvm += __shfl_xor_sync(0xffffffff, kvm, 2);
-      const float vv = __bfloat162float(s.conv_out[r][256 + vr]);
-      const float delta = (vv - kvm) * beta * rk;  // folds the k norm into delta
-      float o = 0.f;
+        for (int i = 0; i < 32; ++i) {
+          c[i] *= g;
+          kvm += c[i] * kk[i];
+        }
+        kvm *= rk;
+        kvm += __shfl_xor_sync(0xffffffff, kvm, 1);
+        kvm += __shfl_xor_sync(0xffffffff, kvm, 2);
+        delta = (__bfloat162float(s.conv_out[r][256 + vr]) - kvm) * beta * rk;  // folds the k norm into delta
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        c[i] += kk[i] * delta;
-        o += c[i] * qk[i];
+        for (int i = 0; i < 32; ++i) {
+          c[i] += kk[i] * delta;
+          o += c[i] * qk[i];
+        }
+      } else {
+        // Row groups: q and k re-read from shared memory in each of the two passes rather
+        // than held in registers (with 17 warps per CTA a thread has 96 registers, and the
+        // state row alone takes 32; the register form spills here).
+        auto ld4 = [&](int off) -> float4 {
+          const uint2 u = *reinterpret_cast<const uint2*>(&s.conv_out[r][off]);
+          const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+          const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+          return make_float4(lo.x, lo.y, hi.x, hi.y);
+        };
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int k0 = ((i + vr) & 7) * 16 + kq * 4;
+          const float4 k4 = ld4(128 + k0);
+          c[4 * i] *= g; c[4 * i + 1] *= g; c[4 * i + 2] *= g; c[4 * i + 3] *= g;
+          kvm += c[4 * i] * k4.x;
+          kvm += c[4 * i + 1] * k4.y;
+          kvm += c[4 * i + 2] * k4.z;
+          kvm += c[4 * i + 3] * k4.w;
+        }
+        kvm *= rk;
+        kvm += __shfl_xor_sync(0xffffffff, kvm, 1);
+        kvm += __shfl_xor_sync(0xffffffff, kvm, 2);
+        delta = (__bfloat162float(s.conv_out[r][256 + vr]) - kvm) * beta * rk;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int k0 = ((i + vr) & 7) * 16 + kq * 4;
+          const float4 k4 = ld4(128 + k0);
+          const float4 q4 = ld4(k0);
+          c[4 * i] += k4.x * delta; c[4 * i + 1] += k4.y * delta;
+          c[4 * i + 2] += k4.z * delta; c[4 * i + 3] += k4.w * delta;
+          o += c[4 * i] * q4.x;
+          o += c[4 * i + 1] * q4.y;
+          o += c[4 * i + 2] * q4.z;
+          o += c[4 * i + 3] * q4.w;
+        }
       }
       o *= rq;
       o += __shfl_xor_sync(0xffffffff, o, 1);
