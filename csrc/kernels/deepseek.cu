@@ -677,8 +677,8 @@ dsa_scores_tc_kernel(DsaScoresArgs a) {
   const int s_begin = blockIdx.y * kTcKeys * kTcTiles;
   if (ctx <= a.topk || s_begin >= ctx) return;  // uniform: before any barrier or TMEM use
   const int n_tiles = min(kTcTiles, (ctx - s_begin + kTcKeys - 1) / kTcKeys);
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t tc_scores_smem[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_scores_smem) + 1023) & ~uintptr_t(1023));
   uint8_t* A = base;                                  // [2][2 chunks][128 rows][128 B]
   uint8_t* B = base + 2 * 2 * kTcKeys * 128;          // [2 chunks][IH rows][128 B]
   float* wsm = reinterpret_cast<float*>(B + 2 * IH * 128);

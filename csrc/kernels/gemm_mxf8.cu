@@ -48,7 +48,6 @@ constexpr int BM = 128;   // weight rows per tile (MMA M)
 constexpr int BK = 128;   // K elements (bytes) per stage = one 128B swizzle span
 constexpr int A_BYTES = BM * BK;
 constexpr int SF_BYTES = 512;
-constexpr int NUM_THREADS = 192;
 constexpr int kMaxGroups = 520;  // grouped mode: per-group tables are staged in smem
 constexpr int kMaxFixSplits = 8; // in-kernel split-K factor limit
 
