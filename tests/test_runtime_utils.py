@@ -34,6 +34,15 @@ def test_dist_env():
         env.dist_env({"RANK": "8", "WORLD_SIZE": "8"})
 
 
+def test_own_process_group_store_drops_the_agent_store_setting():
+    """A worker group started from inside a torchrun job must host its own store."""
+    e = {"TORCHELASTIC_USE_AGENT_STORE": "True", "MASTER_PORT": "1234"}
+    env.own_process_group_store(e)
+    assert e == {"MASTER_PORT": "1234"}
+    env.own_process_group_store(e)  # absent: nothing to do
+    assert e == {"MASTER_PORT": "1234"}
+
+
 def test_no_env_reads_outside_env_module():
     """Only zstep_b200/utils/env.py may read os.environ / os.getenv."""
     offenders = []
