@@ -171,6 +171,7 @@ class Engine {
   const Config& config() const { return cfg_; }
   kv::PrefixTree* prefix_tree() { return tree_.get(); }
   size_t free_pages() const { return pages_.available(); }
+  size_t free_ckpt_slots() const { return ckpt_slots_.available(); }
   size_t free_slots() const { return free_slots_.size(); }
   // The last staged plan (tests and the micro-step benchmark inspect it).
   const StepPlan& last_plan() const { return plan_; }

@@ -330,6 +330,7 @@ PYBIND11_MODULE(_master, m) {
       .def("stats", &engine::Engine::stats)
       .def("free_pages", &engine::Engine::free_pages)
       .def("free_slots", &engine::Engine::free_slots)
+      .def("free_ckpt_slots", &engine::Engine::free_ckpt_slots)
       .def("cached_prefix_nodes", [](engine::Engine& e) { return e.prefix_tree() ? e.prefix_tree()->cached_nodes() : 0; });
 
 

@@ -160,6 +160,56 @@ def test_cancel_releases_everything():
     assert eng.free_pages() == 255 and eng.free_slots() == 8
 
 
+@pytest.mark.parametrize("seed", [1, 2, 3])
+@pytest.mark.parametrize("mode", ["plain", "apc", "ngram"])
+def test_random_cancellation_leaks_nothing(seed, mode):
+    """Half of the requests are cancelled at random steps (while waiting, mid-prefill or
+    mid-decode) among prompts that share prefixes.  Survivors must still produce exactly the
+    model's tokens, and once idle every request slot, KV page and checkpoint slot is free
+    or held by a cached prefix node."""
+    import random
+
+    rng = random.Random(seed)
+    kw = dict(max_seqs=6, num_pages=160, chunk=16, max_step_tokens=48)
+    if mode == "apc":
+        kw.update(apc=True, ppn=1, recurrent=True, ckpt=24)
+    if mode == "ngram":
+        kw.update(spec="ngram", k=3)
+    eng, _ = make(**kw)
+    bases = [[rng.randrange(V) for _ in range(rng.randint(4, 20))] for _ in range(3)]
+    prompts, maxt, live = {}, {}, set()
+    pending = list(range(24))
+    out, cancelled = {}, set()
+    for step in range(4000):
+        while pending and rng.random() < 0.5:
+            rid = pending.pop(0)
+            p = rng.choice(bases) + [rng.randrange(V) for _ in range(rng.randint(1, 24))]
+            prompts[rid], maxt[rid] = p, rng.randint(1, 12)
+            if eng.submit(rid, p, maxt[rid]):
+                live.add(rid)
+        if live and rng.random() < 0.15:
+            rid = rng.choice(sorted(live))
+            if rid % 2 == 0 and eng.cancel(rid):
+                cancelled.add(rid)
+                live.discard(rid)
+        if not eng.has_work() and not pending:
+            break
+        for ev in eng.step():
+            out.setdefault(ev["request_id"], []).extend(ev["tokens"])
+            if ev["finish"]:
+                live.discard(ev["request_id"])
+    assert not eng.has_work() and not pending and not live
+    assert cancelled, "the schedule cancelled nothing"
+    for rid in prompts:
+        if rid not in cancelled:
+            assert out.get(rid) == expected(prompts[rid], maxt[rid]), rid
+    assert eng.free_slots() == 6
+    cached = eng.cached_prefix_nodes()
+    assert eng.free_pages() + cached * (1 if mode == "apc" else 0) == 159
+    if mode == "apc":
+        assert eng.free_ckpt_slots() + cached == 24
+
+
 def test_prefix_cache_reuse_with_recurrent_checkpoints():
     eng, be = make(apc=True, ppn=2, recurrent=True, ckpt=16, chunk=16)
     shared = [(7 * j + 3) % V for j in range(40)]
