@@ -85,6 +85,35 @@ def test_worker_crash_is_detected():
         coord.shutdown()
 
 
+@pytest.mark.timeout(300)
+def test_stalled_worker_is_detected_by_its_heartbeat():
+    """A worker that stays alive but stops making progress (SIGSTOP: its watchdog thread
+    stops refreshing the heartbeat too) turns into an engine error after the heartbeat
+    timeout, long before the step timeout."""
+    import os
+    import signal
+    import time
+
+    eng, coord = launch(model="qwen3.5-tiny", world_size=2, device="cpu", max_seqs=2, max_step_tokens=64,
+                        num_pages=64, max_model_len=256, heartbeat_timeout_ms=1500, step_timeout_ms=120000)
+    pid = coord.pids()[1]
+    try:
+        eng.submit(1, list(range(20)), 50, True)
+        eng.step()
+        os.kill(pid, signal.SIGSTOP)
+        t0 = time.monotonic()
+        with pytest.raises(RuntimeError, match="heartbeat"):
+            run_to_completion(eng)
+        assert time.monotonic() - t0 < 60  # the heartbeat, not the 120 s step timeout
+        assert eng.poisoned()
+    finally:
+        try:
+            os.kill(pid, signal.SIGCONT)
+        except ProcessLookupError:
+            pass
+        coord.shutdown()
+
+
 @pytest.mark.timeout(600)
 @pytest.mark.parametrize("apc", [False, True])
 def test_deepseek_tp2_shm_engine_matches_reference(apc):
