@@ -210,6 +210,51 @@ def test_random_cancellation_leaks_nothing(seed, mode):
         assert eng.free_ckpt_slots() + cached == 24
 
 
+def test_srpt_starvation_cap_admits_the_long_prompt():
+    """SRPT with a steady stream of short prompts and one request slot: the long prompt
+    that arrived first still gets in once it has waited the starvation cap."""
+    eng, _ = make(max_seqs=1, policy="srpt", chunk=64, max_step_tokens=64)
+    cap, slack = 64, 6  # the engine's default starvation cap (steps); steps to finish the short in the slot
+    long_p = [(3 * j + 1) % V for j in range(40)]
+    eng.submit(0, long_p, 2)
+    first_token_step = {}
+    rid = 1
+    for step in range(200):
+        if step < 60:  # a new short prompt every step
+            eng.submit(rid, [rid % V, (rid * 7) % V], 1)
+            rid += 1
+        for ev in eng.step():
+            first_token_step.setdefault(ev["request_id"], step)
+        if not eng.has_work():
+            break
+    # Short prompts overtake it, but only until the cap (in steps) is reached.
+    overtaken = [r for r, s in first_token_step.items() if r != 0 and s < first_token_step[0]]
+    assert overtaken, "SRPT never preferred a short prompt"
+    assert first_token_step[0] <= cap + slack, first_token_step[0]
+
+
+def test_whole_request_reservation_never_overcommits_pages():
+    """Admission reserves a request's whole KV (prompt + max_tokens): with pages for one
+    such request plus a bit, the second waits until the first finishes instead of both
+    starting and running out of pages mid-decode."""
+    # 4-token pages: each request needs ceil((20 + 40) / 4) = 15 pages; 24 usable pages.
+    eng, _ = make(max_seqs=4, num_pages=25, chunk=64, max_step_tokens=64)
+    a = [(5 * j + 2) % V for j in range(20)]
+    b = [(9 * j + 4) % V for j in range(20)]
+    eng.submit(1, a, 40)
+    eng.submit(2, b, 40)
+    events = []
+    for step in range(1000):
+        if not eng.has_work():
+            break
+        for ev in eng.step():
+            events.append((step, ev["request_id"], bool(ev["finish"])))
+    finish_1 = min(s for s, r, f in events if r == 1 and f)
+    first_2 = min(s for s, r, _ in events if r == 2)
+    assert first_2 > finish_1  # request 2 was admitted only after request 1 released its pages
+    assert eng.free_pages() == 24 and eng.free_slots() == 4
+
+
 def test_prefix_cache_reuse_with_recurrent_checkpoints():
     eng, be = make(apc=True, ppn=2, recurrent=True, ckpt=16, chunk=16)
     shared = [(7 * j + 3) % V for j in range(40)]
