@@ -622,8 +622,10 @@ decode_partial_tc_kernel(const AttnArgs a) {
 // one row, each slot masked by its own causal length.  Per 128-key tile the steps are
 // those of the decode kernel above (page-image bulk copies, S^T = K Q^T with N = NS,
 // online softmax with the TMEM rescale, O^T += V^T P^T), with these differences:
-//   * each CTA walks items idx = blockIdx.x + j * gridDim.x and its copies run ahead over
-//     its whole tile stream (K one tile, V two tiles), across item boundaries;
+//   * each CTA walks items idx = blockIdx.x + j * gridDim.x, its copies running ahead over
+//     its whole tile stream (K one tile, V two tiles) across item boundaries; the launch
+//     covers every item with its own CTA (an upper bound on the item count), so a CTA
+//     walks more than one item only when given a smaller grid;
 //   * a tile's page ids are read together, then its page copies issued back to back;
 //   * the item list is built in the CTA from seq_start: a scan of each sequence's row
 //     chunks into shared memory, then a binary search per item.
