@@ -414,7 +414,7 @@ PYBIND11_MODULE(_master, m) {
   m.def("serve_mock",
         [](std::shared_ptr<tok::Tokenizer> t, engine::Config cfg, int port, std::string api_key, int admin_port,
            std::string model_name, size_t max_waiting, int32_t mock_high, int32_t eos_every, bool allow_remote_metrics,
-           std::string template_format, int step_delay_us, int32_t mock_low) {
+           std::string template_format, int step_delay_us, int32_t mock_low, int64_t fail_after) {
           auto ms = std::make_shared<MockServer>();
           ms->tok = t;
           const int32_t eos = t->eos_ids().empty() ? -1 : t->eos_ids()[0];
@@ -432,6 +432,23 @@ PYBIND11_MODULE(_master, m) {
             slow->inner = backend;
             slow->us = step_delay_us;
             backend = slow;
+          }
+          if (fail_after >= 0) {
+            // Fault injection: the backend fails every step after its first `fail_after`,
+            // as a dead worker or a kernel error would.
+            struct Failing : engine::Backend {
+              std::shared_ptr<engine::Backend> inner;
+              int64_t left;
+              bool execute(const engine::StepPlan& p, engine::StepResult* r) override {
+                if (left-- <= 0) return false;
+                return inner->execute(p, r);
+              }
+              std::string error() const override { return "injected backend fault"; }
+            };
+            auto failing = std::make_shared<Failing>();
+            failing->inner = backend;
+            failing->left = fail_after;
+            backend = failing;
           }
           ms->engine = std::make_shared<engine::Engine>(cfg, backend);
           ms->loop.reset(new serve::ServeLoop(ms->engine, nullptr, max_waiting));
@@ -452,7 +469,8 @@ PYBIND11_MODULE(_master, m) {
         py::arg("tokenizer"), py::arg("config"), py::arg("port") = 0, py::arg("api_key") = "",
         py::arg("admin_port") = -1, py::arg("model_name") = "zstep-mock", py::arg("max_waiting") = 64,
         py::arg("mock_high") = 256, py::arg("eos_every") = 0, py::arg("allow_remote_metrics") = true,
-        py::arg("template_format") = "chatml", py::arg("step_delay_us") = 0, py::arg("mock_low") = 0);
+        py::arg("template_format") = "chatml", py::arg("step_delay_us") = 0, py::arg("mock_low") = 0,
+        py::arg("fail_after") = -1);
   m.def("mock_next_token", &serve::mock_next_token);
 
 

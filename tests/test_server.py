@@ -218,3 +218,34 @@ def test_overload_returns_429(tok):
         assert 429 in codes and 200 in codes
     finally:
         s.stop()
+
+
+@pytest.mark.parametrize("stream", [True, False])
+def test_backend_fault_fails_requests_and_reports_faulted(tok, stream):
+    """Fault injection (the mock backend fails every step after its third, as a dead worker
+    or a kernel error would): the request in flight ends with an error, the engine state
+    turns to faulted, probes and new requests answer 503, and the failed request's slot
+    and pages are released."""
+    s = M.serve_mock(tok, engine_cfg(), admin_port=0, mock_low=LOW, mock_high=HIGH, fail_after=3)
+    try:
+        free0 = s.free_pages()
+        status, _, raw = chat(s.port(), body={"max_tokens": 64, "stream": stream})
+        if stream:
+            assert status == 200  # headers went out before the fault
+            events = sse_events(raw)
+            errors = [e for e in events if isinstance(e, dict) and ("error" in e or any(
+                c.get("finish_reason") == "error" for c in e.get("choices", [])))]
+            assert errors, events
+        else:
+            assert status >= 500, raw
+        assert s.state() == "faulted"
+        assert request(s.port(), "GET", "/health")[0] == 503
+        assert request(s.port(), "GET", "/ready")[0] == 503
+        assert request(s.port(), "GET", "/livez")[0] == 200  # the process itself is alive
+        assert chat(s.port())[0] == 503
+        assert s.free_slots() == 4 and s.free_pages() == free0
+        import re
+
+        assert re.search(r"^zstep:engine_state(\{[^}]*\})? 3$", s.metrics_text(), re.M)
+    finally:
+        s.stop()
