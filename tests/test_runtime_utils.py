@@ -146,3 +146,32 @@ def test_runahead_guard_caps_in_flight_steps():
     off.before_launch()
     off.after_launch()
     assert off.depth == 0 and not off.enabled
+
+
+def test_dram_arena_demotes_and_reloads_pages():
+    """Host DRAM arena (CPU tensors here): pages demoted to slots come back bit-identical
+    into other pages, one call may mix both directions, and out-of-range slots are refused."""
+    import numpy as np
+    import torch
+
+    from zstep_b200.runtime.kv_dram import DramKvArena
+
+    g = torch.Generator().manual_seed(0)
+    caches = [torch.randn(3, 10, 2, 4, generator=g), torch.randint(0, 255, (3, 10, 8), generator=g).to(torch.uint8)]
+    orig = [c.clone() for c in caches]
+    arena = DramKvArena(caches, num_blocks=4)
+    assert arena.bytes_per_block == 3 * 2 * 4 * 4 + 3 * 8
+    arena.transfer(np.array([2, 5]), np.array([0, 3]), np.array([0, 0]))  # demote pages 2, 5
+    for c in caches:
+        c[:, 2] = 0
+        c[:, 5] = 0
+    # Reload slot 3 into page 7 and demote page 9 into slot 1 in the same call.
+    arena.transfer(np.array([7, 9]), np.array([3, 1]), np.array([1, 0]))
+    arena.transfer(np.array([1, 2]), np.array([0, 1]), np.array([1, 1]))  # slot 0 -> page 1, slot 1 -> page 2
+    for c, o in zip(caches, orig):
+        assert torch.equal(c[:, 7], o[:, 5])
+        assert torch.equal(c[:, 1], o[:, 2])
+        assert torch.equal(c[:, 2], o[:, 9])
+    assert (arena.d2h_blocks, arena.h2d_blocks) == (3, 3)
+    with pytest.raises(ValueError):
+        arena.transfer(np.array([0]), np.array([4]), np.array([0]))

@@ -23,8 +23,9 @@ class DramKvArena:
         """caches: device tensors [layers, pages, ...] (page is dim 1)."""
         self.caches = caches
         self.num_blocks = num_blocks
-        self.host = [torch.empty((num_blocks, c.shape[0]) + tuple(c.shape[2:]), dtype=c.dtype, pin_memory=True)
-                     for c in caches]
+        # Pinned so the copies are asynchronous DMA (host tensors of CPU caches need no pinning).
+        self.host = [torch.empty((num_blocks, c.shape[0]) + tuple(c.shape[2:]), dtype=c.dtype,
+                                 pin_memory=c.is_cuda) for c in caches]
         self.bytes_per_block = sum(h[0].numel() * h.element_size() for h in self.host)
         self.d2h_blocks = 0
         self.h2d_blocks = 0
