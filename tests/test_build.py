@@ -17,3 +17,21 @@ def test_kernel_extension_exports():
                  "mla_absorb_q", "mla_attn", "mla_up", "dsa_index", "gather_sum"):
         assert hasattr(_C, name), name
     assert _C.mhc_slices(4096) == 8
+
+
+def test_bench_reference_arm_prints_one_json_line():
+    """The benchmark's reference arm (`bench.py --impl reference`) exits 0 with one JSON line
+    naming the arm, here the reason the reference cannot run on B200."""
+    import json
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, os.path.join(root, "bench.py"), "--impl", "reference"], capture_output=True,
+                       text=True, timeout=300, cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1
+    rec = json.loads(lines[0])
+    assert rec["impl"] == "reference" and ("unavailable" in rec or "value" in rec)
