@@ -171,3 +171,27 @@ def test_tp2_workers_ignore_an_inherited_torchrun_agent_store(monkeypatch):
         assert [out[i] for i in range(len(ps))] == ref
     finally:
         coord.shutdown()
+
+
+@pytest.mark.timeout(600)
+def test_tp2_mtp_speculation_matches_greedy_reference():
+    """MTP drafting in the workers: every sampled step returns K drafts from the MTP layer,
+    the engine schedules verify steps of width K+1 and the workers roll their state back to
+    the last accepted row.  Drafts only change how many tokens a step yields, so the output
+    must equal plain greedy decoding exactly."""
+    ps = prompts(n=4)
+    ref = reference_generate(ps, 24)
+    eng, coord = launch(model="qwen3.5-tiny", world_size=2, device="cpu", max_seqs=4, max_step_tokens=96,
+                        page_size=16, num_pages=256, max_model_len=512,
+                        engine={"max_prefill_chunk": 40, "recurrent_state": True, "spec_method": "mtp",
+                                "num_spec_tokens": 3})
+    try:
+        for i, p in enumerate(ps):
+            assert eng.submit(i, p, 24, True)
+        out = run_to_completion(eng)
+        for i in range(len(ps)):
+            assert out[i] == ref[i], f"request {i} diverged"
+        st = eng.stats()
+        assert st.spec_verify_steps > 0 and st.spec_drafts > 0
+    finally:
+        coord.shutdown()

@@ -49,7 +49,8 @@ def launch(*, model: str = "qwen3.5-tiny", world_size: int = 1, device: str = "c
                          **(engine or {}))
     argv = [sys.executable, "-m", "zstep_b200.runtime.worker", "--model", model, "--device", device, "--seed",
             str(seed), "--num-pages", str(num_pages), "--max-model-len", str(max_model_len), "--num-ckpt-slots",
-            str(num_ckpt_slots), "--dram-kv-blocks", str(dram_kv_blocks)]
+            str(num_ckpt_slots), "--dram-kv-blocks", str(dram_kv_blocks), "--spec-method", ecfg.spec_method,
+            "--num-spec-tokens", str(ecfg.num_spec_tokens)]
     root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     env = {"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(free_port()),
            "PYTHONPATH": root + os.pathsep + python_path()}

@@ -107,6 +107,13 @@ class CpuReferenceRunner:
         model_cls = DeepSeekReference if _is_deepseek(self.cfg) else Qwen35Reference
         self.model = model_cls(self.cfg, _weights(self.cfg, args.model, args.seed), device="cpu",
                                quant=False, tp_rank=rank, tp_size=world, allreduce=ar)
+        # MTP drafting (Qwen3.5 only): K greedy drafts per sampled sequence, chained through
+        # the reference model's MTP layer after each step.
+        self.num_spec = 0
+        if getattr(args, "spec_method", "none") == "mtp":
+            if _is_deepseek(self.cfg) or not self.cfg.mtp_num_hidden_layers:
+                raise ValueError("--spec-method mtp needs a model with an MTP layer")
+            self.num_spec = args.num_spec_tokens
         self.states: dict[int, object] = {}
         self.ckpt: dict[int, object] = {}
         self.generated: dict[int, list[int]] = {}  # per slot: generated tokens (penalties)
@@ -140,10 +147,12 @@ class CpuReferenceRunner:
                 self.generated[slot] = []
             st = self.states[slot]
             width = int(plan["spec_width"][i])
-            row_logits, row_states = [], []
+            row_logits, row_states, row_hidden = [], [], []
             for r in range(r0, r1):
                 assert st.pos == int(pos[r]), f"slot {slot}: state at {st.pos}, plan position {int(pos[r])}"
                 lg = self.model.step(st, int(toks[r]))
+                if self.num_spec:
+                    row_hidden.append(st.hidden)
                 if r in ckpt_at:
                     self.ckpt[ckpt_at[r]] = self.model.clone_state(st)
                 if width > 0:
@@ -153,6 +162,9 @@ class CpuReferenceRunner:
                     row_logits.append(self._full_logits(lg))
             out[i]["req_slot"] = slot
             if int(plan["sample_row"][i]) < 0:
+                if self.num_spec:  # prefill chunk: MTP catch-up for the rows whose next token is known
+                    self._mtp_chain(self.states[slot], [int(t) for t in toks[r0 + 1:r1]], row_hidden,
+                                    int(pos[r0]), 0)
                 continue
             sp = plan["sampling"][i]
             if width > 0:
@@ -176,7 +188,34 @@ class CpuReferenceRunner:
             self.generated.setdefault(slot, []).extend(tokens)
             out[i]["num_tokens"] = len(tokens)
             out[i]["tokens"][:len(tokens)] = tokens
+            if self.num_spec:
+                # Row r0+j is followed by the prompt / draft token r0+j+1 (non-verify rows) or by
+                # the target's token acc[j] (verify rows, accepted prefix only).
+                if width > 0:
+                    nxt, hid = tokens, row_hidden[:len(tokens)]
+                else:
+                    nxt, hid = [int(t) for t in toks[r0 + 1:r1]] + tokens[:1], row_hidden
+                d = self._mtp_chain(self.states[slot], nxt, hid, int(pos[r0]), self.num_spec)
+                out[i]["next_drafts"][:len(d)] = d
+                out[i]["num_drafts"] = len(d)
         return out
+
+    def _mtp_chain(self, st, next_tokens: list[int], hidden: list, pos0: int, num_drafts: int) -> list[int]:
+        """MTP catch-up for rows pos0.. (each: the following token + the target's hidden state
+        at that row), then ``num_drafts`` greedy drafts chained from the last MTP output."""
+        lg = h = None
+        for j, tok in enumerate(next_tokens):
+            lg, h = self.model.mtp_step(st, tok, hidden[j], pos0 + j)
+        drafts = []
+        p = pos0 + len(next_tokens)
+        for _ in range(num_drafts if lg is not None else 0):
+            d = int(torch.argmax(self._full_logits(lg)))
+            drafts.append(d)
+            if len(drafts) == num_drafts:
+                break
+            lg, h = self.model.mtp_step(st, d, h, p)
+            p += 1
+        return drafts
 
     def close(self) -> None:
         if dist.is_initialized():
