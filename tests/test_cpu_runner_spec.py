@@ -72,3 +72,47 @@ def test_mtp_drafts_verify_and_roll_back():
     # Plain decode continues from the rolled-back state.
     o = r.execute(plan([ref[K + 2]], [p0 + 1]))
     assert int(o[0]["tokens"][0]) == ref[K + 3]
+
+
+def test_dspark_drafts_verify_and_roll_back():
+    """The DeepSeek-style model with DSpark drafts: contexts stored for every row across
+    prefill chunks (drafts equal a direct call sequence on a fresh reference), a verify step
+    with right drafts advances K+1 rows, one with wrong drafts rolls the caches back."""
+    from zstep_b200.config import deepseek_tiny
+    from zstep_b200.models.deepseek_ref import DeepSeekReference
+    from zstep_b200.models.deepseek_weights import DeepSeekRandomWeights
+
+    cfg = deepseek_tiny()
+    args = argparse.Namespace(model="deepseek-tiny", seed=0, spec_method="dspark", num_spec_tokens=K)
+    r = CpuReferenceRunner(args, 0, 1, wire.Geometry(max_seqs=1))
+    g = torch.Generator().manual_seed(5)
+    prompt = [int(x) for x in torch.randint(0, cfg.vocab_size, (14,), generator=g)]
+
+    m = DeepSeekReference(cfg, DeepSeekRandomWeights(cfg, seed=0))
+    m.load_dspark(DeepSeekRandomWeights(cfg, seed=0))
+    st = m.new_state()
+    for p, t in enumerate(prompt):
+        lg = m.step(st, t)
+        m.dspark_context(st, m.last_aux, p)
+    first = int(torch.argmax(lg))
+    want = m.dspark_draft(m.clone_state(st), first, len(prompt), K)
+    ref = []
+    for _ in range(10):
+        ref.append(int(torch.argmax(lg)))
+        lg = m.step(st, ref[-1])
+
+    o = r.execute(plan(prompt[:6], range(6), sample=False))
+    assert o[0]["num_drafts"] == 0
+    o = r.execute(plan(prompt[6:], range(6, 14)))
+    assert int(o[0]["tokens"][0]) == ref[0] == first
+    assert list(o[0]["next_drafts"][:K]) == want
+    assert all(0 <= d < cfg.vocab_size for d in want)
+
+    o = r.execute(plan([ref[0]] + ref[1:1 + K], range(14, 15 + K), width=K + 1))
+    assert list(o[0]["tokens"][:K + 1]) == ref[1:2 + K] and r.states[0].pos == 15 + K
+    p0 = 15 + K
+    wrong = [(t + 1) % cfg.vocab_size for t in ref[K + 2:2 * K + 2]]
+    o = r.execute(plan([ref[K + 1]] + wrong, range(p0, p0 + K + 1), width=K + 1))
+    assert o[0]["num_tokens"] == 1 and int(o[0]["tokens"][0]) == ref[K + 2] and r.states[0].pos == p0 + 1
+    o = r.execute(plan([ref[K + 2]], [p0 + 1]))
+    assert int(o[0]["tokens"][0]) == ref[K + 3]

@@ -115,10 +115,11 @@ def test_stalled_worker_is_detected_by_its_heartbeat():
 
 
 @pytest.mark.timeout(600)
-@pytest.mark.parametrize("apc", [False, True])
-def test_deepseek_tp2_shm_engine_matches_reference(apc):
+@pytest.mark.parametrize("apc,spec", [(False, "none"), (True, "none"), (False, "dspark")])
+def test_deepseek_tp2_shm_engine_matches_reference(apc, spec):
     """The DeepSeek-style model (MLA + DSA indexer + mHC + expert-parallel MoE) through the
-    same engine and transport: 2 CPU ranks split heads and place experts by rank."""
+    same engine and transport: 2 CPU ranks split heads and place experts by rank.  With
+    DSpark drafts the engine runs verify steps and the output is still plain greedy."""
     from zstep_b200.config import deepseek_tiny
     from zstep_b200.models.deepseek_ref import DeepSeekReference
     from zstep_b200.models.deepseek_weights import DeepSeekRandomWeights
@@ -141,7 +142,8 @@ def test_deepseek_tp2_shm_engine_matches_reference(apc):
     eng, coord = launch(model="deepseek-tiny", world_size=2, device="cpu", max_seqs=2, max_step_tokens=64,
                         page_size=16, num_pages=128, max_model_len=256, num_ckpt_slots=16 if apc else 0,
                         engine={"max_prefill_chunk": 24, "prefix_caching": apc, "pages_per_node": 1,
-                                "recurrent_state": True})
+                                "recurrent_state": True, "spec_method": spec,
+                                "num_spec_tokens": 3 if spec != "none" else 0})
     try:
         for i, p in enumerate(ps):
             assert eng.submit(i, p, 12, True)
@@ -150,6 +152,8 @@ def test_deepseek_tp2_shm_engine_matches_reference(apc):
             assert out[i] == ref[i], f"request {i} diverged"
         if apc:
             assert eng.stats().prefix_hit_tokens >= 16
+        if spec != "none":
+            assert eng.stats().spec_verify_steps > 0 and eng.stats().spec_drafts > 0
     finally:
         coord.shutdown()
 

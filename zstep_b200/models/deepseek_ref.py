@@ -27,6 +27,13 @@ DSA indexer: iq = wq @ rmsnorm(q_a); ik = rope(rmsnorm(wk @ x)) cached;
 I[s] = sum_h w_h relu(iq_h . ik_s) / sqrt(index_dim) with w = (W_w @ x) / sqrt(index_heads);
 attention reads the top-k positions by I (ties: lower position first), or every
 position while the context is at most k.
+
+DSpark draft head (``load_dspark``): a context entry per target row at its position,
+c = MLA projections of rmsnorm(fc @ [FFN inputs of the auxiliary layers]) into the draft
+layer's own caches; a draft block of k rows [newest token, filler...] through that layer
+(every row attends to the contexts and the whole block), plain residual, final norm;
+draft i = argmax(lm_head . h_i + w2 . w1[previous token])
+(worker/zstep_worker/models/deepseek_v41_dspark.py:123,233,387,471).
 """
 
 from __future__ import annotations
@@ -46,6 +53,8 @@ class DsState:
     ckv: list = field(default_factory=list)   # per layer [T, kv_lora + rope] (c_kv | k_pe)
     ik: list = field(default_factory=list)    # per layer [T, index_dim]
     pos: int = 0
+    dckv: torch.Tensor | None = None          # DSpark draft layer's own caches, indexed by
+    dik: torch.Tensor | None = None           # position (rows never written read as zeros)
 
 
 def sinkhorn(logits: torch.Tensor, iters: int) -> torch.Tensor:
@@ -151,7 +160,9 @@ class DeepSeekReference:
         return s
 
     def clone_state(self, s: DsState) -> DsState:
-        return DsState(ckv=[t.clone() for t in s.ckv], ik=[t.clone() for t in s.ik], pos=s.pos)
+        cl = lambda t: None if t is None else t.clone()  # noqa: E731
+        return DsState(ckv=[t.clone() for t in s.ckv], ik=[t.clone() for t in s.ik], pos=s.pos, dckv=cl(s.dckv),
+                       dik=cl(s.dik))
 
     def _q(self, x: torch.Tensor) -> torch.Tensor:
         if not self.quant:
@@ -184,6 +195,8 @@ class DeepSeekReference:
         eps = c.rms_norm_eps
         n = c.hc_mult
         X = self._bf(self.embed[token]).unsqueeze(0).repeat(n, 1)
+        aux_layers = c.dspark_aux()
+        self.last_aux = []  # FFN-site inputs of the DSpark auxiliary layers (its context source)
         for li, L in enumerate(self.layers):
             for site in ("attn", "ffn"):
                 pre, post, res = self._mix(X, L["hc_" + site])
@@ -192,6 +205,8 @@ class DeepSeekReference:
                 if site == "attn":
                     y = self._attention(s, li, L, xq)
                 else:
+                    if li in aux_layers:
+                        self.last_aux.append(xq)
                     y = self._ffn(L, xq)
                 y = self._bf(self._reduce(y))
                 X = res @ X + post[:, None] * y
@@ -204,8 +219,16 @@ class DeepSeekReference:
         return self.lm_head @ self.last_normed
 
     def _attention(self, s: DsState, li: int, L, xq):
+        q, entry, ik = self._mla_project(L, xq, s.pos)
+        s.ckv[li] = torch.cat([s.ckv[li], entry[None]])
+        s.ik[li] = torch.cat([s.ik[li], ik[None]])
+        return self._mla_attend(L, q, s.ckv[li], s.ik[li])
+
+    def _mla_project(self, L, xq, pos: int):
+        """Query side (q_lat, q_pe, index query, index weights) and the cache entries
+        (c_kv | k_pe, index key) of one row at `pos`."""
         c = self.cfg
-        eps, pos, hl = c.rms_norm_eps, s.pos, self.hl
+        eps, hl = c.rms_norm_eps, self.hl
         nope, rope, kl = c.qk_nope_head_dim, c.qk_rope_head_dim, c.kv_lora_rank
         bf = self._bf
         qa = bf(L["q_a"] @ xq)
@@ -221,23 +244,90 @@ class DeepSeekReference:
         ik = bf(torch.cat([ik[:c.index_head_dim - rope], rope_halves(ik[c.index_head_dim - rope:], pos, c.rope_theta)]))
         iq = bf(torch.cat([iq[:, :c.index_head_dim - rope],
                            rope_halves(iq[:, c.index_head_dim - rope:], pos, c.rope_theta)], dim=1))
-        s.ckv[li] = torch.cat([s.ckv[li], torch.cat([ckv, kpe])[None]])
-        s.ik[li] = torch.cat([s.ik[li], ik[None]])
-        T = pos + 1
+        q_pe = bf(rope_halves(q[:, nope:], pos, c.rope_theta))
+        q_lat = bf(torch.einsum("hd,hdc->hc", q[:, :nope], L["w_uk"]))
+        return (q_lat, q_pe, iq, iw), torch.cat([ckv, kpe]), ik
+
+    def _mla_attend(self, L, q, keys: torch.Tensor, ikeys: torch.Tensor):
+        """Absorbed MLA over the cached rows `keys` [T, kv_lora + rope]: the top-k rows by
+        the indexer score when T exceeds index_topk (ties: lower position first), else all."""
+        c = self.cfg
+        kl = c.kv_lora_rank
+        q_lat, q_pe, iq, iw = q
+        T = keys.shape[0]
         if T > c.index_topk:
-            score = (torch.relu(s.ik[li] @ iq.T) * (c.index_head_dim ** -0.5)) @ iw   # [T]
+            score = (torch.relu(ikeys @ iq.T) * (c.index_head_dim ** -0.5)) @ iw   # [T]
             sel = torch.sort(score, descending=True, stable=True).indices[:c.index_topk]
         else:
             sel = torch.arange(T, device=self.dev)
-        kv = s.ckv[li][sel]
-        q_nope = q[:, :nope]
-        q_pe = bf(rope_halves(q[:, nope:], pos, c.rope_theta))
-        q_lat = bf(torch.einsum("hd,hdc->hc", q_nope, L["w_uk"]))
+        kv = keys[sel]
         scores = (q_lat @ kv[:, :kl].T + q_pe @ kv[:, kl:].T) * (c.qk_head_dim ** -0.5)
         p = torch.softmax(scores, dim=-1)
-        o_lat = bf(p @ kv[:, :kl])
-        o = bf(torch.einsum("hc,hvc->hv", o_lat, L["w_uv"])).reshape(-1)
+        o_lat = self._bf(p @ kv[:, :kl])
+        o = self._bf(torch.einsum("hc,hvc->hv", o_lat, L["w_uv"])).reshape(-1)
         return L["o_proj"] @ self._q(o)
+
+    # ------------------------------------------------------------------ DSpark draft head
+    def load_dspark(self, src) -> None:
+        """The draft head: fc over the auxiliary layers' FFN inputs, one dense MLA layer with
+        its own caches, a final norm, and the low-rank Markov correction [V, r] x 2 (vocab
+        rows of w2 sharded like lm_head)."""
+        c, r = self.cfg, self.r
+        g = lambda n: src.get(n, self.dev).float()  # noqa: E731
+        p = "layers.dspark."
+        L = {"attn_norm": g(p + "attn_norm"), "ffn_norm": g(p + "ffn_norm"), "dense": True}
+        L.update(self._mla(g, p))
+        F_ = c.intermediate_size // self.tp
+        sl = slice(r * F_, (r + 1) * F_)
+        L.update(gate=self._w(g(p + "mlp.gate")[sl]), up=self._w(g(p + "mlp.up")[sl]),
+                 down=self._w(g(p + "mlp.down")[:, sl]))
+        V = c.vocab_size // self.tp
+        self.dspark = {"layer": L, "fc": self._w(g("dspark.fc")), "final_norm": g("dspark.final_norm"),
+                       "w1": self._bf(g("dspark.markov_w1")), "w2": self._w(g("dspark.markov_w2")[r * V:(r + 1) * V])}
+
+    def _put(self, cache: torch.Tensor | None, pos: int, row: torch.Tensor) -> torch.Tensor:
+        if cache is None:
+            cache = torch.zeros(0, row.shape[0], device=self.dev)
+        if cache.shape[0] <= pos:
+            cache = torch.cat([cache, torch.zeros(pos + 1 - cache.shape[0], row.shape[0], device=self.dev)])
+        cache[pos] = row
+        return cache
+
+    def dspark_context(self, s: DsState, aux: list, pos: int) -> None:
+        """Context entry at `pos` from the auxiliary FFN inputs of the target row there
+        (``last_aux`` after its step): fc, the draft layer's attention norm, its MLA
+        projections into the draft caches."""
+        D, eps = self.dspark, self.cfg.rms_norm_eps
+        L = D["layer"]
+        h = self._bf(D["fc"] @ torch.cat(aux))
+        _, entry, ik = self._mla_project(L, self._q(R.rmsnorm(h, L["attn_norm"], eps, 0.0)), pos)
+        s.dckv, s.dik = self._put(s.dckv, pos, entry), self._put(s.dik, pos, ik)
+
+    def dspark_draft(self, s: DsState, anchor: int, pos: int, k: int, full_logits=lambda x: x) -> list[int]:
+        """`k` greedy drafts after `anchor` (the newest token, at `pos`): a block of rows
+        [anchor, noise * (k-1)] at pos..pos+k-1 through the draft layer, every row attending
+        to the contexts and the whole block; draft i is the argmax of
+        lm_head . h_i + w2 . w1[previous token].  `full_logits` gathers vocab shards."""
+        c, D = self.cfg, self.dspark
+        L, eps = D["layer"], c.rms_norm_eps
+        noise = c.vocab_size - 1 if c.dspark_noise_token < 0 else c.dspark_noise_token
+        hs, qs = [], []
+        for i, t in enumerate([anchor] + [noise] * (k - 1)):
+            h = self._bf(self.embed[t])
+            q, entry, ik = self._mla_project(L, self._q(R.rmsnorm(h, L["attn_norm"], eps, 0.0)), pos + i)
+            s.dckv, s.dik = self._put(s.dckv, pos + i, entry), self._put(s.dik, pos + i, ik)
+            hs.append(h)
+            qs.append(q)
+        keys, ikeys = s.dckv[:pos + k], s.dik[:pos + k]
+        drafts, prev = [], anchor
+        for i in range(k):
+            h = self._bf(hs[i] + self._reduce(self._mla_attend(L, qs[i], keys, ikeys)))
+            h = self._bf(h + self._reduce(self._ffn(L, self._q(R.rmsnorm(h, L["ffn_norm"], eps, 0.0)))))
+            xf = self._q(R.rmsnorm(h, D["final_norm"], eps, 0.0))
+            lg = self.lm_head @ xf + D["w2"] @ self._q(D["w1"][prev])
+            prev = int(torch.argmax(full_logits(lg)))
+            drafts.append(prev)
+        return drafts
 
     def _ffn(self, L, xq):
         c = self.cfg

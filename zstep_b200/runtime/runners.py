@@ -105,14 +105,18 @@ class CpuReferenceRunner:
         self.rank, self.world = rank, world
         ar = (lambda x: self._allreduce(x)) if world > 1 else None
         model_cls = DeepSeekReference if _is_deepseek(self.cfg) else Qwen35Reference
-        self.model = model_cls(self.cfg, _weights(self.cfg, args.model, args.seed), device="cpu",
-                               quant=False, tp_rank=rank, tp_size=world, allreduce=ar)
-        # MTP drafting (Qwen3.5 only): K greedy drafts per sampled sequence, chained through
-        # the reference model's MTP layer after each step.
+        src = _weights(self.cfg, args.model, args.seed)
+        self.model = model_cls(self.cfg, src, device="cpu", quant=False, tp_rank=rank, tp_size=world, allreduce=ar)
+        # Model-drafted speculation: K greedy drafts per sampled sequence after each step,
+        # from the MTP layer (Qwen3.5) or the DSpark head (DeepSeek).
+        self.spec = getattr(args, "spec_method", "none")
         self.num_spec = 0
-        if getattr(args, "spec_method", "none") == "mtp":
-            if _is_deepseek(self.cfg) or not self.cfg.mtp_num_hidden_layers:
-                raise ValueError("--spec-method mtp needs a model with an MTP layer")
+        if self.spec in ("mtp", "dspark"):
+            want = "dspark" if _is_deepseek(self.cfg) else "mtp"
+            if self.spec != want or (want == "mtp" and not self.cfg.mtp_num_hidden_layers):
+                raise ValueError(f"--spec-method {self.spec} does not fit this model")
+            if want == "dspark":
+                self.model.load_dspark(src)
             self.num_spec = args.num_spec_tokens
         self.states: dict[int, object] = {}
         self.ckpt: dict[int, object] = {}
@@ -152,7 +156,7 @@ class CpuReferenceRunner:
                 assert st.pos == int(pos[r]), f"slot {slot}: state at {st.pos}, plan position {int(pos[r])}"
                 lg = self.model.step(st, int(toks[r]))
                 if self.num_spec:
-                    row_hidden.append(st.hidden)
+                    row_hidden.append(self.model.last_aux if self.spec == "dspark" else st.hidden)
                 if r in ckpt_at:
                     self.ckpt[ckpt_at[r]] = self.model.clone_state(st)
                 if width > 0:
@@ -162,9 +166,8 @@ class CpuReferenceRunner:
                     row_logits.append(self._full_logits(lg))
             out[i]["req_slot"] = slot
             if int(plan["sample_row"][i]) < 0:
-                if self.num_spec:  # prefill chunk: MTP catch-up for the rows whose next token is known
-                    self._mtp_chain(self.states[slot], [int(t) for t in toks[r0 + 1:r1]], row_hidden,
-                                    int(pos[r0]), 0)
+                if self.num_spec:  # prefill chunk: draft-model state for its rows, no drafts
+                    self._draft(self.states[slot], [int(t) for t in toks[r0 + 1:r1]], row_hidden, int(pos[r0]), 0)
                 continue
             sp = plan["sampling"][i]
             if width > 0:
@@ -195,14 +198,23 @@ class CpuReferenceRunner:
                     nxt, hid = tokens, row_hidden[:len(tokens)]
                 else:
                     nxt, hid = [int(t) for t in toks[r0 + 1:r1]] + tokens[:1], row_hidden
-                d = self._mtp_chain(self.states[slot], nxt, hid, int(pos[r0]), self.num_spec)
+                d = self._draft(self.states[slot], nxt, hid, int(pos[r0]), self.num_spec)
                 out[i]["next_drafts"][:len(d)] = d
                 out[i]["num_drafts"] = len(d)
         return out
 
-    def _mtp_chain(self, st, next_tokens: list[int], hidden: list, pos0: int, num_drafts: int) -> list[int]:
-        """MTP catch-up for rows pos0.. (each: the following token + the target's hidden state
-        at that row), then ``num_drafts`` greedy drafts chained from the last MTP output."""
+    def _draft(self, st, next_tokens: list[int], hidden: list, pos0: int, num_drafts: int) -> list[int]:
+        """Draft-model catch-up for the target rows pos0.. (``next_tokens[j]`` follows row j,
+        ``hidden[j]`` is its hidden state, or its auxiliary FFN inputs for DSpark), then
+        ``num_drafts`` greedy drafts after the last of ``next_tokens``."""
+        if self.spec == "dspark":
+            # DSpark contexts need no following token: every row of the chunk gets one.
+            for j, aux in enumerate(hidden):
+                self.model.dspark_context(st, aux, pos0 + j)
+            if not num_drafts or not next_tokens:
+                return []
+            return self.model.dspark_draft(st, next_tokens[-1], pos0 + len(next_tokens), num_drafts,
+                                           self._full_logits)
         lg = h = None
         for j, tok in enumerate(next_tokens):
             lg, h = self.model.mtp_step(st, tok, hidden[j], pos0 + j)
