@@ -31,6 +31,8 @@ from .qwen35 import EPI_BF16, EPI_F32, EPI_SILU, _pad128, pack_linear
 
 
 class DSparkDrafter:
+    context_only = True  # a context entry needs only its own target row
+
     def __init__(self, runner, src):
         r = self.r = runner
         c, C, dev = r.cfg, r.C, r.dev

@@ -34,6 +34,8 @@ from .qwen35 import EPI_BF16, EPI_F32, _pad128, pack_linear
 
 
 class SpecDecoder:
+    context_only = False  # an MTP entry at row p needs the token at p+1
+
     def __init__(self, runner, src):
         r = self.r = runner
         cfg, C, dev = r.cfg, r.C, r.dev

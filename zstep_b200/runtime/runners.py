@@ -418,9 +418,13 @@ class GpuRunner:
         for i in range(n):
             r0, r1 = qs[i], qs[i + 1]
             out[i]["req_slot"] = int(plan["seq_slot"][i])
-            if seq_lm[i] is None:  # prefill chunk that does not sample: MTP catch-up only
-                for rr in range(r0, r1 - 1):
-                    m_ids.append(ids[rr + 1]), m_pos.append(pos[rr]), m_slot.append(rslot[rr]), m_rows.append(rr)
+            if seq_lm[i] is None:  # prefill chunk that does not sample: draft-model catch-up only
+                # An MTP entry needs the token after its row (unknown for the chunk's last
+                # row); a DSpark context needs only the row itself.
+                end = r1 if r.spec.context_only else r1 - 1
+                for rr in range(r0, end):
+                    nxt = ids[rr + 1] if rr + 1 < r1 else 0
+                    m_ids.append(nxt), m_pos.append(pos[rr]), m_slot.append(rslot[rr]), m_rows.append(rr)
                 continue
             st, cnt = seq_lm[i]
             t = targets[st:st + cnt]
