@@ -371,10 +371,12 @@ void fused_allreduce_norm(int64_t rank, int64_t world, int64_t protocol, const T
                           const std::vector<int64_t>& out, const std::vector<int64_t>& flags, const Tensor& epoch,
                           const Tensor& grid_counter, const Tensor& residual, const Tensor& weight, double w_offset,
                           double eps, int64_t rows, const OptT& normed, const OptT& q, const OptT& sf, const OptT& err,
-                          const OptT& term_index, const OptT& term_scale, int64_t timeout_ms, bool pushed) {
+                          const OptT& term_index, const OptT& term_scale, int64_t timeout_ms, bool pushed,
+                          const std::vector<int64_t>& mc) {
   TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)part.size() == world &&
                   (out.empty() || (int64_t)out.size() == world) && (flags.empty() || (int64_t)flags.size() == world),
               "bad world / pointer lists");
+  TORCH_CHECK(mc.empty() || mc.size() == 3, "mc: multicast addresses of part, out and flags");
   check_cuda(delta, "delta");
   check_cuda(residual, "residual");
   FusedArArgs a{};
@@ -407,6 +409,11 @@ void fused_allreduce_norm(int64_t rank, int64_t world, int64_t protocol, const T
   a.term_scale = optptr<const float>(term_scale);
   a.timeout_ms = (unsigned int)timeout_ms;
   a.pushed = pushed ? 1 : 0;
+  if (!mc.empty()) {
+    a.mc_part = reinterpret_cast<void*>(mc[0]);
+    a.mc_out = reinterpret_cast<void*>(mc[1]);
+    a.mc_flags = reinterpret_cast<uint32_t*>(mc[2]);
+  }
   rc(zs_fused_allreduce_norm(&a, stream()), "zs_fused_allreduce_norm");
 }
 
@@ -872,7 +879,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out"), py::arg("flags"), py::arg("epoch"), py::arg("grid_counter"), py::arg("residual"),
         py::arg("weight"), py::arg("w_offset"), py::arg("eps"), py::arg("rows"), py::arg("normed"), py::arg("q"),
         py::arg("sf"), py::arg("err"), py::arg("term_index") = py::none(), py::arg("term_scale") = py::none(),
-        py::arg("timeout_ms") = 0, py::arg("pushed") = false);
+        py::arg("timeout_ms") = 0, py::arg("pushed") = false, py::arg("mc") = std::vector<int64_t>{});
   m.def("allreduce_sum_f32", &allreduce_sum_f32, py::arg("rank"), py::arg("world"), py::arg("data"), py::arg("rows"),
         py::arg("max_rows"), py::arg("buf"), py::arg("epoch"), py::arg("grid_counter"), py::arg("err"),
         py::arg("timeout_ms") = 0, py::arg("part") = std::vector<int64_t>{}, py::arg("out") = std::vector<int64_t>{},

@@ -23,6 +23,9 @@
 //   plain    : the two-shot data flow with plain bf16 rows and per-(source, CTA) flags
 //              released after a system-scope fence, for prefill-sized reductions where
 //              the LL format's doubled bytes would dominate.
+//   nvls     : NVLink SHARP: the buffers are bound to an NVSwitch multicast object, the
+//              switch sums the ranks' copies (multimem.ld_reduce) and broadcasts each
+//              result (multimem.st); each rank reduces 1/world of the columns.
 // All three then apply residual add, RMSNorm and MXFP8 quantization in the same kernel.
 // Every rank computes every row's sum in the same order, so all ranks hold identical
 // bf16 residual streams.
@@ -323,6 +326,106 @@ __global__ void __launch_bounds__(THREADS, 4) ar_twoshot_kernel(const FusedArArg
 }
 
 // ---------------------------------------------------------------------------------
+// NVLS (NVLink SHARP): part, out and flags live in memory bound to one NVSwitch multicast
+// object.  CTA c owns rows c, c + G, ... on every rank (G = FAR_CTAS on every call, so
+// flag c counts every call):
+//  1. this rank's local sums of those rows -> its own part rows (plain local stores)
+//  2. barrier: multimem.red.release adds 1 to flag [0][c] of every rank; wait until the
+//     local copy reaches world * E
+//  3. for this rank's column slice of each row: multimem.ld_reduce (the switch returns
+//     the sum over ranks, accumulated in fp32), + residual, rounded to bf16, multimem.st
+//     into every rank's out row
+//  4. barrier on flag [1][c]; every rank reads its local out rows: finish_row.
+// Reuse needs nothing more: a call's part stores follow the previous call's phase-4
+// barrier (no rank still reduces the old rows) and its out stores follow this call's
+// phase-2 barrier (every rank has finished the previous call: a kernel waits for its
+// predecessor before its first access).  Each result element comes from one reduction
+// and is broadcast, so every rank holds identical bits.
+__device__ __forceinline__ uint4 mm_ld_reduce_bf16x8(const void* mc) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void mm_st_bf16x8(void* mc, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Every thread's stores of this CTA are published, then one thread adds 1 to flag `slot`
+// of every rank through the multicast address and waits (bounded) until its local copy
+// reaches `target`.  Returns false for every thread when the wait ran out.
+__device__ __forceinline__ bool nvls_barrier(const FusedArArgs& a, int slot, uint32_t target, uint64_t budget) {
+  __threadfence_system();
+  asm volatile("fence.proxy.alias;" ::: "memory");
+  __syncthreads();
+  int ok = 1;
+  if (threadIdx.x == 0) {
+    asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(a.mc_flags + slot), "r"(1u) : "memory");
+    ok = wait_flag_sys(a.flags[a.rank] + slot, target, budget, nullptr);
+    if (!ok) report_error(a.err, kErrPeerTimeout);
+  }
+  const bool all_ok = !__syncthreads_or(!ok);
+  asm volatile("fence.proxy.alias;" ::: "memory");
+  return all_ok;
+}
+
+__global__ void __launch_bounds__(THREADS, 4) ar_nvls_kernel(const FusedArArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int H = a.hidden, M = a.rows, W = a.world, L = H / 4, lpt = L / THREADS;
+  const int tid = threadIdx.x, G = gridDim.x, c = blockIdx.x;
+  const uint32_t E = read_epoch(a.epoch);
+  const uint64_t budget = limit_ns(a.timeout_ms);
+  __shared__ float red[THREADS / 32];
+  const int nrows = c < M ? (M - 1 - c) / G + 1 : 0;
+  __nv_bfloat16* part = static_cast<__nv_bfloat16*>(a.part[a.rank]);
+  // 1. local sums -> own part rows
+  for (int k = 0; k < nrows; ++k) {
+    const int row = c + k * G;
+    for (int l = tid; l < L; l += THREADS) {
+      const float4 f = local_line(a, row, l);
+      *reinterpret_cast<uint2*>(part + (size_t)row * H + 4 * l) =
+          make_uint2(pack_bf16x2(f.x, f.y), pack_bf16x2(f.z, f.w));
+    }
+  }
+  // On a timeout every later phase is skipped (the error word tells the host to reset);
+  // the CTA still counts itself in finish_call.
+  bool ok = nvls_barrier(a, c, (uint32_t)W * E, budget);
+  // 2. switch reduction of this rank's column slice, + residual, broadcast
+  const int slice = H / 8 / W;  // 16-byte chunks of the slice
+  const int j0 = a.rank * slice;
+  for (int it = tid; ok && it < nrows * slice; it += THREADS) {
+    const int row = c + (it / slice) * G;
+    const size_t off = (size_t)row * H + (size_t)(j0 + it % slice) * 8;  // elements
+    const uint4 s = mm_ld_reduce_bf16x8(static_cast<const __nv_bfloat16*>(a.mc_part) + off);
+    const uint4 r = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.residual) + off);
+    float fs[8], fr[8];
+    unpack8(s, fs);
+    unpack8(r, fr);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) fs[i] += fr[i];
+    mm_st_bf16x8(static_cast<__nv_bfloat16*>(a.mc_out) + off, pack8(fs));
+  }
+  ok = ok && nvls_barrier(a, FAR_CTAS + c, (uint32_t)W * E, budget);
+  // 3. local result rows -> residual, RMSNorm, MXFP8
+  const __nv_bfloat16* out = static_cast<const __nv_bfloat16*>(a.out[a.rank]);
+  for (int k = 0; ok && k < nrows; ++k) {
+    const int row = c + k * G;
+    uint2 res[MAX_LPT];
+#pragma unroll
+    for (int i = 0; i < MAX_LPT; ++i)
+      if (i < lpt) res[i] = ld_ll(reinterpret_cast<const uint2*>(out + (size_t)row * H + 4 * (tid + i * THREADS)));
+    finish_row(a, row, lpt, res, red);
+  }
+  finish_call(a.grid_counter, a.epoch, E);
+}
+
+// ---------------------------------------------------------------------------------
 // Two-shot with plain bf16 rows (prefill sizes).  Flags: [phase][source][CTA] u32 per rank.
 // After a CTA's stores of a phase, every thread fences at system scope, then thread q
 // releases flag [phase][rank][c] on rank q; a consumer CTA c acquires the W flags of CTA
@@ -579,10 +682,17 @@ extern "C" int zs_fused_allreduce_norm(const FusedArArgs* args, cudaStream_t str
   using namespace zs::coll;
   const FusedArArgs& a = *args;
   if (a.world < 1 || a.world > 8 || a.hidden % (THREADS * 4) != 0 || a.hidden > THREADS * 4 * MAX_LPT) return -1;
-  for (int r = 0; r < a.world; ++r)
-    if (a.part[r] == nullptr || (a.protocol != FAR_ONESHOT && a.out[r] == nullptr) ||
-        (a.protocol == FAR_PLAIN && a.flags[r] == nullptr))
+  if (a.protocol == FAR_NVLS) {
+    if (a.rank < 0 || a.rank >= a.world || a.part[a.rank] == nullptr || a.out[a.rank] == nullptr ||
+        a.flags[a.rank] == nullptr || a.mc_part == nullptr || a.mc_out == nullptr || a.mc_flags == nullptr ||
+        a.pushed || (a.hidden / 8) % a.world != 0)
       return -1;
+  } else {
+    for (int r = 0; r < a.world; ++r)
+      if (a.part[r] == nullptr || (a.protocol != FAR_ONESHOT && a.out[r] == nullptr) ||
+          (a.protocol == FAR_PLAIN && a.flags[r] == nullptr))
+        return -1;
+  }
   if (a.rows <= 0) return 0;
   if (a.pushed && a.protocol == FAR_PLAIN) return -1;
   cudaError_t e;
@@ -593,6 +703,8 @@ extern "C" int zs_fused_allreduce_norm(const FusedArArgs* args, cudaStream_t str
     e = zs_launch(ar_twoshot_kernel, FAR_CTAS, THREADS, 0, stream, a);
   } else if (a.protocol == FAR_PLAIN) {
     e = zs_launch(ar_plain_kernel, FAR_CTAS, THREADS, 0, stream, a);
+  } else if (a.protocol == FAR_NVLS) {
+    e = zs_launch(ar_nvls_kernel, FAR_CTAS, THREADS, 0, stream, a);  // every CTA index on every call
   } else {
     return -1;
   }

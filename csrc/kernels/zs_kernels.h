@@ -271,14 +271,20 @@ int zs_moe_route(const MoeRouteArgs* args, cudaStream_t stream);
 //   FAR_PLAIN    : two-shot with plain bf16 rows (no flag words: full link bandwidth); per
 //                  (source, CTA) flags published with a system-scope release after the
 //                  data, for prefill-sized reductions.
+//   FAR_NVLS     : NVLink SHARP through an NVSwitch multicast object: every rank stores its
+//                  local sums into its own multicast-bound buffer; each rank reduces its
+//                  column slice of every row with multimem.ld_reduce (the switch adds the
+//                  ranks' copies) and broadcasts the result with multimem.st.  Two
+//                  multicast-counter barriers per call.
 #define FAR_ONESHOT 0
 #define FAR_TWOSHOT 1
 #define FAR_PLAIN 2
+#define FAR_NVLS 3
 #define FAR_ONESHOT_ROWS 64  // capacity (rows) of the one-shot buffers
 
 typedef struct FusedArArgs {
   int rank, world;
-  int protocol;              // FAR_ONESHOT / FAR_TWOSHOT / FAR_PLAIN
+  int protocol;              // FAR_ONESHOT / FAR_TWOSHOT / FAR_PLAIN / FAR_NVLS
   const void* delta;         // local partial terms: delta[row*row_stride + t*term_stride + col]
   int n_terms;
   const int* term_index;     // optional gathered terms (as in zs_add_rmsnorm_quant)
@@ -289,9 +295,15 @@ typedef struct FusedArArgs {
   //   ONESHOT: part = LL lines [2 parities][world][FAR_ONESHOT_ROWS][hidden/4]
   //   TWOSHOT: part = LL lines [world][ceil(rows/world)][hidden/4], out = LL lines [rows][hidden/4]
   //   PLAIN  : part = bf16 [world][ceil(rows/world)][hidden],       out = bf16 [rows][hidden]
+  //   NVLS   : part = bf16 [rows][hidden], out = bf16 [rows][hidden], flags = u32 [2][FAR_CTAS];
+  //            only this rank's entries are used, the peers' copies are reached through
+  //            the multicast addresses below
   void* part[8];
   void* out[8];
   uint32_t* flags[8];        // PLAIN: u32 [2][world][FAR_CTAS] per rank (phase, source, CTA)
+  void* mc_part;             // NVLS: multicast addresses of the part / out / flags areas
+  void* mc_out;
+  uint32_t* mc_flags;
   uint32_t* epoch;           // local device counter of this protocol (same sequence on every rank)
   uint32_t* grid_counter;    // local device counter: the last CTA of a call advances the epoch
   void* residual;            // bf16 [rows, hidden], replicated residual stream (in/out)

@@ -316,6 +316,67 @@ def check_model(coll, rank, world, dev):
     runner.graphs.clear()
 
 
+def check_nvls(rank, world, dev):
+    """NVLS protocol (NVSwitch multicast object; run when ZSTEP_TEST_NVLS=1): the residual
+    is the rank-ordered sum up to the switch's bf16 rounding of the partial sum, identical
+    bits on every rank, MXFP8 output equal to the norm kernel's on that residual, rows past
+    `rows` untouched, and repeated calls (epochs) plus a CUDA-graph replay stay right."""
+    from zstep_b200.ops import _ext
+    from zstep_b200.parallel.fused import NVLS
+
+    C = _ext.load()
+    H, R = 2048, 256
+    coll = FusedCollectives(dev)
+    coll.nvls_rows = R
+    coll.reserve(R, H)
+    if coll.nvls is None:
+        print(f"rank {rank}: NVLS unavailable: {coll.nvls_error}", flush=True)
+        coll.close()
+        return
+    g = torch.Generator(device=dev).manual_seed(300)
+    resid0 = torch.randn(R, H, generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.rand(H, generator=g, device=dev) + 0.5).to(torch.bfloat16)
+    terms = 2
+    allp = [torch.randn(terms, R, H, generator=g, device=dev) for _ in range(world)]
+    delta = allp[rank].contiguous()
+    xq = torch.zeros(R, H, dtype=torch.uint8, device=dev)
+    xsf = torch.zeros(mx.atoms_bytes(R, H), dtype=torch.uint8, device=dev)
+    for rows in (17, 130, R):
+        assert coll.protocol_for(rows) == NVLS
+        exp = _expected_residual(resid0, allp, rows, world, terms)
+        for rep in range(3):
+            hidden = resid0.clone()
+            coll.allreduce_add_rmsnorm(delta, terms, H, R * H, hidden, w, 1e-6, rows, xq, xsf, protocol=NVLS)
+            torch.cuda.synchronize()
+            assert coll.check_error() == 0, (rows, rep, coll.check_error())
+            torch.testing.assert_close(hidden[:rows].float(), exp.float(), rtol=2e-2, atol=0.15)
+            assert torch.equal(hidden[rows:], resid0[rows:]), "rows beyond `rows` were touched"
+            everyone = [torch.empty_like(hidden) for _ in range(world)]
+            dist.all_gather(everyone, hidden)
+            assert all(torch.equal(x, hidden) for x in everyone), "ranks hold different residuals"
+        h2 = hidden[:rows].clone()
+        xq2, xsf2 = torch.zeros_like(xq), torch.zeros_like(xsf)
+        C.add_rmsnorm_quant(h2, None, 0, H, H, w, 1.0, 1e-6, rows, None, xq2, xsf2)
+        assert torch.equal(xq[:rows], xq2[:rows]), f"MXFP8 rows differ rows={rows}"
+    hidden = resid0.clone()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(4):
+            coll.allreduce_add_rmsnorm(delta, terms, H, R * H, hidden, w, 1e-6, R, xq, xsf, protocol=NVLS)
+    for _ in range(3):
+        hidden.copy_(resid0)
+        graph.replay()
+        torch.cuda.synchronize()
+        assert coll.check_error() == 0
+        want = resid0.clone()
+        for _ in range(4):
+            coll.allreduce_add_rmsnorm(delta, terms, H, R * H, want, w, 1e-6, R, xq2, xsf2, protocol=NVLS)
+        torch.cuda.synchronize()
+        assert torch.equal(hidden, want), "graph replay differs from eager calls"
+    del graph
+    coll.close()
+
+
 def check_peer_timeout(coll, rank, world, dev):
     """Bounded device waits: rank 1 skips one all-reduce between steps (its GPU runs
     nothing), so rank 0's kernel must give up after timeout_ms, report kErrPeerTimeout (2)
@@ -364,6 +425,8 @@ def main():
         check_allreduce_sum(coll, rank, world, dev)
         check_gemm_push(coll, C, rank, world, dev)
         check_prefill_sized(coll, rank, world, dev)
+        if world > 1 and os.environ.get("ZSTEP_TEST_NVLS") == "1":
+            check_nvls(rank, world, dev)
         coll = FusedCollectives(dev)
         if world > 1:
             check_peer_timeout(coll, rank, world, dev)

@@ -17,6 +17,14 @@ rows one-shot (one NVLink hop), up to ``ZSTEP_COLL_LL_ROWS`` two-shot with LL li
 per-CTA release/acquire flags (full link bandwidth for prefill-sized reductions).  NCCL
 is only used when ``ZSTEP_COLLECTIVES=nccl`` selects the baseline.
 
+NVLS (``ZSTEP_COLL_NVLS_ROWS`` > 0, off by default): a second block from
+``torch.distributed._symmetric_memory`` bound to an NVSwitch multicast object (the
+allocation and handle exchange are the library's; the kernel is ours) holds
+``[flags: 2 x FAR_CTAS u32][part: R x H bf16][out: R x H bf16]``.  All-reduces above the
+one-shot size and up to that many rows then let the switch sum the ranks' copies
+(``multimem.ld_reduce``) and broadcast each result (``multimem.st``).  Every rank must
+see multicast support, or none uses it.
+
 Epoch words and completion counters are rank-local device memory, one pair per protocol;
 the kernels advance them themselves, so every call (eager or CUDA-graph replay) uses
 fresh flag values and nothing needs resetting between steps.  The collectives are issued
@@ -45,9 +53,9 @@ def _up(x: int, a: int = _ALIGN) -> int:
 
 FAR_CTAS = 128          # csrc/kernels/zs_kernels.h
 FAR_ONESHOT_ROWS = 64   # csrc/kernels/zs_kernels.h
-ONESHOT, TWOSHOT, PLAIN = 0, 1, 2
+ONESHOT, TWOSHOT, PLAIN, NVLS = 0, 1, 2, 3
 # Epoch / completion-counter slots, one per kernel family.
-_E_ONE, _E_TWO, _E_PLAIN, _E_ARGMAX, _E_SUM, _E_SUMP = range(6)
+_E_ONE, _E_TWO, _E_PLAIN, _E_ARGMAX, _E_SUM, _E_SUMP, _E_NVLS = range(7)
 
 
 class FusedCollectives:
@@ -63,8 +71,8 @@ class FusedCollectives:
         self.hidden = 0
         self._base = 0
         self._peers: list[int] = []
-        self.epoch = torch.zeros(6, dtype=torch.int32, device=self.device)
-        self.grid = torch.zeros(6, dtype=torch.int32, device=self.device)
+        self.epoch = torch.zeros(7, dtype=torch.int32, device=self.device)
+        self.grid = torch.zeros(7, dtype=torch.int32, device=self.device)
         self.sum_rows = sum_rows
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         cfg = runtime_config()
@@ -72,6 +80,9 @@ class FusedCollectives:
         self.oneshot_rows = min(cfg.coll_oneshot_rows, FAR_ONESHOT_ROWS)
         self.ll_rows = cfg.coll_ll_rows
         self.push = cfg.coll_push
+        self.nvls_rows = cfg.coll_nvls_rows if self.world > 1 else 0
+        self.nvls = None          # (local block tensor, part, out, flags, mc part, mc out, mc flags)
+        self.nvls_error = ""      # why NVLS is not in use, when it was asked for
         from .collectives import NcclCollectives
 
         self.nccl = NcclCollectives(group, self.device)
@@ -130,10 +141,44 @@ class FusedCollectives:
         self.sum_ptrs = at(self.off_sum)
         self.sum_flag_ptrs = at(self.off_sum_flags)
         self.sum_part_ptrs, self.sum_out_ptrs = at(self.off_sum_part), at(self.off_sum_out)
+        if self.nvls_rows:
+            self._nvls_setup(min(R, self.nvls_rows), H)
+
+    def _nvls_setup(self, R: int, H: int) -> None:
+        """Collective: the multicast-bound block of the NVLS protocol (see the module doc)."""
+        ok, err = 1, ""
+        blk = handle = None
+        try:
+            import torch.distributed._symmetric_memory as symm
+
+            if (H // 8) % self.world:
+                raise ValueError(f"hidden {H} does not split into {self.world} column slices of 16 bytes")
+            nbytes = _up(2 * FAR_CTAS * 4) + 2 * _up(R * H * 2)
+            blk = symm.empty(nbytes, dtype=torch.uint8, device=self.device)
+            handle = symm.rendezvous(blk, self.group if self.group is not None else dist.group.WORLD)
+            if not handle.has_multicast_support or not handle.multicast_ptr:
+                raise RuntimeError("no NVSwitch multicast support on this group")
+        except Exception as e:  # any rank without multicast turns NVLS off for all
+            ok, err = 0, f"{type(e).__name__}: {e}"
+        agree = torch.tensor([ok], dtype=torch.int32, device=self.device)
+        dist.all_reduce(agree, op=dist.ReduceOp.MIN, group=self.group)
+        if not int(agree.item()):
+            self.nvls, self.nvls_error = None, err or "a peer has no NVSwitch multicast support"
+            return
+        blk.zero_()
+        base = blk.data_ptr()
+        mc = handle.multicast_ptr + (base - handle.buffer_ptrs[handle.rank])
+        o_part = _up(2 * FAR_CTAS * 4)
+        o_out = o_part + _up(R * H * 2)
+        self.nvls = {"block": blk, "handle": handle, "rows": R, "flags": base, "part": base + o_part,
+                     "out": base + o_out, "mc": [mc + o_part, mc + o_out, mc]}
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
 
     def close(self) -> None:
         if not self._base:
             return
+        self.nvls = None
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)  # no peer may still be reading our block
         for r, p in enumerate(self._peers):
@@ -150,6 +195,8 @@ class FusedCollectives:
     def protocol_for(self, rows: int) -> int:
         if rows <= self.oneshot_rows:
             return ONESHOT
+        if self.nvls is not None and rows <= self.nvls["rows"]:
+            return NVLS
         if rows <= self.ll_cap:
             return TWOSHOT
         return PLAIN
@@ -157,7 +204,8 @@ class FusedCollectives:
     def push_target(self, rows: int):
         """Where a row-parallel GEMM's epilogue pushes its partial sums for an all-reduce of
         `rows` rows: (protocol, receive buffers of every rank, epoch counter), or None when
-        that row count takes the plain protocol (the GEMM then writes its output locally)."""
+        that row count takes the plain or NVLS protocol (the GEMM then writes its output
+        locally)."""
         if rows > self.max_rows or not self.push:
             return None
         proto = self.protocol_for(rows)
@@ -178,7 +226,14 @@ class FusedCollectives:
         if rows > self.max_rows or H != self.hidden:
             raise ValueError(f"fused all-reduce reserved for {self.max_rows}x{self.hidden}, got {rows}x{H}")
         proto = self.protocol_for(rows) if protocol is None else protocol
-        if proto == ONESHOT:
+        mc = []
+        if proto == NVLS:
+            nv = self.nvls
+            if nv is None or rows > nv["rows"] or pushed:
+                raise ValueError("NVLS all-reduce: no multicast block for these rows (or a pushed call)")
+            here = lambda p: [p if r == self.rank else 0 for r in range(self.world)]  # noqa: E731
+            part, out, flags, e, mc = here(nv["part"]), here(nv["out"]), here(nv["flags"]), _E_NVLS, nv["mc"]
+        elif proto == ONESHOT:
             part, out, flags, e = self.one_ptrs, [], [], _E_ONE
         elif proto == TWOSHOT:
             if rows > self.ll_cap:
@@ -189,7 +244,7 @@ class FusedCollectives:
         self.C.fused_allreduce_norm(self.rank, self.world, proto, delta, n_terms, row_stride, term_stride, part, out,
                                     flags, self.epoch[e:e + 1], self.grid[e:e + 1], hidden_buf, norm_w, 1.0, eps,
                                     rows, None, xq, xsf, self.err, term_index, term_scale, self.timeout_ms,
-                                    pushed=pushed)
+                                    pushed=pushed, mc=mc)
 
     def allreduce_sum(self, t: torch.Tensor) -> None:
         """In-place fp32 sum over ranks of t [rows, hidden] (mHC sublayer outputs): one-shot
@@ -226,6 +281,8 @@ class FusedCollectives:
         dist.barrier(group=self.group)
         if self._base:
             self.C.symm_memset(self._base, self.nbytes)
+        if self.nvls is not None:
+            self.nvls["block"].zero_()
         self.epoch.zero_()
         self.grid.zero_()
         self.err.zero_()

@@ -63,6 +63,8 @@ class RuntimeConfig:
     coll_oneshot_rows: int = 16           # ZSTEP_COLL_ONESHOT_ROWS: all-reduces up to this many rows go one-shot
     coll_ll_rows: int = 1024              # ZSTEP_COLL_LL_ROWS: two-shot LL lines up to this many rows, plain above
     coll_push: bool = True                # ZSTEP_COLL_PUSH: row-parallel GEMM epilogues push into the all-reduce
+    coll_nvls_rows: int = 0               # ZSTEP_COLL_NVLS_ROWS: all-reduces above the one-shot size and up to
+                                          # this many rows reduce in the NVSwitch (multicast object; 0: off)
     gemm_fix_splits: bool = False         # ZSTEP_GEMM_FIX_SPLITS: in-kernel split-K for small GEMMs
     gemm_dense_bn: int = 0                # ZSTEP_GEMM_DENSE_BN: dense GEMM token tile 32 | 128 (0: by shape)
     decode_graphs: bool = True            # ZSTEP_DECODE_GRAPHS: CUDA-graph decode buckets
@@ -82,6 +84,7 @@ class RuntimeConfig:
         "ZSTEP_COLL_ONESHOT_ROWS": ("coll_oneshot_rows", lambda n, r: _int(n, r, 0, 64)),
         "ZSTEP_COLL_LL_ROWS": ("coll_ll_rows", lambda n, r: _int(n, r, 0, 1 << 16)),
         "ZSTEP_COLL_PUSH": ("coll_push", _bool),
+        "ZSTEP_COLL_NVLS_ROWS": ("coll_nvls_rows", lambda n, r: _int(n, r, 0, 1 << 16)),
         "ZSTEP_GEMM_FIX_SPLITS": ("gemm_fix_splits", _bool),
         "ZSTEP_GEMM_DENSE_BN": ("gemm_dense_bn", lambda n, r: _choice_int(n, r, (0, 32, 128))),
         "ZSTEP_DECODE_GRAPHS": ("decode_graphs", _bool),
