@@ -11,8 +11,9 @@ Each case captures `calls` back-to-back calls in one CUDA graph, replays it `rep
 between CUDA events and reports the median per call, max over ranks.  Roofline for the
 all-reduce: a two-shot all-reduce moves 2 (W-1)/W * M * H * 2 bytes out of every GPU, so
 the bound is that over the measured 770 GB/s per-direction peer bandwidth.  Every protocol
-of the fused kernel (one-shot LL, two-shot LL, two-shot plain) is timed where it applies;
-``fused_us`` is the one the runner picks for that row count.  Expert
+of the fused kernel (one-shot LL, two-shot LL, two-shot plain, and NVLS when
+``ZSTEP_COLL_NVLS_ROWS`` enables it and the group has multicast support) is timed where it
+applies; ``fused_us`` is the one the runner picks for that row count.  Expert
 all-to-all (hidden 4096, top-8 of 256 experts, uniform random routing): every pair whose
 expert lives on another rank moves one MXFP8 row (hidden + hidden/32 + 8 bytes) out on
 dispatch and one bf16 row (2 * hidden bytes) back on combine; the NCCL baseline is
@@ -31,7 +32,7 @@ import torch.distributed as dist
 from ..ops import _ext, mx
 from .collectives import NcclCollectives
 from ..utils.env import dist_env
-from .fused import FAR_ONESHOT_ROWS, ONESHOT, PLAIN, TWOSHOT, FusedCollectives
+from .fused import FAR_ONESHOT_ROWS, NVLS, ONESHOT, PLAIN, TWOSHOT, FusedCollectives
 
 LINK_GBS = 770.0  # measured peer copy bandwidth per direction per GPU on this pool
 
@@ -77,9 +78,13 @@ def main():
     fused = FusedCollectives(dev)
     nccl = NcclCollectives(None, dev)
     results = []
-    names = {ONESHOT: "oneshot", TWOSHOT: "twoshot_ll", PLAIN: "twoshot_plain"}
+    if fused.nvls_rows and rank == 0:
+        print(json.dumps({"nvls_requested_rows": fused.nvls_rows}), flush=True)
+    names = {ONESHOT: "oneshot", TWOSHOT: "twoshot_ll", PLAIN: "twoshot_plain", NVLS: "nvls"}
     for H in (2048, 4096):
         fused.reserve(R, H)
+        if fused.nvls_rows and fused.nvls is None and rank == 0:
+            print(json.dumps({"nvls_unavailable": fused.nvls_error}), flush=True)
         w = torch.randn(H, device=dev).to(torch.bfloat16)
         hidden = torch.zeros(R, H, dtype=torch.bfloat16, device=dev)
         delta = (0.01 * torch.randn(R, H, device=dev)).to(torch.bfloat16)
@@ -89,8 +94,10 @@ def main():
             row = {"op": "allreduce_add_rmsnorm_mxfp8", "world": world, "rows": m, "hidden": H,
                    "auto_protocol": names[fused.protocol_for(m)]}
             calls = 50 if m <= 256 else 10
-            for proto in (ONESHOT, TWOSHOT, PLAIN):
+            for proto in (ONESHOT, TWOSHOT, PLAIN, NVLS):
                 if (proto == ONESHOT and m > FAR_ONESHOT_ROWS) or (proto == TWOSHOT and m > fused.ll_cap):
+                    continue
+                if proto == NVLS and (fused.nvls is None or m > fused.nvls["rows"]):
                     continue
                 row[f"{names[proto]}_us"] = round(1000 * _time_graph(
                     lambda: fused.allreduce_add_rmsnorm(delta, 1, H, 0, hidden, w, 1e-6, m, xq, xsf, protocol=proto),
