@@ -69,7 +69,9 @@ Coordinator::Coordinator(CoordinatorConfig cfg) : cfg_(std::move(cfg)) { layout_
 Coordinator::~Coordinator() { shutdown(); }
 
 void Coordinator::launch() {
-  const std::string name = "/zstep-" + std::to_string(getpid()) + "-" + std::to_string(g_segment_counter++);
+  const std::string name =
+      cfg_.shm_name.empty() ? "/zstep-" + std::to_string(getpid()) + "-" + std::to_string(g_segment_counter++)
+                            : (cfg_.shm_name[0] == '/' ? cfg_.shm_name : "/" + cfg_.shm_name);
   arena_ = ShmArena::create(name, layout_.total_bytes);
   auto sb = reinterpret_cast<wire::Superblock*>(arena_.base());
   sb->magic = wire::kMagic;

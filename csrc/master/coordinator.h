@@ -30,6 +30,7 @@ struct CoordinatorConfig {
   int step_timeout_ms = 120000;
   int heartbeat_timeout_ms = 5000;
   int slice_ms = 200;
+  std::string shm_name;                      // POSIX shared-memory object name (empty: unique per run)
 };
 
 class Coordinator : public engine::Backend {

@@ -139,6 +139,7 @@ void Engine::set_event_sink(kv::KvEventSink sink) {
 bool Engine::submit(Request r) {
   if (waiting_.size() >= cfg_.max_waiting) return false;
   waiting_since_[r.id] = stats_.steps;
+  waiting_at_[r.id] = std::chrono::steady_clock::now();
   waiting_.push_back(std::move(r));
   return true;
 }
@@ -147,6 +148,7 @@ bool Engine::cancel(uint64_t id) {
   for (auto it = waiting_.begin(); it != waiting_.end(); ++it) {
     if (it->id == id) {
       waiting_since_.erase(id);
+      waiting_at_.erase(id);
       waiting_.erase(it);
       return true;
     }
@@ -203,7 +205,11 @@ bool Engine::admit_one() {
     size_t oldest = 0;
     for (size_t i = 1; i < waiting_.size(); ++i)
       if (waiting_since_[waiting_[i].id] < waiting_since_[waiting_[oldest].id]) oldest = i;
-    if (stats_.steps - waiting_since_[waiting_[oldest].id] >= cfg_.starvation_steps) {
+    const uint64_t oid = waiting_[oldest].id;
+    const auto waited_ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                               std::chrono::steady_clock::now() - waiting_at_[oid]).count();
+    if (stats_.steps - waiting_since_[oid] >= cfg_.starvation_steps ||
+        (cfg_.starvation_ms > 0 && waited_ms >= (long long)cfg_.starvation_ms)) {
       pick = oldest;
     } else {
       for (size_t i = 1; i < waiting_.size(); ++i)
@@ -218,6 +224,7 @@ bool Engine::admit_one() {
     // Can never fit: fail this request (the caller reports it).
     auto s = make_seq(std::move(r));
     waiting_since_.erase(s->req.id);
+    waiting_at_.erase(s->req.id);
     waiting_.erase(waiting_.begin() + pick);
     s->slot = -1;
     error_ = "request " + std::to_string(s->req.id) + " exceeds the model length or KV capacity";
@@ -240,6 +247,7 @@ bool Engine::admit_one() {
   auto own = pages_.allocate(own_needed);
   auto seq = make_seq(std::move(r));
   waiting_since_.erase(seq->req.id);
+  waiting_at_.erase(seq->req.id);
   waiting_.erase(waiting_.begin() + pick);
   seq->slot = free_slots_.back();
   free_slots_.pop_back();
@@ -266,18 +274,38 @@ std::unique_ptr<Engine::Seq> Engine::make_seq(Request&& r) {
 
 // ---------------------------------------------------------------------------- drafting
 std::vector<int32_t> Engine::ngram_drafts(const Seq& s) const {
-  // Most recent earlier occurrence of the last n tokens; propose what followed it.
-  const size_t n = cfg_.ngram_n, k = cfg_.num_spec_tokens;
+  // Longest suffix first (ngram_max down to ngram_min tokens): its most recent earlier
+  // occurrence proposes the up to k tokens that followed it.
   const auto& t = s.tokens;
-  if (t.size() <= n || k == 0) return {};
-  for (size_t start = t.size() - n; start-- > 0;) {
-    if (std::equal(t.begin() + start, t.begin() + start + n, t.end() - n)) {
-      std::vector<int32_t> d;
-      for (size_t j = start + n; j < t.size() - n + n && d.size() < k && j < t.size(); ++j) d.push_back(t[j]);
-      return d;
+  const size_t k = cfg_.num_spec_tokens, lo = std::max<uint32_t>(1, cfg_.ngram_min);
+  if (t.size() < 2 || k == 0) return {};
+  const size_t hi = std::min<size_t>(cfg_.ngram_max, t.size() - 1);
+  for (size_t n = hi; n >= lo; --n) {
+    for (size_t start = t.size() - n; start-- > 0;) {
+      if (std::equal(t.begin() + start, t.begin() + start + n, t.end() - n)) {
+        const size_t b = start + n, e = std::min(b + k, t.size());
+        return std::vector<int32_t>(t.begin() + b, t.begin() + e);
+      }
     }
   }
   return {};
+}
+
+uint32_t Engine::mixed_step_budget(uint32_t decode_rows) const {
+  const uint32_t top = cfg_.max_step_tokens;
+  if (cfg_.max_mixed_step_tokens == 0 || decode_rows == 0) return top;
+  const uint32_t base = std::min(std::max(cfg_.max_mixed_step_tokens, decode_rows + 1), top);
+  if (!cfg_.dynamic_prefill_budget || base >= top) return base;
+  const uint64_t lo = cfg_.backlog_low_tokens, hi = std::max(cfg_.backlog_high_tokens, cfg_.backlog_low_tokens);
+  uint64_t backlog = 0;
+  for (const auto& kvp : running_) backlog += kvp.second->prompt_len - std::min(kvp.second->computed, kvp.second->prompt_len);
+  for (const auto& r : waiting_) {
+    if (backlog >= hi) break;
+    backlog += r.prompt.size();
+  }
+  if (backlog <= lo) return base;
+  if (backlog >= hi || hi == lo) return top;
+  return uint32_t(std::min<uint64_t>(top, base + (uint64_t)(top - base) * (backlog - lo) / (hi - lo)));
 }
 
 // ---------------------------------------------------------------------------- staging
@@ -349,7 +377,13 @@ void Engine::stage(StepPlan& p, std::vector<Seq*>& order) {
     budget -= uint32_t(rows.size());
     add_seq(s, uint32_t(rows.size()), rows.data(), pos, true, spec_w);
   }
-  // 2. Prefill chunks, in admission (slot) order.
+  // 2. Prefill chunks, in admission (slot) order, within the mixed-step budget when the
+  // step also carries decode rows (speculative steps keep the full step budget).
+  if (cfg_.spec_method == "none" && !order.empty()) {
+    const uint32_t used = cfg_.max_step_tokens - budget;
+    const uint32_t cap = mixed_step_budget(uint32_t(order.size()));
+    budget = cap > used ? std::min(budget, cap - used) : 0;
+  }
   for (auto& kvp : running_) {
     Seq* s = kvp.second.get();
     if (s->computed >= s->prompt_len || budget == 0) continue;

@@ -22,6 +22,7 @@
 
 #include <stdint.h>
 
+#include <chrono>
 #include <deque>
 #include <functional>
 #include <map>
@@ -83,11 +84,25 @@ struct Config {
   bool recurrent_state = false;        // model keeps per-slot recurrent state (GDN)
   uint32_t num_ckpt_slots = 0;         // recurrent checkpoint slots (after the live slots)
   std::string prefill_policy = "fifo"; // "fifo" | "srpt"
+  // SRPT starvation cap: the oldest waiting request is admitted next (and holds back shorter
+  // ones until it fits) once it has waited this many engine steps or this many ms (0: off).
   uint32_t starvation_steps = 64;
+  uint32_t starvation_ms = 60000;
+  // Mixed steps (decode rows + prefill chunks): at most max(max_mixed_step_tokens, decodes + 1)
+  // rows (0: off, max_step_tokens).  With dynamic_prefill_budget the cap ramps linearly to
+  // max_step_tokens as the prefill backlog (uncomputed prompt tokens of running and waiting
+  // requests) grows from backlog_low_tokens to backlog_high_tokens.
+  uint32_t max_mixed_step_tokens = 0;
+  bool dynamic_prefill_budget = false;
+  uint32_t backlog_low_tokens = 2048;
+  uint32_t backlog_high_tokens = 16384;
   uint32_t max_waiting = 4096;
   std::string spec_method = "none";    // "none" | "ngram" | "mtp" | "dspark" (last two: drafts from the worker)
   uint32_t num_spec_tokens = 0;
-  uint32_t ngram_n = 3;
+  // n-gram drafts: the longest suffix of ngram_max..ngram_min tokens that occurred earlier
+  // proposes the tokens that followed its most recent earlier occurrence.
+  uint32_t ngram_min = 2;
+  uint32_t ngram_max = 5;
   std::string kv_hash_seed = "42";
   uint32_t dram_blocks = 0;            // host DRAM tier blocks (0: off); needs APC, 1 page per node,
                                        // and a model without recurrent state
@@ -169,6 +184,9 @@ class Engine {
   std::string error() const { return error_; }
   EngineStats stats() const;
   const Config& config() const { return cfg_; }
+  // Prefill chunk size for the steps staged from now on (the parity check's unchunked and
+  // chunked passes run on one engine).
+  void set_max_prefill_chunk(uint32_t n) { cfg_.max_prefill_chunk = n ? n : 1; }
   kv::PrefixTree* prefix_tree() { return tree_.get(); }
   size_t free_pages() const { return pages_.available(); }
   size_t free_ckpt_slots() const { return ckpt_slots_.available(); }
@@ -210,6 +228,8 @@ class Engine {
   std::unique_ptr<kv::DramTier> dram_;
   std::deque<Request> waiting_;
   std::map<uint64_t, uint64_t> waiting_since_;  // request id -> step when queued
+  std::map<uint64_t, std::chrono::steady_clock::time_point> waiting_at_;  // request id -> time queued
+  uint32_t mixed_step_budget(uint32_t decode_rows) const;
   std::vector<int32_t> free_slots_;
   std::map<int32_t, std::unique_ptr<Seq>> running_;  // by request slot
   std::deque<Inflight> inflight_;                     // published, not yet processed steps

@@ -179,11 +179,6 @@ void PrefixTree::set_event_sink(KvEventSink sink) {
 
 namespace {
 
-const std::map<std::vector<int32_t>, uint64_t>& children_of(const TreeState& s, uint64_t parent) {
-  if (parent == 0) return s.roots;
-  return s.nodes.at(parent).children;
-}
-
 std::map<std::vector<int32_t>, uint64_t>& children_of(TreeState& s, uint64_t parent) {
   if (parent == 0) return s.roots;
   return s.nodes.at(parent).children;

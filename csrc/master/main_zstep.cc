@@ -18,6 +18,7 @@
 #include <time.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <fstream>
@@ -61,17 +62,26 @@ const char* kServeUsage =
     "  --max-step-tokens N          Max tokens per step (default 4096)\n"
     "  --max-prefill-chunk N        Max prefill chunk (default 2048)\n"
     "  --page-block-tokens N        KV page size (default 16)\n"
-    "  --num-kv-pages N             KV pages per GPU (default 32768)\n"
+    "  --num-kv-pages N             KV pages per GPU (default: --gpu-memory-utilization x 32768 / 0.95)\n"
+    "  --gpu-memory-utilization F   KV page calibration factor in (0, 1] (default 0.95)\n"
+    "  --kv-cache-dtype auto|bf16   KV cache dtype (the caches are bf16; fp8 is rejected)\n"
     "  --tokenizer-mode auto|chatml|deepseek\n"
     "  --enable-prefix-caching | --no-enable-prefix-caching   (default on)\n"
     "  --apc-node-pages N           Pages per prefix-cache node (default 8)\n"
+    "  --apc-gdn-node-tokens 64|128 Prefix-cache node size in tokens for recurrent (GDN) models\n"
     "  --num-ckpt-slots N           Recurrent-state checkpoint slots (default 64 with APC)\n"
     "  --dram-kv-blocks N           Host DRAM tier of the prefix cache, in blocks (default 0 = off;\n"
     "                               attention-only models; implies --apc-node-pages 1)\n"
-    "  --dram-loading-area-ratio R  Share of HBM pages kept free for DRAM reloads (default 0.10)\n"
+    "  --dram-loading-area-ratio R  Share of HBM pages kept free for DRAM reloads (default 0.10;\n"
+    "                               alias --kv-loading-area-ratio)\n"
     "  --in-flight-depth 0|1        Publish the next decode step before processing the current one (default 0)\n"
     "  --max-waiting-requests N     Bounded waiting queue (default 1024)\n"
     "  --prefill-policy srpt|fifo   (default srpt)\n"
+    "  --prefill-starvation-cap-ms N  Wait after which the oldest prompt preempts SRPT (default 60000, 0 = off)\n"
+    "  --max-mixed-step-tokens N    Cap of steps mixing decode rows and prefill chunks (default 3072 for\n"
+    "                               DeepSeek-style models, 0 = off)\n"
+    "  --dynamic-prefill-budget | --no-dynamic-prefill-budget   Ramp that cap to --max-step-tokens as the\n"
+    "                               prefill backlog grows from 2048 to 16384 tokens (default on with srpt)\n"
     "  --drain-timeout-secs N       SIGTERM drain grace period (default 30)\n"
     "  --python PATH                Python for workers (default: python3)\n"
     "  --worker-root PATH           Directory containing the zstep_b200 package\n"
@@ -79,6 +89,10 @@ const char* kServeUsage =
     "  --step-timeout-secs N        Per-step timeout (default 300)\n"
     "  --speculative-method none|ngram|mtp|dspark\n"
     "  --num-speculative-tokens K   Draft tokens per verify step 1..7\n"
+    "  --prompt-lookup-max N        Longest n-gram suffix tried for ngram drafts (default 5)\n"
+    "  --prompt-lookup-min N        Shortest n-gram suffix tried (default 2)\n"
+    "  --allreduce-blocks N / --allreduce-threads N   Accepted for compatibility; the NVLink\n"
+    "                               collectives size their own grids\n"
     "  --kv-events-endpoint ADDR    Publish prefix-cache events: tcp://host:port (ZMTP PUB) or file://path\n"
     "  --kv-events-topic TOPIC      Topic of published events (default <served-model-name>/0)\n"
     "  --mock                       Scripted backend instead of workers (no GPU)\n";
@@ -90,7 +104,24 @@ const char* kRunUsage =
     "  --prompt-ids 1,2,3           Generate from these token ids\n"
     "  --prompt TEXT                Generate from this text (chat template applied)\n"
     "  --max-tokens N               Tokens to generate (default 32)\n"
-    "  --verify-greedy-json PATH    {\"prompts\": [[ids]], \"expected\": [[ids]]}: exit 1 on mismatch\n"
+    "  --verify-greedy-json PATH    {\"prompts\": [[ids]], \"expected\": [[ids]]}: exit 1 on mismatch; or the\n"
+    "                               multi-case form {\"cases\": [{name, prompt_token_ids, max_tokens,\n"
+    "                               expected_greedy_token_ids, top2_steps?, require_exact?,\n"
+    "                               max_mismatch_margin?}]}: each case alone, all batched, all chunked\n"
+    "  --verify-output-json PATH    Also write the parity report to PATH\n"
+    "  --require-exact-greedy BOOL  Multi-case form: fail on any token difference (default false)\n"
+    "  --require-exact-cases LIST   Multi-case form: cases that must match exactly\n"
+    "  --max-greedy-mismatch-margin F  Multi-case form: fail when a run diverges at a step whose\n"
+    "                               top-1 minus top-2 logit margin exceeds F\n"
+    "  --metrics-output PATH        Also write the JSON report to PATH\n"
+    "  --warmup-prompts N           Untimed 512->64 prompts at concurrency 16 before --bench-tiers (default 0)\n"
+    "  --heartbeat-timeout-ms N     Per-worker heartbeat stall timeout (default 5000)\n"
+    "  --shm-name NAME              POSIX shared-memory object name (default: unique per run)\n"
+    "  --max-pages-per-seq N        Page-table capacity (sets --max-model-len to N x page size)\n"
+    "  --max-decoder-rows N         Decoder rows per step (= --max-step-tokens here; must not be smaller)\n"
+    "  Aliases: --max-new-tokens = --max-tokens, --repeats = --bench-repeats, --steps = --micro-steps,\n"
+    "  --hidden-size / --output-features / --router-experts / --router-top-k = --micro-*;\n"
+    "  `zstep --model-dir ...` without a subcommand is `zstep run`; tiers may be separated by ';'\n"
     "  --bench-tiers SPEC[,SPEC]    label:concurrency:prompts:input_len:output_len[:prefix_len:num_prefixes]\n"
     "                               (with prefix fields, prompt i = shared prefix i % num_prefixes + input_len ids)\n"
     "  --bench-repeats N            Interleaved repeats per tier (default 1)\n"
@@ -128,7 +159,26 @@ const std::set<std::string> kValueFlags = {
     "micro-steps", "token-counts", "in-flight-depth", "micro-hidden", "micro-features", "micro-experts", "micro-topk", "max-waiting-requests", "prefill-policy",
     "drain-timeout-secs", "python", "worker-root", "ready-timeout-secs", "step-timeout-secs", "speculative-method",
     "num-speculative-tokens", "prompt-ids", "prompt", "max-tokens", "verify-greedy-json", "bench-tiers",
-    "bench-repeats", "seed", "kv-events-endpoint", "kv-events-topic"};
+    "bench-repeats", "seed", "kv-events-endpoint", "kv-events-topic", "gpu-memory-utilization", "kv-cache-dtype",
+    "apc-gdn-node-tokens", "kv-loading-area-ratio", "prefill-starvation-cap-ms", "max-mixed-step-tokens",
+    "prompt-lookup-max", "prompt-lookup-min", "allreduce-blocks", "allreduce-threads", "max-new-tokens", "repeats",
+    "steps", "hidden-size", "output-features", "router-experts", "router-top-k", "heartbeat-timeout-ms", "shm-name",
+    "max-decoder-rows", "max-pages-per-seq", "warmup-prompts", "metrics-output", "verify-output-json",
+    "require-exact-greedy", "require-exact-cases", "max-greedy-mismatch-margin"};
+
+// Flag names of the reference's `zstep run` that mean the same as one of ours.
+void apply_aliases(Args* a) {
+  static const std::pair<const char*, const char*> kAlias[] = {
+      {"max-new-tokens", "max-tokens"}, {"repeats", "bench-repeats"},       {"steps", "micro-steps"},
+      {"hidden-size", "micro-hidden"},  {"output-features", "micro-features"}, {"router-experts", "micro-experts"},
+      {"router-top-k", "micro-topk"}};
+  for (const auto& [from, to] : kAlias) {
+    auto it = a->kv.find(from);
+    if (it == a->kv.end()) continue;
+    if (!a->kv.count(to)) a->kv[to] = it->second;
+    a->kv.erase(it);
+  }
+}
 // Model families without per-slot recurrent state: DeepSeek-style presets, or an HF
 // directory whose config.json has MLA fields.
 bool attention_only_model(const std::string& model) {
@@ -144,7 +194,8 @@ bool attention_only_model(const std::string& model) {
 }
 
 const std::set<std::string> kBoolFlags = {"allow-remote-metrics", "no-allow-remote-metrics", "enable-prefix-caching",
-                                          "no-enable-prefix-caching", "mock", "help"};
+                                          "no-enable-prefix-caching", "dynamic-prefill-budget",
+                                          "no-dynamic-prefill-budget", "mock", "help"};
 
 bool parse_args(int argc, char** argv, int start, Args* a, std::string* err) {
   for (int i = start; i < argc; ++i) {
@@ -234,8 +285,36 @@ bool build_engine(const Args& a, Built* b, std::string* err) {
   c.max_step_tokens = (uint32_t)a.num("max-step-tokens", 4096);
   c.max_prefill_chunk = (uint32_t)a.num("max-prefill-chunk", 2048);
   c.page_size = (uint32_t)a.num("page-block-tokens", 16);
-  c.num_pages = (uint32_t)a.num("num-kv-pages", 32768);
+  double util = 0.95;
+  if (a.has("gpu-memory-utilization")) {
+    char* end = nullptr;
+    util = strtod(a.get("gpu-memory-utilization").c_str(), &end);
+    if (end == a.get("gpu-memory-utilization").c_str() || *end || !(util > 0.0) || util > 1.0) {
+      *err = "--gpu-memory-utilization must be in (0, 1]";
+      return false;
+    }
+  }
+  // Calibration as a scale of the default page count (32768 pages x 16 tokens of bf16 KV
+  // fit beside the weights on one 180 GB GPU at 0.95).
+  c.num_pages = (uint32_t)a.num("num-kv-pages", std::max<long>(128, std::lround(util / 0.95 * 32768.0)));
+  const std::string kv_dtype = a.get("kv-cache-dtype", "auto");
+  if (kv_dtype != "auto" && kv_dtype != "bf16" && kv_dtype != "bfloat16") {
+    *err = "--kv-cache-dtype `" + kv_dtype + "` is not supported: the KV caches are bf16 (pass auto or bf16)";
+    return false;
+  }
   c.max_model_len = (uint32_t)a.num("max-model-len", 32768);
+  if (a.has("max-pages-per-seq") && !a.has("max-model-len")) {
+    const long mp = a.num("max-pages-per-seq", 1);
+    if (mp < 1) {
+      *err = "--max-pages-per-seq must be >= 1";
+      return false;
+    }
+    c.max_model_len = uint32_t(mp) * c.page_size;
+  }
+  if (a.has("max-decoder-rows") && a.num("max-decoder-rows", 0) < (long)c.max_step_tokens) {
+    *err = "--max-decoder-rows must be >= --max-step-tokens (a step's rows are its tokens here)";
+    return false;
+  }
   c.prefix_caching = !a.has("no-enable-prefix-caching");
   c.dram_blocks = (uint32_t)a.num("dram-kv-blocks", 0);
   c.in_flight_depth = (uint32_t)a.num("in-flight-depth", 0);
@@ -246,8 +325,17 @@ bool build_engine(const Args& a, Built* b, std::string* err) {
   c.pages_per_node = (uint32_t)a.num("apc-node-pages", c.dram_blocks ? 1 : 8);
   // Attention-only models (the DeepSeek-style family) keep no per-slot recurrent state.
   c.recurrent_state = !attention_only_model(a.get("model", dir));
+  if (a.has("apc-gdn-node-tokens")) {
+    const long t = a.num("apc-gdn-node-tokens", 128);
+    if ((t != 64 && t != 128) || t % c.page_size) {
+      *err = "--apc-gdn-node-tokens must be 64 or 128 (and a multiple of --page-block-tokens)";
+      return false;
+    }
+    if (c.recurrent_state && !a.has("apc-node-pages")) c.pages_per_node = uint32_t(t / c.page_size);
+  }
   c.num_ckpt_slots = (uint32_t)a.num("num-ckpt-slots", c.prefix_caching && c.recurrent_state ? 64 : 0);
   if (a.has("dram-loading-area-ratio")) c.dram_loading_area = strtod(a.get("dram-loading-area-ratio").c_str(), nullptr);
+  if (a.has("kv-loading-area-ratio")) c.dram_loading_area = strtod(a.get("kv-loading-area-ratio").c_str(), nullptr);
   if (c.dram_blocks > 0) {
     if (!c.prefix_caching || c.pages_per_node != 1 || c.recurrent_state) {
       *err = "--dram-kv-blocks needs prefix caching, --apc-node-pages 1 and an attention-only model";
@@ -259,9 +347,35 @@ bool build_engine(const Args& a, Built* b, std::string* err) {
     }
   }
   c.prefill_policy = a.get("prefill-policy", "srpt");
+  const long starve = a.num("prefill-starvation-cap-ms", 60000);
+  const long mixed = a.num("max-mixed-step-tokens", c.recurrent_state ? 0 : 3072);
+  if (starve < 0 || mixed < 0) {
+    *err = "--prefill-starvation-cap-ms and --max-mixed-step-tokens must be >= 0";
+    return false;
+  }
+  // FIFO keeps the plain arrival order: no starvation promotion, a fixed mixed-step cap.
+  c.starvation_ms = c.prefill_policy == "srpt" ? uint32_t(starve) : 0;
+  c.max_mixed_step_tokens = uint32_t(mixed);
+  c.dynamic_prefill_budget = a.has("dynamic-prefill-budget") ||
+                             (c.prefill_policy == "srpt" && !a.has("no-dynamic-prefill-budget"));
   c.max_waiting = (uint32_t)a.num("max-waiting-requests", 1024);
   c.spec_method = a.get("speculative-method", "none");
   c.num_spec_tokens = (uint32_t)a.num("num-speculative-tokens", c.spec_method == "none" ? 0 : 3);
+  const long la_max = a.num("prompt-lookup-max", 5), la_min = a.num("prompt-lookup-min", 2);
+  if (la_min < 1 || la_max < la_min) {
+    *err = "--prompt-lookup-min must be >= 1 and <= --prompt-lookup-max";
+    return false;
+  }
+  c.ngram_min = uint32_t(la_min);
+  c.ngram_max = uint32_t(la_max);
+  for (const char* k : {"allreduce-blocks", "allreduce-threads"})
+    if (a.has(k)) {
+      if (a.num(k, 1) < 1) {
+        *err = std::string("--") + k + " must be >= 1";
+        return false;
+      }
+      fprintf(stderr, "zstep: --%s accepted and ignored: the NVLink collectives size their own grids\n", k);
+    }
   if (c.max_step_tokens < c.max_seqs) {
     *err = "--max-step-tokens must be >= --max-seqs";
     return false;
@@ -328,6 +442,8 @@ bool build_engine(const Args& a, Built* b, std::string* err) {
     cc.env["MASTER_ADDR"] = "127.0.0.1";
     cc.env["MASTER_PORT"] = std::to_string(29500 + (getpid() % 20000));
     cc.ready_timeout_ms = (int)a.num("ready-timeout-secs", 1800) * 1000;
+    cc.heartbeat_timeout_ms = (int)a.num("heartbeat-timeout-ms", 5000);
+    cc.shm_name = a.get("shm-name", "");
     cc.step_timeout_ms = (int)a.num("step-timeout-secs", 300) * 1000;
     b->coord = std::make_shared<Coordinator>(cc);
     b->coord->launch();
@@ -575,6 +691,247 @@ json::Value run_tier(engine::Engine& e, const Tier& t, uint64_t seed, int32_t vo
   return r;
 }
 
+// Writes a report to stdout and, with --metrics-output, to that file too.
+void emit(const Args& a, const json::Value& v) {
+  const std::string text = v.dump();
+  printf("%s\n", text.c_str());
+  if (a.has("metrics-output")) {
+    std::ofstream f(a.get("metrics-output"));
+    f << text << "\n";
+  }
+}
+
+// One greedy generation pass: every prompt submitted at once (ignore EOS), with the top-2
+// log-probabilities of each step; margin = top-1 minus top-2 (NaN when not reported).
+struct GreedyRun {
+  std::vector<int32_t> tokens;
+  std::vector<double> margin;
+};
+
+std::vector<GreedyRun> greedy_pass(engine::Engine& e, const std::vector<std::vector<int32_t>>& prompts,
+                                   const std::vector<uint32_t>& lens, uint64_t id0, std::string* err) {
+  for (size_t i = 0; i < prompts.size(); ++i) {
+    engine::Request r;
+    r.id = id0 + i;
+    r.prompt = prompts[i];
+    r.max_tokens = lens[i];
+    r.ignore_eos = true;
+    r.sampling.logprobs = 2;
+    e.submit(r);
+  }
+  std::vector<GreedyRun> out(prompts.size());
+  while (e.has_work()) {
+    for (auto& ev : e.step()) {
+      if (ev.request_id < id0 || ev.request_id >= id0 + prompts.size()) continue;
+      GreedyRun& g = out[ev.request_id - id0];
+      for (size_t j = 0; j < ev.tokens.size(); ++j) {
+        g.tokens.push_back(ev.tokens[j]);
+        const bool has2 = j < ev.top_logprobs.size() && ev.top_logprobs[j].size() >= 2;
+        g.margin.push_back(has2 ? (double)ev.top_logprobs[j][0].second - ev.top_logprobs[j][1].second : NAN);
+      }
+    }
+    if (e.poisoned()) {
+      *err = e.error();
+      break;
+    }
+  }
+  return out;
+}
+
+json::Value match_report(const std::vector<int32_t>& want, const GreedyRun& got) {
+  size_t first = want.size(), same = 0;
+  for (size_t i = 0; i < want.size(); ++i) {
+    const bool eq = i < got.tokens.size() && got.tokens[i] == want[i];
+    same += eq ? 1 : 0;
+    if (!eq && first == want.size()) first = i;
+  }
+  json::Value r = json::Value::object();
+  r.set("exact_prefix_match_tokens", (int64_t)first);
+  r.set("exact_token_matches", (int64_t)same);
+  r.set("total_tokens", (int64_t)want.size());
+  r.set("exact_token_match_rate", want.empty() ? 1.0 : (double)same / (double)want.size());
+  r.set("all_matched", first == want.size());
+  if (first < want.size()) {
+    r.set("first_mismatch_token_index", (int64_t)first);
+    if (first < got.margin.size() && !std::isnan(got.margin[first]))
+      r.set("zstep_top1_minus_top2_margin", got.margin[first]);
+  }
+  return r;
+}
+
+// First step where two passes differ: {token_index, left/right tokens and margins}, or null.
+json::Value pair_mismatch(const char* ln, const GreedyRun& l, const char* rn, const GreedyRun& r, double* margin) {
+  *margin = NAN;
+  const size_t n = std::max(l.tokens.size(), r.tokens.size());
+  for (size_t i = 0; i < n; ++i) {
+    const int32_t a = i < l.tokens.size() ? l.tokens[i] : -1, b = i < r.tokens.size() ? r.tokens[i] : -1;
+    if (a == b) continue;
+    json::Value m = json::Value::object();
+    m.set("token_index", (int64_t)i);
+    m.set("left_mode", std::string(ln));
+    m.set("right_mode", std::string(rn));
+    m.set("left_token", (int64_t)a);
+    m.set("right_token", (int64_t)b);
+    const double ml = i < l.margin.size() ? l.margin[i] : NAN, mr = i < r.margin.size() ? r.margin[i] : NAN;
+    if (!std::isnan(ml)) m.set("left_margin", ml);
+    if (!std::isnan(mr)) m.set("right_margin", mr);
+    *margin = std::isnan(ml) ? mr : std::isnan(mr) ? ml : std::max(ml, mr);
+    return m;
+  }
+  return json::Value();
+}
+
+bool parse_bool(const std::string& s, bool* out) {
+  if (s == "true" || s == "1" || s == "yes") return (*out = true), true;
+  if (s == "false" || s == "0" || s == "no") return (*out = false), true;
+  return false;
+}
+
+// The multi-case greedy parity check: each case alone and unchunked, all cases batched and
+// unchunked, all cases batched with the configured prefill chunk; every pass against the
+// expected tokens and against each other, then the gates.  Returns the exit code.
+int verify_cases(const Args& a, engine::Engine& e, const json::Value& v, const std::string& root) {
+  struct Case {
+    std::string name;
+    std::vector<int32_t> prompt, want;
+    uint32_t max_tokens = 0;
+    bool require_exact = false;
+    double margin_limit = NAN;
+  };
+  std::vector<Case> cases;
+  for (const auto& c : v.get("cases").items()) {
+    Case k;
+    k.name = c.get("name").as_string();
+    for (const auto& t : c.get("prompt_token_ids").items()) k.prompt.push_back((int32_t)t.as_int());
+    for (const auto& t : c.get("expected_greedy_token_ids").items()) k.want.push_back((int32_t)t.as_int());
+    k.max_tokens = (uint32_t)c.get("max_tokens").as_int();
+    k.require_exact = c.get("require_exact").is_bool() && c.get("require_exact").as_bool();
+    if (c.get("max_mismatch_margin").is_number()) k.margin_limit = c.get("max_mismatch_margin").as_double();
+    const size_t top2 = c.get("top2_steps").is_array() ? c.get("top2_steps").size() : 0;
+    std::string bad;
+    if (k.prompt.empty() || k.max_tokens == 0) bad = "has an empty prompt or zero output length";
+    else if (k.want.size() != k.max_tokens) bad = "expected token count differs from max_tokens";
+    else if (top2 && top2 != k.max_tokens) bad = "has a top2_steps count that differs from max_tokens";
+    if (!bad.empty()) {
+      fprintf(stderr, "zstep run: case `%s` %s\n", k.name.c_str(), bad.c_str());
+      return 2;
+    }
+    cases.push_back(std::move(k));
+  }
+  if (cases.empty()) {
+    fprintf(stderr, "zstep run: the greedy reference has no cases\n");
+    return 2;
+  }
+  bool exact_all = false;
+  if (a.has("require-exact-greedy") && !parse_bool(a.get("require-exact-greedy"), &exact_all)) {
+    fprintf(stderr, "zstep run: --require-exact-greedy takes true or false\n");
+    return 2;
+  }
+  double margin_flag = NAN;
+  if (a.has("max-greedy-mismatch-margin")) margin_flag = strtod(a.get("max-greedy-mismatch-margin").c_str(), nullptr);
+  std::vector<std::vector<int32_t>> prompts;
+  std::vector<uint32_t> lens;
+  for (const auto& k : cases) {
+    prompts.push_back(k.prompt);
+    lens.push_back(k.max_tokens);
+  }
+  std::string err;
+  const uint32_t chunk = e.config().max_prefill_chunk;
+  e.set_max_prefill_chunk(UINT32_MAX);
+  uint64_t id = 1;
+  std::vector<GreedyRun> single;
+  for (size_t i = 0; i < cases.size() && err.empty(); ++i) {
+    single.push_back(greedy_pass(e, {prompts[i]}, {lens[i]}, id, &err)[0]);
+    id += 1;
+  }
+  std::vector<GreedyRun> batched, chunked;
+  if (err.empty()) batched = greedy_pass(e, prompts, lens, id, &err);
+  id += cases.size();
+  e.set_max_prefill_chunk(chunk);
+  if (err.empty()) chunked = greedy_pass(e, prompts, lens, id, &err);
+  json::Value rep = json::Value::object();
+  rep.set("git_sha", git_sha(root));
+  rep.set("vllm_version", v.get("vllm_version").is_string() ? v.get("vllm_version").as_string() : std::string());
+  rep.set("max_prefill_chunk", (int64_t)chunk);
+  if (!err.empty()) {
+    rep.set("error", err);
+    emit(a, rep);
+    return 1;
+  }
+  bool all = true, b_vs_s = true, c_vs_b = true;
+  std::string gate;
+  json::Value cv = json::Value::array();
+  std::set<std::string> names;
+  for (size_t i = 0; i < cases.size(); ++i) {
+    const Case& k = cases[i];
+    names.insert(k.name);
+    const json::Value ms = match_report(k.want, single[i]), mb = match_report(k.want, batched[i]),
+                      mc = match_report(k.want, chunked[i]);
+    double m_sb, m_bc;
+    const json::Value sb = pair_mismatch("single", single[i], "batched", batched[i], &m_sb);
+    const json::Value bc = pair_mismatch("batched", batched[i], "chunked", chunked[i], &m_bc);
+    b_vs_s = b_vs_s && sb.is_null();
+    c_vs_b = c_vs_b && bc.is_null();
+    const bool ok = ms.get("all_matched").as_bool() && mb.get("all_matched").as_bool() &&
+                    mc.get("all_matched").as_bool() && sb.is_null() && bc.is_null();
+    all = all && ok;
+    json::Value r = json::Value::object();
+    r.set("name", k.name);
+    r.set("all_matched", ok);
+    r.set("single_match", ms);
+    r.set("batched_match", mb);
+    r.set("chunked_match", mc);
+    r.set("single_vs_batched_first_mismatch", sb);
+    r.set("batched_vs_chunked_first_mismatch", bc);
+    for (const auto& [key, run] : {std::pair<const char*, const GreedyRun*>{"single_generated_token_ids", &single[i]},
+                                   {"batched_generated_token_ids", &batched[i]},
+                                   {"chunked_generated_token_ids", &chunked[i]}}) {
+      json::Value t = json::Value::array();
+      for (int32_t x : run->tokens) t.push((int64_t)x);
+      r.set(key, t);
+    }
+    cv.push(r);
+    if (!gate.empty()) continue;
+    if (k.require_exact && !ok) gate = "case `" + k.name + "` had token mismatches (reference require_exact=true)";
+    const double limit = std::isnan(margin_flag) ? k.margin_limit : margin_flag;
+    if (gate.empty() && !std::isnan(limit)) {
+      const json::Value& m = ms.get("zstep_top1_minus_top2_margin");
+      if (m.is_number() && m.as_double() > limit)
+        gate = "case `" + k.name + "` diverged from the reference with margin " + std::to_string(m.as_double());
+      for (double pm : {m_sb, m_bc})
+        if (gate.empty() && !std::isnan(pm) && pm > limit)
+          gate = "case `" + k.name + "` diverged between passes with margin " + std::to_string(pm);
+    }
+  }
+  if (gate.empty() && exact_all && !all) gate = "greedy parity report had token mismatches (--require-exact-greedy=true)";
+  if (gate.empty() && a.has("require-exact-cases")) {
+    std::stringstream ss(a.get("require-exact-cases"));
+    std::string name;
+    while (gate.empty() && std::getline(ss, name, ',')) {
+      if (name.empty()) continue;
+      if (!names.count(name)) {
+        gate = "--require-exact-cases names unknown case `" + name + "`";
+        break;
+      }
+      for (const auto& c : cv.items())
+        if (c.get("name").as_string() == name && !c.get("all_matched").as_bool())
+          gate = "case `" + name + "` had token mismatches (--require-exact-cases)";
+    }
+  }
+  rep.set("all_matched", all);
+  rep.set("batched_vs_single_exact_match", b_vs_s);
+  rep.set("chunked_vs_unchunked_exact_match", c_vs_b);
+  rep.set("cases", cv);
+  rep.set("gate", gate.empty() ? std::string("ok") : gate);
+  emit(a, rep);
+  if (a.has("verify-output-json")) {
+    std::ofstream f(a.get("verify-output-json"));
+    f << rep.dump() << "\n";
+  }
+  if (!gate.empty()) fprintf(stderr, "zstep run: %s\n", gate.c_str());
+  return gate.empty() ? 0 : 1;
+}
+
 int cmd_run(const Args& a) {
   if (a.has("help")) {
     fputs(kRunUsage, stdout);
@@ -662,7 +1019,7 @@ int cmd_run(const Args& a) {
     report.set("world_size", (int64_t)a.num("world-size", 1));
     report.set("provenance", provenance(root));
     if (!err.empty()) report.set("error", err);
-    printf("%s\n", report.dump().c_str());
+    emit(a, report);
     if (b.coord) b.coord->shutdown();
     return err.empty() && rc == 0 ? 0 : 1;
   }
@@ -674,6 +1031,11 @@ int cmd_run(const Args& a) {
     if (!json::parse(ss.str(), &v, &err)) {
       fprintf(stderr, "zstep run: bad --verify-greedy-json: %s\n", err.c_str());
       return 2;
+    }
+    if (v.has("cases")) {
+      const int code = verify_cases(a, e, v, root);
+      if (b.coord) b.coord->shutdown();
+      return code;
     }
     const auto& prompts = v.get("prompts");
     const auto& expected = v.get("expected");
@@ -706,11 +1068,17 @@ int cmd_run(const Args& a) {
     json::Value root_v = json::Value::object();
     root_v.set("verify_greedy", rep);
     root_v.set("mismatches", mismatches);
-    printf("%s\n", root_v.dump().c_str());
+    emit(a, root_v);
+    if (a.has("verify-output-json")) {
+      std::ofstream vf(a.get("verify-output-json"));
+      vf << root_v.dump() << "\n";
+    }
     rc = (mismatches || !err.empty()) ? 1 : 0;
   } else if (a.has("bench-tiers")) {
     std::vector<Tier> tiers;
-    std::stringstream ss(a.get("bench-tiers"));
+    std::string specs = a.get("bench-tiers");
+    std::replace(specs.begin(), specs.end(), ';', ',');  // the reference separates tiers with ';'
+    std::stringstream ss(specs);
     std::string spec;
     while (std::getline(ss, spec, ',')) {
       std::vector<std::string> f;
@@ -739,6 +1107,10 @@ int cmd_run(const Args& a) {
     }
     const int repeats = (int)a.num("bench-repeats", 1);
     const int32_t vocab = b.has_tokenizer ? (int32_t)b.tokenizer.vocab_size() : 1000;
+    if (const long w = a.num("warmup-prompts", 0); w > 0) {  // untimed, report discarded
+      Tier wt{"warmup", 16, (int)w, 512, 64};
+      run_tier(e, wt, a.num("seed", 0) + 7777, vocab, &err);
+    }
     std::map<std::string, std::vector<json::Value>> runs;
     for (int rep = 0; rep < repeats && err.empty(); ++rep)  // interleaved: tier order repeats
       for (const auto& t : tiers) runs[t.label].push_back(run_tier(e, t, a.num("seed", 0) + rep, vocab, &err));
@@ -765,7 +1137,7 @@ int cmd_run(const Args& a) {
     report.set("tiers", tv);
     report.set("provenance", provenance(root));
     if (!err.empty()) report.set("error", err);
-    printf("%s\n", report.dump().c_str());
+    emit(a, report);
     rc = err.empty() ? 0 : 1;
   } else {
     engine::Request r;
@@ -794,7 +1166,7 @@ int cmd_run(const Args& a) {
     res.set("tokens", toks);
     if (b.has_tokenizer) res.set("text", tok::sanitize_utf8(b.tokenizer.decode(out[1])));
     if (!err.empty()) res.set("error", err);
-    printf("%s\n", res.dump().c_str());
+    emit(a, res);
     rc = err.empty() ? 0 : 1;
   }
   if (b.coord) b.coord->shutdown();
@@ -808,17 +1180,20 @@ int main(int argc, char** argv) {
     printf("zstep <serve|run> [OPTIONS]\n\n%s\n%s", kServeUsage, kRunUsage);
     return argc < 2 ? 2 : 0;
   }
-  const std::string sub = argv[1];
+  // `zstep --model-dir ... --bench-tiers ...` (options first) is `zstep run`.
+  const bool implicit_run = strncmp(argv[1], "--", 2) == 0;
+  const std::string sub = implicit_run ? "run" : argv[1];
   Args a;
   std::string err;
   if (sub != "serve" && sub != "run") {
     fprintf(stderr, "zstep: unknown subcommand `%s` (serve | run)\n", sub.c_str());
     return 2;
   }
-  if (!parse_args(argc, argv, 2, &a, &err)) {
+  if (!parse_args(argc, argv, implicit_run ? 1 : 2, &a, &err)) {
     fprintf(stderr, "zstep %s: %s\n\n%s", sub.c_str(), err.c_str(), sub == "serve" ? kServeUsage : kRunUsage);
     return 2;
   }
+  apply_aliases(&a);
   try {
     return sub == "serve" ? cmd_serve(a) : cmd_run(a);
   } catch (const std::exception& ex) {

@@ -256,10 +256,16 @@ PYBIND11_MODULE(_master, m) {
       .def_readwrite("num_ckpt_slots", &engine::Config::num_ckpt_slots)
       .def_readwrite("prefill_policy", &engine::Config::prefill_policy)
       .def_readwrite("starvation_steps", &engine::Config::starvation_steps)
+      .def_readwrite("starvation_ms", &engine::Config::starvation_ms)
+      .def_readwrite("max_mixed_step_tokens", &engine::Config::max_mixed_step_tokens)
+      .def_readwrite("dynamic_prefill_budget", &engine::Config::dynamic_prefill_budget)
+      .def_readwrite("backlog_low_tokens", &engine::Config::backlog_low_tokens)
+      .def_readwrite("backlog_high_tokens", &engine::Config::backlog_high_tokens)
       .def_readwrite("max_waiting", &engine::Config::max_waiting)
       .def_readwrite("spec_method", &engine::Config::spec_method)
       .def_readwrite("num_spec_tokens", &engine::Config::num_spec_tokens)
-      .def_readwrite("ngram_n", &engine::Config::ngram_n)
+      .def_readwrite("ngram_min", &engine::Config::ngram_min)
+      .def_readwrite("ngram_max", &engine::Config::ngram_max)
       .def_readwrite("kv_hash_seed", &engine::Config::kv_hash_seed)
       .def_readwrite("dram_blocks", &engine::Config::dram_blocks)
       .def_readwrite("dram_loading_area", &engine::Config::dram_loading_area)

@@ -133,3 +133,79 @@ def test_micro_steps_control_plane_benchmark():
     tiers = rep["micro_steps"]
     assert [t["token_count"] for t in tiers] == [4, 16]
     assert all(t["steps"] == 12 and t["steps_per_s"] > 0 and t["p99_step_us"] >= t["p50_step_us"] for t in tiers)
+
+
+def test_reference_serve_flags(model_dir):
+    """Every flag of the reference's `zstep serve` usage is accepted: calibration, KV dtype,
+    GDN node size, loading-area alias, starvation cap, mixed-step budget, prompt lookup and
+    the (ignored) host all-reduce grid flags; invalid values are rejected."""
+    ok = run("run", "--mock", "--model-dir", model_dir, "--prompt-ids", "5,6,7", "--max-tokens", "4",
+             "--gpu-memory-utilization", "0.5", "--kv-cache-dtype", "bf16", "--apc-gdn-node-tokens", "64",
+             "--kv-loading-area-ratio", "0.2", "--prefill-starvation-cap-ms", "1000", "--max-mixed-step-tokens",
+             "512", "--no-dynamic-prefill-budget", "--prompt-lookup-max", "4", "--prompt-lookup-min", "2",
+             "--allreduce-blocks", "8", "--allreduce-threads", "256")
+    assert ok.returncode == 0, ok.stderr
+    assert json.loads(ok.stdout)["tokens"] == mock_chain([5, 6, 7], 4, vocab_high(model_dir))
+    assert "allreduce-blocks accepted and ignored" in ok.stderr
+    bad = [("--kv-cache-dtype", "fp8", "kv-cache-dtype"), ("--gpu-memory-utilization", "1.5", "gpu-memory"),
+           ("--apc-gdn-node-tokens", "96", "apc-gdn-node-tokens"), ("--prompt-lookup-min", "7", "prompt-lookup"),
+           ("--max-mixed-step-tokens", "-1", "max-mixed-step-tokens")]
+    for flag, value, word in bad:
+        r = run("run", "--mock", "--model-dir", model_dir, "--prompt-ids", "1", flag, value)
+        assert r.returncode == 2 and word in r.stderr, (flag, value, r.stderr[-500:])
+
+
+def test_multi_case_greedy_parity(model_dir, tmp_path):
+    """The reference's parity-gate input: named cases run alone, batched and chunked; a report
+    per case and pass, and the gates (--require-exact-greedy, --require-exact-cases, per-case
+    require_exact)."""
+    high = vocab_high(model_dir)
+    prompts = {"short": [1, 2, 3, 4], "long": list(range(10, 60))}
+    cases = [{"name": n, "prompt_token_ids": p, "max_tokens": 5, "expected_greedy_token_ids": mock_chain(p, 5, high)}
+             for n, p in prompts.items()]
+    ref = tmp_path / "ref.json"
+    ref.write_text(json.dumps({"vllm_version": "x", "cases": cases}))
+    out = tmp_path / "parity.json"
+    metrics = tmp_path / "metrics.json"
+    r = run("run", "--mock", "--model-dir", model_dir, "--verify-greedy-json", str(ref), "--max-prefill-chunk", "16",
+            "--verify-output-json", str(out), "--metrics-output", str(metrics), "--require-exact-greedy", "true")
+    assert r.returncode == 0, r.stdout + r.stderr
+    rep = json.loads(out.read_text())
+    assert rep == json.loads(metrics.read_text()) == json.loads(r.stdout)
+    assert rep["all_matched"] and rep["batched_vs_single_exact_match"] and rep["chunked_vs_unchunked_exact_match"]
+    assert [c["name"] for c in rep["cases"]] == ["short", "long"] and rep["gate"] == "ok"
+    assert rep["cases"][1]["chunked_generated_token_ids"] == cases[1]["expected_greedy_token_ids"]
+    # One wrong expected token: reported; fails only under a gate.
+    cases[0]["expected_greedy_token_ids"][2] += 1
+    ref.write_text(json.dumps({"cases": cases}))
+    base = ("run", "--mock", "--model-dir", model_dir, "--verify-greedy-json", str(ref))
+    r = run(*base)
+    assert r.returncode == 0 and not json.loads(r.stdout)["all_matched"]
+    assert json.loads(r.stdout)["cases"][0]["single_match"]["first_mismatch_token_index"] == 2
+    assert run(*base, "--require-exact-greedy", "true").returncode == 1
+    assert run(*base, "--require-exact-cases", "long").returncode == 0
+    assert run(*base, "--require-exact-cases", "short").returncode == 1
+    assert run(*base, "--require-exact-cases", "nope").returncode == 1
+    cases[0]["require_exact"] = True
+    ref.write_text(json.dumps({"cases": cases}))
+    assert run(*base).returncode == 1
+    cases[0]["max_tokens"] = 4  # expected length must equal max_tokens
+    ref.write_text(json.dumps({"cases": cases}))
+    assert run(*base).returncode == 2
+
+
+def test_reference_run_spellings(model_dir):
+    """`zstep --model-dir ...` without a subcommand, the reference's flag names for the same
+    options, and ';'-separated bench tiers."""
+    r = run("--mock", "--model-dir", model_dir, "--prompt-ids", "5,6,7", "--max-new-tokens", "3")
+    assert r.returncode == 0, r.stderr
+    assert json.loads(r.stdout)["tokens"] == mock_chain([5, 6, 7], 3, vocab_high(model_dir))
+    r = run("--mock", "--model-dir", model_dir, "--bench-tiers", "a:1:2:8:4;b:2:2:8:4", "--repeats", "2",
+            "--max-seqs", "4", "--max-step-tokens", "256", "--max-pages-per-seq", "64", "--max-decoder-rows", "256",
+            "--heartbeat-timeout-ms", "4000")
+    assert r.returncode == 0, r.stderr
+    rep = json.loads(r.stdout)
+    assert [t["label"] for t in rep["tiers"]] == ["a", "b"] and all(len(t["runs"]) == 2 for t in rep["tiers"])
+    r = run("--mock", "--model-dir", model_dir, "--prompt-ids", "1", "--max-step-tokens", "256",
+            "--max-decoder-rows", "8")
+    assert r.returncode == 2 and "max-decoder-rows" in r.stderr

@@ -93,7 +93,12 @@ def make(**kw):
     cfg.prefill_policy = kw.get("policy", "fifo")
     cfg.spec_method = kw.get("spec", "none")
     cfg.num_spec_tokens = kw.get("k", 0)
-    cfg.ngram_n = 2
+    cfg.ngram_min = kw.get("ngram_min", 2)
+    cfg.ngram_max = kw.get("ngram_max", 2)
+    for k in ("starvation_steps", "starvation_ms", "max_mixed_step_tokens", "dynamic_prefill_budget",
+              "backlog_low_tokens", "backlog_high_tokens"):
+        if k in kw:
+            setattr(cfg, k, kw[k])
     be = FakeBackend(kw.get("fn"))
     return m.Engine(cfg, be), be
 
@@ -447,3 +452,81 @@ def test_in_flight_depth_one_matches_synchronous(depth):
     st = eng.stats()
     assert (st.run_ahead_steps > 0) == (depth == 1)
     assert eng.free_slots() == 4
+
+
+def test_srpt_starvation_cap_in_milliseconds():
+    """The wall-clock form of the cap: with the step cap out of reach, the long prompt that
+    arrived first is admitted once it has waited `starvation_ms`, although shorter prompts
+    keep arriving."""
+    import time
+
+    eng, _ = make(max_seqs=1, policy="srpt", chunk=64, max_step_tokens=64, starvation_steps=1 << 30,
+                  starvation_ms=30)
+    eng.submit(0, [(3 * j + 1) % V for j in range(40)], 2)
+    first, rid, t0 = {}, 1, time.monotonic()
+    for step in range(5000):
+        if time.monotonic() - t0 < 0.5:  # a new short prompt every step for half a second
+            eng.submit(rid, [rid % V, (rid * 7) % V], 1)
+            rid += 1
+        for ev in eng.step():
+            first.setdefault(ev["request_id"], time.monotonic() - t0)
+        if not eng.has_work():
+            break
+        time.sleep(0.001)
+    assert any(r != 0 and t < first[0] for r, t in first.items()), "SRPT never preferred a short prompt"
+    assert first[0] < 0.4, first[0]  # well before the stream of short prompts ends
+
+
+def test_ngram_drafts_take_the_longest_matching_suffix():
+    """Prompt-lookup windows: with lookup 2..5 the 3-token suffix [1, 2, 3] matches at the
+    start and proposes what followed it there; with lookup 2..2 only [2, 3] is tried and its
+    most recent earlier occurrence wins."""
+    prompt = [1, 2, 3, 10, 11, 5, 2, 3, 20, 21, 7, 1, 2]
+    for lo, hi, want in ((2, 5, [10, 11, 5]), (2, 2, [20, 21, 7])):
+        eng, be = make(spec="ngram", k=3, ngram_min=lo, ngram_max=hi, fn=lambda h: 3)
+        eng.submit(1, prompt, 8)
+        run(eng)
+        verify = [p for p in be.plans if any(w > 0 for w in p["spec_width"])]
+        assert verify, "no verify step"
+        assert list(verify[0]["token_ids"][1:4]) == want, (lo, hi, verify[0]["token_ids"])
+
+
+def test_mixed_steps_respect_the_token_cap():
+    """Steps that carry decode rows take prefill chunks only up to max(cap, decodes + 1)
+    rows; steps without decode rows still use the full step budget.  Output unchanged."""
+    eng, be = make(max_seqs=4, chunk=32, max_step_tokens=64, max_mixed_step_tokens=12)
+    reqs = {0: [(5 * j) % V for j in range(8)], 1: [(7 * j + 1) % V for j in range(100)],
+            2: [(3 * j + 2) % V for j in range(90)]}
+    for rid, p in reqs.items():
+        eng.submit(rid, p, 6)
+    out, _ = run(eng)
+    for rid, p in reqs.items():
+        assert out[rid] == expected(p, 6)
+    mixed = [p for p in be.plans if any(w == 1 for w in _rows(p)) and any(w > 1 for w in _rows(p))]
+    assert mixed, "no step mixed decode rows with a prefill chunk"
+    for p in mixed:
+        decodes = sum(1 for w in _rows(p) if w == 1)
+        assert len(p["token_ids"]) <= max(12, decodes + 1), (len(p["token_ids"]), decodes)
+    assert max(len(p["token_ids"]) for p in be.plans) > 12  # pure prefill steps are not capped
+
+
+def test_dynamic_prefill_budget_grows_with_the_backlog():
+    """With the dynamic budget a large prefill backlog lifts the mixed-step cap toward
+    max_step_tokens; without it the cap stays fixed."""
+    sizes = {}
+    for dyn in (False, True):
+        eng, be = make(max_seqs=4, chunk=64, max_step_tokens=64, max_mixed_step_tokens=12,
+                       dynamic_prefill_budget=dyn, backlog_low_tokens=16, backlog_high_tokens=64)
+        eng.submit(0, [1, 2, 3], 20)
+        for _ in range(3):  # request 0 is decoding before the long prompts arrive
+            eng.step()
+        for rid in (1, 2, 3):
+            eng.submit(rid, [(11 * j + rid) % V for j in range(200)], 2)
+        run(eng)
+        sizes[dyn] = max(len(p["token_ids"]) for p in be.plans if any(w == 1 for w in _rows(p)))
+    assert sizes[False] <= 12 and sizes[True] > 12, sizes
+
+
+def _rows(p):
+    qs = p["query_start"]
+    return [qs[i + 1] - qs[i] for i in range(len(p["seq_slot"]))]
