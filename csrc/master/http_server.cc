@@ -219,6 +219,7 @@ struct ChatParams {
   uint64_t seed = 0;
   bool thinking = false;
   std::string reasoning_effort;
+  std::string user;  // opaque end-user id (logged only)
 };
 
 bool parse_content(const Value& c, std::string* out, std::string* err) {
@@ -260,6 +261,7 @@ std::string parse_chat(const Value& body, ChatParams* p) {
     if (!known && !kv.second.is_null()) return "unsupported parameter `" + kv.first + "`";
   }
   if (!body.get("tools").is_null() || !body.get("tool_choice").is_null()) return "tool calling is not supported";
+  if (body.get("user").is_string()) p->user = body.get("user").as_string();
   if (!body.get("response_format").is_null()) return "response_format is not supported";
   const Value& n = body.get("n");
   if (!n.is_null() && (!n.is_int() || n.as_int() != 1)) return "n=" + n.dump() + " is not supported";
@@ -681,6 +683,16 @@ void HttpServer::handle(int fd, bool loopback, bool admin_only) {
   if (se != serve::SubmitError::kOk) {
     send_error(fd, 503, "server_error", "unavailable", "engine is not accepting requests", rid_hdr);
     return;
+  }
+  // One line per accepted request (the W3C trace context passes through for correlation).
+  {
+    const std::string tp = req.header("traceparent");
+    fprintf(stderr,
+            "zstep_serve request_id=%s traceparent=%s loop_id=%llu prompt_tokens=%zu max_tokens=%u stream=%s "
+            "stops=%zu seed=%s user=%s\n",
+            rid.c_str(), tp.empty() ? "-" : tp.c_str(), (unsigned long long)er.id, er.prompt.size(), er.max_tokens,
+            cp.stream ? "true" : "false", cp.stop.size(), cp.has_seed ? std::to_string(cp.seed).c_str() : "-",
+            cp.user.empty() ? "-" : cp.user.c_str());
   }
 
   const uint64_t created = (uint64_t)time(nullptr);

@@ -105,14 +105,19 @@ def test_serve_lifecycle_and_sigterm(model_dir):
         ready = json.loads(p.stdout.readline())
         port = ready["port"]
         conn = http.client.HTTPConnection("127.0.0.1", port, timeout=30)
+        tp = "00-0af7651916cd43dd8448eb211c80319c-b7ad6b7169203331-01"
         conn.request("POST", "/v1/chat/completions",
-                     body=json.dumps({"messages": [{"role": "user", "content": "hi"}], "max_tokens": 4}),
-                     headers={"Content-Type": "application/json"})
+                     body=json.dumps({"messages": [{"role": "user", "content": "hi"}], "max_tokens": 4,
+                                      "user": "u-17"}),
+                     headers={"Content-Type": "application/json", "x-request-id": "rq-1", "traceparent": tp})
         r = conn.getresponse()
         body = json.loads(r.read())
         assert r.status == 200 and body["model"] == "m1" and body["usage"]["completion_tokens"] == 4
         p.send_signal(signal.SIGTERM)
         assert p.wait(timeout=30) == 0
+        log = p.stderr.read()
+        line = next(x for x in log.splitlines() if x.startswith("zstep_serve request_id=rq-1 "))
+        assert f"traceparent={tp}" in line and "max_tokens=4" in line and "user=u-17" in line, line
     finally:
         if p.poll() is None:
             p.kill()
