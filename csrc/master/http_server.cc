@@ -502,6 +502,9 @@ std::string HttpServer::render_metrics(serve::ServeLoop* loop, const ServerConfi
                                                        {"rejected", m.requests_rejected.load()}};
   for (const auto& kv : outcomes)
     o += "zstep:request_outcomes_total{" + model + ",outcome=\"" + kv.first + "\"} " + std::to_string(kv.second) + "\n";
+  // Kept for dashboards built on the reference's metric set: nothing is JIT-compiled at run
+  // time here (every kernel is built ahead of time for sm_100a), so it stays 0.
+  counter("triton_recompilations_total", "Runtime kernel recompilations (always 0: kernels are prebuilt).", 0.0);
   if (st.spec_drafts > 0 || st.spec_verify_rows > 0) {
     counter("spec_decode_num_drafts_total", "Verify steps with drafts.", (double)st.spec_verify_steps);
     counter("spec_decode_num_draft_tokens_total", "Draft tokens proposed.", (double)st.spec_drafts);

@@ -168,9 +168,12 @@ def test_metrics_and_drain(server):
     st, hdr, raw = request(p, "GET", "/metrics")
     text = raw.decode()
     assert st == 200 and hdr["Content-Type"].startswith("text/plain")
+    # The reference's metric names (dashboards keep working), plus this engine's own.
     for name in ("zstep:kv_cache_usage_perc", "zstep:time_to_first_token_seconds_bucket",
-                 "zstep:time_per_output_token_seconds_count", "zstep:request_outcomes_total", "zstep:generation_tokens_total"):
-        assert name in text
+                 "zstep:time_per_output_token_seconds_count", "zstep:request_outcomes_total", "zstep:generation_tokens_total",
+                 "zstep:num_requests_running", "zstep:num_requests_waiting", "zstep:num_preemptions_total",
+                 "zstep:triton_recompilations_total"):
+        assert name in text, name
     assert 'outcome="length"} 1' in text
     st, _, raw = request(p, "POST", "/admin/drain")
     assert st == 200 and json.loads(raw)["status"] == "draining"
