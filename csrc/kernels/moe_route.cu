@@ -1,7 +1,7 @@
 // MoE routing for the grouped MXFP8 expert GEMMs.
 //
-//   route_topk : one warp per token.  Softmax (Qwen) or sigmoid + correction bias with
-//                grouped top-k (DeepSeek-V3 style) scoring, top-k with the
+//   route_topk : one warp per token.  Softmax (Qwen), or sigmoid / sqrt(softplus) scores +
+//                correction bias with grouped top-k (DeepSeek style) scoring, top-k with the
 //                smallest-index tie break, optional renormalisation, then a slot in
 //                the expert's segment via an atomic per-expert counter.  Experts
 //                outside [expert_begin, expert_end) belong to other expert-parallel
@@ -96,7 +96,9 @@ __global__ void route_topk_kernel(const MoeRouteArgs a) {
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
       const int e = lane + 32 * j;
-      score[j] = e < E ? sigmoidf_(score[j]) : 0.f;
+      // sqrt(softplus(x)) with softplus = x above 20 (log1p(exp(x)) rounds to x there).
+      const float x = score[j];
+      score[j] = e >= E ? 0.f : a.scoring == 2 ? sqrtf(x > 20.f ? x : log1pf(__expf(x))) : sigmoidf_(x);
       choice[j] = e < E ? score[j] + (a.bias ? a.bias[e] : 0.f) : -INFINITY;
     }
     if (a.n_group > 1) {

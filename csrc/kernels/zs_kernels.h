@@ -228,7 +228,7 @@ typedef struct MoeRouteArgs {
   int num_experts;         // routed experts (global)
   int top_k;
   int norm_topk;           // renormalise the top-k weights to sum 1
-  int scoring;             // 0 = softmax, 1 = sigmoid (+ bias, grouped)
+  int scoring;             // 0 = softmax, 1 = sigmoid, 2 = sqrt(softplus) (1, 2: + bias, grouped)
   const float* bias;       // sigmoid scoring: per-expert correction bias (may be NULL)
   int n_group, topk_group; // grouped routing (sigmoid scoring)
   float routed_scale;

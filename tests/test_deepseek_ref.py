@@ -125,3 +125,34 @@ def test_quantized_reference_tracks_fp32():
         la, lb = a.step(sa, t), b.step(sb, t)
     cos = torch.nn.functional.cosine_similarity(la, lb, dim=0)
     assert cos > 0.9
+
+
+def test_sqrt_softplus_router_and_config(tmp_path):
+    """sqrt(softplus) router scores: top-k on score + bias, unbiased scores renormalised and
+    scaled (restated here); the HF `scoring_func` spelling maps onto the config, and the tiny
+    model runs with it."""
+    import dataclasses
+    import json
+
+    from zstep_b200.config import DeepSeekConfig
+    from zstep_b200.ops import reference as R
+
+    g = torch.Generator().manual_seed(4)
+    logits = torch.randn(6, 16, generator=g) * 3
+    bias = torch.randn(16, generator=g) * 0.1
+    ids, w = R.route(logits, top_k=4, scoring="sqrtsoftplus", bias=bias, routed_scale=2.5)
+    score = torch.sqrt(torch.nn.functional.softplus(logits))
+    want_ids = torch.sort(score + bias, dim=-1, descending=True, stable=True).indices[:, :4]
+    assert torch.equal(ids, want_ids)
+    picked = torch.gather(score, 1, want_ids)
+    torch.testing.assert_close(w, picked / picked.sum(-1, keepdim=True) * 2.5)
+    raw = dataclasses.asdict(deepseek_tiny())
+    raw.update(scoring_func="sqrt_softplus", kv_lora_rank=raw["kv_lora_rank"])
+    (tmp_path / "config.json").write_text(json.dumps(raw))
+    cfg = DeepSeekConfig.from_hf(tmp_path)
+    assert cfg.scoring_func == "sqrtsoftplus"
+    m = DeepSeekReference(cfg, DeepSeekRandomWeights(cfg, seed=0))
+    st = m.new_state()
+    for t in (3, 9, 27):
+        lg = m.step(st, t)
+    assert torch.isfinite(lg).all()

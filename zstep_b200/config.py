@@ -189,6 +189,10 @@ class DeepSeekConfig:
     n_group: int = 8
     topk_group: int = 4
     routed_scaling_factor: float = 2.5
+    # Router scores: "sigmoid" (DeepSeek-V3) or "sqrtsoftplus" (sqrt(softplus(logit)));
+    # either way the top-k runs on score + correction bias within the kept groups and the
+    # weights are the unbiased scores, renormalised and scaled.
+    scoring_func: str = "sigmoid"
     moe_intermediate_size: int = 2048
     n_shared_experts: int = 1
     hc_mult: int = 4
@@ -262,6 +266,10 @@ class DeepSeekConfig:
         kw = {k: v for k, v in raw.items() if k in known}
         if "dspark_aux_layers" in kw:
             kw["dspark_aux_layers"] = tuple(kw["dspark_aux_layers"])
+        if "scoring_func" in kw:
+            kw["scoring_func"] = str(kw["scoring_func"]).replace("_", "")
+            if kw["scoring_func"] not in ("sigmoid", "sqrtsoftplus"):
+                raise ValueError(f"unsupported router scoring_func {raw['scoring_func']!r}")
         kw["name"] = str(raw.get("_name_or_path", raw.get("model_type", "deepseek")))
         return cls(**kw)
 

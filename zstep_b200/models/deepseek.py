@@ -105,6 +105,7 @@ class DeepSeekRunner:
         self.e_begin = tp_rank * self.e_local
         self.groups = self.e_local + 1  # + shared expert
         self.top_k = c.num_experts_per_tok
+        self.scoring = {"sigmoid": 1, "sqrtsoftplus": 2}[c.scoring_func]  # route kernel's scoring mode
         self.k1 = self.top_k + 1
         self.num_slots = max_seqs + 1
         self.dummy_slot = max_seqs
@@ -373,7 +374,7 @@ class DeepSeekRunner:
             E = c.n_routed_experts
             nr = L["router"].n_pad
             self._gemm(L["router"], b["xq"], b["xsf"], rows, b["logits"], nr, EPI_F32)
-            C.moe_route(b["logits"], rows, E, self.top_k, True, 1, L["bias"], c.n_group, c.topk_group,
+            C.moe_route(b["logits"], rows, E, self.top_k, True, self.scoring, L["bias"], c.n_group, c.topk_group,
                         c.routed_scaling_factor, -1, self.e_begin, self.e_begin + self.e_local, True, b["topk_ids"],
                         b["topk_w"], b["gcount"], b["goff"], b["gpre"], b["pair_slot"], b["row_dst"], b["row_scale"],
                         b["xq"], b["xsf"], b["xg"], b["xg_sf"], b["err"], nr, 1, rows * nr, self._moe_bn(rows),

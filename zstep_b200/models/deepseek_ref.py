@@ -335,7 +335,7 @@ class DeepSeekReference:
             h = F.silu(L["gate"] @ xq) * (L["up"] @ xq)
             return L["down"] @ self._q(h)
         logits = L["router"] @ xq
-        ids, w = R.route(logits[None], top_k=c.num_experts_per_tok, scoring="sigmoid", bias=L["bias"],
+        ids, w = R.route(logits[None], top_k=c.num_experts_per_tok, scoring=c.scoring_func, bias=L["bias"],
                          n_group=c.n_group, topk_group=c.topk_group, routed_scale=c.routed_scaling_factor)
         out = torch.zeros(c.hidden_size, device=xq.device)
         eb = self.r * self.e_local

@@ -151,7 +151,13 @@ def route(logits: torch.Tensor, *, top_k: int, scoring: str = "softmax", norm_to
         score = torch.softmax(logits.float(), dim=-1)
         choice = score.clone()
     else:
-        score = torch.sigmoid(logits.float())
+        if scoring == "sqrtsoftplus":
+            x = logits.float()
+            score = torch.sqrt(torch.where(x > 20.0, x, torch.log1p(torch.exp(x))))
+        elif scoring == "sigmoid":
+            score = torch.sigmoid(logits.float())
+        else:
+            raise ValueError(f"unknown router scoring {scoring!r}")
         choice = score + (bias.float() if bias is not None else 0.0)
         if n_group > 1:
             rows, e = choice.shape
