@@ -45,6 +45,9 @@ def prompts(n=8, seed=7, shared=0):
 def test_tp2_shm_engine_matches_reference(apc, depth):
     """depth 1: decode steps are published one step ahead of result processing; workers
     continue each slot with the token they sampled (device tokens)."""
+    import os
+
+    shm0 = {f for f in os.listdir("/dev/shm") if f.startswith("zstep-")}
     ps = prompts(shared=48 if apc else 0)
     ref = reference_generate(ps, 32)
     eng, coord = launch(model="qwen3.5-tiny", world_size=2, device="cpu", max_seqs=4, max_step_tokens=96,
@@ -62,8 +65,11 @@ def test_tp2_shm_engine_matches_reference(apc, depth):
         assert (eng.stats().run_ahead_steps > 0) == (depth == 1)
         # Every page is free or held by a cached prefix node (1 page per node here).
         assert eng.free_pages() + eng.cached_prefix_nodes() == 255 and eng.free_slots() == 4
+        # The segment's name is unlinked once the workers hold its fd: nothing in /dev/shm.
+        assert {f for f in os.listdir("/dev/shm") if f.startswith("zstep-")} == shm0
     finally:
         coord.shutdown()
+    assert {f for f in os.listdir("/dev/shm") if f.startswith("zstep-")} == shm0
 
 
 @pytest.mark.timeout(300)
