@@ -65,7 +65,7 @@ const char* kServeUsage =
     "  --num-kv-pages N             KV pages per GPU (default: --gpu-memory-utilization x 32768 / 0.95)\n"
     "  --gpu-memory-utilization F   KV page calibration factor in (0, 1] (default 0.95)\n"
     "  --kv-cache-dtype auto|bf16   KV cache dtype (the caches are bf16; fp8 is rejected)\n"
-    "  --tokenizer-mode auto|chatml|deepseek\n"
+    "  --tokenizer-mode auto|chatml|deepseek|deepseek_v41\n"
     "  --enable-prefix-caching | --no-enable-prefix-caching   (default on)\n"
     "  --apc-node-pages N           Pages per prefix-cache node (default 8)\n"
     "  --apc-gdn-node-tokens 64|128 Prefix-cache node size in tokens for recurrent (GDN) models\n"
@@ -165,6 +165,23 @@ const std::set<std::string> kValueFlags = {
     "steps", "hidden-size", "output-features", "router-experts", "router-top-k", "heartbeat-timeout-ms", "shm-name",
     "max-decoder-rows", "max-pages-per-seq", "warmup-prompts", "metrics-output", "verify-output-json",
     "require-exact-greedy", "require-exact-cases", "max-greedy-mismatch-margin"};
+
+// --tokenizer-mode: auto (DeepSeek template when the vocabulary has its turn markers, else
+// ChatML), chatml, deepseek (also spelled deepseek_v41).  Returns false on another value.
+bool template_format(const Args& a, const tok::Tokenizer& t, bool has_tokenizer, tok::TemplateFormat* out) {
+  const std::string mode = a.get("tokenizer-mode", "auto");
+  if (mode == "chatml") {
+    *out = tok::TemplateFormat::kChatML;
+  } else if (mode == "deepseek" || mode == "deepseek_v41") {
+    *out = tok::TemplateFormat::kDeepSeek;
+  } else if (mode == "auto") {
+    *out = has_tokenizer && t.token_id("<｜User｜>") >= 0 ? tok::TemplateFormat::kDeepSeek
+                                                          : tok::TemplateFormat::kChatML;
+  } else {
+    return false;
+  }
+  return true;
+}
 
 // Flag names of the reference's `zstep run` that mean the same as one of ours.
 void apply_aliases(Args* a) {
@@ -496,9 +513,10 @@ int cmd_serve(const Args& a) {
   sc.max_model_len = b.cfg.max_model_len;
   const char* arm = getenv("ZSTEP_ALLOW_REMOTE_METRICS");
   sc.allow_remote_metrics = !(a.has("no-allow-remote-metrics") || (arm && std::string(arm) == "0"));
-  const std::string mode = a.get("tokenizer-mode", "auto");
-  sc.template_format = mode == "deepseek" ? tok::TemplateFormat::kDeepSeek : tok::TemplateFormat::kChatML;
-  if (mode == "auto" && b.tokenizer.token_id("<｜User｜>") >= 0) sc.template_format = tok::TemplateFormat::kDeepSeek;
+  if (!template_format(a, b.tokenizer, b.has_tokenizer, &sc.template_format)) {
+    fprintf(stderr, "zstep serve: --tokenizer-mode must be auto, chatml, deepseek or deepseek_v41\n");
+    return 2;
+  }
   http::HttpServer server(sc, &loop, &b.tokenizer);
   if (!server.start(&err)) {
     fprintf(stderr, "zstep serve: %s\n", err.c_str());
@@ -1147,6 +1165,10 @@ int cmd_run(const Args& a) {
     } else if (a.has("prompt") && b.has_tokenizer) {
       std::string prompt;
       tok::TemplateOptions to;
+      if (!template_format(a, b.tokenizer, b.has_tokenizer, &to.format)) {
+        fprintf(stderr, "zstep run: --tokenizer-mode must be auto, chatml, deepseek or deepseek_v41\n");
+        return 2;
+      }
       if (!tok::render_chat({{"user", a.get("prompt"), ""}}, to, &prompt, &err)) {
         fprintf(stderr, "zstep run: %s\n", err.c_str());
         return 2;

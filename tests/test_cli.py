@@ -214,3 +214,12 @@ def test_reference_run_spellings(model_dir):
     r = run("--mock", "--model-dir", model_dir, "--prompt-ids", "1", "--max-step-tokens", "256",
             "--max-decoder-rows", "8")
     assert r.returncode == 2 and "max-decoder-rows" in r.stderr
+
+
+def test_tokenizer_mode_values(model_dir):
+    base = ("run", "--mock", "--model-dir", model_dir, "--prompt", "hi", "--max-tokens", "2")
+    for mode in ("auto", "chatml", "deepseek", "deepseek_v41"):
+        r = run(*base, "--tokenizer-mode", mode)
+        assert r.returncode == 0, (mode, r.stderr)
+    r = run(*base, "--tokenizer-mode", "llama")
+    assert r.returncode == 2 and "tokenizer-mode" in r.stderr
