@@ -728,10 +728,14 @@ void mla_absorb_q(const Tensor& qi, int64_t qk_dim, int64_t nope, const Tensor& 
 
 void mla_attn(const Tensor& q_lat, const Tensor& q_pe, const Tensor& ckv_cache, const Tensor& page_table,
               int64_t page_size, const Tensor& slots, const Tensor& sel, const Tensor& n_sel, int64_t rows,
-              int64_t heads, int64_t splits, double sm_scale, const Tensor& partial) {
+              int64_t heads, int64_t splits, double sm_scale, const Tensor& partial, int64_t impl,
+              const OptT& err) {
   check_cuda(q_lat, "q_lat");
   check_cuda(partial, "partial");
+  TORCH_CHECK(impl >= 0 && impl <= 2, "mla_attn: impl is 0 / 1 (SIMT) or 2 (tensor cores)");
   MlaAttnArgs a{};
+  a.impl = (int)impl;
+  a.err = optptr<int>(err);
   a.q_lat = ptr<const __nv_bfloat16>(q_lat);
   a.q_pe = ptr<const __nv_bfloat16>(q_pe);
   a.ckv_cache = ptr<const __nv_bfloat16>(ckv_cache);
@@ -866,7 +870,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rms_quant", &rms_quant);
   m.def("mla_prologue", &mla_prologue);
   m.def("mla_absorb_q", &mla_absorb_q);
-  m.def("mla_attn", &mla_attn);
+  m.def("mla_attn", &mla_attn, py::arg("q_lat"), py::arg("q_pe"), py::arg("ckv_cache"), py::arg("page_table"),
+        py::arg("page_size"), py::arg("slots"), py::arg("sel"), py::arg("n_sel"), py::arg("rows"), py::arg("heads"),
+        py::arg("splits"), py::arg("sm_scale"), py::arg("partial"), py::arg("impl") = 1, py::arg("err") = py::none());
   m.def("mla_up", &mla_up);
   m.def("dsa_index", &dsa_index, py::arg("iq"), py::arg("iw"), py::arg("ik_cache"), py::arg("page_table"),
         py::arg("page_size"), py::arg("slots"), py::arg("ctx_len"), py::arg("rows"), py::arg("index_heads"),

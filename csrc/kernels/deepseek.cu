@@ -900,6 +900,235 @@ gather_sum_kernel(const __nv_bfloat16* __restrict__ rows_in, const int* __restri
   }
 }
 
+// ------------------------------------------------------------------------------ MLA on tensor cores
+// Tensor-core form of mla_attn_kernel (same partial records).  CTA of 4 warps per (token,
+// split); the split's selected keys go through 128-key tiles:
+//   * Gather: every key row (576 bf16: 512 latent + 64 rope) is copied by cp.async, 16 bytes
+//     at a time, into a K-major 128-byte-swizzled tile image [9 dim chunks][128 keys][128 B]
+//     (rows of a tile come from arbitrary pages, so no bulk copy can place them); rows past
+//     the split's keys are zeroed.
+//   * S^T = K Q^T: one thread issues 36 tcgen05.mma (kind::f16, bf16, M = 128 keys, N = 16
+//     head slots, K = 16 dims each) into TMEM columns 0-15.  Q = [q_lat | q_pe] per head.
+//   * Online softmax in the exp2 domain exactly as the paged decode kernel: thread t owns
+//     key t, per-head maxima / sums through shared memory, P stored bf16 K-major, the
+//     running O rescaled in TMEM.
+//   * O^T += C^T P^T with the same tile image read MN-major (the latent part of a key row
+//     is its value row): 4 x 8 MMAs (M = 128 latent dims, N = 16, K = 16 keys) into TMEM
+//     columns 16-79.
+// The image is single-buffered (147 KiB): the next tile's gather starts once this tile's
+// second product has consumed it.
+constexpr int kMtKeys = 128;
+constexpr int kMtChunks = (kLat + kRope) / 64;       // 9
+constexpr int kMtPlane = kMtKeys * 128;              // bytes per 64-dim chunk plane
+constexpr int kMtN = 16;                             // head slots (heads <= 16)
+
+struct MlaTcSmem {
+  uint8_t k[kMtChunks * kMtPlane];   // key tile image (1024-aligned: first member)
+  uint8_t q[kMtChunks][kMtN * 128];  // [q_lat | q_pe] per head slot, slots >= heads zero
+  uint8_t p[2][kMtN * 128];          // P: [16 slots][128 keys] K-major, 2 chunks of 64 keys
+  float red_max[4][kMtN];
+  float red_sum[4][kMtN];
+  float m[kMtN], l[kMtN], r[kMtN];
+  uint64_t mma1, mma2;
+  uint32_t tmem_base;
+};
+
+__global__ void __launch_bounds__(128, 1)
+mla_attn_tc_kernel(MlaAttnArgs a) {
+  pdl_wait();  // predecessor kernel done: its outputs are visible
+  pdl_trigger();
+  extern __shared__ __align__(1024) uint8_t mla_tc_smem_raw[];
+  MlaTcSmem& s = *reinterpret_cast<MlaTcSmem*>((reinterpret_cast<uintptr_t>(mla_tc_smem_raw) + 1023) & ~uintptr_t(1023));
+  const int t = blockIdx.x, split = blockIdx.y, S = gridDim.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int HL = a.heads;
+  const int n_keys = a.n_sel[t];
+  const int per = (n_keys + S - 1) / S;
+  const int k0 = min(n_keys, split * per), k1 = min(n_keys, k0 + per);
+  const int nk_all = k1 - k0;
+  const int ntiles = (nk_all + kMtKeys - 1) / kMtKeys;
+  const float qscale = a.sm_scale * 1.4426950408889634f;  // exp2 domain
+  if (warp == 0) {
+    tmem_alloc(&s.tmem_base, 128);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&s.mma1, 1);
+    mbar_init(&s.mma2, 1);
+    fence_barrier_init();
+  }
+  if (tid < kMtN) {
+    s.m[tid] = -INFINITY;
+    s.l[tid] = 0.f;
+  }
+  for (int i = tid; i < kMtN * (kLat + kRope) / 8; i += blockDim.x) {
+    const int h = i / 72, piece = i % 72, c = piece >> 3, j = piece & 7;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (h < HL)
+      v = piece < 64 ? *reinterpret_cast<const uint4*>(a.q_lat + ((size_t)t * HL + h) * kLat + piece * 8)
+                     : *reinterpret_cast<const uint4*>(a.q_pe + ((size_t)t * HL + h) * kRope + (piece - 64) * 8);
+    *reinterpret_cast<uint4*>(s.q[c] + h * 128 + ((j ^ (h & 7)) << 4)) = v;
+  }
+  fence_proxy_async_shared();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const uint32_t t_s = tmem, t_o = tmem + kMtN;
+  const int* sel = a.sel + (size_t)t * a.ld_sel + k0;
+  const int* pt = a.page_table + (size_t)a.slot[t] * a.max_pages;
+  bool ok = true;
+  for (int tile = 0; tile < ntiles; ++tile) {
+    const int kb = tile * kMtKeys;
+    const int nk = min(kMtKeys, nk_all - kb);
+    // Gather: warp w copies keys w, w + 4, ...; a row's 72 pieces spread over the lanes.
+    for (int kk = warp; kk < kMtKeys; kk += 4) {
+      uint8_t* rowbase = s.k + kk * 128;
+      if (kk < nk) {
+        const int pos = __ldg(sel + kb + kk);
+        const int page = __ldg(pt + pos / a.page_size);
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(
+            a.ckv_cache + ((size_t)page * a.page_size + pos % a.page_size) * (kLat + kRope));
+        for (int piece = lane; piece < 72; piece += 32)
+          cp_async16(rowbase + (piece >> 3) * kMtPlane + (((piece & 7) ^ (kk & 7)) << 4), src + piece * 16);
+      } else {
+        for (int piece = lane; piece < 72; piece += 32)
+          *reinterpret_cast<uint4*>(rowbase + (piece >> 3) * kMtPlane + (((piece & 7) ^ (kk & 7)) << 4)) =
+              make_uint4(0, 0, 0, 0);
+      }
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+    fence_proxy_async_shared();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t idesc = make_idesc_bf16(kMtKeys, kMtN, 0, 0);
+#pragma unroll
+      for (int c = 0; c < kMtChunks; ++c)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t ad = make_smem_desc(smem_u32(s.k + c * kMtPlane) + k * 32, 16, 1024, 2);
+          const uint64_t bd = make_smem_desc(smem_u32(s.q[c]) + k * 32, 16, 1024, 2);
+          mma_bf16(t_s, ad, bd, idesc, (c | k) ? 1u : 0u);
+        }
+      tc_commit(&s.mma1);
+    }
+    ok = mbar_wait(&s.mma1, (uint32_t)(tile & 1), a.err);
+    if (!__syncthreads_and(ok)) break;
+    tc_fence_after();
+    // ---- online softmax: thread tid owns key tid of the tile
+    uint32_t sr[16];
+    tmem_ld_32x32b_x16(t_s + lane_off, sr);
+    tmem_ld_wait();
+    const bool valid = tid < nk;
+    float sv[kMtN];
+#pragma unroll
+    for (int h = 0; h < kMtN; ++h) sv[h] = (valid && h < HL) ? __uint_as_float(sr[h]) * qscale : -INFINITY;
+#pragma unroll
+    for (int h = 0; h < kMtN; ++h) {
+      const float v = warp_max(sv[h]);
+      if (lane == 0) s.red_max[warp][h] = v;
+    }
+    __syncthreads();
+    float mnew[kMtN];
+#pragma unroll
+    for (int h = 0; h < kMtN; ++h)
+      mnew[h] = fmaxf(fmaxf(s.m[h], fmaxf(s.red_max[0][h], s.red_max[1][h])), fmaxf(s.red_max[2][h], s.red_max[3][h]));
+    {
+      const int chunk = tid >> 6, within = tid & 63, piece = within >> 3, sub = (within & 7) * 2;
+#pragma unroll
+      for (int h = 0; h < kMtN; ++h) {
+        const float pv = sv[h] == -INFINITY ? 0.f : exp2f(sv[h] - mnew[h]);
+        const __nv_bfloat16 pb = __float2bfloat16_rn(pv);
+        *reinterpret_cast<__nv_bfloat16*>(s.p[chunk] + h * 128 + ((piece ^ (h & 7)) << 4) + sub) = pb;
+        const float sum = warp_sum(__bfloat162float(pb));
+        if (lane == 0) s.red_sum[warp][h] = sum;
+      }
+    }
+    fence_proxy_async_shared();
+    __syncthreads();
+    if (tid < kMtN) {
+      const int h = tid;
+      const float mo = s.m[h];
+      const float rr = mo == -INFINITY ? 0.f : exp2f(mo - mnew[h]);
+      s.l[h] = s.l[h] * rr + (s.red_sum[0][h] + s.red_sum[1][h] + s.red_sum[2][h] + s.red_sum[3][h]);
+      s.m[h] = mnew[h];
+      s.r[h] = rr;
+    }
+    __syncthreads();
+    if (tile > 0) {  // rescale the running O^T (TMEM lane = latent dim, column = head slot)
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt) {
+        uint32_t o[16];
+        tmem_ld_32x32b_x16(t_o + mt * kMtN + lane_off, o);
+        tmem_ld_wait();
+#pragma unroll
+        for (int h = 0; h < 16; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * s.r[h]);
+        tmem_st_32x32b_x16(t_o + mt * kMtN + lane_off, o);
+      }
+      tmem_st_wait();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t idesc2 = make_idesc_bf16(128, kMtN, 1, 0);
+#pragma unroll
+      for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          // A: latent dims 128 mt.. (chunks 2mt, 2mt+1, LBO = one chunk plane) x keys
+          // 16 ks.. (two 8-key groups, SBO = 1 KiB), MN-major.
+          const uint64_t ad = make_smem_desc(smem_u32(s.k + 2 * mt * kMtPlane) + ks * 16 * 128, kMtPlane, 1024, 2);
+          const uint64_t bd = make_smem_desc(smem_u32(s.p[ks >> 2]) + (ks & 3) * 32, 16, 1024, 2);
+          mma_bf16(t_o + mt * kMtN, ad, bd, idesc2, (tile > 0 || ks > 0) ? 1u : 0u);
+        }
+      tc_commit(&s.mma2);
+    }
+    ok = mbar_wait(&s.mma2, (uint32_t)(tile & 1), a.err);
+    if (!__syncthreads_and(ok)) break;
+    tc_fence_after();
+  }
+  const int h_lim = HL < kMtN ? HL : kMtN;
+  if (ok) {
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt) {
+      uint32_t o[16];
+      if (ntiles > 0) {
+        tmem_ld_32x32b_x16(t_o + mt * kMtN + lane_off, o);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int h = 0; h < 16; ++h) o[h] = 0u;
+      }
+      const int dim = mt * 128 + tid;
+#pragma unroll
+      for (int h = 0; h < 16; ++h) {
+        if (h >= h_lim) break;
+        a.partial[(((size_t)t * HL + h) * S + split) * (kLat + 4) + dim] = __uint_as_float(o[h]);
+      }
+    }
+    if (tid < h_lim) {
+      float* rec = a.partial + (((size_t)t * HL + tid) * S + split) * (kLat + 4);
+      // Records hold the natural-log maximum (the SIMT kernel's convention).
+      rec[kLat] = s.m[tid] == -INFINITY ? -INFINITY : s.m[tid] * 0.6931471805599453f;
+      rec[kLat + 1] = s.l[tid];
+    }
+  } else if (tid < h_lim) {
+    // Abort (the error word is set): an empty record, so the merge skips this split.
+    float* rec = a.partial + (((size_t)t * HL + tid) * S + split) * (kLat + 4);
+    rec[kLat] = -INFINITY;
+    rec[kLat + 1] = 0.f;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
 }  // namespace ds
 }  // namespace zs
 
@@ -962,6 +1191,16 @@ int zs_mla_attn(const MlaAttnArgs* a, cudaStream_t stream) {
   if (a->heads > ds::kMaxHeads || a->kv_lora != ds::kLat || a->rope != ds::kRope || a->splits < 1 ||
       a->splits > 64)
     return -2;
+  if (a->impl == 2) {  // tensor cores (heads <= 16 as checked above)
+    const size_t smem = sizeof(ds::MlaTcSmem) + 1024;
+    static bool tc_attr_set = false;
+    if (!tc_attr_set) {
+      cudaFuncSetAttribute(ds::mla_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      tc_attr_set = true;
+    }
+    zs_launch(ds::mla_attn_tc_kernel, dim3(a->rows, a->splits), 128, smem, stream, *a);
+    return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  }
   const size_t smem = zs_mla_attn_smem(a->heads);
   static bool attr_set = false;
   if (!attr_set) {

@@ -497,6 +497,8 @@ typedef struct MlaAttnArgs {
   int rows, heads, kv_lora, rope, splits;
   float sm_scale;
   float* partial;              // [rows, heads, splits, kv_lora + 4]
+  int impl;                    // 0 / 1: SIMT kernel; 2: tensor cores (tcgen05)
+  int* err;                    // optional error word (bounded mbarrier waits of impl 2)
 } MlaAttnArgs;
 
 size_t zs_mla_attn_smem(int heads);

@@ -1,6 +1,8 @@
 """DeepSeek-style kernels against PyTorch fp32 references: the tensor-core DSA indexer
 scores + deterministic top-k, and the split-KV latent attention + W_UV up-projection."""
 
+import os
+
 import pytest
 import torch
 
@@ -77,7 +79,11 @@ def test_dsa_topk_ties_prefer_lower_positions():
     assert sel[0].cpu().tolist() == list(range(topk))
 
 
-def test_mla_attention_and_up_projection():
+# The tensor-core latent attention (impl 2) has not run on a GPU yet: its case runs only
+# when ZSTEP_TEST_MLA_TC=1 asks for it.
+@pytest.mark.parametrize("impl", [1, pytest.param(2, marks=pytest.mark.skipif(
+    os.environ.get("ZSTEP_TEST_MLA_TC") != "1", reason="tensor-core MLA not yet validated; ZSTEP_TEST_MLA_TC=1"))])
+def test_mla_attention_and_up_projection(impl):
     C = _ext.load()
     g = torch.Generator().manual_seed(3)
     dev = "cuda"
@@ -103,10 +109,13 @@ def test_mla_attention_and_up_projection():
         part = torch.zeros(n * hl * splits * (kl + 4), device=dev)
         q = torch.zeros(128, hl * vd, dtype=torch.uint8, device=dev)
         sf = torch.zeros(mx.atoms_bytes(128, hl * vd), dtype=torch.uint8, device=dev)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
         C.mla_attn(q_lat.to(dev), q_pe.to(dev), cache.to(dev), table.to(dev), page,
-                   torch.arange(n, dtype=torch.int32, device=dev), sel.to(dev), n_sel.to(dev), n, hl, splits, scale, part)
+                   torch.arange(n, dtype=torch.int32, device=dev), sel.to(dev), n_sel.to(dev), n, hl, splits, scale, part,
+                   impl=impl, err=err)
         C.mla_up(part, n, hl, splits, w_uv_t.to(dev), q, sf)
         torch.cuda.synchronize()
+        assert int(err.item()) == 0
         got = mx.dequantize(q[:n].cpu(), mx.codes_from_atoms(sf.cpu(), n, hl * vd))
         for t in range(n):
             kv = _rows(cache, table, t, ctx[t], page)[picks[t]]

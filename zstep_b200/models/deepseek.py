@@ -38,6 +38,7 @@ import torch
 from ..config import DeepSeekConfig
 from ..ops import _ext
 from ..ops import mx
+from ..utils.env import runtime_config
 from .deepseek_weights import DeepSeekRandomWeights
 from .qwen35 import (DECODE_BUCKETS, EPI_BF16, EPI_F32, EPI_SILU, PackedLinear, Qwen35Runner, _pad128,
                      interleave_gate_up, pack_linear)
@@ -106,6 +107,7 @@ class DeepSeekRunner:
         self.groups = self.e_local + 1  # + shared expert
         self.top_k = c.num_experts_per_tok
         self.scoring = {"sigmoid": 1, "sqrtsoftplus": 2}[c.scoring_func]  # route kernel's scoring mode
+        self.mla_impl = runtime_config().mla_impl  # latent attention: 1 SIMT, 2 tensor cores
         self.k1 = self.top_k + 1
         self.num_slots = max_seqs + 1
         self.dummy_slot = max_seqs
@@ -358,7 +360,8 @@ class DeepSeekRunner:
                     c.index_n_heads, c.index_topk, self.max_model_len, b["scores"], b["sel"], b["n_sel"], b["err"])
         splits = self._attn_splits(rows) if decode else 1
         C.mla_attn(b["q_lat"], b["q_pe"], ckv, self.page_table, self.page_size, slot, b["sel"],
-                   b["n_sel"], rows, hl, splits, c.qk_head_dim ** -0.5, b["attn_part"])
+                   b["n_sel"], rows, hl, splits, c.qk_head_dim ** -0.5, b["attn_part"], impl=self.mla_impl,
+                   err=b["err"])
         C.mla_up(b["attn_part"], rows, hl, splits, L["w_uv_t"], b["o_q"], b["o_sf"])
         self._gemm(L["o_proj"], b["o_q"], b["o_sf"], rows, b["y"], c.hidden_size, EPI_F32)
         self._reduce(rows)

@@ -63,6 +63,7 @@ class RuntimeConfig:
     coll_oneshot_rows: int = 16           # ZSTEP_COLL_ONESHOT_ROWS: all-reduces up to this many rows go one-shot
     coll_ll_rows: int = 1024              # ZSTEP_COLL_LL_ROWS: two-shot LL lines up to this many rows, plain above
     coll_push: bool = True                # ZSTEP_COLL_PUSH: row-parallel GEMM epilogues push into the all-reduce
+    mla_impl: int = 1                     # ZSTEP_MLA_IMPL: DeepSeek latent attention, 1 SIMT, 2 tensor cores
     coll_nvls_rows: int = 0               # ZSTEP_COLL_NVLS_ROWS: all-reduces above the one-shot size and up to
                                           # this many rows reduce in the NVSwitch (multicast object; 0: off)
     gemm_fix_splits: bool = False         # ZSTEP_GEMM_FIX_SPLITS: in-kernel split-K for small GEMMs
@@ -85,6 +86,7 @@ class RuntimeConfig:
         "ZSTEP_COLL_LL_ROWS": ("coll_ll_rows", lambda n, r: _int(n, r, 0, 1 << 16)),
         "ZSTEP_COLL_PUSH": ("coll_push", _bool),
         "ZSTEP_COLL_NVLS_ROWS": ("coll_nvls_rows", lambda n, r: _int(n, r, 0, 1 << 16)),
+        "ZSTEP_MLA_IMPL": ("mla_impl", lambda n, r: _choice_int(n, r, (1, 2))),
         "ZSTEP_GEMM_FIX_SPLITS": ("gemm_fix_splits", _bool),
         "ZSTEP_GEMM_DENSE_BN": ("gemm_dense_bn", lambda n, r: _choice_int(n, r, (0, 32, 128))),
         "ZSTEP_DECODE_GRAPHS": ("decode_graphs", _bool),
