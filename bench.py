@@ -23,7 +23,6 @@ from __future__ import annotations
 import argparse
 import datetime
 import json
-import math
 import os
 import statistics
 import subprocess

@@ -3,7 +3,6 @@ for top-k / top-p / penalties / logprobs go through the f32 lm_head + sampling k
 
 import numpy as np
 import pytest
-import torch
 
 from zstep_b200.config import qwen35_small_gpu
 from zstep_b200.models.qwen35 import Qwen35Runner

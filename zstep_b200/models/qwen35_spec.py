@@ -30,7 +30,7 @@ from __future__ import annotations
 import torch
 
 from ..ops import mx
-from .qwen35 import EPI_BF16, EPI_F32, _pad128, pack_linear
+from .qwen35 import EPI_BF16, _pad128, pack_linear
 
 
 class SpecDecoder:
