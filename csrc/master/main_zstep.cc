@@ -393,6 +393,10 @@ bool build_engine(const Args& a, Built* b, std::string* err) {
       }
       fprintf(stderr, "zstep: --%s accepted and ignored: the NVLink collectives size their own grids\n", k);
     }
+  if (c.max_seqs < 1 || c.max_seqs > 512) {  // 512: the largest decode CUDA-graph bucket
+    *err = "--max-seqs must be within 1..512";
+    return false;
+  }
   if (c.max_step_tokens < c.max_seqs) {
     *err = "--max-step-tokens must be >= --max-seqs";
     return false;

@@ -91,6 +91,8 @@ def test_strict_flags(model_dir):
     assert r.returncode == 2 and "unknown flag --bogus" in r.stderr
     r = run("serve", "--mock", "--model-dir", model_dir, "--max-seqs", "abc")
     assert r.returncode == 2
+    r = run("serve", "--mock", "--model-dir", model_dir, "--max-seqs", "600", "--max-step-tokens", "8192")
+    assert r.returncode == 2 and "max-seqs" in r.stderr
     r = run("run", "--mock", "--model-dir", model_dir, "--speculative-method", "magic", "--prompt-ids", "1")
     assert r.returncode == 2 and "speculative-method" in r.stderr
     assert run("frobnicate").returncode == 2
