@@ -1,0 +1,115 @@
+"""Host-side bookkeeping of the B200 runner's speculative path, on CPU: a fake model runner
+records what `GpuRunner` asks of it (staging, target forward, state replay, draft-head
+catch-up and drafting) for plans mixing a prefill chunk, a plain decode row and a verify
+row.  Covers greedy acceptance, the replay of accepted rows, the catch-up rows an MTP head
+(needs the following token) and a DSpark head (needs only the row) receive, and the
+drafts written back for the engine."""
+
+import numpy as np
+import pytest
+import torch
+
+from zstep_b200.runtime import wire
+from zstep_b200.runtime.runners import GpuRunner
+
+K = 2
+
+
+class FakeSpec:
+    def __init__(self, context_only, targets):
+        self.context_only = context_only
+        self.targets = targets  # next token per lm row, in lm-row order
+        self.calls = []
+
+    def forward(self, rows, n, lm_t, verify_slots, ckpt=None):
+        self.calls.append(("forward", lm_t.tolist(), list(verify_slots)))
+        return torch.tensor(self.targets[:len(lm_t)])
+
+    def replay(self, groups, slots, positions):
+        self.calls.append(("replay", list(groups), list(slots), list(positions)))
+
+    def draft(self, ids, positions, slots, rows_t, last_of_seq):
+        self.calls.append(("draft", list(ids), list(positions), list(slots), rows_t.tolist(), list(last_of_seq)))
+        return [[500 + 10 * i + k for k in range(K)] for i in range(len(last_of_seq))]
+
+    def catch_up(self, ids, positions, slots, rows_t):
+        self.calls.append(("catch_up", list(ids), list(positions), list(slots), rows_t.tolist()))
+
+
+class FakeModel:
+    def __init__(self, spec):
+        self.spec = spec
+        self.num_spec = K
+        self.dev = torch.device("cpu")
+        self.cfg = None
+        self.page_table = torch.zeros(8, 4, dtype=torch.int32)
+        self.max_pages = 4
+        self.spec_slot_base = 100
+        self.dummy_slot = 99
+        self.staged = []
+
+    def stage(self, ids, pos, slots, seq_start=None):
+        self.staged.append((list(ids), list(pos), list(slots), seq_start))
+
+    def copy_recurrent_state(self, src, dst):
+        raise AssertionError("no restores in these plans")
+
+
+def plan(seqs):
+    """seqs: (slot, tokens, pos0, spec_width, sample)."""
+    ids, pos, rslot, qs, srow, sw, slots = [], [], [], [0], [], [], []
+    for slot, toks, p0, width, sample in seqs:
+        ids += toks
+        pos += list(range(p0, p0 + len(toks)))
+        rslot += [slot] * len(toks)
+        qs.append(len(ids))
+        srow.append(len(ids) - 1 if sample else -1)
+        sw.append(width)
+        slots.append(slot)
+    n = len(seqs)
+    return {"opcode": wire.OP_NORMAL, "num_seqs": n, "num_rows": len(ids), "flags": 0,
+            "token_ids": np.array(ids, np.int32), "positions": np.array(pos, np.int32),
+            "row_slot": np.array(rslot, np.int32), "query_start": np.array(qs, np.int32),
+            "sample_row": np.array(srow, np.int32), "spec_width": np.array(sw, np.int32),
+            "seq_slot": np.array(slots, np.int32), "restore_slot": np.full(n, -1, np.int32),
+            "dirty_rows": np.zeros(0, np.int32), "dirty_pages": np.zeros((0, 4), np.int32),
+            "ckpt_row": np.zeros(0, np.int32), "ckpt_slot": np.zeros(0, np.int32),
+            "sampling": np.zeros(n, dtype=wire.SAMPLING_DTYPE)}
+
+
+@pytest.mark.parametrize("context_only", [False, True])
+def test_prefill_chunk_catch_up_rows(context_only):
+    """A chunk that samples nothing: MTP catches up rows 0..L-2 (row j with token j+1);
+    DSpark stores a context for every row, the last one included."""
+    spec = FakeSpec(context_only, [])
+    g = GpuRunner.wrap(FakeModel(spec))
+    out = g.execute(plan([(3, [11, 12, 13], 0, 0, False)]))
+    assert out[0]["num_tokens"] == 0 and out[0]["req_slot"] == 3
+    (kind, ids, positions, slots, rows), = [c for c in spec.calls if c[0] == "catch_up"]
+    assert not [c for c in spec.calls if c[0] == "draft"] and slots == [3] * len(ids)
+    if context_only:
+        assert positions == [0, 1, 2] and rows == [0, 1, 2]
+    else:
+        assert ids == [12, 13] and positions == [0, 1] and rows == [0, 1]
+
+
+def test_decode_and_verify_rows():
+    """Slot 1 decodes one row; slot 2 verifies [last, d1, d2] where the target accepts d1
+    and then disagrees: 2 tokens, replay of the 2 accepted rows, drafts for both."""
+    # lm rows: slot 1's row 0 -> 41; slot 2's rows 1..3 -> 7 (= d1), 9 (!= d2), 10
+    spec = FakeSpec(False, [41, 7, 9, 10])
+    g = GpuRunner.wrap(FakeModel(spec))
+    out = g.execute(plan([(1, [5], 20, 0, True), (2, [6, 7, 8], 30, K + 1, True)]))
+    assert out[0]["num_tokens"] == 1 and out[0]["tokens"][0] == 41
+    assert out[1]["num_tokens"] == 2 and list(out[1]["tokens"][:2]) == [7, 9]
+    fwd = spec.calls[0]
+    assert fwd[0] == "forward" and fwd[1] == [0, 1, 2, 3] and fwd[2] == [None, 100 + 2]
+    replay = [c for c in spec.calls if c[0] == "replay"][0]
+    assert replay[1] == [(1, 2)] and replay[2] == [2] and replay[3] == [30]
+    draft = [c for c in spec.calls if c[0] == "draft"][0]
+    # MTP rows: slot 1 row 0 followed by its sampled token; slot 2 rows 1, 2 followed by
+    # the accepted tokens 7 and 9.
+    assert draft[1] == [41, 7, 9] and draft[2] == [20, 30, 31] and draft[4] == [0, 1, 2]
+    assert draft[5] == [0, 2]  # newest row of each drafting sequence
+    assert list(out[0]["next_drafts"][:K]) == [500, 501] and out[0]["num_drafts"] == K
+    assert list(out[1]["next_drafts"][:K]) == [510, 511] and out[1]["num_drafts"] == K
