@@ -67,6 +67,8 @@ def plan(seqs):
         sw.append(width)
         slots.append(slot)
     n = len(seqs)
+    samp = np.zeros(n, dtype=wire.SAMPLING_DTYPE)  # greedy, no penalties, no logprobs
+    samp["top_p"], samp["repetition"], samp["logprobs"] = 1.0, 1.0, -1
     return {"opcode": wire.OP_NORMAL, "num_seqs": n, "num_rows": len(ids), "flags": 0,
             "token_ids": np.array(ids, np.int32), "positions": np.array(pos, np.int32),
             "row_slot": np.array(rslot, np.int32), "query_start": np.array(qs, np.int32),
@@ -74,7 +76,7 @@ def plan(seqs):
             "seq_slot": np.array(slots, np.int32), "restore_slot": np.full(n, -1, np.int32),
             "dirty_rows": np.zeros(0, np.int32), "dirty_pages": np.zeros((0, 4), np.int32),
             "ckpt_row": np.zeros(0, np.int32), "ckpt_slot": np.zeros(0, np.int32),
-            "sampling": np.zeros(n, dtype=wire.SAMPLING_DTYPE)}
+            "sampling": samp}
 
 
 @pytest.mark.parametrize("context_only", [False, True])
@@ -113,3 +115,52 @@ def test_decode_and_verify_rows():
     assert draft[5] == [0, 2]  # newest row of each drafting sequence
     assert list(out[0]["next_drafts"][:K]) == [500, 501] and out[0]["num_drafts"] == K
     assert list(out[1]["next_drafts"][:K]) == [510, 511] and out[1]["num_drafts"] == K
+
+
+class FakePlain(FakeModel):
+    """No draft head: decode and prefill paths."""
+
+    def __init__(self):
+        super().__init__(None)
+        self.calls = []
+        self.buf = {"xq": None, "xsf": None, "xq_last": None}
+        self.last_lm_sf = None
+
+    def copy_recurrent_state(self, src, dst):
+        self.calls.append(("restore", src, dst))
+
+    def decode_step(self, rows):
+        self.calls.append(("decode", rows))
+        return torch.arange(rows, dtype=torch.int32) + 70
+
+    def prefill_forward(self, rows, n, ckpt=None):
+        self.calls.append(("prefill", rows, n, ckpt))
+        return torch.arange(n, dtype=torch.int32) + 80
+
+    def checkpoint_args(self, rows, slots, qs):
+        return ("ck", list(rows), list(slots))
+
+
+def test_decode_and_prefill_plans():
+    m = FakePlain()
+    g = GpuRunner.wrap(m)
+    # Decode-only step: page-table rows refreshed, one graph step over the rows.
+    p = plan([(1, [5], 20, 0, True), (4, [6], 9, 0, True)])
+    p["flags"] = wire.FLAG_DECODE_ONLY
+    p["dirty_rows"] = np.array([4], np.int32)
+    p["dirty_pages"] = np.array([[7, 8, 9, 10]], np.int32)
+    out = g.execute(p)
+    assert m.calls == [("decode", 2)] and list(out["tokens"][:, 0]) == [70, 71]
+    assert m.page_table[4].tolist() == [7, 8, 9, 10]
+    assert m.staged[-1][:3] == ([5, 6], [20, 9], [1, 4])
+    # Mixed step: a restored slot, a checkpoint row, one chunk that samples, one that does not.
+    m.calls.clear()
+    p = plan([(2, [1, 2, 3], 16, 0, True), (3, [4, 5], 0, 0, False)])
+    p["restore_slot"] = np.array([40, -1], np.int32)
+    p["ckpt_row"], p["ckpt_slot"] = np.array([2], np.int32), np.array([41], np.int32)
+    out = g.execute(p)
+    assert m.calls[0] == ("restore", 40, 2)
+    assert m.calls[1] == ("prefill", 5, 2, ("ck", [2], [41]))
+    assert m.staged[-1][3] == [0, 3, 5]
+    assert out[0]["num_tokens"] == 1 and out[0]["tokens"][0] == 80 and out[1]["num_tokens"] == 0
+    assert list(out["req_slot"]) == [2, 3]
