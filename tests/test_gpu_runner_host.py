@@ -164,3 +164,40 @@ def test_decode_and_prefill_plans():
     assert m.staged[-1][3] == [0, 3, 5]
     assert out[0]["num_tokens"] == 1 and out[0]["tokens"][0] == 80 and out[1]["num_tokens"] == 0
     assert list(out["req_slot"]) == [2, 3]
+
+
+def test_steady_state_verify_uses_the_graph_record():
+    """Every sequence verifying K drafts, greedy, no checkpoints: the step replays the verify
+    graph of the next bucket, with the padding rows on the dummy slot, and reads accepted
+    tokens and next drafts from the device record [n, 2K + 2]."""
+
+    class GraphSpec(FakeSpec):
+        def __init__(self):
+            super().__init__(False, [])
+            self.out_slots = torch.zeros(8, dtype=torch.int32)
+            self.g_record = torch.zeros(8, 2 * K + 2, dtype=torch.int32)
+
+        def graph_bucket(self, n):
+            return 4 if n <= 4 else None
+
+        def run_verify_graph(self, nb):
+            self.calls.append(("graph", nb, self.out_slots[:nb].tolist()))
+            # sequence i accepts i + 1 tokens (tokens 60 + i ...), next drafts 90 + i, 91 + i
+            for i in range(3):
+                acc = i + 1
+                self.g_record[i, 0] = acc
+                self.g_record[i, 1:1 + acc] = torch.arange(acc, dtype=torch.int32) + 60 + i
+                self.g_record[i, K + 2:2 * K + 2] = torch.tensor([90 + i, 91 + i], dtype=torch.int32)
+
+    spec = GraphSpec()
+    m = FakeModel(spec)
+    g = GpuRunner.wrap(m)
+    out = g.execute(plan([(s, [1, 2, 3], 10 * s, K + 1, True) for s in (1, 2, 5)]))
+    (kind, nb, slots), = [c for c in spec.calls if c[0] == "graph"]
+    assert nb == 4 and slots == [101, 102, 105, 99]  # spare state slots, dummy padding
+    ids, pos, rslot, seq_start = m.staged[-1]
+    assert len(ids) == 4 * (K + 1) and rslot[9:] == [99, 99, 99] and pos[9:] == [1, 1, 1]
+    assert seq_start == [0, 3, 6, 9, 12]
+    for i in range(3):
+        assert out[i]["num_tokens"] == i + 1 and list(out[i]["tokens"][:i + 1]) == list(range(60 + i, 61 + 2 * i))
+        assert list(out[i]["next_drafts"][:K]) == [90 + i, 91 + i]
