@@ -93,3 +93,25 @@ def test_gumbel_sampler_reference():
         counts[gumbel_sample(logits, T, seed=99, pos=pos)] += 1
     for c, q in zip(counts, p):
         assert abs(c / n - q) < 4 * math.sqrt(q * (1 - q) / n) + 0.005, (counts, p)
+
+
+def test_full_distribution_head_is_used_only_when_needed():
+    """Greedy and plain temperature rows stay in the lm_head GEMM (argmax / Gumbel
+    epilogue); top-k, top-p, penalties or logprobs route the step to the sampling head."""
+    from zstep_b200.models.sampling_head import needs_full
+
+    def recs(**kw):
+        r = np.zeros(2, dtype=wire.SAMPLING_DTYPE)
+        r["top_p"], r["repetition"], r["logprobs"] = 1.0, 1.0, -1
+        for k, v in kw.items():
+            r[k][1] = v
+        return r
+
+    assert not needs_full(recs(), 2)
+    assert not needs_full(recs(temperature=0.7), 2)
+    assert not needs_full(recs(top_k=5), 2)  # greedy: top-k changes nothing
+    assert needs_full(recs(temperature=0.7, top_k=5), 2)
+    assert needs_full(recs(temperature=0.7, top_p=0.9), 2)
+    assert needs_full(recs(presence=0.5), 2) and needs_full(recs(frequency=0.5), 2)
+    assert needs_full(recs(repetition=1.1), 2) and needs_full(recs(logprobs=0), 2)
+    assert not needs_full(recs(logprobs=0), 1)  # only the first n rows count
