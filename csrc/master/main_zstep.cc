@@ -126,7 +126,8 @@ const char* kRunUsage =
     "                               (with prefix fields, prompt i = shared prefix i % num_prefixes + input_len ids)\n"
     "  --bench-repeats N            Interleaved repeats per tier (default 1)\n"
     "  --micro-steps N              Control-plane benchmark: N synthetic micro-steps per token count on the\n"
-    "                               `micro` worker model (no --model-dir needed); reports round-trip latency\n"
+    "                               `micro` worker model (no --model-dir needed); reports round-trip latency;\n"
+    "                               the default mode (200 steps) when neither a model nor a mode is given\n"
     "  --token-counts LIST          Rows per micro-step, comma separated (default 6,48,192)\n"
     "  --micro-hidden N / --micro-features N / --micro-experts N / --micro-topk N   micro-step model shape\n"
     "  --seed N                     Prompt seed (default 0)\n";
@@ -1220,6 +1221,11 @@ int main(int argc, char** argv) {
     return 2;
   }
   apply_aliases(&a);
+  // `zstep run` with no model and no mode is the control-plane micro-step benchmark (200
+  // steps), as in the reference.
+  if (sub == "run" && !a.has("model-dir") && !a.has("micro-steps") && !a.has("prompt-ids") && !a.has("prompt") &&
+      !a.has("bench-tiers") && !a.has("verify-greedy-json") && !a.has("help") && !a.has("mock"))
+    a.kv["micro-steps"] = "200";
   try {
     return sub == "serve" ? cmd_serve(a) : cmd_run(a);
   } catch (const std::exception& ex) {

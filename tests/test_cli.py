@@ -225,3 +225,19 @@ def test_tokenizer_mode_values(model_dir):
         assert r.returncode == 0, (mode, r.stderr)
     r = run(*base, "--tokenizer-mode", "llama")
     assert r.returncode == 2 and "tokenizer-mode" in r.stderr
+
+
+def test_micro_steps_are_the_default_mode():
+    """Without a model or a mode, `zstep run` (and `zstep --steps N`, the reference's
+    spelling) is the control-plane micro-step benchmark."""
+    import sys
+
+    small = ["--token-counts", "4", "--device", "cpu", "--world-size", "1", "--max-seqs", "8", "--max-step-tokens",
+             "16", "--micro-hidden", "256", "--micro-features", "256", "--micro-experts", "64", "--micro-topk", "4",
+             "--python", sys.executable, "--worker-root", ROOT]
+    r = run("run", *small, timeout=300)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
+    assert json.loads(r.stdout.strip().splitlines()[-1])["micro_steps"][0]["steps"] == 200
+    r = run("--steps", "7", *small, timeout=300)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
+    assert json.loads(r.stdout.strip().splitlines()[-1])["micro_steps"][0]["steps"] == 7
