@@ -205,3 +205,30 @@ def test_tp2_mtp_speculation_matches_greedy_reference():
         assert st.spec_verify_steps > 0 and st.spec_drafts > 0
     finally:
         coord.shutdown()
+
+
+@pytest.mark.timeout(600)
+def test_tp2_ngram_speculation_matches_greedy_reference():
+    """n-gram drafts (prompt lookup, windows 2..5) on prompts with repeated phrases: the
+    engine proposes drafts from earlier occurrences, the workers verify and roll their
+    recurrent state back, and the output is still plain greedy."""
+    rng = random.Random(5)
+    ps = []
+    for _ in range(3):
+        phrase = [rng.randrange(4096) for _ in range(6)]
+        ps.append([rng.randrange(4096) for _ in range(5)] + phrase * 4 + phrase[:3])
+    ref = reference_generate(ps, 16)
+    eng, coord = launch(model="qwen3.5-tiny", world_size=2, device="cpu", max_seqs=4, max_step_tokens=96,
+                        page_size=16, num_pages=256, max_model_len=512,
+                        engine={"max_prefill_chunk": 40, "recurrent_state": True, "spec_method": "ngram",
+                                "num_spec_tokens": 3})
+    try:
+        for i, p in enumerate(ps):
+            assert eng.submit(i, p, 16, True)
+        out = run_to_completion(eng)
+        for i in range(len(ps)):
+            assert out[i] == ref[i], f"request {i} diverged"
+        st = eng.stats()
+        assert st.spec_verify_steps > 0 and st.spec_drafts > 0
+    finally:
+        coord.shutdown()
