@@ -26,7 +26,9 @@ def plan(rows, positions, width=0, sample=True):
             "ckpt_row": np.zeros(0, np.int32), "ckpt_slot": np.zeros(0, np.int32),
             "seq_slot": np.array([0], np.int32), "restore_slot": np.array([-1], np.int32),
             "spec_width": np.array([width], np.int32), "sample_row": np.array([n - 1 if sample else -1], np.int32),
-            "sampling": samp}
+            "sampling": samp,
+            # slot 0's page table (attention-only models keep paged caches)
+            "dirty_rows": np.array([0], np.int32), "dirty_pages": np.arange(1, 9, dtype=np.int32)[None]}
 
 
 def greedy(prompt, n):

@@ -232,3 +232,47 @@ def test_tp2_ngram_speculation_matches_greedy_reference():
         assert st.spec_verify_steps > 0 and st.spec_drafts > 0
     finally:
         coord.shutdown()
+
+
+@pytest.mark.timeout(600)
+def test_deepseek_dram_tier_demotes_and_reloads_through_shm():
+    """The host DRAM tier end to end: attention-only model, prefix caching with one page
+    per node, HBM pages for about one request.  Alternating two prompt families evicts each
+    family's prefix to the workers' host arenas (KvTransfer D2H) and reloads it for the next
+    request of that family (H2D); the 2 CPU ranks keep paged caches, so the output equals the
+    single-process reference only if every page comes back intact."""
+    from zstep_b200.config import deepseek_tiny
+    from zstep_b200.models.deepseek_ref import DeepSeekReference
+    from zstep_b200.models.deepseek_weights import DeepSeekRandomWeights
+
+    cfg = deepseek_tiny()
+    V = cfg.vocab_size
+    fam = [[(7 * i + 3) % V for i in range(40)], [(11 * i + 5) % V for i in range(40)]]
+    ps = [fam[k % 2] + [(k * 13 + j) % V for j in range(5)] for k in range(6)]
+    model = DeepSeekReference(cfg, DeepSeekRandomWeights(cfg, seed=0))
+    ref = []
+    for p in ps:
+        st = model.new_state()
+        for t in p:
+            lg = model.step(st, t)
+        gen = []
+        for _ in range(6):
+            gen.append(int(torch.argmax(lg)))
+            lg = model.step(st, gen[-1])
+        ref.append(gen)
+    eng, coord = launch(model="deepseek-tiny", world_size=2, device="cpu", max_seqs=1, max_step_tokens=64,
+                        page_size=4, num_pages=21, max_model_len=128, dram_kv_blocks=48,
+                        engine={"max_prefill_chunk": 32, "prefix_caching": True, "pages_per_node": 1,
+                                "recurrent_state": False, "dram_blocks": 48})
+    try:
+        for i, p in enumerate(ps):
+            assert eng.submit(i, p, 6, True)
+        out = run_to_completion(eng)
+        for i in range(len(ps)):
+            assert out[i] == ref[i], f"request {i} diverged"
+        st = eng.stats()
+        assert st.dram_offloads > 0 and st.dram_reloads > 0 and st.dram_hit_tokens > 0, \
+            (st.dram_offloads, st.dram_reloads, st.dram_hit_tokens)
+        assert st.prefix_hit_tokens > 0
+    finally:
+        coord.shutdown()

@@ -121,6 +121,26 @@ class CpuReferenceRunner:
         self.states: dict[int, object] = {}
         self.ckpt: dict[int, object] = {}
         self.generated: dict[int, list[int]] = {}  # per slot: generated tokens (penalties)
+        # Attention-only models (DeepSeek-style) also keep their caches paged, like the GPU
+        # runner: [layers, pages, page_size, dim] per cache, addressed through the page
+        # tables the plans carry.  A sequence's state is rebuilt from its pages at every
+        # step, so a prefix shared through the page table, a page reloaded from the host
+        # DRAM tier, or a rejected speculative row all behave as on the GPU.
+        self.paged = None
+        self.dram = None
+        if _is_deepseek(self.cfg):
+            c = self.cfg
+            npg, ps = getattr(args, "num_pages", 256), geo.page_size
+            L = c.num_hidden_layers
+            self.paged = [torch.zeros(L, npg, ps, c.kv_cache_dim), torch.zeros(L, npg, ps, c.index_head_dim)]
+            if self.spec == "dspark":  # the draft layer's own caches, same page table
+                self.paged += [torch.zeros(1, npg, ps, c.kv_cache_dim), torch.zeros(1, npg, ps, c.index_head_dim)]
+            self.page_size = ps
+            self.ptab: dict[int, np.ndarray] = {}
+            if getattr(args, "dram_kv_blocks", 0):
+                from .kv_dram import DramKvArena
+
+                self.dram = DramKvArena(self.paged, args.dram_kv_blocks)
 
     def _allreduce(self, x: torch.Tensor) -> torch.Tensor:
         x = x.contiguous()
@@ -134,17 +154,73 @@ class CpuReferenceRunner:
         dist.all_gather(parts, shard.contiguous())
         return torch.cat(parts)
 
+    # ------------------------------------------------------------------ paged caches
+    def _page_of(self, slot: int, p: int) -> int:
+        t = self.ptab.get(slot)
+        j = p // self.page_size
+        return int(t[j]) if t is not None and j < len(t) else 0
+
+    def _state_from_pages(self, slot: int, pos0: int):
+        """A fresh state holding rows 0..pos0-1 of the slot's paged caches."""
+        st = self.model.new_state()
+        if pos0 > 0:
+            q = np.arange(pos0)
+            pg = torch.as_tensor([self._page_of(slot, int(x)) for x in q], dtype=torch.long)
+            off = torch.as_tensor(q % self.page_size, dtype=torch.long)
+            for li in range(len(st.ckv)):
+                st.ckv[li] = self.paged[0][li, pg, off].clone()
+                st.ik[li] = self.paged[1][li, pg, off].clone()
+            if len(self.paged) > 2:
+                st.dckv = self.paged[2][0, pg, off].clone()
+                st.dik = self.paged[3][0, pg, off].clone()
+            st.pos = pos0
+        return st
+
+    def _rows_to_pages(self, slot: int, st, p: int) -> None:
+        pg = self._page_of(slot, p)
+        if pg == 0:
+            return  # past the sequence's pages (never read back)
+        for li in range(len(st.ckv)):
+            self.paged[0][li, pg, p % self.page_size] = st.ckv[li][p]
+            self.paged[1][li, pg, p % self.page_size] = st.ik[li][p]
+
+    def _draft_rows_to_pages(self, slot: int, st, p0: int) -> None:
+        """Draft-layer cache rows p0.. (contexts and the scratch block rows)."""
+        if len(self.paged) < 3 or st.dckv is None:
+            return
+        for p in range(p0, st.dckv.shape[0]):
+            pg = self._page_of(slot, p)
+            if pg:
+                self.paged[2][0, pg, p % self.page_size] = st.dckv[p]
+                self.paged[3][0, pg, p % self.page_size] = st.dik[p]
+
     def execute(self, plan: dict) -> np.ndarray:
         if plan["opcode"] == wire.OP_KV_TRANSFER:
-            raise RuntimeError("the fp32 reference runner keeps unpaged per-slot state: no DRAM tier")
+            if self.dram is None:
+                raise RuntimeError("KvTransfer step without a DRAM arena (--dram-kv-blocks 0, or a recurrent model)")
+            self.dram.transfer(plan["token_ids"], plan["positions"], plan["row_slot"])
+            # A demoted page is free: on a GPU its next owner overwrites it.  Poison it here,
+            # so a prefix that comes back without its reload diverges instead of reading
+            # rows that merely happen to survive.
+            down = [int(pg) for pg, up in zip(plan["token_ids"], plan["row_slot"]) if not int(up)]
+            if down:
+                idx = torch.as_tensor(down, dtype=torch.long)
+                for c in self.paged:
+                    c[:, idx] = float("nan")
+            return _outputs(0)
         n = plan["num_seqs"]
         out = _outputs(n)
         qs, toks, pos = plan["query_start"], plan["token_ids"], plan["positions"]
         ckpt_at = {int(r): int(s) for r, s in zip(plan["ckpt_row"], plan["ckpt_slot"])}
+        if self.paged is not None:
+            for k, slot in enumerate(plan["dirty_rows"]):
+                self.ptab[int(slot)] = np.array(plan["dirty_pages"][k])
         for i in range(n):
             slot = int(plan["seq_slot"][i])
             r0, r1 = int(qs[i]), int(qs[i + 1])
-            if int(plan["restore_slot"][i]) >= 0:
+            if self.paged is not None and r1 > r0:
+                self.states[slot] = self._state_from_pages(slot, int(pos[r0]))
+            elif int(plan["restore_slot"][i]) >= 0:
                 self.states[slot] = self.model.clone_state(self.ckpt[int(plan["restore_slot"][i])])
             if r1 > r0 and int(pos[r0]) == 0:
                 self.states[slot] = self.model.new_state()
@@ -155,6 +231,8 @@ class CpuReferenceRunner:
             for r in range(r0, r1):
                 assert st.pos == int(pos[r]), f"slot {slot}: state at {st.pos}, plan position {int(pos[r])}"
                 lg = self.model.step(st, int(toks[r]))
+                if self.paged is not None:
+                    self._rows_to_pages(slot, st, int(pos[r]))
                 if self.num_spec:
                     row_hidden.append(self.model.last_aux if self.spec == "dspark" else st.hidden)
                 if r in ckpt_at:
@@ -168,6 +246,8 @@ class CpuReferenceRunner:
             if int(plan["sample_row"][i]) < 0:
                 if self.num_spec:  # prefill chunk: draft-model state for its rows, no drafts
                     self._draft(self.states[slot], [int(t) for t in toks[r0 + 1:r1]], row_hidden, int(pos[r0]), 0)
+                    if self.paged is not None:
+                        self._draft_rows_to_pages(slot, self.states[slot], int(pos[r0]))
                 continue
             sp = plan["sampling"][i]
             if width > 0:
@@ -199,6 +279,8 @@ class CpuReferenceRunner:
                 else:
                     nxt, hid = [int(t) for t in toks[r0 + 1:r1]] + tokens[:1], row_hidden
                 d = self._draft(self.states[slot], nxt, hid, int(pos[r0]), self.num_spec)
+                if self.paged is not None:
+                    self._draft_rows_to_pages(slot, self.states[slot], int(pos[r0]))
                 out[i]["next_drafts"][:len(d)] = d
                 out[i]["num_drafts"] = len(d)
         return out
