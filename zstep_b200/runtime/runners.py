@@ -94,7 +94,9 @@ def _outputs(n: int) -> np.ndarray:
 
 
 class CpuReferenceRunner:
-    """fp32 reference model, one ``SeqState`` per request slot (+ checkpoint slots)."""
+    """fp32 reference model driven by step plans: one state per request slot, plus
+    checkpoint slots (recurrent models) or paged caches rebuilt through the plans' page
+    tables (attention-only models, which also serve the host DRAM tier's transfers)."""
 
     def __init__(self, args, rank: int, world: int, geo):
         from ..models.deepseek_ref import DeepSeekReference
