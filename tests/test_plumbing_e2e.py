@@ -145,10 +145,12 @@ def test_deepseek_tp2_shm_engine_matches_reference(apc, spec):
             gen.append(int(torch.argmax(lg)))
             lg = model.step(st, gen[-1])
         ref.append(gen)
+    # The model keeps no recurrent state: a prefix hit reuses the shared pages through the
+    # page table (the runner's paged caches), with no checkpoint slots.
     eng, coord = launch(model="deepseek-tiny", world_size=2, device="cpu", max_seqs=2, max_step_tokens=64,
-                        page_size=16, num_pages=128, max_model_len=256, num_ckpt_slots=16 if apc else 0,
+                        page_size=16, num_pages=128, max_model_len=256,
                         engine={"max_prefill_chunk": 24, "prefix_caching": apc, "pages_per_node": 1,
-                                "recurrent_state": True, "spec_method": spec,
+                                "recurrent_state": False, "spec_method": spec,
                                 "num_spec_tokens": 3 if spec != "none" else 0})
     try:
         for i, p in enumerate(ps):
