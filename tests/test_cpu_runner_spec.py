@@ -118,3 +118,21 @@ def test_dspark_drafts_verify_and_roll_back():
     assert o[0]["num_tokens"] == 1 and int(o[0]["tokens"][0]) == ref[K + 2] and r.states[0].pos == p0 + 1
     o = r.execute(plan([ref[K + 2]], [p0 + 1]))
     assert int(o[0]["tokens"][0]) == ref[K + 3]
+
+
+def test_new_request_past_position_zero_restarts_penalty_history():
+    """Prefix hit: the new request's first plan starts at position 16 but carries the slot's
+    page-table row, so the slot's generated-token history (penalties) restarts."""
+    from zstep_b200.config import deepseek_tiny
+
+    cfg = deepseek_tiny()
+    args = argparse.Namespace(model="deepseek-tiny", seed=0, spec_method="none", num_spec_tokens=0)
+    r = CpuReferenceRunner(args, 0, 1, wire.Geometry(max_seqs=1))
+    prompt = [(7 * i + 1) % cfg.vocab_size for i in range(20)]
+    r.execute(plan(prompt, range(20)))
+    p = plan([prompt[-1]], [20])
+    p["dirty_rows"], p["dirty_pages"] = np.zeros(0, np.int32), np.zeros((0, 8), np.int32)
+    r.execute(p)  # the same request continues: history grows
+    assert len(r.generated[0]) == 2
+    r.execute(plan(prompt[16:], range(16, 20)))  # new request, prefix pages 0..15 reused
+    assert len(r.generated[0]) == 1

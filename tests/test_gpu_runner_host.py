@@ -201,3 +201,30 @@ def test_steady_state_verify_uses_the_graph_record():
     for i in range(3):
         assert out[i]["num_tokens"] == i + 1 and list(out[i]["tokens"][:i + 1]) == list(range(60 + i, 61 + 2 * i))
         assert list(out[i]["next_drafts"][:K]) == [90 + i, 91 + i]
+
+
+def test_penalty_rings_restart_for_new_requests():
+    """A request that starts past position 0 (prefix hit) in a reused slot is recognised by
+    the page-table row its first plan carries; its penalty ring restarts like one starting
+    at position 0, while a continuing request's ring is kept."""
+
+    class FakeHead:
+        def __init__(self):
+            self.resets = []
+
+        def reset(self, slots):
+            self.resets.append(sorted(slots))
+
+        def sample(self, n, xq, xsf, slots, params, top_n=0, record=None):
+            return np.zeros(n, np.int64), None, None, None
+
+    m = FakePlain()
+    g = GpuRunner.wrap(m)
+    g.head = FakeHead()
+    p = plan([(1, [5], 40, 0, True), (2, [6, 7], 32, 0, True), (3, [8], 0, 0, True)])
+    p["flags"] = 0
+    p["sampling"]["presence"][:] = 0.5  # penalties: the full-distribution head runs
+    p["dirty_rows"] = np.array([2], np.int32)  # slot 2's request is new (prefix hit at 32)
+    p["dirty_pages"] = np.array([[3, 4, 5, 6]], np.int32)
+    g.execute(p)
+    assert g.head.resets == [[2, 3]]  # slot 1 continues; slot 3 starts at position 0

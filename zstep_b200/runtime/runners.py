@@ -214,6 +214,9 @@ class CpuReferenceRunner:
         out = _outputs(n)
         qs, toks, pos = plan["query_start"], plan["token_ids"], plan["positions"]
         ckpt_at = {int(r): int(s) for r, s in zip(plan["ckpt_row"], plan["ckpt_slot"])}
+        # A slot's page-table row travels once per request, in the request's first plan:
+        # those slots start a new request (a prefix hit may start it past position 0).
+        fresh = {int(x) for x in plan["dirty_rows"]}
         if self.paged is not None:
             for k, slot in enumerate(plan["dirty_rows"]):
                 self.ptab[int(slot)] = np.array(plan["dirty_pages"][k])
@@ -226,7 +229,8 @@ class CpuReferenceRunner:
                 self.states[slot] = self.model.clone_state(self.ckpt[int(plan["restore_slot"][i])])
             if r1 > r0 and int(pos[r0]) == 0:
                 self.states[slot] = self.model.new_state()
-                self.generated[slot] = []
+            if slot in fresh or (r1 > r0 and int(pos[r0]) == 0):
+                self.generated[slot] = []  # penalty history of the new request
             st = self.states[slot]
             width = int(plan["spec_width"][i])
             row_logits, row_states, row_hidden = [], [], []
@@ -415,7 +419,12 @@ class GpuRunner:
             r.clear_sampling()
             self._sampling_set = False
         qs, pos = plan["query_start"], plan["positions"]
-        starting = [int(plan["seq_slot"][i]) for i in range(n) if qs[i + 1] > qs[i] and int(pos[qs[i]]) == 0]
+        # New requests: a slot whose page-table row this plan carries (sent once, with the
+        # request's first chunk, also when a prefix hit starts it past position 0) or a
+        # chunk starting at position 0.  Their penalty rings restart.
+        fresh = {int(x) for x in plan["dirty_rows"]}
+        starting = [int(plan["seq_slot"][i]) for i in range(n)
+                    if int(plan["seq_slot"][i]) in fresh or (qs[i + 1] > qs[i] and int(pos[qs[i]]) == 0)]
         full = sampling_head.needs_full(plan["sampling"], n)
         if full and self.head is None:
             self.head = sampling_head.SamplingHead(r)
